@@ -1,0 +1,484 @@
+/*
+ * rnb_oracle.c -- CPU restatement of Runnel's sparse-MoE block arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker for the CUDA path:
+ * only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+ * arm load it.  The product path (runnel_b200) never links or calls it.
+ *
+ * What it restates (paths inside the waylake/runnel project):
+ *   - MLX affine dequant-dot, fp32, sequential per 64-group:
+ *       native/src/fused_moe_probe.mm:630-695   (row_dot, scale applied per group)
+ *       native/src/quantized_qmv_probe.mm:404-431 (scale applied per element)
+ *       native/src/quantized_qmm_probe.mm:281-305
+ *   - packed routed gate/up layout (rows 0..I-1 = up, I..2I-1 = gate) and
+ *     silu(gate)*up: src/runnel/mlx.py:38-48,76-78; native/shaders/fused_moe.metal:449,534-541
+ *   - shared expert swiglu(x_gate, x_up) = silu(gate)*up, sigmoid gate:
+ *       bench/mlx_lm_adapter.py:82-94
+ *   - router softmax / top-k / renormalise of the mlx-lm Qwen3.5 sparse-MoE
+ *     block (third-party mlx-lm @15bcf8b, not vendored; call site
+ *     src/runnel/mlx.py:57-82).
+ *   - the reference's synthetic data generators (xorshift64 + bf16 RNE) used
+ *     to reproduce its recorded known-answer checksums:
+ *       native/src/fused_moe_probe.mm:69-104,449-537,600-628
+ *       native/src/quantized_qmv_probe.mm:64-101,365-431
+ *       native/src/quantized_qmm_probe.mm:245-305
+ *
+ * Rounding points of the block oracle (the "fp32-accumulated result"):
+ *   router logits are fp32 dot products rounded to bf16 (MLX's Linear output
+ *   dtype), expert selection is top-k of those bf16 logits with ties broken
+ *   toward the lower expert index, routing weights are the fp32 softmax over
+ *   all E bf16 logits gathered at the selected experts and renormalised in
+ *   fp32; everything after that (gate/up, SwiGLU, down, combine, shared
+ *   expert and its sigmoid gate) stays fp32.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define RNBO_OK 0
+#define RNBO_EINVAL -1
+
+/* ---------------------------------------------------------------- bf16 */
+
+uint16_t rnbo_f32_to_bf16(float value) {
+  uint32_t bits;
+  memcpy(&bits, &value, 4);
+  if (((bits >> 23) & 0xFFu) == 0xFFu) return (uint16_t)(bits >> 16); /* inf/nan kept */
+  bits += 0x7FFFu + ((bits >> 16) & 1u);                             /* round to nearest even */
+  return (uint16_t)(bits >> 16);
+}
+
+float rnbo_bf16_to_f32(uint16_t value) {
+  uint32_t bits = (uint32_t)value << 16;
+  float out;
+  memcpy(&out, &bits, 4);
+  return out;
+}
+
+void rnbo_f32_to_bf16_array(const float* in, uint16_t* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = rnbo_f32_to_bf16(in[i]);
+}
+
+void rnbo_bf16_to_f32_array(const uint16_t* in, float* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = rnbo_bf16_to_f32(in[i]);
+}
+
+/* ------------------------------------------------- affine dequant-dot */
+
+static inline uint32_t code_at(const uint32_t* row, int bits, size_t k) {
+  const size_t per = 32u / (unsigned)bits;
+  const uint32_t mask = (bits == 8) ? 0xFFu : 0x0Fu;
+  return (row[k / per] >> ((unsigned)bits * (k % per))) & mask;
+}
+
+/* One packed row against an fp32 vector: per group
+ *   result += (sum_k q_k * x_k) * scale + (sum_k x_k) * bias
+ * in fp32, k ascending (fused_moe_probe.mm:630-695).  The reference was built
+ * by clang for arm64, which contracts `acc += a * b` into one fused
+ * multiply-add and `a * b + c * d` into fma(a, b, c * d); the fmaf calls
+ * below make that rounding explicit (it is what reproduces the recorded
+ * QMM q8 checksum -12808.676; uncontracted fp32 gives -12808.682). */
+float rnbo_affine_dot(const uint32_t* w_row, const uint16_t* s_row, const uint16_t* b_row,
+                      const float* x, int K, int bits, int group) {
+  float result = 0.0f;
+  const int groups = K / group;
+  for (int g = 0; g < groups; ++g) {
+    const float scale = rnbo_bf16_to_f32(s_row[g]);
+    const float bias = rnbo_bf16_to_f32(b_row[g]);
+    float weighted = 0.0f, xsum = 0.0f;
+    for (int i = 0; i < group; ++i) {
+      const size_t k = (size_t)g * group + i;
+      weighted = fmaf((float)code_at(w_row, bits, k), x[k], weighted);
+      xsum += x[k];
+    }
+    result += fmaf(weighted, scale, xsum * bias);
+  }
+  return result;
+}
+
+/* Same contraction with the scale applied per element
+ * (quantized_qmv_probe.mm:404-431): weighted += q * scale * x. */
+static float affine_dot_scale_inside(const uint32_t* w_row, const uint16_t* s_row,
+                                     const uint16_t* b_row, const float* x, int K, int bits,
+                                     int group) {
+  float result = 0.0f;
+  const int groups = K / group;
+  for (int g = 0; g < groups; ++g) {
+    const float scale = rnbo_bf16_to_f32(s_row[g]);
+    const float bias = rnbo_bf16_to_f32(b_row[g]);
+    float weighted = 0.0f, xsum = 0.0f;
+    for (int i = 0; i < group; ++i) {
+      const size_t k = (size_t)g * group + i;
+      weighted = fmaf((float)code_at(w_row, bits, k) * scale, x[k], weighted);
+      xsum += x[k];
+    }
+    result += fmaf(xsum, bias, weighted);
+  }
+  return result;
+}
+
+/* y[r] = dot(row r, x) for a dense packed matrix [rows, K]. */
+int rnbo_affine_matvec(const uint32_t* w, const uint16_t* s, const uint16_t* b, const float* x,
+                       int rows, int K, int bits, int group, float* y, int nthreads) {
+  if ((bits != 4 && bits != 8) || group <= 0 || K % group || K % (32 / bits)) return RNBO_EINVAL;
+  const size_t wstride = (size_t)K * bits / 32, sstride = (size_t)K / group;
+#pragma omp parallel for num_threads(nthreads > 0 ? nthreads : 1) schedule(static)
+  for (int r = 0; r < rows; ++r)
+    y[r] = rnbo_affine_dot(w + r * wstride, s + r * sstride, b + r * sstride, x, K, bits, group);
+  return RNBO_OK;
+}
+
+/* ------------------------------------------------------- MoE block */
+
+typedef struct rnbo_block {
+  int T, H, I, E, k, bits, group;
+  const uint16_t* x;             /* [T,H] bf16 */
+  const uint16_t* router_w;      /* [E,H] bf16 */
+  const uint16_t* shared_gate_w; /* [H] bf16, NULL = no shared expert */
+  const uint32_t* gu_w;          /* [E,2I,H*bits/32] packed up||gate */
+  const uint16_t* gu_s;          /* [E,2I,H/group] */
+  const uint16_t* gu_b;
+  const uint32_t* dn_w; /* [E,H,I*bits/32] */
+  const uint16_t* dn_s; /* [E,H,I/group] */
+  const uint16_t* dn_b;
+  const uint32_t* sgu_w; /* [2I,H*bits/32] shared up||gate */
+  const uint16_t* sgu_s;
+  const uint16_t* sgu_b;
+  const uint32_t* sdn_w; /* [H,I*bits/32] */
+  const uint16_t* sdn_s;
+  const uint16_t* sdn_b;
+} rnbo_block;
+
+static int block_valid(const rnbo_block* d) {
+  if (!d || d->T < 0 || d->H <= 0 || d->I <= 0 || d->E <= 0 || d->k <= 0 || d->k > d->E) return 0;
+  if ((d->bits != 4 && d->bits != 8) || d->group <= 0) return 0;
+  if (d->H % d->group || d->I % d->group) return 0;
+  return 1;
+}
+
+static void x_row_f32(const rnbo_block* d, int t, float* xf) {
+  for (int h = 0; h < d->H; ++h) xf[h] = rnbo_bf16_to_f32(d->x[(size_t)t * d->H + h]);
+}
+
+/* Router: bf16 logits, top-k (ties -> lower index), renormalised softmax
+ * weights; slots ordered by descending (logit, -index).  shared_gate[t] is
+ * sigmoid(x . w_sg) in fp32 when a shared expert is present. */
+int rnbo_router(const rnbo_block* d, float* logits, int32_t* inds, float* scores,
+                float* shared_gate, int nthreads) {
+  if (!block_valid(d)) return RNBO_EINVAL;
+  const int T = d->T, H = d->H, E = d->E, K = d->k;
+#pragma omp parallel num_threads(nthreads > 0 ? nthreads : 1)
+  {
+    float* xf = (float*)malloc(sizeof(float) * H);
+    float* lg = (float*)malloc(sizeof(float) * E);
+    unsigned char* taken = (unsigned char*)malloc(E);
+#pragma omp for schedule(static)
+    for (int t = 0; t < T; ++t) {
+      x_row_f32(d, t, xf);
+      for (int e = 0; e < E; ++e) {
+        float acc = 0.0f;
+        const uint16_t* wr = d->router_w + (size_t)e * H;
+        for (int h = 0; h < H; ++h) acc += xf[h] * rnbo_bf16_to_f32(wr[h]);
+        lg[e] = rnbo_bf16_to_f32(rnbo_f32_to_bf16(acc));
+        if (logits) logits[(size_t)t * E + e] = lg[e];
+      }
+      /* softmax over all E in fp32 (mlx-lm: softmax(gates, precise=True)) */
+      float mx = lg[0];
+      for (int e = 1; e < E; ++e) mx = lg[e] > mx ? lg[e] : mx;
+      float denom = 0.0f;
+      for (int e = 0; e < E; ++e) denom += expf(lg[e] - mx);
+      memset(taken, 0, E);
+      float sel_sum = 0.0f;
+      float sel_p[64];
+      for (int s = 0; s < K; ++s) {
+        int best = -1;
+        for (int e = 0; e < E; ++e) {
+          if (taken[e]) continue;
+          if (best < 0 || lg[e] > lg[best]) best = e; /* strict: keeps the lower index on ties */
+        }
+        taken[best] = 1;
+        inds[(size_t)t * K + s] = best;
+        sel_p[s] = expf(lg[best] - mx) / denom;
+        sel_sum += sel_p[s];
+      }
+      for (int s = 0; s < K; ++s) scores[(size_t)t * K + s] = sel_p[s] / sel_sum;
+      if (shared_gate) {
+        if (d->shared_gate_w) {
+          float acc = 0.0f;
+          for (int h = 0; h < H; ++h) acc += xf[h] * rnbo_bf16_to_f32(d->shared_gate_w[h]);
+          shared_gate[t] = 1.0f / (1.0f + expf(-acc));
+        } else {
+          shared_gate[t] = 0.0f;
+        }
+      }
+    }
+    free(xf);
+    free(lg);
+    free(taken);
+  }
+  return RNBO_OK;
+}
+
+/* gate/up -> silu(gate)*up -> down for one expert bank entry. */
+static void expert_forward(int H, int I, int bits, int group, const uint32_t* guw,
+                           const uint16_t* gus, const uint16_t* gub, const uint32_t* dnw,
+                           const uint16_t* dns, const uint16_t* dnb, const float* xf, float* hbuf,
+                           float* y) {
+  const size_t gu_ws = (size_t)H * bits / 32, gu_ss = (size_t)H / group;
+  const size_t dn_ws = (size_t)I * bits / 32, dn_ss = (size_t)I / group;
+  for (int c = 0; c < I; ++c) {
+    const float up = rnbo_affine_dot(guw + c * gu_ws, gus + c * gu_ss, gub + c * gu_ss, xf, H, bits, group);
+    const size_t g = (size_t)(c + I);
+    const float gate = rnbo_affine_dot(guw + g * gu_ws, gus + g * gu_ss, gub + g * gu_ss, xf, H, bits, group);
+    hbuf[c] = (gate / (1.0f + expf(-gate))) * up;
+  }
+  for (int n = 0; n < H; ++n)
+    y[n] = rnbo_affine_dot(dnw + n * dn_ws, dns + n * dn_ss, dnb + n * dn_ss, hbuf, I, bits, group);
+}
+
+/* SwitchGLU: per-slot, unweighted expert outputs y[t,s,:] (fp32) for the
+ * caller's indices [T,k] (src/runnel/mlx.py:57-82 semantics). */
+int rnbo_switchglu(const rnbo_block* d, const int32_t* inds, float* y, int nthreads) {
+  if (!block_valid(d)) return RNBO_EINVAL;
+  const int T = d->T, H = d->H, I = d->I, K = d->k, bits = d->bits, G = d->group;
+  for (int i = 0; i < T * K; ++i)
+    if (inds[i] < 0 || inds[i] >= d->E) return RNBO_EINVAL;
+  const size_t gu_we = (size_t)2 * I * H * bits / 32, gu_se = (size_t)2 * I * H / G;
+  const size_t dn_we = (size_t)H * I * bits / 32, dn_se = (size_t)H * I / G;
+#pragma omp parallel num_threads(nthreads > 0 ? nthreads : 1)
+  {
+    float* xf = (float*)malloc(sizeof(float) * H);
+    float* hb = (float*)malloc(sizeof(float) * I);
+#pragma omp for schedule(dynamic, 1)
+    for (int ts = 0; ts < T * K; ++ts) {
+      const int t = ts / K;
+      const size_t e = (size_t)inds[ts];
+      x_row_f32(d, t, xf);
+      expert_forward(H, I, bits, G, d->gu_w + e * gu_we, d->gu_s + e * gu_se, d->gu_b + e * gu_se,
+                     d->dn_w + e * dn_we, d->dn_s + e * dn_se, d->dn_b + e * dn_se, xf, hb,
+                     y + (size_t)ts * H);
+    }
+    free(xf);
+    free(hb);
+  }
+  return RNBO_OK;
+}
+
+/* Shared expert output (unweighted) per token: down(silu(gate.x)*(up.x)). */
+int rnbo_shared_expert(const rnbo_block* d, float* y, int nthreads) {
+  if (!block_valid(d) || !d->sgu_w) return RNBO_EINVAL;
+  const int T = d->T, H = d->H, I = d->I;
+#pragma omp parallel num_threads(nthreads > 0 ? nthreads : 1)
+  {
+    float* xf = (float*)malloc(sizeof(float) * H);
+    float* hb = (float*)malloc(sizeof(float) * I);
+#pragma omp for schedule(dynamic, 1)
+    for (int t = 0; t < T; ++t) {
+      x_row_f32(d, t, xf);
+      expert_forward(H, I, d->bits, d->group, d->sgu_w, d->sgu_s, d->sgu_b, d->sdn_w, d->sdn_s,
+                     d->sdn_b, xf, hb, y + (size_t)t * H);
+    }
+    free(xf);
+    free(hb);
+  }
+  return RNBO_OK;
+}
+
+/* Whole block: out[t] = sum_s score[t,s] * y[t,s] + sigmoid(x.w_sg) * shared(x). */
+int rnbo_moe_block(const rnbo_block* d, float* out, int32_t* inds, float* scores,
+                   float* logits, int nthreads) {
+  if (!block_valid(d)) return RNBO_EINVAL;
+  const int T = d->T, H = d->H, K = d->k;
+  float* sg = (float*)malloc(sizeof(float) * (T > 0 ? T : 1));
+  float* y = (float*)malloc(sizeof(float) * ((size_t)T * K * H + 1));
+  float* ys = (float*)malloc(sizeof(float) * ((size_t)T * H + 1));
+  int rc = rnbo_router(d, logits, inds, scores, sg, nthreads);
+  if (rc == RNBO_OK) rc = rnbo_switchglu(d, inds, y, nthreads);
+  if (rc == RNBO_OK && d->sgu_w) rc = rnbo_shared_expert(d, ys, nthreads);
+  if (rc == RNBO_OK) {
+    for (int t = 0; t < T; ++t)
+      for (int n = 0; n < H; ++n) {
+        float acc = 0.0f;
+        for (int s = 0; s < K; ++s) acc += scores[(size_t)t * K + s] * y[((size_t)t * K + s) * H + n];
+        if (d->sgu_w) acc += sg[t] * ys[(size_t)t * H + n];
+        out[(size_t)t * H + n] = acc;
+      }
+  }
+  free(sg);
+  free(y);
+  free(ys);
+  return rc;
+}
+
+/* --------------------------- reference synthetic generators (KATs) */
+
+typedef struct {
+  uint64_t state;
+} rnbo_xorshift;
+
+static uint32_t xs_next(rnbo_xorshift* r) {
+  r->state ^= r->state << 13;
+  r->state ^= r->state >> 7;
+  r->state ^= r->state << 17;
+  return (uint32_t)(r->state >> 32);
+}
+
+/* lo + unit * (hi - lo), contracted to one fused multiply-add as the
+ * reference's arm64 clang build does. */
+static float xs_uniform(rnbo_xorshift* r, float lo, float hi) {
+  const double unit = (double)xs_next(r) / 4294967295.0;
+  return fmaf((float)unit, hi - lo, lo);
+}
+
+/* Codes are drawn one per byte, so for 4-bit data only the low nibble of
+ * every byte is populated (fused_moe_probe.mm:620-625). */
+static uint32_t xs_word(rnbo_xorshift* r, int bits) {
+  const uint32_t mask = bits == 4 ? 0x0Fu : 0xFFu;
+  uint32_t v = 0;
+  for (int byte = 0; byte < 4; ++byte) v |= (xs_next(r) & mask) << (byte * 8);
+  return v;
+}
+
+static float kat_scale_lo(int bits) { return bits == 4 ? 0.002f : 0.00005f; }
+static float kat_scale_hi(int bits) { return bits == 4 ? 0.008f : 0.00015f; }
+
+/* quantized_qmv_probe.mm:365-403 data: x[K], then (scale,bias) for every
+ * (row,group) of the bank, then every packed word of the bank. */
+int rnbo_kat_qmv_data(int bits, size_t K, size_t group, size_t bank_rows, uint32_t* w,
+                      uint16_t* s, uint16_t* b, uint16_t* x) {
+  if ((bits != 4 && bits != 8) || !group || K % group) return RNBO_EINVAL;
+  rnbo_xorshift r = {bits == 4 ? 0x4A17C0DEull : 0x8A17C0DEull};
+  for (size_t i = 0; i < K; ++i) x[i] = rnbo_f32_to_bf16(xs_uniform(&r, -1.0f, 1.0f));
+  const size_t params = bank_rows * (K / group);
+  for (size_t p = 0; p < params; ++p) {
+    s[p] = rnbo_f32_to_bf16(xs_uniform(&r, kat_scale_lo(bits), kat_scale_hi(bits)));
+    b[p] = rnbo_f32_to_bf16(xs_uniform(&r, -0.0005f, 0.0005f));
+  }
+  const size_t words = bank_rows * (K * bits / 32);
+  for (size_t i = 0; i < words; ++i) w[i] = xs_word(&r, bits);
+  return RNBO_OK;
+}
+
+/* Reference QMV outputs: active row r maps to bank row
+ * sel[r / rows_per_expert] * rows_per_expert + r % rows_per_expert
+ * (quantized_qmv_probe.mm:352-363); nsel == 0 means the identity map. */
+int rnbo_kat_qmv_expected(int bits, size_t K, size_t group, size_t out_rows,
+                          size_t rows_per_expert, const uint32_t* sel, size_t nsel,
+                          const uint32_t* w, const uint16_t* s, const uint16_t* b,
+                          const uint16_t* x, float* y, double* checksum) {
+  float* xf = (float*)malloc(sizeof(float) * K);
+  for (size_t i = 0; i < K; ++i) xf[i] = rnbo_bf16_to_f32(x[i]);
+  const size_t ws = K * bits / 32, ss = K / group;
+  double sum = 0.0;
+  for (size_t r = 0; r < out_rows; ++r) {
+    size_t row = r;
+    if (nsel) row = (size_t)sel[r / rows_per_expert] * rows_per_expert + r % rows_per_expert;
+    y[r] = affine_dot_scale_inside(w + row * ws, s + row * ss, b + row * ss, xf, (int)K, bits,
+                                   (int)group);
+    sum += y[r];
+  }
+  free(xf);
+  if (checksum) *checksum = sum;
+  return RNBO_OK;
+}
+
+/* quantized_qmm_probe.mm:245-305: x[tokens,K], then per output row its
+ * (scale,bias) pairs followed by its packed words. */
+int rnbo_kat_qmm_data(int bits, size_t tokens, size_t outputs, size_t K, size_t group,
+                      uint32_t* w, uint16_t* s, uint16_t* b, uint16_t* x) {
+  if ((bits != 4 && bits != 8) || !group || K % group) return RNBO_EINVAL;
+  rnbo_xorshift r = {bits == 4 ? 0x4D4D4D01ull : 0x4D4D4D02ull};
+  for (size_t i = 0; i < tokens * K; ++i) x[i] = rnbo_f32_to_bf16(xs_uniform(&r, -1.0f, 1.0f));
+  const size_t groups = K / group, ws = K * bits / 32;
+  for (size_t row = 0; row < outputs; ++row) {
+    for (size_t g = 0; g < groups; ++g) {
+      s[row * groups + g] = rnbo_f32_to_bf16(xs_uniform(&r, kat_scale_lo(bits), kat_scale_hi(bits)));
+      b[row * groups + g] = rnbo_f32_to_bf16(xs_uniform(&r, -0.0005f, 0.0005f));
+    }
+    for (size_t p = 0; p < ws; ++p) w[row * ws + p] = xs_word(&r, bits);
+  }
+  return RNBO_OK;
+}
+
+int rnbo_kat_qmm_expected(int bits, size_t tokens, size_t outputs, size_t K, size_t group,
+                          const uint32_t* w, const uint16_t* s, const uint16_t* b,
+                          const uint16_t* x, float* y, double* checksum, int nthreads) {
+  float* xf = (float*)malloc(sizeof(float) * tokens * K);
+  for (size_t i = 0; i < tokens * K; ++i) xf[i] = rnbo_bf16_to_f32(x[i]);
+  const size_t ws = K * bits / 32, ss = K / group;
+#pragma omp parallel for num_threads(nthreads > 0 ? nthreads : 1) schedule(static)
+  for (long long t = 0; t < (long long)tokens; ++t)
+    for (size_t o = 0; o < outputs; ++o)
+      y[t * outputs + o] = rnbo_affine_dot(w + o * ws, s + o * ss, b + o * ss, xf + t * K,
+                                           (int)K, bits, (int)group);
+  double sum = 0.0;
+  for (size_t i = 0; i < tokens * outputs; ++i) sum += y[i];
+  free(xf);
+  if (checksum) *checksum = sum;
+  return RNBO_OK;
+}
+
+/* fused_moe_probe.mm:449-492: x[2048], the gate/up bank (per row: pairs then
+ * words), the down bank (same), then 8 router weights U(0.5,1.5) normalised. */
+int rnbo_kat_two_stage_data(int bits, size_t experts, size_t H, size_t I, size_t group,
+                            size_t k, uint16_t* x, uint32_t* guw, uint16_t* gus, uint16_t* gub,
+                            uint32_t* dnw, uint16_t* dns, uint16_t* dnb, float* route_w) {
+  if ((bits != 4 && bits != 8) || !group || H % group || I % group) return RNBO_EINVAL;
+  rnbo_xorshift r = {bits == 4 ? 0xF05EEDB1ull : 0xF05EEDB2ull};
+  for (size_t i = 0; i < H; ++i) x[i] = rnbo_f32_to_bf16(xs_uniform(&r, -1.0f, 1.0f));
+  const size_t banks[2][2] = {{experts * 2 * I, H}, {experts * H, I}};
+  uint32_t* ws[2] = {guw, dnw};
+  uint16_t* ss[2] = {gus, dns};
+  uint16_t* bs[2] = {gub, dnb};
+  for (int bank = 0; bank < 2; ++bank) {
+    const size_t rows = banks[bank][0], red = banks[bank][1];
+    const size_t groups = red / group, wstride = red * bits / 32;
+    for (size_t row = 0; row < rows; ++row) {
+      for (size_t g = 0; g < groups; ++g) {
+        ss[bank][row * groups + g] =
+            rnbo_f32_to_bf16(xs_uniform(&r, kat_scale_lo(bits), kat_scale_hi(bits)));
+        bs[bank][row * groups + g] = rnbo_f32_to_bf16(xs_uniform(&r, -0.0005f, 0.0005f));
+      }
+      for (size_t p = 0; p < wstride; ++p) ws[bank][row * wstride + p] = xs_word(&r, bits);
+    }
+  }
+  float total = 0.0f;
+  for (size_t i = 0; i < k; ++i) {
+    route_w[i] = xs_uniform(&r, 0.5f, 1.5f);
+    total += route_w[i];
+  }
+  for (size_t i = 0; i < k; ++i) route_w[i] /= total;
+  return RNBO_OK;
+}
+
+/* expected_direct_ of fused_moe_probe.mm:494-537: out = sum_s w_s * down_e(h_e). */
+int rnbo_kat_two_stage_expected(int bits, size_t H, size_t I, size_t group, size_t k,
+                                const uint32_t* sel, const uint16_t* x, const uint32_t* guw,
+                                const uint16_t* gus, const uint16_t* gub, const uint32_t* dnw,
+                                const uint16_t* dns, const uint16_t* dnb, const float* route_w,
+                                float* out, double* checksum) {
+  float* xf = (float*)malloc(sizeof(float) * H);
+  float* hb = (float*)malloc(sizeof(float) * I);
+  float* y = (float*)malloc(sizeof(float) * H);
+  for (size_t i = 0; i < H; ++i) xf[i] = rnbo_bf16_to_f32(x[i]);
+  for (size_t n = 0; n < H; ++n) out[n] = 0.0f;
+  const size_t gu_we = 2 * I * H * bits / 32, gu_se = 2 * I * H / group;
+  const size_t dn_we = H * I * bits / 32, dn_se = H * I / group;
+  for (size_t s = 0; s < k; ++s) {
+    const size_t e = sel[s];
+    expert_forward((int)H, (int)I, bits, (int)group, guw + e * gu_we, gus + e * gu_se,
+                   gub + e * gu_se, dnw + e * dn_we, dns + e * dn_se, dnb + e * dn_se, xf, hb, y);
+    for (size_t n = 0; n < H; ++n) out[n] += route_w[s] * y[n];
+  }
+  double sum = 0.0;
+  for (size_t n = 0; n < H; ++n) sum += out[n];
+  free(xf);
+  free(hb);
+  free(y);
+  if (checksum) *checksum = sum;
+  return RNBO_OK;
+}
