@@ -1,0 +1,356 @@
+"""Benchmark of the sparse-MoE block (decode) on B200.
+
+Default workload (N=1): configuration 2 of the reference's hot-path benchmark
+set -- one Ornith MoE block, 4-bit MLX affine (group 64), batch-1 decode --
+measured as microseconds per token.  A step is one block call on one batch of
+T tokens (router, top-8, routed experts, shared expert, combine).
+
+Timing: W warm-up steps, then K steps bracketed by barrier + synchronize,
+device-timed with CUDA events.  Every step uses a different token and one of
+R device copies of the block's weights, R chosen so that the copies exceed the
+L2 cache several times over (no step can hit weights left in L2 by the
+previous ones); the K steps are replayed from one CUDA graph.
+
+Also reported:
+  e2e           the same metric through the public API with the token in pinned
+                host memory: per step H2D copy, C-ABI call, D2H copy of the
+                output, launched from Python, device-timed over the K steps.
+  roofline      algorithmic HBM bytes per step (distinct experts' weights +
+                shared expert + router + activations) / step time, against
+                MEASURED_PEAKS.json hbm_gbs.
+  cpu_baseline  the CPU oracle (C restatement, OpenMP) on the same workload.
+  --impl reference  times that CPU path alone (the reference's own MLX path
+                cannot run here: no Apple GPU, no MLX).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+HBM_NOMINAL_GBS = 8000.0
+
+
+def expert_bytes(bits, H=2048, I=512, group=64):
+    gu = 2 * I * H * bits // 8 + 2 * I * (H // group) * 4
+    dn = H * I * bits // 8 + H * (I // group) * 4
+    return gu, dn
+
+
+def step_bytes(bits, distinct_experts, T, H=2048, I=512, E=256, shared=True):
+    gu, dn = expert_bytes(bits, H, I)
+    b = distinct_experts * (gu + dn)
+    if shared:
+        b += gu + dn + H * 2  # shared expert + its gate row
+    b += E * H * 2  # router
+    b += T * H * 2 * 2  # x in, out
+    return b
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            self.path = f"/tmp/rnb_clocks_{os.getpid()}.csv"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 7:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(bits, T, budget_s=10.0, seed=1):
+    from oracle import oracle
+    from runnel_b200 import inputs
+
+    blk = inputs.make_block(bits, seed=seed, T=T)
+    w = oracle.BlockWeights(bits=bits, group=64, **blk.weight_fields())
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.moe_block(w, blk.x, k=8)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or n >= 10000:
+            break
+    cores = os.cpu_count() or 1
+    return {"value": el / (n * T) * 1e6, "unit": "us/token", "cores": cores, "kind": "port",
+            "sample": f"{n} block calls of T={T} tokens, q{bits} (CPU oracle, C + OpenMP, fp32)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    bits, T = 4, args.tokens
+    times = []
+    from oracle import oracle
+    from runnel_b200 import inputs
+
+    blk = inputs.make_block(bits, seed=1, T=T)
+    w = oracle.BlockWeights(bits=bits, group=64, **blk.weight_fields())
+    for _ in range(args.warmup):
+        oracle.moe_block(w, blk.x, k=8)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.moe_block(w, blk.x, k=8)
+    el = time.perf_counter() - t0
+    us_tok = el / (args.steps * T) * 1e6
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference", "metric": "moe_block_decode_us_per_token", "value": us_tok,
+        "unit": "us/token", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config2 q4 decode T={T}", "bits": bits, "tokens_per_step": T},
+        "cpu_baseline": {"value": us_tok, "unit": "us/token", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} block calls of T={T} (CPU oracle, C + OpenMP)"},
+        "e2e": {"value": us_tok, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_profile(args):
+    """Small fixed case for ncu captures: two block copies (~1 GB for q4),
+    W + K plain (non-graph) block calls, no timing, no CPU baseline."""
+    import torch
+
+    from runnel_b200 import inputs, ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    blk = inputs.make_block(args.bits, seed=args.seed, T=1)
+    copies = [ops.BlockTensors.from_numpy(blk, dev)]
+    copies.append(ops.BlockTensors(**{f: (v.clone() if isinstance(v, torch.Tensor) else v)
+                                      for f, v in copies[0].__dict__.items()}))
+    xs = torch.from_numpy(inputs.make_tokens(args.seed, 64 * args.tokens)).view(torch.int16)
+    xs = xs.view(torch.bfloat16).to(dev).reshape(64, args.tokens, -1)
+    ws = ops.Workspace(dev)
+    for i in range(args.warmup + args.steps):
+        ops.moe_block(copies[i % 2], xs[i % 64], ws=ws)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": True, "bits": args.bits, "tokens": args.tokens,
+                      "calls": args.warmup + args.steps}))
+
+
+def run_ours(args):
+    import torch
+
+    from runnel_b200 import inputs, ops
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+
+    bits, T = args.bits, args.tokens
+    blk = inputs.make_block(bits, seed=args.seed, T=1)
+    base = ops.BlockTensors.from_numpy(blk, dev)
+    gu, dn = expert_bytes(bits)
+    block_bytes = base.E * (gu + dn)
+    per_step = step_bytes(bits, min(8 * T, 256), T)
+    R = max(4, int(np.ceil(4 * L2_BYTES / per_step)))
+    R = min(R, 48)
+    copies = [base]
+    for _ in range(R - 1):
+        c = ops.BlockTensors(**{f: (v.clone() if isinstance(v, torch.Tensor) else v)
+                                for f, v in base.__dict__.items()})
+        copies.append(c)
+    ntok = R * T
+    xs_np = inputs.make_tokens(args.seed, ntok)
+    xs = torch.from_numpy(xs_np).view(torch.int16).view(torch.bfloat16).to(dev).reshape(R, T, -1)
+    outs = torch.empty_like(xs)
+    ws = ops.Workspace(dev)
+    stream = torch.cuda.Stream(dev)
+
+    def one(i):
+        outs[i].copy_(ops.moe_block(copies[i], xs[i], ws=ws))
+
+    with torch.cuda.stream(stream):
+        for i in range(R):
+            one(i)
+    stream.synchronize()
+    # distinct experts actually touched per step (for the roofline's bytes)
+    inds_all = []
+    with torch.cuda.stream(stream):
+        for i in range(R):
+            _, ii, _ = ops.moe_block(copies[i], xs[i], ws=ws, return_routing=True)
+            inds_all.append(ii)
+    stream.synchronize()
+    distinct = float(np.mean([len(np.unique(ii.cpu().numpy())) for ii in inds_all]))
+    per_step = step_bytes(bits, distinct, T)
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(R):
+            one(i)
+    reps = max(1, (args.steps + R - 1) // R)
+    K = reps * R
+    wreps = max(1, (args.warmup + R - 1) // R)
+    with torch.cuda.stream(stream):
+        for _ in range(wreps):
+            g.replay()
+    stream.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    # sustained replays so the clock sampler sees the GPU under this load
+    t_end = time.time() + args.soak
+    with torch.cuda.stream(stream):
+        while time.time() < t_end:
+            for _ in range(50):
+                g.replay()
+            stream.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / K
+    us_tok = ms_step * 1e3 / (T * world) if False else ms_step * 1e3 / T
+
+    # end to end through the public API with host buffers
+    xh = torch.from_numpy(xs_np).view(torch.int16).view(torch.bfloat16).reshape(R, T, -1).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty((T, xs.shape[-1]), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(min(R, args.warmup + 1)):
+            xd.copy_(xh[i], non_blocking=True)
+            oh[i].copy_(ops.moe_block(copies[i], xd, ws=ws), non_blocking=True)
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for s in range(K):
+            i = s % R
+            xd.copy_(xh[i], non_blocking=True)
+            oh[i].copy_(ops.moe_block(copies[i], xd, ws=ws), non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_us = e0.elapsed_time(e1) * 1e3 / (K * T)
+
+    hbm, _, src = peaks()
+    achieved = per_step / (ms_step * 1e-3) / 1e9
+    line = {
+        "metric": "moe_block_decode_us_per_token", "value": us_tok, "unit": "us/token",
+        "n_gpus": world, "steps": K, "warmup": wreps * R, "ms_per_step": ms_step,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded MLX-affine block, N(0,1) bf16 tokens)",
+        "config": {"workload": f"config{args.config} q{bits} decode T={T}", "bits": bits,
+                   "tokens_per_step": T, "H": 2048, "I": 512, "E": 256, "top_k": 8,
+                   "weight_copies_rotated": R, "l2": "inputs rotate over R block copies > 4x L2",
+                   "parallelism": "replica" if world > 1 else "single"},
+        "e2e": {"value": e2e_us, "unit": "us/token", "h2d_bytes_per_step": T * 2048 * 2,
+                "d2h_bytes_per_step": T * 2048 * 2},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_source": src, "frac_of_nominal_8tbs": achieved / HBM_NOMINAL_GBS,
+                     "traffic": None, "algorithmic_bytes_per_step": per_step,
+                     "distinct_experts_per_step": distinct, "kernel": "k_route+k_gateup+k_down chain"},
+        "gpu_launches": 3 * K * ((T + 63) // 64),
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(bits, T, budget_s=args.cpu_budget, seed=args.seed)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=480)
+    ap.add_argument("--warmup", type=int, default=48)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--bits", type=int, default=None)
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--seed", type=int, default=None)
+    ap.add_argument("--soak", type=float, default=1.5)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="small case for ncu captures (2 weight copies, plain launches)")
+    args = ap.parse_args()
+    from runnel_b200.inputs import CONFIGS
+    cfg = CONFIGS[args.config]
+    args.bits = args.bits or cfg["bits"]
+    args.seed = cfg["seed"] if args.seed is None else args.seed
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+    elif args.profile:
+        run_profile(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

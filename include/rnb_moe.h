@@ -1,0 +1,144 @@
+/*
+ * rnb_moe.h -- C ABI of runnel-b200's sparse-MoE block for NVIDIA B200 (sm_100a).
+ *
+ * Plain C: device pointers, sizes and a CUDA stream passed as void*.  No
+ * allocation happens inside any entry point: the caller owns the weights,
+ * the activations, the outputs and one workspace sized by
+ * rnb_moe_workspace_size().  Every call is stream-ordered and asynchronous;
+ * it returns RNB_OK or a negative error code, and rnb_last_error() gives a
+ * thread-local message for the last failure on the calling thread.
+ *
+ * Weight layout is MLX affine quantization, exactly as Runnel stores it:
+ *   codes  uint32 words, 32/bits codes per word, code j of a word in bits
+ *          [bits*j, bits*(j+1)) (LSB first); bits = 4 or 8
+ *   scales, biases  bf16, one per 64 consecutive inputs of a row (group 64)
+ *   w = scale * code + bias
+ * Routed gate/up is Runnel's packed tensor: per expert 2*I rows, rows
+ * [0, I) = up_proj, rows [I, 2I) = gate_proj (src/runnel/mlx.py:38-48).
+ *
+ * Reference interfaces replaced (paths inside the waylake/runnel project;
+ * MLX / mlx-lm are third-party and not vendored there):
+ *   rnb_switchglu_fwd  <- FusedQuantizedSwitchGLU.__call__(x, indices)
+ *                         src/runnel/mlx.py:57-82 (one mx.gather_qmm over the
+ *                         packed gate/up, SwiGLU, down_proj gather_qmm)
+ *   rnb_moe_block_fwd  <- layer.mlp(x): mlx-lm Qwen3.5 sparse-MoE block as
+ *                         timed by bench/mlx_component_profile.py:130 (router
+ *                         Linear, softmax, argpartition top-k, renormalise,
+ *                         switch_mlp, weighted sum, sigmoid-gated shared
+ *                         expert bench/mlx_lm_adapter.py:82-94)
+ *   rnb_router_topk    <- the router half of the same block (gate Linear,
+ *                         softmax, top-k, renormalise)
+ */
+#ifndef RNB_MOE_H_
+#define RNB_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RNB_API __attribute__((visibility("default")))
+#else
+#define RNB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RNB_OK 0
+#define RNB_ERR_INVALID -1     /* bad shape, null pointer, unsupported format */
+#define RNB_ERR_ALIGN -2       /* a pointer is not 16-byte aligned */
+#define RNB_ERR_WORKSPACE -3   /* workspace missing or smaller than required */
+#define RNB_ERR_CUDA -4        /* a CUDA runtime call failed */
+#define RNB_ERR_DEVICE -5      /* sm_100 device required */
+#define RNB_ERR_TIMEOUT -6     /* a bounded device-side wait gave up */
+
+/* Device status bits, accumulated in the workspace by the kernels and read
+ * with rnb_moe_status(). */
+#define RNB_STATUS_BAD_INDEX 0x1u  /* an expert index >= E was skipped */
+#define RNB_STATUS_TIMEOUT 0x2u    /* a bounded device wait expired */
+
+typedef struct rnb_moe_desc {
+  int32_t T;             /* tokens in this call (rows of x) */
+  int32_t H;             /* hidden size (2048 for Ornith) */
+  int32_t I;             /* expert intermediate size (512) */
+  int32_t E;             /* experts held in gu_w/dn_w (256, or a shard) */
+  int32_t E_total;       /* router width (256); E_total == E without sharding */
+  int32_t expert_offset; /* global id of gu_w[0] (expert-parallel shard) */
+  int32_t k;             /* experts per token (8) */
+  int32_t bits;          /* 4 or 8 */
+  int32_t group;         /* quantization group, must be 64 */
+  int32_t flags;         /* RNB_FLAG_* */
+  /* routed bank */
+  const uint32_t* gu_w; /* [E, 2I, H*bits/32]  up rows then gate rows */
+  const uint16_t* gu_s; /* [E, 2I, H/64] bf16 */
+  const uint16_t* gu_b; /* [E, 2I, H/64] bf16 */
+  const uint32_t* dn_w; /* [E, H, I*bits/32] */
+  const uint16_t* dn_s; /* [E, H, I/64] bf16 */
+  const uint16_t* dn_b; /* [E, H, I/64] bf16 */
+  /* router and shared expert (rnb_moe_block_fwd / rnb_router_topk only) */
+  const uint16_t* router_w;      /* [E_total, H] bf16 */
+  const uint16_t* shared_gate_w; /* [H] bf16; NULL = block without shared expert */
+  const uint32_t* sgu_w;         /* [2I, H*bits/32]  up rows then gate rows */
+  const uint16_t* sgu_s;         /* [2I, H/64] */
+  const uint16_t* sgu_b;
+  const uint32_t* sdn_w; /* [H, I*bits/32] */
+  const uint16_t* sdn_s; /* [H, I/64] */
+  const uint16_t* sdn_b;
+} rnb_moe_desc;
+
+/* rnb_moe_desc.flags */
+#define RNB_FLAG_SHARED_ON_THIS_RANK 0x1 /* add the shared expert (set on one EP rank only
+                                            when the shared expert is split off) */
+#define RNB_FLAG_NO_SHARED 0x2           /* skip the shared expert even if pointers are set */
+#define RNB_FLAG_Y_F32 0x4               /* rnb_switchglu_fwd writes y as fp32 instead of bf16 */
+
+/* Library version (major*10000 + minor*100 + patch). */
+RNB_API int rnb_version(void);
+
+/* Thread-local message describing the last error returned on this thread. */
+RNB_API const char* rnb_last_error(void);
+
+/* Bytes of workspace a call with this descriptor needs.  The workspace must
+ * be zero-filled once when allocated (rnb_moe_workspace_init does it); every
+ * call leaves its counters at zero again.  Calls that share one workspace
+ * must be ordered on one stream. */
+RNB_API int rnb_moe_workspace_size(const rnb_moe_desc* d, size_t* bytes);
+RNB_API int rnb_moe_workspace_init(void* ws, size_t ws_bytes, void* stream);
+
+/* Router half of the block: bf16 logits = x . router_w^T, top-k of those
+ * logits (ties to the lower expert index), routing weights = fp32 softmax over
+ * all E_total logits at the selected experts, renormalised to sum 1.
+ *   x        [T, H] bf16 (device)
+ *   inds     [T, k] uint32 out, slots ordered by descending logit
+ *   scores   [T, k] fp32 out
+ *   logits   [T, E_total] fp32 out (bf16-rounded values) or NULL */
+RNB_API int rnb_router_topk(const rnb_moe_desc* d, const void* x, uint32_t* inds, float* scores,
+                    float* logits, void* ws, size_t ws_bytes, void* stream);
+
+/* SwitchGLU over caller-chosen experts: for every token t and slot s,
+ *   y[t, s, :] = down_e(silu(gate_e . x_t) * (up_e . x_t)),  e = inds[t, s]
+ * unweighted, in bf16 (fp32 with RNB_FLAG_Y_F32), like
+ * FusedQuantizedSwitchGLU.__call__.
+ *   x    [T, H] bf16;  inds [T, k] uint32 global expert ids;  y [T, k, H] bf16
+ * With expert parallelism (E < E_total) slots whose expert is not in
+ * [expert_offset, expert_offset + E) are written as zeros. */
+RNB_API int rnb_switchglu_fwd(const rnb_moe_desc* d, const void* x, const uint32_t* inds, void* y,
+                      void* ws, size_t ws_bytes, void* stream);
+
+/* Whole sparse-MoE block:
+ *   out[t] = sum_s scores[t,s] * y[t,s] + sigmoid(x_t . shared_gate_w) * shared(x_t)
+ *   x [T, H] bf16 -> out [T, H] bf16; inds_out [T, k] / scores_out [T, k]
+ * are optional copies of the routing (NULL to skip). */
+RNB_API int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out,
+                      float* scores_out, void* ws, size_t ws_bytes, void* stream);
+
+/* Copies the device status word (RNB_STATUS_* bits) to *status and clears it.
+ * Synchronises the stream. */
+RNB_API int rnb_moe_status(void* ws, size_t ws_bytes, uint32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RNB_MOE_H_ */

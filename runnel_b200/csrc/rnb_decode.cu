@@ -1,0 +1,1139 @@
+// rnb_decode.cu -- sparse-MoE block for small token counts (decode, T <= 64).
+//
+// Three kernels per call, chained with programmatic dependent launch so each
+// one is resident (and streaming its weights) before its producer finishes:
+//
+//   k_route    router logits on the tensor cores (bf16 mma; one CTA per 16
+//              router rows, hidden dimension split over 16 warps and reduced
+//              in shared memory), activation prep (per-token power-of-two scale
+//              into fp16 range, per-group sums, MMA pair order), and -- in the
+//              last CTA to arrive -- top-k, softmax weights, shared-expert gate,
+//              and the per-expert token records (a counting sort).
+//   k_gateup   one CTA per (8 channels, active expert): 16 rows (8 up + 8
+//              gate) x the full hidden size, split over H/512 warps, dequantised
+//              in registers from 16-byte streaming loads into fp16 mma; SwiGLU
+//              in the epilogue.  Expert slot 0 of the grid is the shared expert.
+//   k_down     one CTA per (16 output rows, active expert): down projection
+//              from the fp32 SwiGLU activations, then -- in the last CTA to
+//              finish a row tile -- the weighted combine with the sigmoid-gated
+//              shared expert, written as bf16.
+//
+// Reference semantics: src/runnel/mlx.py:57-82 (packed gate/up, SwiGLU, down),
+// bench/mlx_lm_adapter.py:82-94 (shared expert), mlx-lm Qwen3.5 block router.
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+
+#include "rnb_common.cuh"
+#include "rnb_moe.h"
+
+namespace rnb {
+
+constexpr int kMaxDecodeT = 64;
+constexpr int kMaxE = 512;
+constexpr int kMaxK = 16;
+constexpr int kRecWords = 12;
+constexpr int kRouterWarps = 16;  // hidden-dimension split of one router tile
+constexpr int kGateUpGroupsPerWarp = 8;
+constexpr int kDownGroupsPerWarp = 4;
+
+enum Mode { kModeBlock = 0, kModeSwitchGLU = 1, kModeRouter = 2 };
+
+struct Ws {
+  uint32_t* xperm;  // [T][G][4][8] fp16 pairs (as u32)
+  float* xsum;      // [T][G]
+  float* xinv;      // [T]
+  float* logit;     // [T][E_total + 1] fp32 router logits (last = shared gate)
+  uint32_t* inds;   // [T][k]
+  float* scores;    // [T][k]
+  float* sgate;     // [T]
+  uint32_t* nact;   // [1]
+  uint32_t* rec;    // [E][kRecWords]: local expert, entry count, entry offset, 0,
+                    // then the first 8 entry ids (repeating the first past the count)
+  uint32_t* entries;  // [T*k]   entry id = t*(k+1) + slot
+  float* h;           // [T][k+1][I]
+  uint32_t* hmax;     // [T][k+1]
+  float* yws;         // [T][k+1][H]
+  uint32_t* ctr;      // [1 + H/16]
+  uint32_t* status;   // [1]
+};
+
+struct Params {
+  int T, H, I, E, E_total, off, k, has_shared, mode, y_f32;
+  int ncmax;  // columns (token slots) per MMA tile and staging buffer: min(8, T)
+  int router_ctas;
+  const uint16_t* x;
+  const uint32_t* inds_in;
+  const uint16_t* router_w;
+  const uint16_t* sgate_w;
+  const uint32_t *gu_w, *dn_w, *sgu_w, *sdn_w;
+  const uint16_t *gu_s, *gu_b, *dn_s, *dn_b, *sgu_s, *sgu_b, *sdn_s, *sdn_b;
+  void* out;  // bf16 [T][H] (block) or [T][k][H] (switchglu)
+  uint32_t* inds_out;
+  float* scores_out;
+  float* logits_out;
+  Ws ws;
+};
+
+// ----------------------------------------------------------- k_route
+
+__device__ __forceinline__ uint32_t bf16_order_key(uint16_t h) {
+  return (h & 0x8000u) ? (~static_cast<uint32_t>(h) & 0xFFFFu) : (static_cast<uint32_t>(h) | 0x8000u);
+}
+__device__ __forceinline__ uint16_t bf16_from_order_key(uint32_t k) {
+  return (k & 0x8000u) ? static_cast<uint16_t>(k & 0x7FFFu) : static_cast<uint16_t>(~k & 0xFFFFu);
+}
+
+// Router rows of one CTA: virtual rows [16*tile, 16*tile+16) of the
+// (E_total+1)-row matrix whose last row is the shared-expert gate.  Warp w
+// owns hidden range [w*H/16, (w+1)*H/16) in 32-wide chunks.
+struct RouterRegs {
+  uint4 a[4][2];  // up to 4 chunks (H <= 2048) x rows g, g+8
+};
+
+__device__ __forceinline__ const uint16_t* router_row(const Params& p, int r) {
+  if (r < p.E_total) return p.router_w + static_cast<size_t>(r) * p.H;
+  if (r == p.E_total && p.has_shared) return p.sgate_w;
+  return nullptr;
+}
+
+__device__ __forceinline__ void router_load(const Params& p, int tile, int warp, int lane, RouterRegs& rr) {
+  const int g = lane >> 2, c = lane & 3;
+  const int nch = p.H / (kRouterWarps * 32);
+  const uint16_t* pa = router_row(p, tile * 16 + g);
+  const uint16_t* pb = router_row(p, tile * 16 + g + 8);
+  const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) {
+    const int k0 = (warp * nch + ch) * 32 + 8 * c;
+    rr.a[ch][0] = (ch < nch && pa) ? ld_stream_v4(pa + k0) : z;
+    rr.a[ch][1] = (ch < nch && pb) ? ld_stream_v4(pb + k0) : z;
+  }
+}
+
+__device__ void router_cta(const Params& p, int tile, const RouterRegs& rr) {
+  __shared__ float red[kRouterWarps][16][8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int rows = p.E_total + 1;
+  const int nch = p.H / (kRouterWarps * 32);
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  for (int t0 = 0; t0 < p.T; t0 += 8) {
+    const int tb = t0 + g;
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      if (ch < nch) {
+        const int k0 = (warp * nch + ch) * 32 + 8 * c;
+        const uint4 bx = tb < p.T ? __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(tb) * p.H + k0)) : z;
+        mma_bf16(d, rr.a[ch][0].x, rr.a[ch][1].x, rr.a[ch][0].y, rr.a[ch][1].y, bx.x, bx.y);
+        mma_bf16(d, rr.a[ch][0].z, rr.a[ch][1].z, rr.a[ch][0].w, rr.a[ch][1].w, bx.z, bx.w);
+      }
+    }
+    red[warp][g][2 * c] = d[0];
+    red[warp][g][2 * c + 1] = d[1];
+    red[warp][g + 8][2 * c] = d[2];
+    red[warp][g + 8][2 * c + 1] = d[3];
+    __syncthreads();
+    if (threadIdx.x < 128) {
+      const int r = threadIdx.x & 15, n = threadIdx.x >> 4;
+      const int row = tile * 16 + r, t = t0 + n;
+      if (row < rows && t < p.T) {
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < kRouterWarps; ++w) acc += red[w][r][n];
+        p.ws.logit[static_cast<size_t>(t) * rows + row] = acc;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// One warp: activation prep for token t.  Lane handles groups lane, lane+32..
+template <int BITS>
+__device__ void xprep_warp(const Params& p, int t, int lane) {
+  const int G = p.H / kGroup;
+  const uint16_t* xr = p.x + static_cast<size_t>(t) * p.H;
+  float mx = 0.f;
+  for (int gi = lane; gi < G; gi += 32) {
+    const uint4* src = reinterpret_cast<const uint4*>(xr + gi * kGroup);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const uint4 q = __ldg(src + v);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        mx = fmaxf(mx, fabsf(__uint_as_float(w[j] << 16)));
+        mx = fmaxf(mx, fabsf(__uint_as_float(w[j] & 0xFFFF0000u)));
+      }
+    }
+  }
+  mx = warp_max(mx);
+  float scale, inv;
+  fp16_range_scale(mx, scale, inv);
+  for (int gi = lane; gi < G; gi += 32) {
+    const uint4* src = reinterpret_cast<const uint4*>(xr + gi * kGroup);
+    float v[64];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 u = __ldg(src + q);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[8 * q + 2 * j] = __half2float(__float2half_rn(__uint_as_float(w[j] << 16) * scale));
+        v[8 * q + 2 * j + 1] = __half2float(__float2half_rn(__uint_as_float(w[j] & 0xFFFF0000u) * scale));
+      }
+    }
+    float xs = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) xs += v[i];
+    uint32_t* dst = p.ws.xperm + (static_cast<size_t>(t) * G + gi) * 32;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t pr[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const __half2 h2 = __floats2half2_rn(v[pair_pos<BITS>(cc, i, 0)], v[pair_pos<BITS>(cc, i, 1)]);
+        pr[i] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      reinterpret_cast<uint4*>(dst + cc * 8)[0] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+      reinterpret_cast<uint4*>(dst + cc * 8)[1] = make_uint4(pr[4], pr[5], pr[6], pr[7]);
+    }
+    p.ws.xsum[static_cast<size_t>(t) * G + gi] = xs;
+  }
+  if (lane == 0) p.ws.xinv[t] = inv;
+}
+
+// Last CTA of k_route: routing decisions and per-expert token records.
+template <int BITS>
+__device__ void route_finalize(const Params& p) {
+  __shared__ uint32_t s_cnt[kMaxE], s_base[kMaxE], s_fill[kMaxE];
+  __shared__ float s_lg[8][kMaxE + 1];
+  __shared__ float s_p[16][kMaxK];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = p.k, rows = p.E_total + 1;
+
+  if (p.mode != kModeSwitchGLU) {
+    const int nper = (p.E_total + 31) / 32;
+    for (int t0 = 0; t0 < p.T; t0 += 8) {
+      const int nt = p.T - t0 < 8 ? p.T - t0 : 8;
+      for (int q = tid; q < nt * rows; q += blockDim.x)
+        s_lg[q / rows][q % rows] = __ldcg(p.ws.logit + static_cast<size_t>(t0) * rows + q);
+      __syncthreads();
+      if (warp < nt) {
+        const int t = t0 + warp;
+        float l[kMaxE / 32];
+        uint16_t lb[kMaxE / 32];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i) {
+          l[i] = -INFINITY;
+          lb[i] = 0;
+          const int e = lane + 32 * i;
+          if (i < nper && e < p.E_total) {
+            const __nv_bfloat16 b = __float2bfloat16_rn(s_lg[warp][e]);
+            lb[i] = __bfloat16_as_ushort(b);
+            l[i] = __bfloat162float(b);
+            mx = fmaxf(mx, l[i]);
+            if (p.logits_out) p.logits_out[static_cast<size_t>(t) * p.E_total + e] = l[i];
+          }
+        }
+        mx = warp_max(mx);
+        float den = 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxE / 32; ++i)
+          if (l[i] != -INFINITY) den += expf(l[i] - mx);
+        den = warp_sum(den);
+        uint32_t taken = 0;
+        float selsum = 0.f;
+        for (int slot = 0; slot < K; ++slot) {
+          uint32_t best = 0;
+#pragma unroll
+          for (int i = 0; i < kMaxE / 32; ++i) {
+            const int e = lane + 32 * i;
+            if (l[i] != -INFINITY && !((taken >> i) & 1u)) {
+              const uint32_t key = (bf16_order_key(lb[i]) << 16) | (0xFFFFu - static_cast<uint32_t>(e));
+              best = max(best, key);
+            }
+          }
+          const uint32_t win = warp_max_u32(best);
+          const uint32_t e_win = 0xFFFFu - (win & 0xFFFFu);
+          if ((e_win & 31u) == static_cast<uint32_t>(lane)) taken |= 1u << (e_win >> 5);
+          const float l_win = bf16_bits_to_f32(bf16_from_order_key(win >> 16));
+          const float pw = expf(l_win - mx) / den;
+          selsum += pw;
+          if (lane == 0) {
+            s_p[warp][slot] = pw;
+            p.ws.inds[t * K + slot] = e_win;
+            if (p.inds_out) p.inds_out[t * K + slot] = e_win;
+          }
+        }
+        __syncwarp();
+        if (lane < K) {
+          const float sc = s_p[warp][lane] / selsum;
+          p.ws.scores[t * K + lane] = sc;
+          if (p.scores_out) p.scores_out[t * K + lane] = sc;
+        }
+        if (lane == 0) p.ws.sgate[t] = p.has_shared ? 1.0f / (1.0f + expf(-s_lg[warp][p.E_total])) : 0.f;
+      }
+      __syncthreads();
+    }
+  } else {
+    for (int i = tid; i < p.T * K; i += blockDim.x) p.ws.inds[i] = __ldg(p.inds_in + i);
+  }
+  if (p.mode == kModeRouter) return;
+  __syncthreads();
+
+  // Counting sort of (token, slot) entries by local expert.
+  for (int i = tid; i < p.E; i += blockDim.x) {
+    s_cnt[i] = 0;
+    s_fill[i] = 0;
+  }
+  __syncthreads();
+  for (int i = tid; i < p.T * K; i += blockDim.x) {
+    const uint32_t e = p.ws.inds[i];
+    if (e >= static_cast<uint32_t>(p.E_total)) {
+      atomicOr(p.ws.status, RNB_STATUS_BAD_INDEX);
+      continue;
+    }
+    const int le = static_cast<int>(e) - p.off;
+    if (le >= 0 && le < p.E) atomicAdd(&s_cnt[le], 1u);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t running = 0, nact = 0;
+    for (int b0 = 0; b0 < p.E; b0 += 32) {
+      const int e = b0 + lane;
+      const uint32_t v = e < p.E ? s_cnt[e] : 0u;
+      uint32_t incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      const uint32_t base = running + incl - v;
+      const uint32_t flags = __ballot_sync(0xffffffffu, v > 0);
+      if (e < p.E) s_base[e] = base;
+      if (v > 0) {
+        const uint32_t pos = nact + __popc(flags & ((1u << lane) - 1u));
+        s_fill[pos] = static_cast<uint32_t>(e);  // active expert list (s_fill reused below)
+      }
+      running += __shfl_sync(0xffffffffu, incl, 31);
+      nact += __popc(flags);
+    }
+    if (lane == 0) *p.ws.nact = nact;
+  }
+  __syncthreads();
+  const uint32_t nact = *p.ws.nact;  // written by warp 0 of this CTA before the barrier
+  // active list -> records' first words; s_fill becomes the scatter cursor
+  __shared__ uint32_t s_act[kMaxE];
+  for (uint32_t a = tid; a < nact; a += blockDim.x) s_act[a] = s_fill[a];
+  __syncthreads();
+  for (int i = tid; i < p.E; i += blockDim.x) s_fill[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < p.T * K; i += blockDim.x) {
+    const uint32_t e = p.ws.inds[i];
+    if (e >= static_cast<uint32_t>(p.E_total)) continue;
+    const int le = static_cast<int>(e) - p.off;
+    if (le < 0 || le >= p.E) continue;
+    const uint32_t pos = s_base[le] + atomicAdd(&s_fill[le], 1u);
+    p.ws.entries[pos] = static_cast<uint32_t>((i / K) * (K + 1) + (i % K));
+  }
+  for (int i = tid; i < p.T * (K + 1); i += blockDim.x) p.ws.hmax[i] = 0u;
+  __syncthreads();
+  for (uint32_t a = tid; a < nact; a += blockDim.x) {
+    const uint32_t le = s_act[a], cnt = s_cnt[le], off = s_base[le];
+    uint32_t* r = p.ws.rec + a * kRecWords;
+    r[0] = le;
+    r[1] = cnt;
+    r[2] = off;
+    r[3] = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[4 + i] = p.ws.entries[off + (static_cast<uint32_t>(i) < cnt ? i : 0)];
+  }
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(512) k_route(Params p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x;
+  // Router weights are constant inputs: stream them in before waiting for the
+  // previous kernel on the stream (which may still be producing x).
+  RouterRegs rr;
+  if (b < p.router_ctas) router_load(p, b, warp, lane, rr);
+  griddep_wait();
+  griddep_launch_dependents();
+  if (b < p.router_ctas) {
+    router_cta(p, b, rr);
+  } else if (p.mode != kModeRouter) {
+    const int t = (b - p.router_ctas) * 16 + warp;
+    if (t < p.T) xprep_warp<BITS>(p, t, lane);
+  }
+  __shared__ int s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(p.ws.ctr, 1u);
+    s_last = prev == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  route_finalize<BITS>(p);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicExch(p.ws.ctr, 0u);
+  }
+}
+
+// ---------------------------------------------------- quantized tiles
+
+// One warp's weight tile in shared memory: 16 rows (MMA rows g and g+8) x NG
+// quantization groups of the warp's K range, codes plus bf16 scales/biases.
+// Rows are padded so the per-group fragment reads hit distinct banks: an
+// 8-bit group is 64 B read as 16 B per lane (8 lanes = 2 rows per phase,
+// rows 64 B apart mod 128); a 4-bit group is 32 B read as 8 B per lane
+// (16 lanes = 4 rows per phase, rows 32 B apart mod 128).
+template <int BITS, int NG>
+struct Tile {
+  static constexpr int kRowBytes = NG * 8 * BITS;
+  static constexpr int kStride = kRowBytes + (BITS == 8 ? 64 : 32);
+  static constexpr int kCodeBytes = 16 * kStride;
+  static constexpr int kParBytes = 16 * NG * 2;
+  static constexpr int kBytes = kCodeBytes + 2 * kParBytes;
+  static constexpr int kPieces = kRowBytes / 16;  // 16-byte copies per row
+};
+
+// Issues the asynchronous copies of a tile.  row(i) is the global row index
+// of tile row i; g0 the first group of the warp's K range.
+template <int BITS, int NG, typename RowOf>
+__device__ __forceinline__ void tile_issue(char* sm, const uint32_t* wbase, const uint16_t* sbase,
+                                           const uint16_t* bbase, size_t wrow, size_t srow, int g0,
+                                           RowOf row, int lane) {
+  using TL = Tile<BITS, NG>;
+  const size_t kw0 = static_cast<size_t>(g0) * kGroup * BITS / 32;  // first word of the range
+#pragma unroll 4
+  for (int q = lane; q < 16 * TL::kPieces; q += 32) {
+    const int i = q / TL::kPieces, piece = q % TL::kPieces;
+    cp_async16(sm + i * TL::kStride + piece * 16, wbase + row(i) * wrow + kw0 + piece * 4);
+  }
+  if (lane < 16) {
+    const size_t r = row(lane);
+    char* sd = sm + TL::kCodeBytes + lane * NG * 2;
+    char* bd = sd + TL::kParBytes;
+    if (NG == 8) {
+      cp_async16(sd, sbase + r * srow + g0);
+      cp_async16(bd, bbase + r * srow + g0);
+    } else {
+      cp_async8(sd, sbase + r * srow + g0);
+      cp_async8(bd, bbase + r * srow + g0);
+    }
+  }
+}
+
+// acc[0..3] (rows g/g+8 x columns 2c/2c+1) += affine(tile . B) over NG groups.
+// bfrag(gi, hi, lo) fills the 8 activation pairs of group gi for this lane's
+// column (lo only when SPLIT: a second fp16 operand added in the same
+// accumulator); gsum(gi, col) returns the group sum of column col
+// (0 -> 2c, 1 -> 2c+1).
+template <int BITS, int NG, bool SPLIT, typename BFrag, typename GSum>
+__device__ __forceinline__ void tile_mma(const char* sm, int g, int c, BFrag bfrag, GSum gsum,
+                                         float (&acc)[4]) {
+  using TL = Tile<BITS, NG>;
+  const uint16_t* S = reinterpret_cast<const uint16_t*>(sm + TL::kCodeBytes);
+  const uint16_t* B = reinterpret_cast<const uint16_t*>(sm + TL::kCodeBytes + TL::kParBytes);
+  const int q = (c == 1) ? 2 : (c == 2) ? 1 : c;
+#pragma unroll
+  for (int gi = 0; gi < NG; ++gi) {
+    RowPairs pa, pb;
+    if (BITS == 8) {
+      pa = q8_group_pairs(*reinterpret_cast<const uint4*>(sm + g * TL::kStride + gi * 64 + 16 * c));
+      pb = q8_group_pairs(*reinterpret_cast<const uint4*>(sm + (g + 8) * TL::kStride + gi * 64 + 16 * c));
+    } else {
+      pa = q4_group_pairs(*reinterpret_cast<const uint2*>(sm + g * TL::kStride + gi * 32 + 8 * q));
+      pb = q4_group_pairs(*reinterpret_cast<const uint2*>(sm + (g + 8) * TL::kStride + gi * 32 + 8 * q));
+    }
+    uint32_t xh[8], xl[8];
+    bfrag(gi, xh, xl);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xh[2 * m], xh[2 * m + 1]);
+      if (SPLIT)
+        mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xl[2 * m], xl[2 * m + 1]);
+    }
+    const float sa = bf16_bits_to_f32(S[g * NG + gi]), ba = bf16_bits_to_f32(B[g * NG + gi]);
+    const float sb = bf16_bits_to_f32(S[(g + 8) * NG + gi]), bb = bf16_bits_to_f32(B[(g + 8) * NG + gi]);
+    const float xs0 = gsum(gi, 0), xs1 = gsum(gi, 1);
+    acc[0] = fmaf(sa, d[0], fmaf(ba, xs0, acc[0]));
+    acc[1] = fmaf(sa, d[1], fmaf(ba, xs1, acc[1]));
+    acc[2] = fmaf(sb, d[2], fmaf(bb, xs0, acc[2]));
+    acc[3] = fmaf(sb, d[3], fmaf(bb, xs1, acc[3]));
+  }
+}
+
+// Work item of one grid row: expert slot j (0 = shared expert, j >= 1 =
+// j-th active routed expert).  One round trip reads the active count and the
+// expert's record (local id, entry count, entry offset, first 8 entries).
+struct Item {
+  bool active;
+  uint32_t le;   // local expert (routed)
+  int n_ent;     // (token, slot) entries
+  const uint32_t* ents;  // all entries (routed) or nullptr (shared: token t -> t*(K+1)+K)
+  uint32_t first[8];     // entries of the first column tile
+};
+
+__device__ __forceinline__ Item load_item(const Params& p, int j) {
+  Item it;
+  const int K = p.k;
+  if (j == 0) {
+    it.active = p.has_shared != 0;
+    it.le = 0;
+    it.n_ent = p.T;
+    it.ents = nullptr;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) it.first[i] = static_cast<uint32_t>((i < p.T ? i : 0) * (K + 1) + K);
+    return it;
+  }
+  const uint32_t nact = __ldcg(p.ws.nact);
+  const uint4* r = reinterpret_cast<const uint4*>(p.ws.rec + static_cast<size_t>(j - 1) * kRecWords);
+  const uint4 r0 = __ldcg(r), r1 = __ldcg(r + 1), r2 = __ldcg(r + 2);
+  it.active = static_cast<uint32_t>(j - 1) < nact;
+  it.le = r0.x;
+  it.n_ent = static_cast<int>(r0.y);
+  it.ents = p.ws.entries + r0.z;
+  it.first[0] = r1.x; it.first[1] = r1.y; it.first[2] = r1.z; it.first[3] = r1.w;
+  it.first[4] = r2.x; it.first[5] = r2.y; it.first[6] = r2.z; it.first[7] = r2.w;
+  return it;
+}
+
+// Entry id of column `lane` (lanes 0..7) of the column tile at nt; columns
+// past n_ent repeat the tile's first entry.
+__device__ __forceinline__ uint32_t lane_entry(const Item& it, int K, int nt, int lane) {
+  if (lane >= 8) return 0;
+  const int i = nt + lane < it.n_ent ? nt + lane : nt;
+  if (!it.ents) return static_cast<uint32_t>(i * (K + 1) + K);
+  if (nt == 0) {
+    uint32_t v = it.first[0];
+#pragma unroll
+    for (int q = 1; q < 8; ++q) v = (i == q) ? it.first[q] : v;
+    return v;
+  }
+  return __ldcg(it.ents + i);
+}
+
+// ---------------------------------------------------------- k_gateup
+
+constexpr int kGateUpMaxWarps = 4;  // H / 512, H <= 2048
+
+template <int BITS>
+__host__ __device__ constexpr size_t gateup_smem(int nw, int ncmax) {
+  using TL = Tile<BITS, kGateUpGroupsPerWarp>;
+  return static_cast<size_t>(nw) *
+             (TL::kBytes + ncmax * kGateUpGroupsPerWarp * 128 + ncmax * kGateUpGroupsPerWarp * 4) +
+         nw * 16 * 8 * 4;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(32 * kGateUpMaxWarps) k_gateup(Params p) {
+  constexpr int NG = kGateUpGroupsPerWarp;
+  using TL = Tile<BITS, NG>;
+  extern __shared__ __align__(16) char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int j = blockIdx.y;
+  const int ch0 = blockIdx.x * 8;
+  const int K = p.k, G = p.H / kGroup, ncmax = p.ncmax;
+  const size_t wrow = static_cast<size_t>(p.H) * BITS / 32, srow = p.H / kGroup;
+  const int g0 = warp * NG;
+  char* tile = smem + warp * TL::kBytes;
+  uint32_t* sx = reinterpret_cast<uint32_t*>(smem + nw * TL::kBytes) + warp * ncmax * NG * 32;
+  float* sxs = reinterpret_cast<float*>(smem + nw * (TL::kBytes + ncmax * NG * 128)) + warp * ncmax * NG;
+  float* red = reinterpret_cast<float*>(smem + nw * (TL::kBytes + ncmax * NG * 128 + ncmax * NG * 4));
+  // tile row i: up rows ch0..ch0+7, then gate rows I+ch0..I+ch0+7
+  auto row_of = [&](int i) -> size_t { return i < 8 ? ch0 + i : p.I + ch0 + i - 8; };
+
+  __shared__ uint32_t s_ent[8];
+  __shared__ float s_inv[8];
+  // The shared expert (grid row 0) does not depend on routing: start its
+  // copies before waiting for k_route.
+  if (j == 0) {
+    if (!p.has_shared) return;
+    tile_issue<BITS, NG>(tile, p.sgu_w, p.sgu_s, p.sgu_b, wrow, srow, g0, row_of, lane);
+  }
+  griddep_wait();
+  griddep_launch_dependents();
+  const Item it = load_item(p, j);
+  if (!it.active) return;
+  if (j != 0) {
+    const size_t ew = static_cast<size_t>(2) * p.I * wrow, es = static_cast<size_t>(2) * p.I * srow;
+    tile_issue<BITS, NG>(tile, p.gu_w + it.le * ew, p.gu_s + it.le * es, p.gu_b + it.le * es, wrow, srow,
+                         g0, row_of, lane);
+  }
+  const int n_ent = it.n_ent;
+
+  for (int nt = 0; nt < n_ent; nt += ncmax) {
+    const int ncols = n_ent - nt < ncmax ? n_ent - nt : ncmax;
+    const uint32_t ent_l = lane_entry(it, K, nt, lane);
+    if (warp == 0 && lane < 8) {
+      s_ent[lane] = ent_l;
+      s_inv[lane] = __ldcg(p.ws.xinv + ent_l / (K + 1));
+    }
+    // stage this warp's activation fragments (128 B per column and group)
+    for (int q0 = 0; q0 < ncols * NG * 8; q0 += 32) {
+      const int q = q0 + lane;
+      const int col = q / (NG * 8), rem = q % (NG * 8), gi = rem >> 3, part = rem & 7;
+      const uint32_t id = __shfl_sync(0xffffffffu, ent_l, col < 8 ? col : 0);
+      if (q < ncols * NG * 8)
+        cp_async16(sx + (col * NG + gi) * 32 + part * 4,
+                   p.ws.xperm + (static_cast<size_t>(id / (K + 1)) * G + g0 + gi) * 32 + part * 4);
+    }
+    for (int q0 = 0; q0 < ncols * NG; q0 += 32) {
+      const int q = q0 + lane;
+      const int col = q / NG, gi = q % NG;
+      const uint32_t id = __shfl_sync(0xffffffffu, ent_l, col < 8 ? col : 0);
+      if (q < ncols * NG) sxs[col * NG + gi] = __ldcg(p.ws.xsum + static_cast<size_t>(id / (K + 1)) * G + g0 + gi);
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    const int colB = g < ncols ? g : 0;
+    const int cl0 = 2 * c < ncols ? 2 * c : 0, cl1 = 2 * c + 1 < ncols ? 2 * c + 1 : 0;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    tile_mma<BITS, NG, false>(
+        tile, g, c,
+        [&](int gi, uint32_t(&xb)[8], uint32_t(&)[8]) {
+          const uint4 u0 = *reinterpret_cast<const uint4*>(sx + (colB * NG + gi) * 32 + c * 8);
+          const uint4 u1 = *reinterpret_cast<const uint4*>(sx + (colB * NG + gi) * 32 + c * 8 + 4);
+          xb[0] = u0.x; xb[1] = u0.y; xb[2] = u0.z; xb[3] = u0.w;
+          xb[4] = u1.x; xb[5] = u1.y; xb[6] = u1.z; xb[7] = u1.w;
+        },
+        [&](int gi, int col) { return sxs[(col ? cl1 : cl0) * NG + gi]; }, acc);
+    float* rw = red + warp * 128;
+    rw[g * 8 + 2 * c] = acc[0];
+    rw[g * 8 + 2 * c + 1] = acc[1];
+    rw[(g + 8) * 8 + 2 * c] = acc[2];
+    rw[(g + 8) * 8 + 2 * c + 1] = acc[3];
+    __syncthreads();
+    for (int q = threadIdx.x; q < 64; q += blockDim.x) {
+      const int r = q & 7, n = q >> 3;
+      if (n < ncols) {
+        float up = 0.f, gate = 0.f;
+        for (int w = 0; w < nw; ++w) {
+          up += red[w * 128 + r * 8 + n];
+          gate += red[w * 128 + (8 + r) * 8 + n];
+        }
+        const uint32_t id = s_ent[n];
+        const float inv = s_inv[n];
+        up *= inv;
+        gate *= inv;
+        const float hv = (gate / (1.0f + expf(-gate))) * up;
+        p.ws.h[static_cast<size_t>(id) * p.I + ch0 + r] = hv;
+        atomicMax(p.ws.hmax + id, __float_as_uint(fabsf(hv)));
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------ k_down
+
+constexpr int kDownMaxWarps = 4;  // I <= 1024
+
+template <int BITS>
+__host__ __device__ constexpr size_t down_smem(int nw, int ncmax) {
+  using TL = Tile<BITS, kDownGroupsPerWarp>;
+  return static_cast<size_t>(nw) * (TL::kBytes + ncmax * kDownGroupsPerWarp * kGroup * 4) + nw * 16 * 8 * 4;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(32 * kDownMaxWarps) k_down(Params p) {
+  constexpr int NG = kDownGroupsPerWarp;
+  using TL = Tile<BITS, NG>;
+  extern __shared__ __align__(16) char smem[];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int j = blockIdx.y;
+  const int n0 = blockIdx.x * 16;
+  const int K = p.k, ncmax = p.ncmax;
+  const size_t wrow = static_cast<size_t>(p.I) * BITS / 32, srow = p.I / kGroup;
+  const int g0 = warp * NG;
+  char* tile = smem + warp * TL::kBytes;
+  float* sh = reinterpret_cast<float*>(smem + nw * TL::kBytes) + warp * ncmax * NG * kGroup;
+  float* red = reinterpret_cast<float*>(smem + nw * (TL::kBytes + ncmax * NG * kGroup * 4));
+  auto row_of = [&](int i) -> size_t { return n0 + i; };
+
+  __shared__ uint32_t s_ent[8];
+  __shared__ float s_inv[8];
+  // k_gateup launches this grid only after k_route has completed, so the
+  // routing is readable here; the SwiGLU activations are not until the wait.
+  const Item it = load_item(p, j);
+  if (it.active && !(p.mode == kModeSwitchGLU && j == 0)) {
+    if (j == 0) {
+      tile_issue<BITS, NG>(tile, p.sdn_w, p.sdn_s, p.sdn_b, wrow, srow, g0, row_of, lane);
+    } else {
+      const size_t ew = static_cast<size_t>(p.H) * wrow, es = static_cast<size_t>(p.H) * srow;
+      tile_issue<BITS, NG>(tile, p.dn_w + it.le * ew, p.dn_s + it.le * es, p.dn_b + it.le * es, wrow, srow,
+                           g0, row_of, lane);
+    }
+  }
+  // The next call's k_route may start now: it only streams router weights
+  // until it waits for this grid to complete.
+  griddep_launch_dependents();
+  if (p.mode == kModeSwitchGLU && j == 0) {
+    // Slots routed to experts outside this bank produce zeros.
+    griddep_wait();
+    for (int i = threadIdx.x; i < p.T * K * 16; i += blockDim.x) {
+      const int slot = i / 16, r = i % 16;
+      const uint32_t e = __ldcg(p.ws.inds + slot);
+      const int le = static_cast<int>(e) - p.off;
+      if (e >= static_cast<uint32_t>(p.E_total) || le < 0 || le >= p.E) {
+        const size_t at = static_cast<size_t>(slot) * p.H + n0 + r;
+        if (p.y_f32)
+          static_cast<float*>(p.out)[at] = 0.f;
+        else
+          static_cast<__nv_bfloat16*>(p.out)[at] = __float2bfloat16_rn(0.f);
+      }
+    }
+    return;
+  }
+  if (!it.active) return;
+  griddep_wait();
+  const int n_ent = it.n_ent;
+
+  const int pbase = BITS == 8 ? 16 * c : 16 * ((c == 1) ? 2 : (c == 2) ? 1 : c);
+  for (int nt = 0; nt < n_ent; nt += ncmax) {
+    const int ncols = n_ent - nt < ncmax ? n_ent - nt : ncmax;
+    const uint32_t ent_l = lane_entry(it, K, nt, lane);
+    // stage this warp's hidden range of each column's fp32 SwiGLU output
+    constexpr int kPieces = NG * kGroup / 4;  // 16-byte pieces per column
+    for (int q0 = 0; q0 < ncols * kPieces; q0 += 32) {
+      const int q = q0 + lane;
+      const int col = q / kPieces, piece = q % kPieces;
+      const uint32_t id = __shfl_sync(0xffffffffu, ent_l, col < 8 ? col : 0);
+      if (q < ncols * kPieces)
+        cp_async16(sh + col * NG * kGroup + piece * 4, p.ws.h + static_cast<size_t>(id) * p.I + g0 * kGroup + piece * 4);
+    }
+    // per-column fp16 range scale from the column's max |h|
+    float hscale_l = 1.f, hinv_l = 1.f;
+    if (lane < 8) fp16_range_scale(__uint_as_float(__ldcg(p.ws.hmax + ent_l)), hscale_l, hinv_l);
+    if (warp == 0 && lane < 8) {
+      s_ent[lane] = ent_l;
+      s_inv[lane] = hinv_l;
+    }
+    const float hscale = __shfl_sync(0xffffffffu, hscale_l, g < ncols ? g : 0);
+    cp_async_wait_all();
+    __syncwarp();
+    const int colB = g < ncols ? g : 0;
+    float gcur = 0.f;  // group sum of this lane's column g for the group just built
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    // Activation pairs from fp32 h: scaled into fp16 range and split into a
+    // high fp16 part and the fp16 remainder, so hi + lo carries ~22 bits; the
+    // group sums use hi + lo so the affine bias term matches the products.
+    auto bfrag = [&](int gi, uint32_t(&xh)[8], uint32_t(&xl)[8]) {
+      const float* src = sh + colB * NG * kGroup + gi * kGroup + pbase;
+      float f[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 v = reinterpret_cast<const float4*>(src)[q];
+        f[4 * q] = v.x; f[4 * q + 1] = v.y; f[4 * q + 2] = v.z; f[4 * q + 3] = v.w;
+      }
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float a = f[pair_rel<BITS>(i, 0)] * hscale, b = f[pair_rel<BITS>(i, 1)] * hscale;
+        const __half2 hi = __floats2half2_rn(a, b);
+        const float2 hf = __half22float2(hi);
+        const __half2 lo = __floats2half2_rn(a - hf.x, b - hf.y);
+        const float2 lf = __half22float2(lo);
+        xh[i] = *reinterpret_cast<const uint32_t*>(&hi);
+        xl[i] = *reinterpret_cast<const uint32_t*>(&lo);
+        part += (hf.x + lf.x) + (hf.y + lf.y);
+      }
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      gcur = part;
+    };
+    auto gsum = [&](int, int col) { return __shfl_sync(0xffffffffu, gcur, (2 * c + col) * 4); };
+    tile_mma<BITS, NG, true>(tile, g, c, bfrag, gsum, acc);
+    float* rw = red + warp * 128;
+    rw[g * 8 + 2 * c] = acc[0];
+    rw[g * 8 + 2 * c + 1] = acc[1];
+    rw[(g + 8) * 8 + 2 * c] = acc[2];
+    rw[(g + 8) * 8 + 2 * c + 1] = acc[3];
+    __syncthreads();
+    for (int q = threadIdx.x; q < 128; q += blockDim.x) {
+      const int r = q & 15, n = q >> 4;
+      if (n < ncols) {
+        float y = 0.f;
+        for (int w = 0; w < nw; ++w) y += red[w * 128 + r * 8 + n];
+        const uint32_t id = s_ent[n];
+        y *= s_inv[n];
+        if (p.mode == kModeSwitchGLU) {
+          const uint32_t t = id / (K + 1), slot = id % (K + 1);
+          const size_t at = (static_cast<size_t>(t) * K + slot) * p.H + n0 + r;
+          if (p.y_f32)
+            static_cast<float*>(p.out)[at] = y;
+          else
+            static_cast<__nv_bfloat16*>(p.out)[at] = __float2bfloat16_rn(y);
+        } else {
+          p.ws.yws[static_cast<size_t>(id) * p.H + n0 + r] = y;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (p.mode == kModeSwitchGLU) return;
+
+  // Weighted combine by the last CTA to finish this 16-row tile.
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t expected = __ldcg(p.ws.nact) + (p.has_shared ? 1u : 0u);
+    const uint32_t prev = atomicAdd(p.ws.ctr + 1 + blockIdx.x, 1u);
+    s_last = prev == expected - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+  for (int i = threadIdx.x; i < p.T * 16; i += blockDim.x) {
+    const int t = i / 16, r = i % 16, n = n0 + r;
+    // issue every slot's loads before the ordered accumulation
+    uint32_t e[kMaxK];
+    float sc[kMaxK], y[kMaxK];
+#pragma unroll
+    for (int s = 0; s < kMaxK; ++s) {
+      if (s < K) {
+        e[s] = __ldcg(p.ws.inds + t * K + s);
+        sc[s] = __ldcg(p.ws.scores + t * K + s);
+        y[s] = __ldcg(p.ws.yws + (static_cast<size_t>(t) * (K + 1) + s) * p.H + n);
+      }
+    }
+    const float ysh = p.has_shared ? __ldcg(p.ws.yws + (static_cast<size_t>(t) * (K + 1) + K) * p.H + n) : 0.f;
+    const float sg = p.has_shared ? __ldcg(p.ws.sgate + t) : 0.f;
+    float acc = 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxK; ++s) {
+      if (s < K) {
+        const int le = static_cast<int>(e[s]) - p.off;
+        acc += (le >= 0 && le < p.E) ? sc[s] * y[s] : 0.f;
+      }
+    }
+    if (p.has_shared) acc += sg * ysh;
+    out[static_cast<size_t>(t) * p.H + n] = __float2bfloat16_rn(acc);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) atomicExch(p.ws.ctr + 1 + blockIdx.x, 0u);
+}
+
+// ------------------------------------------------------------- host
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+struct Layout {
+  size_t xperm, xsum, xinv, logit, inds, scores, sgate, nact, rec, entries, h,
+      hmax, yws, ctr, status, total;
+};
+
+Layout make_layout(const rnb_moe_desc& d) {
+  const size_t T = kMaxDecodeT, H = d.H, I = d.I, E = d.E, K = d.k, G = H / kGroup;
+  Layout L;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align256(o + bytes);
+    return at;
+  };
+  L.status = take(4);              // offset 0: rnb_moe_status reads it without a descriptor
+  L.ctr = take(4 * (1 + H / 16));  // arrival counters, back to zero after every call
+  L.xperm = take(T * H * 2);
+  L.xsum = take(T * G * 4);
+  L.xinv = take(T * 4);
+  L.logit = take(T * (d.E_total + 1) * 4);
+  L.inds = take(T * K * 4);
+  L.scores = take(T * K * 4);
+  L.sgate = take(T * 4);
+  L.nact = take(4);
+  L.rec = take(E * kRecWords * 4);
+  L.entries = take(T * K * 4);
+  L.h = take(T * (K + 1) * I * 4);
+  L.hmax = take(T * (K + 1) * 4);
+  L.yws = take(T * (K + 1) * H * 4);
+  L.total = o;
+  return L;
+}
+
+Ws bind(const Layout& L, void* ws) {
+  char* b = static_cast<char*>(ws);
+  Ws w;
+  w.xperm = reinterpret_cast<uint32_t*>(b + L.xperm);
+  w.xsum = reinterpret_cast<float*>(b + L.xsum);
+  w.xinv = reinterpret_cast<float*>(b + L.xinv);
+  w.logit = reinterpret_cast<float*>(b + L.logit);
+  w.inds = reinterpret_cast<uint32_t*>(b + L.inds);
+  w.scores = reinterpret_cast<float*>(b + L.scores);
+  w.sgate = reinterpret_cast<float*>(b + L.sgate);
+  w.nact = reinterpret_cast<uint32_t*>(b + L.nact);
+  w.rec = reinterpret_cast<uint32_t*>(b + L.rec);
+  w.entries = reinterpret_cast<uint32_t*>(b + L.entries);
+  w.h = reinterpret_cast<float*>(b + L.h);
+  w.hmax = reinterpret_cast<uint32_t*>(b + L.hmax);
+  w.yws = reinterpret_cast<float*>(b + L.yws);
+  w.ctr = reinterpret_cast<uint32_t*>(b + L.ctr);
+  w.status = reinterpret_cast<uint32_t*>(b + L.status);
+  return w;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int validate(const rnb_moe_desc* d, bool need_router, bool need_bank) {
+  if (!d) return fail(RNB_ERR_INVALID, "descriptor is NULL");
+  if (d->bits != 4 && d->bits != 8) return fail(RNB_ERR_INVALID, "bits must be 4 or 8");
+  if (d->group != kGroup) return fail(RNB_ERR_INVALID, "group size must be 64");
+  if (d->T < 0) return fail(RNB_ERR_INVALID, "T must be >= 0");
+  if (d->H <= 0 || d->H % 512 || d->H > 2048)
+    return fail(RNB_ERR_INVALID, "H must be 512, 1024, 1536 or 2048");
+  if (d->I <= 0 || d->I % 256 || d->I > 1024)
+    return fail(RNB_ERR_INVALID, "I must be 256, 512, 768 or 1024");
+  if (d->k <= 0 || d->k > kMaxK) return fail(RNB_ERR_INVALID, "k must be in [1, 16]");
+  if (d->E_total <= 0 || d->E_total > kMaxE || d->k > d->E_total)
+    return fail(RNB_ERR_INVALID, "E_total must be in [k, 512]");
+  if (d->E <= 0 || d->expert_offset < 0 || d->expert_offset + d->E > d->E_total)
+    return fail(RNB_ERR_INVALID, "expert shard [expert_offset, expert_offset+E) must lie in [0, E_total)");
+  if (need_bank) {
+    const void* ptrs[] = {d->gu_w, d->gu_s, d->gu_b, d->dn_w, d->dn_s, d->dn_b};
+    for (const void* q : ptrs) {
+      if (!q) return fail(RNB_ERR_INVALID, "routed expert weights must be non-NULL");
+      if (!aligned16(q)) return fail(RNB_ERR_ALIGN, "routed expert tensors must be 16-byte aligned");
+    }
+  }
+  if (need_router) {
+    if (!d->router_w) return fail(RNB_ERR_INVALID, "router_w must be non-NULL");
+    if (!aligned16(d->router_w)) return fail(RNB_ERR_ALIGN, "router_w must be 16-byte aligned");
+  }
+  return RNB_OK;
+}
+
+bool has_shared(const rnb_moe_desc* d) {
+  if (d->flags & RNB_FLAG_NO_SHARED) return false;
+  return d->shared_gate_w && d->sgu_w && d->sdn_w;
+}
+
+int check_device() {
+  static std::once_flag once;
+  static int major = -1;
+  std::call_once(once, [] {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  });
+  if (major != 10) return fail(RNB_ERR_DEVICE, "an sm_100 (B200) device is required");
+  return RNB_OK;
+}
+
+template <typename Kern>
+cudaError_t launch(Kern kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, const Params& p,
+                   size_t smem = 0) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <int BITS>
+int run_decode(const rnb_moe_desc* d, Params& p, cudaStream_t st) {
+  const int tiles = (p.E_total + 1 + 15) / 16;
+  p.router_ctas = p.mode == kModeSwitchGLU ? 0 : tiles;
+  const int prep_ctas = p.mode == kModeRouter ? 0 : (p.T + 15) / 16;
+  // Programmatic launch: k_route streams its router weights in while the
+  // previous kernel on the stream finishes, and waits before touching x.
+  cudaError_t e = launch(k_route<BITS>, dim3(p.router_ctas + prep_ctas), dim3(32 * kRouterWarps), st, true, p);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_route launch: ") + cudaGetErrorString(e));
+  if (p.mode == kModeRouter) return RNB_OK;
+  const int slots = 1 + (p.T * p.k < p.E ? p.T * p.k : p.E);
+  p.ncmax = p.T < 8 ? p.T : 8;
+  const int gnw = p.H / (kGroup * kGateUpGroupsPerWarp);
+  const size_t gsm = gateup_smem<BITS>(gnw, p.ncmax);
+  const int dnw = p.I / (kGroup * kDownGroupsPerWarp);
+  const size_t dsm = down_smem<BITS>(dnw, p.ncmax);
+  static bool attr_set = false;  // per template instance
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_gateup<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(gateup_smem<BITS>(kGateUpMaxWarps, 8)));
+    cudaFuncSetAttribute(k_down<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(down_smem<BITS>(kDownMaxWarps, 8)));
+    attr_set = true;
+  }
+  e = launch(k_gateup<BITS>, dim3(p.I / 8, slots), dim3(32 * gnw), st, true, p, gsm);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_gateup launch: ") + cudaGetErrorString(e));
+  e = launch(k_down<BITS>, dim3(p.H / 16, slots), dim3(32 * dnw), st, true, p, dsm);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_down launch: ") + cudaGetErrorString(e));
+  return RNB_OK;
+}
+
+Params base_params(const rnb_moe_desc* d, const void* x, void* ws, int mode) {
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.T = d->T;
+  p.H = d->H;
+  p.I = d->I;
+  p.E = d->E;
+  p.E_total = d->E_total;
+  p.off = d->expert_offset;
+  p.k = d->k;
+  p.mode = mode;
+  p.has_shared = (mode == kModeSwitchGLU) ? 0 : (has_shared(d) ? 1 : 0);
+  p.x = static_cast<const uint16_t*>(x);
+  p.router_w = d->router_w;
+  p.sgate_w = d->shared_gate_w;
+  p.gu_w = d->gu_w;
+  p.gu_s = d->gu_s;
+  p.gu_b = d->gu_b;
+  p.dn_w = d->dn_w;
+  p.dn_s = d->dn_s;
+  p.dn_b = d->dn_b;
+  p.sgu_w = d->sgu_w;
+  p.sgu_s = d->sgu_s;
+  p.sgu_b = d->sgu_b;
+  p.sdn_w = d->sdn_w;
+  p.sdn_s = d->sdn_s;
+  p.sdn_b = d->sdn_b;
+  p.ws = bind(make_layout(*d), ws);
+  return p;
+}
+
+int check_ws(const rnb_moe_desc* d, void* ws, size_t ws_bytes) {
+  if (!ws) return fail(RNB_ERR_WORKSPACE, "workspace is NULL");
+  if (!aligned16(ws)) return fail(RNB_ERR_ALIGN, "workspace must be 16-byte aligned");
+  if (ws_bytes < make_layout(*d).total) return fail(RNB_ERR_WORKSPACE, "workspace too small");
+  return RNB_OK;
+}
+
+// Runs [0, T) in chunks of kMaxDecodeT tokens.
+template <typename F>
+int for_chunks(const rnb_moe_desc* d, F f) {
+  for (int t0 = 0; t0 < d->T; t0 += kMaxDecodeT) {
+    rnb_moe_desc c = *d;
+    c.T = d->T - t0 < kMaxDecodeT ? d->T - t0 : kMaxDecodeT;
+    const int rc = f(c, t0);
+    if (rc != RNB_OK) return rc;
+  }
+  return RNB_OK;
+}
+
+int dispatch_bits(const rnb_moe_desc* d, Params& p, cudaStream_t st) {
+  return d->bits == 8 ? run_decode<8>(d, p, st) : run_decode<4>(d, p, st);
+}
+
+}  // namespace rnb
+
+using namespace rnb;
+
+extern "C" {
+
+int rnb_version(void) { return 100; }
+
+const char* rnb_last_error(void) { return g_last_error.c_str(); }
+
+int rnb_moe_workspace_size(const rnb_moe_desc* d, size_t* bytes) {
+  int rc = validate(d, false, false);
+  if (rc) return rc;
+  if (!bytes) return fail(RNB_ERR_INVALID, "bytes is NULL");
+  *bytes = make_layout(*d).total;
+  return RNB_OK;
+}
+
+int rnb_moe_workspace_init(void* ws, size_t ws_bytes, void* stream) {
+  if (!ws) return fail(RNB_ERR_WORKSPACE, "workspace is NULL");
+  const cudaError_t e = cudaMemsetAsync(ws, 0, ws_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, cudaGetErrorString(e));
+  return RNB_OK;
+}
+
+int rnb_router_topk(const rnb_moe_desc* d, const void* x, uint32_t* inds, float* scores,
+                    float* logits, void* ws, size_t ws_bytes, void* stream) {
+  int rc = validate(d, true, false);
+  if (!rc) rc = check_device();
+  if (!rc) rc = check_ws(d, ws, ws_bytes);
+  if (rc) return rc;
+  if (!x || !inds || !scores) return fail(RNB_ERR_INVALID, "x, inds and scores must be non-NULL");
+  if (!aligned16(x)) return fail(RNB_ERR_ALIGN, "x must be 16-byte aligned");
+  return for_chunks(d, [&](const rnb_moe_desc& c, int t0) {
+    Params p = base_params(&c, static_cast<const uint16_t*>(x) + static_cast<size_t>(t0) * c.H, ws, kModeRouter);
+    p.has_shared = has_shared(d) ? 1 : 0;
+    p.inds_out = inds + static_cast<size_t>(t0) * c.k;
+    p.scores_out = scores + static_cast<size_t>(t0) * c.k;
+    p.logits_out = logits ? logits + static_cast<size_t>(t0) * c.E_total : nullptr;
+    return dispatch_bits(&c, p, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int rnb_switchglu_fwd(const rnb_moe_desc* d, const void* x, const uint32_t* inds, void* y, void* ws,
+                      size_t ws_bytes, void* stream) {
+  int rc = validate(d, false, true);
+  if (!rc) rc = check_device();
+  if (!rc) rc = check_ws(d, ws, ws_bytes);
+  if (rc) return rc;
+  if (!x || !inds || !y) return fail(RNB_ERR_INVALID, "x, inds and y must be non-NULL");
+  if (!aligned16(x) || !aligned16(y)) return fail(RNB_ERR_ALIGN, "x and y must be 16-byte aligned");
+  return for_chunks(d, [&](const rnb_moe_desc& c, int t0) {
+    Params p = base_params(&c, static_cast<const uint16_t*>(x) + static_cast<size_t>(t0) * c.H, ws, kModeSwitchGLU);
+    p.inds_in = inds + static_cast<size_t>(t0) * c.k;
+    p.y_f32 = (d->flags & RNB_FLAG_Y_F32) ? 1 : 0;
+    p.out = p.y_f32 ? static_cast<void*>(static_cast<float*>(y) + static_cast<size_t>(t0) * c.k * c.H)
+                    : static_cast<void*>(static_cast<uint16_t*>(y) + static_cast<size_t>(t0) * c.k * c.H);
+    return dispatch_bits(&c, p, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out,
+                      float* scores_out, void* ws, size_t ws_bytes, void* stream) {
+  int rc = validate(d, true, true);
+  if (!rc) rc = check_device();
+  if (!rc) rc = check_ws(d, ws, ws_bytes);
+  if (rc) return rc;
+  if (!x || !out) return fail(RNB_ERR_INVALID, "x and out must be non-NULL");
+  if (!aligned16(x) || !aligned16(out)) return fail(RNB_ERR_ALIGN, "x and out must be 16-byte aligned");
+  if (has_shared(d)) {
+    const void* sp[] = {d->shared_gate_w, d->sgu_w, d->sgu_s, d->sgu_b, d->sdn_w, d->sdn_s, d->sdn_b};
+    for (const void* q : sp)
+      if (!q || !aligned16(q)) return fail(RNB_ERR_ALIGN, "shared-expert tensors must be non-NULL and 16-byte aligned");
+  }
+  return for_chunks(d, [&](const rnb_moe_desc& c, int t0) {
+    Params p = base_params(&c, static_cast<const uint16_t*>(x) + static_cast<size_t>(t0) * c.H, ws, kModeBlock);
+    p.out = static_cast<uint16_t*>(out) + static_cast<size_t>(t0) * c.H;
+    p.inds_out = inds_out ? inds_out + static_cast<size_t>(t0) * c.k : nullptr;
+    p.scores_out = scores_out ? scores_out + static_cast<size_t>(t0) * c.k : nullptr;
+    return dispatch_bits(&c, p, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int rnb_moe_status(void* ws, size_t ws_bytes, uint32_t* status, void* stream) {
+  if (!ws || !status) return fail(RNB_ERR_INVALID, "ws and status must be non-NULL");
+  if (ws_bytes < 4) return fail(RNB_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(status, ws, 4, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(ws, 0, 4, st);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, cudaGetErrorString(e));
+  return RNB_OK;
+}
+
+}  // extern "C"

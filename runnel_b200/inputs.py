@@ -1,0 +1,152 @@
+"""Seeded synthetic sparse-MoE blocks in MLX affine layout.
+
+One generator for the GPU path, the CPU oracle checks and the benchmarks, so
+every consumer sees identical bytes for a given (seed, shape).  Distributions
+follow the benchmark configurations of the reference's hot path (Ornith-1.5
+MoE block: H=2048, E=256 experts of I=512, top-8, group 64):
+
+* codes uniform on ``[0, 2^bits)`` -- every nibble of a 4-bit word random --
+  which makes every packed uint32 word uniform, so words are drawn directly;
+* scales ``U(0.001, 0.01)`` and biases ``N(0, 0.01)``, rounded to bf16 (RNE);
+* router and shared-expert-gate weights ``N(0, 0.02)`` in bf16;
+* activations ``x ~ N(0, 1)`` in bf16;
+* RMSNorm weights ``1 + N(0, 0.02)`` (eps 1e-6) for layer stacks.
+
+Draw order from ``numpy.random.default_rng(seed)``: x, router W, shared-gate
+W, routed gate/up (words, scales, biases), routed down (words, scales,
+biases), shared gate/up, shared down, RMSNorm weight.  Routing skews draw from
+an independent stream ``default_rng([seed, 1])`` so the weights do not change
+with the skew.
+
+Skews (data-only; the block's arithmetic is untouched):
+
+* ``"zipf"``: per-expert logit offset ``-s * log(rank_e)`` for a seeded random
+  rank permutation (s = 1.1), carried by feature ``H-1``: ``x[:, H-1] = 1`` and
+  ``router_w[:, H-1] = offset``.
+* ``"adversarial"``: a fraction (default 25%) of tokens get ``x[t, H-2] = 1``
+  and one expert gets ``router_w[e_hot, H-2] = +30`` so those tokens all route
+  to it.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .quant import f32_to_bf16_bits
+
+
+@dataclass
+class SyntheticBlock:
+    bits: int
+    group: int
+    x: np.ndarray  # [T,H] u16 (bf16 bits)
+    router_w: np.ndarray  # [E,H] u16
+    shared_gate_w: np.ndarray  # [H] u16
+    gu_w: np.ndarray  # [E,2I,H*bits/32] u32 (up rows, then gate rows)
+    gu_s: np.ndarray  # [E,2I,H/64] u16
+    gu_b: np.ndarray
+    dn_w: np.ndarray  # [E,H,I*bits/32] u32
+    dn_s: np.ndarray  # [E,H,I/64] u16
+    dn_b: np.ndarray
+    sgu_w: np.ndarray  # [2I,H*bits/32]
+    sgu_s: np.ndarray
+    sgu_b: np.ndarray
+    sdn_w: np.ndarray  # [H,I*bits/32]
+    sdn_s: np.ndarray
+    sdn_b: np.ndarray
+    norm_w: np.ndarray  # [H] fp32 RMSNorm weight
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def E(self) -> int:
+        return self.gu_w.shape[0]
+
+    @property
+    def H(self) -> int:
+        return self.dn_w.shape[1]
+
+    @property
+    def I(self) -> int:  # noqa: E743
+        return self.gu_w.shape[1] // 2
+
+    def weight_fields(self) -> dict:
+        names = ("router_w", "shared_gate_w", "gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b",
+                 "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b")
+        return {n: getattr(self, n) for n in names}
+
+
+def _words(rng, shape) -> np.ndarray:
+    return rng.integers(0, 1 << 32, size=shape, dtype=np.uint32)
+
+
+def _scales(rng, shape) -> np.ndarray:
+    return f32_to_bf16_bits(rng.uniform(0.001, 0.01, size=shape).astype(np.float32))
+
+
+def _biases(rng, shape) -> np.ndarray:
+    return f32_to_bf16_bits(rng.normal(0.0, 0.01, size=shape).astype(np.float32))
+
+
+def _bank(rng, lead, rows, K, bits, group):
+    w = _words(rng, (*lead, rows, K * bits // 32))
+    s = _scales(rng, (*lead, rows, K // group))
+    b = _biases(rng, (*lead, rows, K // group))
+    return w, s, b
+
+
+def make_block(bits: int, seed: int, T: int = 1, H: int = 2048, I: int = 512, E: int = 256,
+               group: int = 64, skew: str | None = None, zipf_s: float = 1.1,
+               adversarial_frac: float = 0.25) -> SyntheticBlock:
+    if bits not in (4, 8):
+        raise ValueError("bits must be 4 or 8")
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    router = rng.normal(0.0, 0.02, size=(E, H)).astype(np.float32)
+    sgate = rng.normal(0.0, 0.02, size=(H,)).astype(np.float32)
+    gu = _bank(rng, (E,), 2 * I, H, bits, group)
+    dn = _bank(rng, (E,), H, I, bits, group)
+    sgu = _bank(rng, (), 2 * I, H, bits, group)
+    sdn = _bank(rng, (), H, I, bits, group)
+    norm_w = (1.0 + rng.normal(0.0, 0.02, size=(H,))).astype(np.float32)
+    meta = {"bits": bits, "seed": seed, "T": T, "H": H, "I": I, "E": E, "skew": skew}
+    if skew is not None:
+        srng = np.random.default_rng([seed, 1])
+        if skew == "zipf":
+            rank = srng.permutation(E) + 1
+            offset = (-zipf_s * np.log(rank)).astype(np.float32)
+            x[:, H - 1] = 1.0
+            router[:, H - 1] = offset
+            meta["zipf_rank"] = rank
+        elif skew == "adversarial":
+            hot = int(srng.integers(0, E))
+            chosen = srng.random(T) < adversarial_frac
+            x[:, H - 2] = chosen.astype(np.float32)
+            router[:, H - 2] = 0.0
+            router[hot, H - 2] = 30.0
+            meta["hot_expert"] = hot
+            meta["hot_tokens"] = int(chosen.sum())
+        else:
+            raise ValueError(f"unknown skew {skew!r}")
+    return SyntheticBlock(
+        bits=bits, group=group, x=f32_to_bf16_bits(x), router_w=f32_to_bf16_bits(router),
+        shared_gate_w=f32_to_bf16_bits(sgate), gu_w=gu[0], gu_s=gu[1], gu_b=gu[2], dn_w=dn[0],
+        dn_s=dn[1], dn_b=dn[2], sgu_w=sgu[0], sgu_s=sgu[1], sgu_b=sgu[2], sdn_w=sdn[0],
+        sdn_s=sdn[1], sdn_b=sdn[2], norm_w=norm_w, meta=meta)
+
+
+def make_tokens(seed: int, T: int, H: int = 2048) -> np.ndarray:
+    """Extra bf16 activations ``[T,H]`` from an independent stream."""
+    rng = np.random.default_rng([seed, 2])
+    return f32_to_bf16_bits(rng.standard_normal((T, H), dtype=np.float32))
+
+
+# Benchmark configurations of the reference's hot path (seeded as listed).
+CONFIGS = {
+    1: {"bits": 8, "seed": 0, "T": 1, "name": "q8 decode T=1"},
+    2: {"bits": 4, "seed": 1, "T": 1, "name": "q4 decode T=1 and T=8", "T_alt": 8},
+    3: {"bits": 8, "seed": 2, "T": 2048, "skew": "zipf", "name": "q8 prefill T=2048 Zipf skew"},
+    4: {"bits": 4, "seed": 3, "T": 1, "layers": 40, "steps": 64,
+        "name": "40 q4 layers, 64 sequential batch-1 tokens"},
+    5: {"bits": 8, "seed": 4, "T": 16384, "name": "q8 T=16384, uniform / adversarial"},
+}

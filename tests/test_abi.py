@@ -1,0 +1,80 @@
+"""The C-ABI library loads and exports exactly what include/rnb_moe.h declares;
+host-side validation errors surface with their codes (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from runnel_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    text = open(os.path.join(ROOT, "include", "rnb_moe.h")).read()
+    return set(re.findall(r"RNB_API\s+[\w\s\*]+?\b(rnb_\w+)\s*\(", text))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert {"rnb_switchglu_fwd", "rnb_moe_block_fwd", "rnb_router_topk",
+            "rnb_moe_workspace_size", "rnb_last_error"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert set(_lib.SIGNATURES) == _declared()
+    assert lib.rnb_version() >= 100
+
+
+def test_desc_struct_matches_header_field_order():
+    text = open(os.path.join(ROOT, "include", "rnb_moe.h")).read()
+    body = text[text.index("typedef struct rnb_moe_desc"):text.index("} rnb_moe_desc;")]
+    fields = re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(\w+);", body, re.M)
+    assert fields == [f for f, _ in _lib.RnbMoeDesc._fields_]
+
+
+def _desc(**kw):
+    d = _lib.RnbMoeDesc(T=1, H=2048, I=512, E=256, E_total=256, k=8, bits=8, group=64)
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("field,value,msg", [
+    ("group", 32, "group size"),
+    ("bits", 3, "bits"),
+    ("H", 1000, "H must"),
+    ("H", 4096, "H must"),
+    ("I", 100, "I must"),
+    ("k", 0, "k must"),
+    ("E_total", 600, "E_total"),
+    ("E", 300, "expert shard"),
+    ("expert_offset", 10, "expert shard"),
+])
+def test_workspace_size_rejects_bad_shapes(field, value, msg):
+    n = ctypes.c_size_t()
+    with pytest.raises(_lib.RnbError) as ei:
+        _lib.call("rnb_moe_workspace_size", ctypes.byref(_desc(**{field: value})), ctypes.byref(n))
+    assert ei.value.code == -1 and msg in str(ei.value)
+
+
+def test_workspace_size_positive():
+    n = ctypes.c_size_t()
+    _lib.call("rnb_moe_workspace_size", ctypes.byref(_desc()), ctypes.byref(n))
+    assert n.value > 0 and n.value % 256 == 0
+
+
+def test_calls_without_device_fail_loudly():
+    # no CUDA device here (or a wrong one): the call must fail, never fall back
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    n = ctypes.c_size_t()
+    d = _desc()
+    _lib.call("rnb_moe_workspace_size", ctypes.byref(d), ctypes.byref(n))
+    rc = _lib.load().rnb_switchglu_fwd(ctypes.byref(d), 16, 16, 16, 16, n.value, None)
+    assert rc != 0
