@@ -133,6 +133,19 @@ RNB_API int rnb_switchglu_fwd(const rnb_moe_desc* d, const void* x, const uint32
 RNB_API int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out,
                       float* scores_out, void* ws, size_t ws_bytes, void* stream);
 
+/* rnb_moe_block_fwd for callers that cannot allocate device memory -- for
+ * example a host that may not call cudaMalloc while it captures a CUDA graph,
+ * or an engine plugin that owns no allocator.  It takes no workspace: scratch
+ * is a static 8 MiB device array inside this library, present on every GPU
+ * that loads it (enough for the Ornith shapes; larger shapes are rejected
+ * with RNB_ERR_WORKSPACE).  The first call on a device looks up that array's
+ * address, so make it before any stream capture.  All calls share the one
+ * array: calls that can overlap on the GPU (other streams, other threads)
+ * race and must be serialised by the caller.  No counterpart in the
+ * reference. */
+RNB_API int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void* out,
+                                      uint32_t* inds_out, float* scores_out, void* stream);
+
 /* Copies the device status word (RNB_STATUS_* bits) to *status and clears it.
  * Synchronises the stream. */
 RNB_API int rnb_moe_status(void* ws, size_t ws_bytes, uint32_t* status, void* stream);

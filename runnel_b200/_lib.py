@@ -59,6 +59,7 @@ SIGNATURES = {
     "rnb_switchglu_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _sz, _vp]),
     "rnb_moe_block_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "rnb_moe_status": (ctypes.c_int, [_vp, _sz, ctypes.POINTER(ctypes.c_uint32), _vp]),
+    "rnb_moe_block_fwd_noalloc": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp]),
 }
 
 _lib = None

@@ -1044,6 +1044,39 @@ int dispatch_bits(const rnb_moe_desc* d, Params& p, cudaStream_t st) {
 
 }  // namespace rnb
 
+namespace rnb {
+
+// Scratch for rnb_moe_block_fwd_noalloc: a file-scope device array, so a
+// caller that cannot allocate device memory still gets the workspace the
+// kernels need.  Every GPU that loads this library holds it until exit.
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB; Ornith shapes need 7.2 MB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device.  The host-side
+// name is only a stand-in, so the address is looked up once per device with
+// that device current and cached.
+int noalloc_scratch(void** out) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(RNB_ERR_DEVICE, "device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(RNB_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return RNB_OK;
+}
+
+}  // namespace rnb
+
 using namespace rnb;
 
 extern "C" {
@@ -1134,6 +1167,27 @@ int rnb_moe_status(void* ws, size_t ws_bytes, uint32_t* status, void* stream) {
   if (e == cudaSuccess) e = cudaMemsetAsync(ws, 0, 4, st);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, cudaGetErrorString(e));
   return RNB_OK;
+}
+
+int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out,
+                              float* scores_out, void* stream) {
+  int rc = validate(d, true, true);
+  if (rc) return rc;
+  const Layout L = make_layout(*d);
+  if (L.total > kNoAllocScratchBytes)
+    return fail(RNB_ERR_WORKSPACE, "rnb_moe_block_fwd_noalloc: these shapes need " + std::to_string(L.total) +
+                                       " bytes of scratch; the static scratch holds " +
+                                       std::to_string(kNoAllocScratchBytes) + " bytes");
+  rc = check_device();
+  if (rc) return rc;
+  void* ws = nullptr;
+  rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  // The status word and arrival counters must start at zero; a call leaves
+  // them at zero, but clear them so a call never depends on earlier ones.
+  const cudaError_t e = cudaMemsetAsync(ws, 0, L.xperm, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("clearing scratch counters: ") + cudaGetErrorString(e));
+  return rnb_moe_block_fwd(d, x, out, inds_out, scores_out, ws, kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"
