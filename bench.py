@@ -218,7 +218,7 @@ def run_ours(args):
     stream = torch.cuda.Stream(dev)
 
     def one(i):
-        outs[i].copy_(ops.moe_block(copies[i], xs[i], ws=ws))
+        ops.moe_block(copies[i], xs[i], ws=ws, out=outs[i])
 
     with torch.cuda.stream(stream):
         for i in range(R):
@@ -278,10 +278,12 @@ def run_ours(args):
     xh = torch.from_numpy(xs_np).view(torch.int16).view(torch.bfloat16).reshape(R, T, -1).pin_memory()
     oh = torch.empty_like(xh).pin_memory()
     xd = torch.empty((T, xs.shape[-1]), dtype=torch.bfloat16, device=dev)
+    od = torch.empty_like(xd)
     with torch.cuda.stream(stream):
         for i in range(min(R, args.warmup + 1)):
             xd.copy_(xh[i], non_blocking=True)
-            oh[i].copy_(ops.moe_block(copies[i], xd, ws=ws), non_blocking=True)
+            ops.moe_block(copies[i], xd, ws=ws, out=od)
+            oh[i].copy_(od, non_blocking=True)
     stream.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -289,7 +291,8 @@ def run_ours(args):
         for s in range(K):
             i = s % R
             xd.copy_(xh[i], non_blocking=True)
-            oh[i].copy_(ops.moe_block(copies[i], xd, ws=ws), non_blocking=True)
+            ops.moe_block(copies[i], xd, ws=ws, out=od)
+            oh[i].copy_(od, non_blocking=True)
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_us = e0.elapsed_time(e1) * 1e3 / (K * T)

@@ -92,6 +92,8 @@ typedef struct rnb_moe_desc {
                                             when the shared expert is split off) */
 #define RNB_FLAG_NO_SHARED 0x2           /* skip the shared expert even if pointers are set */
 #define RNB_FLAG_Y_F32 0x4               /* rnb_switchglu_fwd writes y as fp32 instead of bf16 */
+#define RNB_FLAG_CHAIN 0x8               /* rnb_moe_block_fwd: use the three-kernel chain even
+                                            where the persistent single-launch kernel applies */
 
 /* Library version (major*10000 + minor*100 + patch). */
 RNB_API int rnb_version(void);

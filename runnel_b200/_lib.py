@@ -29,6 +29,7 @@ STATUS_TIMEOUT = 0x2
 FLAG_SHARED_ON_THIS_RANK = 0x1
 FLAG_NO_SHARED = 0x2
 FLAG_Y_F32 = 0x4
+FLAG_CHAIN = 0x8
 
 # Every function include/rnb_moe.h declares, with its ctypes signature.
 _vp = ctypes.c_void_p

@@ -54,7 +54,7 @@ struct Ws {
                     // then the first 8 entry ids (repeating the first past the count)
   uint32_t* entries;  // [T*k]   entry id = t*(k+1) + slot
   float* h;           // [T][k+1][I]
-  uint32_t* hmax;     // [T][k+1]
+  float* hmaxp;       // [T][k+1][I/8]: max |h| of each 8-channel gate/up tile
   float* yws;         // [T][k+1][H]
   uint32_t* ctr;      // [1 + H/16]
   uint32_t* status;   // [1]
@@ -76,6 +76,22 @@ struct Params {
   float* logits_out;
   Ws ws;
 };
+
+// Optional phase timeline (compile with -DRNB_TRACE): thread 0 of each CTA
+// records %globaltimer at phase boundaries into the per-slot output area of
+// the workspace, which the persistent kernel does not otherwise use.
+#ifdef RNB_TRACE
+__device__ __forceinline__ void trace_mark(const Params& p, int i) {
+  if (threadIdx.x == 0) {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 16 + i] = t;
+  }
+}
+#define RNB_TRACE_MARK(p, i) trace_mark(p, i)
+#else
+#define RNB_TRACE_MARK(p, i) ((void)0)
+#endif
 
 // ----------------------------------------------------------- k_route
 
@@ -341,7 +357,6 @@ __device__ void route_finalize(const Params& p) {
     const uint32_t pos = s_base[le] + atomicAdd(&s_fill[le], 1u);
     p.ws.entries[pos] = static_cast<uint32_t>((i / K) * (K + 1) + (i % K));
   }
-  for (int i = tid; i < p.T * (K + 1); i += blockDim.x) p.ws.hmax[i] = 0u;
   __syncthreads();
   for (uint32_t a = tid; a < nact; a += blockDim.x) {
     const uint32_t le = s_act[a], cnt = s_cnt[le], off = s_base[le];
@@ -525,6 +540,25 @@ __device__ __forceinline__ uint32_t lane_entry(const Item& it, int K, int nt, in
   return __ldcg(it.ents + i);
 }
 
+// Max |h| of column `lane` (lanes < ncols; others get 0) from the per-tile
+// partial maxima; the warp reads all columns' partials at once.
+__device__ __forceinline__ float column_hmax(const Params& p, uint32_t ent_l, int ncols, int lane) {
+  const int nt = p.I / 8;
+  float mine = 0.f;
+#pragma unroll
+  for (int col = 0; col < 8; ++col) {
+    if (col < ncols) {
+      const uint32_t id = __shfl_sync(0xffffffffu, ent_l, col);
+      const float* src = p.ws.hmaxp + static_cast<size_t>(id) * nt;
+      float m = 0.f;
+      for (int j = lane; j < nt; j += 32) m = fmaxf(m, __ldcg(src + j));
+      m = warp_max(m);
+      if (lane == col) mine = m;
+    }
+  }
+  return mine;
+}
+
 // ---------------------------------------------------------- k_gateup
 
 constexpr int kGateUpMaxWarps = 4;  // H / 512, H <= 2048
@@ -617,22 +651,32 @@ __global__ void __launch_bounds__(32 * kGateUpMaxWarps) k_gateup(Params p) {
     rw[(g + 8) * 8 + 2 * c] = acc[2];
     rw[(g + 8) * 8 + 2 * c + 1] = acc[3];
     __syncthreads();
-    for (int q = threadIdx.x; q < 64; q += blockDim.x) {
+    // SwiGLU; each 8-channel tile also records its column maxima (one plain
+    // store per column: no atomics on shared addresses)
+    for (int q0 = 0; q0 < 64; q0 += blockDim.x) {
+      const int q = q0 + threadIdx.x;
       const int r = q & 7, n = q >> 3;
-      if (n < ncols) {
+      const bool ok = q < 64 && n < ncols;
+      float hv = 0.f;
+      uint32_t id = 0;
+      if (ok) {
         float up = 0.f, gate = 0.f;
         for (int w = 0; w < nw; ++w) {
           up += red[w * 128 + r * 8 + n];
           gate += red[w * 128 + (8 + r) * 8 + n];
         }
-        const uint32_t id = s_ent[n];
+        id = s_ent[n];
         const float inv = s_inv[n];
         up *= inv;
         gate *= inv;
-        const float hv = (gate / (1.0f + expf(-gate))) * up;
+        hv = (gate / (1.0f + expf(-gate))) * up;
         p.ws.h[static_cast<size_t>(id) * p.I + ch0 + r] = hv;
-        atomicMax(p.ws.hmax + id, __float_as_uint(fabsf(hv)));
       }
+      float m = fabsf(hv);
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+      if (ok && r == 0) p.ws.hmaxp[static_cast<size_t>(id) * (p.I / 8) + ch0 / 8] = m;
     }
     __syncthreads();
   }
@@ -719,7 +763,7 @@ __global__ void __launch_bounds__(32 * kDownMaxWarps) k_down(Params p) {
     }
     // per-column fp16 range scale from the column's max |h|
     float hscale_l = 1.f, hinv_l = 1.f;
-    if (lane < 8) fp16_range_scale(__uint_as_float(__ldcg(p.ws.hmax + ent_l)), hscale_l, hinv_l);
+    fp16_range_scale(column_hmax(p, ent_l, ncols, lane), hscale_l, hinv_l);
     if (warp == 0 && lane < 8) {
       s_ent[lane] = ent_l;
       s_inv[lane] = hinv_l;
@@ -829,6 +873,722 @@ __global__ void __launch_bounds__(32 * kDownMaxWarps) k_down(Params p) {
   if (threadIdx.x == 0) atomicExch(p.ws.ctr + 1 + blockIdx.x, 0u);
 }
 
+// ------------------------------------------------- k_decode (persistent)
+//
+// One cooperative launch, one CTA of 16 warps per SM, for small token
+// counts.  CTAs coordinate through three counters in the workspace, each
+// wait bounded in time:
+//   phase A  (no routing needed) router tiles in registers; shared-expert
+//            gate/up and shared-expert down tiles staged with cp.async;
+//            every CTA preps the activations itself in shared memory.
+//            Router CTAs publish logits and arrive on BAR1.
+//   routing  after BAR1 every CTA reads the logits and computes top-k, the
+//            weights and the per-expert token lists redundantly.
+//   phase B  routed gate/up tasks (expert x 8 channels, hidden dim split over
+//            the 16 warps) spread round-robin over CTAs and streamed through
+//            a shared-memory ring; the CTA's routed down tiles are requested
+//            first.  Each CTA arrives once on BAR2 with its task count.
+//   phase C  after BAR2 each CTA owning a 16-row output tile runs the down
+//            projection of every source (routed experts + shared expert) in
+//            K quarters, then the ordered weighted combine.
+//   exit     the last CTA to leave resets the counters.
+
+constexpr int kPWarps = 16;
+constexpr int kPMaxT = 8;
+constexpr uint64_t kSpinLimitNs = 200ull * 1000 * 1000;  // a wait gives up after 200 ms
+
+// Two-group weight tile of one warp (16 rows x 128 inputs): codes with a
+// 16-byte-chunk XOR swizzle instead of padding, then bf16 scales and biases.
+// 8-bit rows are 128 B: chunk ^= (row & 1) << 2, so the 8 lanes of a 16-byte
+// read phase (rows g, g+1) hit disjoint banks; 4-bit rows are 64 B: chunk ^=
+// ((row >> 1) & 1) << 1, so the 16 lanes of an 8-byte phase (rows g..g+3) do.
+template <int BITS>
+struct Tile2 {
+  static constexpr int kRowBytes = 2 * 8 * BITS;
+  static constexpr int kCodeBytes = 16 * kRowBytes;
+  static constexpr int kParBytes = 16 * 2 * 2;
+  static constexpr int kBytes = kCodeBytes + 2 * kParBytes;
+  static constexpr int kChunks = kRowBytes / 16;
+  __device__ static __forceinline__ int swz(int row) {
+    return BITS == 8 ? ((row & 1) << 2) : (((row >> 1) & 1) << 1);
+  }
+};
+
+template <int BITS, typename RowOf>
+__device__ __forceinline__ void tile2_issue(char* sm, const uint32_t* wbase, const uint16_t* sbase,
+                                            const uint16_t* bbase, size_t wrow, size_t srow, int g0,
+                                            RowOf row, int lane) {
+  using TL = Tile2<BITS>;
+  const size_t kw0 = static_cast<size_t>(g0) * kGroup * BITS / 32;
+#pragma unroll
+  for (int q = lane; q < 16 * TL::kChunks; q += 32) {
+    const int i = q / TL::kChunks, j = q % TL::kChunks;
+    cp_async16(sm + i * TL::kRowBytes + ((j ^ TL::swz(i)) * 16), wbase + row(i) * wrow + kw0 + j * 4);
+  }
+  if (lane < 16) {
+    const size_t r = row(lane);
+    cp_async4(sm + TL::kCodeBytes + lane * 4, sbase + r * srow + g0);
+    cp_async4(sm + TL::kCodeBytes + TL::kParBytes + lane * 4, bbase + r * srow + g0);
+  }
+}
+
+template <int BITS, bool SPLIT, typename BFrag, typename GSum>
+__device__ __forceinline__ void tile2_mma(const char* sm, int g, int c, BFrag bfrag, GSum gsum,
+                                          float (&acc)[4]) {
+  using TL = Tile2<BITS>;
+  const uint16_t* S = reinterpret_cast<const uint16_t*>(sm + TL::kCodeBytes);
+  const uint16_t* B = reinterpret_cast<const uint16_t*>(sm + TL::kCodeBytes + TL::kParBytes);
+  const int q = (c == 1) ? 2 : (c == 2) ? 1 : c;
+#pragma unroll
+  for (int gi = 0; gi < 2; ++gi) {
+    RowPairs pa, pb;
+    if (BITS == 8) {
+      const int ch = gi * 4 + c;
+      pa = q8_group_pairs(*reinterpret_cast<const uint4*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16));
+      pb = q8_group_pairs(*reinterpret_cast<const uint4*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16));
+    } else {
+      const int ch = gi * 2 + (q >> 1), off = 8 * (q & 1);
+      pa = q4_group_pairs(*reinterpret_cast<const uint2*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16 + off));
+      pb = q4_group_pairs(*reinterpret_cast<const uint2*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16 + off));
+    }
+    uint32_t xh[8], xl[8];
+    bfrag(gi, xh, xl);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xh[2 * m], xh[2 * m + 1]);
+      if (SPLIT)
+        mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xl[2 * m], xl[2 * m + 1]);
+    }
+    const float sa = bf16_bits_to_f32(S[g * 2 + gi]), ba = bf16_bits_to_f32(B[g * 2 + gi]);
+    const float sb = bf16_bits_to_f32(S[(g + 8) * 2 + gi]), bb = bf16_bits_to_f32(B[(g + 8) * 2 + gi]);
+    const float xs0 = gsum(gi, 0), xs1 = gsum(gi, 1);
+    acc[0] = fmaf(sa, d[0], fmaf(ba, xs0, acc[0]));
+    acc[1] = fmaf(sa, d[1], fmaf(ba, xs1, acc[1]));
+    acc[2] = fmaf(sb, d[2], fmaf(bb, xs0, acc[2]));
+    acc[3] = fmaf(sb, d[3], fmaf(bb, xs1, acc[3]));
+  }
+}
+
+struct PPlan {
+  int db;        // phase-B ring depth (tasks in flight per CTA)
+  int cb;        // phase-C tasks staged together per warp
+  int n_rtiles;  // router tiles of 16 rows (E_total + 1 rows)
+  uint32_t off_x, off_xs, off_br, off_cr, off_h, off_red, off_redc, off_misc;
+};
+
+struct PTask {
+  const uint32_t* ent;  // entry ids t*(K+1)+slot of the columns
+  int ncols;
+  int ch0;
+};
+
+struct PMisc {
+  uint32_t inds[kPMaxT][8];
+  float scores[kPMaxT][8];
+  float sg[kPMaxT];
+  float xinv[kPMaxT];
+  float red[kPWarps];
+  uint32_t n_act;
+  uint32_t act_e[kPMaxT * 8];
+  uint32_t act_cnt[kPMaxT * 8];
+  uint32_t act_ent[kPMaxT * 8][kPMaxT];  // entry ids t*(k+1)+slot
+  uint8_t first[kPMaxT * 8];
+  uint32_t shared_ent[8];
+  PTask tasks[4];
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void arrive_release(uint32_t* p, uint32_t n = 1) {
+  __threadfence();
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(n) : "memory");
+}
+
+// Thread 0 polls (bounded in time); the CTA continues together.  On timeout
+// the status word gets RNB_STATUS_TIMEOUT and the results of the call are void.
+__device__ void cta_wait_count(const uint32_t* ctr, uint32_t target, uint32_t* status) {
+  if (threadIdx.x == 0) {
+    uint64_t t0, now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    while (ld_acquire_gpu(ctr) < target) {
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (now - t0 > kSpinLimitNs) {
+        atomicOr(status, RNB_STATUS_TIMEOUT);
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+// wait until at most n of this thread's committed groups are pending (n <= 7)
+__device__ __forceinline__ void cp_async_wait_pending(int n) {
+  switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;\n" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;\n" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;\n" ::: "memory"); break;
+    case 3: asm volatile("cp.async.wait_group 3;\n" ::: "memory"); break;
+    case 4: asm volatile("cp.async.wait_group 4;\n" ::: "memory"); break;
+    case 5: asm volatile("cp.async.wait_group 5;\n" ::: "memory"); break;
+    case 6: asm volatile("cp.async.wait_group 6;\n" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 7;\n" ::: "memory"); break;
+  }
+}
+
+// Activation prep of T tokens (H = 2048) by the whole CTA (512 threads, 4
+// consecutive values each): power-of-two scale into fp16 range, per-group
+// sums, then the MMA pair order of Ws.xperm.  xh: 2048-half scratch.
+template <int BITS>
+__device__ void xprep_cta(const uint16_t* x, int T, uint32_t* sX, float* sXs, float* xinv, __half* xh,
+                          float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int H = 2048, G = H / kGroup;
+  for (int t = 0; t < T; ++t) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(x + static_cast<size_t>(t) * H) + tid);
+    const float v[4] = {__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                        __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u)};
+    const float m4 = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    const uint32_t mw = __reduce_max_sync(0xffffffffu, __float_as_uint(m4));  // |v| >= 0: bit order = value order
+    if (lane == 0) red[warp] = __uint_as_float(mw);
+    __syncthreads();
+    float mx = red[0];
+#pragma unroll
+    for (int q = 1; q < kPWarps; ++q) mx = fmaxf(mx, red[q]);
+    float scale, inv;
+    fp16_range_scale(mx, scale, inv);
+    const __half2 h0 = __floats2half2_rn(v[0] * scale, v[1] * scale);
+    const __half2 h1 = __floats2half2_rn(v[2] * scale, v[3] * scale);
+    reinterpret_cast<__half2*>(xh)[tid * 2] = h0;
+    reinterpret_cast<__half2*>(xh)[tid * 2 + 1] = h1;
+    const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+    float sum = (f0.x + f0.y) + (f1.x + f1.y);
+    // a 64-group is 16 consecutive threads
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+    if ((tid & 15) == 0) sXs[t * G + (tid >> 4)] = sum;
+    if (tid == 0) xinv[t] = inv;
+    __syncthreads();
+    // pair order: 32 groups x 4 lanes x 8 pairs = 1024 pairs, 2 per thread
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int q = tid + k * 512;
+      const int grp = q >> 5, cc = (q >> 3) & 3, i = q & 7;
+      const __half a = xh[grp * kGroup + pair_pos<BITS>(cc, i, 0)];
+      const __half b = xh[grp * kGroup + pair_pos<BITS>(cc, i, 1)];
+      const __half2 h2 = __halves2half2(a, b);
+      sX[(static_cast<size_t>(t) * G + grp) * 32 + cc * 8 + i] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    __syncthreads();
+  }
+}
+
+// Gate/up tasks: 16 rows = 8 up + 8 gate channels starting at ch0, tile in
+// `slot` (16 per-warp two-group tiles).  p_gateup_mma leaves this warp's
+// K-slice partial sums in red[warp]; after a CTA barrier p_gateup_epilogue
+// finishes up to 4 tasks at once (SwiGLU, activations, per-tile maxima).
+
+template <int BITS>
+__device__ __forceinline__ void p_gateup_mma(const Params& p, const char* slot, const uint32_t* sX,
+                                             const float* sXs, float* red, const PTask& tk) {
+  using TL = Tile2<BITS>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int K = p.k, G = p.H / kGroup, g0 = warp * 2, ncols = tk.ncols;
+  const int colB = g < ncols ? g : 0;
+  const int tB = static_cast<int>(tk.ent[colB] / (K + 1));
+  const int t0 = static_cast<int>(tk.ent[2 * c < ncols ? 2 * c : 0] / (K + 1));
+  const int t1 = static_cast<int>(tk.ent[2 * c + 1 < ncols ? 2 * c + 1 : 0] / (K + 1));
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  tile2_mma<BITS, false>(
+      slot + warp * TL::kBytes, g, c,
+      [&](int gi, uint32_t(&xb)[8], uint32_t(&)[8]) {
+        const uint32_t* src = sX + (static_cast<size_t>(tB) * G + g0 + gi) * 32 + c * 8;
+        const uint4 u0 = reinterpret_cast<const uint4*>(src)[0];
+        const uint4 u1 = reinterpret_cast<const uint4*>(src)[1];
+        xb[0] = u0.x; xb[1] = u0.y; xb[2] = u0.z; xb[3] = u0.w;
+        xb[4] = u1.x; xb[5] = u1.y; xb[6] = u1.z; xb[7] = u1.w;
+      },
+      [&](int gi, int col) { return sXs[(col ? t1 : t0) * G + g0 + gi]; }, acc);
+  float* rw = red + warp * 128;
+  rw[g * 8 + 2 * c] = acc[0];
+  rw[g * 8 + 2 * c + 1] = acc[1];
+  rw[(g + 8) * 8 + 2 * c] = acc[2];
+  rw[(g + 8) * 8 + 2 * c + 1] = acc[3];
+}
+
+// Threads [0, 64*nt) after a barrier: thread q -> task q/64, row q%8, column (q/8)%8.
+__device__ __forceinline__ void p_gateup_epilogue(const Params& p, const float* red, const PTask* tks,
+                                                  int nt, const float* xinv) {
+  const int q = threadIdx.x;
+  if (q >= nt * 64) return;  // whole warps: 64*nt is a multiple of 32
+  const int K = p.k;
+  const PTask& tk = tks[q >> 6];
+  const float* rt = red + (q >> 6) * kPWarps * 128;
+  const int r = q & 7, n = (q >> 3) & 7;
+  const bool ok = n < tk.ncols;
+  float hv = 0.f;
+  uint32_t id = 0;
+  if (ok) {
+    float up = 0.f, gate = 0.f;
+#pragma unroll
+    for (int w = 0; w < kPWarps; ++w) {
+      up += rt[w * 128 + r * 8 + n];
+      gate += rt[w * 128 + (8 + r) * 8 + n];
+    }
+    id = tk.ent[n];
+    const float inv = xinv[id / (K + 1)];
+    up *= inv;
+    gate *= inv;
+    hv = (gate / (1.0f + expf(-gate))) * up;
+    p.ws.h[static_cast<size_t>(id) * p.I + tk.ch0 + r] = hv;
+  }
+  float m = fabsf(hv);
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+  if (ok && r == 0) p.ws.hmaxp[static_cast<size_t>(id) * (p.I / 8) + tk.ch0 / 8] = m;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) {
+  extern __shared__ __align__(16) char sm[];
+  using TL = Tile2<BITS>;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const int cta = blockIdx.x, NC = gridDim.x;
+  const int T = p.T, K = p.k, Et = p.E_total;
+  uint32_t* sX = reinterpret_cast<uint32_t*>(sm + pl.off_x);
+  float* sXs = reinterpret_cast<float*>(sm + pl.off_xs);
+  char* sBR = sm + pl.off_br;
+  char* sCR = sm + pl.off_cr;
+  float* sH = reinterpret_cast<float*>(sm + pl.off_h);
+  float* sRed = reinterpret_cast<float*>(sm + pl.off_red);
+  float* sRedC = reinterpret_cast<float*>(sm + pl.off_redc);
+  PMisc* ms = reinterpret_cast<PMisc*>(sm + pl.off_misc);
+  const size_t task_bytes = static_cast<size_t>(kPWarps) * TL::kBytes;
+  const size_t gwrow = static_cast<size_t>(p.H) * BITS / 32, gsrow = p.H / kGroup;
+  const size_t dwrow = static_cast<size_t>(p.I) * BITS / 32, dsrow = p.I / kGroup;
+  const int n_ch = p.I / 8;
+  const int nq = p.I / 128;  // K quarters of the down projection
+  uint32_t* bar1 = p.ws.ctr + 1 + p.H / 16;
+  uint32_t* bar2 = bar1 + 1;
+  uint32_t* exitc = bar1 + 2;
+  const bool owns_router = cta < pl.n_rtiles;
+  const bool owns_sgu = p.has_shared && cta >= pl.n_rtiles && cta < pl.n_rtiles + n_ch;
+  const int n0 = cta * 16;
+  const bool owns_rows = n0 < p.H;
+  auto gu_row = [&](int ch0) { return [=](int i) -> size_t { return i < 8 ? ch0 + i : p.I + ch0 + i - 8; }; };
+  auto dn_row = [=](int i) -> size_t { return static_cast<size_t>(n0 + i); };
+
+  RNB_TRACE_MARK(p, 0);
+  // ---- phase A: requests that need no routing
+  uint4 ra[4][2];
+  if (owns_router) {
+    const uint16_t* pa = router_row(p, cta * 16 + g);
+    const uint16_t* pb = router_row(p, cta * 16 + g + 8);
+    const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      const int k0 = warp * 128 + ch * 32 + 8 * c;
+      ra[ch][0] = pa ? ld_stream_v4(pa + k0) : z;
+      ra[ch][1] = pb ? ld_stream_v4(pb + k0) : z;
+    }
+  }
+  if (owns_sgu) {
+    const int ch0 = (cta - pl.n_rtiles) * 8;
+    tile2_issue<BITS>(sBR + warp * TL::kBytes, p.sgu_w, p.sgu_s, p.sgu_b, gwrow, gsrow, warp * 2, gu_row(ch0), lane);
+  }
+  cp_async_commit();  // group: shared gate/up
+  if (owns_rows && p.has_shared && warp < nq) {
+    // phase-C slots 0..nq-1: shared expert down, K quarter = warp
+    tile2_issue<BITS>(sCR + warp * TL::kBytes, p.sdn_w, p.sdn_s, p.sdn_b, dwrow, dsrow, warp * 2, dn_row, lane);
+  }
+  cp_async_commit();  // group: shared down
+  RNB_TRACE_MARK(p, 1);
+  griddep_wait();  // x may come from the previous kernel on the stream
+  if (owns_router) {
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      const int k0 = warp * 128 + ch * 32 + 8 * c;
+      const uint4 bx = g < T ? __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(g) * p.H + k0)) : z;
+      mma_bf16(d, ra[ch][0].x, ra[ch][1].x, ra[ch][0].y, ra[ch][1].y, bx.x, bx.y);
+      mma_bf16(d, ra[ch][0].z, ra[ch][1].z, ra[ch][0].w, ra[ch][1].w, bx.z, bx.w);
+    }
+    float* rw = sRed + warp * 128;
+    rw[g * 8 + 2 * c] = d[0];
+    rw[g * 8 + 2 * c + 1] = d[1];
+    rw[(g + 8) * 8 + 2 * c] = d[2];
+    rw[(g + 8) * 8 + 2 * c + 1] = d[3];
+    __syncthreads();
+    if (tid < 128) {
+      const int r = tid & 15, n = tid >> 4, row = cta * 16 + r;
+      if (row <= Et && n < T) {
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < kPWarps; ++w) acc += sRed[w * 128 + r * 8 + n];
+        p.ws.logit[static_cast<size_t>(n) * (Et + 1) + row] = acc;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) arrive_release(bar1);
+    RNB_TRACE_MARK(p, 2);
+  }
+  xprep_cta<BITS>(p.x, T, sX, sXs, ms->xinv, reinterpret_cast<__half*>(sH), ms->red);
+
+  if (owns_sgu) {
+    cp_async_wait_pending(1);  // the shared-down group may still be in flight
+    __syncwarp();
+    if (tid < 8) ms->shared_ent[tid] = static_cast<uint32_t>((tid < T ? tid : 0) * (K + 1) + K);
+    __syncthreads();
+    const PTask tk{ms->shared_ent, T, (cta - pl.n_rtiles) * 8};
+    p_gateup_mma<BITS>(p, sBR, sX, sXs, sRed, tk);
+    __syncthreads();
+    p_gateup_epilogue(p, sRed, &tk, 1, ms->xinv);
+    __syncthreads();
+    RNB_TRACE_MARK(p, 4);
+  }
+  RNB_TRACE_MARK(p, 3);
+
+  // ---- routing (every CTA, redundantly)
+  cta_wait_count(bar1, static_cast<uint32_t>(pl.n_rtiles), p.ws.status);
+  RNB_TRACE_MARK(p, 5);
+  for (int q = tid; q < T * (Et + 1); q += blockDim.x) sH[q] = __ldcg(p.ws.logit + q);
+  __syncthreads();
+  if (warp < T) {
+    // top-k of 256 bf16 logits: unique keys (value order, then lower index),
+    // each lane keeps the best of its 8; one redux per selected expert
+    const int t = warp;
+    const float* lg = sH + t * (Et + 1);
+    uint32_t key[8];
+    float l[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      key[i] = 0;
+      l[i] = -INFINITY;
+      if (e < Et) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(lg[e]);
+        l[i] = __bfloat162float(b);
+        key[i] = (bf16_order_key(__bfloat16_as_ushort(b)) << 16) | (0xFFFFu - static_cast<uint32_t>(e));
+      }
+    }
+    uint32_t best = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) best = max(best, key[i]);
+    uint32_t mine = 0;  // lane s < K: the s-th selected key
+    for (int slot = 0; slot < K; ++slot) {
+      const uint32_t w = __reduce_max_sync(0xffffffffu, best);
+      if (lane == slot) mine = w;
+      if (best == w) {
+        best = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          key[i] = key[i] == w ? 0u : key[i];
+          best = max(best, key[i]);
+        }
+      }
+    }
+    const float mx = bf16_bits_to_f32(bf16_from_order_key(__shfl_sync(0xffffffffu, mine, 0) >> 16));
+    float den = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (l[i] != -INFINITY) den += expf(l[i] - mx);
+    den = warp_sum(den);
+    const float pw = lane < K ? expf(bf16_bits_to_f32(bf16_from_order_key(mine >> 16)) - mx) / den : 0.f;
+    const float selsum = warp_sum(pw);
+    if (lane < K) {
+      ms->inds[t][lane] = 0xFFFFu - (mine & 0xFFFFu);
+      ms->scores[t][lane] = pw / selsum;
+    }
+    if (lane == 0) ms->sg[t] = p.has_shared ? 1.0f / (1.0f + expf(-lg[Et])) : 0.f;
+  }
+  __syncthreads();
+  RNB_TRACE_MARK(p, 15);
+  // per-expert token lists: entry i = t*K + slot, ordered by (expert, i);
+  // one token: its K distinct experts in slot order
+  if (T == 1) {
+    if (tid < K) {
+      ms->act_e[tid] = ms->inds[0][tid];
+      ms->act_cnt[tid] = 1;
+      ms->act_ent[tid][0] = static_cast<uint32_t>(tid);
+    }
+    if (tid == 0) ms->n_act = static_cast<uint32_t>(K);
+  } else if (tid < T * K) {
+    const uint32_t e = ms->inds[tid / K][tid % K];
+    bool first = true;
+    for (int q = 0; q < tid; ++q)
+      if (ms->inds[q / K][q % K] == e) first = false;
+    ms->first[tid] = first;
+  }
+  __syncthreads();
+  if (T > 1 && tid < T * K) {
+    const int i = tid;
+    const uint32_t e = ms->inds[i / K][i % K];
+    uint32_t a = 0, cnt = 0, pos = 0;
+    for (int j = 0; j < T * K; ++j) {
+      const uint32_t ej = ms->inds[j / K][j % K];
+      if (ms->first[j] && ej < e) ++a;
+      if (ej == e) {
+        ++cnt;
+        if (j < i) ++pos;
+      }
+    }
+    ms->act_ent[a][pos] = static_cast<uint32_t>((i / K) * (K + 1) + (i % K));
+    if (ms->first[i]) {
+      ms->act_e[a] = e;
+      ms->act_cnt[a] = cnt;
+    }
+  }
+  if (T > 1 && tid == 0) {
+    uint32_t n = 0;
+    for (int j = 0; j < T * K; ++j) n += ms->first[j];
+    ms->n_act = n;
+  }
+  __syncthreads();
+  const int n_act = static_cast<int>(ms->n_act);
+  RNB_TRACE_MARK(p, 6);
+  if (cta == 0 && tid < T * K) {
+    const int t = tid / K, s = tid % K;
+    if (p.inds_out) p.inds_out[tid] = ms->inds[t][s];
+    if (p.scores_out) p.scores_out[tid] = ms->scores[t][s];
+  }
+
+  // ---- phase B: routed gate/up tasks i = cta, cta + NC, ...
+  const int n_btask = n_act * n_ch;
+  const int mine = n_btask > cta ? (n_btask - cta + NC - 1) / NC : 0;
+  auto issue_b = [&](int m) {
+    const int i = cta + m * NC;
+    const int a = i / n_ch, ch0 = (i % n_ch) * 8;
+    const uint32_t le = ms->act_e[a];
+    const size_t ew = static_cast<size_t>(2) * p.I * gwrow, es = static_cast<size_t>(2) * p.I * gsrow;
+    tile2_issue<BITS>(sBR + (m % pl.db) * task_bytes + warp * TL::kBytes, p.gu_w + le * ew, p.gu_s + le * es,
+                      p.gu_b + le * es, gwrow, gsrow, warp * 2, gu_row(ch0), lane);
+  };
+  // rounds of up to db tasks: all of a round's tiles resident, one barrier
+  // and one epilogue per round; the next round's copies start right after
+  for (int m = 0; m < pl.db && m < mine; ++m) issue_b(m);
+  cp_async_commit();  // group: first gate/up round
+  // phase C requests for routed experts (slots c_base.. ; shared took 0..nq-1),
+  // after the first gate/up round so that round's tiles arrive first
+  const int c_base = p.has_shared ? nq : 0;
+  const int n_ctask = c_base + nq * n_act;
+  if (owns_rows) {
+    for (int q = c_base + warp; q < n_ctask; q += kPWarps) {
+      const int a = (q - c_base) / nq, qq = (q - c_base) % nq;
+      const uint32_t le = ms->act_e[a];
+      const size_t ew = static_cast<size_t>(p.H) * dwrow, es = static_cast<size_t>(p.H) * dsrow;
+      tile2_issue<BITS>(sCR + q * TL::kBytes, p.dn_w + le * ew, p.dn_s + le * es, p.dn_b + le * es, dwrow, dsrow,
+                        qq * 2, dn_row, lane);
+    }
+  }
+  cp_async_commit();  // group: routed down
+
+  for (int r0 = 0; r0 < mine; r0 += pl.db) {
+    const int nr = mine - r0 < pl.db ? mine - r0 : pl.db;
+    cp_async_wait_pending(r0 == 0 ? 1 : 0);  // the routed-down group may stay in flight
+    __syncwarp();
+    if (tid < nr) {
+      const int i = cta + (r0 + tid) * NC, a = i / n_ch;
+      ms->tasks[tid] = PTask{ms->act_ent[a], static_cast<int>(ms->act_cnt[a]), (i % n_ch) * 8};
+    }
+    __syncthreads();
+    for (int k2 = 0; k2 < nr; ++k2)
+      p_gateup_mma<BITS>(p, sBR + ((r0 + k2) % pl.db) * task_bytes, sX, sXs, sRed + k2 * kPWarps * 128, ms->tasks[k2]);
+    __syncthreads();
+    p_gateup_epilogue(p, sRed, ms->tasks, nr, ms->xinv);
+    __syncthreads();
+    if (r0 < 4) RNB_TRACE_MARK(p, 10 + r0 / pl.db);
+    for (int m = r0 + pl.db; m < r0 + 2 * pl.db && m < mine; ++m) issue_b(m);
+    cp_async_commit();
+  }
+  // one release per CTA for all of its gate/up tasks (shared one included)
+  const uint32_t done_tasks = static_cast<uint32_t>(mine) + (owns_sgu ? 1u : 0u);
+  if (tid == 0 && done_tasks) arrive_release(bar2, done_tasks);
+  RNB_TRACE_MARK(p, 7);
+
+  // ---- phase C: down projection + combine for rows [n0, n0 + 16)
+  if (owns_rows) {
+    cp_async_wait_pending(0);
+    __syncwarp();
+    cta_wait_count(bar2, static_cast<uint32_t>(n_btask + (p.has_shared ? n_ch : 0)), p.ws.status);
+    RNB_TRACE_MARK(p, 8);
+    // this warp's tasks q = warp, warp + 16, ... in batches of pl.cb: stage
+    // each task's activations (128 per column) and column maxima (I/8 per
+    // column) with one round trip
+    const int nt_i = p.I / 8;
+    const int per_col = 128 + nt_i;
+    float* hw = sH + static_cast<size_t>(warp) * pl.cb * T * per_col;
+    for (int q0 = warp; q0 < n_ctask; q0 += kPWarps * pl.cb) {
+      uint32_t ent_b[4];
+      int nb = 0;
+      for (int bq = 0; bq < pl.cb; ++bq) {
+        const int q = q0 + bq * kPWarps;
+        if (q >= n_ctask) break;
+        const bool shared = q < c_base;
+        const int a = shared ? 0 : (q - c_base) / nq, qq = shared ? q : (q - c_base) % nq;
+        const int ncols = shared ? T : static_cast<int>(ms->act_cnt[a]);
+        uint32_t ent_l = 0;
+        if (lane < 8) {
+          const int col = lane < ncols ? lane : 0;
+          ent_l = shared ? static_cast<uint32_t>(col * (K + 1) + K) : ms->act_ent[a][col];
+        }
+        float* hq = hw + bq * T * per_col;
+        float* mq = hq + T * 128;
+        // warp-uniform trip counts: every lane reaches the shuffles
+        for (int q3 = 0; q3 < ncols * 32; q3 += 32) {  // 32 16-byte pieces per column
+          const int col = q3 >> 5, piece = lane;
+          const uint32_t id = __shfl_sync(0xffffffffu, ent_l, col);
+          cp_async16(hq + col * 128 + piece * 4, p.ws.h + static_cast<size_t>(id) * p.I + qq * 128 + piece * 4);
+        }
+        for (int q3 = 0; q3 < ncols * (nt_i / 4); q3 += 32) {
+          const int q2 = q3 + lane;
+          const int col = q2 / (nt_i / 4), piece = q2 % (nt_i / 4);
+          const uint32_t id = __shfl_sync(0xffffffffu, ent_l, col < 8 ? col : 0);
+          if (q2 < ncols * (nt_i / 4))
+            cp_async16(mq + col * nt_i + piece * 4, p.ws.hmaxp + static_cast<size_t>(id) * nt_i + piece * 4);
+        }
+        ent_b[bq] = ent_l;
+        ++nb;
+      }
+      cp_async_commit();
+      cp_async_wait_pending(0);
+      __syncwarp();
+      for (int bq = 0; bq < nb; ++bq) {
+        const int q = q0 + bq * kPWarps;
+        const bool shared = q < c_base;
+        const int a = shared ? 0 : (q - c_base) / nq, qq = shared ? q : (q - c_base) % nq;
+        const int ncols = shared ? T : static_cast<int>(ms->act_cnt[a]);
+        const uint32_t ent_l = ent_b[bq];
+        const float* hq = hw + bq * T * per_col;
+        const float* mq = hq + T * 128;
+        float cmax = 0.f;  // lane col: max |h| of column col
+        for (int col = 0; col < ncols; ++col) {
+          float m = 0.f;
+          for (int j = lane; j < nt_i; j += 32) m = fmaxf(m, mq[col * nt_i + j]);
+          m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+          if (lane == col) cmax = m;
+        }
+        float hs_l = 1.f, hi_l = 1.f;
+        fp16_range_scale(cmax, hs_l, hi_l);
+        // Convert this task's activations once, in place: per column, 128
+        // fp32 values become hi and lo fp16 fragments in MMA pair order
+        // (2 groups x 4 lane quads x 8 pairs each) and two group sums of hi+lo.
+        // Lane l converts pairs 2(l&3), 2(l&3)+1 of quad (l>>2)&3, group l>>4.
+        {
+          const int cg = lane >> 4, cq = (lane >> 2) & 3, i0 = (lane & 3) * 2;
+          const int pb = BITS == 8 ? 16 * cq : 16 * ((cq == 1) ? 2 : (cq == 2) ? 1 : cq);
+          uint32_t* frag = reinterpret_cast<uint32_t*>(const_cast<float*>(hq));
+          float* gsb = const_cast<float*>(mq);
+          for (int col = 0; col < ncols; ++col) {
+            const float sc = __shfl_sync(0xffffffffu, hs_l, col);
+            const float* src = hq + col * 128 + cg * kGroup + pb;
+            float v[4];
+#pragma unroll
+            for (int k2 = 0; k2 < 2; ++k2) {
+              v[2 * k2] = src[pair_rel<BITS>(i0 + k2, 0)] * sc;
+              v[2 * k2 + 1] = src[pair_rel<BITS>(i0 + k2, 1)] * sc;
+            }
+            __syncwarp();  // every lane has read the column before it is overwritten
+            float part = 0.f;
+#pragma unroll
+            for (int k2 = 0; k2 < 2; ++k2) {
+              const __half2 hi = __floats2half2_rn(v[2 * k2], v[2 * k2 + 1]);
+              const float2 hf = __half22float2(hi);
+              const __half2 lo = __floats2half2_rn(v[2 * k2] - hf.x, v[2 * k2 + 1] - hf.y);
+              const float2 lf = __half22float2(lo);
+              frag[col * 128 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&hi);
+              frag[col * 128 + 64 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&lo);
+              part += (hf.x + lf.x) + (hf.y + lf.y);
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            part += __shfl_xor_sync(0xffffffffu, part, 4);
+            part += __shfl_xor_sync(0xffffffffu, part, 8);
+            __syncwarp();  // column maxima were read above; group sums reuse that space
+            if ((lane & 15) == 0) gsb[col * nt_i + cg] = part;
+          }
+          __syncwarp();
+        }
+        const int colB = g < ncols ? g : 0;
+        const int cl0 = 2 * c < ncols ? 2 * c : 0, cl1 = 2 * c + 1 < ncols ? 2 * c + 1 : 0;
+        const uint32_t* fr = reinterpret_cast<const uint32_t*>(hq) + colB * 128;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        auto bfrag = [&](int gi, uint32_t(&xh)[8], uint32_t(&xl)[8]) {
+          const uint4 h0 = *reinterpret_cast<const uint4*>(fr + gi * 32 + c * 8);
+          const uint4 h1 = *reinterpret_cast<const uint4*>(fr + gi * 32 + c * 8 + 4);
+          const uint4 l0 = *reinterpret_cast<const uint4*>(fr + 64 + gi * 32 + c * 8);
+          const uint4 l1 = *reinterpret_cast<const uint4*>(fr + 64 + gi * 32 + c * 8 + 4);
+          xh[0] = h0.x; xh[1] = h0.y; xh[2] = h0.z; xh[3] = h0.w;
+          xh[4] = h1.x; xh[5] = h1.y; xh[6] = h1.z; xh[7] = h1.w;
+          xl[0] = l0.x; xl[1] = l0.y; xl[2] = l0.z; xl[3] = l0.w;
+          xl[4] = l1.x; xl[5] = l1.y; xl[6] = l1.z; xl[7] = l1.w;
+        };
+        auto gsum = [&](int gi, int col) { return mq[(col ? cl1 : cl0) * nt_i + gi]; };
+        tile2_mma<BITS, true>(sCR + q * TL::kBytes, g, c, bfrag, gsum, acc);
+        const float inv0 = __shfl_sync(0xffffffffu, hi_l, 2 * c);
+        const float inv1 = __shfl_sync(0xffffffffu, hi_l, 2 * c + 1);
+        const uint32_t id0 = __shfl_sync(0xffffffffu, ent_l, 2 * c);
+        const uint32_t id1 = __shfl_sync(0xffffffffu, ent_l, 2 * c + 1);
+        if (2 * c < ncols) {
+          float* dst = sRedC + (static_cast<size_t>(id0) * nq + qq) * 16;
+          dst[g] = acc[0] * inv0;
+          dst[g + 8] = acc[2] * inv0;
+        }
+        if (2 * c + 1 < ncols) {
+          float* dst = sRedC + (static_cast<size_t>(id1) * nq + qq) * 16;
+          dst[g] = acc[1] * inv1;
+          dst[g + 8] = acc[3] * inv1;
+        }
+      }
+    }
+    __syncthreads();
+    // each source's quarters summed in place (quarter 0 slot), then the
+    // ordered weighted sum per (token, row)
+    const int nsrc = K + (p.has_shared ? 1 : 0);
+    for (int q = tid; q < T * nsrc * 16; q += blockDim.x) {
+      const int t = q / (nsrc * 16), s = (q / 16) % nsrc, r = q % 16;
+      float* y = sRedC + static_cast<size_t>(t * (K + 1) + (s < K ? s : K)) * nq * 16;
+      float ys = 0.f;
+      for (int qq = 0; qq < nq; ++qq) ys += y[qq * 16 + r];
+      y[r] = ys;
+    }
+    __syncthreads();
+    if (tid < T * 16) {
+      const int t = tid >> 4, r = tid & 15;
+      float acc = 0.f;
+      for (int s = 0; s < K; ++s)
+        acc += ms->scores[t][s] * sRedC[static_cast<size_t>(t * (K + 1) + s) * nq * 16 + r];
+      if (p.has_shared) acc += ms->sg[t] * sRedC[static_cast<size_t>(t * (K + 1) + K) * nq * 16 + r];
+      static_cast<__nv_bfloat16*>(p.out)[static_cast<size_t>(t) * p.H + n0 + r] = __float2bfloat16_rn(acc);
+    }
+  }
+
+  RNB_TRACE_MARK(p, 9);
+  // ---- exit: the last CTA out resets the counters
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(exitc, 1u);
+    if (prev == static_cast<uint32_t>(NC - 1)) {
+      __threadfence();
+      atomicExch(bar1, 0u);
+      atomicExch(bar2, 0u);
+      atomicExch(exitc, 0u);
+      __threadfence();
+    }
+  }
+}
+
 // ------------------------------------------------------------- host
 
 thread_local std::string g_last_error;
@@ -855,7 +1615,7 @@ Layout make_layout(const rnb_moe_desc& d) {
     return at;
   };
   L.status = take(4);              // offset 0: rnb_moe_status reads it without a descriptor
-  L.ctr = take(4 * (1 + H / 16));  // arrival counters, back to zero after every call
+  L.ctr = take(4 * (4 + H / 16));  // arrival counters, back to zero after every call
   L.xperm = take(T * H * 2);
   L.xsum = take(T * G * 4);
   L.xinv = take(T * 4);
@@ -867,7 +1627,7 @@ Layout make_layout(const rnb_moe_desc& d) {
   L.rec = take(E * kRecWords * 4);
   L.entries = take(T * K * 4);
   L.h = take(T * (K + 1) * I * 4);
-  L.hmax = take(T * (K + 1) * 4);
+  L.hmax = take(T * (K + 1) * (I / 8) * 4);
   L.yws = take(T * (K + 1) * H * 4);
   L.total = o;
   return L;
@@ -887,7 +1647,7 @@ Ws bind(const Layout& L, void* ws) {
   w.rec = reinterpret_cast<uint32_t*>(b + L.rec);
   w.entries = reinterpret_cast<uint32_t*>(b + L.entries);
   w.h = reinterpret_cast<float*>(b + L.h);
-  w.hmax = reinterpret_cast<uint32_t*>(b + L.hmax);
+  w.hmaxp = reinterpret_cast<float*>(b + L.hmax);
   w.yws = reinterpret_cast<float*>(b + L.yws);
   w.ctr = reinterpret_cast<uint32_t*>(b + L.ctr);
   w.status = reinterpret_cast<uint32_t*>(b + L.status);
@@ -957,8 +1717,106 @@ cudaError_t launch(Kern kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, 
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
+struct DevInfo {
+  int sms = 0;
+  int smem_optin = 0;
+};
+
+DevInfo dev_info() {
+  static std::mutex mu;
+  static DevInfo cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  DevInfo& di = cache[dev & 63];
+  if (di.sms == 0) {
+    cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&di.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  }
+  return di;
+}
+
+// Static shared memory of k_decode (counts against the per-block limit).
+template <int BITS>
+size_t persistent_static_smem() {
+  static size_t bytes = [] {
+    cudaFuncAttributes fa;
+    return cudaFuncGetAttributes(&fa, k_decode<BITS>) == cudaSuccess ? fa.sharedSizeBytes : size_t(1024);
+  }();
+  return bytes;
+}
+
+// Shared-memory plan of k_decode; false when the call does not fit it.
+template <int BITS>
+bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem) {
+  if (p.mode != kModeBlock || p.T < 1 || p.T > kPMaxT || p.H != 2048 || p.I != 512 || p.E_total > 256 ||
+      p.k > 8 || p.off != 0 || p.E != p.E_total)
+    return false;
+  pl.n_rtiles = (p.E_total + 1 + 15) / 16;
+  if (di.sms < p.H / 16 || di.sms < pl.n_rtiles + p.I / 8) return false;
+  using TL = Tile2<BITS>;
+  const int T = p.T, G = p.H / kGroup, nq = p.I / 128;
+  const int n_ctask = nq * (1 + (p.T * p.k < p.E ? p.T * p.k : p.E));
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = (o + bytes + 127) & ~static_cast<size_t>(127);
+    return static_cast<uint32_t>(at);
+  };
+  pl.off_x = take(static_cast<size_t>(T) * G * 32 * 4);
+  pl.off_xs = take(static_cast<size_t>(T) * G * 4);
+  pl.off_misc = take(sizeof(PMisc));
+  pl.off_redc = take(static_cast<size_t>(T) * (p.k + 1) * nq * 16 * 4);
+  pl.cb = (n_ctask + kPWarps - 1) / kPWarps;  // phase-C tasks per warp, staged at once
+  if (pl.cb > 4) pl.cb = 4;
+  const size_t hbytes = static_cast<size_t>(kPWarps) * pl.cb * T * (128 + p.I / 8) * 4;
+  const size_t lbytes = static_cast<size_t>(T) * (p.E_total + 1) * 4;
+  const size_t xbytes = 2048 * 2;
+  size_t hb = hbytes > lbytes ? hbytes : lbytes;
+  hb = hb > xbytes ? hb : xbytes;
+  pl.off_h = take(hb);
+  pl.off_cr = take(static_cast<size_t>(n_ctask) * TL::kBytes);
+  const size_t task = static_cast<size_t>(kPWarps) * TL::kBytes;
+  const size_t red1 = static_cast<size_t>(kPWarps) * 128 * 4;  // partial sums of one task
+  const size_t limit = static_cast<size_t>(di.smem_optin) - persistent_static_smem<BITS>();
+  for (pl.db = 4; pl.db >= 1; --pl.db) {
+    if (o + pl.db * (task + red1) + 256 <= limit) break;
+  }
+  if (pl.db < 1) return false;
+  pl.off_red = take(pl.db * red1);
+  pl.off_br = take(pl.db * task);
+  smem = o;
+  return smem <= limit;
+}
+
+template <int BITS>
+int run_persistent(Params& p, const PPlan& pl, size_t smem, int nc, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(k_decode<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_decode smem attribute: ") + cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nc);
+  cfg.blockDim = dim3(32 * kPWarps);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, k_decode<BITS>, p, pl);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_decode launch: ") + cudaGetErrorString(e));
+  return RNB_OK;
+}
+
 template <int BITS>
 int run_decode(const rnb_moe_desc* d, Params& p, cudaStream_t st) {
+  if (p.mode == kModeBlock && !(d->flags & RNB_FLAG_CHAIN)) {
+    const DevInfo di = dev_info();
+    PPlan pl;
+    size_t smem = 0;
+    if (persistent_plan<BITS>(p, di, pl, smem)) return run_persistent<BITS>(p, pl, smem, di.sms, st);
+  }
   const int tiles = (p.E_total + 1 + 15) / 16;
   p.router_ctas = p.mode == kModeSwitchGLU ? 0 : tiles;
   const int prep_ctas = p.mode == kModeRouter ? 0 : (p.T + 15) / 16;
@@ -975,10 +1833,12 @@ int run_decode(const rnb_moe_desc* d, Params& p, cudaStream_t st) {
   const size_t dsm = down_smem<BITS>(dnw, p.ncmax);
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
-    cudaFuncSetAttribute(k_gateup<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(gateup_smem<BITS>(kGateUpMaxWarps, 8)));
-    cudaFuncSetAttribute(k_down<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(down_smem<BITS>(kDownMaxWarps, 8)));
+    e = cudaFuncSetAttribute(k_gateup<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(gateup_smem<BITS>(kGateUpMaxWarps, 8)));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_down<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(down_smem<BITS>(kDownMaxWarps, 8)));
+    if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("smem attribute: ") + cudaGetErrorString(e));
     attr_set = true;
   }
   e = launch(k_gateup<BITS>, dim3(p.I / 8, slots), dim3(32 * gnw), st, true, p, gsm);
@@ -1157,6 +2017,11 @@ int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, uint32_t*
     return dispatch_bits(&c, p, static_cast<cudaStream_t>(stream));
   });
 }
+
+#ifdef RNB_TRACE
+// Byte offset of the trace area in the workspace (trace builds only).
+RNB_API size_t rnb_trace_offset(const rnb_moe_desc* d) { return make_layout(*d).yws; }
+#endif
 
 int rnb_moe_status(void* ws, size_t ws_bytes, uint32_t* status, void* stream) {
   if (!ws || !status) return fail(RNB_ERR_INVALID, "ws and status must be non-NULL");

@@ -180,11 +180,16 @@ def switchglu(bt: BlockTensors, x: torch.Tensor, indices: torch.Tensor,
 
 
 def moe_block(bt: BlockTensors, x: torch.Tensor, k: int = 8, ws: Workspace | None = None,
-              return_routing: bool = False):
-    """Whole block ``[..., H] -> [..., H]`` bf16; optionally (out, inds, scores)."""
+              return_routing: bool = False, out: torch.Tensor | None = None):
+    """Whole block ``[..., H] -> [..., H]`` bf16; optionally (out, inds, scores).
+
+    ``out`` (contiguous bf16, x's shape) receives the result in place."""
     xt = _tokens(x, bt.H)
     T = xt.shape[0]
-    out = torch.empty_like(xt)
+    if out is None:
+        out = torch.empty_like(xt)
+    elif out.dtype != torch.bfloat16 or out.numel() != xt.numel() or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 tensor with x's number of elements")
     inds = scores = None
     if return_routing:
         inds = torch.empty((T, k), dtype=torch.int32, device=xt.device)

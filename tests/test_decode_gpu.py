@@ -188,3 +188,48 @@ def test_module_api_matches_functional():
     fused = block.switch_mlp._packed
     y = fused(x, inds)
     assert y.shape == (2, 3, 8, 2048)
+
+
+@pytest.mark.parametrize("bits,T", [(8, 1), (4, 1), (4, 2)])
+def test_persistent_kernel_matches_chain_and_oracle(bits, T):
+    """T=1 (and T=2 at 4 bits) run as one cooperative launch; the three-kernel
+    chain (RNB_FLAG_CHAIN) is the independent GPU cross-check."""
+    blk, bt, w = _setup(bits)
+    x = _x(blk, T)
+    out, inds, scores = ops.moe_block(bt, x, return_routing=True)
+    chain = ops.BlockTensors(**{**bt.__dict__, "flags": bt.flags | _lib.FLAG_CHAIN})
+    out_c, inds_c, _ = ops.moe_block(chain, x, return_routing=True)
+    ref, oinds, oscores = oracle.moe_block(w, blk.x[:T], k=8)
+    np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
+    np.testing.assert_array_equal(inds_c.cpu().numpy(), oinds)
+    np.testing.assert_allclose(scores.cpu().numpy(), oscores, rtol=2e-5, atol=1e-7)
+    assert_close(_f32(out), ref, f"persistent q{bits} T={T}")
+    assert_close(_f32(out), _f32(out_c), "persistent vs chain")
+    ws = ops.Workspace("cuda")
+    for i in range(3):  # back-to-back calls reuse the counters
+        xi = torch.from_numpy(inputs.make_tokens(9 + i, T)).view(torch.int16).view(torch.bfloat16).cuda()
+        a = ops.moe_block(bt, xi, ws=ws)
+        b = ops.moe_block(chain, xi, ws=ws)
+        assert_close(_f32(a), _f32(b), f"call {i}")
+    assert ws.status() == 0
+
+
+def test_persistent_kernel_in_cuda_graph():
+    blk, bt, w = _setup(4)
+    x = _x(blk, 1)
+    ws = ops.Workspace("cuda")
+    ref = ops.moe_block(bt, x, ws=ws)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ops.moe_block(bt, x, ws=ws)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    out = torch.empty_like(ref)
+    with torch.cuda.graph(g):
+        out.copy_(ops.moe_block(bt, x, ws=ws))
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    assert ws.status() == 0
