@@ -92,8 +92,9 @@ typedef struct rnb_moe_desc {
                                             when the shared expert is split off) */
 #define RNB_FLAG_NO_SHARED 0x2           /* skip the shared expert even if pointers are set */
 #define RNB_FLAG_Y_F32 0x4               /* rnb_switchglu_fwd writes y as fp32 instead of bf16 */
-#define RNB_FLAG_CHAIN 0x8               /* rnb_moe_block_fwd: use the three-kernel chain even
-                                            where the persistent single-launch kernel applies */
+#define RNB_FLAG_CHAIN 0x8               /* rnb_moe_block_fwd: use the three-kernel decode chain
+                                            (in 64-token chunks) even where the persistent
+                                            single-launch kernel or the prefill path applies */
 
 /* Library version (major*10000 + minor*100 + patch). */
 RNB_API int rnb_version(void);
@@ -131,7 +132,12 @@ RNB_API int rnb_switchglu_fwd(const rnb_moe_desc* d, const void* x, const uint32
 /* Whole sparse-MoE block:
  *   out[t] = sum_s scores[t,s] * y[t,s] + sigmoid(x_t . shared_gate_w) * shared(x_t)
  *   x [T, H] bf16 -> out [T, H] bf16; inds_out [T, k] / scores_out [T, k]
- * are optional copies of the routing (NULL to skip). */
+ * are optional copies of the routing (NULL to skip).  Up to 64 tokens run the
+ * decode kernels; more tokens run the sorted grouped-GEMM path (tensor-core
+ * tcgen05 GEMMs) when the workspace has rnb_moe_workspace_size() bytes for
+ * this T, else the decode kernels in 64-token chunks.  The grouped-GEMM path
+ * sums the experts' contributions with fp32 atomics, so repeated calls agree
+ * to fp32 rounding of that sum rather than bit for bit. */
 RNB_API int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out,
                       float* scores_out, void* ws, size_t ws_bytes, void* stream);
 

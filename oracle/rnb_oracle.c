@@ -24,8 +24,9 @@
  *       native/src/quantized_qmm_probe.mm:245-305
  *
  * Rounding points of the block oracle (the "fp32-accumulated result"):
- *   router logits are fp32 dot products rounded to bf16 (MLX's Linear output
- *   dtype), expert selection is top-k of those bf16 logits with ties broken
+ *   router logits are the correctly rounded bf16 (MLX's Linear output dtype)
+ *   of the exact dot product (double accumulation of exact products), expert
+ *   selection is top-k of those bf16 logits with ties broken
  *   toward the lower expert index, routing weights are the fp32 softmax over
  *   all E bf16 logits gathered at the selected experts and renormalised in
  *   fp32; everything after that (gate/up, SwiGLU, down, combine, shared
@@ -50,6 +51,36 @@ uint16_t rnbo_f32_to_bf16(float value) {
   if (((bits >> 23) & 0xFFu) == 0xFFu) return (uint16_t)(bits >> 16); /* inf/nan kept */
   bits += 0x7FFFu + ((bits >> 16) & 1u);                             /* round to nearest even */
   return (uint16_t)(bits >> 16);
+}
+
+float rnbo_bf16_to_f32(uint16_t value);
+
+/* Round a double directly to bf16 (to nearest, ties to even), returned as
+ * float; used for router logits so they are the correctly rounded bf16 of
+ * the (double-accumulated) dot product.  Magnitudes below 2^-126 are rounded
+ * through fp32; -0 becomes +0 (the selection compares values). */
+float rnbo_f64_to_bf16_f32(double v) {
+  if (v != v) return (float)v;
+  if (fabs(v) < 0x1p-126) return rnbo_bf16_to_f32(rnbo_f32_to_bf16((float)v)) + 0.0f;
+  uint64_t b;
+  memcpy(&b, &v, 8);
+  const uint64_t sign = b >> 63;
+  int e = (int)((b >> 52) & 0x7FF);
+  const uint64_t m = b & ((1ull << 52) - 1);
+  uint64_t q = m >> 45;
+  const uint64_t rem = m & ((1ull << 45) - 1), half = 1ull << 44;
+  if (rem > half || (rem == half && (q & 1))) {
+    if (++q == 128) {
+      q = 0;
+      ++e;
+    }
+  }
+  const int fe = e - 1023 + 127;
+  const uint32_t fb = fe >= 255 ? (uint32_t)(sign << 31) | 0x7F800000u
+                                : (uint32_t)(sign << 31) | ((uint32_t)fe << 23) | (uint32_t)(q << 16);
+  float out;
+  memcpy(&out, &fb, 4);
+  return out;
 }
 
 float rnbo_bf16_to_f32(uint16_t value) {
@@ -180,10 +211,13 @@ int rnbo_router(const rnbo_block* d, float* logits, int32_t* inds, float* scores
     for (int t = 0; t < T; ++t) {
       x_row_f32(d, t, xf);
       for (int e = 0; e < E; ++e) {
-        float acc = 0.0f;
+        /* bf16 x bf16 products are exact in double and the double sum of
+         * 2048 of them is far below bf16 resolution: the logit is the
+         * correctly rounded bf16 of the exact dot product */
+        double acc = 0.0;
         const uint16_t* wr = d->router_w + (size_t)e * H;
-        for (int h = 0; h < H; ++h) acc += xf[h] * rnbo_bf16_to_f32(wr[h]);
-        lg[e] = rnbo_bf16_to_f32(rnbo_f32_to_bf16(acc));
+        for (int h = 0; h < H; ++h) acc += (double)xf[h] * (double)rnbo_bf16_to_f32(wr[h]);
+        lg[e] = rnbo_f64_to_bf16_f32(acc);
         if (logits) logits[(size_t)t * E + e] = lg[e];
       }
       /* softmax over all E in fp32 (mlx-lm: softmax(gates, precise=True)) */

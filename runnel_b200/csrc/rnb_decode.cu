@@ -27,6 +27,8 @@
 #include <string>
 
 #include "rnb_common.cuh"
+#include "rnb_route.cuh"
+#include "rnb_internal.h"
 #include "rnb_moe.h"
 
 namespace rnb {
@@ -95,13 +97,6 @@ __device__ __forceinline__ void trace_mark(const Params& p, int i) {
 
 // ----------------------------------------------------------- k_route
 
-__device__ __forceinline__ uint32_t bf16_order_key(uint16_t h) {
-  return (h & 0x8000u) ? (~static_cast<uint32_t>(h) & 0xFFFFu) : (static_cast<uint32_t>(h) | 0x8000u);
-}
-__device__ __forceinline__ uint16_t bf16_from_order_key(uint32_t k) {
-  return (k & 0x8000u) ? static_cast<uint16_t>(k & 0x7FFFu) : static_cast<uint16_t>(~k & 0xFFFFu);
-}
-
 // Router rows of one CTA: virtual rows [16*tile, 16*tile+16) of the
 // (E_total+1)-row matrix whose last row is the shared-expert gate.  Warp w
 // owns hidden range [w*H/16, (w+1)*H/16) in 32-wide chunks.
@@ -131,6 +126,7 @@ __device__ __forceinline__ void router_load(const Params& p, int tile, int warp,
 
 __device__ void router_cta(const Params& p, int tile, const RouterRegs& rr) {
   __shared__ float red[kRouterWarps][16][8];
+  __shared__ float s_norm[kRouterWarps][48];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int rows = p.E_total + 1;
@@ -139,6 +135,7 @@ __device__ void router_cta(const Params& p, int tile, const RouterRegs& rr) {
   for (int t0 = 0; t0 < p.T; t0 += 8) {
     const int tb = t0 + g;
     float d[4] = {0.f, 0.f, 0.f, 0.f};
+    RouterNorms rn;
 #pragma unroll
     for (int ch = 0; ch < 4; ++ch) {
       if (ch < nch) {
@@ -146,8 +143,11 @@ __device__ void router_cta(const Params& p, int tile, const RouterRegs& rr) {
         const uint4 bx = tb < p.T ? __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(tb) * p.H + k0)) : z;
         mma_bf16(d, rr.a[ch][0].x, rr.a[ch][1].x, rr.a[ch][0].y, rr.a[ch][1].y, bx.x, bx.y);
         mma_bf16(d, rr.a[ch][0].z, rr.a[ch][1].z, rr.a[ch][0].w, rr.a[ch][1].w, bx.z, bx.w);
+        rn.add(bx, rr.a[ch][0], rr.a[ch][1]);
       }
     }
+    rn.reduce_quad();
+    if (c == 0) rn.store(s_norm[warp], g);
     red[warp][g][2 * c] = d[0];
     red[warp][g][2 * c + 1] = d[1];
     red[warp][g + 8][2 * c] = d[2];
@@ -160,7 +160,9 @@ __device__ void router_cta(const Params& p, int tile, const RouterRegs& rr) {
         float acc = 0.f;
 #pragma unroll
         for (int w = 0; w < kRouterWarps; ++w) acc += red[w][r][n];
-        p.ws.logit[static_cast<size_t>(t) * rows + row] = acc;
+        // expert rows: candidate interval of the bf16 logit; last row: fp32 shared-gate logit
+        reinterpret_cast<uint32_t*>(p.ws.logit)[static_cast<size_t>(t) * rows + row] =
+            row < p.E_total ? router_interval_from(&s_norm[0][0], kRouterWarps, r, n, acc) : __float_as_uint(acc);
       }
     }
     __syncthreads();
@@ -227,69 +229,28 @@ template <int BITS>
 __device__ void route_finalize(const Params& p) {
   __shared__ uint32_t s_cnt[kMaxE], s_base[kMaxE], s_fill[kMaxE];
   __shared__ float s_lg[8][kMaxE + 1];
-  __shared__ float s_p[16][kMaxK];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = p.k, rows = p.E_total + 1;
 
   if (p.mode != kModeSwitchGLU) {
-    const int nper = (p.E_total + 31) / 32;
     for (int t0 = 0; t0 < p.T; t0 += 8) {
       const int nt = p.T - t0 < 8 ? p.T - t0 : 8;
       for (int q = tid; q < nt * rows; q += blockDim.x)
-        s_lg[q / rows][q % rows] = __ldcg(p.ws.logit + static_cast<size_t>(t0) * rows + q);
+        reinterpret_cast<uint32_t*>(&s_lg[q / rows][0])[q % rows] =
+            __ldcg(reinterpret_cast<const uint32_t*>(p.ws.logit) + static_cast<size_t>(t0) * rows + q);
       __syncthreads();
       if (warp < nt) {
         const int t = t0 + warp;
-        float l[kMaxE / 32];
-        uint16_t lb[kMaxE / 32];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < kMaxE / 32; ++i) {
-          l[i] = -INFINITY;
-          lb[i] = 0;
-          const int e = lane + 32 * i;
-          if (i < nper && e < p.E_total) {
-            const __nv_bfloat16 b = __float2bfloat16_rn(s_lg[warp][e]);
-            lb[i] = __bfloat16_as_ushort(b);
-            l[i] = __bfloat162float(b);
-            mx = fmaxf(mx, l[i]);
-            if (p.logits_out) p.logits_out[static_cast<size_t>(t) * p.E_total + e] = l[i];
-          }
-        }
-        mx = warp_max(mx);
-        float den = 0.f;
-#pragma unroll
-        for (int i = 0; i < kMaxE / 32; ++i)
-          if (l[i] != -INFINITY) den += expf(l[i] - mx);
-        den = warp_sum(den);
-        uint32_t taken = 0;
-        float selsum = 0.f;
-        for (int slot = 0; slot < K; ++slot) {
-          uint32_t best = 0;
-#pragma unroll
-          for (int i = 0; i < kMaxE / 32; ++i) {
-            const int e = lane + 32 * i;
-            if (l[i] != -INFINITY && !((taken >> i) & 1u)) {
-              const uint32_t key = (bf16_order_key(lb[i]) << 16) | (0xFFFFu - static_cast<uint32_t>(e));
-              best = max(best, key);
-            }
-          }
-          const uint32_t win = warp_max_u32(best);
-          const uint32_t e_win = 0xFFFFu - (win & 0xFFFFu);
-          if ((e_win & 31u) == static_cast<uint32_t>(lane)) taken |= 1u << (e_win >> 5);
-          const float l_win = bf16_bits_to_f32(bf16_from_order_key(win >> 16));
-          const float pw = expf(l_win - mx) / den;
-          selsum += pw;
-          if (lane == 0) {
-            s_p[warp][slot] = pw;
-            p.ws.inds[t * K + slot] = e_win;
-            if (p.inds_out) p.inds_out[t * K + slot] = e_win;
-          }
-        }
-        __syncwarp();
+        int e;
+        float sc;
+        // a caller asking for the logits gets every one resolved exactly
+        warp_route_token(reinterpret_cast<const uint32_t*>(s_lg[warp]), p.E_total, K,
+                         p.x + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane, p.logits_out != nullptr,
+                         p.logits_out ? p.logits_out + static_cast<size_t>(t) * p.E_total : nullptr, &e, &sc);
         if (lane < K) {
-          const float sc = s_p[warp][lane] / selsum;
+          p.ws.inds[t * K + lane] = static_cast<uint32_t>(e);
           p.ws.scores[t * K + lane] = sc;
+          if (p.inds_out) p.inds_out[t * K + lane] = static_cast<uint32_t>(e);
           if (p.scores_out) p.scores_out[t * K + lane] = sc;
         }
         if (lane == 0) p.ws.sgate[t] = p.has_shared ? 1.0f / (1.0f + expf(-s_lg[warp][p.E_total])) : 0.f;
@@ -996,6 +957,7 @@ struct PMisc {
   uint8_t first[kPMaxT * 8];
   uint32_t shared_ent[8];
   PTask tasks[4];
+  float rnorm[kPWarps][48];  // router tile partials: per token sum x^2, max|x|; per row sum w^2, sum |w|
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
@@ -1217,13 +1179,17 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   if (owns_router) {
     const uint4 z = make_uint4(0, 0, 0, 0);
     float d[4] = {0.f, 0.f, 0.f, 0.f};
+    RouterNorms rn;
 #pragma unroll
     for (int ch = 0; ch < 4; ++ch) {
       const int k0 = warp * 128 + ch * 32 + 8 * c;
       const uint4 bx = g < T ? __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(g) * p.H + k0)) : z;
       mma_bf16(d, ra[ch][0].x, ra[ch][1].x, ra[ch][0].y, ra[ch][1].y, bx.x, bx.y);
       mma_bf16(d, ra[ch][0].z, ra[ch][1].z, ra[ch][0].w, ra[ch][1].w, bx.z, bx.w);
+      rn.add(bx, ra[ch][0], ra[ch][1]);
     }
+    rn.reduce_quad();
+    if (c == 0) rn.store(ms->rnorm[warp], g);
     float* rw = sRed + warp * 128;
     rw[g * 8 + 2 * c] = d[0];
     rw[g * 8 + 2 * c + 1] = d[1];
@@ -1236,7 +1202,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
         float acc = 0.f;
 #pragma unroll
         for (int w = 0; w < kPWarps; ++w) acc += sRed[w * 128 + r * 8 + n];
-        p.ws.logit[static_cast<size_t>(n) * (Et + 1) + row] = acc;
+        reinterpret_cast<uint32_t*>(p.ws.logit)[static_cast<size_t>(n) * (Et + 1) + row] =
+            row < Et ? router_interval_from(&ms->rnorm[0][0], kPWarps, r, n, acc) : __float_as_uint(acc);
       }
     }
     __syncthreads();
@@ -1262,55 +1229,20 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   // ---- routing (every CTA, redundantly)
   cta_wait_count(bar1, static_cast<uint32_t>(pl.n_rtiles), p.ws.status);
   RNB_TRACE_MARK(p, 5);
-  for (int q = tid; q < T * (Et + 1); q += blockDim.x) sH[q] = __ldcg(p.ws.logit + q);
+  for (int q = tid; q < T * (Et + 1); q += blockDim.x)
+    reinterpret_cast<uint32_t*>(sH)[q] = __ldcg(reinterpret_cast<const uint32_t*>(p.ws.logit) + q);
   __syncthreads();
   if (warp < T) {
-    // top-k of 256 bf16 logits: unique keys (value order, then lower index),
-    // each lane keeps the best of its 8; one redux per selected expert
     const int t = warp;
-    const float* lg = sH + t * (Et + 1);
-    uint32_t key[8];
-    float l[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int e = lane + 32 * i;
-      key[i] = 0;
-      l[i] = -INFINITY;
-      if (e < Et) {
-        const __nv_bfloat16 b = __float2bfloat16_rn(lg[e]);
-        l[i] = __bfloat162float(b);
-        key[i] = (bf16_order_key(__bfloat16_as_ushort(b)) << 16) | (0xFFFFu - static_cast<uint32_t>(e));
-      }
-    }
-    uint32_t best = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) best = max(best, key[i]);
-    uint32_t mine = 0;  // lane s < K: the s-th selected key
-    for (int slot = 0; slot < K; ++slot) {
-      const uint32_t w = __reduce_max_sync(0xffffffffu, best);
-      if (lane == slot) mine = w;
-      if (best == w) {
-        best = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          key[i] = key[i] == w ? 0u : key[i];
-          best = max(best, key[i]);
-        }
-      }
-    }
-    const float mx = bf16_bits_to_f32(bf16_from_order_key(__shfl_sync(0xffffffffu, mine, 0) >> 16));
-    float den = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (l[i] != -INFINITY) den += expf(l[i] - mx);
-    den = warp_sum(den);
-    const float pw = lane < K ? expf(bf16_bits_to_f32(bf16_from_order_key(mine >> 16)) - mx) / den : 0.f;
-    const float selsum = warp_sum(pw);
+    const uint32_t* ivl = reinterpret_cast<const uint32_t*>(sH + t * (Et + 1));
+    int e;
+    float sc;
+    warp_route_token(ivl, Et, K, p.x + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane, false, nullptr, &e, &sc);
     if (lane < K) {
-      ms->inds[t][lane] = 0xFFFFu - (mine & 0xFFFFu);
-      ms->scores[t][lane] = pw / selsum;
+      ms->inds[t][lane] = static_cast<uint32_t>(e);
+      ms->scores[t][lane] = sc;
     }
-    if (lane == 0) ms->sg[t] = p.has_shared ? 1.0f / (1.0f + expf(-lg[Et])) : 0.f;
+    if (lane == 0) ms->sg[t] = p.has_shared ? 1.0f / (1.0f + expf(-sH[t * (Et + 1) + Et])) : 0.f;
   }
   __syncthreads();
   RNB_TRACE_MARK(p, 15);
@@ -1614,8 +1546,8 @@ Layout make_layout(const rnb_moe_desc& d) {
     o = align256(o + bytes);
     return at;
   };
-  L.status = take(4);              // offset 0: rnb_moe_status reads it without a descriptor
-  L.ctr = take(4 * (4 + H / 16));  // arrival counters, back to zero after every call
+  L.status = take(4);                // offset 0: rnb_moe_status reads it without a descriptor
+  L.ctr = take(ws_counter_bytes(d));  // arrival counters, back to zero after every call
   L.xperm = take(T * H * 2);
   L.xsum = take(T * G * 4);
   L.xinv = take(T * 4);
@@ -1630,6 +1562,7 @@ Layout make_layout(const rnb_moe_desc& d) {
   L.hmax = take(T * (K + 1) * (I / 8) * 4);
   L.yws = take(T * (K + 1) * H * 4);
   L.total = o;
+  static_assert(kWsCountersOffset == 256, "status word takes the first 256-byte slot");
   return L;
 }
 
@@ -1716,11 +1649,6 @@ cudaError_t launch(Kern kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, 
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
-
-struct DevInfo {
-  int sms = 0;
-  int smem_optin = 0;
-};
 
 DevInfo dev_info() {
   static std::mutex mu;
@@ -1949,7 +1877,12 @@ int rnb_moe_workspace_size(const rnb_moe_desc* d, size_t* bytes) {
   int rc = validate(d, false, false);
   if (rc) return rc;
   if (!bytes) return fail(RNB_ERR_INVALID, "bytes is NULL");
-  *bytes = make_layout(*d).total;
+  size_t n = make_layout(*d).total;
+  if (d->T > kMaxDecodeT && prefill_supported(*d)) {
+    const size_t pn = prefill_workspace_bytes(*d);
+    n = pn > n ? pn : n;
+  }
+  *bytes = n;
   return RNB_OK;
 }
 
@@ -2009,6 +1942,11 @@ int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, uint32_t*
     for (const void* q : sp)
       if (!q || !aligned16(q)) return fail(RNB_ERR_ALIGN, "shared-expert tensors must be non-NULL and 16-byte aligned");
   }
+  // Many tokens: the sorted grouped-GEMM (tcgen05) path, when the workspace
+  // was sized for it; otherwise the decode kernels in 64-token chunks.
+  if (d->T > kMaxDecodeT && !(d->flags & RNB_FLAG_CHAIN) && prefill_supported(*d) &&
+      ws_bytes >= prefill_workspace_bytes(*d))
+    return run_prefill(d, x, out, inds_out, scores_out, ws, ws_bytes, static_cast<cudaStream_t>(stream));
   return for_chunks(d, [&](const rnb_moe_desc& c, int t0) {
     Params p = base_params(&c, static_cast<const uint16_t*>(x) + static_cast<size_t>(t0) * c.H, ws, kModeBlock);
     p.out = static_cast<uint16_t*>(out) + static_cast<size_t>(t0) * c.H;

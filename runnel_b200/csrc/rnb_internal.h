@@ -1,0 +1,39 @@
+// rnb_internal.h -- host-side helpers shared by the decode and prefill units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "rnb_moe.h"
+
+namespace rnb {
+
+// Records the message for rnb_last_error() and returns code.
+int fail(int code, const std::string& msg);
+bool aligned16(const void* p);
+bool has_shared(const rnb_moe_desc* d);
+
+struct DevInfo {
+  int sms = 0;
+  int smem_optin = 0;
+};
+DevInfo dev_info();
+
+// Every workspace starts with the status word (offset 0) and, at offset 256,
+// the decode kernels' arrival counters, which each decode call leaves at zero
+// for the next; both layouts reserve this header so any call may follow any
+// other on one workspace.
+constexpr size_t kWsCountersOffset = 256;
+inline size_t ws_counter_bytes(const rnb_moe_desc& d) { return 4u * (4u + static_cast<size_t>(d.H) / 16u); }
+
+// Prefill path (many tokens): workspace bytes it needs for d->T tokens, and
+// whether it supports the descriptor's shapes.
+size_t prefill_workspace_bytes(const rnb_moe_desc& d);
+bool prefill_supported(const rnb_moe_desc& d);
+int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out, float* scores_out,
+                void* ws, size_t ws_bytes, cudaStream_t st);
+
+}  // namespace rnb

@@ -1,0 +1,845 @@
+// rnb_prefill.cu -- sparse-MoE block for many tokens (prefill) on tcgen05.
+//
+//   k_pre_route    router logits (mma.sync bf16, 64 tokens per CTA, x staged
+//                  in shared memory), top-k, softmax weights, shared-expert
+//                  gate, per-token power-of-two scale into fp16 range, and a
+//                  per-expert token histogram.
+//   k_pre_sort     one CTA: per-expert row bases padded to 128-row tiles and
+//                  the m-tile list (the shared expert is expert E, all tokens).
+//   k_pre_scatter  (token, slot) entries -> expert-sorted rows (counting sort).
+//   k_pre_gemm<0>  grouped gate/up GEMM: 128 rows x (128 up + 128 gate)
+//                  channels per work item, K = H in 64-wide stages.
+//   k_pre_gemm<1>  grouped down GEMM: 128 rows x 128 outputs, K = I.
+//   k_pre_final    fp32 accumulator -> bf16 output.
+//
+// k_pre_gemm is warp-specialised: 8 producer warps fill a 4/6-stage shared
+// memory ring (activations converted to fp16, MLX affine weights dequantised
+// straight to fp16 with one fused multiply-add per pair: w = s*q + b rounded
+// once), one thread of warp 8 issues tcgen05.mma (M=128, fp16 x fp16 -> fp32
+// in tensor memory), warps 9-12 drain the accumulator.  The gate/up epilogue
+// applies SwiGLU and stores the activations as fp16 scaled by a power of two
+// per (row, 128 channels); the down GEMM keeps one accumulator per such
+// 128-channel chunk so each chunk's scale is undone exactly, then adds
+// score * y into an fp32 [T, H] accumulator with vector atomics (the order
+// of those additions is not fixed, so results are reproducible to fp32
+// rounding rather than bit-exact).
+//
+// Reference semantics: src/runnel/mlx.py:57-82 (sorted gather_qmm when
+// indices.size >= 64), bench/mlx_lm_adapter.py:82-94 (shared expert).
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+
+#include "rnb_common.cuh"
+#include "rnb_route.cuh"
+#include "rnb_internal.h"
+#include "rnb_moe.h"
+#include "rnb_umma.cuh"
+
+namespace rnb {
+namespace pre {
+
+constexpr int kTileM = 128;
+constexpr int kRouteT = 64;     // tokens per router CTA
+constexpr int kProducerWarps = 8;
+constexpr int kMmaWarp = 8;
+// warps 9..12: epilogue, one per TMEM lane quadrant (warp % 4)
+constexpr int kThreads = 13 * 32;
+constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;
+constexpr int kMaxE = 256;
+constexpr int kMaxK = 8;
+
+struct Ws {
+  uint32_t* status;
+  uint32_t* counts;  // [E+1] rows per local expert (index E: shared expert)
+  uint32_t* fill;    // [E+1]
+  uint32_t* base;    // [E+1] first sorted row
+  uint32_t* n_mt;    // [1] number of 128-row tiles
+  uint4* tiles;      // [max_mt] (expert, row0, nrows, 0)
+  uint32_t* perm;    // [rows_cap] entry id t*(K+1)+slot, 0xFFFFFFFF for padding
+  uint32_t* inds;    // [T][K]
+  float* scores;     // [T][K]
+  float* sg;         // [T]
+  float* xscale;     // [T] power of two bringing max|x_t| into [2^14, 2^15)
+  __half* h16;       // [rows_cap][I] SwiGLU activations, scaled
+  float* hinv;       // [rows_cap][I/128] inverse scale of each 128-channel chunk
+  float* acc;        // [T][H] fp32 output accumulator
+};
+
+struct Params {
+  int T, H, I, E, E_total, off, k, has_shared;
+  int rows_cap, max_mt;
+  const uint16_t* x;
+  const uint16_t* router_w;
+  const uint16_t* sgate_w;
+  const uint32_t *gu_w, *dn_w, *sgu_w, *sdn_w;
+  const uint16_t *gu_s, *gu_b, *dn_s, *dn_b, *sgu_s, *sgu_b, *sdn_s, *sdn_b;
+  __nv_bfloat16* out;
+  uint32_t* inds_out;
+  float* scores_out;
+  Ws ws;
+};
+
+// ------------------------------------------------------------ router
+
+constexpr int kXStride = 160;  // bf16 per staged x row (128 + 32 pad: conflict-free 16-byte reads)
+
+constexpr size_t kRouteXsBytes = 2ull * kRouteT * kXStride * 2;
+constexpr size_t kRouteLgBytes = static_cast<size_t>(kRouteT) * (kMaxE + 1) * 4;
+constexpr size_t kRouteSmem = kRouteXsBytes > kRouteLgBytes ? kRouteXsBytes : kRouteLgBytes;
+
+__global__ void __launch_bounds__(512) k_pre_route(Params p) {
+  // x staging (K loop) and the logits (after it) share one dynamic buffer
+  extern __shared__ __align__(16) char rsm[];
+  uint16_t (*xs)[kRouteT][kXStride] = reinterpret_cast<uint16_t (*)[kRouteT][kXStride]>(rsm);
+  float (*lg)[kMaxE + 1] = reinterpret_cast<float (*)[kMaxE + 1]>(rsm);
+  __shared__ uint32_t xmax[kRouteT];
+  __shared__ float xn2[kRouteT];
+  __shared__ uint32_t hist[kMaxE];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const int t0 = blockIdx.x * kRouteT;
+  const int nt = p.T - t0 < kRouteT ? p.T - t0 : kRouteT;
+  const int Et = p.E_total, K = p.k, H = p.H;
+  const int nkc = H / 128;
+  for (int i = tid; i < kMaxE; i += blockDim.x) hist[i] = 0;
+  if (tid < kRouteT) {
+    xmax[tid] = 0;
+    xn2[tid] = 0.f;
+  }
+  auto stage = [&](int kc, int buf) {
+    // 64 rows x 128 bf16 = 1024 16-byte pieces, two per thread
+    for (int q = tid; q < kRouteT * 16; q += blockDim.x) {
+      const int r = q >> 4, piece = q & 15;
+      const int tr = r < nt ? r : 0;
+      cp_async16(&xs[buf][r][piece * 8], p.x + static_cast<size_t>(t0 + tr) * H + kc * 128 + piece * 8);
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+  float acc[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  float wa2 = 0.f, wa1 = 0.f, wb2 = 0.f, wb1 = 0.f;  // norms of rows row_a, row_b (lane's quarter)
+  const int row_a = warp * 16 + g, row_b = row_a + 8;
+  const uint16_t* wa = row_a < Et ? p.router_w + static_cast<size_t>(row_a) * H : nullptr;
+  const uint16_t* wb = row_b < Et ? p.router_w + static_cast<size_t>(row_b) * H : nullptr;
+  stage(0, 0);
+  for (int kc = 0; kc < nkc; ++kc) {
+    if (kc + 1 < nkc) {
+      stage(kc + 1, (kc + 1) & 1);
+      asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    }
+    __syncthreads();
+    const int buf = kc & 1;
+    // per-token max |x| over this chunk
+    for (int q = tid; q < kRouteT * 16; q += blockDim.x) {
+      const int r = q >> 4, piece = q & 15;
+      const uint4 v = *reinterpret_cast<const uint4*>(&xs[buf][r][piece * 8]);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      float m = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xFFFF0000u);
+        m = fmaxf(m, fmaxf(fabsf(lo), fabsf(hi)));
+        s2 = fmaf(lo, lo, fmaf(hi, hi, s2));
+      }
+      atomicMax(&xmax[r], __float_as_uint(m));
+      atomicAdd(&xn2[r], s2);
+    }
+    if (warp * 16 < Et) {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        const int k0 = kc * 128 + ch * 32 + 8 * c;
+        const uint4 a0 = wa ? __ldg(reinterpret_cast<const uint4*>(wa + k0)) : z;
+        const uint4 a1 = wb ? __ldg(reinterpret_cast<const uint4*>(wb + k0)) : z;
+        {
+          const uint32_t av[4] = {a0.x, a0.y, a0.z, a0.w}, bv[4] = {a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float x0 = __uint_as_float(av[j] << 16), x1 = __uint_as_float(av[j] & 0xFFFF0000u);
+            const float y0 = __uint_as_float(bv[j] << 16), y1 = __uint_as_float(bv[j] & 0xFFFF0000u);
+            wa2 = fmaf(x0, x0, fmaf(x1, x1, wa2));
+            wa1 += fabsf(x0) + fabsf(x1);
+            wb2 = fmaf(y0, y0, fmaf(y1, y1, wb2));
+            wb1 += fabsf(y0) + fabsf(y1);
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const uint4 bx = *reinterpret_cast<const uint4*>(&xs[buf][n * 8 + g][ch * 32 + 8 * c]);
+          mma_bf16(acc[n], a0.x, a1.x, a0.y, a1.y, bx.x, bx.y);
+          mma_bf16(acc[n], a0.z, a1.z, a0.w, a1.w, bx.z, bx.w);
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    wa2 += __shfl_xor_sync(0xffffffffu, wa2, o);
+    wa1 += __shfl_xor_sync(0xffffffffu, wa1, o);
+    wb2 += __shfl_xor_sync(0xffffffffu, wb2, o);
+    wb1 += __shfl_xor_sync(0xffffffffu, wb1, o);
+  }
+  if (warp * 16 < Et) {
+    // candidate intervals of the bf16 logits (rnb_route.cuh)
+    uint32_t(*lgu)[kMaxE + 1] = reinterpret_cast<uint32_t(*)[kMaxE + 1]>(rsm);
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int tA = n * 8 + 2 * c, tB = tA + 1;
+      const float xiA = __uint_as_float(xmax[tA]), xiB = __uint_as_float(xmax[tB]);
+      if (row_a < Et) {
+        lgu[tA][row_a] = route_interval(acc[n][0], xn2[tA], xiA, wa2, wa1);
+        lgu[tB][row_a] = route_interval(acc[n][1], xn2[tB], xiB, wa2, wa1);
+      }
+      if (row_b < Et) {
+        lgu[tA][row_b] = route_interval(acc[n][2], xn2[tA], xiA, wb2, wb1);
+        lgu[tB][row_b] = route_interval(acc[n][3], xn2[tB], xiB, wb2, wb1);
+      }
+    }
+  }
+  // shared-expert gate logit: fp32 dot per token (warp per token)
+  if (p.has_shared) {
+    for (int t = warp; t < nt; t += 16) {
+      const uint16_t* xr = p.x + static_cast<size_t>(t0 + t) * H;
+      float s = 0.f;
+      for (int k = lane * 8; k < H; k += 256) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xr + k));
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.sgate_w + k));
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s = fmaf(__uint_as_float(xw[j] << 16), __uint_as_float(ww[j] << 16), s);
+          s = fmaf(__uint_as_float(xw[j] & 0xFFFF0000u), __uint_as_float(ww[j] & 0xFFFF0000u), s);
+        }
+      }
+      s = warp_sum(s);
+      if (lane == 0) lg[t][Et] = s;
+    }
+  }
+  __syncthreads();
+  // selection per token (warp per token), exact bf16 logits (rnb_route.cuh)
+  for (int t = warp; t < nt; t += 16) {
+    const size_t tg = static_cast<size_t>(t0 + t);
+    int e;
+    float sc;
+    warp_route_token(reinterpret_cast<const uint32_t*>(lg[t]), Et, K, p.x + tg * H, p.router_w, H, lane, false,
+                     nullptr, &e, &sc);
+    if (lane < K) {
+      p.ws.inds[tg * K + lane] = static_cast<uint32_t>(e);
+      p.ws.scores[tg * K + lane] = sc;
+      if (p.inds_out) p.inds_out[tg * K + lane] = static_cast<uint32_t>(e);
+      if (p.scores_out) p.scores_out[tg * K + lane] = sc;
+      const int le = e - p.off;
+      if (le >= 0 && le < p.E) atomicAdd(&hist[le], 1u);
+    }
+    if (lane == 0) {
+      p.ws.sg[tg] = p.has_shared ? 1.0f / (1.0f + expf(-lg[t][Et])) : 0.f;
+      float xsc, xinv;
+      fp16_range_scale(__uint_as_float(xmax[t]), xsc, xinv);
+      p.ws.xscale[tg] = xsc;
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < p.E; e += blockDim.x)
+    if (hist[e]) atomicAdd(&p.ws.counts[e], hist[e]);
+}
+
+// ------------------------------------------------------ sort / scatter
+
+__global__ void __launch_bounds__(512) k_pre_sort(Params p) {
+  __shared__ uint32_t s_rows[kMaxE + 1], s_tiles[kMaxE + 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int E1 = p.E + (p.has_shared ? 1 : 0);
+  for (int e = tid; e < E1; e += blockDim.x) {
+    const uint32_t cnt = e < p.E ? p.ws.counts[e] : static_cast<uint32_t>(p.T);
+    s_rows[e] = cnt;
+    p.ws.fill[e] = 0;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t run_rows = 0, run_tiles = 0;
+    for (int b0 = 0; b0 < E1; b0 += 32) {
+      const int e = b0 + lane;
+      const uint32_t cnt = e < E1 ? s_rows[e] : 0u;
+      const uint32_t nt = (cnt + kTileM - 1) / kTileM;
+      uint32_t ir = nt * kTileM, it = nt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t a = __shfl_up_sync(0xffffffffu, ir, o), b = __shfl_up_sync(0xffffffffu, it, o);
+        if (lane >= o) {
+          ir += a;
+          it += b;
+        }
+      }
+      if (e < E1) {
+        p.ws.base[e] = run_rows + ir - nt * kTileM;
+        s_tiles[e] = run_tiles + it - nt;
+      }
+      run_rows += __shfl_sync(0xffffffffu, ir, 31);
+      run_tiles += __shfl_sync(0xffffffffu, it, 31);
+    }
+    if (lane == 0) *p.ws.n_mt = run_tiles;
+  }
+  __syncthreads();
+  for (int e = tid; e < E1; e += blockDim.x) {
+    const uint32_t cnt = s_rows[e], nt = (cnt + kTileM - 1) / kTileM, b = p.ws.base[e];
+    for (uint32_t j = 0; j < nt; ++j) {
+      const uint32_t rows = cnt - j * kTileM < static_cast<uint32_t>(kTileM) ? cnt - j * kTileM : kTileM;
+      p.ws.tiles[s_tiles[e] + j] = make_uint4(static_cast<uint32_t>(e), b + j * kTileM, rows, 0);
+    }
+  }
+}
+
+__global__ void k_pre_scatter(Params p) {
+  const int K = p.k;
+  const size_t n_routed = static_cast<size_t>(p.T) * K;
+  const size_t total = n_routed + (p.has_shared ? p.T : 0);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    if (i < n_routed) {
+      const int le = static_cast<int>(p.ws.inds[i]) - p.off;
+      if (le < 0 || le >= p.E) continue;
+      const uint32_t pos = p.ws.base[le] + atomicAdd(&p.ws.fill[le], 1u);
+      p.ws.perm[pos] = static_cast<uint32_t>((i / K) * (K + 1) + (i % K));
+    } else {
+      const size_t t = i - n_routed;
+      p.ws.perm[p.ws.base[p.E] + t] = static_cast<uint32_t>(t * (K + 1) + K);
+    }
+  }
+}
+
+// ------------------------------------------------------ grouped GEMM
+
+// fp16 pair helpers
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+  const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b),
+                            *reinterpret_cast<const __half2*>(&c));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t half2_bits(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// 16 bytes of 8-bit codes (16 consecutive K) -> two 16-byte fp16 chunks, w = s*q + b.
+__device__ __forceinline__ void deq_q8_16(const uint4 v, uint32_t s2, uint32_t b2, uint4& o0, uint4& o1) {
+  uint32_t p[8];
+  q8_word_to_pairs(v.x, p[0], p[1]);
+  q8_word_to_pairs(v.y, p[2], p[3]);
+  q8_word_to_pairs(v.z, p[4], p[5]);
+  q8_word_to_pairs(v.w, p[6], p[7]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = hfma2_u32(p[i], s2, b2);
+  o0 = make_uint4(p[0], p[1], p[2], p[3]);
+  o1 = make_uint4(p[4], p[5], p[6], p[7]);
+}
+
+// one word of 4-bit codes (8 consecutive K) -> one 16-byte fp16 chunk in the
+// pair order (0,4),(1,5),(2,6),(3,7); activations use the same order.
+__device__ __forceinline__ uint4 deq_q4_word(uint32_t w, uint32_t s2, uint32_t b2) {
+  uint32_t p0, p1, p2, p3;
+  q4_word_to_pairs(w, p0, p1, p2, p3);
+  return make_uint4(hfma2_u32(p0, s2, b2), hfma2_u32(p1, s2, b2), hfma2_u32(p2, s2, b2), hfma2_u32(p3, s2, b2));
+}
+
+// Reorders 8 consecutive fp16 (as 4 pairs) to (0,4),(1,5),(2,6),(3,7).
+__device__ __forceinline__ uint4 perm_q4_order(const uint4 v) {
+  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
+                    __byte_perm(v.y, v.w, 0x7632));
+}
+
+__device__ __forceinline__ uint32_t bf16_to_half2_dup(uint16_t b) {
+  const float f = __uint_as_float(static_cast<uint32_t>(b) << 16);
+  return half2_bits(f, f);
+}
+
+template <int MODE>
+struct GemmCfg {
+  static constexpr int N = MODE == 0 ? 256 : 128;
+  static constexpr int kA = kTileM * 128;
+  static constexpr int kB = N * 128;
+  static constexpr int kStage = kA + kB;
+  static constexpr int S = MODE == 0 ? 4 : 6;
+  static constexpr uint32_t kTmemCols = MODE == 0 ? 256 : 512;
+  static constexpr size_t kSmem = static_cast<size_t>(S) * kStage + 1024;
+};
+
+template <int BITS, int MODE>
+__global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
+  using C = GemmCfg<MODE>;
+  extern __shared__ char smraw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ __align__(8) uint64_t full[C::S], empty[C::S], tfull, tempty;
+  __shared__ uint32_t tslot;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = p.k, H = p.H, I = p.I;
+  const int kdim = MODE == 0 ? H : I;
+  const int nks = kdim / 64;
+  const int n_nt = MODE == 0 ? I / 128 : H / 128;
+  const uint32_t n_items = __ldcg(p.ws.n_mt) * static_cast<uint32_t>(n_nt);
+
+  if (tid == 0) {
+    for (int s = 0; s < C::S; ++s) {
+      mbar_init(&full[s], kProducerWarps * 32);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&tfull, 1);
+    mbar_init(&tempty, 4 * 32);
+  }
+  if (warp == kMmaWarp) tmem_alloc(&tslot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = tslot;
+  bool timed_out = false;
+
+  if (warp < kProducerWarps) {
+    // ------------------------------------------------ producers
+    const int pt = tid;  // 0..255
+    uint32_t it = 0;
+    for (uint32_t item = blockIdx.x; item < n_items; item += gridDim.x) {
+      const uint32_t mt = item / n_nt, nt = item % n_nt;
+      const uint4 tile = __ldcg(p.ws.tiles + mt);
+      const int e = static_cast<int>(tile.x), row0 = static_cast<int>(tile.y), nrows = static_cast<int>(tile.z);
+      const bool shared_e = e == p.E;
+      // A: rows (pt >> 3) + 32 j, 16-byte chunk (pt & 7)
+      const int ca = pt & 7;
+      const void* asrc[4];
+      float ascale[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = (pt >> 3) + 32 * j;
+        asrc[j] = nullptr;
+        ascale[j] = 0.f;
+        const uint32_t ent = r < nrows ? __ldcg(p.ws.perm + row0 + r) : 0xFFFFFFFFu;
+        if (ent != 0xFFFFFFFFu) {
+          if (MODE == 0) {
+            const uint32_t t = ent / (K + 1);
+            asrc[j] = p.x + static_cast<size_t>(t) * H;
+            ascale[j] = __ldcg(p.ws.xscale + t);
+          } else {
+            asrc[j] = p.ws.h16 + static_cast<size_t>(row0 + r) * I;
+          }
+        }
+      }
+      // B: MODE 0 one row per thread (128 up rows, then 128 gate rows);
+      //    MODE 1 half a row per thread (rows nt*128 + (pt & 127), K half pt >> 7)
+      const uint32_t* bw;
+      const uint16_t *bs, *bb;
+      int brow, khalf = 0;
+      size_t wrow, srow;
+      if (MODE == 0) {
+        brow = pt < 128 ? static_cast<int>(nt) * 128 + pt : I + static_cast<int>(nt) * 128 + (pt - 128);
+        wrow = static_cast<size_t>(H) * BITS / 32;
+        srow = H / 64;
+        const size_t ew = static_cast<size_t>(2) * I * wrow, es = static_cast<size_t>(2) * I * srow;
+        bw = shared_e ? p.sgu_w : p.gu_w + e * ew;
+        bs = shared_e ? p.sgu_s : p.gu_s + e * es;
+        bb = shared_e ? p.sgu_b : p.gu_b + e * es;
+      } else {
+        brow = static_cast<int>(nt) * 128 + (pt & 127);
+        khalf = pt >> 7;
+        wrow = static_cast<size_t>(I) * BITS / 32;
+        srow = I / 64;
+        const size_t ew = static_cast<size_t>(H) * wrow, es = static_cast<size_t>(H) * srow;
+        bw = shared_e ? p.sdn_w : p.dn_w + e * ew;
+        bs = shared_e ? p.sdn_s : p.dn_s + e * es;
+        bb = shared_e ? p.sdn_b : p.dn_b + e * es;
+      }
+      const uint32_t* wr = bw + brow * wrow;
+      const uint16_t* sr = bs + brow * srow;
+      const uint16_t* br = bb + brow * srow;
+      uint4 sc8 = make_uint4(0, 0, 0, 0), bi8 = make_uint4(0, 0, 0, 0);
+      for (int ks = 0; ks < nks; ++ks) {
+        const int s = static_cast<int>(it % C::S);
+        const uint32_t n = it / C::S;
+        if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, kWaitNs)) {
+          timed_out = true;
+          break;
+        }
+        char* sA = sm + s * C::kStage;
+        char* sB = sA + C::kA;
+        // ---- A chunk: 8 values at K = ks*64 + ca*8
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = (pt >> 3) + 32 * j;
+          uint4 o = make_uint4(0, 0, 0, 0);
+          if (asrc[j]) {
+            if (MODE == 0) {
+              const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(asrc[j]) + ks * 64 + ca * 8));
+              const float sc = ascale[j];
+              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+              float f[8];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                f[2 * q] = __uint_as_float(w[q] << 16) * sc;
+                f[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u) * sc;
+              }
+              if (BITS == 4)
+                o = make_uint4(half2_bits(f[0], f[4]), half2_bits(f[1], f[5]), half2_bits(f[2], f[6]), half2_bits(f[3], f[7]));
+              else
+                o = make_uint4(half2_bits(f[0], f[1]), half2_bits(f[2], f[3]), half2_bits(f[4], f[5]), half2_bits(f[6], f[7]));
+            } else {
+              const uint4 v = __ldcg(reinterpret_cast<const uint4*>(static_cast<const __half*>(asrc[j]) + ks * 64 + ca * 8));
+              o = BITS == 4 ? perm_q4_order(v) : v;
+            }
+          }
+          *reinterpret_cast<uint4*>(sA + sw128_offset(r, ca * 8)) = o;
+        }
+        // ---- B: dequantised weights
+        if (MODE == 0) {
+          if ((ks & 7) == 0) {
+            sc8 = __ldg(reinterpret_cast<const uint4*>(sr + ks));
+            bi8 = __ldg(reinterpret_cast<const uint4*>(br + ks));
+          }
+          const int gi = ks & 7;
+          const uint32_t sw = (gi >> 1) == 0 ? sc8.x : (gi >> 1) == 1 ? sc8.y : (gi >> 1) == 2 ? sc8.z : sc8.w;
+          const uint32_t bw2 = (gi >> 1) == 0 ? bi8.x : (gi >> 1) == 1 ? bi8.y : (gi >> 1) == 2 ? bi8.z : bi8.w;
+          const uint32_t s2 = bf16_to_half2_dup(static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu)));
+          const uint32_t b2 = bf16_to_half2_dup(static_cast<uint16_t>((gi & 1) ? (bw2 >> 16) : (bw2 & 0xFFFFu)));
+          if (BITS == 8) {
+            const uint4* src = reinterpret_cast<const uint4*>(wr + ks * 16);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 o0, o1;
+              deq_q8_16(ld_stream_v4(src + q), s2, b2, o0, o1);
+              *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 16)) = o0;  // tile row pt
+              *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 16 + 8)) = o1;
+            }
+          } else {
+            const uint4* src = reinterpret_cast<const uint4*>(wr + ks * 8);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const uint4 v = ld_stream_v4(src + q);
+              const int rl = pt;  // tile row of this thread (up rows 0..127, gate rows 128..255)
+              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, q * 32)) = deq_q4_word(v.x, s2, b2);
+              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, q * 32 + 8)) = deq_q4_word(v.y, s2, b2);
+              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, q * 32 + 16)) = deq_q4_word(v.z, s2, b2);
+              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, q * 32 + 24)) = deq_q4_word(v.w, s2, b2);
+            }
+          }
+        } else {
+          if (ks == 0) {
+            sc8 = __ldg(reinterpret_cast<const uint4*>(sr));
+            bi8 = __ldg(reinterpret_cast<const uint4*>(br));
+          }
+          const int gi = ks;  // I / 64 <= 8 groups
+          const uint32_t sw = (gi >> 1) == 0 ? sc8.x : (gi >> 1) == 1 ? sc8.y : (gi >> 1) == 2 ? sc8.z : sc8.w;
+          const uint32_t bw2 = (gi >> 1) == 0 ? bi8.x : (gi >> 1) == 1 ? bi8.y : (gi >> 1) == 2 ? bi8.z : bi8.w;
+          const uint32_t s2 = bf16_to_half2_dup(static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu)));
+          const uint32_t b2 = bf16_to_half2_dup(static_cast<uint16_t>((gi & 1) ? (bw2 >> 16) : (bw2 & 0xFFFFu)));
+          const int rl = pt & 127;
+          if (BITS == 8) {
+            // 32 codes (K half) = 2 x 16 bytes
+            const uint4* src = reinterpret_cast<const uint4*>(wr + ks * 16 + khalf * 8);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              uint4 o0, o1;
+              deq_q8_16(ld_stream_v4(src + q), s2, b2, o0, o1);
+              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + q * 16)) = o0;
+              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + q * 16 + 8)) = o1;
+            }
+          } else {
+            const uint4 v = ld_stream_v4(reinterpret_cast<const uint4*>(wr + ks * 8 + khalf * 4));
+            *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32)) = deq_q4_word(v.x, s2, b2);
+            *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + 8)) = deq_q4_word(v.y, s2, b2);
+            *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + 16)) = deq_q4_word(v.z, s2, b2);
+            *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + 24)) = deq_q4_word(v.w, s2, b2);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&full[s]);
+        ++it;
+      }
+      if (timed_out) break;
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------ MMA issue (one thread)
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(kTileM, C::N, false);
+      uint32_t it = 0, j = 0;
+      for (uint32_t item = blockIdx.x; item < n_items; item += gridDim.x, ++j) {
+        if (j > 0 && !mbar_wait(&tempty, (j - 1) & 1, kWaitNs)) {
+          timed_out = true;
+          break;
+        }
+        tc_fence_after();
+        for (int ks = 0; ks < nks; ++ks, ++it) {
+          const int s = static_cast<int>(it % C::S);
+          if (!mbar_wait(&full[s], (it / C::S) & 1, kWaitNs)) {
+            timed_out = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sm + s * C::kStage), b0 = a0 + C::kA;
+          const uint32_t d = MODE == 0 ? taddr : taddr + (ks >> 1) * 128;
+          const bool fresh = MODE == 0 ? ks == 0 : (ks & 1) == 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(d, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(b0 + k * 32), idesc,
+                     (fresh && k == 0) ? 0u : 1u);
+          umma_commit(smem_u32(&empty[s]));
+        }
+        if (timed_out) break;
+        umma_commit(smem_u32(&tfull));
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 9..12)
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t tl = taddr + (static_cast<uint32_t>(quad * 32) << 16);
+    uint32_t j = 0;
+    for (uint32_t item = blockIdx.x; item < n_items; item += gridDim.x, ++j) {
+      const uint32_t mt = item / n_nt, nt = item % n_nt;
+      const uint4 tile = __ldcg(p.ws.tiles + mt);
+      const int row0 = static_cast<int>(tile.y), nrows = static_cast<int>(tile.z);
+      uint32_t ent = r < nrows ? __ldcg(p.ws.perm + row0 + r) : 0xFFFFFFFFu;
+      const bool valid = ent != 0xFFFFFFFFu;
+      if (!valid) ent = 0u;
+      // the whole warp leaves together: tcgen05.ld below is warp-collective
+      const bool ok = mbar_wait(&tfull, j & 1, kWaitNs);
+      if (__any_sync(0xffffffffu, !ok)) {
+        timed_out = true;
+        break;
+      }
+      tc_fence_after();
+      if (MODE == 0) {
+        const uint32_t t = ent / (K + 1);
+        const float xinv = valid ? 1.0f / __ldcg(p.ws.xscale + t) : 1.f;
+        float mx = 0.f;
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t u[16], gt[16];
+          tmem_ld16(tl + cc * 16, u);
+          tmem_ld16(tl + 128 + cc * 16, gt);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const float up = __uint_as_float(u[q]) * xinv, ga = __uint_as_float(gt[q]) * xinv;
+            mx = fmaxf(mx, fabsf((ga / (1.0f + expf(-ga))) * up));
+          }
+        }
+        float hs, hi;
+        fp16_range_scale(mx, hs, hi);
+        __half* dst = p.ws.h16 + static_cast<size_t>(row0 + r) * I + nt * 128;
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t u[16], gt[16];
+          tmem_ld16(tl + cc * 16, u);
+          tmem_ld16(tl + 128 + cc * 16, gt);
+          tmem_wait_ld();
+          uint32_t hv[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float up0 = __uint_as_float(u[2 * q]) * xinv, ga0 = __uint_as_float(gt[2 * q]) * xinv;
+            const float up1 = __uint_as_float(u[2 * q + 1]) * xinv, ga1 = __uint_as_float(gt[2 * q + 1]) * xinv;
+            hv[q] = half2_bits((ga0 / (1.0f + expf(-ga0))) * up0 * hs, (ga1 / (1.0f + expf(-ga1))) * up1 * hs);
+          }
+          if (valid) {
+            reinterpret_cast<uint4*>(dst + cc * 16)[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            reinterpret_cast<uint4*>(dst + cc * 16)[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+          }
+        }
+        if (valid) p.ws.hinv[static_cast<size_t>(row0 + r) * (I / 128) + nt] = hi;
+      } else {
+        const uint32_t t = ent / (K + 1), slot = ent % (K + 1);
+        float w = 0.f;
+        float hinv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (valid) {
+          w = slot < static_cast<uint32_t>(K) ? __ldcg(p.ws.scores + static_cast<size_t>(t) * K + slot)
+                                              : __ldcg(p.ws.sg + t);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4)
+            if (c4 < I / 128) hinv[c4] = __ldcg(p.ws.hinv + static_cast<size_t>(row0 + r) * (I / 128) + c4) * w;
+        }
+        float* dst = p.ws.acc + static_cast<size_t>(t) * H + nt * 128;
+        for (int cc = 0; cc < 8; ++cc) {
+          float y[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) y[q] = 0.f;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            if (c4 < I / 128) {
+              uint32_t v[16];
+              tmem_ld16(tl + c4 * 128 + cc * 16, v);
+              tmem_wait_ld();
+#pragma unroll
+              for (int q = 0; q < 16; ++q) y[q] = fmaf(__uint_as_float(v[q]), hinv[c4], y[q]);
+            }
+          }
+          if (valid) {
+#pragma unroll
+            for (int q = 0; q < 16; q += 4)
+              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + cc * 16 + q), "f"(y[q]),
+                           "f"(y[q + 1]), "f"(y[q + 2]), "f"(y[q + 3])
+                           : "memory");
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty);
+    }
+  }
+  if (timed_out) atomicOr(p.ws.status, RNB_STATUS_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) {
+    tmem_dealloc(taddr, C::kTmemCols);
+    tmem_relinquish();
+  }
+}
+
+__global__ void k_pre_final(Params p) {
+  const size_t n = static_cast<size_t>(p.T) * p.H / 4;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(p.ws.acc) + i);
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&a);
+    o.y = *reinterpret_cast<const uint32_t*>(&b);
+    reinterpret_cast<uint2*>(p.out)[i] = o;
+  }
+}
+
+// ----------------------------------------------------------- host side
+
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+struct Layout {
+  size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, h16, hinv, acc, total;
+  int rows_cap, max_mt;
+};
+
+Layout make_layout(const rnb_moe_desc& d) {
+  Layout L;
+  const size_t T = d.T, K = d.k, E1 = d.E + 1;
+  L.rows_cap = static_cast<int>(T * K + T + E1 * (kTileM - 1) + kTileM);
+  L.max_mt = L.rows_cap / kTileM + static_cast<int>(E1) + 1;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align256(o + bytes);
+    return at;
+  };
+  L.status = take(4);
+  take(ws_counter_bytes(d));  // the decode kernels' arrival counters: never touched here
+  L.counts = take(E1 * 4);
+  L.fill = take(E1 * 4);
+  L.base = take(E1 * 4);
+  L.n_mt = take(4);
+  L.tiles = take(static_cast<size_t>(L.max_mt) * 16);
+  L.perm = take(static_cast<size_t>(L.rows_cap) * 4);
+  L.inds = take(T * K * 4);
+  L.scores = take(T * K * 4);
+  L.sg = take(T * 4);
+  L.xscale = take(T * 4);
+  L.h16 = take(static_cast<size_t>(L.rows_cap) * d.I * 2);
+  L.hinv = take(static_cast<size_t>(L.rows_cap) * (d.I / 128) * 4);
+  L.acc = take(T * d.H * 4);
+  L.total = o;
+  return L;
+}
+
+}  // namespace pre
+
+size_t prefill_workspace_bytes(const rnb_moe_desc& d) { return pre::make_layout(d).total; }
+
+bool prefill_supported(const rnb_moe_desc& d) {
+  return d.H % 128 == 0 && d.I % 128 == 0 && d.I <= 512 && d.E_total <= pre::kMaxE && d.E <= pre::kMaxE &&
+         d.k <= pre::kMaxK && (d.bits == 4 || d.bits == 8) && d.group == 64;
+}
+
+template <int BITS>
+static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st) {
+  using namespace pre;
+  cudaError_t e;
+  // zero the histogram and the fp32 accumulator; padding rows of perm = ~0
+  e = cudaMemsetAsync(p.ws.counts, 0, (p.E + 1) * 4, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.perm, 0xFF, static_cast<size_t>(L.rows_cap) * 4, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.acc, 0, static_cast<size_t>(p.T) * p.H * 4, st);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill memset: ") + cudaGetErrorString(e));
+  static bool attr = false;
+  if (!attr) {
+    e = cudaFuncSetAttribute(k_pre_route, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kRouteSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_pre_gemm<BITS, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(GemmCfg<0>::kSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_pre_gemm<BITS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(GemmCfg<1>::kSmem));
+    if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill smem attribute: ") + cudaGetErrorString(e));
+    attr = true;
+  }
+  k_pre_route<<<(p.T + kRouteT - 1) / kRouteT, 512, kRouteSmem, st>>>(p);
+  k_pre_sort<<<1, 512, 0, st>>>(p);
+  const size_t n_scatter = static_cast<size_t>(p.T) * (p.k + 1);
+  k_pre_scatter<<<static_cast<unsigned>((n_scatter + 255) / 256), 256, 0, st>>>(p);
+  const int nc = dev_info().sms;
+  k_pre_gemm<BITS, 0><<<nc, kThreads, GemmCfg<0>::kSmem, st>>>(p);
+  k_pre_gemm<BITS, 1><<<nc, kThreads, GemmCfg<1>::kSmem, st>>>(p);
+  k_pre_final<<<nc * 4, 256, 0, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e));
+  return RNB_OK;
+}
+
+int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out, float* scores_out, void* ws,
+                size_t ws_bytes, cudaStream_t st) {
+  using namespace pre;
+  const Layout L = make_layout(*d);
+  if (ws_bytes < L.total) return fail(RNB_ERR_WORKSPACE, "workspace too small for the prefill path");
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.T = d->T;
+  p.H = d->H;
+  p.I = d->I;
+  p.E = d->E;
+  p.E_total = d->E_total;
+  p.off = d->expert_offset;
+  p.k = d->k;
+  p.has_shared = has_shared(d) ? 1 : 0;
+  p.rows_cap = L.rows_cap;
+  p.max_mt = L.max_mt;
+  p.x = static_cast<const uint16_t*>(x);
+  p.router_w = d->router_w;
+  p.sgate_w = d->shared_gate_w;
+  p.gu_w = d->gu_w;
+  p.gu_s = d->gu_s;
+  p.gu_b = d->gu_b;
+  p.dn_w = d->dn_w;
+  p.dn_s = d->dn_s;
+  p.dn_b = d->dn_b;
+  p.sgu_w = d->sgu_w;
+  p.sgu_s = d->sgu_s;
+  p.sgu_b = d->sgu_b;
+  p.sdn_w = d->sdn_w;
+  p.sdn_s = d->sdn_s;
+  p.sdn_b = d->sdn_b;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.inds_out = inds_out;
+  p.scores_out = scores_out;
+  char* b = static_cast<char*>(ws);
+  p.ws.status = reinterpret_cast<uint32_t*>(b + L.status);
+  p.ws.counts = reinterpret_cast<uint32_t*>(b + L.counts);
+  p.ws.fill = reinterpret_cast<uint32_t*>(b + L.fill);
+  p.ws.base = reinterpret_cast<uint32_t*>(b + L.base);
+  p.ws.n_mt = reinterpret_cast<uint32_t*>(b + L.n_mt);
+  p.ws.tiles = reinterpret_cast<uint4*>(b + L.tiles);
+  p.ws.perm = reinterpret_cast<uint32_t*>(b + L.perm);
+  p.ws.inds = reinterpret_cast<uint32_t*>(b + L.inds);
+  p.ws.scores = reinterpret_cast<float*>(b + L.scores);
+  p.ws.sg = reinterpret_cast<float*>(b + L.sg);
+  p.ws.xscale = reinterpret_cast<float*>(b + L.xscale);
+  p.ws.h16 = reinterpret_cast<__half*>(b + L.h16);
+  p.ws.hinv = reinterpret_cast<float*>(b + L.hinv);
+  p.ws.acc = reinterpret_cast<float*>(b + L.acc);
+  return d->bits == 8 ? launch_prefill<8>(p, L, st) : launch_prefill<4>(p, L, st);
+}
+
+}  // namespace rnb

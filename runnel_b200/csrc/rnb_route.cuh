@@ -1,0 +1,237 @@
+// rnb_route.cuh -- exact bf16 router logits and top-k selection.
+//
+// A router logit is defined as the correctly rounded bf16 of the exact dot
+// product x . w_e (bf16 inputs; MLX's Linear returns bf16).  The kernels
+// compute it fast on the tensor cores with fp32 accumulation, which is exact
+// in every product but rounds partial sums, so the fp32 value L may sit on
+// the other side of a bf16 rounding midpoint than the exact one.  Each fp32
+// logit is therefore published as an interval of bf16 candidates
+//     lo = bf16(L - B),  hi = bf16(L + B),  B = 2^-16 |x|_2 |w_e|_2 + 2^-21 |L|
+// (|x|_2 |w_e|_2 >= sum |x_i w_i| by Cauchy-Schwarz, so B allows two fp32
+// ulps of error per 16-wide MMA step over a chain of 128 steps at the
+// largest possible partial sum).  lo == hi certifies the rounding.  The
+// selection warp recomputes, in fp64 from the bf16 inputs, exactly those
+// uncertain logits that could still reach the top k; every selected logit
+// is then the correctly rounded value, and so is the selection.
+#pragma once
+
+#include "rnb_common.cuh"
+
+namespace rnb {
+
+// Unique selection key: bf16 value order in the high half (-0 counts as +0,
+// as a float comparison does), then the lower expert index.
+__device__ __forceinline__ uint32_t route_key(uint16_t bits, int e) {
+  if ((bits & 0x7FFFu) == 0) bits = 0;
+  const uint32_t ord = (bits & 0x8000u) ? (~static_cast<uint32_t>(bits) & 0xFFFFu) : (static_cast<uint32_t>(bits) | 0x8000u);
+  return (ord << 16) | (0xFFFFu - static_cast<uint32_t>(e));
+}
+__device__ __forceinline__ float route_key_value(uint32_t key) {
+  const uint32_t ord = key >> 16;
+  const uint32_t bits = (ord & 0x8000u) ? (ord & 0x7FFFu) : (~ord & 0xFFFFu);
+  return __uint_as_float(bits << 16);
+}
+__device__ __forceinline__ int route_key_expert(uint32_t key) { return static_cast<int>(0xFFFFu - (key & 0xFFFFu)); }
+
+// Round a double to bf16 (nearest, ties to even) in one step.  Magnitudes
+// below 2^-126 are rounded through fp32.
+__device__ __forceinline__ uint16_t f64_to_bf16_bits(double v) {
+  if (v != v) return 0x7FC0u;
+  if (fabs(v) < 0x1p-126) return __bfloat16_as_ushort(__float2bfloat16_rn(__double2float_rn(v)));
+  const uint64_t b = static_cast<uint64_t>(__double_as_longlong(v));
+  const uint32_t sign = static_cast<uint32_t>(b >> 63);
+  int e = static_cast<int>((b >> 52) & 0x7FF);
+  const uint64_t m = b & ((1ull << 52) - 1);
+  uint32_t q = static_cast<uint32_t>(m >> 45);
+  const uint64_t rem = m & ((1ull << 45) - 1), half = 1ull << 44;
+  if (rem > half || (rem == half && (q & 1u))) {
+    if (++q == 128) {
+      q = 0;
+      ++e;
+    }
+  }
+  const int fe = e - 1023 + 127;
+  if (fe >= 255) return static_cast<uint16_t>((sign << 15) | 0x7F80u);
+  return static_cast<uint16_t>((sign << 15) | (static_cast<uint32_t>(fe) << 7) | q);
+}
+
+// Packed candidate interval (lo | hi << 16) of an fp32 logit L.  Norms of
+// the token (xn2 = sum x^2, xinf = max |x|) and of the router row (wn2 =
+// sum w^2, wn1 = sum |w|), fp32: the bound uses |x|_2 |w|_2 when the squares
+// cannot have underflowed, else |x|_inf |w|_1 (both >= sum |x_i w_i|; an
+// all-zero token gets B = 0, its logits are exact zeros).
+__device__ __forceinline__ uint32_t route_interval(float L, float xn2, float xinf, float wn2, float wn1) {
+  float nb = xinf * wn1;
+  if (xn2 >= 0x1p-100f && wn2 >= 0x1p-100f) nb = fminf(nb, sqrtf(xn2) * sqrtf(wn2));
+  const float B = 0x1p-16f * 1.001f * nb + 0x1p-21f * fabsf(L);
+  if (!(B <= 3.0e38f) || L != L) return 0xFF80u | (0x7F80u << 16);  // (-inf, +inf): recompute
+  const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(L - B));
+  const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(L + B));
+  return lo | (hi << 16);
+}
+
+// Per-lane partial norms of a router tile in the mma.sync m16n8k16 layout:
+// lane 4g+c sees, per 32-wide chunk, 8 activations of token g and 8 weights
+// of each of the tile rows g and g+8.
+struct RouterNorms {
+  float xs2 = 0.f, xmx = 0.f, a2 = 0.f, a1 = 0.f, b2 = 0.f, b1 = 0.f;
+  __device__ __forceinline__ void add(const uint4 x, const uint4 wa, const uint4 wb) {
+    const uint32_t xv[4] = {x.x, x.y, x.z, x.w}, av[4] = {wa.x, wa.y, wa.z, wa.w}, bv[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float xf = __uint_as_float(h ? (xv[j] & 0xFFFF0000u) : (xv[j] << 16));
+        const float af = __uint_as_float(h ? (av[j] & 0xFFFF0000u) : (av[j] << 16));
+        const float bf = __uint_as_float(h ? (bv[j] & 0xFFFF0000u) : (bv[j] << 16));
+        xs2 = fmaf(xf, xf, xs2);
+        xmx = fmaxf(xmx, fabsf(xf));
+        a2 = fmaf(af, af, a2);
+        a1 += fabsf(af);
+        b2 = fmaf(bf, bf, b2);
+        b1 += fabsf(bf);
+      }
+    }
+  }
+  // sum over the four lanes of one g
+  __device__ __forceinline__ void reduce_quad() {
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      xs2 += __shfl_xor_sync(0xffffffffu, xs2, o);
+      xmx = fmaxf(xmx, __shfl_xor_sync(0xffffffffu, xmx, o));
+      a2 += __shfl_xor_sync(0xffffffffu, a2, o);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+      b2 += __shfl_xor_sync(0xffffffffu, b2, o);
+      b1 += __shfl_xor_sync(0xffffffffu, b1, o);
+    }
+  }
+  // one warp's 48 partials: token g at [g], [8+g]; row g at [16+g], [32+g]; row g+8 at [24+g], [40+g]
+  __device__ __forceinline__ void store(float* dst, int g) const {
+    dst[g] = xs2;
+    dst[8 + g] = xmx;
+    dst[16 + g] = a2;
+    dst[24 + g] = b2;
+    dst[32 + g] = a1;
+    dst[40 + g] = b1;
+  }
+};
+
+// Interval of tile row r (0..15), token n (0..7) from nw warps' partials.
+__device__ __forceinline__ uint32_t router_interval_from(const float* part, int nw, int r, int n, float L) {
+  float xn2 = 0.f, xinf = 0.f, wn2 = 0.f, wn1 = 0.f;
+  for (int w = 0; w < nw; ++w) {
+    const float* q = part + w * 48;
+    xn2 += q[n];
+    xinf = fmaxf(xinf, q[8 + n]);
+    wn2 += q[16 + r];  // rows 8..15 continue into [24, 32)
+    wn1 += q[32 + r];
+  }
+  return route_interval(L, xn2, xinf, wn2, wn1);
+}
+
+// fp64 dot product of two bf16 rows of length H (H % 8 == 0, 16-byte
+// aligned), warp-cooperative; every lane returns the sum.  bf16 products are
+// exact in fp64 and the fp64 sum of up to 2^11 of them errs by < 2^-42 of
+// sum |x_i w_i|.
+static __device__ __noinline__ double warp_dot_f64(const uint16_t* x, const uint16_t* w, int H, int lane) {
+  double a0 = 0.0, a1 = 0.0;
+#pragma unroll 2
+  for (int k = lane * 8; k < H; k += 256) {
+    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + k));
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + k));
+    const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a0 = fma(static_cast<double>(__uint_as_float(xs[j] << 16)), static_cast<double>(__uint_as_float(ws[j] << 16)), a0);
+      a1 = fma(static_cast<double>(__uint_as_float(xs[j] & 0xFFFF0000u)),
+               static_cast<double>(__uint_as_float(ws[j] & 0xFFFF0000u)), a1);
+    }
+  }
+  double s = a0 + a1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
+// The K largest of the warp's keys (8 per lane, unique, 0 = empty): lane
+// s < K receives the s-th in `mine`; returns the K-th.  One redux per pick.
+__device__ __forceinline__ uint32_t warp_select_k(const uint32_t (&keys)[8], int K, int lane, uint32_t& mine) {
+  uint32_t k2[8], best = 0, w = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    k2[i] = keys[i];
+    best = max(best, k2[i]);
+  }
+  mine = 0;
+  for (int slot = 0; slot < K; ++slot) {
+    w = __reduce_max_sync(0xffffffffu, best);
+    if (lane == slot) mine = w;
+    if (best == w) {
+      best = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        k2[i] = k2[i] == w ? 0u : k2[i];
+        best = max(best, k2[i]);
+      }
+    }
+  }
+  return w;
+}
+
+// One token's routing, by one full warp.  ivl[e] (e < Et <= 256) holds the
+// packed candidate interval of expert e's logit.  Lane s < K returns the
+// s-th selected expert (descending logit, ties to the lower index) in *e_out
+// and its weight, softmax over all Et logits gathered at the selection and
+// renormalised, in *score_out.  With exact_all every uncertain logit is
+// resolved (not only those that can reach the top k) and, if logits_row is
+// non-null, all Et bf16 logits are written there as fp32.
+static __device__ __noinline__ void warp_route_token(const uint32_t* ivl, int Et, int K, const uint16_t* xrow,
+                                                     const uint16_t* router_w, int H, int lane, bool exact_all,
+                                                     float* logits_row, int* e_out, float* score_out) {
+  uint32_t klo[8], khi[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i;
+    klo[i] = khi[i] = 0;
+    if (e < Et) {
+      const uint32_t v = ivl[e];
+      klo[i] = route_key(static_cast<uint16_t>(v & 0xFFFFu), e);
+      khi[i] = route_key(static_cast<uint16_t>(v >> 16), e);
+    }
+  }
+  // theta = K-th largest lower key: an expert whose upper key is below it is
+  // beaten for certain by K others
+  uint32_t mine;
+  const uint32_t theta = warp_select_k(klo, K, lane, mine);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool need = klo[i] != khi[i] && (exact_all || khi[i] >= theta);
+    uint32_t m = __ballot_sync(0xffffffffu, need);
+    while (m) {
+      const int src = __ffs(m) - 1;
+      m &= m - 1;
+      const int e = src + 32 * i;
+      const double d = warp_dot_f64(xrow, router_w + static_cast<size_t>(e) * H, H, lane);
+      if (lane == src) klo[i] = khi[i] = route_key(f64_to_bf16_bits(d), e);
+    }
+  }
+  warp_select_k(klo, K, lane, mine);
+  const float mx = route_key_value(__shfl_sync(0xffffffffu, mine, 0));
+  float den = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i;
+    if (e < Et) {
+      const float l = route_key_value(klo[i]);
+      den += expf(l - mx);
+      if (logits_row) logits_row[e] = l;
+    }
+  }
+  den = warp_sum(den);
+  const float pw = lane < K ? expf(route_key_value(mine) - mx) / den : 0.f;
+  const float selsum = warp_sum(pw);
+  *e_out = route_key_expert(mine);
+  *score_out = pw / selsum;
+}
+
+}  // namespace rnb

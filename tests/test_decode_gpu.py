@@ -51,12 +51,8 @@ def test_router_matches_oracle(bits):
     ologits, oinds, oscores, _ = oracle.router(w, blk.x[:64], k=8)
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
     np.testing.assert_allclose(scores.cpu().numpy(), oscores, rtol=2e-5, atol=1e-7)
-    lg = logits.cpu().numpy()
-    # bf16-rounded logits: identical except where fp32 accumulation order moves a
-    # value across a bf16 rounding boundary (at most one bf16 step)
-    diff = np.abs(lg - ologits)
-    assert np.mean(diff > 0) < 1e-3
-    assert np.all(diff <= np.abs(ologits) * 2.0 ** -7 + 1e-30)
+    # every logit is the correctly rounded bf16 of the exact dot product
+    np.testing.assert_array_equal(logits.cpu().numpy(), ologits)
 
 
 @pytest.mark.parametrize("bits", [8, 4])

@@ -1,0 +1,83 @@
+"""GPU parity of the prefill path (T > 64: sorted grouped tcgen05 GEMMs).
+
+Checked against the CPU oracle on whole small batches and on sampled tokens
+of large ones (the block is per-token, so a token's output depends only on
+its own row), and against the decode kernels (RNB_FLAG_CHAIN) on the same
+input.  Routing must match exactly; outputs use the bounds of tests/_parity.py.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from runnel_b200 import _lib, inputs, ops
+from tests._parity import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(bits, seed, T, skew=None, sample=None):
+    blk = inputs.make_block(bits, seed=seed, T=T, skew=skew)
+    bt = ops.BlockTensors.from_numpy(blk, "cuda")
+    x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
+    out, inds, scores = ops.moe_block(bt, x, return_routing=True)
+    w = oracle.BlockWeights(bits=bits, group=64, **blk.weight_fields())
+    rows = np.arange(T) if sample is None else np.sort(np.random.default_rng(seed).choice(T, sample, replace=False))
+    ref, oinds, oscores = oracle.moe_block(w, np.ascontiguousarray(blk.x[rows]), k=8)
+    np.testing.assert_array_equal(inds.cpu().numpy()[rows], oinds)
+    np.testing.assert_allclose(scores.cpu().numpy()[rows], oscores, rtol=2e-5, atol=1e-7)
+    s = assert_close(out.float().cpu().numpy()[rows], ref, f"prefill q{bits} T={T} skew={skew}")
+    return blk, bt, x, out, s
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_prefill_matches_oracle_small_batch(bits):
+    _run(bits, seed={8: 0, 4: 1}[bits], T=128)
+
+
+@pytest.mark.parametrize("bits,T", [(8, 200), (4, 65)])
+def test_prefill_ragged_token_counts(bits, T):
+    _run(bits, seed=5, T=T)
+
+
+def test_prefill_zipf_skew_config3_sampled():
+    """Configuration 3 of the benchmark set: q8, 2048 tokens, log-Zipf routing skew."""
+    blk, bt, x, out, _ = _run(8, seed=2, T=2048, skew="zipf", sample=48)
+    chain = ops.BlockTensors(**{**bt.__dict__, "flags": bt.flags | _lib.FLAG_CHAIN})
+    out_c = ops.moe_block(chain, x)
+    assert_close(out.float().cpu().numpy(), out_c.float().cpu().numpy(), "prefill vs decode chain")
+
+
+def test_prefill_adversarial_routing_sampled():
+    """A quarter of the tokens all route to one expert (many 128-row tiles of one expert)."""
+    blk, bt, x, out, _ = _run(8, seed=4, T=1024, skew="adversarial", sample=32)
+    hot = blk.meta["hot_expert"]
+    inds = ops.router_topk(bt, x)[0].cpu().numpy()
+    assert (inds == hot).any(axis=1).sum() >= 200
+
+
+def test_prefill_workspace_and_status():
+    blk = inputs.make_block(4, seed=1, T=256)
+    bt = ops.BlockTensors.from_numpy(blk, "cuda")
+    x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
+    ws = ops.Workspace("cuda")
+    a = ops.moe_block(bt, x, ws=ws)
+    b = ops.moe_block(bt, x, ws=ws)
+    assert ws.status() == 0
+    # fp32 atomics may reorder the per-token sum: agreement to fp32 rounding
+    assert_close(a.float().cpu().numpy(), b.float().cpu().numpy(), "repeat")
+
+
+def test_decode_after_prefill_on_one_workspace():
+    """Prefill, chained decode and the persistent decode kernel alternate on
+    one workspace; each call still matches a call on a fresh workspace."""
+    blk = inputs.make_block(8, seed=6, T=200)
+    bt = ops.BlockTensors.from_numpy(blk, "cuda")
+    chain = ops.BlockTensors(**{**bt.__dict__, "flags": bt.flags | _lib.FLAG_CHAIN})
+    x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
+    shared = ops.Workspace("cuda")
+    for tensors, xs in ((bt, x), (chain, x), (bt, x[:3]), (bt, x), (chain, x[:64]), (bt, x[:1])):
+        got = ops.moe_block(tensors, xs, ws=shared)
+        fresh = ops.moe_block(tensors, xs, ws=ops.Workspace("cuda"))
+        assert shared.status() == 0
+        assert_close(got.float().cpu().numpy(), fresh.float().cpu().numpy(), "shared workspace")
