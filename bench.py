@@ -1,9 +1,14 @@
-"""Benchmark of the sparse-MoE block (decode) on B200.
+"""Benchmark of the sparse-MoE block on B200.
 
 Default workload (N=1): configuration 2 of the reference's hot-path benchmark
 set -- one Ornith MoE block, 4-bit MLX affine (group 64), batch-1 decode --
 measured as microseconds per token.  A step is one block call on one batch of
 T tokens (router, top-8, routed experts, shared expert, combine).
+``--config 3`` (q8, 2048 tokens, log-Zipf routing skew) and ``--config 5``
+(q8, 16384 tokens, uniform and adversarial routing on alternate steps) time
+the prefill path in tokens per second instead; their roofline is the tensor
+pipe (the two grouped GEMM launches, timed with CUDA events on the launching
+stream through the library's stage timing).
 
 Timing: W warm-up steps, then K steps bracketed by barrier + synchronize,
 device-timed with CUDA events.  Every step uses a different token and one of
@@ -55,6 +60,12 @@ def step_bytes(bits, distinct_experts, T, H=2048, I=512, E=256, shared=True):
     b += E * H * 2  # router
     b += T * H * 2 * 2  # x in, out
     return b
+
+
+def prefill_flops(T, H=2048, I=512, E=256, k=8, shared=True):
+    """Algorithmic FLOPs of one block call on T tokens: (routed GEMMs, all)."""
+    gemm = 2.0 * T * (k + (1 if shared else 0)) * 3 * I * H
+    return gemm, gemm + 2.0 * T * E * H + (2.0 * T * H if shared else 0.0)
 
 
 def peaks():
@@ -127,10 +138,12 @@ def cpu_baseline(bits, T, budget_s=10.0, seed=1):
             "sample": f"{n} block calls of T={T} tokens, q{bits} (CPU oracle, C + OpenMP, fp32)"}
 
 
-def run_reference(args):
+def run_reference(args, cfg=None):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if cfg is not None:
+        return run_reference_prefill(args, cfg)
     bits, T = 4, args.tokens
     times = []
     from oracle import oracle
@@ -159,7 +172,39 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_profile(args):
+def run_reference_prefill(args, cfg, sample_T=16):
+    """The CPU path (oracle) on the prefill workload: each step is the first
+    sample_T tokens of that step's batch, alternating over the step kinds."""
+    from oracle import oracle
+
+    bits = args.bits
+    blocks, routing = prefill_blocks(cfg, bits, args.seed)
+    ws = [(oracle.BlockWeights(bits=bits, group=64, **b.weight_fields()), np.ascontiguousarray(b.x[:sample_T]))
+          for b in blocks]
+    for i in range(args.warmup):
+        w, x = ws[i % len(ws)]
+        oracle.moe_block(w, x, k=8)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        w, x = ws[i % len(ws)]
+        oracle.moe_block(w, x, k=8)
+    el = time.perf_counter() - t0
+    tok_s = args.steps * sample_T / el
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference", "metric": "moe_block_prefill_tokens_per_s", "value": tok_s, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config{args.config} q{bits} prefill T={cfg['T']}", "bits": bits,
+                   "tokens_per_step": sample_T, "routing": routing},
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} oracle calls of the first {sample_T} tokens of each batch"},
+        "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_profile(args, cfg=None):
     """Small fixed case for ncu captures: two block copies (~1 GB for q4),
     W + K plain (non-graph) block calls, no timing, no CPU baseline."""
     import torch
@@ -168,6 +213,18 @@ def run_profile(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if cfg is not None:
+        # prefill: the configuration's first step kind, plain calls
+        blk = prefill_blocks(cfg, args.bits, args.seed)[0][0]
+        bt = ops.BlockTensors.from_numpy(blk, dev)
+        x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).to(dev)
+        ws = ops.Workspace(dev)
+        for _ in range(args.warmup + args.steps):
+            ops.moe_block(bt, x, ws=ws)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": True, "bits": args.bits, "tokens": cfg["T"],
+                          "calls": args.warmup + args.steps}))
+        return
     blk = inputs.make_block(args.bits, seed=args.seed, T=1)
     copies = [ops.BlockTensors.from_numpy(blk, dev)]
     copies.append(ops.BlockTensors(**{f: (v.clone() if isinstance(v, torch.Tensor) else v)
@@ -180,6 +237,169 @@ def run_profile(args):
     torch.cuda.synchronize()
     print(json.dumps({"profile": True, "bits": args.bits, "tokens": args.tokens,
                       "calls": args.warmup + args.steps}))
+
+
+def cpu_baseline_prefill(blocks, bits, sample_T=32, budget_s=10.0):
+    """CPU oracle tokens/s on a bounded sample: the first sample_T tokens of
+    each step's batch, alternating over the step kinds of the workload."""
+    from oracle import oracle
+
+    ws = [(oracle.BlockWeights(bits=bits, group=64, **b.weight_fields()), np.ascontiguousarray(b.x[:sample_T]))
+          for b in blocks]
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        w, x = ws[n % len(ws)]
+        oracle.moe_block(w, x, k=8)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return {"value": n * sample_T / el, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{n} oracle block calls of {sample_T} tokens (first tokens of the workload's batches), "
+                      f"q{bits}, C + OpenMP fp32"}
+
+
+def prefill_blocks(cfg, bits, seed):
+    """Synthetic blocks of one prefill configuration: one per step kind."""
+    from runnel_b200 import inputs
+
+    T = cfg["T"]
+    if cfg.get("skew") == "zipf":
+        return [inputs.make_block(bits, seed=seed, T=T, skew="zipf")], "log-Zipf(s=1.1) expert skew"
+    return ([inputs.make_block(bits, seed=seed, T=T), inputs.make_block(bits, seed=seed, T=T, skew="adversarial")],
+            "uniform / adversarial (25% of tokens on one expert) on alternate steps")
+
+
+def run_prefill_bench(args, cfg):
+    import torch
+
+    from runnel_b200 import _lib, ops
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+
+    bits, T = args.bits, cfg["T"]
+    blocks, routing = prefill_blocks(cfg, bits, args.seed)
+    base = ops.BlockTensors.from_numpy(blocks[0], dev)
+    kinds = [base]
+    for b in blocks[1:]:  # same expert weights, the step kind's router
+        rw = torch.from_numpy(b.router_w).view(torch.int16).view(torch.bfloat16).to(dev)
+        kinds.append(ops.BlockTensors(**{**base.__dict__, "router_w": rw}))
+    xs = [torch.from_numpy(b.x).view(torch.int16).view(torch.bfloat16).to(dev) for b in blocks]
+    out = torch.empty_like(xs[0])
+    ws = ops.Workspace(dev)
+    stream = torch.cuda.Stream(dev)
+    nk = len(kinds)
+
+    def step(i):
+        ops.moe_block(kinds[i % nk], xs[i % nk], ws=ws, out=out)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    stream.synchronize()
+    assert ws.status() == 0
+    K = args.steps
+    sampler = ClockSampler(local)
+    sampler.start()
+    t_end = time.time() + args.soak
+    with torch.cuda.stream(stream):
+        while time.time() < t_end:
+            for i in range(4):
+                step(i)
+            stream.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    _lib.stage_timing(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for i in range(K):
+            step(i)
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    _lib.stage_timing(False)
+    stages, ncalls = _lib.stage_times()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / K
+    tok_s = T * K * world / (ms * 1e-3)
+    assert ws.status() == 0
+
+    # end to end through the public API: pinned host tokens in, host output back
+    xh = [x.cpu().pin_memory() for x in xs]
+    oh = torch.empty_like(xh[0]).pin_memory()
+    xd = torch.empty_like(xs[0])
+    od = torch.empty_like(xd)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            xd.copy_(xh[i % nk], non_blocking=True)
+            ops.moe_block(kinds[i % nk], xd, ws=ws, out=od)
+            oh.copy_(od, non_blocking=True)
+    stream.synchronize()
+    Ke = max(4, min(K, 64))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(Ke):
+            xd.copy_(xh[i % nk], non_blocking=True)
+            ops.moe_block(kinds[i % nk], xd, ws=ws, out=od)
+            oh.copy_(od, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_tok_s = T * Ke * world / (e0.elapsed_time(e1) * 1e-3)
+
+    gemm_flops, all_flops = prefill_flops(T)
+    _, bf16_burst, src = peaks()
+    sustained = None
+    pth = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pth):
+        sustained = json.load(open(pth)).get("bf16_tflops_sustained")
+    peak = sustained or bf16_burst
+    gemm_ms = (stages.get("gateup", 0.0) + stages.get("down", 0.0)) / max(ncalls, 1)
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    line = {
+        "metric": "moe_block_prefill_tokens_per_s", "value": tok_s, "unit": "tokens/s",
+        "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded MLX-affine block, N(0,1) bf16 tokens)",
+        "config": {"workload": f"config{args.config} q{bits} prefill T={T}", "bits": bits,
+                   "tokens_per_step": T, "routing": routing, "H": 2048, "I": 512, "E": 256, "top_k": 8,
+                   "l2": "inputs larger than L2: every step reads the whole expert bank (>= 0.8 GB)",
+                   "parallelism": "replica" if world > 1 else "single"},
+        "e2e": {"value": e2e_tok_s, "unit": "tokens/s", "h2d_bytes_per_step": T * 2048 * 2,
+                "d2h_bytes_per_step": T * 2048 * 2},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": (achieved / peak) if achieved else None,
+                     "peak_source": f"{src} bf16 {'sustained' if sustained else 'burst'}",
+                     "frac_of_burst": (achieved / bf16_burst) if achieved and bf16_burst else None,
+                     "traffic": None, "algorithmic_flops_per_step": gemm_flops,
+                     "kernel": "k_pre_gemm (gate/up + down launches)", "gemm_ms_per_step": gemm_ms,
+                     "block_tflops": all_flops / (ms_step * 1e-3) / 1e12},
+        "stages_ms_per_step": {k: v / max(ncalls, 1) for k, v in stages.items()},
+        "gpu_launches": 6 * K,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline_prefill(blocks, bits, budget_s=args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_ours(args):
@@ -199,12 +419,30 @@ def run_ours(args):
 
     bits, T = args.bits, args.tokens
     blk = inputs.make_block(bits, seed=args.seed, T=1)
-    base = ops.BlockTensors.from_numpy(blk, dev)
+    ctx = None
+    ws = ops.Workspace(dev)
+    if world > 1:
+        # expert parallel: this rank's expert shard and shared-expert quarters,
+        # partial outputs exchanged over NVLink inside the decode kernel
+        from runnel_b200 import ep as epm
+
+        lo, hi, _ = epm.plan(rank, world, blk.E, blk.I)
+        base = ops.BlockTensors.from_numpy(blk, dev, E_range=(lo, hi))
+        ctx = epm.ExpertParallel(rank, world, blk.H)
+
+        def block_call(bt, x, out):
+            return ctx.moe_block(bt, x, ws=ws, out=out)
+    else:
+        base = ops.BlockTensors.from_numpy(blk, dev)
+
+        def block_call(bt, x, out):
+            return ops.moe_block(bt, x, ws=ws, out=out)
     gu, dn = expert_bytes(bits)
-    block_bytes = base.E * (gu + dn)
-    per_step = step_bytes(bits, min(8 * T, 256), T)
+    # bytes one rank streams per step: its share of the selected experts and
+    # of the shared expert, plus the whole router
+    per_step = step_bytes(bits, min(8 * T, 256), T) / world + 256 * 2048 * 2 * (1 - 1 / world)
     R = max(4, int(np.ceil(4 * L2_BYTES / per_step)))
-    R = min(R, 48)
+    R = min(R, 48 if world == 1 else 160)
     copies = [base]
     for _ in range(R - 1):
         c = ops.BlockTensors(**{f: (v.clone() if isinstance(v, torch.Tensor) else v)
@@ -214,11 +452,10 @@ def run_ours(args):
     xs_np = inputs.make_tokens(args.seed, ntok)
     xs = torch.from_numpy(xs_np).view(torch.int16).view(torch.bfloat16).to(dev).reshape(R, T, -1)
     outs = torch.empty_like(xs)
-    ws = ops.Workspace(dev)
     stream = torch.cuda.Stream(dev)
 
     def one(i):
-        ops.moe_block(copies[i], xs[i], ws=ws, out=outs[i])
+        block_call(copies[i], xs[i], outs[i])
 
     with torch.cuda.stream(stream):
         for i in range(R):
@@ -226,13 +463,13 @@ def run_ours(args):
     stream.synchronize()
     # distinct experts actually touched per step (for the roofline's bytes)
     inds_all = []
+    rws = ops.Workspace(dev)
     with torch.cuda.stream(stream):
         for i in range(R):
-            _, ii, _ = ops.moe_block(copies[i], xs[i], ws=ws, return_routing=True)
-            inds_all.append(ii)
+            inds_all.append(ops.router_topk(copies[i], xs[i], ws=rws)[0])
     stream.synchronize()
     distinct = float(np.mean([len(np.unique(ii.cpu().numpy())) for ii in inds_all]))
-    per_step = step_bytes(bits, distinct, T)
+    per_step = step_bytes(bits, distinct, T)  # whole block, all ranks
 
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
@@ -248,13 +485,21 @@ def run_ours(args):
 
     sampler = ClockSampler(local)
     sampler.start()
-    # sustained replays so the clock sampler sees the GPU under this load
-    t_end = time.time() + args.soak
+    # sustained replays so the clock sampler sees the GPU under this load; the
+    # count is the same on every rank (expert-parallel steps pair up across ranks)
+    t0 = time.time()
     with torch.cuda.stream(stream):
-        while time.time() < t_end:
-            for _ in range(50):
-                g.replay()
-            stream.synchronize()
+        g.replay()
+    stream.synchronize()
+    n_soak = max(1, int(args.soak / max(time.time() - t0, 1e-4)))
+    if dist:
+        t = torch.tensor([n_soak], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        n_soak = int(t.item())
+    with torch.cuda.stream(stream):
+        for _ in range(n_soak):
+            g.replay()
+    stream.synchronize()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -272,7 +517,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_step = ms / K
-    us_tok = ms_step * 1e3 / (T * world) if False else ms_step * 1e3 / T
+    us_tok = ms_step * 1e3 / T
 
     # end to end through the public API with host buffers
     xh = torch.from_numpy(xs_np).view(torch.int16).view(torch.bfloat16).reshape(R, T, -1).pin_memory()
@@ -282,39 +527,54 @@ def run_ours(args):
     with torch.cuda.stream(stream):
         for i in range(min(R, args.warmup + 1)):
             xd.copy_(xh[i], non_blocking=True)
-            ops.moe_block(copies[i], xd, ws=ws, out=od)
+            block_call(copies[i], xd, od)
             oh[i].copy_(od, non_blocking=True)
     stream.synchronize()
+    if dist:
+        dist.barrier()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
         for s in range(K):
             i = s % R
             xd.copy_(xh[i], non_blocking=True)
-            ops.moe_block(copies[i], xd, ws=ws, out=od)
+            block_call(copies[i], xd, od)
             oh[i].copy_(od, non_blocking=True)
         e1.record(stream)
     torch.cuda.synchronize()
-    e2e_us = e0.elapsed_time(e1) * 1e3 / (K * T)
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_us = e2e_ms * 1e3 / (K * T)
+    assert ws.status() == 0, "device status reported a timeout or a bad index"
 
     hbm, _, src = peaks()
-    achieved = per_step / (ms_step * 1e-3) / 1e9
+    achieved = per_step / (ms_step * 1e-3) / 1e9  # all ranks together
+    persistent = T <= (2 if bits == 4 else 1)
     line = {
         "metric": "moe_block_decode_us_per_token", "value": us_tok, "unit": "us/token",
         "n_gpus": world, "steps": K, "warmup": wreps * R, "ms_per_step": ms_step,
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f16",
         "data": "synthetic (seeded MLX-affine block, N(0,1) bf16 tokens)",
         "config": {"workload": f"config{args.config} q{bits} decode T={T}", "bits": bits,
                    "tokens_per_step": T, "H": 2048, "I": 512, "E": 256, "top_k": 8,
-                   "weight_copies_rotated": R, "l2": "inputs rotate over R block copies > 4x L2",
-                   "parallelism": "replica" if world > 1 else "single"},
+                   "weight_copies_rotated": R, "l2": "inputs rotate over R block copies (>= 4x L2 where memory allows)",
+                   "parallelism": f"ep{world} (experts {256 // world}/GPU, NVLink exchange in-kernel)"
+                   if world > 1 else "single"},
         "e2e": {"value": e2e_us, "unit": "us/token", "h2d_bytes_per_step": T * 2048 * 2,
                 "d2h_bytes_per_step": T * 2048 * 2},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "peak_source": src, "frac_of_nominal_8tbs": achieved / HBM_NOMINAL_GBS,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm * world, "unit": "GB/s",
+                     "frac": achieved / (hbm * world), "peak_source": f"{src} x {world} GPU",
+                     "frac_of_nominal_8tbs": achieved / (HBM_NOMINAL_GBS * world),
                      "traffic": None, "algorithmic_bytes_per_step": per_step,
-                     "distinct_experts_per_step": distinct, "kernel": "k_route+k_gateup+k_down chain"},
-        "gpu_launches": 3 * K * ((T + 63) // 64),
+                     "distinct_experts_per_step": distinct,
+                     "kernel": "k_decode (persistent, one launch per step)" if persistent
+                     else "k_route+k_gateup+k_down chain" + (" + k_ep_reduce" if world > 1 else "")},
+        "gpu_launches": K if persistent else (3 + (1 if world > 1 else 0)) * K * ((T + 63) // 64),
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -322,7 +582,10 @@ def run_ours(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:
+        del g
         dist.barrier()
+        if ctx is not None:
+            ctx.close()
         dist.destroy_process_group()
 
 
@@ -347,10 +610,13 @@ def main():
     args.bits = args.bits or cfg["bits"]
     args.seed = cfg["seed"] if args.seed is None else args.seed
     args.warmup = max(args.warmup, 3)
+    prefill = cfg.get("T", 1) > 64
     if args.impl == "reference":
-        run_reference(args)
+        run_reference(args, cfg) if prefill else run_reference(args)
     elif args.profile:
-        run_profile(args)
+        run_profile(args, cfg if prefill else None)
+    elif prefill:
+        run_prefill_bench(args, cfg)
     else:
         run_ours(args)
 

@@ -91,7 +91,8 @@ typedef struct rnb_moe_desc {
 #define RNB_FLAG_SHARED_ON_THIS_RANK 0x1 /* add the shared expert (set on one EP rank only
                                             when the shared expert is split off) */
 #define RNB_FLAG_NO_SHARED 0x2           /* skip the shared expert even if pointers are set */
-#define RNB_FLAG_Y_F32 0x4               /* rnb_switchglu_fwd writes y as fp32 instead of bf16 */
+#define RNB_FLAG_Y_F32 0x4               /* rnb_switchglu_fwd / rnb_moe_block_fwd write fp32
+                                            instead of bf16 (partial sums for a cross-rank reduce) */
 #define RNB_FLAG_CHAIN 0x8               /* rnb_moe_block_fwd: use the three-kernel decode chain
                                             (in 64-token chunks) even where the persistent
                                             single-launch kernel or the prefill path applies */
@@ -157,6 +158,53 @@ RNB_API int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void
 /* Copies the device status word (RNB_STATUS_* bits) to *status and clears it.
  * Synchronises the stream. */
 RNB_API int rnb_moe_status(void* ws, size_t ws_bytes, uint32_t* status, void* stream);
+
+/* ---- Expert parallelism (one process per GPU, ranks on one node) ----
+ * Reference counterpart: none in waylake/runnel (single Apple GPU); this is
+ * the rnb_ep_* surface of the B200 build.  Rank r holds experts
+ * [expert_offset, expert_offset + E) of E_total (its rnb_moe_desc says so),
+ * the router and the shared expert; the shared expert's 128-channel
+ * intermediate quarters are split round-robin over the ranks.
+ * rnb_ep_create allocates this rank's receive buffer and writes its CUDA IPC
+ * handle (RNB_EP_HANDLE_BYTES) to handle_out; the caller gathers every rank's
+ * handle (rank order) and passes them to rnb_ep_connect.  Every rank then
+ * makes the same sequence of rnb_moe_block_ep_fwd calls with the same T; each
+ * returns the full block output (the sum over ranks, in rank order) in bf16,
+ * or fp32 with RNB_FLAG_Y_F32.  The ranks exchange partial outputs by NVLink
+ * stores inside the kernel (no multicast); device waits are bounded and set
+ * RNB_STATUS_TIMEOUT if a peer does not arrive.  Token counts the
+ * persistent decode kernel takes (T <= 2) run as one launch with the shared
+ * expert split by quarter; larger T runs in 64-token chunks of the decode
+ * chain (shared expert on rank 0) followed by an exchange kernel.
+ * Call rnb_ep_destroy on every rank after a host barrier. */
+#define RNB_EP_HANDLE_BYTES 64
+typedef struct rnb_ep rnb_ep;
+RNB_API int rnb_ep_create(int rank, int world, int H, rnb_ep** ep, void* handle_out);
+RNB_API int rnb_ep_connect(rnb_ep* ep, const void* handles);
+RNB_API int rnb_ep_destroy(rnb_ep* ep);
+RNB_API int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* x, void* out,
+                                 uint32_t* inds_out, float* scores_out, void* ws, size_t ws_bytes,
+                                 void* stream);
+
+/* Per-stage device timing (diagnostics; no reference counterpart -- the
+ * reference profiles its block from the host, bench/mlx_component_profile.py).
+ * While enabled, every block call records CUDA events on its stream between
+ * its kernels: prefill stages route, sort, scatter, gateup, down, final;
+ * decode stages decode (persistent kernel) or route, gateup, down (chain).
+ * Do not enable it while a stream is being captured into a graph.
+ * rnb_stage_times waits for the recorded calls, writes per stage the summed
+ * milliseconds over them (ms[i], i < max_stages, stage ids below) and the
+ * number of timed calls, and forgets them; returns the number of stage ids. */
+#define RNB_STAGE_DECODE 0
+#define RNB_STAGE_ROUTE 1
+#define RNB_STAGE_SORT 2
+#define RNB_STAGE_SCATTER 3
+#define RNB_STAGE_GATEUP 4
+#define RNB_STAGE_DOWN 5
+#define RNB_STAGE_FINAL 6
+#define RNB_NUM_STAGES 7
+RNB_API int rnb_stage_timing(int enable);
+RNB_API int rnb_stage_times(float* ms, int max_stages, int* calls);
 
 #ifdef __cplusplus
 }

@@ -30,6 +30,7 @@ FLAG_SHARED_ON_THIS_RANK = 0x1
 FLAG_NO_SHARED = 0x2
 FLAG_Y_F32 = 0x4
 FLAG_CHAIN = 0x8
+EP_HANDLE_BYTES = 64
 
 # Every function include/rnb_moe.h declares, with its ctypes signature.
 _vp = ctypes.c_void_p
@@ -61,7 +62,30 @@ SIGNATURES = {
     "rnb_moe_block_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "rnb_moe_status": (ctypes.c_int, [_vp, _sz, ctypes.POINTER(ctypes.c_uint32), _vp]),
     "rnb_moe_block_fwd_noalloc": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp]),
+    "rnb_ep_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp), _vp]),
+    "rnb_ep_connect": (ctypes.c_int, [_vp, _vp]),
+    "rnb_ep_destroy": (ctypes.c_int, [_vp]),
+    "rnb_moe_block_ep_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "rnb_stage_timing": (ctypes.c_int, [ctypes.c_int]),
+    "rnb_stage_times": (ctypes.c_int, [ctypes.POINTER(ctypes.c_float), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
 }
+
+STAGES = ("decode", "route", "sort", "scatter", "gateup", "down", "final")  # RNB_STAGE_* ids
+
+
+def stage_timing(enable: bool) -> None:
+    """Turn per-stage device timing of block calls on or off."""
+    load().rnb_stage_timing(1 if enable else 0)
+
+
+def stage_times() -> tuple[dict, int]:
+    """({stage: summed ms} over the timed calls since the last read, calls)."""
+    ms = (ctypes.c_float * len(STAGES))()
+    n = ctypes.c_int(0)
+    rc = load().rnb_stage_times(ms, len(STAGES), ctypes.byref(n))
+    if rc < 0:
+        raise RnbError("rnb_stage_times", rc, load().rnb_last_error().decode())
+    return {name: float(ms[i]) for i, name in enumerate(STAGES) if ms[i] > 0}, int(n.value)
 
 _lib = None
 _lock = threading.Lock()

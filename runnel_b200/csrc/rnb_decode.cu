@@ -34,6 +34,8 @@
 namespace rnb {
 
 constexpr int kMaxDecodeT = 64;
+constexpr int kMaxEpRanks = 8;
+constexpr int kEpMaxT = 64;  // tokens per exchange (receive buffers [2][world][kEpMaxT][H])
 constexpr int kMaxE = 512;
 constexpr int kMaxK = 16;
 constexpr int kRecWords = 12;
@@ -77,6 +79,17 @@ struct Params {
   float* scores_out;
   float* logits_out;
   Ws ws;
+  // Shared-expert quarters (128 intermediate channels each) this call
+  // computes: all of them, or this rank's share under expert parallelism.
+  uint32_t shared_qmask;
+  // Expert-parallel exchange (ep_world > 1): every rank's fp32 partial
+  // output goes into each rank's receive buffer [2 parities][world]
+  // [kEpMaxT][H] as 8-byte words {value, epoch}; the epoch is this rank's
+  // sequence word + 1 (device memory, so graph replays advance it; the
+  // kernel's last CTA increments it).
+  int ep_world, ep_rank;
+  uint2* ep_recv[kMaxEpRanks];
+  uint32_t* ep_seq;  // [0] sequence word, [1] exit counter of k_ep_reduce
 };
 
 // Optional phase timeline (compile with -DRNB_TRACE): thread 0 of each CTA
@@ -89,6 +102,9 @@ __device__ __forceinline__ void trace_mark(const Params& p, int i) {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 16 + i] = t;
   }
+}
+__device__ __forceinline__ void trace_value(const Params& p, int i, int v) {
+  reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 16 + i] = static_cast<uint64_t>(v);
 }
 #define RNB_TRACE_MARK(p, i) trace_mark(p, i)
 #else
@@ -828,7 +844,10 @@ __global__ void __launch_bounds__(32 * kDownMaxWarps) k_down(Params p) {
       }
     }
     if (p.has_shared) acc += sg * ysh;
-    out[static_cast<size_t>(t) * p.H + n] = __float2bfloat16_rn(acc);
+    if (p.y_f32)
+      static_cast<float*>(p.out)[static_cast<size_t>(t) * p.H + n] = acc;
+    else
+      out[static_cast<size_t>(t) * p.H + n] = __float2bfloat16_rn(acc);
   }
   __syncthreads();
   if (threadIdx.x == 0) atomicExch(p.ws.ctr + 1 + blockIdx.x, 0u);
@@ -857,6 +876,8 @@ __global__ void __launch_bounds__(32 * kDownMaxWarps) k_down(Params p) {
 constexpr int kPWarps = 16;
 constexpr int kPMaxT = 8;
 constexpr uint64_t kSpinLimitNs = 200ull * 1000 * 1000;  // a wait gives up after 200 ms
+// Waits on other GPUs: ranks launch independently, so allow host-side skew.
+constexpr uint64_t kEpSpinLimitNs = 2000ull * 1000 * 1000;
 
 // Two-group weight tile of one warp (16 rows x 128 inputs): codes with a
 // 16-byte-chunk XOR swizzle instead of padding, then bf16 scales and biases.
@@ -1120,6 +1141,84 @@ __device__ __forceinline__ void p_gateup_epilogue(const Params& p, const float* 
   if (ok && r == 0) p.ws.hmaxp[static_cast<size_t>(id) * (p.I / 8) + tk.ch0 / 8] = m;
 }
 
+// Expert-parallel all-reduce of one 16-column output tile for T tokens.
+// Every rank's fp32 partial part(t, r) (t < T, r < 16) goes to each rank as
+// one 8-byte store {value, epoch} (single-copy atomic), so a word that
+// carries this call's epoch carries this call's value: the receiver polls
+// the words themselves, with no separate flag and no fence, and sums the
+// ranks' values in rank order (the same order on every rank) before
+// handing them to emit(t, r, sum).  Polls are bounded; on timeout the status
+// word gets RNB_STATUS_TIMEOUT and that value is not emitted.  Buffers
+// alternate by epoch parity: a rank cannot start epoch e+2 before every rank
+// has sent epoch e+1, which each rank does only after reading epoch e.
+template <typename Part, typename Emit>
+__device__ void ep_exchange_tile(const Params& p, int n0, int T, Part part, Emit emit) {
+  const int tid = threadIdx.x, W = p.ep_world;
+  __shared__ uint32_t s_epoch;
+  if (tid == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(p.ep_seq) + 1u;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const size_t par = static_cast<size_t>(epoch & 1u) * W * kEpMaxT * p.H;
+  for (int i = tid; i < T * 16; i += blockDim.x) {
+    const int t = i >> 4, r = i & 15;
+    const uint32_t v = __float_as_uint(part(t, r));
+    const size_t o = par + (static_cast<size_t>(p.ep_rank) * kEpMaxT + t) * p.H + n0 + r;
+    for (int q = 0; q < W; ++q)
+      asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};\n" ::"l"(p.ep_recv[q] + o), "r"(v), "r"(epoch)
+                   : "memory");
+  }
+  for (int i = tid; i < T * 16; i += blockDim.x) {
+    const int t = i >> 4, r = i & 15;
+    const uint2* own = p.ep_recv[p.ep_rank] + par + static_cast<size_t>(t) * p.H + n0 + r;
+    float sum = 0.f;
+    bool ok = true;
+    for (int q = 0; q < W && ok; ++q) {
+      const uint2* src = own + static_cast<size_t>(q) * kEpMaxT * p.H;
+      uint32_t val, ep;
+      uint64_t t0 = 0, now;
+      for (int spin = 0;; ++spin) {
+        asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];\n" : "=r"(val), "=r"(ep) : "l"(src) : "memory");
+        if (ep == epoch) break;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+        if (spin == 0) t0 = now;
+        if (now - t0 > kEpSpinLimitNs) {
+          atomicOr(p.ws.status, RNB_STATUS_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+      sum += __uint_as_float(val);
+    }
+    if (ok) emit(t, r, sum);
+  }
+}
+
+// Expert-parallel reduction after the decode chain: CTA b owns output
+// columns [16b, 16b+16) of the fp32 partial (p.ws.yws reused as [T][H]).
+// Cooperative launch, so every CTA is resident while it waits for peers.
+__global__ void __launch_bounds__(256) k_ep_reduce(Params p, const float* partial) {
+  const int n0 = blockIdx.x * 16;
+  ep_exchange_tile(
+      p, n0, p.T, [&](int t, int r) { return __ldcg(partial + static_cast<size_t>(t) * p.H + n0 + r); },
+      [&](int t, int r, float v) {
+        const size_t o = static_cast<size_t>(t) * p.H + n0 + r;
+        if (p.y_f32)
+          static_cast<float*>(p.out)[o] = v;
+        else
+          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
+      });
+  // the last CTA out advances the sequence word for the next exchange
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.ep_seq + 1, 1u) == gridDim.x - 1) {
+      p.ep_seq[1] = 0;
+      p.ep_seq[0] += 1;
+      __threadfence();
+    }
+  }
+}
+
 template <int BITS>
 __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) {
   extern __shared__ __align__(16) char sm[];
@@ -1144,7 +1243,10 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   uint32_t* bar2 = bar1 + 1;
   uint32_t* exitc = bar1 + 2;
   const bool owns_router = cta < pl.n_rtiles;
-  const bool owns_sgu = p.has_shared && cta >= pl.n_rtiles && cta < pl.n_rtiles + n_ch;
+  const bool owns_sgu = p.has_shared && cta >= pl.n_rtiles && cta < pl.n_rtiles + n_ch &&
+                        ((p.shared_qmask >> (((cta - pl.n_rtiles) * 8) / 128)) & 1u);
+  const int n_sch = p.has_shared ? __popc(p.shared_qmask & ((1u << nq) - 1u)) * 16 : 0;  // shared gate/up tasks
+  auto is_local = [&](uint32_t e) { return e - static_cast<uint32_t>(p.off) < static_cast<uint32_t>(p.E); };
   const int n0 = cta * 16;
   const bool owns_rows = n0 < p.H;
   auto gu_row = [&](int ch0) { return [=](int i) -> size_t { return i < 8 ? ch0 + i : p.I + ch0 + i - 8; }; };
@@ -1169,7 +1271,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     tile2_issue<BITS>(sBR + warp * TL::kBytes, p.sgu_w, p.sgu_s, p.sgu_b, gwrow, gsrow, warp * 2, gu_row(ch0), lane);
   }
   cp_async_commit();  // group: shared gate/up
-  if (owns_rows && p.has_shared && warp < nq) {
+  if (owns_rows && p.has_shared && warp < nq && ((p.shared_qmask >> warp) & 1u)) {
     // phase-C slots 0..nq-1: shared expert down, K quarter = warp
     tile2_issue<BITS>(sCR + warp * TL::kBytes, p.sdn_w, p.sdn_s, p.sdn_b, dwrow, dsrow, warp * 2, dn_row, lane);
   }
@@ -1237,7 +1339,15 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     const uint32_t* ivl = reinterpret_cast<const uint32_t*>(sH + t * (Et + 1));
     int e;
     float sc;
-    warp_route_token(ivl, Et, K, p.x + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane, false, nullptr, &e, &sc);
+    RNB_TRACE_MARK(p, 12);
+    const int nre = warp_route_token(ivl, Et, K, p.x + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane, false,
+                                     nullptr, &e, &sc);
+    RNB_TRACE_MARK(p, 13);
+#ifdef RNB_TRACE
+    if (t == 0 && lane == 0) trace_value(p, 11, nre);
+#else
+    (void)nre;
+#endif
     if (lane < K) {
       ms->inds[t][lane] = static_cast<uint32_t>(e);
       ms->scores[t][lane] = sc;
@@ -1248,22 +1358,29 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   RNB_TRACE_MARK(p, 15);
   // per-expert token lists: entry i = t*K + slot, ordered by (expert, i);
   // one token: its K distinct experts in slot order
+  // (act_e holds local expert indices; experts of other ranks are left out)
   if (T == 1) {
-    if (tid < K) {
-      ms->act_e[tid] = ms->inds[0][tid];
-      ms->act_cnt[tid] = 1;
-      ms->act_ent[tid][0] = static_cast<uint32_t>(tid);
+    if (tid == 0) {
+      uint32_t n = 0;
+      for (int s2 = 0; s2 < K; ++s2) {
+        const uint32_t e = ms->inds[0][s2];
+        if (!is_local(e)) continue;
+        ms->act_e[n] = e - static_cast<uint32_t>(p.off);
+        ms->act_cnt[n] = 1;
+        ms->act_ent[n][0] = static_cast<uint32_t>(s2);
+        ++n;
+      }
+      ms->n_act = n;
     }
-    if (tid == 0) ms->n_act = static_cast<uint32_t>(K);
   } else if (tid < T * K) {
     const uint32_t e = ms->inds[tid / K][tid % K];
-    bool first = true;
+    bool first = is_local(e);
     for (int q = 0; q < tid; ++q)
       if (ms->inds[q / K][q % K] == e) first = false;
     ms->first[tid] = first;
   }
   __syncthreads();
-  if (T > 1 && tid < T * K) {
+  if (T > 1 && tid < T * K && is_local(ms->inds[tid / K][tid % K])) {
     const int i = tid;
     const uint32_t e = ms->inds[i / K][i % K];
     uint32_t a = 0, cnt = 0, pos = 0;
@@ -1277,7 +1394,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     }
     ms->act_ent[a][pos] = static_cast<uint32_t>((i / K) * (K + 1) + (i % K));
     if (ms->first[i]) {
-      ms->act_e[a] = e;
+      ms->act_e[a] = e - static_cast<uint32_t>(p.off);
       ms->act_cnt[a] = cnt;
     }
   }
@@ -1352,7 +1469,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   if (owns_rows) {
     cp_async_wait_pending(0);
     __syncwarp();
-    cta_wait_count(bar2, static_cast<uint32_t>(n_btask + (p.has_shared ? n_ch : 0)), p.ws.status);
+    cta_wait_count(bar2, static_cast<uint32_t>(n_btask + n_sch), p.ws.status);
     RNB_TRACE_MARK(p, 8);
     // this warp's tasks q = warp, warp + 16, ... in batches of pl.cb: stage
     // each task's activations (128 per column) and column maxima (I/8 per
@@ -1367,6 +1484,9 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
         const int q = q0 + bq * kPWarps;
         if (q >= n_ctask) break;
         const bool shared = q < c_base;
+        ++nb;
+        ent_b[bq] = 0;
+        if (shared && !((p.shared_qmask >> q) & 1u)) continue;  // another rank's quarter
         const int a = shared ? 0 : (q - c_base) / nq, qq = shared ? q : (q - c_base) % nq;
         const int ncols = shared ? T : static_cast<int>(ms->act_cnt[a]);
         uint32_t ent_l = 0;
@@ -1390,7 +1510,6 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
             cp_async16(mq + col * nt_i + piece * 4, p.ws.hmaxp + static_cast<size_t>(id) * nt_i + piece * 4);
         }
         ent_b[bq] = ent_l;
-        ++nb;
       }
       cp_async_commit();
       cp_async_wait_pending(0);
@@ -1398,6 +1517,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
       for (int bq = 0; bq < nb; ++bq) {
         const int q = q0 + bq * kPWarps;
         const bool shared = q < c_base;
+        if (shared && !((p.shared_qmask >> q) & 1u)) continue;
         const int a = shared ? 0 : (q - c_base) / nq, qq = shared ? q : (q - c_base) % nq;
         const int ncols = shared ? T : static_cast<int>(ms->act_cnt[a]);
         const uint32_t ent_l = ent_b[bq];
@@ -1489,19 +1609,37 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     const int nsrc = K + (p.has_shared ? 1 : 0);
     for (int q = tid; q < T * nsrc * 16; q += blockDim.x) {
       const int t = q / (nsrc * 16), s = (q / 16) % nsrc, r = q % 16;
+      if (s < K && !is_local(ms->inds[t][s])) continue;
       float* y = sRedC + static_cast<size_t>(t * (K + 1) + (s < K ? s : K)) * nq * 16;
       float ys = 0.f;
-      for (int qq = 0; qq < nq; ++qq) ys += y[qq * 16 + r];
+      for (int qq = 0; qq < nq; ++qq)
+        if (s < K || ((p.shared_qmask >> qq) & 1u)) ys += y[qq * 16 + r];
       y[r] = ys;
     }
     __syncthreads();
+    float acc = 0.f;
     if (tid < T * 16) {
       const int t = tid >> 4, r = tid & 15;
-      float acc = 0.f;
       for (int s = 0; s < K; ++s)
-        acc += ms->scores[t][s] * sRedC[static_cast<size_t>(t * (K + 1) + s) * nq * 16 + r];
-      if (p.has_shared) acc += ms->sg[t] * sRedC[static_cast<size_t>(t * (K + 1) + K) * nq * 16 + r];
-      static_cast<__nv_bfloat16*>(p.out)[static_cast<size_t>(t) * p.H + n0 + r] = __float2bfloat16_rn(acc);
+        if (is_local(ms->inds[t][s])) acc += ms->scores[t][s] * sRedC[static_cast<size_t>(t * (K + 1) + s) * nq * 16 + r];
+      if (p.has_shared && (p.shared_qmask & ((1u << nq) - 1u)))
+        acc += ms->sg[t] * sRedC[static_cast<size_t>(t * (K + 1) + K) * nq * 16 + r];
+    }
+    auto emit = [&](int t, int r, float v) {
+      const size_t o = static_cast<size_t>(t) * p.H + n0 + r;
+      if (p.y_f32)
+        static_cast<float*>(p.out)[o] = v;
+      else
+        static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
+    };
+    RNB_TRACE_MARK(p, 14);
+    if (p.ep_world > 1) {
+      float* stage = sRed;  // this tile's partials, [t][r]
+      if (tid < T * 16) stage[tid] = acc;
+      __syncthreads();
+      ep_exchange_tile(p, n0, T, [&](int t, int r) { return stage[t * 16 + r]; }, emit);
+    } else if (tid < T * 16) {
+      emit(tid >> 4, tid & 15, acc);
     }
   }
 
@@ -1516,6 +1654,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
       atomicExch(bar1, 0u);
       atomicExch(bar2, 0u);
       atomicExch(exitc, 0u);
+      if (p.ep_world > 1) p.ep_seq[0] += 1;  // every CTA's exchange is done
       __threadfence();
     }
   }
@@ -1678,7 +1817,7 @@ size_t persistent_static_smem() {
 template <int BITS>
 bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem) {
   if (p.mode != kModeBlock || p.T < 1 || p.T > kPMaxT || p.H != 2048 || p.I != 512 || p.E_total > 256 ||
-      p.k > 8 || p.off != 0 || p.E != p.E_total)
+      p.k > 8 || p.off < 0 || p.off + p.E > p.E_total)
     return false;
   pl.n_rtiles = (p.E_total + 1 + 15) / 16;
   if (di.sms < p.H / 16 || di.sms < pl.n_rtiles + p.I / 8) return false;
@@ -1732,8 +1871,10 @@ int run_persistent(Params& p, const PPlan& pl, size_t smem, int nc, cudaStream_t
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  stage_begin(st);
   e = cudaLaunchKernelEx(&cfg, k_decode<BITS>, p, pl);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_decode launch: ") + cudaGetErrorString(e));
+  stage_end(st, RNB_STAGE_DECODE);
   return RNB_OK;
 }
 
@@ -1750,8 +1891,10 @@ int run_decode(const rnb_moe_desc* d, Params& p, cudaStream_t st) {
   const int prep_ctas = p.mode == kModeRouter ? 0 : (p.T + 15) / 16;
   // Programmatic launch: k_route streams its router weights in while the
   // previous kernel on the stream finishes, and waits before touching x.
+  stage_begin(st);
   cudaError_t e = launch(k_route<BITS>, dim3(p.router_ctas + prep_ctas), dim3(32 * kRouterWarps), st, true, p);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_route launch: ") + cudaGetErrorString(e));
+  stage_end(st, RNB_STAGE_ROUTE);
   if (p.mode == kModeRouter) return RNB_OK;
   const int slots = 1 + (p.T * p.k < p.E ? p.T * p.k : p.E);
   p.ncmax = p.T < 8 ? p.T : 8;
@@ -1771,8 +1914,10 @@ int run_decode(const rnb_moe_desc* d, Params& p, cudaStream_t st) {
   }
   e = launch(k_gateup<BITS>, dim3(p.I / 8, slots), dim3(32 * gnw), st, true, p, gsm);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_gateup launch: ") + cudaGetErrorString(e));
+  stage_end(st, RNB_STAGE_GATEUP);
   e = launch(k_down<BITS>, dim3(p.H / 16, slots), dim3(32 * dnw), st, true, p, dsm);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_down launch: ") + cudaGetErrorString(e));
+  stage_end(st, RNB_STAGE_DOWN);
   return RNB_OK;
 }
 
@@ -1804,6 +1949,9 @@ Params base_params(const rnb_moe_desc* d, const void* x, void* ws, int mode) {
   p.sdn_s = d->sdn_s;
   p.sdn_b = d->sdn_b;
   p.ws = bind(make_layout(*d), ws);
+  p.shared_qmask = (1u << (d->I / 128)) - 1u;
+  p.ep_world = 1;
+  p.y_f32 = (mode == kModeBlock && (d->flags & RNB_FLAG_Y_F32)) ? 1 : 0;
   return p;
 }
 
@@ -1991,6 +2139,179 @@ int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void* out, u
   const cudaError_t e = cudaMemsetAsync(ws, 0, L.xperm, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("clearing scratch counters: ") + cudaGetErrorString(e));
   return rnb_moe_block_fwd(d, x, out, inds_out, scores_out, ws, kNoAllocScratchBytes, stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ expert parallel
+
+struct rnb_ep {
+  int rank = 0, world = 1, H = 0, dev = 0;
+  size_t recv_bytes = 0, bytes = 0;
+  void* local = nullptr;
+  uint2* recv[rnb::kMaxEpRanks] = {};
+  void* opened[rnb::kMaxEpRanks] = {};
+  float* partial = nullptr;  // [kEpMaxT][H] fp32: the chain's partial before the exchange
+  uint32_t* seq = nullptr;   // this rank's sequence word and exit counter (after the flags)
+  bool connected = false;
+};
+
+namespace rnb {
+namespace {
+
+size_t ep_recv_bytes(int world, int H) { return static_cast<size_t>(2) * world * kEpMaxT * H * sizeof(uint2); }
+constexpr size_t kEpSeqBytes = 256;  // sequence word and exit counter after the receive buffer
+
+}  // namespace
+}  // namespace rnb
+
+extern "C" {
+
+int rnb_ep_create(int rank, int world, int H, rnb_ep** ep_out, void* handle_out) {
+  using namespace rnb;
+  if (!ep_out || !handle_out) return fail(RNB_ERR_INVALID, "rnb_ep_create: NULL output pointer");
+  *ep_out = nullptr;
+  if (world < 1 || world > kMaxEpRanks || rank < 0 || rank >= world)
+    return fail(RNB_ERR_INVALID, "rnb_ep_create: need 0 <= rank < world <= 8");
+  if (H <= 0 || H % 16) return fail(RNB_ERR_INVALID, "rnb_ep_create: H must be a positive multiple of 16");
+  int rc = check_device();
+  if (rc) return rc;
+  rnb_ep* ep = new rnb_ep();
+  ep->rank = rank;
+  ep->world = world;
+  ep->H = H;
+  cudaGetDevice(&ep->dev);
+  ep->recv_bytes = ep_recv_bytes(world, H);
+  ep->bytes = ep->recv_bytes + kEpSeqBytes;
+  cudaError_t e = cudaMalloc(&ep->local, ep->bytes);
+  if (e == cudaSuccess) e = cudaMemset(ep->local, 0, ep->bytes);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&ep->partial), static_cast<size_t>(kEpMaxT) * H * 4);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, ep->local);
+  if (e != cudaSuccess) {
+    if (ep->local) cudaFree(ep->local);
+    if (ep->partial) cudaFree(ep->partial);
+    delete ep;
+    return fail(RNB_ERR_CUDA, std::string("rnb_ep_create: ") + cudaGetErrorString(e));
+  }
+  memcpy(handle_out, &h, sizeof(h));
+  ep->recv[rank] = static_cast<uint2*>(ep->local);
+  ep->seq = reinterpret_cast<uint32_t*>(static_cast<char*>(ep->local) + ep->recv_bytes);
+  *ep_out = ep;
+  return RNB_OK;
+}
+
+int rnb_ep_connect(rnb_ep* ep, const void* handles) {
+  using namespace rnb;
+  if (!ep || !handles) return fail(RNB_ERR_INVALID, "rnb_ep_connect: NULL argument");
+  if (ep->connected) return fail(RNB_ERR_INVALID, "rnb_ep_connect: already connected");
+  for (int q = 0; q < ep->world; ++q) {
+    if (q == ep->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const char*>(handles) + static_cast<size_t>(q) * RNB_EP_HANDLE_BYTES, sizeof(h));
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int j = 0; j < q; ++j)
+        if (ep->opened[j]) {
+          cudaIpcCloseMemHandle(ep->opened[j]);
+          ep->opened[j] = nullptr;
+        }
+      return fail(RNB_ERR_CUDA, std::string("rnb_ep_connect: peer ") + std::to_string(q) + ": " +
+                                    cudaGetErrorString(e));
+    }
+    ep->opened[q] = ptr;
+    ep->recv[q] = static_cast<uint2*>(ptr);
+  }
+  ep->connected = true;
+  return RNB_OK;
+}
+
+int rnb_ep_destroy(rnb_ep* ep) {
+  if (!ep) return RNB_OK;
+  for (int q = 0; q < ep->world; ++q)
+    if (ep->opened[q]) cudaIpcCloseMemHandle(ep->opened[q]);
+  if (ep->local) cudaFree(ep->local);
+  if (ep->partial) cudaFree(ep->partial);
+  delete ep;
+  return RNB_OK;
+}
+
+int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* x, void* out, uint32_t* inds_out,
+                         float* scores_out, void* ws, size_t ws_bytes, void* stream) {
+  using namespace rnb;
+  if (!ep) return fail(RNB_ERR_INVALID, "rnb_moe_block_ep_fwd: ep is NULL");
+  if (ep->world > 1 && !ep->connected) return fail(RNB_ERR_INVALID, "rnb_moe_block_ep_fwd: call rnb_ep_connect first");
+  int rc = validate(d, true, true);
+  if (!rc) rc = check_device();
+  if (!rc) rc = check_ws(d, ws, ws_bytes);
+  if (rc) return rc;
+  if (!x || !out) return fail(RNB_ERR_INVALID, "x and out must be non-NULL");
+  if (!aligned16(x) || !aligned16(out)) return fail(RNB_ERR_ALIGN, "x and out must be 16-byte aligned");
+  if (d->H != ep->H) return fail(RNB_ERR_INVALID, "rnb_moe_block_ep_fwd: H differs from the EP context's");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != ep->dev) return fail(RNB_ERR_INVALID, "rnb_moe_block_ep_fwd: current device is not the EP context's");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto set_ep = [&](Params& p) {
+    p.ep_world = ep->world;
+    p.ep_rank = ep->rank;
+    for (int q = 0; q < ep->world; ++q) {
+      p.ep_recv[q] = ep->recv[q];
+    }
+    p.ep_seq = ep->seq;
+  };
+  // Few tokens: one persistent launch; the shared expert's 128-channel
+  // quarters are split round-robin over the ranks and the partial tiles are
+  // exchanged inside the kernel.
+  {
+    Params p = base_params(d, x, ws, kModeBlock);
+    p.out = out;
+    p.inds_out = inds_out;
+    p.scores_out = scores_out;
+    const int nq = d->I / 128;
+    p.shared_qmask = 0;
+    for (int q = ep->rank; q < nq; q += ep->world) p.shared_qmask |= 1u << q;
+    const DevInfo di = dev_info();
+    PPlan pl;
+    size_t smem = 0;
+    const bool ok = d->bits == 8 ? persistent_plan<8>(p, di, pl, smem) : persistent_plan<4>(p, di, pl, smem);
+    if (ok) {
+      set_ep(p);
+      return d->bits == 8 ? run_persistent<8>(p, pl, smem, di.sms, st) : run_persistent<4>(p, pl, smem, di.sms, st);
+    }
+  }
+  // Otherwise per 64-token chunk: the decode chain writes this rank's fp32
+  // partial (shared expert on rank 0), then k_ep_reduce exchanges and sums.
+  rnb_moe_desc dc = *d;
+  dc.flags |= RNB_FLAG_CHAIN | RNB_FLAG_Y_F32;
+  if (ep->rank != 0) dc.flags |= RNB_FLAG_NO_SHARED;
+  const bool f32_out = (d->flags & RNB_FLAG_Y_F32) != 0;
+  return for_chunks(&dc, [&](const rnb_moe_desc& c, int t0) {
+    Params p = base_params(&c, static_cast<const uint16_t*>(x) + static_cast<size_t>(t0) * c.H, ws, kModeBlock);
+    p.out = ep->partial;
+    p.inds_out = inds_out ? inds_out + static_cast<size_t>(t0) * c.k : nullptr;
+    p.scores_out = scores_out ? scores_out + static_cast<size_t>(t0) * c.k : nullptr;
+    int rc2 = dispatch_bits(&c, p, st);
+    if (rc2) return rc2;
+    Params r = p;
+    r.y_f32 = f32_out ? 1 : 0;
+    r.out = f32_out ? static_cast<void*>(static_cast<float*>(out) + static_cast<size_t>(t0) * c.H)
+                    : static_cast<void*>(static_cast<uint16_t*>(out) + static_cast<size_t>(t0) * c.H);
+    set_ep(r);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c.H / 16);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_ep_reduce, r, static_cast<const float*>(ep->partial));
+    if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_ep_reduce launch: ") + cudaGetErrorString(e));
+    return RNB_OK;
+  });
 }
 
 }  // extern "C"

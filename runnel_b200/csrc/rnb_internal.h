@@ -29,6 +29,10 @@ DevInfo dev_info();
 constexpr size_t kWsCountersOffset = 256;
 inline size_t ws_counter_bytes(const rnb_moe_desc& d) { return 4u * (4u + static_cast<size_t>(d.H) / 16u); }
 
+// Stage timing (rnb_timing.cu): no-ops unless rnb_stage_timing(1) was called.
+void stage_begin(cudaStream_t st);
+void stage_end(cudaStream_t st, int stage);
+
 // Prefill path (many tokens): workspace bytes it needs for d->T tokens, and
 // whether it supports the descriptor's shapes.
 size_t prefill_workspace_bytes(const rnb_moe_desc& d);

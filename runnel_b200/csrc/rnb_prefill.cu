@@ -69,14 +69,14 @@ struct Ws {
 };
 
 struct Params {
-  int T, H, I, E, E_total, off, k, has_shared;
+  int T, H, I, E, E_total, off, k, has_shared, y_f32;
   int rows_cap, max_mt;
   const uint16_t* x;
   const uint16_t* router_w;
   const uint16_t* sgate_w;
   const uint32_t *gu_w, *dn_w, *sgu_w, *sdn_w;
   const uint16_t *gu_s, *gu_b, *dn_s, *dn_b, *sgu_s, *sgu_b, *sdn_s, *sdn_b;
-  __nv_bfloat16* out;
+  void* out;  // bf16 [T][H], or fp32 with y_f32
   uint32_t* inds_out;
   float* scores_out;
   Ws ws;
@@ -193,12 +193,12 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
       const int tA = n * 8 + 2 * c, tB = tA + 1;
       const float xiA = __uint_as_float(xmax[tA]), xiB = __uint_as_float(xmax[tB]);
       if (row_a < Et) {
-        lgu[tA][row_a] = route_interval(acc[n][0], xn2[tA], xiA, wa2, wa1);
-        lgu[tB][row_a] = route_interval(acc[n][1], xn2[tB], xiB, wa2, wa1);
+        lgu[tA][row_a] = route_interval(acc[n][0], xn2[tA], xiA, wa2, wa1, kRouteRelPrefill);
+        lgu[tB][row_a] = route_interval(acc[n][1], xn2[tB], xiB, wa2, wa1, kRouteRelPrefill);
       }
       if (row_b < Et) {
-        lgu[tA][row_b] = route_interval(acc[n][2], xn2[tA], xiA, wb2, wb1);
-        lgu[tB][row_b] = route_interval(acc[n][3], xn2[tB], xiB, wb2, wb1);
+        lgu[tA][row_b] = route_interval(acc[n][2], xn2[tA], xiA, wb2, wb1, kRouteRelPrefill);
+        lgu[tB][row_b] = route_interval(acc[n][3], xn2[tB], xiB, wb2, wb1, kRouteRelPrefill);
       }
     }
   }
@@ -699,6 +699,10 @@ __global__ void k_pre_final(Params p) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const float4 v = __ldcg(reinterpret_cast<const float4*>(p.ws.acc) + i);
+    if (p.y_f32) {
+      reinterpret_cast<float4*>(p.out)[i] = v;
+      continue;
+    }
     const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
     uint2 o;
     o.x = *reinterpret_cast<const uint32_t*>(&a);
@@ -759,6 +763,7 @@ template <int BITS>
 static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st) {
   using namespace pre;
   cudaError_t e;
+  stage_begin(st);
   // zero the histogram and the fp32 accumulator; padding rows of perm = ~0
   e = cudaMemsetAsync(p.ws.counts, 0, (p.E + 1) * 4, st);
   if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.perm, 0xFF, static_cast<size_t>(L.rows_cap) * 4, st);
@@ -777,13 +782,19 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
     attr = true;
   }
   k_pre_route<<<(p.T + kRouteT - 1) / kRouteT, 512, kRouteSmem, st>>>(p);
+  stage_end(st, RNB_STAGE_ROUTE);
   k_pre_sort<<<1, 512, 0, st>>>(p);
+  stage_end(st, RNB_STAGE_SORT);
   const size_t n_scatter = static_cast<size_t>(p.T) * (p.k + 1);
   k_pre_scatter<<<static_cast<unsigned>((n_scatter + 255) / 256), 256, 0, st>>>(p);
+  stage_end(st, RNB_STAGE_SCATTER);
   const int nc = dev_info().sms;
   k_pre_gemm<BITS, 0><<<nc, kThreads, GemmCfg<0>::kSmem, st>>>(p);
+  stage_end(st, RNB_STAGE_GATEUP);
   k_pre_gemm<BITS, 1><<<nc, kThreads, GemmCfg<1>::kSmem, st>>>(p);
+  stage_end(st, RNB_STAGE_DOWN);
   k_pre_final<<<nc * 4, 256, 0, st>>>(p);
+  stage_end(st, RNB_STAGE_FINAL);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e));
   return RNB_OK;
@@ -821,7 +832,8 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
   p.sdn_w = d->sdn_w;
   p.sdn_s = d->sdn_s;
   p.sdn_b = d->sdn_b;
-  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out = out;
+  p.y_f32 = (d->flags & RNB_FLAG_Y_F32) ? 1 : 0;
   p.inds_out = inds_out;
   p.scores_out = scores_out;
   char* b = static_cast<char*>(ws);

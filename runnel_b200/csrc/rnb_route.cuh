@@ -6,10 +6,10 @@
 // in every product but rounds partial sums, so the fp32 value L may sit on
 // the other side of a bf16 rounding midpoint than the exact one.  Each fp32
 // logit is therefore published as an interval of bf16 candidates
-//     lo = bf16(L - B),  hi = bf16(L + B),  B = 2^-16 |x|_2 |w_e|_2 + 2^-21 |L|
-// (|x|_2 |w_e|_2 >= sum |x_i w_i| by Cauchy-Schwarz, so B allows two fp32
-// ulps of error per 16-wide MMA step over a chain of 128 steps at the
-// largest possible partial sum).  lo == hi certifies the rounding.  The
+//     lo = bf16(L - B),  hi = bf16(L + B),  B = rel |x|_2 |w_e|_2 + 2^-21 |L|
+// (|x|_2 |w_e|_2 >= sum |x_i w_i| by Cauchy-Schwarz; rel allows two fp32
+// ulps of error per accumulation step at the largest possible partial sum,
+// see kRouteRel*).  lo == hi certifies the rounding.  The
 // selection warp recomputes, in fp64 from the bf16 inputs, exactly those
 // uncertain logits that could still reach the top k; every selected logit
 // is then the correctly rounded value, and so is the selection.
@@ -55,15 +55,22 @@ __device__ __forceinline__ uint16_t f64_to_bf16_bits(double v) {
   return static_cast<uint16_t>((sign << 15) | (static_cast<uint32_t>(fe) << 7) | q);
 }
 
-// Packed candidate interval (lo | hi << 16) of an fp32 logit L.  Norms of
-// the token (xn2 = sum x^2, xinf = max |x|) and of the router row (wn2 =
-// sum w^2, wn1 = sum |w|), fp32: the bound uses |x|_2 |w|_2 when the squares
-// cannot have underflowed, else |x|_inf |w|_1 (both >= sum |x_i w_i|; an
-// all-zero token gets B = 0, its logits are exact zeros).
-__device__ __forceinline__ uint32_t route_interval(float L, float xn2, float xinf, float wn2, float wn1) {
+// Error allowances (multiples of sum |x_i w_i|): two fp32 ulps per MMA step
+// and per cross-warp add.  Decode routers accumulate 8 k16 steps per warp
+// and add 16 warp partials; the prefill router accumulates 128 steps.
+constexpr float kRouteRelDecode = 0x1p-18f;
+constexpr float kRouteRelPrefill = 0x1p-16f;
+
+// Packed candidate interval (lo | hi << 16) of an fp32 logit L with error
+// allowance rel * sum |x_i w_i|.  Norms of the token (xn2 = sum x^2, xinf =
+// max |x|) and of the router row (wn2 = sum w^2, wn1 = sum |w|), fp32: the
+// bound uses |x|_2 |w|_2 when the squares cannot have underflowed, else
+// |x|_inf |w|_1 (both >= sum |x_i w_i|; an all-zero token gets B = 0, its
+// logits are exact zeros).
+__device__ __forceinline__ uint32_t route_interval(float L, float xn2, float xinf, float wn2, float wn1, float rel) {
   float nb = xinf * wn1;
   if (xn2 >= 0x1p-100f && wn2 >= 0x1p-100f) nb = fminf(nb, sqrtf(xn2) * sqrtf(wn2));
-  const float B = 0x1p-16f * 1.001f * nb + 0x1p-21f * fabsf(L);
+  const float B = rel * 1.001f * nb + 0x1p-21f * fabsf(L);
   if (!(B <= 3.0e38f) || L != L) return 0xFF80u | (0x7F80u << 16);  // (-inf, +inf): recompute
   const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(L - B));
   const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(L + B));
@@ -126,25 +133,33 @@ __device__ __forceinline__ uint32_t router_interval_from(const float* part, int 
     wn2 += q[16 + r];  // rows 8..15 continue into [24, 32)
     wn1 += q[32 + r];
   }
-  return route_interval(L, xn2, xinf, wn2, wn1);
+  return route_interval(L, xn2, xinf, wn2, wn1, kRouteRelDecode);
 }
 
 // fp64 dot product of two bf16 rows of length H (H % 8 == 0, 16-byte
 // aligned), warp-cooperative; every lane returns the sum.  bf16 products are
 // exact in fp64 and the fp64 sum of up to 2^11 of them errs by < 2^-42 of
-// sum |x_i w_i|.
+// sum |x_i w_i|.  All of a 2048-wide chunk's loads are issued before any
+// arithmetic (one memory round trip per chunk).
 static __device__ __noinline__ double warp_dot_f64(const uint16_t* x, const uint16_t* w, int H, int lane) {
   double a0 = 0.0, a1 = 0.0;
-#pragma unroll 2
-  for (int k = lane * 8; k < H; k += 256) {
-    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + k));
-    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + k));
-    const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
+  for (int k0 = 0; k0 < H; k0 += 2048) {
+    uint4 xv[8], wv[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      a0 = fma(static_cast<double>(__uint_as_float(xs[j] << 16)), static_cast<double>(__uint_as_float(ws[j] << 16)), a0);
-      a1 = fma(static_cast<double>(__uint_as_float(xs[j] & 0xFFFF0000u)),
-               static_cast<double>(__uint_as_float(ws[j] & 0xFFFF0000u)), a1);
+    for (int j = 0; j < 8; ++j) {
+      const int k = k0 + j * 256 + lane * 8;
+      xv[j] = k < H ? __ldg(reinterpret_cast<const uint4*>(x + k)) : make_uint4(0, 0, 0, 0);
+      wv[j] = k < H ? __ldg(reinterpret_cast<const uint4*>(w + k)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t xs[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w}, ws[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a0 = fma(static_cast<double>(__uint_as_float(xs[i] << 16)), static_cast<double>(__uint_as_float(ws[i] << 16)), a0);
+        a1 = fma(static_cast<double>(__uint_as_float(xs[i] & 0xFFFF0000u)),
+                 static_cast<double>(__uint_as_float(ws[i] & 0xFFFF0000u)), a1);
+      }
     }
   }
   double s = a0 + a1;
@@ -181,57 +196,62 @@ __device__ __forceinline__ uint32_t warp_select_k(const uint32_t (&keys)[8], int
 // One token's routing, by one full warp.  ivl[e] (e < Et <= 256) holds the
 // packed candidate interval of expert e's logit.  Lane s < K returns the
 // s-th selected expert (descending logit, ties to the lower index) in *e_out
-// and its weight, softmax over all Et logits gathered at the selection and
-// renormalised, in *score_out.  With exact_all every uncertain logit is
-// resolved (not only those that can reach the top k) and, if logits_row is
-// non-null, all Et bf16 logits are written there as fp32.
-static __device__ __noinline__ void warp_route_token(const uint32_t* ivl, int Et, int K, const uint16_t* xrow,
+// and its weight in *score_out: exp(l_s - l_max) over the sum of that term
+// for the K selected, which equals the softmax over all Et logits gathered
+// at the selection and renormalised (the full denominator cancels; only the
+// fp32 rounding differs).  The selection runs on the lower candidates; the
+// uncertain logits that can still reach the top k are then resolved in fp64
+// and, if there were any, the selection runs again.  With exact_all every
+// uncertain logit is resolved and, if logits_row is non-null, all Et bf16
+// logits are written there as fp32.  Returns the number of logits resolved.
+static __device__ __noinline__ int warp_route_token(const uint32_t* ivl, int Et, int K, const uint16_t* xrow,
                                                      const uint16_t* router_w, int H, int lane, bool exact_all,
                                                      float* logits_row, int* e_out, float* score_out) {
-  uint32_t klo[8], khi[8];
+  uint32_t klo[8], vhi = 0;  // vhi bit i: lo != hi for expert lane + 32 i
+  uint16_t hib[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int e = lane + 32 * i;
-    klo[i] = khi[i] = 0;
+    klo[i] = 0;
+    hib[i] = 0;
     if (e < Et) {
       const uint32_t v = ivl[e];
       klo[i] = route_key(static_cast<uint16_t>(v & 0xFFFFu), e);
-      khi[i] = route_key(static_cast<uint16_t>(v >> 16), e);
+      hib[i] = static_cast<uint16_t>(v >> 16);
+      if ((v & 0xFFFFu) != (v >> 16)) vhi |= 1u << i;
     }
   }
-  // theta = K-th largest lower key: an expert whose upper key is below it is
-  // beaten for certain by K others
   uint32_t mine;
-  const uint32_t theta = warp_select_k(klo, K, lane, mine);
+  const uint32_t theta = warp_select_k(klo, K, lane, mine);  // the K-th largest lower key
+  int n_exact = 0;
+  if (__any_sync(0xffffffffu, vhi != 0)) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const bool need = klo[i] != khi[i] && (exact_all || khi[i] >= theta);
-    uint32_t m = __ballot_sync(0xffffffffu, need);
-    while (m) {
-      const int src = __ffs(m) - 1;
-      m &= m - 1;
-      const int e = src + 32 * i;
-      const double d = warp_dot_f64(xrow, router_w + static_cast<size_t>(e) * H, H, lane);
-      if (lane == src) klo[i] = khi[i] = route_key(f64_to_bf16_bits(d), e);
+    for (int i = 0; i < 8; ++i) {
+      // an expert whose upper key is below theta is beaten for certain by K others
+      const bool need = ((vhi >> i) & 1u) && (exact_all || route_key(hib[i], lane + 32 * i) >= theta);
+      uint32_t m = __ballot_sync(0xffffffffu, need);
+      n_exact += __popc(m);
+      while (m) {
+        const int src = __ffs(m) - 1;
+        m &= m - 1;
+        const int e = src + 32 * i;
+        const double d = warp_dot_f64(xrow, router_w + static_cast<size_t>(e) * H, H, lane);
+        if (lane == src) klo[i] = route_key(f64_to_bf16_bits(d), e);
+      }
     }
+    if (n_exact) warp_select_k(klo, K, lane, mine);
   }
-  warp_select_k(klo, K, lane, mine);
+  if (logits_row) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (lane + 32 * i < Et) logits_row[lane + 32 * i] = route_key_value(klo[i]);
+  }
   const float mx = route_key_value(__shfl_sync(0xffffffffu, mine, 0));
-  float den = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int e = lane + 32 * i;
-    if (e < Et) {
-      const float l = route_key_value(klo[i]);
-      den += expf(l - mx);
-      if (logits_row) logits_row[e] = l;
-    }
-  }
-  den = warp_sum(den);
-  const float pw = lane < K ? expf(route_key_value(mine) - mx) / den : 0.f;
+  const float pw = lane < K ? expf(route_key_value(mine) - mx) : 0.f;
   const float selsum = warp_sum(pw);
   *e_out = route_key_expert(mine);
   *score_out = pw / selsum;
+  return n_exact;
 }
 
 }  // namespace rnb

@@ -180,16 +180,20 @@ def switchglu(bt: BlockTensors, x: torch.Tensor, indices: torch.Tensor,
 
 
 def moe_block(bt: BlockTensors, x: torch.Tensor, k: int = 8, ws: Workspace | None = None,
-              return_routing: bool = False, out: torch.Tensor | None = None):
+              return_routing: bool = False, out: torch.Tensor | None = None, out_dtype=None):
     """Whole block ``[..., H] -> [..., H]`` bf16; optionally (out, inds, scores).
 
-    ``out`` (contiguous bf16, x's shape) receives the result in place."""
+    ``out`` (contiguous, x's shape) receives the result in place.  With
+    ``bt.flags & FLAG_Y_F32`` the result is fp32 (``out_dtype=torch.float32``)."""
     xt = _tokens(x, bt.H)
     T = xt.shape[0]
+    dt = torch.float32 if bt.flags & _lib.FLAG_Y_F32 else torch.bfloat16
+    if out_dtype is not None and out_dtype != dt:
+        raise ValueError(f"out_dtype {out_dtype} does not match the descriptor's output ({dt})")
     if out is None:
-        out = torch.empty_like(xt)
-    elif out.dtype != torch.bfloat16 or out.numel() != xt.numel() or not out.is_contiguous():
-        raise ValueError("out must be a contiguous bf16 tensor with x's number of elements")
+        out = torch.empty(xt.shape, dtype=dt, device=xt.device)
+    elif out.dtype != dt or out.numel() != xt.numel() or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {dt} tensor with x's number of elements")
     inds = scores = None
     if return_routing:
         inds = torch.empty((T, k), dtype=torch.int32, device=xt.device)

@@ -1,0 +1,97 @@
+"""Expert-parallel decode on GPUs: the in-kernel NVLink exchange
+(rnb_moe_block_ep_fwd) and the NCCL baseline against the oracle.
+
+The two-rank test needs two GPUs (one process each) and is skipped on a
+single-GPU box; the single-rank test runs the same entry point with world 1.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from runnel_b200 import _lib, ep, inputs, ops
+from tests._parity import assert_close
+
+pytestmark = pytest.mark.gpu
+
+BITS, SEED = 4, 1
+
+
+def _ref(blk, T):
+    w = oracle.BlockWeights(bits=BITS, group=64, **blk.weight_fields())
+    return oracle.moe_block(w, blk.x[:T], k=8)
+
+
+def test_single_rank_context_matches_block():
+    blk = inputs.make_block(BITS, seed=SEED, T=8)
+    dev = torch.device("cuda", 0)
+    bt = ep.shard_tensors(blk, 0, 1, dev)
+    x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).to(dev)
+    ctx = ep.ExpertParallel(0, 1, handles_fn=lambda h: [h])
+    try:
+        for T in (1, 8, 5):
+            out, inds, _ = ctx.moe_block(bt, x[:T], return_routing=True)
+            ref, oinds, _ = _ref(blk, T)
+            np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
+            assert_close(out.float().cpu().numpy(), ref, f"ep world 1 T={T}")
+        f32 = ops.BlockTensors(**{**bt.__dict__, "flags": _lib.FLAG_Y_F32})
+        out = ctx.moe_block(f32, x[:2])
+        assert out.dtype == torch.float32
+        assert_close(out.cpu().numpy(), _ref(blk, 2)[0], "ep world 1 fp32")
+    finally:
+        ctx.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    gloo = dist.new_group(backend="gloo")
+    ctx = None
+    try:
+        blk = inputs.make_block(BITS, seed=SEED, T=8)
+        shard = ep.shard_tensors(blk, rank, world, dev)
+        x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).to(dev)
+        ws = ops.Workspace(dev)
+        ctx = ep.ExpertParallel(rank, world, handles_fn=lambda h: ep.gather_handles(h, group=gloo))
+        for T in (1, 8, 3, 1, 8, 2):  # repeated calls alternate the exchange parity
+            dist.barrier(group=gloo)  # ranks enter each exchange together
+            out, inds, _ = ctx.moe_block(shard, x[:T], ws=ws, return_routing=True)
+            ref, oinds, _ = _ref(blk, T)
+            np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
+            assert_close(out.float().cpu().numpy(), ref, f"ep p2p rank {rank} T={T}")
+            # every rank holds the same bits (the sum runs in rank order everywhere)
+            allv = [torch.empty_like(out) for _ in range(world)]
+            dist.all_gather(allv, out)
+            for v in allv:
+                assert torch.equal(v, out)
+        assert ws.status() == 0
+        out_n = ep.moe_block_nccl(shard, x[:8], rank, ws=ws)
+        assert_close(out_n.float().cpu().numpy(), _ref(blk, 8)[0], f"ep nccl rank {rank}")
+        torch.cuda.synchronize()
+        dist.barrier()
+    finally:
+        if ctx is not None:
+            ctx.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_expert_parallel_decode():
+    import torch.multiprocessing as mp
+
+    mp.spawn(_rank_main, args=(2, _free_port()), nprocs=2, join=True)
