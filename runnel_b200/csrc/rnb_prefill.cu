@@ -42,7 +42,7 @@ namespace rnb {
 namespace pre {
 
 constexpr int kTileM = 128;
-constexpr int kRouteT = 64;     // tokens per router CTA
+constexpr int kRouteT = 32;     // tokens per router CTA
 constexpr int kProducerWarps = 8;
 constexpr int kMmaWarp = 8;
 // warps 9..12: epilogue, one per TMEM lane quadrant (warp % 4)
@@ -63,8 +63,10 @@ struct Ws {
   float* scores;     // [T][K]
   float* sg;         // [T]
   float* xscale;     // [T] power of two bringing max|x_t| into [2^14, 2^15)
-  __half* h16;       // [rows_cap][I] SwiGLU activations, scaled
-  float* hinv;       // [rows_cap][I/128] inverse scale of each 128-channel chunk
+  __half* x16;       // [T][H] activations times xscale, fp16 (gate/up A operand)
+  __half* h16;       // [rows_cap][I] SwiGLU activations, scaled per 128-channel chunk
+  float* hinv;       // [rows_cap][I/128] inverse scale of each chunk; after k_pre_hrow its factor
+  float* hrow;       // [rows_cap] inverse scale of the row (largest chunk inverse scale)
   float* acc;        // [T][H] fp32 output accumulator
 };
 
@@ -81,6 +83,53 @@ struct Params {
   float* scores_out;
   Ws ws;
 };
+
+// fp16 pair helpers
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+  const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b),
+                            *reinterpret_cast<const __half2*>(&c));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t half2_bits(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// 16 bytes of 8-bit codes (16 consecutive K) -> two 16-byte fp16 chunks, w = s*q + b.
+__device__ __forceinline__ void deq_q8_16(const uint4 v, uint32_t s2, uint32_t b2, uint4& o0, uint4& o1) {
+  uint32_t p[8];
+  q8_word_to_pairs(v.x, p[0], p[1]);
+  q8_word_to_pairs(v.y, p[2], p[3]);
+  q8_word_to_pairs(v.z, p[4], p[5]);
+  q8_word_to_pairs(v.w, p[6], p[7]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = hfma2_u32(p[i], s2, b2);
+  o0 = make_uint4(p[0], p[1], p[2], p[3]);
+  o1 = make_uint4(p[4], p[5], p[6], p[7]);
+}
+
+// one word of 4-bit codes (8 consecutive K) -> one 16-byte fp16 chunk in the
+// pair order (0,4),(1,5),(2,6),(3,7); activations use the same order.
+__device__ __forceinline__ uint4 deq_q4_word(uint32_t w, uint32_t s2, uint32_t b2) {
+  uint32_t p0, p1, p2, p3;
+  q4_word_to_pairs(w, p0, p1, p2, p3);
+  return make_uint4(hfma2_u32(p0, s2, b2), hfma2_u32(p1, s2, b2), hfma2_u32(p2, s2, b2), hfma2_u32(p3, s2, b2));
+}
+
+// Reorders 8 consecutive fp16 (as 4 pairs) to (0,4),(1,5),(2,6),(3,7).
+__device__ __forceinline__ uint4 perm_q4_order(const uint4 v) {
+  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
+                    __byte_perm(v.y, v.w, 0x7632));
+}
+
+__device__ __forceinline__ uint32_t bf16_to_half2_dup(uint16_t b) {
+  const float f = __uint_as_float(static_cast<uint32_t>(b) << 16);
+  return half2_bits(f, f);
+}
 
 // ------------------------------------------------------------ router
 
@@ -117,13 +166,25 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
   };
-  float acc[8][4];
+  constexpr int kNC = kRouteT / 8;  // 8-token MMA column blocks
+  float acc[kNC][4];
 #pragma unroll
-  for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  for (int n = 0; n < kNC; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
   float wa2 = 0.f, wa1 = 0.f, wb2 = 0.f, wb1 = 0.f;  // norms of rows row_a, row_b (lane's quarter)
   const int row_a = warp * 16 + g, row_b = row_a + 8;
   const uint16_t* wa = row_a < Et ? p.router_w + static_cast<size_t>(row_a) * H : nullptr;
   const uint16_t* wb = row_b < Et ? p.router_w + static_cast<size_t>(row_b) * H : nullptr;
+  uint4 na0[4], na1[4];  // router rows of the next 128-wide chunk, in flight during this one
+  auto load_w = [&](int kc) {
+    const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      const int k0 = kc * 128 + ch * 32 + 8 * c;
+      na0[ch] = wa ? __ldg(reinterpret_cast<const uint4*>(wa + k0)) : z;
+      na1[ch] = wb ? __ldg(reinterpret_cast<const uint4*>(wb + k0)) : z;
+    }
+  };
+  load_w(0);
   stage(0, 0);
   for (int kc = 0; kc < nkc; ++kc) {
     if (kc + 1 < nkc) {
@@ -150,12 +211,18 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
       atomicAdd(&xn2[r], s2);
     }
     if (warp * 16 < Et) {
-      const uint4 z = make_uint4(0, 0, 0, 0);
+      // this chunk's router rows were loaded during the previous chunk; start the next
+      uint4 ca0[4], ca1[4];
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
-        const int k0 = kc * 128 + ch * 32 + 8 * c;
-        const uint4 a0 = wa ? __ldg(reinterpret_cast<const uint4*>(wa + k0)) : z;
-        const uint4 a1 = wb ? __ldg(reinterpret_cast<const uint4*>(wb + k0)) : z;
+        ca0[ch] = na0[ch];
+        ca1[ch] = na1[ch];
+      }
+      if (kc + 1 < nkc) load_w(kc + 1);
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        const uint4 a0 = ca0[ch];
+        const uint4 a1 = ca1[ch];
         {
           const uint32_t av[4] = {a0.x, a0.y, a0.z, a0.w}, bv[4] = {a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
@@ -169,7 +236,7 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
           }
         }
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
+        for (int n = 0; n < kNC; ++n) {
           const uint4 bx = *reinterpret_cast<const uint4*>(&xs[buf][n * 8 + g][ch * 32 + 8 * c]);
           mma_bf16(acc[n], a0.x, a1.x, a0.y, a1.y, bx.x, bx.y);
           mma_bf16(acc[n], a0.z, a1.z, a0.w, a1.w, bx.z, bx.w);
@@ -177,6 +244,28 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
       }
     }
     __syncthreads();
+  }
+  // fp16 copy of the tokens times their power-of-two scale (gate/up A operand)
+  {
+    __shared__ float xsc[kRouteT];
+    if (tid < kRouteT) {
+      float sc, inv;
+      fp16_range_scale(__uint_as_float(xmax[tid]), sc, inv);
+      xsc[tid] = sc;
+    }
+    __syncthreads();
+    const int n8 = H / 8;
+    for (int q = tid; q < nt * n8; q += blockDim.x) {
+      const int t = q / n8, c8 = q % n8;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t0 + t) * H) + c8);
+      const float sc = xsc[t];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = half2_bits(__uint_as_float(w[j] << 16) * sc, __uint_as_float(w[j] & 0xFFFF0000u) * sc);
+      reinterpret_cast<uint4*>(p.ws.x16 + static_cast<size_t>(t0 + t) * H)[c8] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 #pragma unroll
   for (int o = 1; o <= 2; o <<= 1) {
@@ -189,7 +278,7 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
     // candidate intervals of the bf16 logits (rnb_route.cuh)
     uint32_t(*lgu)[kMaxE + 1] = reinterpret_cast<uint32_t(*)[kMaxE + 1]>(rsm);
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+    for (int n = 0; n < kNC; ++n) {
       const int tA = n * 8 + 2 * c, tB = tA + 1;
       const float xiA = __uint_as_float(xmax[tA]), xiB = __uint_as_float(xmax[tB]);
       if (row_a < Et) {
@@ -315,81 +404,62 @@ __global__ void k_pre_scatter(Params p) {
 
 // ------------------------------------------------------ grouped GEMM
 
-// fp16 pair helpers
-__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
-  const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b),
-                            *reinterpret_cast<const __half2*>(&c));
-  return *reinterpret_cast<const uint32_t*>(&r);
-}
-__device__ __forceinline__ uint32_t half2_bits(float a, float b) {
-  const __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-// 16 bytes of 8-bit codes (16 consecutive K) -> two 16-byte fp16 chunks, w = s*q + b.
-__device__ __forceinline__ void deq_q8_16(const uint4 v, uint32_t s2, uint32_t b2, uint4& o0, uint4& o1) {
-  uint32_t p[8];
-  q8_word_to_pairs(v.x, p[0], p[1]);
-  q8_word_to_pairs(v.y, p[2], p[3]);
-  q8_word_to_pairs(v.z, p[4], p[5]);
-  q8_word_to_pairs(v.w, p[6], p[7]);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = hfma2_u32(p[i], s2, b2);
-  o0 = make_uint4(p[0], p[1], p[2], p[3]);
-  o1 = make_uint4(p[4], p[5], p[6], p[7]);
-}
-
-// one word of 4-bit codes (8 consecutive K) -> one 16-byte fp16 chunk in the
-// pair order (0,4),(1,5),(2,6),(3,7); activations use the same order.
-__device__ __forceinline__ uint4 deq_q4_word(uint32_t w, uint32_t s2, uint32_t b2) {
-  uint32_t p0, p1, p2, p3;
-  q4_word_to_pairs(w, p0, p1, p2, p3);
-  return make_uint4(hfma2_u32(p0, s2, b2), hfma2_u32(p1, s2, b2), hfma2_u32(p2, s2, b2), hfma2_u32(p3, s2, b2));
-}
-
-// Reorders 8 consecutive fp16 (as 4 pairs) to (0,4),(1,5),(2,6),(3,7).
-__device__ __forceinline__ uint4 perm_q4_order(const uint4 v) {
-  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
-                    __byte_perm(v.y, v.w, 0x7632));
-}
-
-__device__ __forceinline__ uint32_t bf16_to_half2_dup(uint16_t b) {
-  const float f = __uint_as_float(static_cast<uint32_t>(b) << 16);
-  return half2_bits(f, f);
-}
-
-template <int MODE>
+// k_pre_gemm: persistent, one CTA per SM, work item = (128-row m-tile, 256-column n-tile).
+//   warps 0-7  producers: thread pt owns B row pt of the n-tile and four
+//              16-byte A chunks (rows pt/8 + 32j, K chunk pt%8) per stage; the
+//              global loads of stage s+2 are issued before stage s is
+//              converted (a three-deep register ring), so HBM/L2 latency is
+//              covered by two stages of MMA.  B: MLX codes -> fp16 s*q + b.
+//              A: gate/up reads the pre-scaled fp16 activations x16 gathered
+//              by token; down reads the fp16 SwiGLU rows times the row's
+//              chunk factor (all chunks of a row share one scale).
+//   warp 8     one thread issues tcgen05.mma (M=128, N=256, K=16) into one of
+//              two TMEM accumulators (256 columns each).
+//   warps 9-12 epilogue, one TMEM lane quadrant each; drains accumulator j&1
+//              while the MMA fills the other.
 struct GemmCfg {
-  static constexpr int N = MODE == 0 ? 256 : 128;
+  static constexpr int N = 256;
+  static constexpr int S = 4;  // shared-memory stages
   static constexpr int kA = kTileM * 128;
   static constexpr int kB = N * 128;
   static constexpr int kStage = kA + kB;
-  static constexpr int S = MODE == 0 ? 4 : 6;
-  static constexpr uint32_t kTmemCols = MODE == 0 ? 256 : 512;
+  static constexpr uint32_t kTmemCols = 512;
   static constexpr size_t kSmem = static_cast<size_t>(S) * kStage + 1024;
+};
+
+// One stage's weight loads of one producer thread (its B row).
+template <int BITS>
+struct StageRegs {
+  uint4 b[BITS == 8 ? 4 : 2];
+  uint32_t sb;  // scale | bias << 16 (bf16 bits) of the row's group
 };
 
 template <int BITS, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
-  using C = GemmCfg<MODE>;
+  using C = GemmCfg;
   extern __shared__ char smraw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t full[C::S], empty[C::S], tfull, tempty;
+  __shared__ __align__(8) uint64_t full[C::S], empty[C::S], tfull[2], tempty[2], mdone;
   __shared__ uint32_t tslot;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = p.k, H = p.H, I = p.I;
   const int kdim = MODE == 0 ? H : I;
   const int nks = kdim / 64;
-  const int n_nt = MODE == 0 ? I / 128 : H / 128;
+  const int n_nt = MODE == 0 ? (2 * I) / C::N : H / C::N;
   const uint32_t n_items = __ldcg(p.ws.n_mt) * static_cast<uint32_t>(n_nt);
+  const uint32_t G = gridDim.x;
+  const uint32_t n_local = n_items > blockIdx.x ? (n_items - blockIdx.x + G - 1) / G : 0u;
 
   if (tid == 0) {
     for (int s = 0; s < C::S; ++s) {
       mbar_init(&full[s], kProducerWarps * 32);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(&tfull, 1);
-    mbar_init(&tempty, 4 * 32);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4 * 32);
+    }
+    mbar_init(&mdone, 1);
   }
   if (warp == kMmaWarp) tmem_alloc(&tslot, C::kTmemCols);
   tc_fence_before();
@@ -401,209 +471,225 @@ __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
   if (warp < kProducerWarps) {
     // ------------------------------------------------ producers
     const int pt = tid;  // 0..255
-    uint32_t it = 0;
-    for (uint32_t item = blockIdx.x; item < n_items; item += gridDim.x) {
-      const uint32_t mt = item / n_nt, nt = item % n_nt;
-      const uint4 tile = __ldcg(p.ws.tiles + mt);
-      const int e = static_cast<int>(tile.x), row0 = static_cast<int>(tile.y), nrows = static_cast<int>(tile.z);
-      const bool shared_e = e == p.E;
-      // A: rows (pt >> 3) + 32 j, 16-byte chunk (pt & 7)
-      const int ca = pt & 7;
-      const void* asrc[4];
-      float ascale[4];
+    const int ca = pt & 7;
+    const uint32_t n_stages = n_local * static_cast<uint32_t>(nks);
+    const size_t wrow = static_cast<size_t>(kdim) * BITS / 32, srow = kdim / 64;
+    // B row of this thread within the n-tile
+    auto b_row = [&](uint32_t nt) -> int {
+      if (MODE == 0) return pt < 128 ? static_cast<int>(nt) * 128 + pt : I + static_cast<int>(nt) * 128 + (pt - 128);
+      return static_cast<int>(nt) * C::N + pt;
+    };
+    // Per-item sources of this thread (rows' A addresses, B row).  The next
+    // item's tile record is loaded on entering an item and its rows' entry
+    // ids one stage later, so entering the next item waits on nothing.
+    uint32_t cur_li = 0xFFFFFFFFu;
+    uint32_t aoff[4];  // A row element offsets into x16 / h16 (0xFFFFFFFF: padding row)
+    const uint32_t* bsrc = nullptr;
+    const uint16_t *ssrc = nullptr, *bisrc = nullptr;
+    const __half* abase = MODE == 0 ? p.ws.x16 : p.ws.h16;
+    uint4 nx_tile = make_uint4(0, 0, 0, 0);
+    uint32_t nx_ent[4] = {0, 0, 0, 0};
+    int nx_phase = 0;  // 0: nothing pending, 1: nx_tile loading, 2: nx_ent loading
+    auto tile_of = [&](uint32_t li) -> uint4 {
+      const uint32_t item = blockIdx.x + li * G;
+      return __ldg(p.ws.tiles + item / n_nt);
+    };
+    auto ents_of = [&](const uint4& tile, uint32_t (&ent)[4]) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int r = (pt >> 3) + 32 * j;
-        asrc[j] = nullptr;
-        ascale[j] = 0.f;
-        const uint32_t ent = r < nrows ? __ldcg(p.ws.perm + row0 + r) : 0xFFFFFFFFu;
-        if (ent != 0xFFFFFFFFu) {
-          if (MODE == 0) {
-            const uint32_t t = ent / (K + 1);
-            asrc[j] = p.x + static_cast<size_t>(t) * H;
-            ascale[j] = __ldcg(p.ws.xscale + t);
-          } else {
-            asrc[j] = p.ws.h16 + static_cast<size_t>(row0 + r) * I;
-          }
-        }
+        ent[j] = (MODE == 0 && r < static_cast<int>(tile.z)) ? __ldg(p.ws.perm + tile.y + r) : 0u;
       }
-      // B: MODE 0 one row per thread (128 up rows, then 128 gate rows);
-      //    MODE 1 half a row per thread (rows nt*128 + (pt & 127), K half pt >> 7)
+    };
+    auto enter_item = [&](uint32_t li) {
+      uint4 tile;
+      uint32_t ent[4];
+      if (nx_phase == 2 && cur_li + 1 == li) {
+        tile = nx_tile;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ent[j] = nx_ent[j];
+      } else {
+        tile = tile_of(li);
+        ents_of(tile, ent);
+      }
+      cur_li = li;
+      nx_phase = 0;
+      if (li + 1 < n_local) {
+        nx_tile = tile_of(li + 1);
+        nx_phase = 1;
+      }
+      const uint32_t nt = (blockIdx.x + li * G) % n_nt;
+      const int e = static_cast<int>(tile.x), row0 = static_cast<int>(tile.y), nrows = static_cast<int>(tile.z);
+      const bool shared_e = e == p.E;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = (pt >> 3) + 32 * j;
+        aoff[j] = 0xFFFFFFFFu;
+        if (r < nrows)  // rows past nrows are padding
+          aoff[j] = MODE == 0 ? (ent[j] / (K + 1)) * static_cast<uint32_t>(H) + ca * 8
+                              : static_cast<uint32_t>(row0 + r) * static_cast<uint32_t>(I) + ca * 8;
+      }
       const uint32_t* bw;
       const uint16_t *bs, *bb;
-      int brow, khalf = 0;
-      size_t wrow, srow;
       if (MODE == 0) {
-        brow = pt < 128 ? static_cast<int>(nt) * 128 + pt : I + static_cast<int>(nt) * 128 + (pt - 128);
-        wrow = static_cast<size_t>(H) * BITS / 32;
-        srow = H / 64;
         const size_t ew = static_cast<size_t>(2) * I * wrow, es = static_cast<size_t>(2) * I * srow;
         bw = shared_e ? p.sgu_w : p.gu_w + e * ew;
         bs = shared_e ? p.sgu_s : p.gu_s + e * es;
         bb = shared_e ? p.sgu_b : p.gu_b + e * es;
       } else {
-        brow = static_cast<int>(nt) * 128 + (pt & 127);
-        khalf = pt >> 7;
-        wrow = static_cast<size_t>(I) * BITS / 32;
-        srow = I / 64;
         const size_t ew = static_cast<size_t>(H) * wrow, es = static_cast<size_t>(H) * srow;
         bw = shared_e ? p.sdn_w : p.dn_w + e * ew;
         bs = shared_e ? p.sdn_s : p.dn_s + e * es;
         bb = shared_e ? p.sdn_b : p.dn_b + e * es;
       }
-      const uint32_t* wr = bw + brow * wrow;
-      const uint16_t* sr = bs + brow * srow;
-      const uint16_t* br = bb + brow * srow;
-      uint4 sc8 = make_uint4(0, 0, 0, 0), bi8 = make_uint4(0, 0, 0, 0);
-      for (int ks = 0; ks < nks; ++ks) {
-        const int s = static_cast<int>(it % C::S);
-        const uint32_t n = it / C::S;
-        if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, kWaitNs)) {
-          timed_out = true;
-          break;
-        }
-        char* sA = sm + s * C::kStage;
-        char* sB = sA + C::kA;
-        // ---- A chunk: 8 values at K = ks*64 + ca*8
+      const size_t brow = static_cast<size_t>(b_row(nt));
+      bsrc = bw + brow * wrow;
+      ssrc = bs + brow * srow;
+      bisrc = bb + brow * srow;
+    };
+    // issue stage st: the A tile by cp.async into its ring slot (which must
+    // be free), the B row's codes and scale/bias into registers
+    auto issue = [&](uint32_t st, StageRegs<BITS>& R) -> bool {
+      const int slot = static_cast<int>(st % C::S);
+      const uint32_t n = st / C::S;
+      if (n > 0 && !mbar_wait(&empty[slot], (n - 1) & 1, kWaitNs)) return false;
+      const uint32_t li = st / nks;
+      const int ks = static_cast<int>(st % nks);
+      if (li != cur_li) {
+        enter_item(li);
+      } else if (nx_phase == 1) {
+        ents_of(nx_tile, nx_ent);  // the next item's tile record has had a stage to arrive
+        nx_phase = 2;
+      }
+      char* sA = sm + slot * C::kStage;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        char* dst = sA + sw128_offset((pt >> 3) + 32 * j, ca * 8);
+        if (aoff[j] != 0xFFFFFFFFu)
+          cp_async16(dst, abase + aoff[j] + ks * 64);
+        else
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+      }
+      asm volatile("cp.async.commit_group;\n" ::: "memory");
+      const uint4* src = reinterpret_cast<const uint4*>(bsrc + ks * (BITS * 2));
+#pragma unroll
+      for (int q = 0; q < (BITS == 8 ? 4 : 2); ++q) R.b[q] = ld_stream_v4(src + q);
+      R.sb = static_cast<uint32_t>(__ldg(ssrc + ks)) | (static_cast<uint32_t>(__ldg(bisrc + ks)) << 16);
+      return true;
+    };
+    // finish stage st: dequantised B into its slot; the slot's A has landed
+    auto finish = [&](uint32_t st, const StageRegs<BITS>& R) {
+      const int slot = static_cast<int>(st % C::S);
+      char* sA = sm + slot * C::kStage;
+      char* sB = sA + C::kA;
+      if (BITS == 4) {
+        // 4-bit weights come out in the pair order (0,4),(1,5),(2,6),(3,7):
+        // permute this thread's A chunks the same way
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int r = (pt >> 3) + 32 * j;
-          uint4 o = make_uint4(0, 0, 0, 0);
-          if (asrc[j]) {
-            if (MODE == 0) {
-              const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(asrc[j]) + ks * 64 + ca * 8));
-              const float sc = ascale[j];
-              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-              float f[8];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                f[2 * q] = __uint_as_float(w[q] << 16) * sc;
-                f[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u) * sc;
-              }
-              if (BITS == 4)
-                o = make_uint4(half2_bits(f[0], f[4]), half2_bits(f[1], f[5]), half2_bits(f[2], f[6]), half2_bits(f[3], f[7]));
-              else
-                o = make_uint4(half2_bits(f[0], f[1]), half2_bits(f[2], f[3]), half2_bits(f[4], f[5]), half2_bits(f[6], f[7]));
-            } else {
-              const uint4 v = __ldcg(reinterpret_cast<const uint4*>(static_cast<const __half*>(asrc[j]) + ks * 64 + ca * 8));
-              o = BITS == 4 ? perm_q4_order(v) : v;
-            }
-          }
-          *reinterpret_cast<uint4*>(sA + sw128_offset(r, ca * 8)) = o;
+          uint4* q = reinterpret_cast<uint4*>(sA + sw128_offset((pt >> 3) + 32 * j, ca * 8));
+          *q = perm_q4_order(*q);
         }
-        // ---- B: dequantised weights
-        if (MODE == 0) {
-          if ((ks & 7) == 0) {
-            sc8 = __ldg(reinterpret_cast<const uint4*>(sr + ks));
-            bi8 = __ldg(reinterpret_cast<const uint4*>(br + ks));
-          }
-          const int gi = ks & 7;
-          const uint32_t sw = (gi >> 1) == 0 ? sc8.x : (gi >> 1) == 1 ? sc8.y : (gi >> 1) == 2 ? sc8.z : sc8.w;
-          const uint32_t bw2 = (gi >> 1) == 0 ? bi8.x : (gi >> 1) == 1 ? bi8.y : (gi >> 1) == 2 ? bi8.z : bi8.w;
-          const uint32_t s2 = bf16_to_half2_dup(static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu)));
-          const uint32_t b2 = bf16_to_half2_dup(static_cast<uint16_t>((gi & 1) ? (bw2 >> 16) : (bw2 & 0xFFFFu)));
-          if (BITS == 8) {
-            const uint4* src = reinterpret_cast<const uint4*>(wr + ks * 16);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 o0, o1;
-              deq_q8_16(ld_stream_v4(src + q), s2, b2, o0, o1);
-              *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 16)) = o0;  // tile row pt
-              *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 16 + 8)) = o1;
-            }
-          } else {
-            const uint4* src = reinterpret_cast<const uint4*>(wr + ks * 8);
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              const uint4 v = ld_stream_v4(src + q);
-              const int rl = pt;  // tile row of this thread (up rows 0..127, gate rows 128..255)
-              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, q * 32)) = deq_q4_word(v.x, s2, b2);
-              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, q * 32 + 8)) = deq_q4_word(v.y, s2, b2);
-              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, q * 32 + 16)) = deq_q4_word(v.z, s2, b2);
-              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, q * 32 + 24)) = deq_q4_word(v.w, s2, b2);
-            }
-          }
-        } else {
-          if (ks == 0) {
-            sc8 = __ldg(reinterpret_cast<const uint4*>(sr));
-            bi8 = __ldg(reinterpret_cast<const uint4*>(br));
-          }
-          const int gi = ks;  // I / 64 <= 8 groups
-          const uint32_t sw = (gi >> 1) == 0 ? sc8.x : (gi >> 1) == 1 ? sc8.y : (gi >> 1) == 2 ? sc8.z : sc8.w;
-          const uint32_t bw2 = (gi >> 1) == 0 ? bi8.x : (gi >> 1) == 1 ? bi8.y : (gi >> 1) == 2 ? bi8.z : bi8.w;
-          const uint32_t s2 = bf16_to_half2_dup(static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu)));
-          const uint32_t b2 = bf16_to_half2_dup(static_cast<uint16_t>((gi & 1) ? (bw2 >> 16) : (bw2 & 0xFFFFu)));
-          const int rl = pt & 127;
-          if (BITS == 8) {
-            // 32 codes (K half) = 2 x 16 bytes
-            const uint4* src = reinterpret_cast<const uint4*>(wr + ks * 16 + khalf * 8);
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              uint4 o0, o1;
-              deq_q8_16(ld_stream_v4(src + q), s2, b2, o0, o1);
-              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + q * 16)) = o0;
-              *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + q * 16 + 8)) = o1;
-            }
-          } else {
-            const uint4 v = ld_stream_v4(reinterpret_cast<const uint4*>(wr + ks * 8 + khalf * 4));
-            *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32)) = deq_q4_word(v.x, s2, b2);
-            *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + 8)) = deq_q4_word(v.y, s2, b2);
-            *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + 16)) = deq_q4_word(v.z, s2, b2);
-            *reinterpret_cast<uint4*>(sB + sw128_offset(rl, khalf * 32 + 24)) = deq_q4_word(v.w, s2, b2);
-          }
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&full[s]);
-        ++it;
       }
-      if (timed_out) break;
+      const uint32_t s2 = bf16_to_half2_dup(static_cast<uint16_t>(R.sb & 0xFFFFu));
+      const uint32_t b2 = bf16_to_half2_dup(static_cast<uint16_t>(R.sb >> 16));
+      if (BITS == 8) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 o0, o1;
+          deq_q8_16(R.b[q], s2, b2, o0, o1);
+          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 16)) = o0;
+          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 16 + 8)) = o1;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 32)) = deq_q4_word(R.b[q].x, s2, b2);
+          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 32 + 8)) = deq_q4_word(R.b[q].y, s2, b2);
+          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 32 + 16)) = deq_q4_word(R.b[q].z, s2, b2);
+          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 32 + 24)) = deq_q4_word(R.b[q].w, s2, b2);
+        }
+      }
+    };
+    // step st: issue st+2 (two stages of MMA cover its latency), then finish
+    // st, whose loads were issued two steps earlier; one cp.async group per
+    // issued stage, so at most two younger groups may still be in flight.
+    // Issuing st+2 needs its slot, freed by the MMA of st+2-S = st-2, which
+    // leaves two stages of slack between the producers and the MMA.
+    auto step = [&](uint32_t st, StageRegs<BITS>& use, StageRegs<BITS>& fill) -> bool {
+      if (st >= n_stages) return true;
+      if (st + 2 < n_stages) {
+        if (!issue(st + 2, fill)) return false;
+        asm volatile("cp.async.wait_group 2;\n" ::: "memory");
+      } else if (st + 1 < n_stages) {
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      }
+      finish(st, use);
+      fence_proxy_async_smem();
+      mbar_arrive(&full[st % C::S]);
+      return true;
+    };
+    StageRegs<BITS> r0, r1, r2;
+    bool ok = true;
+    if (n_stages > 0) ok = issue(0, r0);
+    if (ok && n_stages > 1) ok = issue(1, r1);
+    if (!ok) timed_out = true;
+    for (uint32_t st = 0; st < n_stages && !timed_out; st += 3) {
+      if (!step(st, r0, r2) || !step(st + 1, r1, r0) || !step(st + 2, r2, r1)) timed_out = true;
     }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------ MMA issue (one thread)
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(kTileM, C::N, false);
-      uint32_t it = 0, j = 0;
-      for (uint32_t item = blockIdx.x; item < n_items; item += gridDim.x, ++j) {
-        if (j > 0 && !mbar_wait(&tempty, (j - 1) & 1, kWaitNs)) {
+      uint32_t st = 0;
+      for (uint32_t j = 0; j < n_local && !timed_out; ++j) {
+        const uint32_t buf = j & 1;
+        if (j >= 2 && !mbar_wait(&tempty[buf], ((j >> 1) - 1) & 1, kWaitNs)) {
           timed_out = true;
           break;
         }
         tc_fence_after();
-        for (int ks = 0; ks < nks; ++ks, ++it) {
-          const int s = static_cast<int>(it % C::S);
-          if (!mbar_wait(&full[s], (it / C::S) & 1, kWaitNs)) {
+        const uint32_t d = taddr + buf * C::N;
+        for (int ks = 0; ks < nks; ++ks, ++st) {
+          const int s = static_cast<int>(st % C::S);
+          if (!mbar_wait(&full[s], (st / C::S) & 1, kWaitNs)) {
             timed_out = true;
             break;
           }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sm + s * C::kStage), b0 = a0 + C::kA;
-          const uint32_t d = MODE == 0 ? taddr : taddr + (ks >> 1) * 128;
-          const bool fresh = MODE == 0 ? ks == 0 : (ks & 1) == 0;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             umma_f16(d, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(b0 + k * 32), idesc,
-                     (fresh && k == 0) ? 0u : 1u);
+                     (ks == 0 && k == 0) ? 0u : 1u);
           umma_commit(smem_u32(&empty[s]));
         }
         if (timed_out) break;
-        umma_commit(smem_u32(&tfull));
+        umma_commit(smem_u32(&tfull[buf]));
       }
+      // every MMA this thread issued has completed before TMEM is released
+      umma_commit(smem_u32(&mdone));
+      if (!mbar_wait(&mdone, 0, kWaitNs)) timed_out = true;
     }
   } else {
     // ------------------------------------------------ epilogue (warps 9..12)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const uint32_t tl = taddr + (static_cast<uint32_t>(quad * 32) << 16);
-    uint32_t j = 0;
-    for (uint32_t item = blockIdx.x; item < n_items; item += gridDim.x, ++j) {
+    for (uint32_t j = 0; j < n_local; ++j) {
+      const uint32_t item = blockIdx.x + j * G;
       const uint32_t mt = item / n_nt, nt = item % n_nt;
+      const uint32_t buf = j & 1;
+      const uint32_t tl = taddr + buf * C::N + (static_cast<uint32_t>(quad * 32) << 16);
       const uint4 tile = __ldcg(p.ws.tiles + mt);
       const int row0 = static_cast<int>(tile.y), nrows = static_cast<int>(tile.z);
       uint32_t ent = r < nrows ? __ldcg(p.ws.perm + row0 + r) : 0xFFFFFFFFu;
       const bool valid = ent != 0xFFFFFFFFu;
       if (!valid) ent = 0u;
       // the whole warp leaves together: tcgen05.ld below is warp-collective
-      const bool ok = mbar_wait(&tfull, j & 1, kWaitNs);
+      const bool ok = mbar_wait(&tfull[buf], (j >> 1) & 1, kWaitNs);
       if (__any_sync(0xffffffffu, !ok)) {
         timed_out = true;
         break;
@@ -648,40 +734,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
       } else {
         const uint32_t t = ent / (K + 1), slot = ent % (K + 1);
         float w = 0.f;
-        float hinv[4] = {0.f, 0.f, 0.f, 0.f};
         if (valid) {
           w = slot < static_cast<uint32_t>(K) ? __ldcg(p.ws.scores + static_cast<size_t>(t) * K + slot)
                                               : __ldcg(p.ws.sg + t);
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4)
-            if (c4 < I / 128) hinv[c4] = __ldcg(p.ws.hinv + static_cast<size_t>(row0 + r) * (I / 128) + c4) * w;
+          w *= __ldcg(p.ws.hrow + row0 + r);
         }
-        float* dst = p.ws.acc + static_cast<size_t>(t) * H + nt * 128;
-        for (int cc = 0; cc < 8; ++cc) {
-          float y[16];
-#pragma unroll
-          for (int q = 0; q < 16; ++q) y[q] = 0.f;
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            if (c4 < I / 128) {
-              uint32_t v[16];
-              tmem_ld16(tl + c4 * 128 + cc * 16, v);
-              tmem_wait_ld();
-#pragma unroll
-              for (int q = 0; q < 16; ++q) y[q] = fmaf(__uint_as_float(v[q]), hinv[c4], y[q]);
-            }
-          }
+        float* dst = p.ws.acc + static_cast<size_t>(t) * H + nt * C::N;
+        for (int cc = 0; cc < C::N / 16; ++cc) {
+          uint32_t v[16];
+          tmem_ld16(tl + cc * 16, v);
+          tmem_wait_ld();
           if (valid) {
 #pragma unroll
             for (int q = 0; q < 16; q += 4)
-              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + cc * 16 + q), "f"(y[q]),
-                           "f"(y[q + 1]), "f"(y[q + 2]), "f"(y[q + 3])
+              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + cc * 16 + q),
+                           "f"(__uint_as_float(v[q]) * w), "f"(__uint_as_float(v[q + 1]) * w),
+                           "f"(__uint_as_float(v[q + 2]) * w), "f"(__uint_as_float(v[q + 3]) * w)
                            : "memory");
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty);
+      mbar_arrive(&tempty[buf]);
     }
   }
   if (timed_out) atomicOr(p.ws.status, RNB_STATUS_TIMEOUT);
@@ -691,6 +765,36 @@ __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
   if (warp == kMmaWarp) {
     tmem_dealloc(taddr, C::kTmemCols);
     tmem_relinquish();
+  }
+}
+
+// Between the GEMMs: give all 128-channel chunks of a SwiGLU row one scale,
+// the smallest of the chunks' (the chunk with the largest values keeps its
+// scale; the others are multiplied by a power of two <= 1, exact unless a
+// value falls below fp16's normal range).  hrow = that scale's inverse.
+// One warp per row; lane l handles 8-value pieces l, l+32.
+__global__ void k_pre_hrow(Params p) {
+  const int nq = p.I / 128, lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  for (int row = blockIdx.x * wpb + (threadIdx.x >> 5); row < p.rows_cap; row += gridDim.x * wpb) {
+    if (__ldcg(p.ws.perm + row) == 0xFFFFFFFFu) continue;
+    const float* h = p.ws.hinv + static_cast<size_t>(row) * nq;
+    float m = 0.f;
+    for (int c = 0; c < nq; ++c) m = fmaxf(m, __ldcg(h + c));
+    uint4* hv = reinterpret_cast<uint4*>(p.ws.h16 + static_cast<size_t>(row) * p.I);
+    for (int q = lane; q < p.I / 8; q += 32) {
+      const float f = __ldcg(h + q / 16) / m;
+      if (f != 1.0f) {
+        const uint32_t f2 = half2_bits(f, f);
+        uint4 v = hv[q];
+        v.x = hmul2_u32(v.x, f2);
+        v.y = hmul2_u32(v.y, f2);
+        v.z = hmul2_u32(v.z, f2);
+        v.w = hmul2_u32(v.w, f2);
+        hv[q] = v;
+      }
+    }
+    if (lane == 0) p.ws.hrow[row] = m;
   }
 }
 
@@ -716,7 +820,7 @@ __global__ void k_pre_final(Params p) {
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 struct Layout {
-  size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, h16, hinv, acc, total;
+  size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, x16, h16, hinv, hrow, acc, total;
   int rows_cap, max_mt;
 };
 
@@ -743,8 +847,10 @@ Layout make_layout(const rnb_moe_desc& d) {
   L.scores = take(T * K * 4);
   L.sg = take(T * 4);
   L.xscale = take(T * 4);
+  L.x16 = take(T * d.H * 2);
   L.h16 = take(static_cast<size_t>(L.rows_cap) * d.I * 2);
   L.hinv = take(static_cast<size_t>(L.rows_cap) * (d.I / 128) * 4);
+  L.hrow = take(static_cast<size_t>(L.rows_cap) * 4);
   L.acc = take(T * d.H * 4);
   L.total = o;
   return L;
@@ -774,10 +880,10 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
     e = cudaFuncSetAttribute(k_pre_route, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kRouteSmem));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(k_pre_gemm<BITS, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(GemmCfg<0>::kSmem));
+                               static_cast<int>(GemmCfg::kSmem));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(k_pre_gemm<BITS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(GemmCfg<1>::kSmem));
+                               static_cast<int>(GemmCfg::kSmem));
     if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill smem attribute: ") + cudaGetErrorString(e));
     attr = true;
   }
@@ -789,9 +895,10 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
   k_pre_scatter<<<static_cast<unsigned>((n_scatter + 255) / 256), 256, 0, st>>>(p);
   stage_end(st, RNB_STAGE_SCATTER);
   const int nc = dev_info().sms;
-  k_pre_gemm<BITS, 0><<<nc, kThreads, GemmCfg<0>::kSmem, st>>>(p);
+  k_pre_gemm<BITS, 0><<<nc, kThreads, GemmCfg::kSmem, st>>>(p);
   stage_end(st, RNB_STAGE_GATEUP);
-  k_pre_gemm<BITS, 1><<<nc, kThreads, GemmCfg<1>::kSmem, st>>>(p);
+  k_pre_hrow<<<(L.rows_cap + 7) / 8, 256, 0, st>>>(p);
+  k_pre_gemm<BITS, 1><<<nc, kThreads, GemmCfg::kSmem, st>>>(p);
   stage_end(st, RNB_STAGE_DOWN);
   k_pre_final<<<nc * 4, 256, 0, st>>>(p);
   stage_end(st, RNB_STAGE_FINAL);
@@ -848,8 +955,10 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
   p.ws.scores = reinterpret_cast<float*>(b + L.scores);
   p.ws.sg = reinterpret_cast<float*>(b + L.sg);
   p.ws.xscale = reinterpret_cast<float*>(b + L.xscale);
+  p.ws.x16 = reinterpret_cast<__half*>(b + L.x16);
   p.ws.h16 = reinterpret_cast<__half*>(b + L.h16);
   p.ws.hinv = reinterpret_cast<float*>(b + L.hinv);
+  p.ws.hrow = reinterpret_cast<float*>(b + L.hrow);
   p.ws.acc = reinterpret_cast<float*>(b + L.acc);
   return d->bits == 8 ? launch_prefill<8>(p, L, st) : launch_prefill<4>(p, L, st);
 }
