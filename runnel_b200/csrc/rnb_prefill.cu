@@ -1,31 +1,31 @@
 // rnb_prefill.cu -- sparse-MoE block for many tokens (prefill) on tcgen05.
 //
-//   k_pre_route    router logits (mma.sync bf16, 64 tokens per CTA, x staged
-//                  in shared memory), top-k, softmax weights, shared-expert
-//                  gate, per-token power-of-two scale into fp16 range, and a
-//                  per-expert token histogram.
-//   k_pre_sort     one CTA: per-expert row bases padded to 128-row tiles and
-//                  the m-tile list (the shared expert is expert E, all tokens).
+//   k_pre_route    router logits (mma.sync bf16, 32 tokens per CTA, x staged
+//                  in shared memory) with exact bf16 rounding (rnb_route.cuh),
+//                  top-k, softmax weights, shared-expert gate, per-token
+//                  power-of-two scale into fp16 range, the scaled fp16 copy
+//                  of the tokens, and a per-expert token histogram.
+//   k_pre_sort     one CTA: per-expert row bases padded to 128 rows and the
+//                  list of 256-row work tiles (the shared expert is expert E,
+//                  all tokens).
 //   k_pre_scatter  (token, slot) entries -> expert-sorted rows (counting sort).
-//   k_pre_gemm<0>  grouped gate/up GEMM: 128 rows x (128 up + 128 gate)
+//   k_pre_gather   the sorted rows' fp16 tokens (the gate/up A operand).
+//   k_pre_gemm<0>  grouped gate/up GEMM + SwiGLU: 256 rows x (64 up + 64 gate)
 //                  channels per work item, K = H in 64-wide stages.
-//   k_pre_gemm<1>  grouped down GEMM: 128 rows x 128 outputs, K = I.
-//   k_pre_final    fp32 accumulator -> bf16 output.
+//   k_pre_hrow     one power-of-two scale per SwiGLU row.
+//   k_pre_gemm<1>  grouped down GEMM: 256 rows x 128 outputs, K = I; adds
+//                  score * y into an fp32 [T, H] accumulator with vector
+//                  atomics (their order is not fixed: results reproduce to
+//                  fp32 rounding rather than bit for bit).
+//   k_pre_final    fp32 accumulator -> bf16 (or fp32) output.
 //
-// k_pre_gemm is warp-specialised: 8 producer warps fill a 4/6-stage shared
-// memory ring (activations converted to fp16, MLX affine weights dequantised
-// straight to fp16 with one fused multiply-add per pair: w = s*q + b rounded
-// once), one thread of warp 8 issues tcgen05.mma (M=128, fp16 x fp16 -> fp32
-// in tensor memory), warps 9-12 drain the accumulator.  The gate/up epilogue
-// applies SwiGLU and stores the activations as fp16 scaled by a power of two
-// per (row, 128 channels); the down GEMM keeps one accumulator per such
-// 128-channel chunk so each chunk's scale is undone exactly, then adds
-// score * y into an fp32 [T, H] accumulator with vector atomics (the order
-// of those additions is not fixed, so results are reproducible to fp32
-// rounding rather than bit-exact).
+// The weights stay in MLX's affine layout; k_pre_gemm's converter warps
+// dequantise them in shared memory to fp16 (w = s*q + b with one rounding)
+// right before the tensor cores read them; see k_pre_gemm for the pipeline.
 //
 // Reference semantics: src/runnel/mlx.py:57-82 (sorted gather_qmm when
 // indices.size >= 64), bench/mlx_lm_adapter.py:82-94 (shared expert).
+#include <cuda.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -41,12 +41,12 @@
 namespace rnb {
 namespace pre {
 
-constexpr int kTileM = 128;
+constexpr int kTileM = 128;  // MMA M; expert rows are padded to multiples of it
+constexpr int kItemM = 256;  // rows of a GEMM work item: two M tiles sharing one dequantised B tile
 constexpr int kRouteT = 32;     // tokens per router CTA
 constexpr int kProducerWarps = 8;
 constexpr int kMmaWarp = 8;
-// warps 9..12: epilogue, one per TMEM lane quadrant (warp % 4)
-constexpr int kThreads = 13 * 32;
+// warps 9..12: epilogue, one per TMEM lane quadrant (warp % 4); warp 13: TMA loader
 constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;
 constexpr int kMaxE = 256;
 constexpr int kMaxK = 8;
@@ -56,16 +56,17 @@ struct Ws {
   uint32_t* counts;  // [E+1] rows per local expert (index E: shared expert)
   uint32_t* fill;    // [E+1]
   uint32_t* base;    // [E+1] first sorted row
-  uint32_t* n_mt;    // [1] number of 128-row tiles
-  uint4* tiles;      // [max_mt] (expert, row0, nrows, 0)
+  uint32_t* n_mt;    // [1] number of 256-row item tiles
+  uint4* tiles;      // [max_mt] (expert, row0, nrows <= 256, 0)
   uint32_t* perm;    // [rows_cap] entry id t*(K+1)+slot, 0xFFFFFFFF for padding
   uint32_t* inds;    // [T][K]
   float* scores;     // [T][K]
   float* sg;         // [T]
   float* xscale;     // [T] power of two bringing max|x_t| into [2^14, 2^15)
-  __half* x16;       // [T][H] activations times xscale, fp16 (gate/up A operand)
-  __half* h16;       // [rows_cap][I] SwiGLU activations, scaled per 128-channel chunk
-  float* hinv;       // [rows_cap][I/128] inverse scale of each chunk; after k_pre_hrow its factor
+  __half* x16;       // [T][H] activations times xscale, fp16
+  __half* xs16;      // [rows_cap][H] x16 rows in expert order (gate/up A operand)
+  __half* h16;       // [rows_cap][I] SwiGLU activations, one scale per row after k_pre_hrow
+  float* hinv;       // [rows_cap][I/64] inverse scale of each 64-channel chunk
   float* hrow;       // [rows_cap] inverse scale of the row (largest chunk inverse scale)
   float* acc;        // [T][H] fp32 output accumulator
 };
@@ -112,19 +113,20 @@ __device__ __forceinline__ void deq_q8_16(const uint4 v, uint32_t s2, uint32_t b
   o1 = make_uint4(p[4], p[5], p[6], p[7]);
 }
 
-// one word of 4-bit codes (8 consecutive K) -> one 16-byte fp16 chunk in the
-// pair order (0,4),(1,5),(2,6),(3,7); activations use the same order.
-__device__ __forceinline__ uint4 deq_q4_word(uint32_t w, uint32_t s2, uint32_t b2) {
-  uint32_t p0, p1, p2, p3;
-  q4_word_to_pairs(w, p0, p1, p2, p3);
+
+// one word of 4-bit codes (8 consecutive K) -> one 16-byte fp16 chunk in
+// natural K order, pairs (0,1),(2,3),(4,5),(6,7): even nibbles sit in the
+// low nibbles of x's bytes, odd ones in y's; a byte permute puts nibbles 2j
+// and 2j+1 into the two halves, the AND/OR makes 1024 + q of each.
+__device__ __forceinline__ uint4 deq_q4_word_nat(uint32_t w, uint32_t s2, uint32_t b2) {
+  const uint32_t x = w & 0x0F0F0F0Fu, y = (w >> 4) & 0x0F0F0F0Fu;
+  const uint32_t p0 = hsub_1024(lop3_and_or(__byte_perm(x, y, 0x0400), 0x000F000Fu, 0x64006400u));
+  const uint32_t p1 = hsub_1024(lop3_and_or(__byte_perm(x, y, 0x0501), 0x000F000Fu, 0x64006400u));
+  const uint32_t p2 = hsub_1024(lop3_and_or(__byte_perm(x, y, 0x0602), 0x000F000Fu, 0x64006400u));
+  const uint32_t p3 = hsub_1024(lop3_and_or(__byte_perm(x, y, 0x0703), 0x000F000Fu, 0x64006400u));
   return make_uint4(hfma2_u32(p0, s2, b2), hfma2_u32(p1, s2, b2), hfma2_u32(p2, s2, b2), hfma2_u32(p3, s2, b2));
 }
 
-// Reorders 8 consecutive fp16 (as 4 pairs) to (0,4),(1,5),(2,6),(3,7).
-__device__ __forceinline__ uint4 perm_q4_order(const uint4 v) {
-  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
-                    __byte_perm(v.y, v.w, 0x7632));
-}
 
 __device__ __forceinline__ uint32_t bf16_to_half2_dup(uint16_t b) {
   const float f = __uint_as_float(static_cast<uint32_t>(b) << 16);
@@ -355,8 +357,8 @@ __global__ void __launch_bounds__(512) k_pre_sort(Params p) {
     for (int b0 = 0; b0 < E1; b0 += 32) {
       const int e = b0 + lane;
       const uint32_t cnt = e < E1 ? s_rows[e] : 0u;
-      const uint32_t nt = (cnt + kTileM - 1) / kTileM;
-      uint32_t ir = nt * kTileM, it = nt;
+      const uint32_t nt = (cnt + kTileM - 1) / kTileM, nst = (cnt + kItemM - 1) / kItemM;
+      uint32_t ir = nt * kTileM, it = nst;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const uint32_t a = __shfl_up_sync(0xffffffffu, ir, o), b = __shfl_up_sync(0xffffffffu, it, o);
@@ -367,7 +369,7 @@ __global__ void __launch_bounds__(512) k_pre_sort(Params p) {
       }
       if (e < E1) {
         p.ws.base[e] = run_rows + ir - nt * kTileM;
-        s_tiles[e] = run_tiles + it - nt;
+        s_tiles[e] = run_tiles + it - nst;
       }
       run_rows += __shfl_sync(0xffffffffu, ir, 31);
       run_tiles += __shfl_sync(0xffffffffu, it, 31);
@@ -376,10 +378,10 @@ __global__ void __launch_bounds__(512) k_pre_sort(Params p) {
   }
   __syncthreads();
   for (int e = tid; e < E1; e += blockDim.x) {
-    const uint32_t cnt = s_rows[e], nt = (cnt + kTileM - 1) / kTileM, b = p.ws.base[e];
-    for (uint32_t j = 0; j < nt; ++j) {
-      const uint32_t rows = cnt - j * kTileM < static_cast<uint32_t>(kTileM) ? cnt - j * kTileM : kTileM;
-      p.ws.tiles[s_tiles[e] + j] = make_uint4(static_cast<uint32_t>(e), b + j * kTileM, rows, 0);
+    const uint32_t cnt = s_rows[e], nst = (cnt + kItemM - 1) / kItemM, b = p.ws.base[e];
+    for (uint32_t j = 0; j < nst; ++j) {
+      const uint32_t rows = cnt - j * kItemM < static_cast<uint32_t>(kItemM) ? cnt - j * kItemM : kItemM;
+      p.ws.tiles[s_tiles[e] + j] = make_uint4(static_cast<uint32_t>(e), b + j * kItemM, rows, 0);
     }
   }
 }
@@ -404,54 +406,66 @@ __global__ void k_pre_scatter(Params p) {
 
 // ------------------------------------------------------ grouped GEMM
 
-// k_pre_gemm: persistent, one CTA per SM, work item = (128-row m-tile, 256-column n-tile).
-//   warps 0-7  producers: thread pt owns B row pt of the n-tile and four
-//              16-byte A chunks (rows pt/8 + 32j, K chunk pt%8) per stage; the
-//              global loads of stage s+2 are issued before stage s is
-//              converted (a three-deep register ring), so HBM/L2 latency is
-//              covered by two stages of MMA.  B: MLX codes -> fp16 s*q + b.
-//              A: gate/up reads the pre-scaled fp16 activations x16 gathered
-//              by token; down reads the fp16 SwiGLU rows times the row's
-//              chunk factor (all chunks of a row share one scale).
-//   warp 8     one thread issues tcgen05.mma (M=128, N=256, K=16) into one of
-//              two TMEM accumulators (256 columns each).
+// k_pre_gemm: persistent, one CTA per SM; work item = 256 rows of one
+// expert (two M=128 tiles) x one 128-column n-tile (64 up + 64 gate
+// channels, or 128 down outputs).  All global -> shared traffic is TMA,
+// issued by one thread, so the SMs keep few requests of their own in flight:
+//   warp 13    loader: per stage one 256-row A box (128-byte swizzle, the
+//              tensor-core operand layout), the n-tile's raw MLX codes and
+//              its scales and biases, all counted on one transaction barrier;
+//              runs up to S stages ahead of the tensor core.
+//   warps 0-7  converters: raw codes -> fp16 s*q + b into the swizzled B tile.
+//   warp 8     one thread issues tcgen05.mma (M=128, N=128, K=16) for both
+//              M halves into one of two TMEM accumulators (256 columns each).
 //   warps 9-12 epilogue, one TMEM lane quadrant each; drains accumulator j&1
 //              while the MMA fills the other.
+// The gate/up A operand is the tokens' fp16 copy gathered into expert order
+// (k_pre_gather); the down A operand is the SwiGLU rows, already in order.
+template <int BITS>
 struct GemmCfg {
-  static constexpr int N = 256;
-  static constexpr int S = 4;  // shared-memory stages
-  static constexpr int kA = kTileM * 128;
-  static constexpr int kB = N * 128;
-  static constexpr int kStage = kA + kB;
+  static constexpr int N = 128;
+  static constexpr int S = 3;                          // shared-memory stages
+  static constexpr int kA = kItemM * 128;              // two M=128 operands, 16 KB apart
+  static constexpr int kB = N * 128;                   // fp16 B tile (swizzled)
+  static constexpr int kRawRow = 64 * BITS / 8;        // raw code bytes of a B row per stage
+  static constexpr int kRaw = N * kRawRow;
+  static constexpr int kScl = N * 16;                  // 8 groups of bf16 scales per B row
+  static constexpr int kStage = kA + kB + kRaw + 2 * kScl;
+  static constexpr uint32_t kTx = kA + kRaw + 2 * kScl;  // TMA bytes per stage
   static constexpr uint32_t kTmemCols = 512;
   static constexpr size_t kSmem = static_cast<size_t>(S) * kStage + 1024;
+  static_assert(kStage % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
 };
 
-// One stage's weight loads of one producer thread (its B row).
-template <int BITS>
-struct StageRegs {
-  uint4 b[BITS == 8 ? 4 : 2];
-  uint32_t sb;  // scale | bias << 16 (bf16 bits) of the row's group
+// TMA descriptors of one grouped GEMM: the A operand and the routed and
+// shared experts' codes, scales and biases.
+struct TmaMaps {
+  CUtensorMap a, bw, bs, bb, sbw, sbs, sbb;
 };
+
+constexpr int kGemmThreads = 14 * 32;
+constexpr int kLoaderWarp = 13;
 
 template <int BITS, int MODE>
-__global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
-  using C = GemmCfg;
+__global__ void __launch_bounds__(kGemmThreads, 1) k_pre_gemm(Params p, const __grid_constant__ TmaMaps tm) {
+  using C = GemmCfg<BITS>;
   extern __shared__ char smraw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t full[C::S], empty[C::S], tfull[2], tempty[2], mdone;
+  __shared__ __align__(8) uint64_t tld[C::S], full[C::S], empty[C::S], tfull[2], tempty[2], mdone;
   __shared__ uint32_t tslot;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = p.k, H = p.H, I = p.I;
   const int kdim = MODE == 0 ? H : I;
   const int nks = kdim / 64;
-  const int n_nt = MODE == 0 ? (2 * I) / C::N : H / C::N;
+  const int n_nt = MODE == 0 ? (2 * I) / C::N : H / C::N;  // n-tiles: 64 up + 64 gate channels, or 128 outputs
   const uint32_t n_items = __ldcg(p.ws.n_mt) * static_cast<uint32_t>(n_nt);
   const uint32_t G = gridDim.x;
   const uint32_t n_local = n_items > blockIdx.x ? (n_items - blockIdx.x + G - 1) / G : 0u;
+  const uint32_t n_stages = n_local * static_cast<uint32_t>(nks);
 
   if (tid == 0) {
     for (int s = 0; s < C::S; ++s) {
+      mbar_init(&tld[s], 1);
       mbar_init(&full[s], kProducerWarps * 32);
       mbar_init(&empty[s], 1);
     }
@@ -460,6 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
       mbar_init(&tempty[b], 4 * 32);
     }
     mbar_init(&mdone, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == kMmaWarp) tmem_alloc(&tslot, C::kTmemCols);
   tc_fence_before();
@@ -468,191 +483,117 @@ __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
   const uint32_t taddr = tslot;
   bool timed_out = false;
 
-  if (warp < kProducerWarps) {
-    // ------------------------------------------------ producers
+  if (warp == kLoaderWarp) {
+    // ------------------------------------------------ TMA loader (one thread)
+    if (lane == 0) {
+      uint32_t cur_li = 0xFFFFFFFFu;
+      int ya = 0, yb = 0;
+      bool se = false;
+      for (uint32_t st = 0; st < n_stages; ++st) {
+        const int slot = static_cast<int>(st % C::S);
+        const uint32_t n = st / C::S;
+        if (n > 0 && !mbar_wait(&empty[slot], (n - 1) & 1, kWaitNs)) {
+          timed_out = true;
+          break;
+        }
+        const uint32_t li = st / nks;
+        const int ks = static_cast<int>(st % nks);
+        if (li != cur_li) {
+          cur_li = li;
+          const uint32_t item = blockIdx.x + li * G;
+          const uint4 tile = __ldg(p.ws.tiles + item / n_nt);
+          const int e = static_cast<int>(tile.x), nt = static_cast<int>(item % n_nt);
+          se = e == p.E;
+          ya = static_cast<int>(tile.y);
+          // first B row of the n-tile in the expert bank (or the shared expert)
+          yb = MODE == 0 ? (se ? 0 : e * 2 * I) + nt * 64 : (se ? 0 : e * H) + nt * C::N;
+        }
+        char* sA = sm + slot * C::kStage;
+        char* sRaw = sA + C::kA + C::kB;
+        char* sScl = sRaw + C::kRaw;
+        const uint32_t bar = smem_u32(&tld[slot]);
+        mbar_arrive_expect_tx(&tld[slot], C::kTx);
+        tma_load_2d(smem_u32(sA), &tm.a, ks * 64, ya, bar);
+        const CUtensorMap* mw = se ? &tm.sbw : &tm.bw;
+        const CUtensorMap* ms = se ? &tm.sbs : &tm.bs;
+        const CUtensorMap* mb = se ? &tm.sbb : &tm.bb;
+        const int xs = (ks >> 3) * 8;  // 8-group block of the scales holding group ks
+        if (MODE == 0) {
+          // up rows then gate rows, 64 each
+          for (int h = 0; h < 2; ++h) {
+            const int y = yb + h * I;
+            tma_load_2d(smem_u32(sRaw + h * 64 * C::kRawRow), mw, ks * C::kRawRow, y, bar);
+            tma_load_2d(smem_u32(sScl + h * 64 * 16), ms, xs, y, bar);
+            tma_load_2d(smem_u32(sScl + C::kScl + h * 64 * 16), mb, xs, y, bar);
+          }
+        } else {
+          tma_load_2d(smem_u32(sRaw), mw, ks * C::kRawRow, yb, bar);
+          tma_load_2d(smem_u32(sScl), ms, xs, yb, bar);
+          tma_load_2d(smem_u32(sScl + C::kScl), mb, xs, yb, bar);
+        }
+      }
+    }
+  } else if (warp < kProducerWarps) {
+    // ------------------------------------------------ converters
     const int pt = tid;  // 0..255
-    const int ca = pt & 7;
-    const uint32_t n_stages = n_local * static_cast<uint32_t>(nks);
-    const size_t wrow = static_cast<size_t>(kdim) * BITS / 32, srow = kdim / 64;
-    // B row of this thread within the n-tile
-    auto b_row = [&](uint32_t nt) -> int {
-      if (MODE == 0) return pt < 128 ? static_cast<int>(nt) * 128 + pt : I + static_cast<int>(nt) * 128 + (pt - 128);
-      return static_cast<int>(nt) * C::N + pt;
-    };
-    // Per-item sources of this thread (rows' A addresses, B row).  The next
-    // item's tile record is loaded on entering an item and its rows' entry
-    // ids one stage later, so entering the next item waits on nothing.
-    uint32_t cur_li = 0xFFFFFFFFu;
-    uint32_t aoff[4];  // A row element offsets into x16 / h16 (0xFFFFFFFF: padding row)
-    const uint32_t* bsrc = nullptr;
-    const uint16_t *ssrc = nullptr, *bisrc = nullptr;
-    const __half* abase = MODE == 0 ? p.ws.x16 : p.ws.h16;
-    uint4 nx_tile = make_uint4(0, 0, 0, 0);
-    uint32_t nx_ent[4] = {0, 0, 0, 0};
-    int nx_phase = 0;  // 0: nothing pending, 1: nx_tile loading, 2: nx_ent loading
-    auto tile_of = [&](uint32_t li) -> uint4 {
-      const uint32_t item = blockIdx.x + li * G;
-      return __ldg(p.ws.tiles + item / n_nt);
-    };
-    auto ents_of = [&](const uint4& tile, uint32_t (&ent)[4]) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = (pt >> 3) + 32 * j;
-        ent[j] = (MODE == 0 && r < static_cast<int>(tile.z)) ? __ldg(p.ws.perm + tile.y + r) : 0u;
-      }
-    };
-    auto enter_item = [&](uint32_t li) {
-      uint4 tile;
-      uint32_t ent[4];
-      if (nx_phase == 2 && cur_li + 1 == li) {
-        tile = nx_tile;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) ent[j] = nx_ent[j];
-      } else {
-        tile = tile_of(li);
-        ents_of(tile, ent);
-      }
-      cur_li = li;
-      nx_phase = 0;
-      if (li + 1 < n_local) {
-        nx_tile = tile_of(li + 1);
-        nx_phase = 1;
-      }
-      const uint32_t nt = (blockIdx.x + li * G) % n_nt;
-      const int e = static_cast<int>(tile.x), row0 = static_cast<int>(tile.y), nrows = static_cast<int>(tile.z);
-      const bool shared_e = e == p.E;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = (pt >> 3) + 32 * j;
-        aoff[j] = 0xFFFFFFFFu;
-        if (r < nrows)  // rows past nrows are padding
-          aoff[j] = MODE == 0 ? (ent[j] / (K + 1)) * static_cast<uint32_t>(H) + ca * 8
-                              : static_cast<uint32_t>(row0 + r) * static_cast<uint32_t>(I) + ca * 8;
-      }
-      const uint32_t* bw;
-      const uint16_t *bs, *bb;
-      if (MODE == 0) {
-        const size_t ew = static_cast<size_t>(2) * I * wrow, es = static_cast<size_t>(2) * I * srow;
-        bw = shared_e ? p.sgu_w : p.gu_w + e * ew;
-        bs = shared_e ? p.sgu_s : p.gu_s + e * es;
-        bb = shared_e ? p.sgu_b : p.gu_b + e * es;
-      } else {
-        const size_t ew = static_cast<size_t>(H) * wrow, es = static_cast<size_t>(H) * srow;
-        bw = shared_e ? p.sdn_w : p.dn_w + e * ew;
-        bs = shared_e ? p.sdn_s : p.dn_s + e * es;
-        bb = shared_e ? p.sdn_b : p.dn_b + e * es;
-      }
-      const size_t brow = static_cast<size_t>(b_row(nt));
-      bsrc = bw + brow * wrow;
-      ssrc = bs + brow * srow;
-      bisrc = bb + brow * srow;
-    };
-    // issue stage st: the A tile by cp.async into its ring slot (which must
-    // be free), the B row's codes and scale/bias into registers
-    auto issue = [&](uint32_t st, StageRegs<BITS>& R) -> bool {
+    for (uint32_t st = 0; st < n_stages; ++st) {
       const int slot = static_cast<int>(st % C::S);
       const uint32_t n = st / C::S;
-      if (n > 0 && !mbar_wait(&empty[slot], (n - 1) & 1, kWaitNs)) return false;
-      const uint32_t li = st / nks;
+      const bool ok = mbar_wait(&tld[slot], n & 1, kWaitNs);
+      if (!ok) {
+        timed_out = true;
+        break;
+      }
       const int ks = static_cast<int>(st % nks);
-      if (li != cur_li) {
-        enter_item(li);
-      } else if (nx_phase == 1) {
-        ents_of(nx_tile, nx_ent);  // the next item's tile record has had a stage to arrive
-        nx_phase = 2;
-      }
-      char* sA = sm + slot * C::kStage;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        char* dst = sA + sw128_offset((pt >> 3) + 32 * j, ca * 8);
-        if (aoff[j] != 0xFFFFFFFFu)
-          cp_async16(dst, abase + aoff[j] + ks * 64);
-        else
-          *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-      }
-      asm volatile("cp.async.commit_group;\n" ::: "memory");
-      const uint4* src = reinterpret_cast<const uint4*>(bsrc + ks * (BITS * 2));
-#pragma unroll
-      for (int q = 0; q < (BITS == 8 ? 4 : 2); ++q) R.b[q] = ld_stream_v4(src + q);
-      R.sb = static_cast<uint32_t>(__ldg(ssrc + ks)) | (static_cast<uint32_t>(__ldg(bisrc + ks)) << 16);
-      return true;
-    };
-    // finish stage st: dequantised B into its slot; the slot's A has landed
-    auto finish = [&](uint32_t st, const StageRegs<BITS>& R) {
-      const int slot = static_cast<int>(st % C::S);
       char* sA = sm + slot * C::kStage;
       char* sB = sA + C::kA;
-      if (BITS == 4) {
-        // 4-bit weights come out in the pair order (0,4),(1,5),(2,6),(3,7):
-        // permute this thread's A chunks the same way
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4* q = reinterpret_cast<uint4*>(sA + sw128_offset((pt >> 3) + 32 * j, ca * 8));
-          *q = perm_q4_order(*q);
-        }
-      }
-      const uint32_t s2 = bf16_to_half2_dup(static_cast<uint16_t>(R.sb & 0xFFFFu));
-      const uint32_t b2 = bf16_to_half2_dup(static_cast<uint16_t>(R.sb >> 16));
+      const char* sRaw = sB + C::kB;
+      const uint16_t* sSc = reinterpret_cast<const uint16_t*>(sRaw + C::kRaw);
+      const uint16_t* sBi = sSc + C::kScl / 2;
+      const int g = ks & 7;
       if (BITS == 8) {
+        // 128 rows x 4 16-byte chunks: thread -> chunk pt % 4 of rows pt / 4 and pt / 4 + 64
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int i = 0; i < 2; ++i) {
+          const int tr = (pt >> 2) + 64 * i, c = pt & 3;
+          const uint4 v = *reinterpret_cast<const uint4*>(sRaw + tr * C::kRawRow + c * 16);
+          const uint32_t s2 = bf16_to_half2_dup(sSc[tr * 8 + g]);
+          const uint32_t b2 = bf16_to_half2_dup(sBi[tr * 8 + g]);
           uint4 o0, o1;
-          deq_q8_16(R.b[q], s2, b2, o0, o1);
-          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 16)) = o0;
-          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 16 + 8)) = o1;
+          deq_q8_16(v, s2, b2, o0, o1);
+          *reinterpret_cast<uint4*>(sB + sw128_offset(tr, c * 16)) = o0;
+          *reinterpret_cast<uint4*>(sB + sw128_offset(tr, c * 16 + 8)) = o1;
         }
       } else {
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 32)) = deq_q4_word(R.b[q].x, s2, b2);
-          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 32 + 8)) = deq_q4_word(R.b[q].y, s2, b2);
-          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 32 + 16)) = deq_q4_word(R.b[q].z, s2, b2);
-          *reinterpret_cast<uint4*>(sB + sw128_offset(pt, q * 32 + 24)) = deq_q4_word(R.b[q].w, s2, b2);
-        }
+        // 128 rows x 2 16-byte chunks (32 codes each): thread -> chunk pt % 2 of row pt / 2
+        const int tr = pt >> 1, c = pt & 1;
+        const uint4 v = *reinterpret_cast<const uint4*>(sRaw + tr * C::kRawRow + c * 16);
+        const uint32_t s2 = bf16_to_half2_dup(sSc[tr * 8 + g]);
+        const uint32_t b2 = bf16_to_half2_dup(sBi[tr * 8 + g]);
+        *reinterpret_cast<uint4*>(sB + sw128_offset(tr, c * 32)) = deq_q4_word_nat(v.x, s2, b2);
+        *reinterpret_cast<uint4*>(sB + sw128_offset(tr, c * 32 + 8)) = deq_q4_word_nat(v.y, s2, b2);
+        *reinterpret_cast<uint4*>(sB + sw128_offset(tr, c * 32 + 16)) = deq_q4_word_nat(v.z, s2, b2);
+        *reinterpret_cast<uint4*>(sB + sw128_offset(tr, c * 32 + 24)) = deq_q4_word_nat(v.w, s2, b2);
       }
-    };
-    // step st: issue st+2 (two stages of MMA cover its latency), then finish
-    // st, whose loads were issued two steps earlier; one cp.async group per
-    // issued stage, so at most two younger groups may still be in flight.
-    // Issuing st+2 needs its slot, freed by the MMA of st+2-S = st-2, which
-    // leaves two stages of slack between the producers and the MMA.
-    auto step = [&](uint32_t st, StageRegs<BITS>& use, StageRegs<BITS>& fill) -> bool {
-      if (st >= n_stages) return true;
-      if (st + 2 < n_stages) {
-        if (!issue(st + 2, fill)) return false;
-        asm volatile("cp.async.wait_group 2;\n" ::: "memory");
-      } else if (st + 1 < n_stages) {
-        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-      } else {
-        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-      }
-      finish(st, use);
       fence_proxy_async_smem();
-      mbar_arrive(&full[st % C::S]);
-      return true;
-    };
-    StageRegs<BITS> r0, r1, r2;
-    bool ok = true;
-    if (n_stages > 0) ok = issue(0, r0);
-    if (ok && n_stages > 1) ok = issue(1, r1);
-    if (!ok) timed_out = true;
-    for (uint32_t st = 0; st < n_stages && !timed_out; st += 3) {
-      if (!step(st, r0, r2) || !step(st + 1, r1, r0) || !step(st + 2, r2, r1)) timed_out = true;
+      mbar_arrive(&full[slot]);
     }
-    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------ MMA issue (one thread)
+    // item j accumulates in TMEM columns [256 (j & 1), +256): M half h in
+    // [+128 h, +128); a second half with no rows is skipped
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(kTileM, C::N, false);
       uint32_t st = 0;
       for (uint32_t j = 0; j < n_local && !timed_out; ++j) {
         const uint32_t buf = j & 1;
+        const uint32_t nrows = __ldcg(p.ws.tiles + (blockIdx.x + j * G) / n_nt).z;
+        const int nh = nrows > static_cast<uint32_t>(kTileM) ? 2 : 1;
         if (j >= 2 && !mbar_wait(&tempty[buf], ((j >> 1) - 1) & 1, kWaitNs)) {
           timed_out = true;
           break;
         }
         tc_fence_after();
-        const uint32_t d = taddr + buf * C::N;
         for (int ks = 0; ks < nks; ++ks, ++st) {
           const int s = static_cast<int>(st % C::S);
           if (!mbar_wait(&full[s], (st / C::S) & 1, kWaitNs)) {
@@ -661,10 +602,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
           }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sm + s * C::kStage), b0 = a0 + C::kA;
+          for (int h = 0; h < nh; ++h) {
+            const uint32_t d = taddr + buf * 256 + h * 128;
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_f16(d, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(b0 + k * 32), idesc,
-                     (ks == 0 && k == 0) ? 0u : 1u);
+            for (int k = 0; k < 4; ++k)
+              umma_f16(d, umma_desc_sw128(a0 + h * (C::kA / 2) + k * 32), umma_desc_sw128(b0 + k * 32), idesc,
+                       (ks == 0 && k == 0) ? 0u : 1u);
+          }
           umma_commit(smem_u32(&empty[s]));
         }
         if (timed_out) break;
@@ -676,18 +620,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
     }
   } else {
     // ------------------------------------------------ epilogue (warps 9..12)
+    // thread (quad, lane) owns TMEM lane r = 32 quad + lane: item row r of
+    // M half 0 and row 128 + r of M half 1
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     for (uint32_t j = 0; j < n_local; ++j) {
       const uint32_t item = blockIdx.x + j * G;
       const uint32_t mt = item / n_nt, nt = item % n_nt;
       const uint32_t buf = j & 1;
-      const uint32_t tl = taddr + buf * C::N + (static_cast<uint32_t>(quad * 32) << 16);
       const uint4 tile = __ldcg(p.ws.tiles + mt);
       const int row0 = static_cast<int>(tile.y), nrows = static_cast<int>(tile.z);
-      uint32_t ent = r < nrows ? __ldcg(p.ws.perm + row0 + r) : 0xFFFFFFFFu;
-      const bool valid = ent != 0xFFFFFFFFu;
-      if (!valid) ent = 0u;
+      const int nh = nrows > kTileM ? 2 : 1;
+      uint32_t ent[2];
+      for (int h = 0; h < 2; ++h) {
+        const int rr = h * kTileM + r;
+        ent[h] = (h < nh && rr < nrows) ? __ldcg(p.ws.perm + row0 + rr) : 0xFFFFFFFFu;
+      }
       // the whole warp leaves together: tcgen05.ld below is warp-collective
       const bool ok = mbar_wait(&tfull[buf], (j >> 1) & 1, kWaitNs);
       if (__any_sync(0xffffffffu, !ok)) {
@@ -695,62 +643,69 @@ __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
         break;
       }
       tc_fence_after();
-      if (MODE == 0) {
-        const uint32_t t = ent / (K + 1);
-        const float xinv = valid ? 1.0f / __ldcg(p.ws.xscale + t) : 1.f;
-        float mx = 0.f;
-        for (int cc = 0; cc < 8; ++cc) {
-          uint32_t u[16], gt[16];
-          tmem_ld16(tl + cc * 16, u);
-          tmem_ld16(tl + 128 + cc * 16, gt);
-          tmem_wait_ld();
+      for (int h = 0; h < nh; ++h) {
+        const uint32_t tl = taddr + buf * 256 + h * 128 + (static_cast<uint32_t>(quad * 32) << 16);
+        const bool valid = ent[h] != 0xFFFFFFFFu;
+        const uint32_t e_id = valid ? ent[h] : 0u;
+        const size_t row = static_cast<size_t>(row0 + h * kTileM + r);
+        if (MODE == 0) {
+          // up in columns [0, 64), gate in [64, 128): 64 SwiGLU channels nt*64..
+          const uint32_t t = e_id / (K + 1);
+          const float xinv = valid ? 1.0f / __ldcg(p.ws.xscale + t) : 1.f;
+          float mx = 0.f;
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t u[16], gt[16];
+            tmem_ld16(tl + cc * 16, u);
+            tmem_ld16(tl + 64 + cc * 16, gt);
+            tmem_wait_ld();
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const float up = __uint_as_float(u[q]) * xinv, ga = __uint_as_float(gt[q]) * xinv;
-            mx = fmaxf(mx, fabsf((ga / (1.0f + expf(-ga))) * up));
+            for (int q = 0; q < 16; ++q) {
+              const float up = __uint_as_float(u[q]) * xinv, ga = __uint_as_float(gt[q]) * xinv;
+              mx = fmaxf(mx, fabsf((ga / (1.0f + expf(-ga))) * up));
+            }
           }
-        }
-        float hs, hi;
-        fp16_range_scale(mx, hs, hi);
-        __half* dst = p.ws.h16 + static_cast<size_t>(row0 + r) * I + nt * 128;
-        for (int cc = 0; cc < 8; ++cc) {
-          uint32_t u[16], gt[16];
-          tmem_ld16(tl + cc * 16, u);
-          tmem_ld16(tl + 128 + cc * 16, gt);
-          tmem_wait_ld();
-          uint32_t hv[8];
+          float hs, hi;
+          fp16_range_scale(mx, hs, hi);
+          __half* dst = p.ws.h16 + row * I + nt * 64;
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t u[16], gt[16];
+            tmem_ld16(tl + cc * 16, u);
+            tmem_ld16(tl + 64 + cc * 16, gt);
+            tmem_wait_ld();
+            uint32_t hv[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float up0 = __uint_as_float(u[2 * q]) * xinv, ga0 = __uint_as_float(gt[2 * q]) * xinv;
-            const float up1 = __uint_as_float(u[2 * q + 1]) * xinv, ga1 = __uint_as_float(gt[2 * q + 1]) * xinv;
-            hv[q] = half2_bits((ga0 / (1.0f + expf(-ga0))) * up0 * hs, (ga1 / (1.0f + expf(-ga1))) * up1 * hs);
+            for (int q = 0; q < 8; ++q) {
+              const float up0 = __uint_as_float(u[2 * q]) * xinv, ga0 = __uint_as_float(gt[2 * q]) * xinv;
+              const float up1 = __uint_as_float(u[2 * q + 1]) * xinv, ga1 = __uint_as_float(gt[2 * q + 1]) * xinv;
+              hv[q] = half2_bits((ga0 / (1.0f + expf(-ga0))) * up0 * hs, (ga1 / (1.0f + expf(-ga1))) * up1 * hs);
+            }
+            if (valid) {
+              reinterpret_cast<uint4*>(dst + cc * 16)[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+              reinterpret_cast<uint4*>(dst + cc * 16)[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+            }
           }
+          if (valid) p.ws.hinv[row * (I / 64) + nt] = hi;
+        } else {
+          const uint32_t t = e_id / (K + 1), slot = e_id % (K + 1);
+          float w = 0.f;
           if (valid) {
-            reinterpret_cast<uint4*>(dst + cc * 16)[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-            reinterpret_cast<uint4*>(dst + cc * 16)[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+            w = slot < static_cast<uint32_t>(K) ? __ldcg(p.ws.scores + static_cast<size_t>(t) * K + slot)
+                                                : __ldcg(p.ws.sg + t);
+            w *= __ldcg(p.ws.hrow + row);
           }
-        }
-        if (valid) p.ws.hinv[static_cast<size_t>(row0 + r) * (I / 128) + nt] = hi;
-      } else {
-        const uint32_t t = ent / (K + 1), slot = ent % (K + 1);
-        float w = 0.f;
-        if (valid) {
-          w = slot < static_cast<uint32_t>(K) ? __ldcg(p.ws.scores + static_cast<size_t>(t) * K + slot)
-                                              : __ldcg(p.ws.sg + t);
-          w *= __ldcg(p.ws.hrow + row0 + r);
-        }
-        float* dst = p.ws.acc + static_cast<size_t>(t) * H + nt * C::N;
-        for (int cc = 0; cc < C::N / 16; ++cc) {
-          uint32_t v[16];
-          tmem_ld16(tl + cc * 16, v);
-          tmem_wait_ld();
-          if (valid) {
+          float* dst = p.ws.acc + static_cast<size_t>(t) * H + nt * C::N;
+          for (int cc = 0; cc < C::N / 16; ++cc) {
+            uint32_t v[16];
+            tmem_ld16(tl + cc * 16, v);
+            tmem_wait_ld();
+            if (valid) {
 #pragma unroll
-            for (int q = 0; q < 16; q += 4)
-              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + cc * 16 + q),
-                           "f"(__uint_as_float(v[q]) * w), "f"(__uint_as_float(v[q + 1]) * w),
-                           "f"(__uint_as_float(v[q + 2]) * w), "f"(__uint_as_float(v[q + 3]) * w)
-                           : "memory");
+              for (int q = 0; q < 16; q += 4)
+                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + cc * 16 + q),
+                             "f"(__uint_as_float(v[q]) * w), "f"(__uint_as_float(v[q + 1]) * w),
+                             "f"(__uint_as_float(v[q + 2]) * w), "f"(__uint_as_float(v[q + 3]) * w)
+                             : "memory");
+            }
           }
         }
       }
@@ -768,13 +723,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_pre_gemm(Params p) {
   }
 }
 
-// Between the GEMMs: give all 128-channel chunks of a SwiGLU row one scale,
+// Gate/up A operand: each routed row's fp16 token copy, in expert order
+// (a warp per row; padding rows stay unwritten and are never stored from).
+__global__ void k_pre_gather(Params p) {
+  const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+  const int n16 = p.H / 8;
+  for (int row = blockIdx.x * wpb + (threadIdx.x >> 5); row < p.rows_cap; row += gridDim.x * wpb) {
+    const uint32_t ent = __ldcg(p.ws.perm + row);
+    if (ent == 0xFFFFFFFFu) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(p.ws.x16 + static_cast<size_t>(ent / (p.k + 1)) * p.H);
+    uint4* dst = reinterpret_cast<uint4*>(p.ws.xs16 + static_cast<size_t>(row) * p.H);
+    for (int q = lane; q < n16; q += 32) dst[q] = __ldcg(src + q);
+  }
+}
+
+// Between the GEMMs: give all 64-channel chunks of a SwiGLU row one scale,
 // the smallest of the chunks' (the chunk with the largest values keeps its
 // scale; the others are multiplied by a power of two <= 1, exact unless a
 // value falls below fp16's normal range).  hrow = that scale's inverse.
 // One warp per row; lane l handles 8-value pieces l, l+32.
 __global__ void k_pre_hrow(Params p) {
-  const int nq = p.I / 128, lane = threadIdx.x & 31;
+  const int nq = p.I / 64, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   for (int row = blockIdx.x * wpb + (threadIdx.x >> 5); row < p.rows_cap; row += gridDim.x * wpb) {
     if (__ldcg(p.ws.perm + row) == 0xFFFFFFFFu) continue;
@@ -783,7 +752,7 @@ __global__ void k_pre_hrow(Params p) {
     for (int c = 0; c < nq; ++c) m = fmaxf(m, __ldcg(h + c));
     uint4* hv = reinterpret_cast<uint4*>(p.ws.h16 + static_cast<size_t>(row) * p.I);
     for (int q = lane; q < p.I / 8; q += 32) {
-      const float f = __ldcg(h + q / 16) / m;
+      const float f = __ldcg(h + q / 8) / m;
       if (f != 1.0f) {
         const uint32_t f2 = half2_bits(f, f);
         uint4 v = hv[q];
@@ -820,7 +789,7 @@ __global__ void k_pre_final(Params p) {
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 struct Layout {
-  size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, x16, h16, hinv, hrow, acc, total;
+  size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, x16, xs16, h16, hinv, hrow, acc, total;
   int rows_cap, max_mt;
 };
 
@@ -848,8 +817,9 @@ Layout make_layout(const rnb_moe_desc& d) {
   L.sg = take(T * 4);
   L.xscale = take(T * 4);
   L.x16 = take(T * d.H * 2);
+  L.xs16 = take(static_cast<size_t>(L.rows_cap) * d.H * 2);
   L.h16 = take(static_cast<size_t>(L.rows_cap) * d.I * 2);
-  L.hinv = take(static_cast<size_t>(L.rows_cap) * (d.I / 128) * 4);
+  L.hinv = take(static_cast<size_t>(L.rows_cap) * (d.I / 64) * 4);
   L.hrow = take(static_cast<size_t>(L.rows_cap) * 4);
   L.acc = take(T * d.H * 4);
   L.total = o;
@@ -865,10 +835,63 @@ bool prefill_supported(const rnb_moe_desc& d) {
          d.k <= pre::kMaxK && (d.bits == 4 || d.bits == 8) && d.group == 64;
 }
 
+namespace pre {
+
+// 2-D tensor map over a row-major [rows][inner] array (inner in elements).
+bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  return cuTensorMapEncodeTiled(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Descriptors of one GEMM: A (rows of xs16 or h16, 256-row boxes, 128-byte
+// swizzle) and the codes / scales / biases of the routed and shared experts
+// (boxes of one stage's 64 K for the n-tile's rows).
+template <int BITS>
+bool make_maps(const Params& p, int mode, int rows_cap, TmaMaps& tm) {
+  using C = GemmCfg<BITS>;
+  const int K = mode == 0 ? p.H : p.I;              // contraction length
+  const uint64_t rows_e = mode == 0 ? 2ull * p.I : static_cast<uint64_t>(p.H);  // weight rows per expert
+  const uint32_t box_rows = mode == 0 ? 64 : 128;   // gate/up: up and gate halves separately
+  const uint64_t wbytes = static_cast<uint64_t>(K) * BITS / 8, groups = K / 64;
+  bool ok = encode_2d(&tm.a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, mode == 0 ? static_cast<const void*>(p.ws.xs16) : p.ws.h16,
+                      K, rows_cap, static_cast<uint64_t>(K) * 2, 64, kItemM, CU_TENSOR_MAP_SWIZZLE_128B);
+  const void* w = mode == 0 ? static_cast<const void*>(p.gu_w) : p.dn_w;
+  const void* sc = mode == 0 ? static_cast<const void*>(p.gu_s) : p.dn_s;
+  const void* bi = mode == 0 ? static_cast<const void*>(p.gu_b) : p.dn_b;
+  ok = ok && encode_2d(&tm.bw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, wbytes, rows_e * p.E, wbytes, C::kRawRow, box_rows,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  ok = ok && encode_2d(&tm.bs, CU_TENSOR_MAP_DATA_TYPE_UINT16, sc, groups, rows_e * p.E, groups * 2, 8, box_rows,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  ok = ok && encode_2d(&tm.bb, CU_TENSOR_MAP_DATA_TYPE_UINT16, bi, groups, rows_e * p.E, groups * 2, 8, box_rows,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  // shared expert (the routed bank again when there is none: never read)
+  const void* sw = p.has_shared ? (mode == 0 ? static_cast<const void*>(p.sgu_w) : p.sdn_w) : w;
+  const void* ss = p.has_shared ? (mode == 0 ? static_cast<const void*>(p.sgu_s) : p.sdn_s) : sc;
+  const void* sb = p.has_shared ? (mode == 0 ? static_cast<const void*>(p.sgu_b) : p.sdn_b) : bi;
+  ok = ok && encode_2d(&tm.sbw, CU_TENSOR_MAP_DATA_TYPE_UINT8, sw, wbytes, rows_e, wbytes, C::kRawRow, box_rows,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  ok = ok && encode_2d(&tm.sbs, CU_TENSOR_MAP_DATA_TYPE_UINT16, ss, groups, rows_e, groups * 2, 8, box_rows,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  ok = ok && encode_2d(&tm.sbb, CU_TENSOR_MAP_DATA_TYPE_UINT16, sb, groups, rows_e, groups * 2, 8, box_rows,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  return ok;
+}
+
+}  // namespace pre
+
 template <int BITS>
 static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st) {
   using namespace pre;
+  using C = GemmCfg<BITS>;
   cudaError_t e;
+  TmaMaps tm0, tm1;
+  if (!make_maps<BITS>(p, 0, L.rows_cap, tm0) || !make_maps<BITS>(p, 1, L.rows_cap, tm1))
+    return fail(RNB_ERR_CUDA, "prefill: tensor map encoding failed");
   stage_begin(st);
   // zero the histogram and the fp32 accumulator; padding rows of perm = ~0
   e = cudaMemsetAsync(p.ws.counts, 0, (p.E + 1) * 4, st);
@@ -880,10 +903,10 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
     e = cudaFuncSetAttribute(k_pre_route, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kRouteSmem));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(k_pre_gemm<BITS, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(GemmCfg::kSmem));
+                               static_cast<int>(C::kSmem));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(k_pre_gemm<BITS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(GemmCfg::kSmem));
+                               static_cast<int>(C::kSmem));
     if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill smem attribute: ") + cudaGetErrorString(e));
     attr = true;
   }
@@ -893,12 +916,13 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
   stage_end(st, RNB_STAGE_SORT);
   const size_t n_scatter = static_cast<size_t>(p.T) * (p.k + 1);
   k_pre_scatter<<<static_cast<unsigned>((n_scatter + 255) / 256), 256, 0, st>>>(p);
+  k_pre_gather<<<(L.rows_cap + 7) / 8, 256, 0, st>>>(p);
   stage_end(st, RNB_STAGE_SCATTER);
   const int nc = dev_info().sms;
-  k_pre_gemm<BITS, 0><<<nc, kThreads, GemmCfg::kSmem, st>>>(p);
+  k_pre_gemm<BITS, 0><<<nc, kGemmThreads, C::kSmem, st>>>(p, tm0);
   stage_end(st, RNB_STAGE_GATEUP);
   k_pre_hrow<<<(L.rows_cap + 7) / 8, 256, 0, st>>>(p);
-  k_pre_gemm<BITS, 1><<<nc, kThreads, GemmCfg::kSmem, st>>>(p);
+  k_pre_gemm<BITS, 1><<<nc, kGemmThreads, C::kSmem, st>>>(p, tm1);
   stage_end(st, RNB_STAGE_DOWN);
   k_pre_final<<<nc * 4, 256, 0, st>>>(p);
   stage_end(st, RNB_STAGE_FINAL);
@@ -956,6 +980,7 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
   p.ws.sg = reinterpret_cast<float*>(b + L.sg);
   p.ws.xscale = reinterpret_cast<float*>(b + L.xscale);
   p.ws.x16 = reinterpret_cast<__half*>(b + L.x16);
+  p.ws.xs16 = reinterpret_cast<__half*>(b + L.xs16);
   p.ws.h16 = reinterpret_cast<__half*>(b + L.h16);
   p.ws.hinv = reinterpret_cast<float*>(b + L.hinv);
   p.ws.hrow = reinterpret_cast<float*>(b + L.hrow);
