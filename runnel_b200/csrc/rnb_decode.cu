@@ -1219,7 +1219,9 @@ __global__ void __launch_bounds__(256) k_ep_reduce(Params p, const float* partia
   }
 }
 
-template <int BITS>
+// EP: compiled with the expert-parallel exchange (ep_world > 1); the
+// single-GPU instance carries no exchange code.
+template <int BITS, bool EP>
 __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) {
   extern __shared__ __align__(16) char sm[];
   using TL = Tile2<BITS>;
@@ -1340,8 +1342,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     int e;
     float sc;
     RNB_TRACE_MARK(p, 12);
-    const int nre = warp_route_token(ivl, Et, K, p.x + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane, false,
-                                     nullptr, &e, &sc);
+    const int nre = warp_route_token_body(ivl, Et, K, p.x + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane,
+                                          false, nullptr, &e, &sc);
     RNB_TRACE_MARK(p, 13);
 #ifdef RNB_TRACE
     if (t == 0 && lane == 0) trace_value(p, 11, nre);
@@ -1633,7 +1635,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
         static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
     };
     RNB_TRACE_MARK(p, 14);
-    if (p.ep_world > 1) {
+    if (EP) {
       float* stage = sRed;  // this tile's partials, [t][r]
       if (tid < T * 16) stage[tid] = acc;
       __syncthreads();
@@ -1654,7 +1656,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
       atomicExch(bar1, 0u);
       atomicExch(bar2, 0u);
       atomicExch(exitc, 0u);
-      if (p.ep_world > 1) p.ep_seq[0] += 1;  // every CTA's exchange is done
+      if (EP) p.ep_seq[0] += 1;  // every CTA's exchange is done
       __threadfence();
     }
   }
@@ -1808,7 +1810,10 @@ template <int BITS>
 size_t persistent_static_smem() {
   static size_t bytes = [] {
     cudaFuncAttributes fa;
-    return cudaFuncGetAttributes(&fa, k_decode<BITS>) == cudaSuccess ? fa.sharedSizeBytes : size_t(1024);
+    cudaFuncAttributes fb;
+    const bool ok = cudaFuncGetAttributes(&fa, k_decode<BITS, false>) == cudaSuccess &&
+                    cudaFuncGetAttributes(&fb, k_decode<BITS, true>) == cudaSuccess;
+    return ok ? (fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes) : size_t(1024);
   }();
   return bytes;
 }
@@ -1858,8 +1863,8 @@ bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem
 
 template <int BITS>
 int run_persistent(Params& p, const PPlan& pl, size_t smem, int nc, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(k_decode<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  auto kern = p.ep_world > 1 ? k_decode<BITS, true> : k_decode<BITS, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_decode smem attribute: ") + cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nc);
@@ -1872,7 +1877,7 @@ int run_persistent(Params& p, const PPlan& pl, size_t smem, int nc, cudaStream_t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   stage_begin(st);
-  e = cudaLaunchKernelEx(&cfg, k_decode<BITS>, p, pl);
+  e = cudaLaunchKernelEx(&cfg, kern, p, pl);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_decode launch: ") + cudaGetErrorString(e));
   stage_end(st, RNB_STAGE_DECODE);
   return RNB_OK;

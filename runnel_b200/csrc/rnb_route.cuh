@@ -204,7 +204,7 @@ __device__ __forceinline__ uint32_t warp_select_k(const uint32_t (&keys)[8], int
 // and, if there were any, the selection runs again.  With exact_all every
 // uncertain logit is resolved and, if logits_row is non-null, all Et bf16
 // logits are written there as fp32.  Returns the number of logits resolved.
-static __device__ __noinline__ int warp_route_token(const uint32_t* ivl, int Et, int K, const uint16_t* xrow,
+__device__ __forceinline__ int warp_route_token_body(const uint32_t* ivl, int Et, int K, const uint16_t* xrow,
                                                      const uint16_t* router_w, int H, int lane, bool exact_all,
                                                      float* logits_row, int* e_out, float* score_out) {
   uint32_t klo[8], vhi = 0;  // vhi bit i: lo != hi for expert lane + 32 i
@@ -252,6 +252,13 @@ static __device__ __noinline__ int warp_route_token(const uint32_t* ivl, int Et,
   *e_out = route_key_expert(mine);
   *score_out = pw / selsum;
   return n_exact;
+}
+
+// Out-of-line form for kernels where code size matters less than one copy.
+static __device__ __noinline__ int warp_route_token(const uint32_t* ivl, int Et, int K, const uint16_t* xrow,
+                                                     const uint16_t* router_w, int H, int lane, bool exact_all,
+                                                     float* logits_row, int* e_out, float* score_out) {
+  return warp_route_token_body(ivl, Et, K, xrow, router_w, H, lane, exact_all, logits_row, e_out, score_out);
 }
 
 }  // namespace rnb
