@@ -62,6 +62,14 @@ def step_bytes(bits, distinct_experts, T, H=2048, I=512, E=256, shared=True):
     return b
 
 
+# DRAM bytes (read + write) per step of the dominant kernel, from one ncu
+# capture of the same workload (profiles/ holds the summary and the command).
+MEASURED_TRAFFIC = {
+    "config2 q4 decode T=1": (17_090_560, "profiles/k_decode_q4_T1.md"),
+    "config3 q8 prefill T=2048": (577_900_000, "profiles/k_pre_gemm_q8_T2048.md"),
+}
+
+
 def prefill_flops(T, H=2048, I=512, E=256, k=8, shared=True):
     """Algorithmic FLOPs of one block call on T tokens: (routed GEMMs, all)."""
     gemm = 2.0 * T * (k + (1 if shared else 0)) * 3 * I * H
@@ -386,11 +394,13 @@ def run_prefill_bench(args, cfg):
                      "frac": (achieved / peak) if achieved else None,
                      "peak_source": f"{src} bf16 {'sustained' if sustained else 'burst'}",
                      "frac_of_burst": (achieved / bf16_burst) if achieved and bf16_burst else None,
-                     "traffic": None, "algorithmic_flops_per_step": gemm_flops,
+                     "traffic": MEASURED_TRAFFIC.get(f"config{args.config} q{bits} prefill T={T}", (None,))[0],
+                     "traffic_source": MEASURED_TRAFFIC.get(f"config{args.config} q{bits} prefill T={T}", (None, None))[1],
+                     "algorithmic_flops_per_step": gemm_flops,
                      "kernel": "k_pre_gemm (gate/up + down launches)", "gemm_ms_per_step": gemm_ms,
                      "block_tflops": all_flops / (ms_step * 1e-3) / 1e12},
         "stages_ms_per_step": {k: v / max(ncalls, 1) for k, v in stages.items()},
-        "gpu_launches": 6 * K,
+        "gpu_launches": 8 * K,  # route, sort, scatter, gather, gate/up, row scale, down, final
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -570,7 +580,11 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm * world, "unit": "GB/s",
                      "frac": achieved / (hbm * world), "peak_source": f"{src} x {world} GPU",
                      "frac_of_nominal_8tbs": achieved / (HBM_NOMINAL_GBS * world),
-                     "traffic": None, "algorithmic_bytes_per_step": per_step,
+                     "traffic": MEASURED_TRAFFIC.get(f"config{args.config} q{bits} decode T={T}", (None,))[0]
+                     if world == 1 else None,
+                     "traffic_source": MEASURED_TRAFFIC.get(f"config{args.config} q{bits} decode T={T}", (None, None))[1]
+                     if world == 1 else None,
+                     "algorithmic_bytes_per_step": per_step,
                      "distinct_experts_per_step": distinct,
                      "kernel": "k_decode (persistent, one launch per step)" if persistent
                      else "k_route+k_gateup+k_down chain" + (" + k_ep_reduce" if world > 1 else "")},
