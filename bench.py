@@ -180,6 +180,46 @@ def run_reference(args, cfg=None):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_stack(args, cfg, n_layers=4):
+    """The CPU path (oracle) on the stack workload: each step is one token
+    through n_layers seeded q4 layers, scaled to the configuration's layers."""
+    from oracle import oracle
+    from runnel_b200 import inputs, stack
+    from runnel_b200.quant import f32_to_bf16_bits
+
+    bits, L = args.bits, args.layers or cfg["layers"]
+    blks = [inputs.make_block(bits, seed=args.seed * 1000 + l, T=1) for l in range(n_layers)]
+    ws = [oracle.BlockWeights(bits=bits, group=64, **b.weight_fields()) for b in blks]
+    nw = [f32_to_bf16_bits(b.norm_w) for b in blks] + [f32_to_bf16_bits(blks[-1].norm_w)]
+    x = blks[0].x
+
+    def token(x):
+        xa, xn = stack.reference_add_rmsnorm(x, None, nw[0])
+        for l in range(n_layers):
+            y, _, _ = oracle.moe_block(ws[l], xn, k=8)
+            xa, xn = stack.reference_add_rmsnorm(xa, f32_to_bf16_bits(y), nw[l + 1])
+        return xa
+
+    for _ in range(args.warmup):
+        x = token(x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        x = token(x)
+    el = time.perf_counter() - t0
+    us_tok = el / args.steps * 1e6 * L / n_layers
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference", "metric": "moe_stack_decode_us_per_token", "value": us_tok, "unit": "us/token",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": us_tok * 1e-3,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config4 {L} q{bits} layers, batch-1 sequential decode", "bits": bits, "layers": L},
+        "cpu_baseline": {"value": us_tok, "unit": "us/token", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} tokens through {n_layers} layers, scaled by {L}/{n_layers}"},
+        "e2e": {"value": us_tok, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference_prefill(args, cfg, sample_T=16):
     """The CPU path (oracle) on the prefill workload: each step is the first
     sample_T tokens of that step's batch, alternating over the step kinds."""
@@ -412,6 +452,191 @@ def run_prefill_bench(args, cfg):
         dist.destroy_process_group()
 
 
+def run_stack_bench(args, cfg):
+    """Configuration 4: a stack of L distinct q4 MoE blocks with residual adds
+    and RMSNorms, batch-1 decode of sequential tokens (each token's input is
+    the previous token's output).  One token's layers are one CUDA graph that
+    also copies its output back to its input; a step is one replay (one token
+    through all layers).  N > 1: expert parallel, every layer sharded."""
+    import torch
+
+    from runnel_b200 import ops, stack
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    from runnel_b200 import ep as epm
+    from runnel_b200.inputs import make_tokens
+
+    bits, L = args.bits, args.layers or cfg["layers"]
+    E_range = epm.plan(rank, world)[:2] if world > 1 else None
+    layers, norms = stack.synthetic_layers(L, bits, args.seed, dev, E_range=E_range)
+    ctx = epm.ExpertParallel(rank, world) if world > 1 else None
+    ws = ops.Workspace(dev)
+    st = stack.LayerStack(layers, norms, ep=ctx, ws=ws)
+    x0 = torch.from_numpy(make_tokens(args.seed, 1)).view(torch.int16).view(torch.bfloat16).to(dev)
+    xin, xout = x0.clone(), torch.empty_like(x0)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        st.forward(xin, out=xout)  # workspace allocation outside the capture
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            st.forward(xin, out=xout)
+            xin.copy_(xout)
+    # routing of every layer for the roofline's bytes (one eager pass on token 0)
+    rec = []
+    with torch.cuda.stream(stream):
+        xin.copy_(x0)
+        st.forward(xin, out=xout, record=rec)
+    stream.synchronize()
+    rws = ops.Workspace(dev)
+    distinct = []
+    for l, (_, xn, _) in enumerate(rec):
+        inds = ops.router_topk(layers[l], xn, ws=rws)[0]
+        distinct.append(len(np.unique(inds.cpu().numpy())))
+    per_tok = sum(step_bytes(bits, d, 1) for d in distinct)
+    K, W = args.steps, args.warmup
+    with torch.cuda.stream(stream):
+        xin.copy_(x0)
+        for _ in range(W):
+            g.replay()
+    stream.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    # sustained replays so the clock sampler sees the GPU under this load (the
+    # count is the same on every rank: expert-parallel layers pair up)
+    t0 = time.time()
+    with torch.cuda.stream(stream):
+        g.replay()
+    stream.synchronize()
+    n_soak = max(1, int(args.soak / max(time.time() - t0, 1e-4)))
+    if dist:
+        t = torch.tensor([n_soak], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        n_soak = int(t.item())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(n_soak):
+            g.replay()
+        ev0.record(stream)
+        for _ in range(K):
+            g.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us_tok = ms * 1e3 / K
+    # end to end: each token's input copied in from pinned host memory and its
+    # output read back, every step
+    xh = x0.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(K):
+            xin.copy_(xh, non_blocking=True)
+            g.replay()
+            oh.copy_(xout, non_blocking=True)
+            xh, oh = oh, xh
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    assert ws.status() == 0, "device status reported a timeout or a bad index"
+    hbm, _, src = peaks()
+    achieved = per_tok / (us_tok * 1e-6) / 1e9
+    line = {
+        "metric": "moe_stack_decode_us_per_token", "value": us_tok, "unit": "us/token",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": us_tok * 1e-3,
+        "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic (seeded torch generator on the device, inputs.py distributions)",
+        "config": {"workload": f"config4 {L} q{bits} layers, batch-1 sequential decode", "bits": bits,
+                   "layers": L, "tokens_per_step": 1, "H": 2048, "I": 512, "E": 256, "top_k": 8,
+                   "l2": f"inputs larger than L2: {L} layers of weights per step",
+                   "parallelism": f"ep{world}" if world > 1 else "single"},
+        "e2e": {"value": e2e_ms * 1e3 / K, "unit": "us/token", "h2d_bytes_per_step": 2048 * 2,
+                "d2h_bytes_per_step": 2048 * 2},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm * world, "unit": "GB/s",
+                     "frac": achieved / (hbm * world), "peak_source": f"{src} x {world} GPU",
+                     "traffic": None, "algorithmic_bytes_per_step": per_tok,
+                     "kernel": "k_decode + k_add_rmsnorm per layer"},
+        "gpu_launches": K * (2 * L + 1),
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline_stack(layers, norms, bits, x0, budget_s=args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        del g
+        dist.barrier()
+        if ctx is not None:
+            ctx.close()
+        dist.destroy_process_group()
+
+
+def cpu_baseline_stack(layers, norms, bits, x0, n_layers=4, budget_s=10.0):
+    """CPU oracle on a bounded sample: one token through the first n_layers
+    layers (same weights, copied to the host), repeated; scaled to all layers."""
+    import torch
+
+    from oracle import oracle
+    from runnel_b200 import stack
+    from runnel_b200.quant import f32_to_bf16_bits
+
+    def u16(t):
+        return t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    def u32(t):
+        return t.cpu().contiguous().view(torch.int32).numpy().view(np.uint32)
+
+    ws = []
+    for bt in layers[:n_layers]:
+        ws.append(oracle.BlockWeights(bits=bits, group=64, router_w=u16(bt.router_w), shared_gate_w=u16(bt.shared_gate_w),
+                                      gu_w=u32(bt.gu_w), gu_s=u16(bt.gu_s), gu_b=u16(bt.gu_b), dn_w=u32(bt.dn_w),
+                                      dn_s=u16(bt.dn_s), dn_b=u16(bt.dn_b), sgu_w=u32(bt.sgu_w), sgu_s=u16(bt.sgu_s),
+                                      sgu_b=u16(bt.sgu_b), sdn_w=u32(bt.sdn_w), sdn_s=u16(bt.sdn_s),
+                                      sdn_b=u16(bt.sdn_b)))
+    nw = [u16(w) for w in norms[:n_layers + 1]]
+    x = u16(x0)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        xa, xn = stack.reference_add_rmsnorm(x, None, nw[0])
+        for l in range(n_layers):
+            y, _, _ = oracle.moe_block(ws[l], xn, k=8)
+            xa, xn = stack.reference_add_rmsnorm(xa, f32_to_bf16_bits(y), nw[l + 1])
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    L = len(layers)
+    return {"value": el / n * 1e6 * L / n_layers, "unit": "us/token", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{n} tokens through the first {n_layers} of {L} layers (CPU oracle, C + OpenMP fp32), "
+                      f"scaled by {L}/{n_layers}"}
+
+
 def run_ours(args):
     import torch
 
@@ -612,6 +837,7 @@ def main():
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--bits", type=int, default=None)
     ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=None, help="configuration 4: number of layers (default 40)")
     ap.add_argument("--seed", type=int, default=None)
     ap.add_argument("--soak", type=float, default=1.5)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
@@ -625,6 +851,14 @@ def main():
     args.seed = cfg["seed"] if args.seed is None else args.seed
     args.warmup = max(args.warmup, 3)
     prefill = cfg.get("T", 1) > 64
+    if "layers" in cfg and not args.profile:
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                run_reference_stack(args, cfg)
+            return
+        if "--steps" not in sys.argv:
+            args.steps = cfg.get("steps", 64)
+        return run_stack_bench(args, cfg)
     if args.impl == "reference":
         run_reference(args, cfg) if prefill else run_reference(args)
     elif args.profile:

@@ -82,6 +82,16 @@ def _rank_main(rank, world, port):
         assert ws.status() == 0
         out_n = ep.moe_block_nccl(shard, x[:8], rank, ws=ws)
         assert_close(out_n.float().cpu().numpy(), _ref(blk, 8)[0], f"ep nccl rank {rank}")
+        # a two-layer stack, expert parallel, against the same stack on one GPU
+        from runnel_b200 import stack
+        lo, hi, _ = ep.plan(rank, world)
+        full_l, norms = stack.synthetic_layers(2, BITS, seed=3, device=dev)
+        shard_l, _ = stack.synthetic_layers(2, BITS, seed=3, device=dev, E_range=(lo, hi))
+        one = stack.LayerStack(full_l, norms, ws=ops.Workspace(dev)).forward(x[:1])
+        dist.barrier(group=gloo)
+        par = stack.LayerStack(shard_l, norms, ep=ctx, ws=ws).forward(x[:1])
+        assert_close(par.float().cpu().numpy(), one.float().cpu().numpy(), f"ep stack rank {rank}")
+        assert ws.status() == 0
         torch.cuda.synchronize()
         dist.barrier()
     finally:
