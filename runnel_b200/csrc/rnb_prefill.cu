@@ -649,10 +649,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pre_gemm(Params p, const __
         const uint32_t e_id = valid ? ent[h] : 0u;
         const size_t row = static_cast<size_t>(row0 + h * kTileM + r);
         if (MODE == 0) {
-          // up in columns [0, 64), gate in [64, 128): 64 SwiGLU channels nt*64..
+          // up in columns [0, 64), gate in [64, 128): 64 SwiGLU channels nt*64..,
+          // computed once into registers, then scaled into fp16 and stored
           const uint32_t t = e_id / (K + 1);
           const float xinv = valid ? 1.0f / __ldcg(p.ws.xscale + t) : 1.f;
+          float hv[64];
           float mx = 0.f;
+#pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
             uint32_t u[16], gt[16];
             tmem_ld16(tl + cc * 16, u);
@@ -661,30 +664,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pre_gemm(Params p, const __
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
               const float up = __uint_as_float(u[q]) * xinv, ga = __uint_as_float(gt[q]) * xinv;
-              mx = fmaxf(mx, fabsf((ga / (1.0f + expf(-ga))) * up));
+              // silu(g) = g / (1 + e^-g); the clamp keeps the denominator finite
+              const float hq = __fdividef(ga, 1.0f + __expf(fminf(-ga, 80.0f))) * up;
+              hv[cc * 16 + q] = hq;
+              mx = fmaxf(mx, fabsf(hq));
             }
           }
           float hs, hi;
           fp16_range_scale(mx, hs, hi);
-          __half* dst = p.ws.h16 + row * I + nt * 64;
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t u[16], gt[16];
-            tmem_ld16(tl + cc * 16, u);
-            tmem_ld16(tl + 64 + cc * 16, gt);
-            tmem_wait_ld();
-            uint32_t hv[8];
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(p.ws.h16 + row * I + nt * 64);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float up0 = __uint_as_float(u[2 * q]) * xinv, ga0 = __uint_as_float(gt[2 * q]) * xinv;
-              const float up1 = __uint_as_float(u[2 * q + 1]) * xinv, ga1 = __uint_as_float(gt[2 * q + 1]) * xinv;
-              hv[q] = half2_bits((ga0 / (1.0f + expf(-ga0))) * up0 * hs, (ga1 / (1.0f + expf(-ga1))) * up1 * hs);
-            }
-            if (valid) {
-              reinterpret_cast<uint4*>(dst + cc * 16)[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-              reinterpret_cast<uint4*>(dst + cc * 16)[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
-            }
+            for (int c8 = 0; c8 < 8; ++c8)
+              dst[c8] = make_uint4(half2_bits(hv[c8 * 8] * hs, hv[c8 * 8 + 1] * hs),
+                                   half2_bits(hv[c8 * 8 + 2] * hs, hv[c8 * 8 + 3] * hs),
+                                   half2_bits(hv[c8 * 8 + 4] * hs, hv[c8 * 8 + 5] * hs),
+                                   half2_bits(hv[c8 * 8 + 6] * hs, hv[c8 * 8 + 7] * hs));
+            p.ws.hinv[row * (I / 64) + nt] = hi;
           }
-          if (valid) p.ws.hinv[row * (I / 64) + nt] = hi;
         } else {
           const uint32_t t = e_id / (K + 1), slot = e_id % (K + 1);
           float w = 0.f;
@@ -694,17 +691,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pre_gemm(Params p, const __
             w *= __ldcg(p.ws.hrow + row);
           }
           float* dst = p.ws.acc + static_cast<size_t>(t) * H + nt * C::N;
-          for (int cc = 0; cc < C::N / 16; ++cc) {
-            uint32_t v[16];
-            tmem_ld16(tl + cc * 16, v);
+          for (int cc = 0; cc < C::N / 16; cc += 2) {
+            uint32_t v[2][16];
+            tmem_ld16(tl + cc * 16, v[0]);
+            tmem_ld16(tl + (cc + 1) * 16, v[1]);
             tmem_wait_ld();
             if (valid) {
 #pragma unroll
-              for (int q = 0; q < 16; q += 4)
-                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + cc * 16 + q),
-                             "f"(__uint_as_float(v[q]) * w), "f"(__uint_as_float(v[q + 1]) * w),
-                             "f"(__uint_as_float(v[q + 2]) * w), "f"(__uint_as_float(v[q + 3]) * w)
-                             : "memory");
+              for (int b2 = 0; b2 < 2; ++b2)
+#pragma unroll
+                for (int q = 0; q < 16; q += 4)
+                  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + (cc + b2) * 16 + q),
+                               "f"(__uint_as_float(v[b2][q]) * w), "f"(__uint_as_float(v[b2][q + 1]) * w),
+                               "f"(__uint_as_float(v[b2][q + 2]) * w), "f"(__uint_as_float(v[b2][q + 3]) * w)
+                               : "memory");
             }
           }
         }
