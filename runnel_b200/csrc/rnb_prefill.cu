@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
     xn2[tid] = 0.f;
   }
   auto stage = [&](int kc, int buf) {
-    // 64 rows x 128 bf16 = 1024 16-byte pieces, two per thread
+    // kRouteT rows x 128 bf16 = 16-byte pieces, one per thread
     for (int q = tid; q < kRouteT * 16; q += blockDim.x) {
       const int r = q >> 4, piece = q & 15;
       const int tr = r < nt ? r : 0;
@@ -168,6 +168,8 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
   };
+  static_assert(kRouteT * 16 == 512, "one 16-byte piece of one token per thread and chunk");
+  float xm_acc = 0.f, xs_acc = 0.f;
   constexpr int kNC = kRouteT / 8;  // 8-token MMA column blocks
   float acc[kNC][4];
 #pragma unroll
@@ -197,20 +199,17 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
     }
     __syncthreads();
     const int buf = kc & 1;
-    // per-token max |x| over this chunk
-    for (int q = tid; q < kRouteT * 16; q += blockDim.x) {
-      const int r = q >> 4, piece = q & 15;
-      const uint4 v = *reinterpret_cast<const uint4*>(&xs[buf][r][piece * 8]);
+    // per-token max |x| and sum of squares: thread tid always sees 16-byte
+    // piece tid % 16 of token tid / 16, so it accumulates in registers
+    {
+      const uint4 v = *reinterpret_cast<const uint4*>(&xs[buf][tid >> 4][(tid & 15) * 8]);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-      float m = 0.f, s2 = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xFFFF0000u);
-        m = fmaxf(m, fmaxf(fabsf(lo), fabsf(hi)));
-        s2 = fmaf(lo, lo, fmaf(hi, hi, s2));
+        xm_acc = fmaxf(xm_acc, fmaxf(fabsf(lo), fabsf(hi)));
+        xs_acc = fmaf(lo, lo, fmaf(hi, hi, xs_acc));
       }
-      atomicMax(&xmax[r], __float_as_uint(m));
-      atomicAdd(&xn2[r], s2);
     }
     if (warp * 16 < Et) {
       // this chunk's router rows were loaded during the previous chunk; start the next
@@ -247,6 +246,16 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
     }
     __syncthreads();
   }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    xm_acc = fmaxf(xm_acc, __shfl_xor_sync(0xffffffffu, xm_acc, o));
+    xs_acc += __shfl_xor_sync(0xffffffffu, xs_acc, o);
+  }
+  if ((tid & 15) == 0) {
+    xmax[tid >> 4] = __float_as_uint(xm_acc);
+    xn2[tid >> 4] = xs_acc;
+  }
+  __syncthreads();
   // fp16 copy of the tokens times their power-of-two scale (gate/up A operand)
   {
     __shared__ float xsc[kRouteT];
@@ -433,7 +442,11 @@ struct GemmCfg {
   static constexpr int kStage = kA + kB + kRaw + 2 * kScl;
   static constexpr uint32_t kTx = kA + kRaw + 2 * kScl;  // TMA bytes per stage
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr size_t kSmem = static_cast<size_t>(S) * kStage + 1024;
+  // down epilogue: per epilogue warp a 32 x 32 fp32 tile (rows padded to 36
+  // floats) to turn row-per-lane results into row-contiguous atomics
+  static constexpr int kTpPitch = 36;
+  static constexpr int kTp = 4 * 32 * kTpPitch * 4;
+  static constexpr size_t kSmem = static_cast<size_t>(S) * kStage + kTp + 1024;
   static_assert(kStage % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
 };
 
@@ -690,21 +703,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pre_gemm(Params p, const __
                                                 : __ldcg(p.ws.sg + t);
             w *= __ldcg(p.ws.hrow + row);
           }
-          float* dst = p.ws.acc + static_cast<size_t>(t) * H + nt * C::N;
+          // Lane = row: each row belongs to another token.  Stage 32 columns
+          // of the warp's 32 rows in shared memory, then let 8 lanes cover one
+          // row's 128 contiguous bytes, so an atomic instruction touches 4 rows
+          // instead of 32.
+          float* tp = reinterpret_cast<float*>(sm + C::S * C::kStage) + quad * 32 * C::kTpPitch;
           for (int cc = 0; cc < C::N / 16; cc += 2) {
             uint32_t v[2][16];
             tmem_ld16(tl + cc * 16, v[0]);
             tmem_ld16(tl + (cc + 1) * 16, v[1]);
             tmem_wait_ld();
-            if (valid) {
+            __syncwarp();  // the previous chunk's reads are done
 #pragma unroll
-              for (int b2 = 0; b2 < 2; ++b2)
+            for (int q = 0; q < 8; ++q) {
+              const uint32_t* vq = v[q >> 2] + (q & 3) * 4;
+              *reinterpret_cast<float4*>(tp + lane * C::kTpPitch + q * 4) =
+                  make_float4(__uint_as_float(vq[0]) * w, __uint_as_float(vq[1]) * w, __uint_as_float(vq[2]) * w,
+                              __uint_as_float(vq[3]) * w);
+            }
+            __syncwarp();
 #pragma unroll
-                for (int q = 0; q < 16; q += 4)
-                  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + (cc + b2) * 16 + q),
-                               "f"(__uint_as_float(v[b2][q]) * w), "f"(__uint_as_float(v[b2][q + 1]) * w),
-                               "f"(__uint_as_float(v[b2][q + 2]) * w), "f"(__uint_as_float(v[b2][q + 3]) * w)
-                               : "memory");
+            for (int i = 0; i < 8; ++i) {
+              const int rr = (lane >> 3) + 4 * i, c4 = (lane & 7) * 4;
+              const uint32_t tr = __shfl_sync(0xffffffffu, t, rr);
+              const bool vr = __shfl_sync(0xffffffffu, valid ? 1 : 0, rr) != 0;
+              const float4 q4 = *reinterpret_cast<const float4*>(tp + rr * C::kTpPitch + c4);
+              if (vr)
+                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                                 p.ws.acc + static_cast<size_t>(tr) * H + nt * C::N + cc * 16 + c4),
+                             "f"(q4.x), "f"(q4.y), "f"(q4.z), "f"(q4.w)
+                             : "memory");
             }
           }
         }
