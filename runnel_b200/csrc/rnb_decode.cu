@@ -1244,7 +1244,6 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   uint32_t* bar1 = p.ws.ctr + 1 + p.H / 16;
   uint32_t* bar2 = bar1 + 1;
   uint32_t* exitc = bar1 + 2;
-  const bool owns_router = cta < pl.n_rtiles;
   const bool owns_sgu = p.has_shared && cta >= pl.n_rtiles && cta < pl.n_rtiles + n_ch &&
                         ((p.shared_qmask >> (((cta - pl.n_rtiles) * 8) / 128)) & 1u);
   const int n_sch = p.has_shared ? __popc(p.shared_qmask & ((1u << nq) - 1u)) * 16 : 0;  // shared gate/up tasks
@@ -1256,17 +1255,15 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
 
   RNB_TRACE_MARK(p, 0);
   // ---- phase A: requests that need no routing
-  uint4 ra[4][2];
-  if (owns_router) {
-    const uint16_t* pa = router_row(p, cta * 16 + g);
-    const uint16_t* pb = router_row(p, cta * 16 + g + 8);
-    const uint4 z = make_uint4(0, 0, 0, 0);
+  // Router rows of this CTA: cta and cta + NC of the E_total + 1 rows (the
+  // last is the shared-expert gate); warp w covers hidden [128 w, 128 w + 128),
+  // 4 values per lane.  The rows are read before the programmatic-launch wait.
+  const int k0r = warp * 128 + lane * 4;
+  uint2 wr[2];
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      const int k0 = warp * 128 + ch * 32 + 8 * c;
-      ra[ch][0] = pa ? ld_stream_v4(pa + k0) : z;
-      ra[ch][1] = pb ? ld_stream_v4(pb + k0) : z;
-    }
+  for (int i = 0; i < 2; ++i) {
+    const uint16_t* pr = router_row(p, cta + i * NC);
+    wr[i] = pr ? __ldg(reinterpret_cast<const uint2*>(pr + k0r)) : make_uint2(0, 0);
   }
   if (owns_sgu) {
     const int ch0 = (cta - pl.n_rtiles) * 8;
@@ -1280,34 +1277,82 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   cp_async_commit();  // group: shared down
   RNB_TRACE_MARK(p, 1);
   griddep_wait();  // x may come from the previous kernel on the stream
-  if (owns_router) {
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    RouterNorms rn;
+  {
+    // Per lane 4 products per (row, token), summed with FMAs, then a 5-level
+    // shuffle tree and a 4-level tree over the warps: at most 12 roundings of
+    // partial sums bounded by sum |x_i w_i|, well inside the 2^-18 allowance
+    // of the rounding certificate (rnb_route.cuh).
+    float* q = ms->rnorm[warp];  // [0,4): dots (row i, token t) at 2i+t; [4,6) sum w^2; [6,8) sum |w|; [8,10) sum x^2; [10,12) max |x|
+    float xf[2][4];
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      const int k0 = warp * 128 + ch * 32 + 8 * c;
-      const uint4 bx = g < T ? __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(g) * p.H + k0)) : z;
-      mma_bf16(d, ra[ch][0].x, ra[ch][1].x, ra[ch][0].y, ra[ch][1].y, bx.x, bx.y);
-      mma_bf16(d, ra[ch][0].z, ra[ch][1].z, ra[ch][0].w, ra[ch][1].w, bx.z, bx.w);
-      rn.add(bx, ra[ch][0], ra[ch][1]);
+    for (int t = 0; t < 2; ++t) {
+      const uint2 xv = t < T ? __ldg(reinterpret_cast<const uint2*>(p.x + static_cast<size_t>(t) * p.H + k0r))
+                             : make_uint2(0, 0);
+      xf[t][0] = __uint_as_float(xv.x << 16);
+      xf[t][1] = __uint_as_float(xv.x & 0xFFFF0000u);
+      xf[t][2] = __uint_as_float(xv.y << 16);
+      xf[t][3] = __uint_as_float(xv.y & 0xFFFF0000u);
     }
-    rn.reduce_quad();
-    if (c == 0) rn.store(ms->rnorm[warp], g);
-    float* rw = sRed + warp * 128;
-    rw[g * 8 + 2 * c] = d[0];
-    rw[g * 8 + 2 * c + 1] = d[1];
-    rw[(g + 8) * 8 + 2 * c] = d[2];
-    rw[(g + 8) * 8 + 2 * c + 1] = d[3];
-    __syncthreads();
-    if (tid < 128) {
-      const int r = tid & 15, n = tid >> 4, row = cta * 16 + r;
-      if (row <= Et && n < T) {
-        float acc = 0.f;
+    float v[12];
 #pragma unroll
-        for (int w = 0; w < kPWarps; ++w) acc += sRed[w * 128 + r * 8 + n];
-        reinterpret_cast<uint32_t*>(p.ws.logit)[static_cast<size_t>(n) * (Et + 1) + row] =
-            row < Et ? router_interval_from(&ms->rnorm[0][0], kPWarps, r, n, acc) : __float_as_uint(acc);
+    for (int i = 0; i < 2; ++i) {
+      const float wf[4] = {__uint_as_float(wr[i].x << 16), __uint_as_float(wr[i].x & 0xFFFF0000u),
+                           __uint_as_float(wr[i].y << 16), __uint_as_float(wr[i].y & 0xFFFF0000u)};
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        float d = wf[0] * xf[t][0];
+        d = fmaf(wf[1], xf[t][1], d);
+        d = fmaf(wf[2], xf[t][2], d);
+        d = fmaf(wf[3], xf[t][3], d);
+        v[2 * i + t] = d;
+      }
+      v[4 + i] = fmaf(wf[0], wf[0], fmaf(wf[1], wf[1], fmaf(wf[2], wf[2], wf[3] * wf[3])));
+      v[6 + i] = (fabsf(wf[0]) + fabsf(wf[1])) + (fabsf(wf[2]) + fabsf(wf[3]));
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      v[8 + t] = fmaf(xf[t][0], xf[t][0], fmaf(xf[t][1], xf[t][1], fmaf(xf[t][2], xf[t][2], xf[t][3] * xf[t][3])));
+      v[10 + t] = fmaxf(fmaxf(fabsf(xf[t][0]), fabsf(xf[t][1])), fmaxf(fabsf(xf[t][2]), fabsf(xf[t][3])));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < 12; ++j) {
+        const float u = __shfl_xor_sync(0xffffffffu, v[j], o);
+        v[j] = j >= 10 ? fmaxf(v[j], u) : v[j] + u;
+      }
+    if (lane < 12) {
+      float mine = v[0];
+#pragma unroll
+      for (int j = 1; j < 12; ++j) mine = lane == j ? v[j] : mine;
+      q[lane] = mine;
+    }
+    __syncthreads();
+    if (tid < 4) {
+      const int i = tid >> 1, t = tid & 1, row = cta + i * NC;
+      if (row <= Et && t < T) {
+        float a[5][16];
+#pragma unroll
+        for (int w = 0; w < kPWarps; ++w) {
+          const float* qw = ms->rnorm[w];
+          a[0][w] = qw[2 * i + t];
+          a[1][w] = qw[4 + i];
+          a[2][w] = qw[6 + i];
+          a[3][w] = qw[8 + t];
+          a[4][w] = qw[10 + t];
+        }
+#pragma unroll
+        for (int st = 8; st > 0; st >>= 1)
+#pragma unroll
+          for (int w = 0; w < st; ++w) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) a[j][w] += a[j][w + st];
+            a[4][w] = fmaxf(a[4][w], a[4][w + st]);
+          }
+        // expert rows: candidate interval of the bf16 logit; last row: fp32 shared-gate logit
+        reinterpret_cast<uint32_t*>(p.ws.logit)[static_cast<size_t>(t) * (Et + 1) + row] =
+            row < Et ? route_interval(a[0][0], a[3][0], a[4][0], a[1][0], a[2][0], kRouteRelDecode)
+                     : __float_as_uint(a[0][0]);
       }
     }
     __syncthreads();
@@ -1331,7 +1376,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   RNB_TRACE_MARK(p, 3);
 
   // ---- routing (every CTA, redundantly)
-  cta_wait_count(bar1, static_cast<uint32_t>(pl.n_rtiles), p.ws.status);
+  cta_wait_count(bar1, static_cast<uint32_t>(NC), p.ws.status);
   RNB_TRACE_MARK(p, 5);
   for (int q = tid; q < T * (Et + 1); q += blockDim.x)
     reinterpret_cast<uint32_t*>(sH)[q] = __ldcg(reinterpret_cast<const uint32_t*>(p.ws.logit) + q);
@@ -1826,6 +1871,7 @@ bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem
     return false;
   pl.n_rtiles = (p.E_total + 1 + 15) / 16;
   if (di.sms < p.H / 16 || di.sms < pl.n_rtiles + p.I / 8) return false;
+  if (2 * di.sms < p.E_total + 1) return false;  // each CTA computes at most two router rows
   using TL = Tile2<BITS>;
   const int T = p.T, G = p.H / kGroup, nq = p.I / 128;
   const int n_ctask = nq * (1 + (p.T * p.k < p.E ? p.T * p.k : p.E));
