@@ -336,19 +336,36 @@ def run_prefill_bench(args, cfg):
 
     bits, T = args.bits, cfg["T"]
     blocks, routing = prefill_blocks(cfg, bits, args.seed)
-    base = ops.BlockTensors.from_numpy(blocks[0], dev)
+    a2a = world > 1 and args.prefill_par == "a2a"
+    E_range = None
+    if a2a:
+        from runnel_b200 import ep as epm
+        E_range = epm.plan(rank, world)[:2]
+    base = ops.BlockTensors.from_numpy(blocks[0], dev, E_range=E_range)
     kinds = [base]
     for b in blocks[1:]:  # same expert weights, the step kind's router
         rw = torch.from_numpy(b.router_w).view(torch.int16).view(torch.bfloat16).to(dev)
         kinds.append(ops.BlockTensors(**{**base.__dict__, "router_w": rw}))
-    xs = [torch.from_numpy(b.x).view(torch.int16).view(torch.bfloat16).to(dev) for b in blocks]
+    # every rank has its own tokens (the batch rotated by a rank-dependent offset)
+    xs = [torch.roll(torch.from_numpy(b.x).view(torch.int16).view(torch.bfloat16).to(dev), 997 * rank, 0)
+          for b in blocks]
     out = torch.empty_like(xs[0])
     ws = ops.Workspace(dev)
     stream = torch.cuda.Stream(dev)
     nk = len(kinds)
+    moved = {"sent": 0, "received": 0}
+
+    def block(i, x, o):
+        if a2a:
+            st = {}
+            o.copy_(epm.moe_block_a2a(kinds[i % nk], x, rank, world, ws=ws, stats=st))
+            moved["sent"] += st["sent"]
+            moved["received"] += st["received"]
+        else:
+            ops.moe_block(kinds[i % nk], x, ws=ws, out=o)
 
     def step(i):
-        ops.moe_block(kinds[i % nk], xs[i % nk], ws=ws, out=out)
+        block(i, xs[i % nk], out)
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
@@ -358,15 +375,28 @@ def run_prefill_bench(args, cfg):
     K = args.steps
     sampler = ClockSampler(local)
     sampler.start()
-    t_end = time.time() + args.soak
+    # a calibrated, rank-uniform number of soak rounds (all-to-all steps are collective)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
-        while time.time() < t_end:
+        c0.record(stream)
+        for i in range(4):
+            step(i)
+        c1.record(stream)
+    torch.cuda.synchronize()
+    round_ms = torch.tensor([c0.elapsed_time(c1)], device=dev)
+    if dist:
+        dist.all_reduce(round_ms, op=dist.ReduceOp.MAX)
+    n_soak = int(min(2000, max(1, args.soak * 1e3 / max(float(round_ms.item()), 1e-3))))
+    with torch.cuda.stream(stream):
+        for r in range(n_soak):
             for i in range(4):
                 step(i)
-            stream.synchronize()
+            if r % 8 == 7:
+                stream.synchronize()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
+    moved.update(sent=0, received=0)
     _lib.stage_timing(True)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -378,6 +408,7 @@ def run_prefill_bench(args, cfg):
     _lib.stage_timing(False)
     stages, ncalls = _lib.stage_times()
     clocks = sampler.stop()
+    moved_timed = dict(moved)
     ms = ev0.elapsed_time(ev1)
     if dist:
         t = torch.tensor([ms], device=dev)
@@ -395,7 +426,7 @@ def run_prefill_bench(args, cfg):
     with torch.cuda.stream(stream):
         for i in range(3):
             xd.copy_(xh[i % nk], non_blocking=True)
-            ops.moe_block(kinds[i % nk], xd, ws=ws, out=od)
+            block(i, xd, od)
             oh.copy_(od, non_blocking=True)
     stream.synchronize()
     Ke = max(4, min(K, 64))
@@ -404,11 +435,16 @@ def run_prefill_bench(args, cfg):
         e0.record(stream)
         for i in range(Ke):
             xd.copy_(xh[i % nk], non_blocking=True)
-            ops.moe_block(kinds[i % nk], xd, ws=ws, out=od)
+            block(i, xd, od)
             oh.copy_(od, non_blocking=True)
         e1.record(stream)
     torch.cuda.synchronize()
-    e2e_tok_s = T * Ke * world / (e0.elapsed_time(e1) * 1e-3)
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_tok_s = T * Ke * world / (e2e_ms * 1e-3)
 
     gemm_flops, all_flops = prefill_flops(T)
     _, bf16_burst, src = peaks()
@@ -417,7 +453,7 @@ def run_prefill_bench(args, cfg):
     if os.path.exists(pth):
         sustained = json.load(open(pth)).get("bf16_tflops_sustained")
     peak = sustained or bf16_burst
-    gemm_ms = (stages.get("gateup", 0.0) + stages.get("down", 0.0)) / max(ncalls, 1)
+    gemm_ms = (stages.get("gateup", 0.0) + stages.get("down", 0.0)) / K
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
     line = {
         "metric": "moe_block_prefill_tokens_per_s", "value": tok_s, "unit": "tokens/s",
@@ -427,7 +463,10 @@ def run_prefill_bench(args, cfg):
         "config": {"workload": f"config{args.config} q{bits} prefill T={T}", "bits": bits,
                    "tokens_per_step": T, "routing": routing, "H": 2048, "I": 512, "E": 256, "top_k": 8,
                    "l2": "inputs larger than L2: every step reads the whole expert bank (>= 0.8 GB)",
-                   "parallelism": "replica" if world > 1 else "single"},
+                   "tokens_per_step_per_gpu": T,
+                   "parallelism": ((f"ep{world} all-to-all ({256 // world} experts/GPU, NCCL all_to_all_single "
+                                    "dispatch/combine, shared expert on every rank for its own tokens)")
+                                   if a2a else "replica") if world > 1 else "single"},
         "e2e": {"value": e2e_tok_s, "unit": "tokens/s", "h2d_bytes_per_step": T * 2048 * 2,
                 "d2h_bytes_per_step": T * 2048 * 2},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -439,10 +478,16 @@ def run_prefill_bench(args, cfg):
                      "algorithmic_flops_per_step": gemm_flops,
                      "kernel": "k_pre_gemm (gate/up + down launches)", "gemm_ms_per_step": gemm_ms,
                      "block_tflops": all_flops / (ms_step * 1e-3) / 1e12},
-        "stages_ms_per_step": {k: v / max(ncalls, 1) for k, v in stages.items()},
-        "gpu_launches": 8 * K,  # route, sort, scatter, gather, gate/up, row scale, down, final
+        "stages_ms_per_step": {k: v / K for k, v in stages.items()},
+        # route, sort, scatter, gather, gate/up, row scale, down, final (twice per step with all-to-all)
+        "gpu_launches": 8 * K * (2 if a2a else 1),
         "clocks": clocks,
     }
+    if a2a:
+        mv = moved_timed
+        line["a2a_rows_per_step"] = {"sent": mv["sent"] / K, "received": mv["received"] / K,
+                                     "bytes_out": mv["sent"] / K * (2048 * 2 + 64),
+                                     "bytes_back": mv["sent"] / K * 2048 * 4, "rank": rank}
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline_prefill(blocks, bits, budget_s=args.cpu_budget)
     if rank == 0:
@@ -842,6 +887,8 @@ def main():
     ap.add_argument("--soak", type=float, default=1.5)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--prefill-par", default="a2a", choices=["a2a", "replica"],
+                    help="prefill at N > 1: expert parallel with all-to-all, or whole-bank replicas")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu captures (2 weight copies, plain launches)")
     args = ap.parse_args()

@@ -159,6 +159,19 @@ RNB_API int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void
  * Synchronises the stream. */
 RNB_API int rnb_moe_status(void* ws, size_t ws_bytes, uint32_t* status, void* stream);
 
+/* Routed experts with given routing (the receive side of an expert-parallel
+ * all-to-all; no reference counterpart).  T rows x, each with k global
+ * expert ids inds[t][j] and weights scores[t][j]:
+ *   out[t] = sum over j with inds[t][j] in this descriptor's shard of
+ *            scores[t][j] * expert_{inds[t][j]}(x[t])
+ * (bf16 out, or fp32 with RNB_FLAG_Y_F32).  No router and no shared expert;
+ * ids >= E_total are skipped and set RNB_STATUS_BAD_INDEX.  Runs the grouped
+ * GEMM pipeline for any T; its workspace size comes from
+ * rnb_moe_experts_workspace_size. */
+RNB_API int rnb_moe_experts_workspace_size(const rnb_moe_desc* d, size_t* bytes);
+RNB_API int rnb_moe_experts_fwd(const rnb_moe_desc* d, const void* x, const uint32_t* inds, const float* scores,
+                                void* out, void* ws, size_t ws_bytes, void* stream);
+
 /* ---- Expert parallelism (one process per GPU, ranks on one node) ----
  * Reference counterpart: none in waylake/runnel (single Apple GPU); this is
  * the rnb_ep_* surface of the B200 build.  Rank r holds experts

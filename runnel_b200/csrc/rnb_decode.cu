@@ -2110,6 +2110,30 @@ int rnb_router_topk(const rnb_moe_desc* d, const void* x, uint32_t* inds, float*
   });
 }
 
+int rnb_moe_experts_workspace_size(const rnb_moe_desc* d, size_t* bytes) {
+  using namespace rnb;
+  if (!bytes) return fail(RNB_ERR_INVALID, "bytes must be non-NULL");
+  int rc = validate(d, false, false);
+  if (rc) return rc;
+  if (!prefill_supported(*d)) return fail(RNB_ERR_INVALID, "rnb_moe_experts_fwd does not support these shapes");
+  *bytes = prefill_workspace_bytes(*d);
+  return RNB_OK;
+}
+
+int rnb_moe_experts_fwd(const rnb_moe_desc* d, const void* x, const uint32_t* inds, const float* scores, void* out,
+                        void* ws, size_t ws_bytes, void* stream) {
+  using namespace rnb;
+  int rc = validate(d, false, true);
+  if (!rc) rc = check_device();
+  if (rc) return rc;
+  if (!x || !inds || !scores || !out || !ws) return fail(RNB_ERR_INVALID, "x, inds, scores, out and ws must be non-NULL");
+  if (!aligned16(x) || !aligned16(out) || !aligned16(ws)) return fail(RNB_ERR_ALIGN, "x, out and ws must be 16-byte aligned");
+  if (!prefill_supported(*d)) return fail(RNB_ERR_INVALID, "rnb_moe_experts_fwd does not support these shapes");
+  if (ws_bytes < prefill_workspace_bytes(*d)) return fail(RNB_ERR_WORKSPACE, "workspace too small (rnb_moe_experts_workspace_size)");
+  if (d->T == 0) return RNB_OK;
+  return run_prefill(d, x, out, nullptr, nullptr, ws, ws_bytes, static_cast<cudaStream_t>(stream), inds, scores);
+}
+
 int rnb_switchglu_fwd(const rnb_moe_desc* d, const void* x, const uint32_t* inds, void* y, void* ws,
                       size_t ws_bytes, void* stream) {
   int rc = validate(d, false, true);

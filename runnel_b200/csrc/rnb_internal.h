@@ -37,7 +37,9 @@ void stage_end(cudaStream_t st, int stage);
 // whether it supports the descriptor's shapes.
 size_t prefill_workspace_bytes(const rnb_moe_desc& d);
 bool prefill_supported(const rnb_moe_desc& d);
+// inds_in / scores_in ([T][k]): given routing (no router, no shared expert).
 int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out, float* scores_out,
-                void* ws, size_t ws_bytes, cudaStream_t st);
+                void* ws, size_t ws_bytes, cudaStream_t st, const uint32_t* inds_in = nullptr,
+                const float* scores_in = nullptr);
 
 }  // namespace rnb

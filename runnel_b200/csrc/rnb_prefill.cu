@@ -82,6 +82,9 @@ struct Params {
   void* out;  // bf16 [T][H], or fp32 with y_f32
   uint32_t* inds_out;
   float* scores_out;
+  // given routing (rnb_moe_experts_fwd): [T][k] global expert ids and weights
+  const uint32_t* inds_in;
+  const float* scores_in;
   Ws ws;
 };
 
@@ -349,6 +352,53 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
     if (hist[e]) atomicAdd(&p.ws.counts[e], hist[e]);
 }
 
+// Given routing (no router): a warp per token copies its k expert ids and
+// weights, computes the power-of-two fp16 scale and the fp16 token copy, and
+// counts local experts.  Ids outside [0, E_total) are skipped and flagged.
+__global__ void __launch_bounds__(512) k_pre_given(Params p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * 16 + warp;
+  if (t >= p.T) return;
+  const int K = p.k, H = p.H;
+  if (lane < K) {
+    const uint32_t e = __ldg(p.inds_in + static_cast<size_t>(t) * K + lane);
+    const float w = __ldg(p.scores_in + static_cast<size_t>(t) * K + lane);
+    const bool bad = e >= static_cast<uint32_t>(p.E_total);
+    if (bad) atomicOr(p.ws.status, RNB_STATUS_BAD_INDEX);
+    const uint32_t eo = bad ? 0xFFFFFFFFu : e;
+    p.ws.inds[static_cast<size_t>(t) * K + lane] = eo;
+    p.ws.scores[static_cast<size_t>(t) * K + lane] = w;
+    const int le = static_cast<int>(eo) - p.off;
+    if (!bad && le >= 0 && le < p.E) atomicAdd(&p.ws.counts[le], 1u);
+  }
+  const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * H);
+  float m = 0.f;
+  for (int q = lane; q < H / 8; q += 32) {
+    const uint4 v = __ldg(xr + q);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[j] << 16)), fabsf(__uint_as_float(w[j] & 0xFFFF0000u))));
+  }
+  m = warp_max(m);
+  float sc, inv;
+  fp16_range_scale(m, sc, inv);
+  if (lane == 0) {
+    p.ws.xscale[t] = sc;
+    p.ws.sg[t] = 0.f;
+  }
+  uint4* xo = reinterpret_cast<uint4*>(p.ws.x16 + static_cast<size_t>(t) * H);
+  for (int q = lane; q < H / 8; q += 32) {
+    const uint4 v = __ldg(xr + q);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      o[j] = half2_bits(__uint_as_float(w[j] << 16) * sc, __uint_as_float(w[j] & 0xFFFF0000u) * sc);
+    xo[q] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // ------------------------------------------------------ sort / scatter
 
 __global__ void __launch_bounds__(512) k_pre_sort(Params p) {
@@ -402,6 +452,7 @@ __global__ void k_pre_scatter(Params p) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     if (i < n_routed) {
+      if (p.ws.inds[i] == 0xFFFFFFFFu) continue;
       const int le = static_cast<int>(p.ws.inds[i]) - p.off;
       if (le < 0 || le >= p.E) continue;
       const uint32_t pos = p.ws.base[le] + atomicAdd(&p.ws.fill[le], 1u);
@@ -957,7 +1008,10 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
     if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill smem attribute: ") + cudaGetErrorString(e));
     attr = true;
   }
-  k_pre_route<<<(p.T + kRouteT - 1) / kRouteT, 512, kRouteSmem, st>>>(p);
+  if (p.inds_in)
+    k_pre_given<<<(p.T + 15) / 16, 512, 0, st>>>(p);
+  else
+    k_pre_route<<<(p.T + kRouteT - 1) / kRouteT, 512, kRouteSmem, st>>>(p);
   stage_end(st, RNB_STAGE_ROUTE);
   k_pre_sort<<<1, 512, 0, st>>>(p);
   stage_end(st, RNB_STAGE_SORT);
@@ -979,7 +1033,7 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
 }
 
 int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out, float* scores_out, void* ws,
-                size_t ws_bytes, cudaStream_t st) {
+                size_t ws_bytes, cudaStream_t st, const uint32_t* inds_in, const float* scores_in) {
   using namespace pre;
   const Layout L = make_layout(*d);
   if (ws_bytes < L.total) return fail(RNB_ERR_WORKSPACE, "workspace too small for the prefill path");
@@ -992,7 +1046,9 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
   p.E_total = d->E_total;
   p.off = d->expert_offset;
   p.k = d->k;
-  p.has_shared = has_shared(d) ? 1 : 0;
+  p.has_shared = (has_shared(d) && !inds_in) ? 1 : 0;
+  p.inds_in = inds_in;
+  p.scores_in = scores_in;
   p.rows_cap = L.rows_cap;
   p.max_mt = L.max_mt;
   p.x = static_cast<const uint16_t*>(x);

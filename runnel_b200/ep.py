@@ -20,6 +20,14 @@ Two reductions are offered:
 * ``"nccl"``: the block with ``RNB_FLAG_Y_F32`` (fp32 partial, shared expert
   on rank 0 only) followed by ``torch.distributed.all_reduce`` -- the
   library-collective baseline, any T.
+
+For throughput (every rank with its own tokens, e.g. a 16384-token prefill
+chunk per GPU) :func:`moe_block_a2a` dispatches instead of replicating: each
+rank routes its tokens, runs its local experts and the whole shared expert on
+them, sends every token once to each other rank that holds one of its
+selected experts (with its full routing row), and the owners send back fp32
+partial sums (``rnb_moe_experts_fwd`` on the received rows), which are added
+to the home partial.
 """
 from __future__ import annotations
 
@@ -132,3 +140,71 @@ def moe_block_nccl(bt: BlockTensors, x: torch.Tensor, rank: int, group=None, k: 
         part = partial_fn(shard, x)
     dist.all_reduce(part, op=dist.ReduceOp.SUM, group=group)
     return part.to(torch.bfloat16)
+
+
+def _a2a_rows(t: torch.Tensor, send: list[int], recv: list[int], group) -> torch.Tensor:
+    import torch.distributed as dist
+
+    out = t.new_empty((sum(recv),) + tuple(t.shape[1:]))
+    dist.all_to_all_single(out, t.contiguous(), output_split_sizes=recv, input_split_sizes=send, group=group)
+    return out
+
+
+def moe_block_a2a(bt: BlockTensors, x: torch.Tensor, rank: int, world: int, group=None, k: int = 8,
+                  ws: Workspace | None = None, block_fn=None, experts_fn=None, stats: dict | None = None):
+    """Expert-parallel block over this rank's own tokens with all-to-all
+    dispatch and combine.  ``bt`` is this rank's expert shard (experts
+    ``[rank*E, (rank+1)*E)`` of ``E_total``, router and shared expert whole).
+
+    1. home: ``moe_block`` with fp32 output -> router, this rank's selected
+       experts and the whole shared expert for every local token;
+    2. dispatch: token t goes once to each other rank owning one of its k
+       experts, as one int32 row (bf16 x, k ids, k fp32 weights);
+    3. remote: ``rnb_moe_experts_fwd`` sums the receiving shard's experts
+       of each row (fp32);
+    4. combine: the fp32 rows go back and are added to the home partial,
+       which is rounded to bf16 once.
+
+    ``block_fn(bt, x) -> (fp32 out, inds, scores)`` and
+    ``experts_fn(bt, x, inds, scores) -> fp32`` replace the device calls
+    (host tests).  ``stats`` (a dict) receives the rows sent and received."""
+    import torch.distributed as dist
+
+    from .ops import experts_fwd, moe_block
+
+    xt = _tokens(x, bt.H)
+    T, H = xt.shape
+    Et = bt.E_total if bt.E_total is not None else bt.E
+    per = bt.E
+    if per * world != Et or bt.expert_offset != rank * per:
+        raise ValueError(f"shard [{bt.expert_offset}, +{per}) is not rank {rank}'s of {Et} experts over {world}")
+    f32 = BlockTensors(**{**bt.__dict__, "flags": bt.flags | _lib.FLAG_Y_F32})
+    if block_fn is None:
+        part, inds, scores = moe_block(f32, xt, k=k, ws=ws, return_routing=True)
+    else:
+        part, inds, scores = block_fn(f32, xt)
+    # (destination rank, token) pairs, sorted by rank then token; home excluded
+    dest = torch.zeros((T, world), dtype=torch.bool, device=xt.device)
+    dest.scatter_(1, (inds.long() // per).clamp_(0, world - 1), True)
+    dest[:, rank] = False
+    d_idx, t_idx = dest.t().nonzero(as_tuple=True)
+    send_n = torch.bincount(d_idx, minlength=world)
+    recv_n = torch.empty_like(send_n)
+    dist.all_to_all_single(recv_n, send_n, group=group)
+    send, recv = send_n.tolist(), recv_n.tolist()
+    if stats is not None:
+        stats.update(sent=sum(send), received=sum(recv))
+    hw = H // 2
+    rows = torch.cat([xt.view(torch.int32)[t_idx], inds.to(torch.int32)[t_idx],
+                      scores.view(torch.int32)[t_idx]], dim=1)
+    got = _a2a_rows(rows, send, recv, group)
+    rx = got[:, :hw].contiguous().view(torch.bfloat16)
+    ri = got[:, hw:hw + k].contiguous()
+    rs = got[:, hw + k:].contiguous().view(torch.float32)
+    if experts_fn is None:
+        y = experts_fwd(bt, rx, ri, rs) if rx.shape[0] else rx.new_zeros((0, H), dtype=torch.float32)
+    else:
+        y = experts_fn(bt, rx, ri, rs)
+    back = _a2a_rows(y, recv, send, group)
+    part.index_add_(0, t_idx, back)
+    return part.to(torch.bfloat16).reshape(x.shape)

@@ -210,6 +210,29 @@ def moe_block(bt: BlockTensors, x: torch.Tensor, k: int = 8, ws: Workspace | Non
     return out
 
 
+def experts_fwd(bt: BlockTensors, x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor,
+                out_f32: bool = True, ws: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed experts of this shard with given routing: [T, H] bf16 rows,
+    [T, k] int32 global expert ids and fp32 weights -> [T, H] weighted sum over
+    the ids this shard holds (fp32 by default).  No router, no shared expert."""
+    xt = _tokens(x, bt.H)
+    T, k = inds.shape
+    flags = (bt.flags | _lib.FLAG_Y_F32) if out_f32 else (bt.flags & ~_lib.FLAG_Y_F32)
+    d = BlockTensors(**{**bt.__dict__, "flags": flags}).desc(T, k)
+    out = torch.empty(xt.shape, dtype=torch.float32 if out_f32 else torch.bfloat16, device=xt.device)
+    if T == 0:
+        return out
+    need = ctypes.c_size_t()
+    _lib.call("rnb_moe_experts_workspace_size", ctypes.byref(d), ctypes.byref(need))
+    if ws is None or ws.numel() < need.value:
+        ws = torch.zeros(need.value, dtype=torch.uint8, device=xt.device)
+    inds = inds.to(torch.int32).contiguous()
+    scores = scores.to(torch.float32).contiguous()
+    _lib.call("rnb_moe_experts_fwd", ctypes.byref(d), _ptr(xt), _ptr(inds), _ptr(scores), _ptr(out),
+              ws.data_ptr(), ws.numel(), _stream())
+    return out
+
+
 def router_topk(bt: BlockTensors, x: torch.Tensor, k: int = 8, ws: Workspace | None = None,
                 return_logits: bool = False):
     """(inds int32 [T,k], scores fp32 [T,k][, bf16-rounded logits fp32 [T,E_total]])."""

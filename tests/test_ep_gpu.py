@@ -92,6 +92,21 @@ def _rank_main(rank, world, port):
         par = stack.LayerStack(shard_l, norms, ep=ctx, ws=ws).forward(x[:1])
         assert_close(par.float().cpu().numpy(), one.float().cpu().numpy(), f"ep stack rank {rank}")
         assert ws.status() == 0
+        # all-to-all dispatch/combine over each rank's own tokens against the
+        # whole bank on one GPU (prefill-size, decode-size, ragged and empty)
+        full = ops.BlockTensors.from_numpy(blk, dev)
+        g = torch.Generator(device=dev)
+        for i, (t0, t1) in enumerate(((300, 77), (5, 64), (0, 130))):
+            g.manual_seed(100 * i + rank)
+            xr = torch.randn(((t0, t1)[rank], blk.H), device=dev, generator=g).to(torch.bfloat16)
+            dist.barrier(group=gloo)
+            stats = {}
+            got = ep.moe_block_a2a(shard, xr, rank, world, ws=ws, stats=stats)
+            want, winds, _ = ops.moe_block(full, xr, ws=ws, return_routing=True)
+            if xr.shape[0]:
+                assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(), f"ep a2a rank {rank} case {i}")
+            assert stats["sent"] <= xr.shape[0] * (world - 1)
+        assert ws.status() == 0
         torch.cuda.synchronize()
         dist.barrier()
     finally:

@@ -131,3 +131,60 @@ def test_two_rank_reduction_over_gloo():
     import torch.multiprocessing as mp
 
     mp.spawn(_rank_main, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _a2a_rank_main(rank, world, port):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        blk = inputs.make_block(BITS, seed=SEED, T=2 * world)
+        w = _weights(blk)
+        mine = blk.x[rank * 2:(rank + 1) * 2]  # every rank has its own tokens
+        if rank == world - 1:
+            mine = mine[:1]  # ragged
+        lo, hi, _ = ep.plan(rank, world)
+        shard = ops.BlockTensors.from_numpy(blk, "cpu", E_range=(lo, hi))
+        seen = {}
+
+        def block_fn(bt, x):
+            assert bt.flags & _lib.FLAG_Y_F32 and (bt.expert_offset, bt.E) == (lo, hi - lo)
+            xb = x.view(torch.int16).numpy().view(np.uint16)
+            _, inds, scores, _ = oracle.router(w, xb, k=8)
+            p = partial_block(blk, xb, lo, hi, 0, full_shared=True)
+            return torch.from_numpy(p), torch.from_numpy(inds.astype(np.int32)), torch.from_numpy(scores)
+
+        def experts_fn(bt, x, inds, scores):
+            seen["rows"] = x.shape[0]
+            if x.shape[0] == 0:
+                return torch.zeros((0, bt.H), dtype=torch.float32)
+            xb = x.view(torch.int16).numpy().view(np.uint16)
+            ind = inds.numpy()
+            # a received row always holds at least one of this shard's experts
+            assert (((ind >= lo) & (ind < hi)).any(axis=1)).all()
+            y = oracle.switchglu(w, xb, ind.astype(np.uint32))
+            local = (ind >= lo) & (ind < hi)
+            return torch.from_numpy(np.einsum("tk,tkh->th", np.where(local, scores.numpy(), 0.0)
+                                              .astype(np.float32), y).astype(np.float32))
+
+        x = torch.from_numpy(mine).view(torch.int16).view(torch.bfloat16)
+        stats = {}
+        out = ep.moe_block_a2a(shard, x, rank, world, block_fn=block_fn, experts_fn=experts_fn, stats=stats)
+        ref, _, _ = oracle.moe_block(w, mine, k=8)
+        err = np.abs(out.float().numpy() - ref).max() / np.abs(ref).max()
+        assert err < 1e-2, err
+        assert stats["received"] == seen["rows"]
+        tot = torch.tensor([stats["sent"], stats["received"]])
+        dist.all_reduce(tot)
+        assert tot[0] == tot[1]  # every row sent is received once
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_all_to_all_dispatch_combine_over_gloo(world):
+    import torch.multiprocessing as mp
+
+    mp.spawn(_a2a_rank_main, args=(world, _free_port()), nprocs=world, join=True)

@@ -81,3 +81,36 @@ def test_decode_after_prefill_on_one_workspace():
         fresh = ops.moe_block(tensors, xs, ws=ops.Workspace("cuda"))
         assert shared.status() == 0
         assert_close(got.float().cpu().numpy(), fresh.float().cpu().numpy(), "shared workspace")
+
+
+def test_experts_fwd_given_routing_matches_oracle():
+    """rnb_moe_experts_fwd (the receive side of all-to-all expert parallelism):
+    given ids and weights, the shard's experts only, no router or shared expert."""
+    blk = inputs.make_block(4, seed=1, T=70)
+    w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
+    _, inds, scores, _ = oracle.router(w, blk.x, k=8)
+    y = oracle.switchglu(w, blk.x, inds)
+    x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
+    ti = torch.from_numpy(inds.astype(np.int32)).cuda()
+    ts = torch.from_numpy(scores).cuda()
+    for lo, hi in ((0, 256), (64, 128)):
+        bt = ops.BlockTensors.from_numpy(blk, "cuda", E_range=(lo, hi))
+        local = (inds >= lo) & (inds < hi)
+        ref = np.einsum("tk,tkh->th", np.where(local, scores, 0.0).astype(np.float32), y)
+        for T in (70, 3):
+            out = ops.experts_fwd(bt, x[:T], ti[:T], ts[:T])
+            assert out.dtype == torch.float32
+            assert_close(out.cpu().numpy(), ref[:T], f"experts_fwd [{lo},{hi}) T={T}")
+    out16 = ops.experts_fwd(bt, x, ti, ts, out_f32=False)
+    assert out16.dtype == torch.bfloat16
+    assert_close(out16.float().cpu().numpy(), ref, "experts_fwd bf16")
+    # an id outside [0, E_total) is skipped and flagged
+    bad = ti.clone()
+    bad[0, 0] = 999
+    ws = torch.zeros(1 << 26, dtype=torch.uint8, device="cuda")
+    out = ops.experts_fwd(bt, x[:2], bad[:2], ts[:2], ws=ws)
+    st = int(ws[:4].view(torch.int32).item())
+    assert st & _lib.STATUS_BAD_INDEX
+    keep = np.where(local[:2], scores[:2], 0.0)
+    keep[0, 0] = 0.0
+    assert_close(out.cpu().numpy(), np.einsum("tk,tkh->th", keep.astype(np.float32), y[:2]), "experts_fwd bad id")
