@@ -100,11 +100,11 @@ __device__ __forceinline__ void trace_mark(const Params& p, int i) {
   if (threadIdx.x == 0) {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 16 + i] = t;
+    reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 32 + i] = t;
   }
 }
 __device__ __forceinline__ void trace_value(const Params& p, int i, int v) {
-  reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 16 + i] = static_cast<uint64_t>(v);
+  reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 32 + i] = static_cast<uint64_t>(v);
 }
 #define RNB_TRACE_MARK(p, i) trace_mark(p, i)
 #else
@@ -1034,6 +1034,7 @@ __device__ void xprep_cta(const uint16_t* x, int T, uint32_t* sX, float* sXs, fl
                           float* red) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int H = 2048, G = H / kGroup;
+#pragma unroll 1
   for (int t = 0; t < T; ++t) {
     const uint2 u = __ldg(reinterpret_cast<const uint2*>(x + static_cast<size_t>(t) * H) + tid);
     const float v[4] = {__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
@@ -1489,17 +1490,21 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   }
   cp_async_commit();  // group: routed down
 
+#pragma unroll 1
   for (int r0 = 0; r0 < mine; r0 += pl.db) {
     const int nr = mine - r0 < pl.db ? mine - r0 : pl.db;
     cp_async_wait_pending(r0 == 0 ? 1 : 0);  // the routed-down group may stay in flight
     __syncwarp();
+    if (r0 == 0) RNB_TRACE_MARK(p, 16);
     if (tid < nr) {
       const int i = cta + (r0 + tid) * NC, a = i / n_ch;
       ms->tasks[tid] = PTask{ms->act_ent[a], static_cast<int>(ms->act_cnt[a]), (i % n_ch) * 8};
     }
     __syncthreads();
+#pragma unroll 1
     for (int k2 = 0; k2 < nr; ++k2)
       p_gateup_mma<BITS>(p, sBR + ((r0 + k2) % pl.db) * task_bytes, sX, sXs, sRed + k2 * kPWarps * 128, ms->tasks[k2]);
+    if (r0 == 0) RNB_TRACE_MARK(p, 17);
     __syncthreads();
     p_gateup_epilogue(p, sRed, ms->tasks, nr, ms->xinv);
     __syncthreads();
@@ -1527,6 +1532,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     for (int q0 = warp; q0 < n_ctask; q0 += kPWarps * pl.cb) {
       uint32_t ent_b[4];
       int nb = 0;
+#pragma unroll 1
       for (int bq = 0; bq < pl.cb; ++bq) {
         const int q = q0 + bq * kPWarps;
         if (q >= n_ctask) break;
@@ -1561,6 +1567,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
       cp_async_commit();
       cp_async_wait_pending(0);
       __syncwarp();
+      if (q0 == warp) RNB_TRACE_MARK(p, 19);
+#pragma unroll 1
       for (int bq = 0; bq < nb; ++bq) {
         const int q = q0 + bq * kPWarps;
         const bool shared = q < c_base;
@@ -1571,6 +1579,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
         const float* hq = hw + bq * T * per_col;
         const float* mq = hq + T * 128;
         float cmax = 0.f;  // lane col: max |h| of column col
+#pragma unroll 1
         for (int col = 0; col < ncols; ++col) {
           float m = 0.f;
           for (int j = lane; j < nt_i; j += 32) m = fmaxf(m, mq[col * nt_i + j]);
@@ -1588,6 +1597,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
           const int pb = BITS == 8 ? 16 * cq : 16 * ((cq == 1) ? 2 : (cq == 2) ? 1 : cq);
           uint32_t* frag = reinterpret_cast<uint32_t*>(const_cast<float*>(hq));
           float* gsb = const_cast<float*>(mq);
+#pragma unroll 1
           for (int col = 0; col < ncols; ++col) {
             const float sc = __shfl_sync(0xffffffffu, hs_l, col);
             const float* src = hq + col * 128 + cg * kGroup + pb;
@@ -1618,6 +1628,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
           }
           __syncwarp();
         }
+        if (q0 == warp && bq == 0) RNB_TRACE_MARK(p, 20);
         const int colB = g < ncols ? g : 0;
         const int cl0 = 2 * c < ncols ? 2 * c : 0, cl1 = 2 * c + 1 < ncols ? 2 * c + 1 : 0;
         const uint32_t* fr = reinterpret_cast<const uint32_t*>(hq) + colB * 128;
@@ -1634,6 +1645,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
         };
         auto gsum = [&](int gi, int col) { return mq[(col ? cl1 : cl0) * nt_i + gi]; };
         tile2_mma<BITS, true>(sCR + q * TL::kBytes, g, c, bfrag, gsum, acc);
+        if (q0 == warp && bq == 0) RNB_TRACE_MARK(p, 21);
         const float inv0 = __shfl_sync(0xffffffffu, hi_l, 2 * c);
         const float inv1 = __shfl_sync(0xffffffffu, hi_l, 2 * c + 1);
         const uint32_t id0 = __shfl_sync(0xffffffffu, ent_l, 2 * c);
@@ -1650,7 +1662,9 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
         }
       }
     }
+    RNB_TRACE_MARK(p, 22);
     __syncthreads();
+    RNB_TRACE_MARK(p, 23);
     // each source's quarters summed in place (quarter 0 slot), then the
     // ordered weighted sum per (token, row)
     const int nsrc = K + (p.has_shared ? 1 : 0);

@@ -178,6 +178,7 @@ __device__ __forceinline__ uint32_t warp_select_k(const uint32_t (&keys)[8], int
     best = max(best, k2[i]);
   }
   mine = 0;
+#pragma unroll 1
   for (int slot = 0; slot < K; ++slot) {
     w = __reduce_max_sync(0xffffffffu, best);
     if (lane == slot) mine = w;
@@ -204,6 +205,29 @@ __device__ __forceinline__ uint32_t warp_select_k(const uint32_t (&keys)[8], int
 // and, if there were any, the selection runs again.  With exact_all every
 // uncertain logit is resolved and, if logits_row is non-null, all Et bf16
 // logits are written there as fp32.  Returns the number of logits resolved.
+// The uncertain candidates flagged in `need` (bit i: expert lane + 32 i) are
+// resolved in fp64 and the selection runs again.  Out of line and not
+// unrolled: it runs for a minority of tokens, and the common path stays
+// small (its instructions are fetched once per token by the decode kernel).
+static __device__ __noinline__ int route_resolve(uint32_t (&klo)[8], uint32_t need, int K, const uint16_t* xrow,
+                                                 const uint16_t* router_w, int H, int lane, uint32_t& mine) {
+  int n = 0;
+#pragma unroll 1
+  for (int i = 0; i < 8; ++i) {
+    uint32_t m = __ballot_sync(0xffffffffu, (need >> i) & 1u);
+    n += __popc(m);
+    while (m) {
+      const int src = __ffs(m) - 1;
+      m &= m - 1;
+      const int e = src + 32 * i;
+      const double d = warp_dot_f64(xrow, router_w + static_cast<size_t>(e) * H, H, lane);
+      if (lane == src) klo[i] = route_key(f64_to_bf16_bits(d), e);
+    }
+  }
+  if (n) warp_select_k(klo, K, lane, mine);
+  return n;
+}
+
 __device__ __forceinline__ int warp_route_token_body(const uint32_t* ivl, int Et, int K, const uint16_t* xrow,
                                                      const uint16_t* router_w, int H, int lane, bool exact_all,
                                                      float* logits_row, int* e_out, float* score_out) {
@@ -223,24 +247,13 @@ __device__ __forceinline__ int warp_route_token_body(const uint32_t* ivl, int Et
   }
   uint32_t mine;
   const uint32_t theta = warp_select_k(klo, K, lane, mine);  // the K-th largest lower key
-  int n_exact = 0;
-  if (__any_sync(0xffffffffu, vhi != 0)) {
+  // an expert whose upper key is below theta is beaten for certain by K others
+  uint32_t need = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      // an expert whose upper key is below theta is beaten for certain by K others
-      const bool need = ((vhi >> i) & 1u) && (exact_all || route_key(hib[i], lane + 32 * i) >= theta);
-      uint32_t m = __ballot_sync(0xffffffffu, need);
-      n_exact += __popc(m);
-      while (m) {
-        const int src = __ffs(m) - 1;
-        m &= m - 1;
-        const int e = src + 32 * i;
-        const double d = warp_dot_f64(xrow, router_w + static_cast<size_t>(e) * H, H, lane);
-        if (lane == src) klo[i] = route_key(f64_to_bf16_bits(d), e);
-      }
-    }
-    if (n_exact) warp_select_k(klo, K, lane, mine);
-  }
+  for (int i = 0; i < 8; ++i)
+    if (((vhi >> i) & 1u) && (exact_all || route_key(hib[i], lane + 32 * i) >= theta)) need |= 1u << i;
+  int n_exact = 0;
+  if (__any_sync(0xffffffffu, need != 0)) n_exact = route_resolve(klo, need, K, xrow, router_w, H, lane, mine);
   if (logits_row) {
 #pragma unroll
     for (int i = 0; i < 8; ++i)
