@@ -873,6 +873,91 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_probe(args):
+    """The reference's QMV / QMM probe CLIs on their default shapes
+    (quantized_qmv.cpp: 65536 x 2048; quantized_qmm.cpp: 64 tokens x 4096 x
+    2048), K-step timed with CUDA events over weight copies rotated so that
+    every step reads from HBM (4 copies > L2).  --impl reference times the
+    oracle's restatement of the probes' CPU reference on the host cores."""
+    import torch
+
+    from runnel_b200 import probes
+
+    bits = args.bits or 4
+    qmv = args.probe == "qmv"
+    rows, K, T = (65536, 2048, 1) if qmv else (4096, 2048, 64)
+    wbytes = rows * (K * bits // 8 + 2 * (K // 64) * 2)
+    workload = f"{args.probe} q{bits} " + (f"{rows}x{K}" if qmv else f"T={T} N={rows} K={K}")
+    if args.impl == "reference":
+        from oracle import oracle
+        data = (oracle.kat_qmv(bits, 4096, K=K) if qmv else oracle.kat_qmm(bits, T, 512, K))[0]
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < min(args.cpu_budget, 10.0):
+            if qmv:
+                oracle.kat_qmv(bits, 4096, K=K)
+            else:
+                oracle.kat_qmm(bits, T, 512, K)
+            n += 1
+        el = (time.perf_counter() - t0) / n
+        # the sample regenerates its data each call: the rate is a bound from below
+        frac = 4096 / rows if qmv else 512 / rows
+        value = wbytes * frac / el / 1e9
+        print(json.dumps({"metric": f"{args.probe}_weight_GBps", "value": value, "unit": "GB/s", "impl": "reference",
+                          "n_gpus": 1, "steps": n, "warmup": 0, "higher_is_better": True, "dtype": f"u{bits}",
+                          "config": {"workload": workload},
+                          "cpu_baseline": {"value": value, "unit": "GB/s", "cores": os.cpu_count() or 1,
+                                           "kind": "port", "sample": f"{n} oracle calls on {frac:.4f} of the rows "
+                                                                     "(data generation included)"},
+                          "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    copies = [probes.synthetic(bits, rows, K, tokens=T, seed=i) for i in range(4)]
+    ws = None
+    if not qmv:
+        import ctypes
+        from runnel_b200 import _lib
+        need = ctypes.c_size_t()
+        _lib.call("rnb_qmm_workspace_size", bits, 64, T, rows, K, ctypes.byref(need))
+        ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
+
+    def step(i):
+        w, s_, b_, x = copies[i % 4]
+        return probes.qmv(bits, w, s_, b_, x[0]) if qmv else probes.qmm(bits, w, s_, b_, x, ws=ws)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    K_ = args.steps
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_end = time.time() + args.soak  # clock samples under load
+    while time.time() < t_end:
+        for i in range(64):
+            step(i)
+        torch.cuda.synchronize()
+    ev0.record()
+    for i in range(K_):
+        step(i)
+    ev1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1) / K_
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    hbm, bf16_burst, src = peaks()
+    flops = 2.0 * T * rows * K
+    line = {"metric": f"{args.probe}_weight_GBps", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": K_,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": f"u{bits}", "data": "synthetic (seeded uniform codes, N(0,1) bf16 x)",
+            "config": {"workload": workload, "l2": "4 rotated weight copies (> L2)"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_source": src, "traffic": None, "kernel": "k_qmv" if qmv else "k_pre_gemm<1>",
+                         "tflops": flops / (ms * 1e-3) / 1e12},
+            "gpu_launches": K_ * (1 if qmv else 3), "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -891,7 +976,12 @@ def main():
                     help="prefill at N > 1: expert parallel with all-to-all, or whole-bank replicas")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu captures (2 weight copies, plain launches)")
+    ap.add_argument("--probe", default=None, choices=["qmv", "qmm"],
+                    help="time the standalone QMV / QMM probe instead of a configuration")
     args = ap.parse_args()
+    if args.probe:
+        args.steps = args.steps if "--steps" in sys.argv else 200
+        return run_probe(args) if int(os.environ.get("RANK", "0")) == 0 else None
     from runnel_b200.inputs import CONFIGS
     cfg = CONFIGS[args.config]
     args.bits = args.bits or cfg["bits"]

@@ -172,6 +172,31 @@ RNB_API int rnb_moe_experts_workspace_size(const rnb_moe_desc* d, size_t* bytes)
 RNB_API int rnb_moe_experts_fwd(const rnb_moe_desc* d, const void* x, const uint32_t* inds, const float* scores,
                                 void* out, void* ws, size_t ws_bytes, void* stream);
 
+/* ---- Standalone quantized matvec / matmul probes ----
+ * The reference's runnel-metal-qmv and runnel-metal-qmm CLIs
+ * (native/bench/quantized_qmv.cpp:186-270, quantized_qmm.cpp:112-145; kernels
+ * and CPU checks in native/src/quantized_qmv_probe.mm and
+ * quantized_qmm_probe.mm).  W is MLX affine: [rows][K*bits/32] uint32 codes,
+ * [rows][K/group] bf16 scales and biases; x is bf16.
+ *
+ * rnb_qmv: y[r] = W[row(r)] . x for r < rows (fp32).  Dense when selected is
+ * NULL: row(r) = r.  Expert mode (the gather QMV): selected is a HOST array of
+ * n_selected expert ids, rows = n_selected * rows_per_expert and
+ * row(r) = selected[r / rows_per_expert] * rows_per_expert + r % rows_per_expert
+ * within a bank of bank_rows rows.  K: multiple of 512 up to 16384; rows and
+ * rows_per_expert: multiples of 16. */
+#define RNB_QMV_MAX_EXPERTS 64
+RNB_API int rnb_qmv(int bits, int group, int64_t rows, int64_t K, const uint32_t* w, const uint16_t* scales,
+                    const uint16_t* biases, const void* x, const uint32_t* selected, int n_selected,
+                    int64_t rows_per_expert, int64_t bank_rows, float* y, void* stream);
+/* rnb_qmm: y[t][n] = W[n] . x[t] for t < T, n < N (bf16 out, fp32 with y_f32).
+ * N: multiple of 128; K: multiple of 512.  Workspace from
+ * rnb_qmm_workspace_size. */
+RNB_API int rnb_qmm_workspace_size(int bits, int group, int T, int N, int K, size_t* bytes);
+RNB_API int rnb_qmm(int bits, int group, int T, int N, int K, const uint32_t* w, const uint16_t* scales,
+                    const uint16_t* biases, const void* x, void* y, int y_f32, void* ws, size_t ws_bytes,
+                    void* stream);
+
 /* ---- Expert parallelism (one process per GPU, ranks on one node) ----
  * Reference counterpart: none in waylake/runnel (single Apple GPU); this is
  * the rnb_ep_* surface of the B200 build.  Rank r holds experts

@@ -64,6 +64,13 @@ SIGNATURES = {
     "rnb_moe_block_fwd_noalloc": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp]),
     "rnb_moe_experts_workspace_size": (ctypes.c_int, [_DescP, ctypes.POINTER(_sz)]),
     "rnb_moe_experts_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "rnb_qmv": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _vp, _vp, _vp, _vp,
+                               ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _vp,
+                               _vp]),
+    "rnb_qmm_workspace_size": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.POINTER(_sz)]),
+    "rnb_qmm": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp,
+                               _vp, _vp, ctypes.c_int, _vp, _sz, _vp]),
     "rnb_ep_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp), _vp]),
     "rnb_ep_connect": (ctypes.c_int, [_vp, _vp]),
     "rnb_ep_destroy": (ctypes.c_int, [_vp]),

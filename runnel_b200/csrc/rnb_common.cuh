@@ -122,6 +122,27 @@ __device__ __forceinline__ void q4_word_to_pairs(uint32_t w, uint32_t& p0, uint3
   p3 = hsub_1024(lop3_and_or(w >> 12, 0x000F000Fu, 0x64006400u));
 }
 
+// Subnormal form (no magic-number subtraction): a code placed in the low
+// mantissa bits of an fp16 with a zero exponent IS the fp16 subnormal
+// q * 2^-24, exactly, so one mask (4-bit) or one byte permute (8-bit) makes
+// two operands.  The tensor cores take fp16 subnormals at full precision, so
+// products with x stay exact in fp32 and a contraction's result is
+// 2^-24 * sum q x.  4-bit: pairs 1 and 3 of a word keep their nibbles at bits
+// 4-7 (value 16 q 2^-24); their activations are staged times 2^-4 instead.
+__device__ __forceinline__ void q8_word_to_pairs_sub(uint32_t w, uint32_t& p0, uint32_t& p1) {
+  p0 = __byte_perm(w, 0u, 0x4140);
+  p1 = __byte_perm(w, 0u, 0x4342);
+}
+
+__device__ __forceinline__ void q4_word_to_pairs_sub(uint32_t w, uint32_t& p0, uint32_t& p1, uint32_t& p2,
+                                                     uint32_t& p3) {
+  const uint32_t h = w >> 8;
+  p0 = w & 0x000F000Fu;
+  p1 = w & 0x00F000F0u;  // 16 x
+  p2 = h & 0x000F000Fu;
+  p3 = h & 0x00F000F0u;  // 16 x
+}
+
 // Position (within a 64-group) of the two halves of pair i held by lane c.
 template <int BITS>
 __host__ __device__ __forceinline__ int pair_pos(int c, int i, int half) {
@@ -175,6 +196,23 @@ __device__ __forceinline__ RowPairs q4_group_pairs(const uint2 v) {
   RowPairs r;
   q4_word_to_pairs(v.x, r.p[0], r.p[1], r.p[2], r.p[3]);
   q4_word_to_pairs(v.y, r.p[4], r.p[5], r.p[6], r.p[7]);
+  return r;
+}
+
+__device__ __forceinline__ RowPairs q8_group_pairs_sub(const uint4 v) {
+  RowPairs r;
+  q8_word_to_pairs_sub(v.x, r.p[0], r.p[1]);
+  q8_word_to_pairs_sub(v.y, r.p[2], r.p[3]);
+  q8_word_to_pairs_sub(v.z, r.p[4], r.p[5]);
+  q8_word_to_pairs_sub(v.w, r.p[6], r.p[7]);
+  return r;
+}
+
+// Pairs i with i & 1 set come out times 16 (see q4_word_to_pairs_sub).
+__device__ __forceinline__ RowPairs q4_group_pairs_sub(const uint2 v) {
+  RowPairs r;
+  q4_word_to_pairs_sub(v.x, r.p[0], r.p[1], r.p[2], r.p[3]);
+  q4_word_to_pairs_sub(v.y, r.p[4], r.p[5], r.p[6], r.p[7]);
   return r;
 }
 

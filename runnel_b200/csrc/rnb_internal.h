@@ -42,4 +42,12 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
                 void* ws, size_t ws_bytes, cudaStream_t st, const uint32_t* inds_in = nullptr,
                 const float* scores_in = nullptr);
 
+// RNB_ERR_DEVICE (with a message) unless the current device is an sm_100 part.
+int check_device();
+
+// Standalone quantized matmul through the prefill GEMM (rnb_prefill.cu).
+int qmm_workspace_bytes(int bits, int group, int T, int N, int K, size_t* bytes);
+int run_qmm(int bits, int T, int N, int K, const uint32_t* w, const uint16_t* s, const uint16_t* b, const void* x,
+            void* y, bool y_f32, void* ws, size_t ws_bytes, cudaStream_t st);
+
 }  // namespace rnb

@@ -399,6 +399,52 @@ __global__ void __launch_bounds__(512) k_pre_given(Params p) {
   }
 }
 
+// Standalone quantized matmul (rnb_qmm) through the down GEMM: one expert (the
+// whole W, H = N outputs, I = K), every token one row with weight 1.  A warp
+// per token: the fp16 row with a power-of-two scale (h16, hrow = its inverse)
+// and the row's entry; thread 0 of block 0 writes the 256-row item tiles.
+__global__ void __launch_bounds__(512) k_qmm_prep(Params p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const uint32_t n = static_cast<uint32_t>((p.T + kItemM - 1) / kItemM);
+    for (uint32_t j = 0; j < n; ++j) {
+      const uint32_t left = static_cast<uint32_t>(p.T) - j * kItemM;
+      p.ws.tiles[j] = make_uint4(0u, j * kItemM, left < static_cast<uint32_t>(kItemM) ? left : kItemM, 0u);
+    }
+    *p.ws.n_mt = n;
+  }
+  const int t = blockIdx.x * 16 + warp;
+  if (t >= p.T) return;
+  const int K = p.I;
+  const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * K);
+  float m = 0.f;
+  for (int q = lane; q < K / 8; q += 32) {
+    const uint4 v = __ldg(xr + q);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[j] << 16)), fabsf(__uint_as_float(w[j] & 0xFFFF0000u))));
+  }
+  m = warp_max(m);
+  float sc, inv;
+  fp16_range_scale(m, sc, inv);
+  uint4* ho = reinterpret_cast<uint4*>(p.ws.h16 + static_cast<size_t>(t) * K);
+  for (int q = lane; q < K / 8; q += 32) {
+    const uint4 v = __ldg(xr + q);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      o[j] = half2_bits(__uint_as_float(w[j] << 16) * sc, __uint_as_float(w[j] & 0xFFFF0000u) * sc);
+    ho[q] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (lane == 0) {
+    p.ws.hrow[t] = inv;
+    p.ws.perm[t] = static_cast<uint32_t>(t) * 2u;  // entry t * (k + 1) + 0 with k = 1
+    p.ws.scores[t] = 1.0f;
+  }
+}
+
 // ------------------------------------------------------ sort / scatter
 
 __global__ void __launch_bounds__(512) k_pre_sort(Params p) {
@@ -1089,6 +1135,94 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
   p.ws.hrow = reinterpret_cast<float*>(b + L.hrow);
   p.ws.acc = reinterpret_cast<float*>(b + L.acc);
   return d->bits == 8 ? launch_prefill<8>(p, L, st) : launch_prefill<4>(p, L, st);
+}
+
+// ---------------------------------------------------------------- QMM probe
+
+static rnb_moe_desc qmm_desc(int bits, int T, int N, int K) {
+  rnb_moe_desc d;
+  memset(&d, 0, sizeof(d));
+  d.T = T;
+  d.H = N;
+  d.I = K;
+  d.E = 1;
+  d.E_total = 1;
+  d.k = 1;
+  d.bits = bits;
+  d.group = 64;
+  return d;
+}
+
+int qmm_workspace_bytes(int bits, int group, int T, int N, int K, size_t* bytes) {
+  if (bits != 4 && bits != 8) return fail(RNB_ERR_INVALID, "bits must be 4 or 8");
+  if (group != 64) return fail(RNB_ERR_INVALID, "group size must be 64");
+  if (T < 0 || N <= 0 || N % 128 || K <= 0 || K % 512 || K > 16384)
+    return fail(RNB_ERR_INVALID, "qmm: T >= 0, N a multiple of 128, K a multiple of 512 up to 16384");
+  *bytes = pre::make_layout(qmm_desc(bits, T, N, K)).total;
+  return RNB_OK;
+}
+
+template <int BITS>
+static int launch_qmm(pre::Params& p, const pre::Layout& L, cudaStream_t st) {
+  using namespace pre;
+  using C = GemmCfg<BITS>;
+  TmaMaps tm;
+  if (!make_maps<BITS>(p, 1, L.rows_cap, tm)) return fail(RNB_ERR_CUDA, "qmm: tensor map encoding failed");
+  cudaError_t e = cudaFuncSetAttribute(k_pre_gemm<BITS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(C::kSmem));
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.perm, 0xFF, static_cast<size_t>(L.rows_cap) * 4, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.acc, 0, static_cast<size_t>(p.T) * p.H * 4, st);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("qmm setup: ") + cudaGetErrorString(e));
+  k_qmm_prep<<<(p.T + 15) / 16, 512, 0, st>>>(p);
+  const int nc = dev_info().sms;
+  k_pre_gemm<BITS, 1><<<nc, kGemmThreads, C::kSmem, st>>>(p, tm);
+  k_pre_final<<<nc * 4, 256, 0, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("qmm launch: ") + cudaGetErrorString(e));
+  return RNB_OK;
+}
+
+int run_qmm(int bits, int T, int N, int K, const uint32_t* w, const uint16_t* s, const uint16_t* b, const void* x,
+            void* y, bool y_f32, void* ws, size_t ws_bytes, cudaStream_t st) {
+  using namespace pre;
+  const rnb_moe_desc d = qmm_desc(bits, T, N, K);
+  const Layout L = make_layout(d);
+  if (ws_bytes < L.total) return fail(RNB_ERR_WORKSPACE, "workspace too small for qmm");
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.T = T;
+  p.H = N;
+  p.I = K;
+  p.E = 1;
+  p.E_total = 1;
+  p.k = 1;
+  p.rows_cap = L.rows_cap;
+  p.max_mt = L.max_mt;
+  p.x = static_cast<const uint16_t*>(x);
+  p.dn_w = w;
+  p.dn_s = s;
+  p.dn_b = b;
+  p.out = y;
+  p.y_f32 = y_f32 ? 1 : 0;
+  char* base = static_cast<char*>(ws);
+  p.ws.status = reinterpret_cast<uint32_t*>(base + L.status);
+  p.ws.counts = reinterpret_cast<uint32_t*>(base + L.counts);
+  p.ws.fill = reinterpret_cast<uint32_t*>(base + L.fill);
+  p.ws.base = reinterpret_cast<uint32_t*>(base + L.base);
+  p.ws.n_mt = reinterpret_cast<uint32_t*>(base + L.n_mt);
+  p.ws.tiles = reinterpret_cast<uint4*>(base + L.tiles);
+  p.ws.perm = reinterpret_cast<uint32_t*>(base + L.perm);
+  p.ws.inds = reinterpret_cast<uint32_t*>(base + L.inds);
+  p.ws.scores = reinterpret_cast<float*>(base + L.scores);
+  p.ws.sg = reinterpret_cast<float*>(base + L.sg);
+  p.ws.xscale = reinterpret_cast<float*>(base + L.xscale);
+  p.ws.x16 = reinterpret_cast<__half*>(base + L.x16);
+  p.ws.xs16 = reinterpret_cast<__half*>(base + L.xs16);
+  p.ws.h16 = reinterpret_cast<__half*>(base + L.h16);
+  p.ws.hinv = reinterpret_cast<float*>(base + L.hinv);
+  p.ws.hrow = reinterpret_cast<float*>(base + L.hrow);
+  p.ws.acc = reinterpret_cast<float*>(base + L.acc);
+  return bits == 8 ? launch_qmm<8>(p, L, st) : launch_qmm<4>(p, L, st);
 }
 
 }  // namespace rnb

@@ -78,3 +78,27 @@ def test_calls_without_device_fail_loudly():
     _lib.call("rnb_moe_workspace_size", ctypes.byref(d), ctypes.byref(n))
     rc = _lib.load().rnb_switchglu_fwd(ctypes.byref(d), 16, 16, 16, 16, n.value, None)
     assert rc != 0
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(K=100), "K must"),
+    (dict(bits=3), "bits"),
+    (dict(rows=20), "rows must"),
+    (dict(sel=[5], rpe=16, rows=16, bank=64), "outside the bank"),
+    (dict(sel=[0, 1], rpe=16, rows=16, bank=64), "expert mode"),
+])
+def test_qmv_rejects_bad_shapes(kw, msg):
+    sel = kw.get("sel")
+    arr = (ctypes.c_uint32 * len(sel))(*sel) if sel else None
+    fake = ctypes.c_void_p(1 << 20)  # never dereferenced: validation fails first
+    rc = _lib.load().rnb_qmv(kw.get("bits", 4), 64, kw.get("rows", 16), kw.get("K", 512), fake, fake, fake, fake,
+                             arr, len(sel) if sel else 0, kw.get("rpe", 0), kw.get("bank", 0), fake, None)
+    assert rc == -1  # RNB_ERR_INVALID
+    assert msg in _lib.load().rnb_last_error().decode()
+
+
+def test_qmm_workspace_size_rejects_bad_shapes():
+    n = ctypes.c_size_t()
+    assert _lib.load().rnb_qmm_workspace_size(4, 64, 64, 100, 2048, ctypes.byref(n)) == -1
+    assert _lib.load().rnb_qmm_workspace_size(4, 64, 64, 4096, 2048, ctypes.byref(n)) == 0
+    assert n.value > 64 * 2048 * 2

@@ -1,0 +1,92 @@
+"""GPU parity of the standalone QMV / QMM probes (rnb_qmv, rnb_qmm) against
+the reference's recorded known-answer values.
+
+The data of every QMV and QMM record in tests/golden/kats.json is regenerated
+by the oracle's restatement of the reference generators; the GPU result must
+pass the reference CLI's own validation bars (native/bench/quantized_qmv.cpp:
+rmse <= 1e-4 and |checksum - reference| <= 1e-3; quantized_qmm.cpp: max abs
+<= 0.2 and rmse <= 0.05) against the oracle's outputs, and its checksum must
+match the checksum the reference recorded.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from runnel_b200 import _lib, probes
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "kats.json")))["records"]
+QMV = [r for r in GOLDEN if r["kind"] == "qmv"]
+QMM = [r for r in GOLDEN if r["kind"] == "qmm"]
+
+
+def _dev(a):
+    if a.dtype == np.uint32:
+        return torch.from_numpy(a.view(np.int32)).cuda().view(torch.uint32)
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16)).cuda().view(torch.uint16)
+    return torch.from_numpy(a).cuda()
+
+
+@pytest.mark.parametrize("rec", QMV, ids=[r["source"].split("/")[-1] for r in QMV])
+def test_qmv_reference_kat(rec):
+    pr = rec["protocol"]
+    bits = 4 if pr["bits"] == "q4" else 8
+    sel = tuple(pr.get("selected_experts", ()))
+    data, y_ref, cs_ref = oracle.kat_qmv(bits, pr["output_size"], K=pr["reduction_size"],
+                                         bank_rows=pr.get("weight_bank_output_size", 0),
+                                         rows_per_expert=pr.get("rows_per_expert", 0), selected=sel)
+    x = _dev(data["x"]).view(torch.bfloat16)
+    y = probes.qmv(bits, _dev(data["w"]), _dev(data["s"]), _dev(data["b"]), x, selected=sel or None,
+                   rows_per_expert=pr.get("rows_per_expert", 0), rows=pr["output_size"])
+    yh = y.cpu().numpy().astype(np.float64)
+    rmse = float(np.sqrt(np.mean((yh - y_ref) ** 2)))
+    cs = float(yh.sum())
+    assert rmse <= 1e-4, rmse
+    assert abs(cs - cs_ref) <= 1e-3, (cs, cs_ref)
+    assert abs(cs - rec["reference_checksum"]) <= 1.5e-3, (cs, rec["reference_checksum"])
+
+
+@pytest.mark.parametrize("rec", QMM[::2], ids=[r["source"].split("/")[-1] for r in QMM[::2]])
+def test_qmm_reference_kat(rec):
+    pr = rec["protocol"]
+    bits = 4 if pr["bits"] == "q4" else 8
+    data, y_ref, cs_ref = oracle.kat_qmm(bits, pr["tokens"], pr["outputs"], pr["reduction_size"])
+    x = _dev(data["x"]).view(torch.bfloat16)
+    for f32 in (True, False):
+        y = probes.qmm(bits, _dev(data["w"]), _dev(data["s"]), _dev(data["b"]), x, out_f32=f32)
+        yh = y.float().cpu().numpy().astype(np.float64)
+        err = np.abs(yh - y_ref)
+        assert err.max() <= 0.2 and np.sqrt(np.mean(err ** 2)) <= 0.05, (err.max(), np.sqrt(np.mean(err ** 2)))
+    # fp32 output: the checksum agrees with the recorded one to the fp16-weight rounding
+    y = probes.qmm(bits, _dev(data["w"]), _dev(data["s"]), _dev(data["b"]), x).cpu().numpy().astype(np.float64)
+    rel = abs(y.sum() - rec["reference_checksum"]) / np.abs(y_ref).sum()
+    assert rel < 1e-4, rel
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_qmv_dense_and_gather_match_float64(bits):
+    w, s, b, x = probes.synthetic(bits, 4096, 4096 if bits == 4 else 2560, seed=bits)
+    x = x[0]
+    y = probes.qmv(bits, w, s, b, x)
+    ref = probes.dequant_reference(bits, w, s, b) @ x.to(torch.float64)
+    err = (y.double() - ref).abs()
+    assert float(err.max()) <= 2e-5 * float(ref.abs().max()) + 1e-5
+    sel = [31, 0, 7, 7]
+    y = probes.qmv(bits, w, s, b, x, selected=sel, rows_per_expert=128)
+    rows = torch.tensor(sel, device=w.device).repeat_interleave(128) * 128 + torch.arange(512, device=w.device) % 128
+    torch.testing.assert_close(y.double(), ref[rows], rtol=0, atol=2e-5 * float(ref.abs().max()) + 1e-5)
+    assert probes.qmv(bits, w, s, b, x, rows=0).numel() == 0
+
+
+def test_qmm_ragged_tokens_match_float64():
+    w, s, b, x = probes.synthetic(8, 1024, 1536, tokens=300, seed=3)
+    y = probes.qmm(8, w, s, b, x)
+    ref = x.to(torch.float64) @ probes.dequant_reference(8, w, s, b).T
+    err = (y.double() - ref).abs()
+    assert float(err.max()) <= 1e-3 * float(ref.abs().max())
