@@ -100,6 +100,67 @@ def synthetic(bits: int, rows: int, K: int, tokens: int = 1, seed: int = 0, devi
     return w, s.view(torch.uint16), b.view(torch.uint16), x
 
 
+def dataset_tensors(ds, device="cuda"):
+    """A :class:`runnel_b200.checkpoint.LayerDataset` on the device:
+    (BlockTensors of the whole bank, x [1, H] bf16, ids [1, k], weights [1, k])."""
+    import numpy as np
+
+    from .ops import BlockTensors
+
+    def up(a):
+        if a.dtype == np.uint32:
+            return torch.from_numpy(np.ascontiguousarray(a).view(np.int32)).to(device).view(torch.uint32)
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(device).view(torch.bfloat16)
+
+    bt = BlockTensors(bits=ds.bits, gu_w=up(ds.gu_w), gu_s=up(ds.gu_s), gu_b=up(ds.gu_b), dn_w=up(ds.dn_w),
+                      dn_s=up(ds.dn_s), dn_b=up(ds.dn_b))
+    x = up(ds.x).reshape(1, -1)
+    inds = torch.from_numpy(ds.selected.astype(np.int32)).reshape(1, -1).to(device)
+    w = torch.from_numpy(ds.route_w.astype(np.float32)).reshape(1, -1).to(device)
+    return bt, x, inds, w
+
+
+def two_stage(ds, device="cuda", tensors=None) -> torch.Tensor:
+    """The reference's two-stage MoE probe on one dataset: fp32 [H] =
+    sum_j w_j * down_e(silu(gate_e x) * up_e x) over the dataset's experts,
+    through ``rnb_moe_experts_fwd``."""
+    from .ops import experts_fwd
+
+    bt, x, inds, w = tensors or dataset_tensors(ds, device)
+    return experts_fwd(bt, x, inds, w)[0]
+
+
+def two_stage_reference(ds, device="cuda") -> torch.Tensor:
+    """float64 form of :func:`two_stage` (dequantised weights, exact SwiGLU)."""
+    bt, x, inds, w = dataset_tensors(ds, device)
+    xf = x[0].to(torch.float64)
+    out = torch.zeros(bt.H, dtype=torch.float64, device=x.device)
+    for j, e in enumerate(ds.selected.tolist()):
+        gu = dequant_reference(ds.bits, bt.gu_w[e], bt.gu_s[e].view(torch.uint16), bt.gu_b[e].view(torch.uint16)) @ xf
+        up_, gate = gu[:bt.I], gu[bt.I:]
+        h = gate / (1.0 + torch.exp(-gate)) * up_
+        out += float(ds.route_w[j]) * (dequant_reference(ds.bits, bt.dn_w[e], bt.dn_s[e].view(torch.uint16),
+                                                         bt.dn_b[e].view(torch.uint16)) @ h)
+    return out
+
+
+def measure_two_stage(ds, warmups: int = 2, trials: int = 5, device="cuda") -> dict:
+    """One measurement record in the reference fused-MoE CLI's shape."""
+    tensors = dataset_tensors(ds, device)
+    y = two_stage(ds, tensors=tensors)
+    ref = two_stage_reference(ds, device)
+    err = y.to(torch.float64) - ref
+    gpu = _time(lambda: two_stage(ds, tensors=tensors), warmups, trials)
+    bt = tensors[0]
+    per_expert = (bt.gu_w[0].numel() + bt.dn_w[0].numel()) * 4 + (bt.gu_s[0].numel() + bt.dn_s[0].numel()) * 4
+    nbytes = per_expert * len(ds.selected)
+    med = _median(gpu)
+    return {"weight_bytes": nbytes, "two_stage": True, "weight_gib_per_second": nbytes / (med * 1e3),
+            "median_gpu_micros": med, "output_checksum": float(y.to(torch.float64).sum()),
+            "reference_checksum": float(ref.sum()), "max_absolute_error": float(err.abs().max()),
+            "rmse": float(err.pow(2).mean().sqrt()), "trials": [{"gpu_micros": t} for t in gpu]}
+
+
 def _time(fn, warmups: int, trials: int) -> list[float]:
     for _ in range(warmups):
         fn()
@@ -141,7 +202,34 @@ def main(argv=None) -> int:
     m.add_argument("--quant-group-size", type=int, default=64)
     m.add_argument("--warmups", type=int, default=2)
     m.add_argument("--trials", type=int, default=7)
+    t = sub.add_parser("two-stage")
+    t.add_argument("--bits", default="q4", choices=["q4", "q8"])
+    t.add_argument("--total-experts", type=int, default=256)
+    t.add_argument("--experts", default="3,17,29,42,50,61,7,55")
+    t.add_argument("--dataset", required=True)
+    t.add_argument("--warmups", type=int, default=2)
+    t.add_argument("--trials", type=int, default=5)
+    t.set_defaults(quant_group_size=64)
     args = ap.parse_args(argv)
+    if args.probe == "two-stage":
+        from .checkpoint import read_layer_dataset
+
+        bits = 4 if args.bits == "q4" else 8
+        ds = read_layer_dataset(args.dataset, bits=bits, total_experts=args.total_experts)
+        if [int(e) for e in args.experts.split(",")] != ds.selected.tolist():
+            print("runnel_b200.probes: fused MoE dataset expert selection does not match the probe",
+                  file=sys.stderr)
+            return 1
+        meas = measure_two_stage(ds, args.warmups, args.trials)
+        limit = max(5.0, abs(meas["reference_checksum"]) * 0.25)
+        if meas["max_absolute_error"] > 1.0 or meas["rmse"] > 0.2 or \
+                abs(meas["output_checksum"] - meas["reference_checksum"]) > limit:
+            print("runnel_b200.probes: fused MoE failed reference validation", file=sys.stderr)
+            return 1
+        proto = {"bits": args.bits, "total_experts": args.total_experts, "selected_experts": ds.selected.tolist(),
+                 "schedule": "two-stage", "dataset_loaded": True, "warmups": args.warmups, "trials": args.trials}
+        print(json.dumps({"protocol": proto, "measurements": [meas]}, indent=2))
+        return 0
     if args.quant_group_size != 64:
         print("runnel_b200.probes: only group size 64 is supported", file=sys.stderr)
         return 1

@@ -90,3 +90,54 @@ def test_qmm_ragged_tokens_match_float64():
     ref = x.to(torch.float64) @ probes.dequant_reference(8, w, s, b).T
     err = (y.double() - ref).abs()
     assert float(err.max()) <= 1e-3 * float(ref.abs().max())
+
+
+@pytest.mark.parametrize("bits,expected", [(8, 6.836), (4, 170.073)])
+def test_two_stage_dataset_probe_reference_kat(bits, expected, tmp_path):
+    """The two-stage KAT bank written as an RNLMOE01 dataset, read back and run
+    by the dataset probe (rnb_moe_experts_fwd): the reference's recorded checksum."""
+    from runnel_b200 import checkpoint
+    data, ref_out, ref_cs = oracle.kat_two_stage(bits)
+    ds = checkpoint.LayerDataset(bits=bits, selected=data["selected"], x=data["x"], route_w=data["route_w"],
+                                 **{k: data[k] for k in ("gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b")})
+    path = str(tmp_path / "kat.bin")
+    checkpoint.write_layer_dataset(path, ds)
+    back = checkpoint.read_layer_dataset(path, bits=bits, total_experts=64)
+    y = probes.two_stage(back).cpu().numpy().astype(np.float64)
+    assert abs(y.sum() - expected) < 5e-3, (y.sum(), expected)
+    np.testing.assert_allclose(y, ref_out, rtol=0, atol=2e-3 * np.abs(ref_out).max())
+    meas = probes.measure_two_stage(back, warmups=1, trials=2)
+    assert meas["rmse"] < 1e-3 and abs(meas["output_checksum"] - meas["reference_checksum"]) < 5e-3
+
+
+def test_checkpoint_block_and_layer_sweep(tmp_path):
+    """A synthetic MLX checkpoint: the whole block loaded by name runs and
+    matches the oracle on the same (dequantised-router) arrays; the layer sweep
+    writes one record per layer."""
+    import importlib.util
+    from runnel_b200 import checkpoint, layers, ops
+    spec = importlib.util.spec_from_file_location(
+        "mkgold", os.path.join(os.path.dirname(__file__), "golden", "make_checkpoint_golden.py"))
+    mk = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mk)
+    root = str(tmp_path / "ornith-synthetic")
+    mk.synthetic_checkpoint(root)
+    st = checkpoint.TensorStore(root)
+    bt = checkpoint.load_block(st, 0)
+    a = checkpoint.load_block_arrays(st, 0)
+    x_bits = np.random.default_rng(5).standard_normal((3, 2048)).astype(np.float32)
+    from runnel_b200.quant import f32_to_bf16_bits
+    x_bits = f32_to_bf16_bits(x_bits)
+    x = torch.from_numpy(x_bits.view(np.int16)).view(torch.bfloat16).cuda()
+    out, inds, _ = ops.moe_block(bt, x, return_routing=True)
+    fields = {k: a[k] for k in ("router_w", "shared_gate_w", "gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b",
+                                "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b")}
+    ref, oinds, _ = oracle.moe_block(oracle.BlockWeights(bits=4, group=64, **fields), x_bits, k=8)
+    np.testing.assert_array_equal(np.sort(inds.cpu().numpy(), 1), np.sort(oinds, 1))
+    from tests._parity import assert_close
+    assert_close(out.float().cpu().numpy(), ref, "checkpoint block")
+    doc = layers.sweep(root, "q4", [0], experts="3,1,7,0,5,2,6,4", warmups=1, trials=2)
+    rec = doc["records"][0]
+    assert rec["layer"] == 0 and rec["manifest"]["total_experts"] == 8
+    m = rec["native"]["measurements"][0]
+    assert m["rmse"] < 1e-3 and abs(m["output_checksum"] - m["reference_checksum"]) < 5e-3
