@@ -1880,7 +1880,9 @@ size_t persistent_static_smem() {
 // Shared-memory plan of k_decode; false when the call does not fit it.
 template <int BITS>
 bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem) {
-  if (p.mode != kModeBlock || p.T < 1 || p.T > kPMaxT || p.H != 2048 || p.I != 512 || p.E_total > 256 ||
+  // Phase A computes the router dots of two tokens at once (tokens 0 and 1):
+  // more tokens take the decode chain, whatever the shared-memory plan allows.
+  if (p.mode != kModeBlock || p.T < 1 || p.T > 2 || p.H != 2048 || p.I != 512 || p.E_total > 256 ||
       p.k > 8 || p.off < 0 || p.off + p.E > p.E_total)
     return false;
   pl.n_rtiles = (p.E_total + 1 + 15) / 16;

@@ -229,3 +229,26 @@ def test_persistent_kernel_in_cuda_graph():
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
     assert ws.status() == 0
+
+
+@pytest.mark.parametrize("T", [3, 5, 8])
+def test_small_bank_many_tokens_fresh_workspace(T):
+    """A small expert bank (E = 16) lets several tokens fit the persistent
+    kernel's shared-memory plan; each call on a fresh workspace (no data left
+    by earlier calls) must still match the oracle for every token."""
+    blk = inputs.make_block(4, seed=11, T=T, E=16)
+    bt = ops.BlockTensors.from_numpy(blk, "cuda")
+    x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
+    w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
+    ref, oinds, _ = oracle.moe_block(w, blk.x, k=8)
+    out, inds, _ = ops.moe_block(bt, x, ws=ops.Workspace("cuda"), return_routing=True)
+    np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
+    assert_close(out.float().cpu().numpy(), ref, f"E=16 T={T} fresh workspace")
+    shard = ops.BlockTensors.from_numpy(blk, "cuda", E_range=(4, 12))
+    part = ops.moe_block(ops.BlockTensors(**{**shard.__dict__, "flags": _lib.FLAG_Y_F32 | _lib.FLAG_NO_SHARED}),
+                         x, ws=ops.Workspace("cuda"))
+    keep = (oinds >= 4) & (oinds < 12)
+    _, _, osc, _ = oracle.router(w, blk.x, k=8)
+    y = oracle.switchglu(w, blk.x, oinds)
+    assert_close(part.cpu().numpy(), np.einsum("tk,tkh->th", np.where(keep, osc, 0.0).astype(np.float32), y),
+                 f"E=16 shard T={T} fresh workspace")

@@ -104,10 +104,15 @@ def test_two_stage_dataset_probe_reference_kat(bits, expected, tmp_path):
     checkpoint.write_layer_dataset(path, ds)
     back = checkpoint.read_layer_dataset(path, bits=bits, total_experts=64)
     y = probes.two_stage(back).cpu().numpy().astype(np.float64)
-    assert abs(y.sum() - expected) < 5e-3, (y.sum(), expected)
-    np.testing.assert_allclose(y, ref_out, rtol=0, atol=2e-3 * np.abs(ref_out).max())
+    from tests._parity import assert_close
+    assert_close(y, ref_out, f"two-stage dataset q{bits}")
+    # The grouped GEMM feeds the SwiGLU rows to the down projection as fp16
+    # (11-bit significand); every output shares those rows, so their rounding
+    # reaches the checksum coherently: within 1e-3 of it, not the 5e-3
+    # absolute of the decode kernels' split-fp16 activations.
+    assert abs(y.sum() - expected) < 1e-3 * abs(expected) + 5e-4, (y.sum(), expected)
     meas = probes.measure_two_stage(back, warmups=1, trials=2)
-    assert meas["rmse"] < 1e-3 and abs(meas["output_checksum"] - meas["reference_checksum"]) < 5e-3
+    assert meas["rmse"] < 1e-3 and abs(meas["output_checksum"] - meas["reference_checksum"]) < 1e-3 * abs(expected)
 
 
 def test_checkpoint_block_and_layer_sweep(tmp_path):
@@ -140,4 +145,4 @@ def test_checkpoint_block_and_layer_sweep(tmp_path):
     rec = doc["records"][0]
     assert rec["layer"] == 0 and rec["manifest"]["total_experts"] == 8
     m = rec["native"]["measurements"][0]
-    assert m["rmse"] < 1e-3 and abs(m["output_checksum"] - m["reference_checksum"]) < 5e-3
+    assert m["rmse"] < 1e-3 and abs(m["output_checksum"] - m["reference_checksum"]) < 1e-3 * abs(m["reference_checksum"]) + 5e-3
