@@ -1461,10 +1461,14 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   }
 
   // ---- phase B: routed gate/up tasks i = cta, cta + NC, ...
+  // Tasks i = rc, rc + NC, ... with the CTA order rotated so that the CTAs
+  // which computed a shared gate/up task in phase A (they leave the routing
+  // barrier last) come last and get the smaller task counts.
   const int n_btask = n_act * n_ch;
-  const int mine = n_btask > cta ? (n_btask - cta + NC - 1) / NC : 0;
+  const int rc = (cta + NC - (pl.n_rtiles + n_ch) % NC) % NC;
+  const int mine = n_btask > rc ? (n_btask - rc + NC - 1) / NC : 0;
   auto issue_b = [&](int m) {
-    const int i = cta + m * NC;
+    const int i = rc + m * NC;
     const int a = i / n_ch, ch0 = (i % n_ch) * 8;
     const uint32_t le = ms->act_e[a];
     const size_t ew = static_cast<size_t>(2) * p.I * gwrow, es = static_cast<size_t>(2) * p.I * gsrow;
@@ -1497,7 +1501,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     __syncwarp();
     if (r0 == 0) RNB_TRACE_MARK(p, 16);
     if (tid < nr) {
-      const int i = cta + (r0 + tid) * NC, a = i / n_ch;
+      const int i = rc + (r0 + tid) * NC, a = i / n_ch;
       ms->tasks[tid] = PTask{ms->act_ent[a], static_cast<int>(ms->act_cnt[a]), (i % n_ch) * 8};
     }
     __syncthreads();
