@@ -874,6 +874,11 @@ __global__ void __launch_bounds__(32 * kDownMaxWarps) k_down(Params p) {
 //   exit     the last CTA to leave resets the counters.
 
 constexpr int kPWarps = 16;
+// Phase C feeds the SwiGLU activations to the down projection as one fp16
+// per value (11-bit significand, per-column power-of-two scale) -- the
+// precision of the prefill GEMMs.  With true it adds the fp16 remainder
+// (about 22 bits) at twice the MMAs and conversions.
+constexpr bool kPhaseCSplit = false;
 constexpr int kPMaxT = 8;
 constexpr uint64_t kSpinLimitNs = 200ull * 1000 * 1000;  // a wait gives up after 200 ms
 // Waits on other GPUs: ranks launch independently, so allow host-side skew.
@@ -1593,9 +1598,11 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
         float hs_l = 1.f, hi_l = 1.f;
         fp16_range_scale(cmax, hs_l, hi_l);
         // Convert this task's activations once, in place: per column, 128
-        // fp32 values become hi and lo fp16 fragments in MMA pair order
-        // (2 groups x 4 lane quads x 8 pairs each) and two group sums of hi+lo.
-        // Lane l converts pairs 2(l&3), 2(l&3)+1 of quad (l>>2)&3, group l>>4.
+        // fp32 values become fp16 fragments in MMA pair order (2 groups x 4
+        // lane quads x 8 pairs each; with kPhaseCSplit also the fp16
+        // remainders, 64 words further) and two group sums of what the MMAs
+        // see.  Lane l converts pairs 2(l&3), 2(l&3)+1 of quad (l>>2)&3,
+        // group l>>4.
         {
           const int cg = lane >> 4, cq = (lane >> 2) & 3, i0 = (lane & 3) * 2;
           const int pb = BITS == 8 ? 16 * cq : 16 * ((cq == 1) ? 2 : (cq == 2) ? 1 : cq);
@@ -1617,11 +1624,14 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
             for (int k2 = 0; k2 < 2; ++k2) {
               const __half2 hi = __floats2half2_rn(v[2 * k2], v[2 * k2 + 1]);
               const float2 hf = __half22float2(hi);
-              const __half2 lo = __floats2half2_rn(v[2 * k2] - hf.x, v[2 * k2 + 1] - hf.y);
-              const float2 lf = __half22float2(lo);
               frag[col * 128 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&hi);
-              frag[col * 128 + 64 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&lo);
-              part += (hf.x + lf.x) + (hf.y + lf.y);
+              if (kPhaseCSplit) {
+                const __half2 lo = __floats2half2_rn(v[2 * k2] - hf.x, v[2 * k2 + 1] - hf.y);
+                const float2 lf = __half22float2(lo);
+                frag[col * 128 + 64 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&lo);
+                part += lf.x + lf.y;
+              }
+              part += hf.x + hf.y;
             }
             part += __shfl_xor_sync(0xffffffffu, part, 1);
             part += __shfl_xor_sync(0xffffffffu, part, 2);
@@ -1648,7 +1658,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
           xl[4] = l1.x; xl[5] = l1.y; xl[6] = l1.z; xl[7] = l1.w;
         };
         auto gsum = [&](int gi, int col) { return mq[(col ? cl1 : cl0) * nt_i + gi]; };
-        tile2_mma<BITS, true>(sCR + q * TL::kBytes, g, c, bfrag, gsum, acc);
+        tile2_mma<BITS, kPhaseCSplit>(sCR + q * TL::kBytes, g, c, bfrag, gsum, acc);
         if (q0 == warp && bq == 0) RNB_TRACE_MARK(p, 21);
         const float inv0 = __shfl_sync(0xffffffffu, hi_l, 2 * c);
         const float inv1 = __shfl_sync(0xffffffffu, hi_l, 2 * c + 1);
