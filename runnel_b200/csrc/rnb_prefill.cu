@@ -13,11 +13,12 @@
 //   k_pre_gemm<0>  grouped gate/up GEMM + SwiGLU: 256 rows x (64 up + 64 gate)
 //                  channels per work item, K = H in 64-wide stages.
 //   k_pre_hrow     one power-of-two scale per SwiGLU row.
-//   k_pre_gemm<1>  grouped down GEMM: 256 rows x 128 outputs, K = I; adds
-//                  score * y into an fp32 [T, H] accumulator with vector
-//                  atomics (their order is not fixed: results reproduce to
-//                  fp32 rounding rather than bit for bit).
-//   k_pre_final    fp32 accumulator -> bf16 (or fp32) output.
+//   k_pre_gemm<1>  grouped down GEMM: 256 rows x 128 outputs, K = I; writes
+//                  score * y of every sorted row as fp16 with one power-of-two
+//                  scale per (row, 128-column n-tile) -- no atomics.
+//   k_pre_final    per token, the sum of its rows (routed slots, then the
+//                  shared expert) in slot order -> bf16 (or fp32) output;
+//                  results do not depend on the schedule.
 //
 // The weights stay in MLX's affine layout; k_pre_gemm's converter warps
 // dequantise them in shared memory to fp16 (w = s*q + b with one rounding)
@@ -68,7 +69,9 @@ struct Ws {
   __half* h16;       // [rows_cap][I] SwiGLU activations, one scale per row after k_pre_hrow
   float* hinv;       // [rows_cap][I/64] inverse scale of each 64-channel chunk
   float* hrow;       // [rows_cap] inverse scale of the row (largest chunk inverse scale)
-  float* acc;        // [T][H] fp32 output accumulator
+  __half* y16;       // [rows_cap][H] down outputs times their weight, fp16, one scale per (row, n-tile)
+  float* yinv;       // [rows_cap][H/128] inverse of that scale
+  uint32_t* rowpos;  // [T][K+1] sorted row of entry t*(K+1)+slot, 0xFFFFFFFF if none
 };
 
 struct Params {
@@ -441,6 +444,7 @@ __global__ void __launch_bounds__(512) k_qmm_prep(Params p) {
   if (lane == 0) {
     p.ws.hrow[t] = inv;
     p.ws.perm[t] = static_cast<uint32_t>(t) * 2u;  // entry t * (k + 1) + 0 with k = 1
+    p.ws.rowpos[static_cast<size_t>(t) * 2] = static_cast<uint32_t>(t);
     p.ws.scores[t] = 1.0f;
   }
 }
@@ -502,10 +506,13 @@ __global__ void k_pre_scatter(Params p) {
       const int le = static_cast<int>(p.ws.inds[i]) - p.off;
       if (le < 0 || le >= p.E) continue;
       const uint32_t pos = p.ws.base[le] + atomicAdd(&p.ws.fill[le], 1u);
-      p.ws.perm[pos] = static_cast<uint32_t>((i / K) * (K + 1) + (i % K));
+      const uint32_t ent = static_cast<uint32_t>((i / K) * (K + 1) + (i % K));
+      p.ws.perm[pos] = ent;
+      p.ws.rowpos[ent] = pos;
     } else {
       const size_t t = i - n_routed;
       p.ws.perm[p.ws.base[p.E] + t] = static_cast<uint32_t>(t * (K + 1) + K);
+      p.ws.rowpos[t * (K + 1) + K] = p.ws.base[p.E] + static_cast<uint32_t>(t);
     }
   }
 }
@@ -800,11 +807,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pre_gemm(Params p, const __
                                                 : __ldcg(p.ws.sg + t);
             w *= __ldcg(p.ws.hrow + row);
           }
-          // Lane = row: each row belongs to another token.  Stage 32 columns
-          // of the warp's 32 rows in shared memory, then let 8 lanes cover one
-          // row's 128 contiguous bytes, so an atomic instruction touches 4 rows
-          // instead of 32.
-          float* tp = reinterpret_cast<float*>(sm + C::S * C::kStage) + quad * 32 * C::kTpPitch;
+          // The n-tile of this row, times its weight, goes to y16 as fp16
+          // with one power-of-two scale (the largest |value| of the 128
+          // columns into fp16 range; read from TMEM twice) -- no atomics:
+          // k_pre_final adds a token's rows in slot order.  The rows are
+          // written through a shared-memory transpose so that four lanes
+          // cover one row's 64 contiguous bytes.
+          float mx = 0.f;
+          for (int cc = 0; cc < C::N / 16; cc += 2) {
+            uint32_t v[2][16];
+            tmem_ld16(tl + cc * 16, v[0]);
+            tmem_ld16(tl + (cc + 1) * 16, v[1]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(v[0][q])), fabsf(__uint_as_float(v[1][q]))));
+          }
+          float ysc, yiv;
+          fp16_range_scale(mx * fabsf(w), ysc, yiv);
+          const float m = w * ysc;
+          uint32_t* tp = reinterpret_cast<uint32_t*>(sm + C::S * C::kStage) + quad * 32 * C::kTpPitch;
+          const size_t grow0 = static_cast<size_t>(row0 + h * kTileM + quad * 32);
           for (int cc = 0; cc < C::N / 16; cc += 2) {
             uint32_t v[2][16];
             tmem_ld16(tl + cc * 16, v[0]);
@@ -812,26 +835,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pre_gemm(Params p, const __
             tmem_wait_ld();
             __syncwarp();  // the previous chunk's reads are done
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const uint32_t* vq = v[q >> 2] + (q & 3) * 4;
-              *reinterpret_cast<float4*>(tp + lane * C::kTpPitch + q * 4) =
-                  make_float4(__uint_as_float(vq[0]) * w, __uint_as_float(vq[1]) * w, __uint_as_float(vq[2]) * w,
-                              __uint_as_float(vq[3]) * w);
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t* vq = v[q >> 1] + (q & 1) * 8;
+              *reinterpret_cast<uint4*>(tp + lane * C::kTpPitch + q * 4) =
+                  make_uint4(half2_bits(__uint_as_float(vq[0]) * m, __uint_as_float(vq[1]) * m),
+                             half2_bits(__uint_as_float(vq[2]) * m, __uint_as_float(vq[3]) * m),
+                             half2_bits(__uint_as_float(vq[4]) * m, __uint_as_float(vq[5]) * m),
+                             half2_bits(__uint_as_float(vq[6]) * m, __uint_as_float(vq[7]) * m));
             }
             __syncwarp();
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int rr = (lane >> 3) + 4 * i, c4 = (lane & 7) * 4;
-              const uint32_t tr = __shfl_sync(0xffffffffu, t, rr);
+            for (int i = 0; i < 4; ++i) {
+              const int rr = (lane >> 2) + 8 * i, pc = lane & 3;
               const bool vr = __shfl_sync(0xffffffffu, valid ? 1 : 0, rr) != 0;
-              const float4 q4 = *reinterpret_cast<const float4*>(tp + rr * C::kTpPitch + c4);
+              const uint4 d = *reinterpret_cast<const uint4*>(tp + rr * C::kTpPitch + pc * 4);
               if (vr)
-                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
-                                 p.ws.acc + static_cast<size_t>(tr) * H + nt * C::N + cc * 16 + c4),
-                             "f"(q4.x), "f"(q4.y), "f"(q4.z), "f"(q4.w)
-                             : "memory");
+                *reinterpret_cast<uint4*>(p.ws.y16 + (grow0 + rr) * H + nt * C::N + cc * 16 + pc * 8) = d;
             }
           }
+          if (valid) p.ws.yinv[row * (H / C::N) + nt] = yiv;
         }
       }
       tc_fence_before();
@@ -892,20 +914,52 @@ __global__ void k_pre_hrow(Params p) {
   }
 }
 
+// out[t] = sum over slots s = 0..k (routed slots, then the shared expert) of
+// yinv * y16 of the entry's sorted row, in slot order; 8 columns a thread.
 __global__ void k_pre_final(Params p) {
-  const size_t n = static_cast<size_t>(p.T) * p.H / 4;
+  const int K = p.k, H = p.H, per_t = H / 8, ntile = H / 128;
+  const size_t n = static_cast<size_t>(p.T) * per_t;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(p.ws.acc) + i);
-    if (p.y_f32) {
-      reinterpret_cast<float4*>(p.out)[i] = v;
-      continue;
+    const size_t t = i / per_t;
+    const int c8 = static_cast<int>(i % per_t);
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // all rows first, then all their loads, then the ordered sum
+    uint32_t row[kMaxK + 1];
+#pragma unroll
+    for (int s = 0; s <= kMaxK; ++s) row[s] = s <= K ? __ldcg(p.ws.rowpos + t * (K + 1) + s) : 0xFFFFFFFFu;
+    float inv[kMaxK + 1];
+    uint4 v[kMaxK + 1];
+#pragma unroll
+    for (int s = 0; s <= kMaxK; ++s) {
+      const bool ok = row[s] != 0xFFFFFFFFu;
+      inv[s] = ok ? __ldcg(p.ws.yinv + static_cast<size_t>(row[s]) * ntile + c8 / 16) : 0.f;
+      v[s] = ok ? __ldcg(reinterpret_cast<const uint4*>(p.ws.y16 + static_cast<size_t>(row[s]) * H) + c8)
+                : make_uint4(0u, 0u, 0u, 0u);
     }
-    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
-    uint2 o;
-    o.x = *reinterpret_cast<const uint32_t*>(&a);
-    o.y = *reinterpret_cast<const uint32_t*>(&b);
-    reinterpret_cast<uint2*>(p.out)[i] = o;
+#pragma unroll
+    for (int s = 0; s <= kMaxK; ++s) {
+      const uint32_t w[4] = {v[s].x, v[s].y, v[s].z, v[s].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+        a[2 * j] = fmaf(f.x, inv[s], a[2 * j]);
+        a[2 * j + 1] = fmaf(f.y, inv[s], a[2 * j + 1]);
+      }
+    }
+    if (p.y_f32) {
+      float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + t * H + c8 * 8);
+      o[0] = make_float4(a[0], a[1], a[2], a[3]);
+      o[1] = make_float4(a[4], a[5], a[6], a[7]);
+    } else {
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(a[2 * j], a[2 * j + 1]);
+        o[j] = *reinterpret_cast<const uint32_t*>(&b2);
+      }
+      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + t * H)[c8] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 }
 
@@ -914,14 +968,18 @@ __global__ void k_pre_final(Params p) {
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 struct Layout {
-  size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, x16, xs16, h16, hinv, hrow, acc, total;
+  size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, x16, xs16, h16, hinv, hrow, y16, yinv,
+      rowpos, total;
   int rows_cap, max_mt;
 };
 
 Layout make_layout(const rnb_moe_desc& d) {
   Layout L;
   const size_t T = d.T, K = d.k, E1 = d.E + 1;
-  L.rows_cap = static_cast<int>(T * K + T + E1 * (kTileM - 1) + kTileM);
+  // sorted rows: every entry plus each non-empty expert's padding to 128
+  // rows (at most T*(K+1) experts can be non-empty)
+  const size_t nonempty = E1 < T * (K + 1) ? E1 : T * (K + 1);
+  L.rows_cap = static_cast<int>(T * K + T + nonempty * (kTileM - 1) + kTileM);
   L.max_mt = L.rows_cap / kTileM + static_cast<int>(E1) + 1;
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -946,7 +1004,9 @@ Layout make_layout(const rnb_moe_desc& d) {
   L.h16 = take(static_cast<size_t>(L.rows_cap) * d.I * 2);
   L.hinv = take(static_cast<size_t>(L.rows_cap) * (d.I / 64) * 4);
   L.hrow = take(static_cast<size_t>(L.rows_cap) * 4);
-  L.acc = take(T * d.H * 4);
+  L.y16 = take(static_cast<size_t>(L.rows_cap) * d.H * 2);
+  L.yinv = take(static_cast<size_t>(L.rows_cap) * (d.H / 128) * 4);
+  L.rowpos = take(T * (K + 1) * 4);
   L.total = o;
   return L;
 }
@@ -1040,7 +1100,7 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
   // zero the histogram and the fp32 accumulator; padding rows of perm = ~0
   e = cudaMemsetAsync(p.ws.counts, 0, (p.E + 1) * 4, st);
   if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.perm, 0xFF, static_cast<size_t>(L.rows_cap) * 4, st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.acc, 0, static_cast<size_t>(p.T) * p.H * 4, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.rowpos, 0xFF, static_cast<size_t>(p.T) * (p.k + 1) * 4, st);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill memset: ") + cudaGetErrorString(e));
   static bool attr = false;
   if (!attr) {
@@ -1071,7 +1131,8 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
   k_pre_hrow<<<(L.rows_cap + 7) / 8, 256, 0, st>>>(p);
   k_pre_gemm<BITS, 1><<<nc, kGemmThreads, C::kSmem, st>>>(p, tm1);
   stage_end(st, RNB_STAGE_DOWN);
-  k_pre_final<<<nc * 4, 256, 0, st>>>(p);
+  const size_t n_final = static_cast<size_t>(p.T) * (p.H / 8);
+  k_pre_final<<<static_cast<unsigned>((n_final + 255) / 256), 256, 0, st>>>(p);
   stage_end(st, RNB_STAGE_FINAL);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e));
@@ -1133,7 +1194,9 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
   p.ws.h16 = reinterpret_cast<__half*>(b + L.h16);
   p.ws.hinv = reinterpret_cast<float*>(b + L.hinv);
   p.ws.hrow = reinterpret_cast<float*>(b + L.hrow);
-  p.ws.acc = reinterpret_cast<float*>(b + L.acc);
+  p.ws.y16 = reinterpret_cast<__half*>(b + L.y16);
+  p.ws.yinv = reinterpret_cast<float*>(b + L.yinv);
+  p.ws.rowpos = reinterpret_cast<uint32_t*>(b + L.rowpos);
   return d->bits == 8 ? launch_prefill<8>(p, L, st) : launch_prefill<4>(p, L, st);
 }
 
@@ -1171,12 +1234,13 @@ static int launch_qmm(pre::Params& p, const pre::Layout& L, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(k_pre_gemm<BITS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(C::kSmem));
   if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.perm, 0xFF, static_cast<size_t>(L.rows_cap) * 4, st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.acc, 0, static_cast<size_t>(p.T) * p.H * 4, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p.ws.rowpos, 0xFF, static_cast<size_t>(p.T) * 2 * 4, st);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("qmm setup: ") + cudaGetErrorString(e));
   k_qmm_prep<<<(p.T + 15) / 16, 512, 0, st>>>(p);
   const int nc = dev_info().sms;
   k_pre_gemm<BITS, 1><<<nc, kGemmThreads, C::kSmem, st>>>(p, tm);
-  k_pre_final<<<nc * 4, 256, 0, st>>>(p);
+  const size_t n_final = static_cast<size_t>(p.T) * (p.H / 8);
+  k_pre_final<<<static_cast<unsigned>((n_final + 255) / 256), 256, 0, st>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("qmm launch: ") + cudaGetErrorString(e));
   return RNB_OK;
@@ -1221,7 +1285,9 @@ int run_qmm(int bits, int T, int N, int K, const uint32_t* w, const uint16_t* s,
   p.ws.h16 = reinterpret_cast<__half*>(base + L.h16);
   p.ws.hinv = reinterpret_cast<float*>(base + L.hinv);
   p.ws.hrow = reinterpret_cast<float*>(base + L.hrow);
-  p.ws.acc = reinterpret_cast<float*>(base + L.acc);
+  p.ws.y16 = reinterpret_cast<__half*>(base + L.y16);
+  p.ws.yinv = reinterpret_cast<float*>(base + L.yinv);
+  p.ws.rowpos = reinterpret_cast<uint32_t*>(base + L.rowpos);
   return bits == 8 ? launch_qmm<8>(p, L, st) : launch_qmm<4>(p, L, st);
 }
 

@@ -107,7 +107,11 @@ def test_experts_fwd_given_routing_matches_oracle():
     # an id outside [0, E_total) is skipped and flagged
     bad = ti.clone()
     bad[0, 0] = 999
-    ws = torch.zeros(1 << 26, dtype=torch.uint8, device="cuda")
+    import ctypes
+    need = ctypes.c_size_t()
+    d = ops.BlockTensors(**{**bt.__dict__, "flags": _lib.FLAG_Y_F32}).desc(2, 8)
+    _lib.call("rnb_moe_experts_workspace_size", ctypes.byref(d), ctypes.byref(need))
+    ws = torch.zeros(need.value, dtype=torch.uint8, device="cuda")
     out = ops.experts_fwd(bt, x[:2], bad[:2], ts[:2], ws=ws)
     st = int(ws[:4].view(torch.int32).item())
     assert st & _lib.STATUS_BAD_INDEX
