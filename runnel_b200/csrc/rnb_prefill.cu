@@ -177,9 +177,15 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
   static_assert(kRouteT * 16 == 512, "one 16-byte piece of one token per thread and chunk");
   float xm_acc = 0.f, xs_acc = 0.f;
   constexpr int kNC = kRouteT / 8;  // 8-token MMA column blocks
+  // Each 128-wide K chunk accumulates in fp32 (8 MMA steps), the chunks in
+  // fp64: the logit error stays within kRouteRelPrefill (8 steps, not 128).
   float acc[kNC][4];
+  double accd[kNC][4];
 #pragma unroll
-  for (int n = 0; n < kNC; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  for (int n = 0; n < kNC; ++n) {
+    acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    accd[n][0] = accd[n][1] = accd[n][2] = accd[n][3] = 0.0;
+  }
   float wa2 = 0.f, wa1 = 0.f, wb2 = 0.f, wb1 = 0.f;  // norms of rows row_a, row_b (lane's quarter)
   const int row_a = warp * 16 + g, row_b = row_a + 8;
   const uint16_t* wa = row_a < Et ? p.router_w + static_cast<size_t>(row_a) * H : nullptr;
@@ -249,6 +255,13 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
           mma_bf16(acc[n], a0.z, a1.z, a0.w, a1.w, bx.z, bx.w);
         }
       }
+#pragma unroll
+      for (int n = 0; n < kNC; ++n)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          accd[n][j] += static_cast<double>(acc[n][j]);
+          acc[n][j] = 0.f;
+        }
     }
     __syncthreads();
   }
@@ -299,12 +312,12 @@ __global__ void __launch_bounds__(512) k_pre_route(Params p) {
       const int tA = n * 8 + 2 * c, tB = tA + 1;
       const float xiA = __uint_as_float(xmax[tA]), xiB = __uint_as_float(xmax[tB]);
       if (row_a < Et) {
-        lgu[tA][row_a] = route_interval(acc[n][0], xn2[tA], xiA, wa2, wa1, kRouteRelPrefill);
-        lgu[tB][row_a] = route_interval(acc[n][1], xn2[tB], xiB, wa2, wa1, kRouteRelPrefill);
+        lgu[tA][row_a] = route_interval(static_cast<float>(accd[n][0]), xn2[tA], xiA, wa2, wa1, kRouteRelPrefill);
+        lgu[tB][row_a] = route_interval(static_cast<float>(accd[n][1]), xn2[tB], xiB, wa2, wa1, kRouteRelPrefill);
       }
       if (row_b < Et) {
-        lgu[tA][row_b] = route_interval(acc[n][2], xn2[tA], xiA, wb2, wb1, kRouteRelPrefill);
-        lgu[tB][row_b] = route_interval(acc[n][3], xn2[tB], xiB, wb2, wb1, kRouteRelPrefill);
+        lgu[tA][row_b] = route_interval(static_cast<float>(accd[n][2]), xn2[tA], xiA, wb2, wb1, kRouteRelPrefill);
+        lgu[tB][row_b] = route_interval(static_cast<float>(accd[n][3]), xn2[tB], xiB, wb2, wb1, kRouteRelPrefill);
       }
     }
   }
