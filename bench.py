@@ -336,7 +336,7 @@ def run_prefill_bench(args, cfg):
 
     bits, T = args.bits, cfg["T"]
     blocks, routing = prefill_blocks(cfg, bits, args.seed)
-    a2a = world > 1 and args.prefill_par == "a2a"
+    a2a = world > 1 and args.prefill_par in ("a2a", "gather")
     E_range = None
     if a2a:
         from runnel_b200 import ep as epm
@@ -356,7 +356,11 @@ def run_prefill_bench(args, cfg):
     moved = {"sent": 0, "received": 0}
 
     def block(i, x, o):
-        if a2a:
+        if a2a and args.prefill_par == "gather":
+            o.copy_(epm.moe_block_gather(kinds[i % nk], x, rank, world, ws=ws))
+            moved["sent"] += x.shape[0] * (world - 1)
+            moved["received"] += x.shape[0] * (world - 1)
+        elif a2a:
             st = {}
             o.copy_(epm.moe_block_a2a(kinds[i % nk], x, rank, world, ws=ws, stats=st))
             moved["sent"] += st["sent"]
@@ -464,7 +468,10 @@ def run_prefill_bench(args, cfg):
                    "tokens_per_step": T, "routing": routing, "H": 2048, "I": 512, "E": 256, "top_k": 8,
                    "l2": "inputs larger than L2: every step reads the whole expert bank (>= 0.8 GB)",
                    "tokens_per_step_per_gpu": T,
-                   "parallelism": ((f"ep{world} all-to-all ({256 // world} experts/GPU, NCCL all_to_all_single "
+                   "parallelism": ((f"ep{world} ({256 // world} experts/GPU; dispatch NCCL all_gather, combine "
+                                    "NCCL reduce_scatter of fp32 partials; shared expert on every rank for its "
+                                    "own tokens)" if args.prefill_par == "gather" else
+                                    f"ep{world} all-to-all ({256 // world} experts/GPU, NCCL all_to_all_single "
                                     "dispatch/combine, shared expert on every rank for its own tokens)")
                                    if a2a else "replica") if world > 1 else "single"},
         "e2e": {"value": e2e_tok_s, "unit": "tokens/s", "h2d_bytes_per_step": T * 2048 * 2,
@@ -485,9 +492,10 @@ def run_prefill_bench(args, cfg):
     }
     if a2a:
         mv = moved_timed
-        line["a2a_rows_per_step"] = {"sent": mv["sent"] / K, "received": mv["received"] / K,
-                                     "bytes_out": mv["sent"] / K * (2048 * 2 + 64),
-                                     "bytes_back": mv["sent"] / K * 2048 * 4, "rank": rank}
+        line["ep_rows_per_step"] = {"sent": mv["sent"] / K, "received": mv["received"] / K,
+                                    "bytes_out": mv["sent"] / K * (2048 * 2 + 64),
+                                    "bytes_back": mv["sent"] / K * 2048 * 4, "rank": rank,
+                                    "exchange": args.prefill_par}
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline_prefill(blocks, bits, budget_s=args.cpu_budget)
     if rank == 0:
@@ -972,8 +980,9 @@ def main():
     ap.add_argument("--soak", type=float, default=1.5)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--prefill-par", default="a2a", choices=["a2a", "replica"],
-                    help="prefill at N > 1: expert parallel with all-to-all, or whole-bank replicas")
+    ap.add_argument("--prefill-par", default="gather", choices=["gather", "a2a", "replica"],
+                    help="prefill at N > 1: expert parallel with gather/reduce-scatter or all-to-all exchange, "
+                         "or whole-bank replicas")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu captures (2 weight copies, plain launches)")
     ap.add_argument("--probe", default=None, choices=["qmv", "qmm"],

@@ -22,7 +22,11 @@ Two reductions are offered:
   library-collective baseline, any T.
 
 For throughput (every rank with its own tokens, e.g. a 16384-token prefill
-chunk per GPU) :func:`moe_block_a2a` dispatches instead of replicating: each
+chunk per GPU) two exchanges are offered.  :func:`moe_block_gather` needs no
+host synchronisation: every rank gathers all ranks' tokens with their routing
+(``all_gather``), runs its experts on the other ranks' rows, and the fp32
+partials are summed onto their home ranks (``reduce_scatter``).
+:func:`moe_block_a2a` sends only the rows each rank needs: each
 rank routes its tokens, runs its local experts and the whole shared expert on
 them, sends every token once to each other rank that holds one of its
 selected experts (with its full routing row), and the owners send back fp32
@@ -208,3 +212,62 @@ def moe_block_a2a(bt: BlockTensors, x: torch.Tensor, rank: int, world: int, grou
     back = _a2a_rows(y, recv, send, group)
     part.index_add_(0, t_idx, back)
     return part.to(torch.bfloat16).reshape(x.shape)
+
+
+def moe_block_gather(bt: BlockTensors, x: torch.Tensor, rank: int, world: int, group=None, k: int = 8,
+                     ws: Workspace | None = None, block_fn=None, experts_fn=None,
+                     gather_fn=None, reduce_scatter_fn=None):
+    """Expert-parallel block over this rank's own tokens (every rank the same
+    token count) with gather dispatch and reduce-scatter combine:
+
+    1. home: ``moe_block`` with fp32 output -> routing, this rank's selected
+       experts and the whole shared expert for its tokens, written into its
+       slot of a [world, T, H] fp32 partial;
+    2. dispatch: ``all_gather`` of every rank's rows (bf16 x, k ids, k fp32
+       weights as one int32 row);
+    3. remote: ``rnb_moe_experts_fwd`` on each other rank's rows (experts of
+       other shards are skipped, so a row none of whose experts is here costs
+       no tensor-core work) into that rank's slot;
+    4. combine: ``reduce_scatter`` (sum) of the partial: each rank gets the
+       sum for its own tokens, rounded to bf16 once.
+
+    ``block_fn``/``experts_fn`` replace the device calls and
+    ``gather_fn(out, inp)`` / ``reduce_scatter_fn(out, inp)`` the collectives
+    (host tests)."""
+    import torch.distributed as dist
+
+    from .ops import experts_fwd, moe_block
+
+    xt = _tokens(x, bt.H)
+    T, H = xt.shape
+    Et = bt.E_total if bt.E_total is not None else bt.E
+    if bt.E * world != Et or bt.expert_offset != rank * bt.E:
+        raise ValueError(f"shard [{bt.expert_offset}, +{bt.E}) is not rank {rank}'s of {Et} experts over {world}")
+    gather_fn = gather_fn or (lambda out, inp: dist.all_gather_into_tensor(out, inp, group=group))
+    reduce_scatter_fn = reduce_scatter_fn or (
+        lambda out, inp: dist.reduce_scatter_tensor(out, inp, op=dist.ReduceOp.SUM, group=group))
+    f32 = BlockTensors(**{**bt.__dict__, "flags": bt.flags | _lib.FLAG_Y_F32})
+    part = torch.empty((world, T, H), dtype=torch.float32, device=xt.device)
+    if block_fn is None:
+        _, inds, scores = moe_block(f32, xt, k=k, ws=ws, return_routing=True, out=part[rank])
+    else:
+        home, inds, scores = block_fn(f32, xt)
+        part[rank].copy_(home)
+    hw = H // 2
+    rows = torch.cat([xt.view(torch.int32), inds.to(torch.int32), scores.view(torch.int32)], dim=1).contiguous()
+    allrows = torch.empty((world,) + tuple(rows.shape), dtype=torch.int32, device=xt.device)
+    gather_fn(allrows, rows)
+    for q in range(world):
+        if q == rank:
+            continue
+        rq = allrows[q]
+        xq = rq[:, :hw].contiguous().view(torch.bfloat16)
+        iq = rq[:, hw:hw + k].contiguous()
+        sq = rq[:, hw + k:].contiguous().view(torch.float32)
+        if experts_fn is None:
+            experts_fwd(bt, xq, iq, sq, out=part[q])
+        else:
+            part[q].copy_(experts_fn(bt, xq, iq, sq))
+    out = torch.empty((T, H), dtype=torch.float32, device=xt.device)
+    reduce_scatter_fn(out, part.view(world * T, H))
+    return out.to(torch.bfloat16).reshape(x.shape)

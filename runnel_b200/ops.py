@@ -211,15 +211,20 @@ def moe_block(bt: BlockTensors, x: torch.Tensor, k: int = 8, ws: Workspace | Non
 
 
 def experts_fwd(bt: BlockTensors, x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor,
-                out_f32: bool = True, ws: torch.Tensor | None = None) -> torch.Tensor:
+                out_f32: bool = True, ws: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
     """Routed experts of this shard with given routing: [T, H] bf16 rows,
     [T, k] int32 global expert ids and fp32 weights -> [T, H] weighted sum over
-    the ids this shard holds (fp32 by default).  No router, no shared expert."""
+    the ids this shard holds (fp32 by default; ``out``, contiguous, receives
+    it in place).  No router, no shared expert."""
     xt = _tokens(x, bt.H)
     T, k = inds.shape
     flags = (bt.flags | _lib.FLAG_Y_F32) if out_f32 else (bt.flags & ~_lib.FLAG_Y_F32)
     d = BlockTensors(**{**bt.__dict__, "flags": flags}).desc(T, k)
-    out = torch.empty(xt.shape, dtype=torch.float32 if out_f32 else torch.bfloat16, device=xt.device)
+    dt = torch.float32 if out_f32 else torch.bfloat16
+    if out is None:
+        out = torch.empty(xt.shape, dtype=dt, device=xt.device)
+    elif out.dtype != dt or out.numel() != xt.numel() or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {dt} tensor with x's number of elements")
     if T == 0:
         return out
     need = ctypes.c_size_t()

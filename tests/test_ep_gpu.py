@@ -106,6 +106,17 @@ def _rank_main(rank, world, port):
             if xr.shape[0]:
                 assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(), f"ep a2a rank {rank} case {i}")
             assert stats["sent"] <= xr.shape[0] * (world - 1)
+            if t0 == t1:  # the gather / reduce-scatter form needs equal token counts
+                got = ep.moe_block_gather(shard, xr, rank, world, ws=ws)
+                if xr.shape[0]:
+                    assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(),
+                                 f"ep gather rank {rank} case {i}")
+        g.manual_seed(7 + rank)
+        xr = torch.randn((200, blk.H), device=dev, generator=g).to(torch.bfloat16)
+        dist.barrier(group=gloo)
+        got = ep.moe_block_gather(shard, xr, rank, world, ws=ws)
+        want = ops.moe_block(full, xr, ws=ws)
+        assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(), f"ep gather rank {rank} T=200")
         assert ws.status() == 0
         torch.cuda.synchronize()
         dist.barrier()

@@ -161,8 +161,7 @@ def _a2a_rank_main(rank, world, port):
                 return torch.zeros((0, bt.H), dtype=torch.float32)
             xb = x.view(torch.int16).numpy().view(np.uint16)
             ind = inds.numpy()
-            # a received row always holds at least one of this shard's experts
-            assert (((ind >= lo) & (ind < hi)).any(axis=1)).all()
+            seen["all_local"] = bool((((ind >= lo) & (ind < hi)).any(axis=1)).all())
             y = oracle.switchglu(w, xb, ind.astype(np.uint32))
             local = (ind >= lo) & (ind < hi)
             return torch.from_numpy(np.einsum("tk,tkh->th", np.where(local, scores.numpy(), 0.0)
@@ -175,9 +174,28 @@ def _a2a_rank_main(rank, world, port):
         err = np.abs(out.float().numpy() - ref).max() / np.abs(ref).max()
         assert err < 1e-2, err
         assert stats["received"] == seen["rows"]
+        assert seen.get("all_local", True)  # the all-to-all sends only rows with an expert here
         tot = torch.tensor([stats["sent"], stats["received"]])
         dist.all_reduce(tot)
         assert tot[0] == tot[1]  # every row sent is received once
+        # gather / reduce-scatter form (equal token counts on every rank)
+        eq = blk.x[rank * 2:(rank + 1) * 2]
+        xe = torch.from_numpy(eq).view(torch.int16).view(torch.bfloat16)
+
+        def gather(outb, inp):
+            parts = list(outb.unbind(0))
+            dist.all_gather(parts, inp)
+
+        def reduce_scatter(outb, inp):
+            full = inp.clone()
+            dist.all_reduce(full)
+            outb.copy_(full.view(world, -1, full.shape[-1])[rank])
+
+        out = ep.moe_block_gather(shard, xe, rank, world, block_fn=block_fn, experts_fn=experts_fn,
+                                  gather_fn=gather, reduce_scatter_fn=reduce_scatter)
+        ref, _, _ = oracle.moe_block(w, eq, k=8)
+        err = np.abs(out.float().numpy() - ref).max() / np.abs(ref).max()
+        assert err < 1e-2, err
         dist.barrier()
     finally:
         dist.destroy_process_group()
