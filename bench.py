@@ -633,8 +633,9 @@ def run_stack_bench(args, cfg):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm * world, "unit": "GB/s",
                      "frac": achieved / (hbm * world), "peak_source": f"{src} x {world} GPU",
                      "traffic": None, "algorithmic_bytes_per_step": per_tok,
-                     "kernel": "k_decode + k_add_rmsnorm per layer"},
-        "gpu_launches": K * (2 * L + 1),
+                     "kernel": "k_decode per layer (residual add + RMSNorm fused into its prologue), "
+                               "one k_add_rmsnorm per token (the last residual add)"},
+        "gpu_launches": K * (L + 1),
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu:

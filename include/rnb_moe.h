@@ -233,6 +233,18 @@ RNB_API int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* 
 RNB_API int rnb_add_rmsnorm(const void* x, const void* y, const void* w, void* x_out, void* xn_out, int T, int H,
                             float eps, void* stream);
 
+/* One decoder layer's glue plus block (no reference counterpart; the layer
+ * glue of the 40-layer configuration):
+ *   resid_out = bf16(resid + y_prev)            (y_prev may be NULL: a copy)
+ *   xn_out    = bf16(rms_norm(resid_out) * norm_w)   (as rnb_add_rmsnorm)
+ *   out       = block(xn_out)                   (expert parallel when ep != NULL)
+ * bit-identical to rnb_add_rmsnorm followed by the block call.  For 1-2 tokens
+ * the glue runs inside the block's single persistent launch.  resid_out and
+ * xn_out must not alias resid or y_prev; out may alias y_prev. */
+RNB_API int rnb_moe_block_norm_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* resid, const void* y_prev,
+                                   const void* norm_w, float eps, void* resid_out, void* xn_out, void* out,
+                                   void* ws, size_t ws_bytes, void* stream);
+
 /* Per-stage device timing (diagnostics; no reference counterpart -- the
  * reference profiles its block from the host, bench/mlx_component_profile.py).
  * While enabled, every block call records CUDA events on its stream between

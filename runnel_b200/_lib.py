@@ -75,6 +75,8 @@ SIGNATURES = {
     "rnb_ep_connect": (ctypes.c_int, [_vp, _vp]),
     "rnb_ep_destroy": (ctypes.c_int, [_vp]),
     "rnb_moe_block_ep_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "rnb_moe_block_norm_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _sz,
+                                              _vp]),
     "rnb_add_rmsnorm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
     "rnb_stage_timing": (ctypes.c_int, [ctypes.c_int]),
     "rnb_stage_times": (ctypes.c_int, [ctypes.POINTER(ctypes.c_float), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),

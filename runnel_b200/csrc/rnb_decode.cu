@@ -90,6 +90,16 @@ struct Params {
   int ep_world, ep_rank;
   uint2* ep_recv[kMaxEpRanks];
   uint32_t* ep_seq;  // [0] sequence word, [1] exit counter of k_ep_reduce
+  // Fused layer glue (persistent kernel, norm_w non-null): the block input
+  // is xn = bf16(rms_norm(r) * norm_w) with r = bf16(resid + y_prev) (y_prev
+  // may be null); r goes to resid_out and xn to xn_out.  resid_out must not
+  // alias resid or y_prev (other CTAs are still reading them).
+  const uint16_t* resid;
+  const uint16_t* y_prev;
+  const uint16_t* norm_w;
+  float norm_eps;
+  uint16_t* resid_out;
+  uint16_t* xn_out;
 };
 
 // Optional phase timeline (compile with -DRNB_TRACE): thread 0 of each CTA
@@ -962,6 +972,7 @@ struct PPlan {
   int cb;        // phase-C tasks staged together per warp
   int n_rtiles;  // router tiles of 16 rows (E_total + 1 rows)
   uint32_t off_x, off_xs, off_br, off_cr, off_h, off_red, off_redc, off_misc;
+  uint32_t off_xn;  // fused glue: the normalised tokens [T][H] bf16
 };
 
 struct PTask {
@@ -1041,7 +1052,7 @@ __device__ void xprep_cta(const uint16_t* x, int T, uint32_t* sX, float* sXs, fl
   constexpr int H = 2048, G = H / kGroup;
 #pragma unroll 1
   for (int t = 0; t < T; ++t) {
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(x + static_cast<size_t>(t) * H) + tid);
+    const uint2 u = reinterpret_cast<const uint2*>(x + static_cast<size_t>(t) * H)[tid];  // global or shared
     const float v[4] = {__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
                         __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u)};
     const float m4 = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
@@ -1283,6 +1294,45 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
   cp_async_commit();  // group: shared down
   RNB_TRACE_MARK(p, 1);
   griddep_wait();  // x may come from the previous kernel on the stream
+  // Fused layer glue: this CTA's own copy of the normalised tokens.  The sum
+  // of squares runs exactly as in rnb_add_rmsnorm (threads 0..255 striding by
+  // 256, a shuffle tree, the 8 warp sums in order), so both paths give the
+  // same bits.  CTA 0 also writes the residual sum and the normalised tokens.
+  const uint16_t* xin = p.x;
+  if (p.norm_w) {
+    uint16_t* sXn = reinterpret_cast<uint16_t*>(sm + pl.off_xn);
+    for (int t = 0; t < T; ++t) {
+      const size_t b = static_cast<size_t>(t) * p.H;
+      if (tid < 256) {
+        float ss = 0.f;
+        for (int i = tid; i < p.H; i += 256) {
+          float v = bf16_bits_to_f32(p.resid[b + i]);
+          if (p.y_prev) v = bf16_round(v + bf16_bits_to_f32(p.y_prev[b + i]));
+          sXn[b + i] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+          ss = fmaf(v, v, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if ((tid & 31) == 0) ms->red[tid >> 5] = ss;
+      }
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) tot += ms->red[i];
+      const float r = rsqrtf(tot / static_cast<float>(p.H) + p.norm_eps);
+      for (int i = tid; i < p.H; i += blockDim.x) {
+        const uint16_t rv = sXn[b + i];
+        const uint16_t xn = __bfloat16_as_ushort(__float2bfloat16_rn(bf16_bits_to_f32(rv) * r * bf16_bits_to_f32(p.norm_w[i])));
+        if (cta == 0) {
+          p.resid_out[b + i] = rv;
+          if (p.xn_out) p.xn_out[b + i] = xn;
+        }
+        sXn[b + i] = xn;
+      }
+      __syncthreads();
+    }
+    xin = sXn;
+  }
   {
     // Per lane 4 products per (row, token), summed with FMAs, then a 5-level
     // shuffle tree and a 4-level tree over the warps: at most 12 roundings of
@@ -1292,7 +1342,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     float xf[2][4];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      const uint2 xv = t < T ? __ldg(reinterpret_cast<const uint2*>(p.x + static_cast<size_t>(t) * p.H + k0r))
+      const uint2 xv = t < T ? *reinterpret_cast<const uint2*>(xin + static_cast<size_t>(t) * p.H + k0r)
                              : make_uint2(0, 0);
       xf[t][0] = __uint_as_float(xv.x << 16);
       xf[t][1] = __uint_as_float(xv.x & 0xFFFF0000u);
@@ -1365,7 +1415,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     if (tid == 0) arrive_release(bar1);
     RNB_TRACE_MARK(p, 2);
   }
-  xprep_cta<BITS>(p.x, T, sX, sXs, ms->xinv, reinterpret_cast<__half*>(sH), ms->red);
+  xprep_cta<BITS>(xin, T, sX, sXs, ms->xinv, reinterpret_cast<__half*>(sH), ms->red);
 
   if (owns_sgu) {
     cp_async_wait_pending(1);  // the shared-down group may still be in flight
@@ -1393,7 +1443,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     int e;
     float sc;
     RNB_TRACE_MARK(p, 12);
-    const int nre = warp_route_token_body(ivl, Et, K, p.x + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane,
+    const int nre = warp_route_token_body(ivl, Et, K, xin + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane,
                                           false, nullptr, &e, &sc);
     RNB_TRACE_MARK(p, 13);
 #ifdef RNB_TRACE
@@ -1911,6 +1961,7 @@ bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem
     o = (o + bytes + 127) & ~static_cast<size_t>(127);
     return static_cast<uint32_t>(at);
   };
+  pl.off_xn = p.norm_w ? take(static_cast<size_t>(T) * p.H * 2) : 0u;
   pl.off_x = take(static_cast<size_t>(T) * G * 32 * 4);
   pl.off_xs = take(static_cast<size_t>(T) * G * 4);
   pl.off_misc = take(sizeof(PMisc));
@@ -2420,3 +2471,53 @@ int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* x, void*
 }
 
 }  // extern "C"
+
+int rnb_moe_block_norm_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* resid, const void* y_prev,
+                           const void* norm_w, float eps, void* resid_out, void* xn_out, void* out, void* ws,
+                           size_t ws_bytes, void* stream) {
+  using namespace rnb;
+  int rc = validate(d, true, true);
+  if (!rc) rc = check_device();
+  if (!rc) rc = check_ws(d, ws, ws_bytes);
+  if (rc) return rc;
+  if (!resid || !norm_w || !resid_out || !xn_out || !out)
+    return fail(RNB_ERR_INVALID, "resid, norm_w, resid_out, xn_out and out must be non-NULL");
+  if (!aligned16(resid) || !aligned16(resid_out) || !aligned16(xn_out) || !aligned16(out) ||
+      (y_prev && !aligned16(y_prev)))
+    return fail(RNB_ERR_ALIGN, "resid, y_prev, resid_out, xn_out and out must be 16-byte aligned");
+  if (resid_out == resid || resid_out == y_prev || xn_out == resid || xn_out == y_prev)
+    return fail(RNB_ERR_INVALID, "resid_out and xn_out must not alias resid or y_prev");
+  if (ep && ep->world > 1 && !ep->connected) return fail(RNB_ERR_INVALID, "call rnb_ep_connect first");
+  if (ep && d->H != ep->H) return fail(RNB_ERR_INVALID, "H differs from the EP context's");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // One persistent launch when the plan fits: the glue runs in its prologue.
+  if (!(d->flags & RNB_FLAG_CHAIN)) {
+    Params p = base_params(d, resid, ws, kModeBlock);
+    p.out = out;
+    p.resid = static_cast<const uint16_t*>(resid);
+    p.y_prev = static_cast<const uint16_t*>(y_prev);
+    p.norm_w = static_cast<const uint16_t*>(norm_w);
+    p.norm_eps = eps;
+    p.resid_out = static_cast<uint16_t*>(resid_out);
+    p.xn_out = static_cast<uint16_t*>(xn_out);
+    if (ep) {
+      const int nq = d->I / 128;
+      p.shared_qmask = 0;
+      for (int q = ep->rank; q < nq; q += ep->world) p.shared_qmask |= 1u << q;
+      p.ep_world = ep->world;
+      p.ep_rank = ep->rank;
+      for (int q = 0; q < ep->world; ++q) p.ep_recv[q] = ep->recv[q];
+      p.ep_seq = ep->seq;
+    }
+    const DevInfo di = dev_info();
+    PPlan pl;
+    size_t smem = 0;
+    const bool ok = d->bits == 8 ? persistent_plan<8>(p, di, pl, smem) : persistent_plan<4>(p, di, pl, smem);
+    if (ok) return d->bits == 8 ? run_persistent<8>(p, pl, smem, di.sms, st) : run_persistent<4>(p, pl, smem, di.sms, st);
+  }
+  // Otherwise the glue kernel, then the block on its output.
+  rc = rnb_add_rmsnorm(resid, y_prev, norm_w, resid_out, xn_out, d->T, d->H, eps, stream);
+  if (rc) return rc;
+  return ep ? rnb_moe_block_ep_fwd(d, ep, xn_out, out, nullptr, nullptr, ws, ws_bytes, stream)
+            : rnb_moe_block_fwd(d, xn_out, out, nullptr, nullptr, ws, ws_bytes, stream);
+}

@@ -150,7 +150,7 @@ static __device__ __noinline__ double warp_dot_f64(const uint16_t* x, const uint
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int k = k0 + j * 256 + lane * 8;
-      xv[j] = k < H ? __ldg(reinterpret_cast<const uint4*>(x + k)) : make_uint4(0, 0, 0, 0);
+      xv[j] = k < H ? *reinterpret_cast<const uint4*>(x + k) : make_uint4(0, 0, 0, 0);  // x: global or shared
       wv[j] = k < H ? __ldg(reinterpret_cast<const uint4*>(w + k)) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll

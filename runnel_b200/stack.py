@@ -5,8 +5,10 @@
 with bf16 activations between layers (mlx-lm's Qwen3.5 decoder layer without
 attention: ``h = x + mlp(post_attention_layernorm(x))``).  Each layer is one
 :class:`runnel_b200.ops.BlockTensors` (or this rank's expert shard of it) and a
-bf16 RMSNorm weight; the glue between blocks is one fused kernel
-(``rnb_add_rmsnorm``: residual add, then the next layer's norm).  With an
+bf16 RMSNorm weight.  A layer is one call, ``rnb_moe_block_norm_fwd``: the
+residual add of the previous block's output and this layer's norm, then the
+block; for one or two tokens the glue runs inside the block's persistent
+launch (bit-identical to ``rnb_add_rmsnorm`` + block).  With an
 :class:`runnel_b200.ep.ExpertParallel` context every block call is expert
 parallel: each rank holds its shard of every layer and all ranks end with
 the same activations.
@@ -19,7 +21,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .ops import BlockTensors, Workspace, _ptr, _stream, moe_block
+from .ops import BlockTensors, Workspace, _ptr, _stream
 
 RMS_EPS = 1e-6
 
@@ -42,11 +44,18 @@ class LayerStack:
         self.layers, self.norm_w, self.eps, self.ep = layers, norm_w, eps, ep
         self.ws = ws
 
-    def _block(self, bt: BlockTensors, xn: torch.Tensor, y: torch.Tensor) -> None:
-        if self.ep is not None:
-            self.ep.moe_block(bt, xn, ws=self.ws, out=y)
-        else:
-            moe_block(bt, xn, ws=self.ws, out=y)
+    def _layer(self, bt: BlockTensors, resid, y_prev, w, resid_out, xn, y) -> None:
+        """resid_out = resid + y_prev, xn = norm(resid_out) * w, y = block(xn)."""
+        from .ops import default_workspace
+        T = resid.shape[0]
+        d = bt.desc(T, 8)
+        ws = self.ws or default_workspace(resid.device)
+        wp, wn = ws.get(d)
+        ep = self.ep._ep if self.ep is not None else None
+        if self.ep is not None and not ep:
+            raise RuntimeError("ExpertParallel context is closed")
+        _lib.call("rnb_moe_block_norm_fwd", ctypes.byref(d), ep, _ptr(resid), _ptr(y_prev), _ptr(w),
+                  ctypes.c_float(self.eps), _ptr(resid_out), _ptr(xn), _ptr(y), wp, wn, _stream())
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, record: list | None = None) -> torch.Tensor:
         """[T, H] bf16 -> [T, H] bf16.  ``record`` (a list) receives per layer
@@ -54,18 +63,18 @@ class LayerStack:
         T, H = x.shape
         if out is None:
             out = torch.empty_like(x)
-        xa = out  # running residual stream
+        resid_bufs = (torch.empty_like(x), torch.empty_like(x))  # the residual stream, alternating
         xn = torch.empty_like(x)
         y = torch.empty_like(x)
-        add_rmsnorm(x, None, self.norm_w[0], xa, xn, self.eps)
+        resid, y_prev = x, None
         for l, bt in enumerate(self.layers):
+            r_out = resid_bufs[l % 2]
+            self._layer(bt, resid, y_prev, self.norm_w[l], r_out, xn, y)
             if record is not None:
-                record.append([xa.clone(), xn.clone(), None])
-            self._block(bt, xn, y)
-            if record is not None:
-                record[-1][2] = y.clone()
-            w_next = self.norm_w[l + 1] if l + 1 < len(self.layers) else self.norm_w[l]
-            add_rmsnorm(xa, y, w_next, xa, xn, self.eps)
+                record.append([r_out.clone(), xn.clone(), y.clone()])
+            resid, y_prev = r_out, y
+        # the last block's residual add (its norm output is not used)
+        add_rmsnorm(resid, y, self.norm_w[-1], out, xn, self.eps)
         return out
 
 

@@ -104,3 +104,24 @@ def test_stack_graph_replay_chains_tokens():
         g.replay()
         torch.cuda.synchronize()
         assert torch.equal(xout, eager[i])
+
+
+@pytest.mark.parametrize("T", [1, 2, 3])
+def test_fused_layer_glue_is_bit_identical(T):
+    """rnb_moe_block_norm_fwd (glue inside the persistent launch for T <= 2, the
+    glue kernel then the block otherwise) equals rnb_add_rmsnorm + the block."""
+    L, bits = 3, 4
+    blks = [inputs.make_block(bits, seed=4000 + l, T=T) for l in range(L)]
+    layers = [ops.BlockTensors.from_numpy(b, DEV) for b in blks]
+    norms = [_dev(f32_to_bf16_bits(b.norm_w)) for b in blks]
+    x = _dev(blks[0].x)
+    fused = stack.LayerStack(layers, norms, ws=ops.Workspace(DEV)).forward(x)
+    xa = torch.empty_like(x)
+    xn = torch.empty_like(x)
+    y = torch.empty_like(x)
+    ws = ops.Workspace(DEV)
+    stack.add_rmsnorm(x, None, norms[0], xa, xn)
+    for l in range(L):
+        ops.moe_block(layers[l], xn, ws=ws, out=y)
+        stack.add_rmsnorm(xa, y, norms[l + 1] if l + 1 < L else norms[l], xa, xn)
+    assert torch.equal(_dev(_bits(fused)), _dev(_bits(xa)))
