@@ -136,9 +136,9 @@ RNB_API int rnb_switchglu_fwd(const rnb_moe_desc* d, const void* x, const uint32
  * are optional copies of the routing (NULL to skip).  Up to 64 tokens run the
  * decode kernels; more tokens run the sorted grouped-GEMM path (tensor-core
  * tcgen05 GEMMs) when the workspace has rnb_moe_workspace_size() bytes for
- * this T, else the decode kernels in 64-token chunks.  The grouped-GEMM path
- * sums the experts' contributions with fp32 atomics, so repeated calls agree
- * to fp32 rounding of that sum rather than bit for bit. */
+ * this T, else the decode kernels in 64-token chunks.  Both paths add a
+ * token's expert contributions in slot order, so repeated calls give the same
+ * bits. */
 RNB_API int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out,
                       float* scores_out, void* ws, size_t ws_bytes, void* stream);
 
