@@ -1,10 +1,12 @@
 // rnb_prefill.cu -- sparse-MoE block for many tokens (prefill) on tcgen05.
 //
-//   k_pre_route    router logits (mma.sync bf16, 32 tokens per CTA, x staged
-//                  in shared memory) with exact bf16 rounding (rnb_route.cuh),
-//                  top-k, softmax weights, shared-expert gate, per-token
-//                  power-of-two scale into fp16 range, the scaled fp16 copy
-//                  of the tokens, and a per-expert token histogram.
+//   k_route_gemm   router logits of 128 tokens x 128 experts per CTA on
+//                  tcgen05 (bf16, fp32 TMEM accumulation in four K quarters
+//                  added in fp64) and the router rows' norms.
+//   k_pre_select   a warp per token: candidate intervals of the bf16 logits
+//                  (rnb_route.cuh), exact top-k, softmax weights,
+//                  shared-expert gate, power-of-two fp16 scale and fp16 copy
+//                  of the token, per-expert token histogram.
 //   k_pre_sort     one CTA: per-expert row bases padded to 128 rows and the
 //                  list of 256-row work tiles (the shared expert is expert E,
 //                  all tokens).
@@ -44,7 +46,6 @@ namespace pre {
 
 constexpr int kTileM = 128;  // MMA M; expert rows are padded to multiples of it
 constexpr int kItemM = 256;  // rows of a GEMM work item: two M tiles sharing one dequantised B tile
-constexpr int kRouteT = 32;     // tokens per router CTA
 constexpr int kProducerWarps = 8;
 constexpr int kMmaWarp = 8;
 // warps 9..12: epilogue, one per TMEM lane quadrant (warp % 4); warp 13: TMA loader
@@ -69,6 +70,8 @@ struct Ws {
   __half* h16;       // [rows_cap][I] SwiGLU activations, one scale per row after k_pre_hrow
   float* hinv;       // [rows_cap][I/64] inverse scale of each 64-channel chunk
   float* hrow;       // [rows_cap] inverse scale of the row (largest chunk inverse scale)
+  uint32_t* lg;      // [T][E_total+1] fp32 router logits (tcgen05 router; the last column unused)
+  float* wn;         // [2][E_total] router rows' sums of squares and of absolute values
   __half* y16;       // [rows_cap][H] down outputs times their weight, fp16, one scale per (row, n-tile)
   float* yinv;       // [rows_cap][H/128] inverse of that scale
   uint32_t* rowpos;  // [T][K+1] sorted row of entry t*(K+1)+slot, 0xFFFFFFFF if none
@@ -140,233 +143,6 @@ __device__ __forceinline__ uint32_t bf16_to_half2_dup(uint16_t b) {
 }
 
 // ------------------------------------------------------------ router
-
-constexpr int kXStride = 160;  // bf16 per staged x row (128 + 32 pad: conflict-free 16-byte reads)
-
-constexpr size_t kRouteXsBytes = 2ull * kRouteT * kXStride * 2;
-constexpr size_t kRouteLgBytes = static_cast<size_t>(kRouteT) * (kMaxE + 1) * 4;
-constexpr size_t kRouteSmem = kRouteXsBytes > kRouteLgBytes ? kRouteXsBytes : kRouteLgBytes;
-
-__global__ void __launch_bounds__(512) k_pre_route(Params p) {
-  // x staging (K loop) and the logits (after it) share one dynamic buffer
-  extern __shared__ __align__(16) char rsm[];
-  uint16_t (*xs)[kRouteT][kXStride] = reinterpret_cast<uint16_t (*)[kRouteT][kXStride]>(rsm);
-  float (*lg)[kMaxE + 1] = reinterpret_cast<float (*)[kMaxE + 1]>(rsm);
-  __shared__ uint32_t xmax[kRouteT];
-  __shared__ float xn2[kRouteT];
-  __shared__ uint32_t hist[kMaxE];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-  const int t0 = blockIdx.x * kRouteT;
-  const int nt = p.T - t0 < kRouteT ? p.T - t0 : kRouteT;
-  const int Et = p.E_total, K = p.k, H = p.H;
-  const int nkc = H / 128;
-  for (int i = tid; i < kMaxE; i += blockDim.x) hist[i] = 0;
-  if (tid < kRouteT) {
-    xmax[tid] = 0;
-    xn2[tid] = 0.f;
-  }
-  auto stage = [&](int kc, int buf) {
-    // kRouteT rows x 128 bf16 = 16-byte pieces, one per thread
-    for (int q = tid; q < kRouteT * 16; q += blockDim.x) {
-      const int r = q >> 4, piece = q & 15;
-      const int tr = r < nt ? r : 0;
-      cp_async16(&xs[buf][r][piece * 8], p.x + static_cast<size_t>(t0 + tr) * H + kc * 128 + piece * 8);
-    }
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-  };
-  static_assert(kRouteT * 16 == 512, "one 16-byte piece of one token per thread and chunk");
-  float xm_acc = 0.f, xs_acc = 0.f;
-  constexpr int kNC = kRouteT / 8;  // 8-token MMA column blocks
-  // Each 128-wide K chunk accumulates in fp32 (8 MMA steps), the chunks in
-  // fp64: the logit error stays within kRouteRelPrefill (8 steps, not 128).
-  float acc[kNC][4];
-  double accd[kNC][4];
-#pragma unroll
-  for (int n = 0; n < kNC; ++n) {
-    acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-    accd[n][0] = accd[n][1] = accd[n][2] = accd[n][3] = 0.0;
-  }
-  float wa2 = 0.f, wa1 = 0.f, wb2 = 0.f, wb1 = 0.f;  // norms of rows row_a, row_b (lane's quarter)
-  const int row_a = warp * 16 + g, row_b = row_a + 8;
-  const uint16_t* wa = row_a < Et ? p.router_w + static_cast<size_t>(row_a) * H : nullptr;
-  const uint16_t* wb = row_b < Et ? p.router_w + static_cast<size_t>(row_b) * H : nullptr;
-  uint4 na0[4], na1[4];  // router rows of the next 128-wide chunk, in flight during this one
-  auto load_w = [&](int kc) {
-    const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      const int k0 = kc * 128 + ch * 32 + 8 * c;
-      na0[ch] = wa ? __ldg(reinterpret_cast<const uint4*>(wa + k0)) : z;
-      na1[ch] = wb ? __ldg(reinterpret_cast<const uint4*>(wb + k0)) : z;
-    }
-  };
-  load_w(0);
-  stage(0, 0);
-  for (int kc = 0; kc < nkc; ++kc) {
-    if (kc + 1 < nkc) {
-      stage(kc + 1, (kc + 1) & 1);
-      asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-    }
-    __syncthreads();
-    const int buf = kc & 1;
-    // per-token max |x| and sum of squares: thread tid always sees 16-byte
-    // piece tid % 16 of token tid / 16, so it accumulates in registers
-    {
-      const uint4 v = *reinterpret_cast<const uint4*>(&xs[buf][tid >> 4][(tid & 15) * 8]);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xFFFF0000u);
-        xm_acc = fmaxf(xm_acc, fmaxf(fabsf(lo), fabsf(hi)));
-        xs_acc = fmaf(lo, lo, fmaf(hi, hi, xs_acc));
-      }
-    }
-    if (warp * 16 < Et) {
-      // this chunk's router rows were loaded during the previous chunk; start the next
-      uint4 ca0[4], ca1[4];
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        ca0[ch] = na0[ch];
-        ca1[ch] = na1[ch];
-      }
-      if (kc + 1 < nkc) load_w(kc + 1);
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        const uint4 a0 = ca0[ch];
-        const uint4 a1 = ca1[ch];
-        {
-          const uint32_t av[4] = {a0.x, a0.y, a0.z, a0.w}, bv[4] = {a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float x0 = __uint_as_float(av[j] << 16), x1 = __uint_as_float(av[j] & 0xFFFF0000u);
-            const float y0 = __uint_as_float(bv[j] << 16), y1 = __uint_as_float(bv[j] & 0xFFFF0000u);
-            wa2 = fmaf(x0, x0, fmaf(x1, x1, wa2));
-            wa1 += fabsf(x0) + fabsf(x1);
-            wb2 = fmaf(y0, y0, fmaf(y1, y1, wb2));
-            wb1 += fabsf(y0) + fabsf(y1);
-          }
-        }
-#pragma unroll
-        for (int n = 0; n < kNC; ++n) {
-          const uint4 bx = *reinterpret_cast<const uint4*>(&xs[buf][n * 8 + g][ch * 32 + 8 * c]);
-          mma_bf16(acc[n], a0.x, a1.x, a0.y, a1.y, bx.x, bx.y);
-          mma_bf16(acc[n], a0.z, a1.z, a0.w, a1.w, bx.z, bx.w);
-        }
-      }
-#pragma unroll
-      for (int n = 0; n < kNC; ++n)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          accd[n][j] += static_cast<double>(acc[n][j]);
-          acc[n][j] = 0.f;
-        }
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) {
-    xm_acc = fmaxf(xm_acc, __shfl_xor_sync(0xffffffffu, xm_acc, o));
-    xs_acc += __shfl_xor_sync(0xffffffffu, xs_acc, o);
-  }
-  if ((tid & 15) == 0) {
-    xmax[tid >> 4] = __float_as_uint(xm_acc);
-    xn2[tid >> 4] = xs_acc;
-  }
-  __syncthreads();
-  // fp16 copy of the tokens times their power-of-two scale (gate/up A operand)
-  {
-    __shared__ float xsc[kRouteT];
-    if (tid < kRouteT) {
-      float sc, inv;
-      fp16_range_scale(__uint_as_float(xmax[tid]), sc, inv);
-      xsc[tid] = sc;
-    }
-    __syncthreads();
-    const int n8 = H / 8;
-    for (int q = tid; q < nt * n8; q += blockDim.x) {
-      const int t = q / n8, c8 = q % n8;
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t0 + t) * H) + c8);
-      const float sc = xsc[t];
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        o[j] = half2_bits(__uint_as_float(w[j] << 16) * sc, __uint_as_float(w[j] & 0xFFFF0000u) * sc);
-      reinterpret_cast<uint4*>(p.ws.x16 + static_cast<size_t>(t0 + t) * H)[c8] = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-  }
-#pragma unroll
-  for (int o = 1; o <= 2; o <<= 1) {
-    wa2 += __shfl_xor_sync(0xffffffffu, wa2, o);
-    wa1 += __shfl_xor_sync(0xffffffffu, wa1, o);
-    wb2 += __shfl_xor_sync(0xffffffffu, wb2, o);
-    wb1 += __shfl_xor_sync(0xffffffffu, wb1, o);
-  }
-  if (warp * 16 < Et) {
-    // candidate intervals of the bf16 logits (rnb_route.cuh)
-    uint32_t(*lgu)[kMaxE + 1] = reinterpret_cast<uint32_t(*)[kMaxE + 1]>(rsm);
-#pragma unroll
-    for (int n = 0; n < kNC; ++n) {
-      const int tA = n * 8 + 2 * c, tB = tA + 1;
-      const float xiA = __uint_as_float(xmax[tA]), xiB = __uint_as_float(xmax[tB]);
-      if (row_a < Et) {
-        lgu[tA][row_a] = route_interval(static_cast<float>(accd[n][0]), xn2[tA], xiA, wa2, wa1, kRouteRelPrefill);
-        lgu[tB][row_a] = route_interval(static_cast<float>(accd[n][1]), xn2[tB], xiB, wa2, wa1, kRouteRelPrefill);
-      }
-      if (row_b < Et) {
-        lgu[tA][row_b] = route_interval(static_cast<float>(accd[n][2]), xn2[tA], xiA, wb2, wb1, kRouteRelPrefill);
-        lgu[tB][row_b] = route_interval(static_cast<float>(accd[n][3]), xn2[tB], xiB, wb2, wb1, kRouteRelPrefill);
-      }
-    }
-  }
-  // shared-expert gate logit: fp32 dot per token (warp per token)
-  if (p.has_shared) {
-    for (int t = warp; t < nt; t += 16) {
-      const uint16_t* xr = p.x + static_cast<size_t>(t0 + t) * H;
-      float s = 0.f;
-      for (int k = lane * 8; k < H; k += 256) {
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xr + k));
-        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.sgate_w + k));
-        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          s = fmaf(__uint_as_float(xw[j] << 16), __uint_as_float(ww[j] << 16), s);
-          s = fmaf(__uint_as_float(xw[j] & 0xFFFF0000u), __uint_as_float(ww[j] & 0xFFFF0000u), s);
-        }
-      }
-      s = warp_sum(s);
-      if (lane == 0) lg[t][Et] = s;
-    }
-  }
-  __syncthreads();
-  // selection per token (warp per token), exact bf16 logits (rnb_route.cuh)
-  for (int t = warp; t < nt; t += 16) {
-    const size_t tg = static_cast<size_t>(t0 + t);
-    int e;
-    float sc;
-    warp_route_token(reinterpret_cast<const uint32_t*>(lg[t]), Et, K, p.x + tg * H, p.router_w, H, lane, false,
-                     nullptr, &e, &sc);
-    if (lane < K) {
-      p.ws.inds[tg * K + lane] = static_cast<uint32_t>(e);
-      p.ws.scores[tg * K + lane] = sc;
-      if (p.inds_out) p.inds_out[tg * K + lane] = static_cast<uint32_t>(e);
-      if (p.scores_out) p.scores_out[tg * K + lane] = sc;
-      const int le = e - p.off;
-      if (le >= 0 && le < p.E) atomicAdd(&hist[le], 1u);
-    }
-    if (lane == 0) {
-      p.ws.sg[tg] = p.has_shared ? 1.0f / (1.0f + expf(-lg[t][Et])) : 0.f;
-      float xsc, xinv;
-      fp16_range_scale(__uint_as_float(xmax[t]), xsc, xinv);
-      p.ws.xscale[tg] = xsc;
-    }
-  }
-  __syncthreads();
-  for (int e = tid; e < p.E; e += blockDim.x)
-    if (hist[e]) atomicAdd(&p.ws.counts[e], hist[e]);
-}
 
 // Given routing (no router): a warp per token copies its k expert ids and
 // weights, computes the power-of-two fp16 scale and the fp16 token copy, and
@@ -460,6 +236,232 @@ __global__ void __launch_bounds__(512) k_qmm_prep(Params p) {
     p.ws.rowpos[static_cast<size_t>(t) * 2] = static_cast<uint32_t>(t);
     p.ws.scores[t] = 1.0f;
   }
+}
+
+// ------------------------------------------------ router on tcgen05
+
+// k_route_gemm: router logits of 128 tokens x 128 experts per CTA on the
+// tensor cores (kind::f16 with bf16 x and bf16 router rows, fp32 TMEM
+// accumulation).  The K range is split into four quarters accumulated
+// separately (4 x 128 TMEM columns) and added in fp64, so each fp32
+// accumulation spans 32 MMA steps: the error allowance is kRouteRelTc
+// (rnb_route.cuh).  Roles (8 warps):
+//   warp 0    TMA: per 64-wide K stage the 128 x rows and the 128 router rows
+//             (128-byte swizzle; boxes reaching past T or E_total read zeros);
+//   warp 1    one thread issues the MMAs (M=128, N=128, K=16) into the
+//             stage's K quarter;
+//   warps 2-3 a share of the router rows' norms (sum of squares, sum of
+//             absolute values; rows spread over the token tiles);
+//   warps 4-7 one token per thread (one TMEM lane each): the 128 fp32 logits.
+// k_pre_select turns the logits into candidate intervals and routes.
+constexpr int kRgStages = 6;
+constexpr int kRgTile = 128 * 128;                    // 128 rows x 64 bf16
+constexpr int kRgStage = 2 * kRgTile;                 // x tile + router tile
+constexpr size_t kRgSmem = static_cast<size_t>(kRgStages) * kRgStage + 1024;
+static_assert(kRgStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+
+struct RouteMaps {
+  CUtensorMap x, w;
+};
+
+__global__ void __launch_bounds__(256, 1) k_route_gemm(Params p, const __grid_constant__ RouteMaps tm) {
+  extern __shared__ char rgraw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(rgraw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ __align__(8) uint64_t full[kRgStages], empty[kRgStages], mdone;
+  __shared__ uint32_t tslot;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = blockIdx.x * 128, e0 = blockIdx.y * 128;
+  const int H = p.H, Et = p.E_total, nks = H / 64, qk = nks / 4;
+  if (tid == 0) {
+    for (int s = 0; s < kRgStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&mdone, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(&tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = tslot;
+  bool timed_out = false;
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int ks = 0; ks < nks; ++ks) {
+        const int s = ks % kRgStages, n = ks / kRgStages;
+        if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, kWaitNs)) {
+          timed_out = true;
+          break;
+        }
+        const uint32_t bar = smem_u32(&full[s]);
+        mbar_arrive_expect_tx(&full[s], kRgStage);
+        tma_load_2d(smem_u32(sm + s * kRgStage), &tm.x, ks * 64, t0, bar);
+        tma_load_2d(smem_u32(sm + s * kRgStage + kRgTile), &tm.w, ks * 64, e0, bar);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(128, 128, true);
+      for (int ks = 0; ks < nks; ++ks) {
+        const int s = ks % kRgStages, n = ks / kRgStages;
+        if (!mbar_wait(&full[s], n & 1, kWaitNs)) {
+          timed_out = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sm + s * kRgStage), b0 = a0 + kRgTile;
+        const uint32_t d = taddr + static_cast<uint32_t>(ks / qk) * 128u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_f16(d, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(b0 + k * 32), idesc,
+                   (ks % qk == 0 && k == 0) ? 0u : 1u);
+        umma_commit(smem_u32(&empty[s]));
+      }
+      umma_commit(smem_u32(&mdone));  // also when the loop ended early: every issued MMA done
+      // every MMA this thread issued has completed before TMEM is released
+      if (!mbar_wait(&mdone, 0, kWaitNs)) timed_out = true;
+    }
+  } else if (warp < 4) {
+    // router-row norms, a warp per row: rows e0 + r with r / 8 = blockIdx.x
+    // (mod gridDim.x); every CTA column covers its 128 rows once
+    for (int r = blockIdx.x * 8 + (warp - 2); r < 128; r += gridDim.x * 8) {
+      for (int rr = r; rr < r + 8 && rr < 128; rr += 2) {
+        const int e = e0 + rr;
+        if (e >= Et) break;
+        const uint4* wr = reinterpret_cast<const uint4*>(p.router_w + static_cast<size_t>(e) * H);
+        float n2 = 0.f, n1 = 0.f;
+        for (int q = lane; q < H / 8; q += 32) {
+          const uint4 v = __ldg(wr + q);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xFFFF0000u);
+            n2 = fmaf(lo, lo, fmaf(hi, hi, n2));
+            n1 += fabsf(lo) + fabsf(hi);
+          }
+        }
+        n2 = warp_sum(n2);
+        n1 = warp_sum(n1);
+        if (lane == 0) {
+          p.ws.wn[e] = n2;
+          p.ws.wn[Et + e] = n1;
+        }
+      }
+    }
+  } else {
+    // one token per thread: TMEM lane 32 (warp % 4) + lane
+    const int q4 = warp & 3, t = t0 + 32 * q4 + lane;
+    const bool ok = mbar_wait(&mdone, 0, kWaitNs);
+    // the whole warp leaves together: tcgen05.ld below is warp-collective
+    if (__any_sync(0xffffffffu, !ok)) {
+      timed_out = true;
+    } else {
+      tc_fence_after();
+      uint32_t* lg = p.ws.lg + static_cast<size_t>(t < p.T ? t : 0) * (Et + 1);
+      const uint32_t tl = taddr + (static_cast<uint32_t>(q4 * 32) << 16);
+      for (int c0 = 0; c0 < 128; c0 += 16) {
+        uint32_t v[4][16];
+#pragma unroll
+        for (int kq = 0; kq < 4; ++kq) tmem_ld16(tl + kq * 128 + c0, v[kq]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int e = e0 + c0 + j;
+          const double L = (static_cast<double>(__uint_as_float(v[0][j])) + __uint_as_float(v[1][j])) +
+                           (static_cast<double>(__uint_as_float(v[2][j])) + __uint_as_float(v[3][j]));
+          if (t < p.T && e < Et) lg[e] = __float_as_uint(static_cast<float>(L));
+        }
+      }
+    }
+  }
+  if (timed_out) atomicOr(p.ws.status, RNB_STATUS_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    tmem_dealloc(taddr, 512);
+    tmem_relinquish();
+  }
+}
+
+// One warp per token, after k_route_gemm: the token's norms, the candidate
+// intervals of its bf16 logits (rnb_route.cuh), top-k selection with the
+// exact recompute of uncertain candidates, the weights, the shared-expert
+// gate (fp32 dot), the power-of-two fp16 scale and fp16 copy of the token,
+// and the local-expert histogram.
+constexpr int kSelMaxH = 2048;
+__global__ void __launch_bounds__(512, 1) k_pre_select(Params p) {
+  __shared__ uint32_t hist[kMaxE];
+  __shared__ uint32_t s_ivl[16][kMaxE + 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < kMaxE; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int t = blockIdx.x * 16 + warp;
+  const int K = p.k, H = p.H, Et = p.E_total, nq = H / 256;  // 16-byte pieces per lane
+  if (t < p.T) {
+    const size_t tg = static_cast<size_t>(t);
+    const uint4* xr = reinterpret_cast<const uint4*>(p.x + tg * H);
+    const uint4* gr = reinterpret_cast<const uint4*>(p.sgate_w);
+    uint4 xv[kSelMaxH / 256];
+    float xn2 = 0.f, xinf = 0.f, sgl = 0.f;
+#pragma unroll
+    for (int q = 0; q < kSelMaxH / 256; ++q) {
+      if (q < nq) {
+        xv[q] = __ldg(xr + q * 32 + lane);
+        uint4 gw = make_uint4(0u, 0u, 0u, 0u);
+        if (p.has_shared) gw = __ldg(gr + q * 32 + lane);
+        const uint32_t w[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w}, g[4] = {gw.x, gw.y, gw.z, gw.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xFFFF0000u);
+          xn2 = fmaf(lo, lo, fmaf(hi, hi, xn2));
+          xinf = fmaxf(xinf, fmaxf(fabsf(lo), fabsf(hi)));
+          sgl = fmaf(lo, __uint_as_float(g[j] << 16), fmaf(hi, __uint_as_float(g[j] & 0xFFFF0000u), sgl));
+        }
+      }
+    }
+    xn2 = warp_sum(xn2);
+    sgl = warp_sum(sgl);
+    xinf = warp_max(xinf);
+    const uint32_t* lgt = p.ws.lg + tg * (Et + 1);
+    for (int e = lane; e < Et; e += 32)
+      s_ivl[warp][e] = route_interval(__uint_as_float(__ldcg(lgt + e)), xn2, xinf, __ldcg(p.ws.wn + e),
+                                      __ldcg(p.ws.wn + Et + e), kRouteRelTc);
+    __syncwarp();
+    int e;
+    float sc;
+    warp_route_token(s_ivl[warp], Et, K, p.x + tg * H, p.router_w, H, lane, false, nullptr, &e, &sc);
+    if (lane < K) {
+      p.ws.inds[tg * K + lane] = static_cast<uint32_t>(e);
+      p.ws.scores[tg * K + lane] = sc;
+      if (p.inds_out) p.inds_out[tg * K + lane] = static_cast<uint32_t>(e);
+      if (p.scores_out) p.scores_out[tg * K + lane] = sc;
+      const int le = e - p.off;
+      if (le >= 0 && le < p.E) atomicAdd(&hist[le], 1u);
+    }
+    float xsc, xinv;
+    fp16_range_scale(xinf, xsc, xinv);
+    if (lane == 0) {
+      p.ws.sg[tg] = p.has_shared ? 1.0f / (1.0f + expf(-sgl)) : 0.f;
+      p.ws.xscale[tg] = xsc;
+    }
+    uint4* xo = reinterpret_cast<uint4*>(p.ws.x16 + tg * H);
+#pragma unroll
+    for (int q = 0; q < kSelMaxH / 256; ++q) {
+      if (q < nq) {
+        const uint32_t w[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o[j] = half2_bits(__uint_as_float(w[j] << 16) * xsc, __uint_as_float(w[j] & 0xFFFF0000u) * xsc);
+        xo[q * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < p.E; e += blockDim.x)
+    if (hist[e]) atomicAdd(&p.ws.counts[e], hist[e]);
 }
 
 // ------------------------------------------------------ sort / scatter
@@ -981,7 +983,7 @@ __global__ void k_pre_final(Params p) {
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 struct Layout {
-  size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, x16, xs16, h16, hinv, hrow, y16, yinv,
+  size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, x16, xs16, h16, hinv, hrow, lg, wn, y16, yinv,
       rowpos, total;
   int rows_cap, max_mt;
 };
@@ -1017,6 +1019,8 @@ Layout make_layout(const rnb_moe_desc& d) {
   L.h16 = take(static_cast<size_t>(L.rows_cap) * d.I * 2);
   L.hinv = take(static_cast<size_t>(L.rows_cap) * (d.I / 64) * 4);
   L.hrow = take(static_cast<size_t>(L.rows_cap) * 4);
+  L.lg = take(T * (d.E_total + 1) * 4);
+  L.wn = take(static_cast<size_t>(d.E_total) * 2 * 4);
   L.y16 = take(static_cast<size_t>(L.rows_cap) * d.H * 2);
   L.yinv = take(static_cast<size_t>(L.rows_cap) * (d.H / 128) * 4);
   L.rowpos = take(T * (K + 1) * 4);
@@ -1117,7 +1121,7 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill memset: ") + cudaGetErrorString(e));
   static bool attr = false;
   if (!attr) {
-    e = cudaFuncSetAttribute(k_pre_route, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kRouteSmem));
+    e = cudaFuncSetAttribute(k_route_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kRgSmem));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(k_pre_gemm<BITS, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(C::kSmem));
@@ -1127,10 +1131,19 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
     if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("prefill smem attribute: ") + cudaGetErrorString(e));
     attr = true;
   }
-  if (p.inds_in)
+  if (p.inds_in) {
     k_pre_given<<<(p.T + 15) / 16, 512, 0, st>>>(p);
-  else
-    k_pre_route<<<(p.T + kRouteT - 1) / kRouteT, 512, kRouteSmem, st>>>(p);
+  } else {
+    RouteMaps rm;
+    if (!encode_2d(&rm.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.x, p.H, static_cast<uint64_t>(p.T),
+                   static_cast<uint64_t>(p.H) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&rm.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.router_w, p.H, static_cast<uint64_t>(p.E_total),
+                   static_cast<uint64_t>(p.H) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(RNB_ERR_CUDA, "prefill: router tensor map encoding failed");
+    const dim3 rg((p.T + 127) / 128, (p.E_total + 127) / 128);
+    k_route_gemm<<<rg, 256, kRgSmem, st>>>(p, rm);
+    k_pre_select<<<(p.T + 15) / 16, 512, 0, st>>>(p);
+  }
   stage_end(st, RNB_STAGE_ROUTE);
   k_pre_sort<<<1, 512, 0, st>>>(p);
   stage_end(st, RNB_STAGE_SORT);
@@ -1207,6 +1220,8 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
   p.ws.h16 = reinterpret_cast<__half*>(b + L.h16);
   p.ws.hinv = reinterpret_cast<float*>(b + L.hinv);
   p.ws.hrow = reinterpret_cast<float*>(b + L.hrow);
+  p.ws.lg = reinterpret_cast<uint32_t*>(b + L.lg);
+  p.ws.wn = reinterpret_cast<float*>(b + L.wn);
   p.ws.y16 = reinterpret_cast<__half*>(b + L.y16);
   p.ws.yinv = reinterpret_cast<float*>(b + L.yinv);
   p.ws.rowpos = reinterpret_cast<uint32_t*>(b + L.rowpos);
@@ -1298,6 +1313,8 @@ int run_qmm(int bits, int T, int N, int K, const uint32_t* w, const uint16_t* s,
   p.ws.h16 = reinterpret_cast<__half*>(base + L.h16);
   p.ws.hinv = reinterpret_cast<float*>(base + L.hinv);
   p.ws.hrow = reinterpret_cast<float*>(base + L.hrow);
+  p.ws.lg = reinterpret_cast<uint32_t*>(base + L.lg);
+  p.ws.wn = reinterpret_cast<float*>(base + L.wn);
   p.ws.y16 = reinterpret_cast<__half*>(base + L.y16);
   p.ws.yinv = reinterpret_cast<float*>(base + L.yinv);
   p.ws.rowpos = reinterpret_cast<uint32_t*>(base + L.rowpos);

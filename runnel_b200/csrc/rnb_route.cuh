@@ -57,11 +57,11 @@ __device__ __forceinline__ uint16_t f64_to_bf16_bits(double v) {
 
 // Error allowances (multiples of sum |x_i w_i|): two fp32 ulps per MMA step
 // and per cross-warp add.  Decode routers accumulate 8 k16 steps per warp
-// and add 16 warp partials; the prefill router accumulates 8 steps per
-// 128-wide chunk in fp32 and the chunks in fp64 (the fp64 sum's rounding to
-// fp32 is the 2^-21 |L| term of the bound).
+// and add 16 warp partials.  The prefill router (tcgen05) accumulates four K
+// quarters of 32 steps each in fp32 and adds the quarters in fp64 (the fp64
+// sum's rounding to fp32 is the 2^-21 |L| term of the bound).
 constexpr float kRouteRelDecode = 0x1p-18f;
-constexpr float kRouteRelPrefill = 0x1p-20f;
+constexpr float kRouteRelTc = 0x1p-18f;
 
 // Packed candidate interval (lo | hi << 16) of an fp32 logit L with error
 // allowance rel * sum |x_i w_i|.  Norms of the token (xn2 = sum x^2, xinf =
