@@ -895,7 +895,14 @@ __global__ void k_pre_gather(Params p) {
     if (ent == 0xFFFFFFFFu) continue;
     const uint4* src = reinterpret_cast<const uint4*>(p.ws.x16 + static_cast<size_t>(ent / (p.k + 1)) * p.H);
     uint4* dst = reinterpret_cast<uint4*>(p.ws.xs16 + static_cast<size_t>(row) * p.H);
-    for (int q = lane; q < n16; q += 32) dst[q] = __ldcg(src + q);
+    // the whole row's loads in flight before its stores (H <= 2048: 8 per lane)
+    uint4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (lane + 32 * j < n16) v[j] = __ldcg(src + lane + 32 * j);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (lane + 32 * j < n16) dst[lane + 32 * j] = v[j];
   }
 }
 
