@@ -941,12 +941,12 @@ __device__ __forceinline__ void tile2_mma(const char* sm, int g, int c, BFrag bf
     RowPairs pa, pb;
     if (BITS == 8) {
       const int ch = gi * 4 + c;
-      pa = q8_group_pairs(*reinterpret_cast<const uint4*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16));
-      pb = q8_group_pairs(*reinterpret_cast<const uint4*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16));
+      pa = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16));
+      pb = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16));
     } else {
       const int ch = gi * 2 + (q >> 1), off = 8 * (q & 1);
-      pa = q4_group_pairs(*reinterpret_cast<const uint2*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16 + off));
-      pb = q4_group_pairs(*reinterpret_cast<const uint2*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16 + off));
+      pa = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16 + off));
+      pb = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16 + off));
     }
     uint32_t xh[8], xl[8];
     bfrag(gi, xh, xl);
@@ -957,8 +957,10 @@ __device__ __forceinline__ void tile2_mma(const char* sm, int g, int c, BFrag bf
       if (SPLIT)
         mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xl[2 * m], xl[2 * m + 1]);
     }
-    const float sa = bf16_bits_to_f32(S[g * 2 + gi]), ba = bf16_bits_to_f32(B[g * 2 + gi]);
-    const float sb = bf16_bits_to_f32(S[(g + 8) * 2 + gi]), bb = bf16_bits_to_f32(B[(g + 8) * 2 + gi]);
+    // the codes entered the MMAs as fp16 subnormals q * 2^-24 (rnb_common.cuh):
+    // the scales carry the 2^24 back (exact)
+    const float sa = bf16_bits_to_f32(S[g * 2 + gi]) * 0x1p24f, ba = bf16_bits_to_f32(B[g * 2 + gi]);
+    const float sb = bf16_bits_to_f32(S[(g + 8) * 2 + gi]) * 0x1p24f, bb = bf16_bits_to_f32(B[(g + 8) * 2 + gi]);
     const float xs0 = gsum(gi, 0), xs1 = gsum(gi, 1);
     acc[0] = fmaf(sa, d[0], fmaf(ba, xs0, acc[0]));
     acc[1] = fmaf(sa, d[1], fmaf(ba, xs1, acc[1]));
@@ -1085,7 +1087,9 @@ __device__ void xprep_cta(const uint16_t* x, int T, uint32_t* sX, float* sXs, fl
       const int grp = q >> 5, cc = (q >> 3) & 3, i = q & 7;
       const __half a = xh[grp * kGroup + pair_pos<BITS>(cc, i, 0)];
       const __half b = xh[grp * kGroup + pair_pos<BITS>(cc, i, 1)];
-      const __half2 h2 = __halves2half2(a, b);
+      __half2 h2 = __halves2half2(a, b);
+      // 4-bit pairs 1 and 3 of a word meet codes times 16 (subnormal form)
+      if (BITS == 4 && (i & 1)) h2 = __hmul2(h2, __float2half2_rn(0.0625f));
       sX[(static_cast<size_t>(t) * G + grp) * 32 + cc * 8 + i] = *reinterpret_cast<const uint32_t*>(&h2);
     }
     __syncthreads();
@@ -1555,14 +1559,19 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     cp_async_wait_pending(r0 == 0 ? 1 : 0);  // the routed-down group may stay in flight
     __syncwarp();
     if (r0 == 0) RNB_TRACE_MARK(p, 16);
+    // A warp needs only its own tiles (its cp.async groups, waited above):
+    // it starts its MMAs without waiting for the other warps' copies; the
+    // task records for the epilogue are read after the next barrier.
     if (tid < nr) {
       const int i = rc + (r0 + tid) * NC, a = i / n_ch;
       ms->tasks[tid] = PTask{ms->act_ent[a], static_cast<int>(ms->act_cnt[a]), (i % n_ch) * 8};
     }
-    __syncthreads();
 #pragma unroll 1
-    for (int k2 = 0; k2 < nr; ++k2)
-      p_gateup_mma<BITS>(p, sBR + ((r0 + k2) % pl.db) * task_bytes, sX, sXs, sRed + k2 * kPWarps * 128, ms->tasks[k2]);
+    for (int k2 = 0; k2 < nr; ++k2) {
+      const int i = rc + (r0 + k2) * NC, a = i / n_ch;
+      const PTask tk{ms->act_ent[a], static_cast<int>(ms->act_cnt[a]), (i % n_ch) * 8};
+      p_gateup_mma<BITS>(p, sBR + ((r0 + k2) % pl.db) * task_bytes, sX, sXs, sRed + k2 * kPWarps * 128, tk);
+    }
     if (r0 == 0) RNB_TRACE_MARK(p, 17);
     __syncthreads();
     p_gateup_epilogue(p, sRed, ms->tasks, nr, ms->xinv);
@@ -1674,11 +1683,16 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
             for (int k2 = 0; k2 < 2; ++k2) {
               const __half2 hi = __floats2half2_rn(v[2 * k2], v[2 * k2 + 1]);
               const float2 hf = __half22float2(hi);
-              frag[col * 128 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&hi);
+              // 4-bit pairs 1 and 3 of a word meet codes times 16 (subnormal form)
+              const bool x16 = BITS == 4 && ((i0 + k2) & 1);
+              const __half2 q = __float2half2_rn(x16 ? 0.0625f : 1.0f);
+              const __half2 his = __hmul2(hi, q);
+              frag[col * 128 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&his);
               if (kPhaseCSplit) {
                 const __half2 lo = __floats2half2_rn(v[2 * k2] - hf.x, v[2 * k2 + 1] - hf.y);
                 const float2 lf = __half22float2(lo);
-                frag[col * 128 + 64 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&lo);
+                const __half2 los = __hmul2(lo, q);
+                frag[col * 128 + 64 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&los);
                 part += lf.x + lf.y;
               }
               part += hf.x + hf.y;
