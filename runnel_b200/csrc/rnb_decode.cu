@@ -239,7 +239,9 @@ __device__ void xprep_warp(const Params& p, int t, int lane) {
       uint32_t pr[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const __half2 h2 = __floats2half2_rn(v[pair_pos<BITS>(cc, i, 0)], v[pair_pos<BITS>(cc, i, 1)]);
+        // 4-bit pairs 1 and 3 of a word meet codes times 16 (subnormal form; exact)
+        const float f = (BITS == 4 && (i & 1)) ? 0.0625f : 1.0f;
+        const __half2 h2 = __floats2half2_rn(v[pair_pos<BITS>(cc, i, 0)] * f, v[pair_pos<BITS>(cc, i, 1)] * f);
         pr[i] = *reinterpret_cast<const uint32_t*>(&h2);
       }
       reinterpret_cast<uint4*>(dst + cc * 8)[0] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
@@ -452,11 +454,11 @@ __device__ __forceinline__ void tile_mma(const char* sm, int g, int c, BFrag bfr
   for (int gi = 0; gi < NG; ++gi) {
     RowPairs pa, pb;
     if (BITS == 8) {
-      pa = q8_group_pairs(*reinterpret_cast<const uint4*>(sm + g * TL::kStride + gi * 64 + 16 * c));
-      pb = q8_group_pairs(*reinterpret_cast<const uint4*>(sm + (g + 8) * TL::kStride + gi * 64 + 16 * c));
+      pa = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(sm + g * TL::kStride + gi * 64 + 16 * c));
+      pb = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(sm + (g + 8) * TL::kStride + gi * 64 + 16 * c));
     } else {
-      pa = q4_group_pairs(*reinterpret_cast<const uint2*>(sm + g * TL::kStride + gi * 32 + 8 * q));
-      pb = q4_group_pairs(*reinterpret_cast<const uint2*>(sm + (g + 8) * TL::kStride + gi * 32 + 8 * q));
+      pa = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(sm + g * TL::kStride + gi * 32 + 8 * q));
+      pb = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(sm + (g + 8) * TL::kStride + gi * 32 + 8 * q));
     }
     uint32_t xh[8], xl[8];
     bfrag(gi, xh, xl);
@@ -467,8 +469,9 @@ __device__ __forceinline__ void tile_mma(const char* sm, int g, int c, BFrag bfr
       if (SPLIT)
         mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xl[2 * m], xl[2 * m + 1]);
     }
-    const float sa = bf16_bits_to_f32(S[g * NG + gi]), ba = bf16_bits_to_f32(B[g * NG + gi]);
-    const float sb = bf16_bits_to_f32(S[(g + 8) * NG + gi]), bb = bf16_bits_to_f32(B[(g + 8) * NG + gi]);
+    // subnormal code form (rnb_common.cuh): the scales carry the 2^24 back
+    const float sa = bf16_bits_to_f32(S[g * NG + gi]) * 0x1p24f, ba = bf16_bits_to_f32(B[g * NG + gi]);
+    const float sb = bf16_bits_to_f32(S[(g + 8) * NG + gi]) * 0x1p24f, bb = bf16_bits_to_f32(B[(g + 8) * NG + gi]);
     const float xs0 = gsum(gi, 0), xs1 = gsum(gi, 1);
     acc[0] = fmaf(sa, d[0], fmaf(ba, xs0, acc[0]));
     acc[1] = fmaf(sa, d[1], fmaf(ba, xs1, acc[1]));
@@ -780,8 +783,11 @@ __global__ void __launch_bounds__(32 * kDownMaxWarps) k_down(Params p) {
         const float2 hf = __half22float2(hi);
         const __half2 lo = __floats2half2_rn(a - hf.x, b - hf.y);
         const float2 lf = __half22float2(lo);
-        xh[i] = *reinterpret_cast<const uint32_t*>(&hi);
-        xl[i] = *reinterpret_cast<const uint32_t*>(&lo);
+        // 4-bit pairs 1 and 3 of a word meet codes times 16 (subnormal form)
+        const __half2 q16 = __float2half2_rn((BITS == 4 && (i & 1)) ? 0.0625f : 1.0f);
+        const __half2 his = __hmul2(hi, q16), los = __hmul2(lo, q16);
+        xh[i] = *reinterpret_cast<const uint32_t*>(&his);
+        xl[i] = *reinterpret_cast<const uint32_t*>(&los);
         part += (hf.x + lf.x) + (hf.y + lf.y);
       }
       part += __shfl_xor_sync(0xffffffffu, part, 1);
