@@ -1,11 +1,15 @@
 // rnb_common.cuh -- device helpers shared by the MoE kernels (sm_100a).
 //
 // Quantized rows are contracted on the tensor cores with mma.sync m16n8k16
-// (fp16 x fp16 -> fp32).  MLX affine codes (4 or 8 bit) become exact fp16
-// integers with a magic-number OR (0x6400 | q == 1024 + q) and a subtraction of
-// 1024, so every product q * x is exact and the per-group affine
+// (fp16 x fp16 -> fp32).  MLX affine codes (4 or 8 bit) enter the MMAs as
+// exact fp16 subnormals q * 2^-24 (the code in the low mantissa bits of a
+// zero-exponent fp16: one mask or byte permute per two codes), so every
+// product q * x is exact and the per-group affine
 //     sum_k (s q_k + b) x_k = s * sum_k q_k x_k + b * sum_k x_k
-// is applied in fp32 once per 64-group, with sum_k x_k precomputed.
+// is applied in fp32 once per 64-group (the scale carrying the 2^24 back),
+// with sum_k x_k precomputed.  The prefill converters, which write real fp16
+// weights s * q + b, use the magic-number form (0x6400 | q == 1024 + q, then
+// subtract 1024).
 //
 // Lane layout of one 64-wide group for one weight row (lane = 4*g + c):
 // lane c owns 16 of the 64 positions and hands them to the MMA as 8 fp16
@@ -182,22 +186,6 @@ __device__ __forceinline__ void q4_exchange(const uint4 v, int c, uint2& ev, uin
 struct RowPairs {
   uint32_t p[8];
 };
-
-__device__ __forceinline__ RowPairs q8_group_pairs(const uint4 v) {
-  RowPairs r;
-  q8_word_to_pairs(v.x, r.p[0], r.p[1]);
-  q8_word_to_pairs(v.y, r.p[2], r.p[3]);
-  q8_word_to_pairs(v.z, r.p[4], r.p[5]);
-  q8_word_to_pairs(v.w, r.p[6], r.p[7]);
-  return r;
-}
-
-__device__ __forceinline__ RowPairs q4_group_pairs(const uint2 v) {
-  RowPairs r;
-  q4_word_to_pairs(v.x, r.p[0], r.p[1], r.p[2], r.p[3]);
-  q4_word_to_pairs(v.y, r.p[4], r.p[5], r.p[6], r.p[7]);
-  return r;
-}
 
 __device__ __forceinline__ RowPairs q8_group_pairs_sub(const uint4 v) {
   RowPairs r;
