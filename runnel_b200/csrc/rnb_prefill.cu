@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(256, 1) k_route_gemm(Params p, const __grid_co
 // gate (fp32 dot), the power-of-two fp16 scale and fp16 copy of the token,
 // and the local-expert histogram.
 constexpr int kSelMaxH = 2048;
-__global__ void __launch_bounds__(512, 1) k_pre_select(Params p) {
+__global__ void __launch_bounds__(512, 2) k_pre_select(Params p) {
   __shared__ uint32_t hist[kMaxE];
   __shared__ uint32_t s_ivl[16][kMaxE + 1];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -424,22 +424,7 @@ __global__ void __launch_bounds__(512, 1) k_pre_select(Params p) {
     xn2 = warp_sum(xn2);
     sgl = warp_sum(sgl);
     xinf = warp_max(xinf);
-    const uint32_t* lgt = p.ws.lg + tg * (Et + 1);
-    for (int e = lane; e < Et; e += 32)
-      s_ivl[warp][e] = route_interval(__uint_as_float(__ldcg(lgt + e)), xn2, xinf, __ldcg(p.ws.wn + e),
-                                      __ldcg(p.ws.wn + Et + e), kRouteRelTc);
-    __syncwarp();
-    int e;
-    float sc;
-    warp_route_token(s_ivl[warp], Et, K, p.x + tg * H, p.router_w, H, lane, false, nullptr, &e, &sc);
-    if (lane < K) {
-      p.ws.inds[tg * K + lane] = static_cast<uint32_t>(e);
-      p.ws.scores[tg * K + lane] = sc;
-      if (p.inds_out) p.inds_out[tg * K + lane] = static_cast<uint32_t>(e);
-      if (p.scores_out) p.scores_out[tg * K + lane] = sc;
-      const int le = e - p.off;
-      if (le >= 0 && le < p.E) atomicAdd(&hist[le], 1u);
-    }
+    // the fp16 copy first, so the token's registers are free before routing
     float xsc, xinv;
     fp16_range_scale(xinf, xsc, xinv);
     if (lane == 0) {
@@ -457,6 +442,34 @@ __global__ void __launch_bounds__(512, 1) k_pre_select(Params p) {
           o[j] = half2_bits(__uint_as_float(w[j] << 16) * xsc, __uint_as_float(w[j] & 0xFFFF0000u) * xsc);
         xo[q * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
       }
+    }
+    // every load of the token's logits and the router-row norms is issued
+    // before the intervals are formed (E_total <= kMaxE = 256: 8 per lane)
+    const uint32_t* lgt = p.ws.lg + tg * (Et + 1);
+    float lv[kMaxE / 32], w2[kMaxE / 32], w1[kMaxE / 32];
+#pragma unroll
+    for (int i = 0; i < kMaxE / 32; ++i) {
+      const int e = lane + 32 * i;
+      lv[i] = e < Et ? __uint_as_float(__ldcg(lgt + e)) : 0.f;
+      w2[i] = e < Et ? __ldcg(p.ws.wn + e) : 0.f;
+      w1[i] = e < Et ? __ldcg(p.ws.wn + Et + e) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxE / 32; ++i) {
+      const int e = lane + 32 * i;
+      if (e < Et) s_ivl[warp][e] = route_interval(lv[i], xn2, xinf, w2[i], w1[i], kRouteRelTc);
+    }
+    __syncwarp();
+    int e;
+    float sc;
+    warp_route_token(s_ivl[warp], Et, K, p.x + tg * H, p.router_w, H, lane, false, nullptr, &e, &sc);
+    if (lane < K) {
+      p.ws.inds[tg * K + lane] = static_cast<uint32_t>(e);
+      p.ws.scores[tg * K + lane] = sc;
+      if (p.inds_out) p.inds_out[tg * K + lane] = static_cast<uint32_t>(e);
+      if (p.scores_out) p.scores_out[tg * K + lane] = sc;
+      const int le = e - p.off;
+      if (le >= 0 && le < p.E) atomicAdd(&hist[le], 1u);
     }
   }
   __syncthreads();
