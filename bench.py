@@ -18,8 +18,11 @@ previous ones); the K steps are replayed from one CUDA graph.
 
 Also reported:
   e2e           the same metric through the public API with the token in pinned
-                host memory: per step H2D copy, C-ABI call, D2H copy of the
-                output, launched from Python, device-timed over the K steps.
+                host memory: per step H2D copy, block, D2H copy of the output,
+                launched from Python, device-timed over the K steps.  On one
+                GPU the three are one C-ABI call (ops.BlockCall.host ->
+                rnb_moe_block_fwd_host); under expert parallelism they are two
+                torch copies around the expert-parallel block call.
   roofline      algorithmic HBM bytes per step (distinct experts' weights +
                 shared expert + router + activations) / step time, against
                 MEASURED_PEAKS.json hbm_gbs.
@@ -814,11 +817,21 @@ def run_ours(args):
     oh = torch.empty_like(xh).pin_memory()
     xd = torch.empty((T, xs.shape[-1]), dtype=torch.bfloat16, device=dev)
     od = torch.empty_like(xd)
-    with torch.cuda.stream(stream):
-        for i in range(min(R, args.warmup + 1)):
+    if world == 1:
+        # one prepared call per bank copy: copy-in, block and copy-out are one
+        # C call (rnb_moe_block_fwd_host) from pinned host memory
+        calls = [ops.BlockCall(copies[i], T, ws=ws) for i in range(R)]
+
+        def host_step(i):
+            calls[i].host(xh[i], oh[i])
+    else:
+        def host_step(i):
             xd.copy_(xh[i], non_blocking=True)
             block_call(copies[i], xd, od)
             oh[i].copy_(od, non_blocking=True)
+    with torch.cuda.stream(stream):
+        for i in range(min(R, args.warmup + 1)):
+            host_step(i)
     stream.synchronize()
     if dist:
         dist.barrier()
@@ -827,10 +840,7 @@ def run_ours(args):
     with torch.cuda.stream(stream):
         e0.record(stream)
         for s in range(K):
-            i = s % R
-            xd.copy_(xh[i], non_blocking=True)
-            block_call(copies[i], xd, od)
-            oh[i].copy_(od, non_blocking=True)
+            host_step(s % R)
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)

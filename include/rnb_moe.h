@@ -155,6 +155,21 @@ RNB_API int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, u
 RNB_API int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void* out,
                                       uint32_t* inds_out, float* scores_out, void* stream);
 
+/* rnb_moe_block_fwd from host memory, one call for the whole round trip:
+ * copies x_host ([T, H] bf16) into the device staging buffer x_dev, runs the
+ * block into out_dev, and copies out_dev back to out_host ([T, H] bf16, or
+ * fp32 with RNB_FLAG_Y_F32).  The three steps are queued on `stream` and the
+ * call returns without waiting: out_host holds the result once the stream has
+ * been synchronised.  Use page-locked (pinned) host buffers, since copies from
+ * pageable memory are staged and partly synchronous.  x_dev and out_dev are
+ * caller-owned, 16-byte aligned and sized for T tokens.  No routing copies are
+ * returned (use rnb_moe_block_fwd for those).  The reference's block call takes
+ * unified-memory MLX arrays and needs no copies; on a discrete GPU this is the
+ * closest call with host buffers. */
+RNB_API int rnb_moe_block_fwd_host(const rnb_moe_desc* d, const void* x_host, void* out_host,
+                                   void* x_dev, void* out_dev, void* ws, size_t ws_bytes,
+                                   void* stream);
+
 /* Copies the device status word (RNB_STATUS_* bits) to *status and clears it.
  * Synchronises the stream. */
 RNB_API int rnb_moe_status(void* ws, size_t ws_bytes, uint32_t* status, void* stream);

@@ -2285,6 +2285,28 @@ int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, uint32_t*
 RNB_API size_t rnb_trace_offset(const rnb_moe_desc* d) { return make_layout(*d).yws; }
 #endif
 
+int rnb_moe_block_fwd_host(const rnb_moe_desc* d, const void* x_host, void* out_host, void* x_dev,
+                           void* out_dev, void* ws, size_t ws_bytes, void* stream) {
+  // everything the block call checks is checked before the first copy is queued
+  int rc = validate(d, true, true);
+  if (!rc) rc = check_device();
+  if (!rc) rc = check_ws(d, ws, ws_bytes);
+  if (rc) return rc;
+  if (!x_host || !out_host || !x_dev || !out_dev)
+    return fail(RNB_ERR_INVALID, "x_host, out_host, x_dev and out_dev must be non-NULL");
+  if (!aligned16(x_dev) || !aligned16(out_dev)) return fail(RNB_ERR_ALIGN, "x_dev and out_dev must be 16-byte aligned");
+  const size_t n = static_cast<size_t>(d->T) * static_cast<size_t>(d->H);
+  const size_t out_bytes = n * ((d->flags & RNB_FLAG_Y_F32) ? 4 : 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(x_dev, x_host, n * 2, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("copying x to the device: ") + cudaGetErrorString(e));
+  rc = rnb_moe_block_fwd(d, x_dev, out_dev, nullptr, nullptr, ws, ws_bytes, stream);
+  if (rc) return rc;
+  e = cudaMemcpyAsync(out_host, out_dev, out_bytes, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("copying out to the host: ") + cudaGetErrorString(e));
+  return RNB_OK;
+}
+
 int rnb_moe_status(void* ws, size_t ws_bytes, uint32_t* status, void* stream) {
   if (!ws || !status) return fail(RNB_ERR_INVALID, "ws and status must be non-NULL");
   if (ws_bytes < 4) return fail(RNB_ERR_WORKSPACE, "workspace too small");

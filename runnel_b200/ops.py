@@ -27,6 +27,11 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return t.data_ptr()
 
 
+# the descriptor's tensor fields, in rnb_moe_desc order
+_BANK_FIELDS = ("gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b", "router_w", "shared_gate_w",
+                "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b")
+
+
 @dataclass
 class BlockTensors:
     """Device tensors of one sparse-MoE block (MLX layout)."""
@@ -96,8 +101,7 @@ class BlockTensors:
         d.E_total = self.E_total if self.E_total is not None else self.E
         d.expert_offset = self.expert_offset
         d.k, d.bits, d.group, d.flags = k, self.bits, self.group, self.flags
-        for name in ("gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b", "router_w", "shared_gate_w",
-                     "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b"):
+        for name in _BANK_FIELDS:
             setattr(d, name, _ptr(getattr(self, name)))
         return d
 
@@ -208,6 +212,64 @@ def moe_block(bt: BlockTensors, x: torch.Tensor, k: int = 8, ws: Workspace | Non
     if return_routing:
         return out, inds, scores
     return out
+
+
+class BlockCall:
+    """``moe_block`` prepared once for a fixed token count ``T``, for callers
+    that repeat one call shape (decode loops, serving steps).
+
+    The descriptor and the device staging buffers are built here, so a call is
+    one C call with no per-call descriptor or workspace-size query.  The bank's
+    tensors are captured at construction: in-place updates of them are seen,
+    but assigning a new tensor to a ``BlockTensors`` field is not.  Calls are
+    asynchronous on the current stream and reuse the staging buffers, so calls
+    on one object must share a stream.
+
+    ``host(x_host, out_host)`` takes CPU tensors and queues copy-in, block and
+    copy-out as one C call (``rnb_moe_block_fwd_host``).  Pin both tensors so
+    the copies are asynchronous; ``out_host`` holds the result once the stream
+    is synchronised.  ``__call__(x, out)`` runs on CUDA tensors."""
+
+    def __init__(self, bt: BlockTensors, T: int, k: int = 8, ws: Workspace | None = None):
+        if T <= 0:
+            raise ValueError("T must be positive")
+        self.T, self.H, self.k = T, bt.H, k
+        self._bank = tuple(getattr(bt, f) for f in _BANK_FIELDS)  # keeps the pointed-to tensors alive
+        self.desc = bt.desc(T, k)
+        self._dref = ctypes.byref(self.desc)
+        self.device = bt.gu_w.device
+        self.ws = ws or Workspace(self.device)
+        self.ws.get(self.desc)  # sized (and zeroed) for this call once
+        self.out_dtype = torch.float32 if bt.flags & _lib.FLAG_Y_F32 else torch.bfloat16
+        self.x_dev = torch.empty((T, bt.H), dtype=torch.bfloat16, device=self.device)
+        self.out_dev = torch.empty((T, bt.H), dtype=self.out_dtype, device=self.device)
+        lib = _lib.load()
+        self._fwd, self._fwd_host = lib.rnb_moe_block_fwd, lib.rnb_moe_block_fwd_host
+
+    def _check(self, x: torch.Tensor, out: torch.Tensor, cuda: bool) -> None:
+        n = self.T * self.H
+        if (x.is_cuda != cuda or out.is_cuda != cuda or x.dtype != torch.bfloat16 or out.dtype != self.out_dtype
+                or x.numel() != n or out.numel() != n or not x.is_contiguous() or not out.is_contiguous()):
+            where = "CUDA" if cuda else "CPU"
+            raise ValueError(f"x must be a contiguous {where} bfloat16 tensor of {self.T}x{self.H} elements and "
+                             f"out a contiguous {where} {self.out_dtype} tensor of as many")
+
+    def host(self, x_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
+        self._check(x_host, out_host, cuda=False)
+        buf = self.ws.buf
+        _lib.check("rnb_moe_block_fwd_host",
+                   self._fwd_host(self._dref, x_host.data_ptr(), out_host.data_ptr(), self.x_dev.data_ptr(),
+                                  self.out_dev.data_ptr(), buf.data_ptr(), buf.numel(), _stream()))
+        return out_host
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(x.shape, dtype=self.out_dtype, device=x.device)
+        self._check(x, out, cuda=True)
+        buf = self.ws.buf
+        _lib.check("rnb_moe_block_fwd", self._fwd(self._dref, x.data_ptr(), out.data_ptr(), None, None,
+                                                  buf.data_ptr(), buf.numel(), _stream()))
+        return out
 
 
 def experts_fwd(bt: BlockTensors, x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor,

@@ -78,6 +78,9 @@ def test_calls_without_device_fail_loudly():
     _lib.call("rnb_moe_workspace_size", ctypes.byref(d), ctypes.byref(n))
     rc = _lib.load().rnb_switchglu_fwd(ctypes.byref(d), 16, 16, 16, 16, n.value, None)
     assert rc != 0
+    # the host-buffer entry point checks the device before it queues a copy
+    rc = _lib.load().rnb_moe_block_fwd_host(ctypes.byref(d), 16, 16, 16, 16, 16, n.value, None)
+    assert rc != 0
 
 
 @pytest.mark.parametrize("kw,msg", [

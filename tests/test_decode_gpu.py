@@ -172,6 +172,27 @@ def test_bitwise_deterministic_and_graph_capturable():
     assert torch.equal(out, a)
 
 
+@pytest.mark.parametrize("T", [1, 8, 130])
+def test_block_call_host_round_trip_matches_moe_block(T):
+    # rnb_moe_block_fwd_host: copy-in, block (decode or, at T > 64, the
+    # grouped-GEMM path) and copy-out in one call gives moe_block's bits
+    blk, bt, w = _setup(4)
+    x = torch.from_numpy(inputs.make_tokens(7, T)).view(torch.int16).view(torch.bfloat16).cuda()
+    ref = ops.moe_block(bt, x)
+    bc = ops.BlockCall(bt, T)
+    xh = x.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    for _ in range(2):
+        oh.zero_()
+        bc.host(xh, oh)
+        torch.cuda.current_stream().synchronize()
+        assert torch.equal(oh, ref.cpu())
+    assert torch.equal(bc(x), ref)
+    assert bc.ws.status() == 0
+    with pytest.raises(ValueError):
+        bc.host(x, oh)  # a device tensor where a host one is expected
+
+
 def test_module_api_matches_functional():
     blk, bt, w = _setup(8)
     block = sl.block_from_tensors(bt, fused=False)  # stock modules, packed on first use
