@@ -18,11 +18,13 @@ previous ones); the K steps are replayed from one CUDA graph.
 
 Also reported:
   e2e           the same metric through the public API with the token in pinned
-                host memory: per step H2D copy, block, D2H copy of the output,
-                launched from Python, device-timed over the K steps.  On one
-                GPU the three are one C-ABI call (ops.BlockCall.host ->
-                rnb_moe_block_fwd_host); under expert parallelism they are two
-                torch copies around the expert-parallel block call.
+                host memory: per step H2D copy of the token, block, and the
+                output written back to pinned host memory, launched from Python,
+                device-timed over the K steps.  On one GPU this is one C-ABI
+                call (ops.BlockCall.host -> rnb_moe_block_fwd_host, whose kernels
+                store the output straight into the mapped pinned buffer); under
+                expert parallelism it is two torch copies around the
+                expert-parallel block call.
   roofline      algorithmic HBM bytes per step (distinct experts' weights +
                 shared expert + router + activations) / step time, against
                 MEASURED_PEAKS.json hbm_gbs.

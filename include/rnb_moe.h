@@ -161,8 +161,10 @@ RNB_API int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void
  * fp32 with RNB_FLAG_Y_F32).  The three steps are queued on `stream` and the
  * call returns without waiting: out_host holds the result once the stream has
  * been synchronised.  Use page-locked (pinned) host buffers, since copies from
- * pageable memory are staged and partly synchronous.  x_dev and out_dev are
- * caller-owned, 16-byte aligned and sized for T tokens.  No routing copies are
+ * pageable memory are staged and partly synchronous.  When out_host is
+ * page-locked, mapped for this device and 16-byte aligned, the block's kernels
+ * store the result straight into it and out_dev is not used.  x_dev and out_dev
+ * are caller-owned, 16-byte aligned and sized for T tokens.  No routing copies are
  * returned (use rnb_moe_block_fwd for those).  The reference's block call takes
  * unified-memory MLX arrays and needs no copies; on a discrete GPU this is the
  * closest call with host buffers. */

@@ -2298,10 +2298,21 @@ int rnb_moe_block_fwd_host(const rnb_moe_desc* d, const void* x_host, void* out_
   const size_t n = static_cast<size_t>(d->T) * static_cast<size_t>(d->H);
   const size_t out_bytes = n * ((d->flags & RNB_FLAG_Y_F32) ? 4 : 2);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Page-locked host memory mapped into this device's address space takes the
+  // kernels' stores directly (every path only stores to out), which saves the
+  // copy-out and its wait.  Pageable or unmapped memory is never handed to a
+  // kernel: it gets the device-to-host copy.
+  void* direct = nullptr;
+  cudaPointerAttributes pa{};
+  if (cudaPointerGetAttributes(&pa, out_host) == cudaSuccess) {
+    if (pa.type == cudaMemoryTypeHost && pa.devicePointer && aligned16(pa.devicePointer)) direct = pa.devicePointer;
+  } else {
+    (void)cudaGetLastError();  // an unknown (pageable) pointer is not an error here
+  }
   cudaError_t e = cudaMemcpyAsync(x_dev, x_host, n * 2, cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("copying x to the device: ") + cudaGetErrorString(e));
-  rc = rnb_moe_block_fwd(d, x_dev, out_dev, nullptr, nullptr, ws, ws_bytes, stream);
-  if (rc) return rc;
+  rc = rnb_moe_block_fwd(d, x_dev, direct ? direct : out_dev, nullptr, nullptr, ws, ws_bytes, stream);
+  if (rc || direct) return rc;
   e = cudaMemcpyAsync(out_host, out_dev, out_bytes, cudaMemcpyDeviceToHost, st);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("copying out to the host: ") + cudaGetErrorString(e));
   return RNB_OK;

@@ -184,9 +184,14 @@ def test_block_call_host_round_trip_matches_moe_block(T):
     oh = torch.empty_like(xh).pin_memory()
     for _ in range(2):
         oh.zero_()
-        bc.host(xh, oh)
+        bc.host(xh, oh)  # pinned: the kernels store into oh directly
         torch.cuda.current_stream().synchronize()
         assert torch.equal(oh, ref.cpu())
+    pageable = torch.zeros_like(xh, device="cpu")
+    assert not pageable.is_pinned()
+    bc.host(xh, pageable)  # pageable: copied back from the staging buffer
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(pageable, ref.cpu())
     assert torch.equal(bc(x), ref)
     assert bc.ws.status() == 0
     with pytest.raises(ValueError):
