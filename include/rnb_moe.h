@@ -241,9 +241,8 @@ RNB_API int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* 
                                  uint32_t* inds_out, float* scores_out, void* ws, size_t ws_bytes,
                                  void* stream);
 
-/* Layer glue of a decoder stack (SURVEY's "layer glue around the block"; no
- * reference counterpart in runnel itself -- mlx-lm's Qwen3.5 decoder layer does
- * `x + mlp(rms_norm(x))`).  For T tokens of H bf16 values:
+/* Layer glue of a decoder stack, around the block (no reference counterpart in
+ * runnel itself -- mlx-lm's Qwen3.5 decoder layer does `x + mlp(rms_norm(x))`).  For T tokens of H bf16 values:
  *   x_out = bf16(x + y)   (y may be NULL: x_out = x)
  *   xn_out = bf16(x_out * rsqrt(mean(x_out^2) + eps) * w)   (fp32 math, w bf16 [H])
  * x_out may alias x. */

@@ -1,7 +1,6 @@
 """Extracts the reference's recorded known-answer values into kats.json.
 
-Run in a checkout that has the waylake/runnel tree (default path below, or
-pass it as argv[1]).  Every record comes from the reference's own result
+Pass the root of a waylake/runnel checkout as argv[1] (or set RUNNEL_REF).  Every record comes from the reference's own result
 files under bench/results/m0/: the protocol the native probe ran with, the
 checksum its CPU reference produced and, where recorded, the first eight
 CPU-reference outputs.  Only the reference's CPU-side numbers are kept (the
@@ -9,7 +8,7 @@ Metal outputs of its two-stage kernel are loosely gated and not an oracle),
 and records measured on real checkpoint layers (dataset_loaded) are skipped
 because their inputs are not regenerable from a seed.
 
-    python tests/golden/make_golden.py [/path/to/runnel]
+    python tests/golden/make_golden.py /path/to/runnel
 """
 from __future__ import annotations
 
@@ -60,4 +59,7 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("RUNNEL_REF")
+    if not ref:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/runnel  (or set RUNNEL_REF)")
+    main(ref)
