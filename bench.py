@@ -433,20 +433,28 @@ def run_prefill_bench(args, cfg):
     oh = torch.empty_like(xh[0]).pin_memory()
     xd = torch.empty_like(xs[0])
     od = torch.empty_like(xd)
-    with torch.cuda.stream(stream):
-        for i in range(3):
+    if not a2a:
+        # one C call per step (rnb_moe_block_fwd_host): the batch is split into
+        # chunks whose copies in and out overlap the other chunks' compute
+        calls = [ops.BlockCall(kd, T, ws=ws) for kd in kinds]
+
+        def host_step(i):
+            calls[i % nk].host(xh[i % nk], oh)
+    else:
+        def host_step(i):
             xd.copy_(xh[i % nk], non_blocking=True)
             block(i, xd, od)
             oh.copy_(od, non_blocking=True)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            host_step(i)
     stream.synchronize()
     Ke = max(4, min(K, 64))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
         for i in range(Ke):
-            xd.copy_(xh[i % nk], non_blocking=True)
-            block(i, xd, od)
-            oh.copy_(od, non_blocking=True)
+            host_step(i)
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)

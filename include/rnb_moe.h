@@ -161,10 +161,14 @@ RNB_API int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void
  * fp32 with RNB_FLAG_Y_F32).  The three steps are queued on `stream` and the
  * call returns without waiting: out_host holds the result once the stream has
  * been synchronised.  Use page-locked (pinned) host buffers, since copies from
- * pageable memory are staged and partly synchronous.  When out_host is
- * page-locked, mapped for this device and 16-byte aligned, the block's kernels
- * store the result straight into it and out_dev is not used.  x_dev and out_dev
- * are caller-owned, 16-byte aligned and sized for T tokens.  No routing copies are
+ * pageable memory are staged and partly synchronous.  Up to 64 tokens, when
+ * out_host is page-locked, mapped for this device and 16-byte aligned, the
+ * block's kernels store the result straight into it and out_dev is not used.  x_dev and out_dev
+ * are caller-owned, 16-byte aligned and sized for T tokens.  From 4096 tokens
+ * on, the call is split into 2-4 chunks of whole tokens whose copies run on
+ * two copy streams of the library's own and overlap the other chunks' compute;
+ * the first such call on a device creates those streams, so make it before any
+ * stream capture.  No routing copies are
  * returned (use rnb_moe_block_fwd for those).  The reference's block call takes
  * unified-memory MLX arrays and needs no copies; on a discrete GPU this is the
  * closest call with host buffers. */

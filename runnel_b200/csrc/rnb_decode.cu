@@ -23,6 +23,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -2163,6 +2164,43 @@ int noalloc_scratch(void** out) {
   return RNB_OK;
 }
 
+// Copy streams and events of rnb_moe_block_fwd_host's chunked form, made once
+// per device.  g_host_pipe_mu is held while a call queues its work, so two
+// host threads never interleave records and waits on the shared events.
+constexpr int kHostMaxChunks = 4;
+constexpr int kHostChunkMin = 2048;  // tokens per chunk when a call is split
+struct HostPipe {
+  cudaStream_t in = nullptr, out = nullptr;
+  cudaEvent_t start = nullptr, done = nullptr;
+  cudaEvent_t ready[kHostMaxChunks] = {}, computed[kHostMaxChunks] = {};
+};
+std::mutex g_host_pipe_mu;
+
+int host_pipe(HostPipe** out) {
+  constexpr int kMaxDevices = 64;
+  static HostPipe pipes[kMaxDevices];
+  static bool made[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(RNB_ERR_DEVICE, "device index out of range");
+  HostPipe& hp = pipes[dev];
+  if (!made[dev]) {
+    e = cudaStreamCreateWithFlags(&hp.in, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&hp.out, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&hp.start, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&hp.done, cudaEventDisableTiming);
+    for (int j = 0; j < kHostMaxChunks && e == cudaSuccess; ++j) {
+      e = cudaEventCreateWithFlags(&hp.ready[j], cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&hp.computed[j], cudaEventDisableTiming);
+    }
+    if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("creating copy streams: ") + cudaGetErrorString(e));
+    made[dev] = true;
+  }
+  *out = &hp;
+  return RNB_OK;
+}
+
 }  // namespace rnb
 
 using namespace rnb;
@@ -2298,23 +2336,89 @@ int rnb_moe_block_fwd_host(const rnb_moe_desc* d, const void* x_host, void* out_
   const size_t n = static_cast<size_t>(d->T) * static_cast<size_t>(d->H);
   const size_t out_bytes = n * ((d->flags & RNB_FLAG_Y_F32) ? 4 : 2);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Page-locked host memory mapped into this device's address space takes the
-  // kernels' stores directly (every path only stores to out), which saves the
-  // copy-out and its wait.  Pageable or unmapped memory is never handed to a
+  // For decode-sized calls, page-locked host memory mapped into this device's
+  // address space takes the kernels' stores directly (every path only stores
+  // to out), which saves the copy-out and its wait.  Larger outputs cross PCIe
+  // faster as one copy.  Pageable or unmapped memory is never handed to a
   // kernel: it gets the device-to-host copy.
   void* direct = nullptr;
   cudaPointerAttributes pa{};
-  if (cudaPointerGetAttributes(&pa, out_host) == cudaSuccess) {
+  if (d->T > kMaxDecodeT) {
+    // copy-out below
+  } else if (cudaPointerGetAttributes(&pa, out_host) == cudaSuccess) {
     if (pa.type == cudaMemoryTypeHost && pa.devicePointer && aligned16(pa.devicePointer)) direct = pa.devicePointer;
   } else {
     (void)cudaGetLastError();  // an unknown (pageable) pointer is not an error here
   }
-  cudaError_t e = cudaMemcpyAsync(x_dev, x_host, n * 2, cudaMemcpyHostToDevice, st);
-  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("copying x to the device: ") + cudaGetErrorString(e));
-  rc = rnb_moe_block_fwd(d, x_dev, direct ? direct : out_dev, nullptr, nullptr, ws, ws_bytes, stream);
-  if (rc || direct) return rc;
-  e = cudaMemcpyAsync(out_host, out_dev, out_bytes, cudaMemcpyDeviceToHost, st);
-  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("copying out to the host: ") + cudaGetErrorString(e));
+  const int nchunk = std::min(kHostMaxChunks, d->T / kHostChunkMin);
+  if (nchunk < 2) {
+    cudaError_t e = cudaMemcpyAsync(x_dev, x_host, n * 2, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("copying x to the device: ") + cudaGetErrorString(e));
+    rc = rnb_moe_block_fwd(d, x_dev, direct ? direct : out_dev, nullptr, nullptr, ws, ws_bytes, stream);
+    if (rc || direct) return rc;
+    e = cudaMemcpyAsync(out_host, out_dev, out_bytes, cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("copying out to the host: ") + cudaGetErrorString(e));
+    return RNB_OK;
+  }
+  // Many tokens: the call is split into chunks of whole tokens.  All
+  // copies-in run back to back on one copy stream; chunk j's block waits for
+  // its copy-in, and its copy-out on a second copy stream waits for the block,
+  // so the copies overlap the other chunks' compute.  The caller's stream
+  // waits for the last copy-out before the call's work counts as done.
+  std::lock_guard<std::mutex> lock(g_host_pipe_mu);
+  HostPipe* hp = nullptr;
+  rc = host_pipe(&hp);
+  if (rc) return rc;
+  const size_t osz = (d->flags & RNB_FLAG_Y_F32) ? 4 : 2, row_in = static_cast<size_t>(d->H) * 2,
+               row_out = static_cast<size_t>(d->H) * osz;
+  int t0s[kHostMaxChunks + 1];
+  for (int j = 0; j <= nchunk; ++j)
+    t0s[j] = static_cast<int>(static_cast<long long>(d->T) * j / nchunk);
+  // on an error the caller's stream still waits for whatever was queued on
+  // the copy streams (best effort), so out_host is not written after it
+  auto join = [&]() {
+    for (cudaStream_t cs : {hp->in, hp->out})
+      if (cudaEventRecord(hp->done, cs) == cudaSuccess) (void)cudaStreamWaitEvent(st, hp->done, 0);
+  };
+  auto cuda_fail = [&](const char* what, cudaError_t e) {
+    const int r = fail(RNB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    join();
+    return r;
+  };
+  // the staging buffers and out_host are reused: start after earlier work on the caller's stream
+  cudaError_t e = cudaEventRecord(hp->start, st);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(hp->in, hp->start, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(hp->out, hp->start, 0);
+  if (e != cudaSuccess) return cuda_fail("ordering the copy streams", e);
+  for (int j = 0; j < nchunk; ++j) {
+    const size_t off = static_cast<size_t>(t0s[j]), rows = static_cast<size_t>(t0s[j + 1] - t0s[j]);
+    e = cudaMemcpyAsync(static_cast<char*>(x_dev) + off * row_in, static_cast<const char*>(x_host) + off * row_in,
+                        rows * row_in, cudaMemcpyHostToDevice, hp->in);
+    if (e == cudaSuccess) e = cudaEventRecord(hp->ready[j], hp->in);
+    if (e != cudaSuccess) return cuda_fail("copying x to the device", e);
+  }
+  for (int j = 0; j < nchunk; ++j) {
+    const size_t off = static_cast<size_t>(t0s[j]), rows = static_cast<size_t>(t0s[j + 1] - t0s[j]);
+    rnb_moe_desc c = *d;
+    c.T = t0s[j + 1] - t0s[j];
+    e = cudaStreamWaitEvent(st, hp->ready[j], 0);
+    if (e != cudaSuccess) return cuda_fail("waiting for the copy-in", e);
+    rc = rnb_moe_block_fwd(&c, static_cast<char*>(x_dev) + off * row_in, static_cast<char*>(out_dev) + off * row_out,
+                           nullptr, nullptr, ws, ws_bytes, stream);
+    if (rc) {
+      join();
+      return rc;
+    }
+    e = cudaEventRecord(hp->computed[j], st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hp->out, hp->computed[j], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(static_cast<char*>(out_host) + off * row_out, static_cast<char*>(out_dev) + off * row_out,
+                          rows * row_out, cudaMemcpyDeviceToHost, hp->out);
+    if (e != cudaSuccess) return cuda_fail("copying out to the host", e);
+  }
+  e = cudaEventRecord(hp->done, hp->out);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(st, hp->done, 0);
+  if (e != cudaSuccess) return cuda_fail("joining the copy streams", e);
   return RNB_OK;
 }
 

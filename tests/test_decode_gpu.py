@@ -184,7 +184,7 @@ def test_block_call_host_round_trip_matches_moe_block(T):
     oh = torch.empty_like(xh).pin_memory()
     for _ in range(2):
         oh.zero_()
-        bc.host(xh, oh)  # pinned: the kernels store into oh directly
+        bc.host(xh, oh)  # pinned: direct stores up to 64 tokens, a copy-out above
         torch.cuda.current_stream().synchronize()
         assert torch.equal(oh, ref.cpu())
     pageable = torch.zeros_like(xh, device="cpu")

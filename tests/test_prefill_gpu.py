@@ -48,6 +48,31 @@ def test_prefill_zipf_skew_config3_sampled():
     assert_close(out.float().cpu().numpy(), out_c.float().cpu().numpy(), "prefill vs decode chain")
 
 
+@pytest.mark.parametrize("T", [4096, 8194])
+def test_host_entry_point_chunked_copies(T):
+    """From 4096 tokens rnb_moe_block_fwd_host splits the call into chunks of
+    whole tokens (2 here; 4 uneven ones at 8194) whose copies overlap compute.
+    The host buffer must hold exactly one block call per chunk, and stay
+    within the parity bounds of the whole-batch call."""
+    blk = inputs.make_block(4, seed=1, T=64)
+    bt = ops.BlockTensors.from_numpy(blk, "cuda")
+    x = torch.from_numpy(inputs.make_tokens(11, T)).view(torch.int16).view(torch.bfloat16).cuda()
+    n = min(4, T // 2048)
+    bounds = [T * j // n for j in range(n + 1)]
+    per_chunk = torch.cat([ops.moe_block(bt, x[a:b]) for a, b in zip(bounds[:-1], bounds[1:])]).cpu()
+    whole = ops.moe_block(bt, x).float().cpu().numpy()
+    bc = ops.BlockCall(bt, T)
+    xh = x.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    for _ in range(2):
+        oh.zero_()
+        bc.host(xh, oh)
+        torch.cuda.current_stream().synchronize()
+        assert torch.equal(oh, per_chunk)
+    assert_close(oh.float().numpy(), whole, f"chunked host call T={T}")
+    assert bc.ws.status() == 0
+
+
 def test_prefill_adversarial_routing_sampled():
     """A quarter of the tokens all route to one expert (many 128-row tiles of one expert)."""
     blk, bt, x, out, _ = _run(8, seed=4, T=1024, skew="adversarial", sample=32)
