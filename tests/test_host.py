@@ -141,3 +141,17 @@ def test_oracle_block_routing_semantics():
     ys = oracle.shared_expert(w, blk.x)
     ref = np.einsum("tk,tkh->th", scores, y) + sg[:, None] * ys
     np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-4)
+
+
+def test_prepared_block_call_refuses_host_tensors():
+    # the prepared call builds the same descriptor as every other entry point:
+    # a bank held in host memory fails loudly instead of running anywhere else
+    from runnel_b200 import ops
+
+    blk = inputs.make_block(4, seed=3, T=1, H=512, I=256, E=16)
+    bt = ops.BlockTensors(bits=4, **{f: torch.from_numpy(np.ascontiguousarray(getattr(blk, f)))
+                                    for f in ("gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b")})
+    with pytest.raises(ValueError, match="must be CUDA tensors"):
+        ops.BlockCall(bt, 1)
+    with pytest.raises(ValueError, match="T must be positive"):
+        ops.BlockCall(bt, 0)
