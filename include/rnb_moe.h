@@ -150,10 +150,17 @@ RNB_API int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, u
  * with RNB_ERR_WORKSPACE).  The first call on a device looks up that array's
  * address, so make it before any stream capture.  All calls share the one
  * array: calls that can overlap on the GPU (other streams, other threads)
- * race and must be serialised by the caller.  No counterpart in the
- * reference. */
+ * race and must be serialised by the caller.  The device status bits of
+ * these calls (RNB_STATUS_*) accumulate in the static array until
+ * rnb_moe_noalloc_status reads them.  No counterpart in the reference. */
 RNB_API int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void* out,
                                       uint32_t* inds_out, float* scores_out, void* stream);
+/* Status bits (RNB_STATUS_*) of the rnb_moe_block_fwd_noalloc calls on the
+ * current device since the last read: copies them to *status and clears
+ * them.  Synchronises the stream.  A call whose status has
+ * RNB_STATUS_TIMEOUT produced void results.  No counterpart in the
+ * reference. */
+RNB_API int rnb_moe_noalloc_status(uint32_t* status, void* stream);
 
 /* rnb_moe_block_fwd from host memory, one call for the whole round trip:
  * copies x_host ([T, H] bf16) into the device staging buffer x_dev, runs the
@@ -165,10 +172,12 @@ RNB_API int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void
  * out_host is page-locked, mapped for this device and 16-byte aligned, the
  * block's kernels store the result straight into it and out_dev is not used.  x_dev and out_dev
  * are caller-owned, 16-byte aligned and sized for T tokens.  From 4096 tokens
- * on, the call is split into 2-4 chunks of whole tokens whose copies run on
- * two copy streams of the library's own and overlap the other chunks' compute;
- * the first such call on a device creates those streams, so make it before any
- * stream capture.  No routing copies are
+ * on, when both host buffers are page-locked, the call is split into 2-4
+ * chunks of whole tokens whose copies run on two copy streams of the
+ * library's own and overlap the other chunks' compute; the output bits are
+ * those of one whole-batch call.  The first such call on a device creates
+ * those streams (valid for that device's context only, like every cached
+ * per-device object of this library), so make it before any stream capture.  No routing copies are
  * returned (use rnb_moe_block_fwd for those).  The reference's block call takes
  * unified-memory MLX arrays and needs no copies; on a discrete GPU this is the
  * closest call with host buffers. */

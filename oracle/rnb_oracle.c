@@ -322,6 +322,91 @@ int rnbo_shared_expert(const rnbo_block* d, float* y, int nthreads) {
   return RNBO_OK;
 }
 
+/* Sum of |terms| of one affine row against an fp32 vector:
+ * sum_k |(scale_g q_k + bias_g) x_k|, in double.  This is the magnitude the
+ * fp32 accumulation error of the dot product scales with. */
+static double affine_absdot(const uint32_t* w_row, const uint16_t* s_row, const uint16_t* b_row,
+                            const float* x, int K, int bits, int group) {
+  double acc = 0.0;
+  for (int k = 0; k < K; ++k) {
+    const int g = k / group;
+    const double w = (double)rnbo_bf16_to_f32(s_row[g]) * (double)code_at(w_row, bits, (size_t)k) +
+                     (double)rnbo_bf16_to_f32(b_row[g]);
+    acc += fabs(w * (double)x[k]);
+  }
+  return acc;
+}
+
+/* Per-output magnitude of one expert on one token: mag[n] += weight *
+ * sum_i |w_dn[n,i] h_i| with h the expert's fp32 SwiGLU row for x. */
+static void expert_mag(int H, int I, int bits, int group, const uint32_t* guw, const uint16_t* gus,
+                       const uint16_t* gub, const uint32_t* dnw, const uint16_t* dns, const uint16_t* dnb,
+                       const float* xf, float* hbuf, double weight, double* mag) {
+  const size_t gu_ws = (size_t)H * bits / 32, gu_ss = (size_t)H / group;
+  const size_t dn_ws = (size_t)I * bits / 32, dn_ss = (size_t)I / group;
+  for (int c = 0; c < I; ++c) {
+    const float up = rnbo_affine_dot(guw + c * gu_ws, gus + c * gu_ss, gub + c * gu_ss, xf, H, bits, group);
+    const size_t g = (size_t)(c + I);
+    const float gate = rnbo_affine_dot(guw + g * gu_ws, gus + g * gu_ss, gub + g * gu_ss, xf, H, bits, group);
+    hbuf[c] = (gate / (1.0f + expf(-gate))) * up;
+  }
+  for (int n = 0; n < H; ++n)
+    mag[n] += weight * affine_absdot(dnw + n * dn_ws, dns + n * dn_ss, dnb + n * dn_ss, hbuf, I, bits, group);
+}
+
+/* Magnitude of every block output element: the sum of the absolute values
+ * of the products its final accumulation adds,
+ *   mag[t,n] = sum_s |score[t,s]| sum_i |w_dn_e[n,i] h_e,i| + |sg[t]| sum_i |w_sdn[n,i] hs_i|
+ * (per-slot unweighted magnitudes of rnbo_switchglu when scores is NULL:
+ * mag [T,k,H]).  inds/scores/sg are the routing of rnbo_router; sg may be
+ * NULL (no shared expert).  fp32 summation of n such products in any order
+ * errs by at most (n-1) 2^-24 mag, which the parity tests use as the floor of
+ * their tolerance for outputs that cancel. */
+int rnbo_block_mag(const rnbo_block* d, const int32_t* inds, const float* scores, const float* sg,
+                   float* mag, int nthreads) {
+  if (!block_valid(d)) return RNBO_EINVAL;
+  const int T = d->T, H = d->H, I = d->I, K = d->k, bits = d->bits, G = d->group;
+  for (int i = 0; i < T * K; ++i)
+    if (inds[i] < 0 || inds[i] >= d->E) return RNBO_EINVAL;
+  const size_t gu_we = (size_t)2 * I * H * bits / 32, gu_se = (size_t)2 * I * H / G;
+  const size_t dn_we = (size_t)H * I * bits / 32, dn_se = (size_t)H * I / G;
+  const int per_slot = scores == NULL;
+  int rc = RNBO_OK;
+#pragma omp parallel num_threads(nthreads > 0 ? nthreads : 1)
+  {
+    float* xf = (float*)malloc(sizeof(float) * H);
+    float* hb = (float*)malloc(sizeof(float) * I);
+    double* acc = (double*)malloc(sizeof(double) * H);
+#pragma omp for schedule(dynamic, 1)
+    for (int t = 0; t < T; ++t) {
+      x_row_f32(d, t, xf);
+      for (int n = 0; n < H; ++n) acc[n] = 0.0;
+      for (int s = 0; s < K; ++s) {
+        const size_t e = (size_t)inds[(size_t)t * K + s];
+        const double wgt = per_slot ? 1.0 : fabs((double)scores[(size_t)t * K + s]);
+        expert_mag(H, I, bits, G, d->gu_w + e * gu_we, d->gu_s + e * gu_se, d->gu_b + e * gu_se,
+                   d->dn_w + e * dn_we, d->dn_s + e * dn_se, d->dn_b + e * dn_se, xf, hb, wgt, acc);
+        if (per_slot) {
+          for (int n = 0; n < H; ++n) {
+            mag[((size_t)t * K + s) * H + n] = (float)acc[n];
+            acc[n] = 0.0;
+          }
+        }
+      }
+      if (!per_slot) {
+        if (sg && d->sgu_w)
+          expert_mag(H, I, bits, G, d->sgu_w, d->sgu_s, d->sgu_b, d->sdn_w, d->sdn_s, d->sdn_b, xf, hb,
+                     fabs((double)sg[t]), acc);
+        for (int n = 0; n < H; ++n) mag[(size_t)t * H + n] = (float)acc[n];
+      }
+    }
+    free(xf);
+    free(hb);
+    free(acc);
+  }
+  return rc;
+}
+
 /* Whole block: out[t] = sum_s score[t,s] * y[t,s] + sigmoid(x.w_sg) * shared(x). */
 int rnbo_moe_block(const rnbo_block* d, float* out, int32_t* inds, float* scores,
                    float* logits, int nthreads) {

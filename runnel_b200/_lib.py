@@ -62,6 +62,7 @@ SIGNATURES = {
     "rnb_moe_block_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "rnb_moe_status": (ctypes.c_int, [_vp, _sz, ctypes.POINTER(ctypes.c_uint32), _vp]),
     "rnb_moe_block_fwd_noalloc": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp]),
+    "rnb_moe_noalloc_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _vp]),
     "rnb_moe_block_fwd_host": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "rnb_moe_experts_workspace_size": (ctypes.c_int, [_DescP, ctypes.POINTER(_sz)]),
     "rnb_moe_experts_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -2194,7 +2194,19 @@ int host_pipe(HostPipe** out) {
       e = cudaEventCreateWithFlags(&hp.ready[j], cudaEventDisableTiming);
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(&hp.computed[j], cudaEventDisableTiming);
     }
-    if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("creating copy streams: ") + cudaGetErrorString(e));
+    if (e != cudaSuccess) {
+      // release what was made, so a later attempt starts from nothing
+      for (cudaStream_t* s : {&hp.in, &hp.out})
+        if (*s) (void)cudaStreamDestroy(*s);
+      for (cudaEvent_t* v : {&hp.start, &hp.done})
+        if (*v) (void)cudaEventDestroy(*v);
+      for (int j = 0; j < kHostMaxChunks; ++j) {
+        if (hp.ready[j]) (void)cudaEventDestroy(hp.ready[j]);
+        if (hp.computed[j]) (void)cudaEventDestroy(hp.computed[j]);
+      }
+      hp = HostPipe{};
+      return fail(RNB_ERR_CUDA, std::string("creating copy streams: ") + cudaGetErrorString(e));
+    }
     made[dev] = true;
   }
   *out = &hp;
@@ -2350,7 +2362,19 @@ int rnb_moe_block_fwd_host(const rnb_moe_desc* d, const void* x_host, void* out_
   } else {
     (void)cudaGetLastError();  // an unknown (pageable) pointer is not an error here
   }
-  const int nchunk = std::min(kHostMaxChunks, d->T / kHostChunkMin);
+  // Chunked copies only between page-locked host buffers: a copy from or to
+  // pageable memory blocks the host thread, which would serialise the chunks
+  // while the pipe's lock is held.
+  auto pinned = [](const void* ptr) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+  };
+  int nchunk = std::min(kHostMaxChunks, d->T / kHostChunkMin);
+  if (nchunk >= 2 && !(pinned(x_host) && pinned(out_host))) nchunk = 1;
   if (nchunk < 2) {
     cudaError_t e = cudaMemcpyAsync(x_dev, x_host, n * 2, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("copying x to the device: ") + cudaGetErrorString(e));
@@ -2447,11 +2471,24 @@ int rnb_moe_block_fwd_noalloc(const rnb_moe_desc* d, const void* x, void* out, u
   void* ws = nullptr;
   rc = noalloc_scratch(&ws);
   if (rc) return rc;
-  // The status word and arrival counters must start at zero; a call leaves
-  // them at zero, but clear them so a call never depends on earlier ones.
-  const cudaError_t e = cudaMemsetAsync(ws, 0, L.xperm, static_cast<cudaStream_t>(stream));
+  // The arrival counters must start at zero; a call leaves them at zero, but
+  // clear them so a call never depends on earlier ones.  The status word (the
+  // first 256-byte slot) is left alone: its bits add up over calls until
+  // rnb_moe_noalloc_status reads and clears them.
+  const cudaError_t e = cudaMemsetAsync(static_cast<char*>(ws) + L.ctr, 0, L.xperm - L.ctr,
+                                        static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("clearing scratch counters: ") + cudaGetErrorString(e));
   return rnb_moe_block_fwd(d, x, out, inds_out, scores_out, ws, kNoAllocScratchBytes, stream);
+}
+
+int rnb_moe_noalloc_status(uint32_t* status, void* stream) {
+  if (!status) return fail(RNB_ERR_INVALID, "status must be non-NULL");
+  int rc = check_device();
+  if (rc) return rc;
+  void* ws = nullptr;
+  rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  return rnb_moe_status(ws, kNoAllocScratchBytes, status, stream);
 }
 
 }  // extern "C"

@@ -1,14 +1,25 @@
 """Tolerance checks shared by the parity tests.
 
-Block and SwitchGLU outputs are bf16; they are compared with the oracle's
-fp32-accumulated result by two bounds (stated once here, used everywhere):
+Block and SwitchGLU outputs are bf16 (or fp32); they are compared with the
+oracle's fp32-accumulated result, element by element, by the bound the
+reference's correctness criterion states:
 
 * relative L2 error ``||out - ref|| / ||ref|| <= 5e-3``;
-* element-wise ``|out - ref| <= 2 ulp_bf16(max(|ref|, rms(ref)))`` -- two
-  bf16 units in the last place at the element's own magnitude, with
-  magnitudes below the tensor's RMS measured at the RMS (an element far
-  below the typical output magnitude is a cancellation, and its absolute
-  error is that of the typical terms that cancelled).
+* every element ``|out - ref| <= max(2 ulp_bf16(|ref|), FLOOR * mag)``:
+  two bf16 units in the last place at the element's OWN magnitude, with one
+  floor for outputs that cancel.  ``mag`` is the sum of the absolute values
+  of the products the element's final accumulation adds
+  (``oracle.block_mag``: routing weights x |down row| . |SwiGLU row|, over the
+  selected experts and the shared expert).  Any fp32 evaluation of a sum of n
+  products errs by up to (n - 1) 2^-24 mag; with n = 9 x 512 = 4608
+  products per block output (8 routed experts and the shared expert, 512
+  channels each) that is 2^-11.8 mag, and FLOOR = 2^-12 mag sits just
+  under it.  An element is held to the floor only where 2 ulps of its own
+  value are smaller, i.e. where the products cancel to well under mag.
+
+``strict_ulp_max`` (the largest error in ulps of the element's own value,
+no floor) and ``floor_elements`` (how many elements needed the floor) are
+reported with every comparison.
 
 Routing must match exactly: the same expert indices in the same slot order.
 """
@@ -18,6 +29,7 @@ import numpy as np
 
 REL_L2 = 5e-3
 ULPS = 2.0
+FLOOR = 2.0 ** -12
 
 
 def bf16_ulp(mag: np.ndarray) -> np.ndarray:
@@ -25,26 +37,57 @@ def bf16_ulp(mag: np.ndarray) -> np.ndarray:
     return 2.0 ** (np.floor(np.log2(mag)) - 7)
 
 
-def compare(out, ref, rel_l2: float = REL_L2, ulps: float = ULPS) -> dict:
+def compare(out, ref, mag=None, rel_l2: float = REL_L2, ulps: float = ULPS, floor: float = FLOOR) -> dict:
     out = np.asarray(out, np.float64)
     ref = np.asarray(ref, np.float64)
-    err = out - ref
-    rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
-    mag = np.maximum(np.abs(ref), rms)
-    tol = ulps * bf16_ulp(mag)
-    ratio = np.abs(err) / tol
+    err = np.abs(out - ref)
+    own = ulps * bf16_ulp(ref)
+    tol = own if mag is None else np.maximum(own, floor * np.asarray(mag, np.float64))
+    ratio = err / tol
     stats = {
-        "rel_l2": float(np.linalg.norm(err) / max(np.linalg.norm(ref), 1e-30)),
-        "max_abs": float(np.max(np.abs(err))) if err.size else 0.0,
-        "max_ulp_ratio": float(np.max(ratio)) if err.size else 0.0,
-        "strict_ulp_max": float(np.max(np.abs(err) / bf16_ulp(ref))) if err.size else 0.0,
-        "rms_ref": rms,
+        "rel_l2": float(np.linalg.norm(out - ref) / max(np.linalg.norm(ref), 1e-30)),
+        "max_abs": float(np.max(err)) if err.size else 0.0,
+        "strict_ulp_max": float(np.max(err / bf16_ulp(ref))) if err.size else 0.0,
+        "max_tol_ratio": float(np.max(ratio)) if err.size else 0.0,
+        "floor_elements": int(np.count_nonzero(err > own)),
+        "elements": int(err.size),
     }
-    stats["ok"] = bool(stats["rel_l2"] <= rel_l2 and stats["max_ulp_ratio"] <= 1.0)
+    stats["ok"] = bool(stats["rel_l2"] <= rel_l2 and stats["max_tol_ratio"] <= 1.0)
     return stats
 
 
-def assert_close(out, ref, what: str = "output", **kw):
-    s = compare(out, ref, **kw)
+def assert_close(out, ref, what: str = "output", mag=None, **kw):
+    s = compare(out, ref, mag=mag, **kw)
+    print(f"{what}: strict_ulp_max={s['strict_ulp_max']:.3f} rel_l2={s['rel_l2']:.2e} "
+          f"floor_elements={s['floor_elements']}/{s['elements']} max_tol_ratio={s['max_tol_ratio']:.3f}")
     assert s["ok"], f"{what}: {s}"
     return s
+
+
+def assert_close_gpu_pair(a, b, what: str = "output"):
+    """Cross-check of two GPU paths of the same block (no oracle in the
+    loop), e.g. expert-parallel against single-GPU.  Each side is already
+    held to the oracle bound in its own test; here elements below the
+    tensor's RMS are measured at the RMS (two correct results can differ by
+    both errors, and without the oracle's magnitudes there is no per-element
+    floor).  Never used for an oracle comparison."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    rms = float(np.sqrt(np.mean(b * b))) if b.size else 0.0
+    err = np.abs(a - b)
+    tol = 2 * ULPS * bf16_ulp(np.maximum(np.abs(b), rms))
+    rel = float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+    ratio = float(np.max(err / tol)) if err.size else 0.0
+    print(f"{what} (GPU pair): rel_l2={rel:.2e} max_ratio={ratio:.3f}")
+    assert rel <= REL_L2 and ratio <= 1.0, f"{what}: rel_l2={rel} max_ratio={ratio}"
+
+
+def oracle_block(w, x, k: int = 8):
+    """The oracle's block output, routing and output magnitudes for x:
+    (ref [T,H], inds [T,k], scores [T,k], mag [T,H])."""
+    from oracle import oracle
+
+    _, inds, scores, sg = oracle.router(w, x, k=k)
+    ref, oinds, oscores = oracle.moe_block(w, x, k=k)
+    mag = oracle.block_mag(w, x, inds, scores, sg if w.sgu_w is not None else None)
+    return ref, oinds, oscores, mag

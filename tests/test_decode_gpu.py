@@ -16,7 +16,7 @@ from oracle import oracle
 from runnel_b200 import inputs, ops
 from runnel_b200 import switch_layers as sl
 from runnel_b200 import _lib
-from tests._parity import assert_close, compare
+from tests._parity import assert_close, compare, oracle_block
 
 pytestmark = pytest.mark.gpu
 
@@ -61,10 +61,10 @@ def test_block_matches_oracle(bits, T):
     blk, bt, w = _setup(bits)
     x = _x(blk, T)
     out, inds, scores = ops.moe_block(bt, x, return_routing=True)
-    ref, oinds, oscores = oracle.moe_block(w, blk.x[:T], k=8)
+    ref, oinds, oscores, mag = oracle_block(w, blk.x[:T])
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
     np.testing.assert_allclose(scores.cpu().numpy(), oscores, rtol=2e-5, atol=1e-7)
-    s = assert_close(_f32(out), ref, f"block q{bits} T={T}")
+    s = assert_close(_f32(out), ref, f"block q{bits} T={T}", mag=mag)
     print(f"q{bits} T={T}: {json.dumps(s)}")
 
 
@@ -79,11 +79,11 @@ def test_switchglu_matches_oracle_with_repeated_experts(bits):
     x = _x(blk, T)
     y = ops.switchglu(bt, x, torch.from_numpy(inds).cuda(), out_dtype=torch.float32)
     ref = oracle.switchglu(w, blk.x[:T], inds)
-    s = compare(y.cpu().numpy(), ref)
-    assert s["ok"], s
+    mag = oracle.block_mag(w, blk.x[:T], inds)
+    assert_close(y.cpu().numpy(), ref, "switchglu fp32", mag=mag)
     yb = ops.switchglu(bt, x, torch.from_numpy(inds).cuda())
     assert yb.dtype == torch.bfloat16 and yb.shape == (T, k, 2048)
-    assert_close(_f32(yb), ref, "switchglu bf16")
+    assert_close(_f32(yb), ref, "switchglu bf16", mag=mag)
 
 
 @pytest.mark.parametrize("bits,expected", [(8, 6.836), (4, 170.073)])
@@ -103,10 +103,11 @@ def test_reference_two_stage_kat_on_gpu(bits, expected):
     inds = torch.from_numpy(data["selected"].astype(np.int32)).reshape(1, 8).cuda()
     y = ops.switchglu(bt, x, inds, out_dtype=torch.float32)[0].cpu().numpy().astype(np.float64)
     out = (data["route_w"].astype(np.float64)[:, None] * y).sum(0)
-    # fp32 output: the only rounding left is the fp16 copy of the SwiGLU
-    # activations fed to the down projection (11-bit significand)
-    s = compare(out, ref_out, rel_l2=1e-3, ulps=2)
-    assert s["ok"], s
+    kw = oracle.BlockWeights(bits=bits, group=64, router_w=np.zeros((64, 2048), np.uint16),
+                             **{n: data[n] for n in ("gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b")})
+    mag = oracle.block_mag(kw, data["x"].reshape(1, -1), data["selected"].astype(np.int32).reshape(1, 8),
+                           data["route_w"].reshape(1, 8))[0]
+    assert_close(out, ref_out, f"two-stage KAT q{bits}", mag=mag, rel_l2=1e-3)
     assert abs(out.sum() - ref_cs) < 5e-3, (out.sum(), ref_cs)
 
 
@@ -122,9 +123,9 @@ def test_block_beyond_one_launch_chain(T):
     bt = ops.BlockTensors.from_numpy(blk, "cuda")
     w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
     out, inds, _ = ops.moe_block(bt, _x(blk, T), return_routing=True)
-    ref, oinds, _ = oracle.moe_block(w, blk.x, k=8)
+    ref, oinds, _, mag = oracle_block(w, blk.x)
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
-    assert_close(_f32(out), ref, f"block T={T}")
+    assert_close(_f32(out), ref, f"block T={T}", mag=mag)
 
 
 def test_expert_shard_switchglu():
@@ -221,18 +222,21 @@ def test_persistent_kernel_matches_chain_and_oracle(bits, T):
     out, inds, scores = ops.moe_block(bt, x, return_routing=True)
     chain = ops.BlockTensors(**{**bt.__dict__, "flags": bt.flags | _lib.FLAG_CHAIN})
     out_c, inds_c, _ = ops.moe_block(chain, x, return_routing=True)
-    ref, oinds, oscores = oracle.moe_block(w, blk.x[:T], k=8)
+    ref, oinds, oscores, mag = oracle_block(w, blk.x[:T])
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
     np.testing.assert_array_equal(inds_c.cpu().numpy(), oinds)
     np.testing.assert_allclose(scores.cpu().numpy(), oscores, rtol=2e-5, atol=1e-7)
-    assert_close(_f32(out), ref, f"persistent q{bits} T={T}")
-    assert_close(_f32(out), _f32(out_c), "persistent vs chain")
+    assert_close(_f32(out), ref, f"persistent q{bits} T={T}", mag=mag)
+    assert_close(_f32(out_c), ref, f"chain q{bits} T={T}", mag=mag)
     ws = ops.Workspace("cuda")
     for i in range(3):  # back-to-back calls reuse the counters
-        xi = torch.from_numpy(inputs.make_tokens(9 + i, T)).view(torch.int16).view(torch.bfloat16).cuda()
+        xn = inputs.make_tokens(9 + i, T)
+        xi = torch.from_numpy(xn).view(torch.int16).view(torch.bfloat16).cuda()
         a = ops.moe_block(bt, xi, ws=ws)
         b = ops.moe_block(chain, xi, ws=ws)
-        assert_close(_f32(a), _f32(b), f"call {i}")
+        ref_i, _, _, mag_i = oracle_block(w, xn)
+        assert_close(_f32(a), ref_i, f"persistent call {i}", mag=mag_i)
+        assert_close(_f32(b), ref_i, f"chain call {i}", mag=mag_i)
     assert ws.status() == 0
 
 
@@ -266,15 +270,16 @@ def test_small_bank_many_tokens_fresh_workspace(T):
     bt = ops.BlockTensors.from_numpy(blk, "cuda")
     x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
     w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
-    ref, oinds, _ = oracle.moe_block(w, blk.x, k=8)
+    ref, oinds, _, mag = oracle_block(w, blk.x)
     out, inds, _ = ops.moe_block(bt, x, ws=ops.Workspace("cuda"), return_routing=True)
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
-    assert_close(out.float().cpu().numpy(), ref, f"E=16 T={T} fresh workspace")
+    assert_close(out.float().cpu().numpy(), ref, f"E=16 T={T} fresh workspace", mag=mag)
     shard = ops.BlockTensors.from_numpy(blk, "cuda", E_range=(4, 12))
     part = ops.moe_block(ops.BlockTensors(**{**shard.__dict__, "flags": _lib.FLAG_Y_F32 | _lib.FLAG_NO_SHARED}),
                          x, ws=ops.Workspace("cuda"))
     keep = (oinds >= 4) & (oinds < 12)
     _, _, osc, _ = oracle.router(w, blk.x, k=8)
     y = oracle.switchglu(w, blk.x, oinds)
-    assert_close(part.cpu().numpy(), np.einsum("tk,tkh->th", np.where(keep, osc, 0.0).astype(np.float32), y),
-                 f"E=16 shard T={T} fresh workspace")
+    wk = np.where(keep, osc, 0.0).astype(np.float32)
+    assert_close(part.cpu().numpy(), np.einsum("tk,tkh->th", wk, y), f"E=16 shard T={T} fresh workspace",
+                 mag=oracle.block_mag(w, blk.x, oinds, wk))

@@ -13,7 +13,7 @@ import torch
 
 from oracle import oracle
 from runnel_b200 import _lib, ep, inputs, ops
-from tests._parity import assert_close
+from tests._parity import assert_close, assert_close_gpu_pair, oracle_block
 
 pytestmark = pytest.mark.gpu
 
@@ -21,8 +21,9 @@ BITS, SEED = 4, 1
 
 
 def _ref(blk, T):
+    """(ref, inds, scores, mag) of the oracle on the first T tokens."""
     w = oracle.BlockWeights(bits=BITS, group=64, **blk.weight_fields())
-    return oracle.moe_block(w, blk.x[:T], k=8)
+    return oracle_block(w, blk.x[:T])
 
 
 def test_single_rank_context_matches_block():
@@ -34,13 +35,14 @@ def test_single_rank_context_matches_block():
     try:
         for T in (1, 8, 5):
             out, inds, _ = ctx.moe_block(bt, x[:T], return_routing=True)
-            ref, oinds, _ = _ref(blk, T)
+            ref, oinds, _, mag = _ref(blk, T)
             np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
-            assert_close(out.float().cpu().numpy(), ref, f"ep world 1 T={T}")
+            assert_close(out.float().cpu().numpy(), ref, f"ep world 1 T={T}", mag=mag)
         f32 = ops.BlockTensors(**{**bt.__dict__, "flags": _lib.FLAG_Y_F32})
         out = ctx.moe_block(f32, x[:2])
         assert out.dtype == torch.float32
-        assert_close(out.cpu().numpy(), _ref(blk, 2)[0], "ep world 1 fp32")
+        r2 = _ref(blk, 2)
+        assert_close(out.cpu().numpy(), r2[0], "ep world 1 fp32", mag=r2[3])
     finally:
         ctx.close()
 
@@ -71,9 +73,9 @@ def _rank_main(rank, world, port):
         for T in (1, 8, 3, 1, 8, 2):  # repeated calls alternate the exchange parity
             dist.barrier(group=gloo)  # ranks enter each exchange together
             out, inds, _ = ctx.moe_block(shard, x[:T], ws=ws, return_routing=True)
-            ref, oinds, _ = _ref(blk, T)
+            ref, oinds, _, mag = _ref(blk, T)
             np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
-            assert_close(out.float().cpu().numpy(), ref, f"ep p2p rank {rank} T={T}")
+            assert_close(out.float().cpu().numpy(), ref, f"ep p2p rank {rank} T={T}", mag=mag)
             # every rank holds the same bits (the sum runs in rank order everywhere)
             allv = [torch.empty_like(out) for _ in range(world)]
             dist.all_gather(allv, out)
@@ -81,7 +83,8 @@ def _rank_main(rank, world, port):
                 assert torch.equal(v, out)
         assert ws.status() == 0
         out_n = ep.moe_block_nccl(shard, x[:8], rank, ws=ws)
-        assert_close(out_n.float().cpu().numpy(), _ref(blk, 8)[0], f"ep nccl rank {rank}")
+        r8 = _ref(blk, 8)
+        assert_close(out_n.float().cpu().numpy(), r8[0], f"ep nccl rank {rank}", mag=r8[3])
         # a two-layer stack, expert parallel, against the same stack on one GPU
         from runnel_b200 import stack
         lo, hi, _ = ep.plan(rank, world)
@@ -90,7 +93,7 @@ def _rank_main(rank, world, port):
         one = stack.LayerStack(full_l, norms, ws=ops.Workspace(dev)).forward(x[:1])
         dist.barrier(group=gloo)
         par = stack.LayerStack(shard_l, norms, ep=ctx, ws=ws).forward(x[:1])
-        assert_close(par.float().cpu().numpy(), one.float().cpu().numpy(), f"ep stack rank {rank}")
+        assert_close_gpu_pair(par.float().cpu().numpy(), one.float().cpu().numpy(), f"ep stack rank {rank}")
         assert ws.status() == 0
         # all-to-all dispatch/combine over each rank's own tokens against the
         # whole bank on one GPU (prefill-size, decode-size, ragged and empty)
@@ -104,19 +107,20 @@ def _rank_main(rank, world, port):
             got = ep.moe_block_a2a(shard, xr, rank, world, ws=ws, stats=stats)
             want, winds, _ = ops.moe_block(full, xr, ws=ws, return_routing=True)
             if xr.shape[0]:
-                assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(), f"ep a2a rank {rank} case {i}")
+                assert_close_gpu_pair(got.float().cpu().numpy(), want.float().cpu().numpy(),
+                                      f"ep a2a rank {rank} case {i}")
             assert stats["sent"] <= xr.shape[0] * (world - 1)
             if t0 == t1:  # the gather / reduce-scatter form needs equal token counts
                 got = ep.moe_block_gather(shard, xr, rank, world, ws=ws)
                 if xr.shape[0]:
-                    assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(),
-                                 f"ep gather rank {rank} case {i}")
+                    assert_close_gpu_pair(got.float().cpu().numpy(), want.float().cpu().numpy(),
+                                          f"ep gather rank {rank} case {i}")
         g.manual_seed(7 + rank)
         xr = torch.randn((200, blk.H), device=dev, generator=g).to(torch.bfloat16)
         dist.barrier(group=gloo)
         got = ep.moe_block_gather(shard, xr, rank, world, ws=ws)
         want = ops.moe_block(full, xr, ws=ws)
-        assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(), f"ep gather rank {rank} T=200")
+        assert_close_gpu_pair(got.float().cpu().numpy(), want.float().cpu().numpy(), f"ep gather rank {rank} T=200")
         assert ws.status() == 0
         torch.cuda.synchronize()
         dist.barrier()

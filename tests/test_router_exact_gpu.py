@@ -17,7 +17,7 @@ import torch
 from oracle import oracle
 from runnel_b200 import inputs, ops
 from runnel_b200.quant import bf16_bits_to_f32, f32_to_bf16_bits
-from tests._parity import assert_close
+from tests._parity import assert_close, oracle_block
 
 H, E = 2048, 256
 
@@ -79,10 +79,10 @@ def test_block_midpoints(T):
     bt = ops.BlockTensors.from_numpy(blk, "cuda")
     x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
     out, inds, scores = ops.moe_block(bt, x, return_routing=True)
-    ref, oinds, oscores = oracle.moe_block(_oracle(blk, bits), blk.x, k=8)
+    ref, oinds, oscores, mag = oracle_block(_oracle(blk, bits), blk.x)
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
     np.testing.assert_allclose(scores.cpu().numpy(), oscores, rtol=2e-5, atol=1e-7)
-    assert_close(out.float().cpu().numpy(), ref, f"midpoint block T={T}")
+    assert_close(out.float().cpu().numpy(), ref, f"midpoint block T={T}", mag=mag)
 
 
 @pytest.mark.gpu

@@ -9,7 +9,7 @@ import torch
 from oracle import oracle
 from runnel_b200 import inputs, ops, stack
 from runnel_b200.quant import bf16_bits_to_f32, f32_to_bf16_bits
-from tests._parity import assert_close
+from tests._parity import assert_close, oracle_block
 
 pytestmark = pytest.mark.gpu
 
@@ -70,8 +70,8 @@ def test_stack_layer_by_layer_matches_oracle():
             np.testing.assert_array_equal(_bits(xa), rxa)
             assert _ulp_steps(_bits(xn), rxn).max() <= 1
             # block l on the GPU's own input
-            ref, oinds, _ = oracle.moe_block(ws[l], _bits(xn), k=8)
-            assert_close(y.float().cpu().numpy(), ref, f"token {tok} layer {l}")
+            ref, oinds, _, mag = oracle_block(ws[l], _bits(xn))
+            assert_close(y.float().cpu().numpy(), ref, f"token {tok} layer {l}", mag=mag)
         last = stack.reference_add_rmsnorm(_bits(rec[-1][0]), _bits(rec[-1][2]), norms_bits[-1])[0]
         np.testing.assert_array_equal(_bits(out), last)
         x = out

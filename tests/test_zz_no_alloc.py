@@ -7,6 +7,8 @@ variant keeps its scratch in a static device array of the library instead.
 Here it is called through the C ABI and must agree with the workspace entry
 point on the same inputs, on two calls in a row (the second with other
 tokens, so nothing left in the shared scratch by the first can leak in).
+The status bits of these calls are read back with rnb_moe_noalloc_status,
+since the caller has no workspace to pass to rnb_moe_status.
 This file sorts last so a run that stops at the first failure has run every
 other test before it.
 """
@@ -16,8 +18,9 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import oracle
 from runnel_b200 import _lib, inputs, ops
-from tests._parity import assert_close
+from tests._parity import assert_close, oracle_block
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
@@ -53,4 +56,17 @@ def test_noalloc_matches_workspace_entry_point_twice():
         torch.cuda.synchronize()
         assert torch.equal(inds, rinds)
         np.testing.assert_allclose(scores.cpu().numpy(), rscores.cpu().numpy(), rtol=2e-5, atol=1e-7)
-        assert_close(out.float().cpu().numpy(), ref.float().cpu().numpy(), "noalloc vs workspace")
+        assert torch.equal(out, ref), "the no-alloc call differs from the workspace call"
+        # and on its own against the CPU oracle
+        w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
+        oref, oinds, _, mag = oracle_block(w, x_np)
+        np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
+        assert_close(out.float().cpu().numpy(), oref, "noalloc vs oracle", mag=mag)
+    # the two calls set no status bit (no timeout, no bad index), and reading
+    # the status clears it
+    status = ctypes.c_uint32(0xFFFFFFFF)
+    rc = lib.rnb_moe_noalloc_status(ctypes.byref(status), stream)
+    assert rc == 0, lib.rnb_last_error().decode()
+    assert status.value == 0
+    rc = lib.rnb_moe_noalloc_status(ctypes.byref(status), stream)
+    assert rc == 0 and status.value == 0
