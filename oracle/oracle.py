@@ -199,14 +199,17 @@ def moe_block(w: BlockWeights, x: np.ndarray, k: int = 8, nthreads: int | None =
     return out, inds, scores
 
 
-def block_mag(w: BlockWeights, x: np.ndarray, inds: np.ndarray, scores: np.ndarray | None = None,
-              sg: np.ndarray | None = None, nthreads: int | None = None) -> np.ndarray:
-    """Magnitude (sum of |products| of the final accumulation) of every output.
+def block_bound(w: BlockWeights, x: np.ndarray, inds: np.ndarray, scores: np.ndarray | None = None,
+                sg: np.ndarray | None = None, nthreads: int | None = None) -> np.ndarray:
+    """First-order forward error bound of an fp32 evaluation of every output.
 
-    With ``scores`` (and the shared gate ``sg`` of :func:`router`) it is the
-    block output's magnitude ``[T, H]``; without, the per-slot unweighted
-    SwitchGLU magnitude ``[T, k, H]``.  The parity tolerance's floor for
-    cancelling outputs scales with it (tests/_parity.py)."""
+    With ``scores`` (and the shared gate ``sg`` of :func:`router`) it bounds
+    the block output ``[T, H]``; without, each slot's unweighted SwitchGLU
+    output ``[T, k, H]``.  Every dot product is allowed the classical
+    any-order fp32 summation error gamma_n * sum|terms| (n its length, u =
+    2^-24), propagated through SwiGLU, the down projection and the combine
+    (rnb_oracle.c, rnbo_block_bound).  The parity tolerance uses it as the
+    floor for outputs that cancel (tests/_parity.py)."""
     inds = np.ascontiguousarray(inds, dtype=np.int32)
     keep: list = []
     d = _block_struct(w, x, inds.shape[1], keep)
@@ -214,23 +217,17 @@ def block_mag(w: BlockWeights, x: np.ndarray, inds: np.ndarray, scores: np.ndarr
     if scores is not None:
         scores = np.ascontiguousarray(scores, dtype=np.float32)
         keep.append(scores)
-        mag = np.empty((T, w.H), np.float32)
+        out = np.empty((T, w.H), np.float32)
     else:
-        mag = np.empty((T, K, w.H), np.float32)
+        out = np.empty((T, K, w.H), np.float32)
     if sg is not None:
         sg = np.ascontiguousarray(sg, dtype=np.float32)
         keep.append(sg)
-    rc = lib().rnbo_block_mag(ctypes.byref(d), _p(inds, _i32p), _p(scores, _f32p), _p(sg, _f32p),
-                              _p(mag, _f32p), nthreads or nthreads_default())
+    rc = lib().rnbo_block_bound(ctypes.byref(d), _p(inds, _i32p), _p(scores, _f32p), _p(sg, _f32p),
+                                _p(out, _f32p), nthreads or nthreads_default())
     if rc:
-        raise ValueError(f"oracle block_mag rejected the call (rc={rc})")
-    return mag
-
-
-def moe_block_mag(w: BlockWeights, x: np.ndarray, k: int = 8, nthreads: int | None = None) -> np.ndarray:
-    """Block output magnitude ``[T, H]`` for the oracle's own routing of x."""
-    _, inds, scores, sg = router(w, x, k=k, nthreads=nthreads)
-    return block_mag(w, x, inds, scores, sg if w.sgu_w is not None else None, nthreads=nthreads)
+        raise ValueError(f"oracle block_bound rejected the call (rc={rc})")
+    return out
 
 
 def affine_matvec(w, s, b, x_f32, bits: int, group: int, nthreads: int | None = None):

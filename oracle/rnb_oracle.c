@@ -322,48 +322,84 @@ int rnbo_shared_expert(const rnbo_block* d, float* y, int nthreads) {
   return RNBO_OK;
 }
 
-/* Sum of |terms| of one affine row against an fp32 vector:
- * sum_k |(scale_g q_k + bias_g) x_k|, in double.  This is the magnitude the
- * fp32 accumulation error of the dot product scales with. */
-static double affine_absdot(const uint32_t* w_row, const uint16_t* s_row, const uint16_t* b_row,
-                            const float* x, int K, int bits, int group) {
-  double acc = 0.0;
+/* ------------------------------------------- forward error bound */
+
+/* gamma_n = n u / (1 - n u), u = 2^-24: the classical bound on the relative
+ * error (to the sum of |terms|) of an n-term fp32 sum in any order. */
+static double gamma_n(double n) {
+  const double u = 0x1p-24;
+  return n * u / (1.0 - n * u);
+}
+
+/* Dot product of one affine row with x, in double, plus sum |terms|. */
+static double affine_dot_abs(const uint32_t* w_row, const uint16_t* s_row, const uint16_t* b_row,
+                             const double* x, int K, int bits, int group, double* abs_sum) {
+  double acc = 0.0, a = 0.0;
   for (int k = 0; k < K; ++k) {
     const int g = k / group;
     const double w = (double)rnbo_bf16_to_f32(s_row[g]) * (double)code_at(w_row, bits, (size_t)k) +
                      (double)rnbo_bf16_to_f32(b_row[g]);
-    acc += fabs(w * (double)x[k]);
+    acc += w * x[k];
+    a += fabs(w * x[k]);
   }
+  *abs_sum = a;
   return acc;
 }
 
-/* Per-output magnitude of one expert on one token: mag[n] += weight *
- * sum_i |w_dn[n,i] h_i| with h the expert's fp32 SwiGLU row for x. */
-static void expert_mag(int H, int I, int bits, int group, const uint32_t* guw, const uint16_t* gus,
-                       const uint16_t* gub, const uint32_t* dnw, const uint16_t* dns, const uint16_t* dnb,
-                       const float* xf, float* hbuf, double weight, double* mag) {
+/* One expert on one token: y[n] (double) and the first-order forward error
+ * bound eb[n] of evaluating it in fp32 from the exact inputs, with every
+ * dot product accumulated in any order:
+ *   gate/up  g, u = W x (K = H terms):     |dg| <= gamma_H sum|W x|
+ *   SwiGLU   h = silu(g) u:                 |dh| <= |silu'(g) u| |dg| + |silu(g)| |du| + 3u |h|
+ *   down     y = W_dn h (I terms):          |dy| <= gamma_I sum|W_dn h| + sum |W_dn| |dh| */
+static void expert_bound(int H, int I, int bits, int group, const uint32_t* guw, const uint16_t* gus,
+                         const uint16_t* gub, const uint32_t* dnw, const uint16_t* dns, const uint16_t* dnb,
+                         const double* xd, double* h, double* dh, double* y, double* eb) {
   const size_t gu_ws = (size_t)H * bits / 32, gu_ss = (size_t)H / group;
   const size_t dn_ws = (size_t)I * bits / 32, dn_ss = (size_t)I / group;
+  const double gH = gamma_n(H), gI = gamma_n(I), u = 0x1p-24;
   for (int c = 0; c < I; ++c) {
-    const float up = rnbo_affine_dot(guw + c * gu_ws, gus + c * gu_ss, gub + c * gu_ss, xf, H, bits, group);
-    const size_t g = (size_t)(c + I);
-    const float gate = rnbo_affine_dot(guw + g * gu_ws, gus + g * gu_ss, gub + g * gu_ss, xf, H, bits, group);
-    hbuf[c] = (gate / (1.0f + expf(-gate))) * up;
+    double au, ag;
+    const double up = affine_dot_abs(guw + c * gu_ws, gus + c * gu_ss, gub + c * gu_ss, xd, H, bits, group, &au);
+    const size_t r = (size_t)(c + I);
+    const double gate = affine_dot_abs(guw + r * gu_ws, gus + r * gu_ss, gub + r * gu_ss, xd, H, bits, group, &ag);
+    const double sig = 1.0 / (1.0 + exp(-gate));
+    const double silu = gate * sig, dsilu = sig * (1.0 + gate * (1.0 - sig));
+    h[c] = silu * up;
+    dh[c] = fabs(dsilu * up) * gH * ag + fabs(silu) * gH * au + 3.0 * u * fabs(h[c]);
   }
-  for (int n = 0; n < H; ++n)
-    mag[n] += weight * affine_absdot(dnw + n * dn_ws, dns + n * dn_ss, dnb + n * dn_ss, hbuf, I, bits, group);
+  for (int n = 0; n < H; ++n) {
+    const uint32_t* wr = dnw + n * dn_ws;
+    const uint16_t* sr = dns + n * dn_ss;
+    const uint16_t* br = dnb + n * dn_ss;
+    double acc = 0.0, a = 0.0, prop = 0.0;
+    for (int i = 0; i < I; ++i) {
+      const int g = i / group;
+      const double w = (double)rnbo_bf16_to_f32(sr[g]) * (double)code_at(wr, bits, (size_t)i) +
+                       (double)rnbo_bf16_to_f32(br[g]);
+      acc += w * h[i];
+      a += fabs(w * h[i]);
+      prop += fabs(w) * dh[i];
+    }
+    y[n] = acc;
+    eb[n] = gI * a + prop;
+  }
 }
 
-/* Magnitude of every block output element: the sum of the absolute values
- * of the products its final accumulation adds,
- *   mag[t,n] = sum_s |score[t,s]| sum_i |w_dn_e[n,i] h_e,i| + |sg[t]| sum_i |w_sdn[n,i] hs_i|
- * (per-slot unweighted magnitudes of rnbo_switchglu when scores is NULL:
- * mag [T,k,H]).  inds/scores/sg are the routing of rnbo_router; sg may be
- * NULL (no shared expert).  fp32 summation of n such products in any order
- * errs by at most (n-1) 2^-24 mag, which the parity tests use as the floor of
- * their tolerance for outputs that cancel. */
-int rnbo_block_mag(const rnbo_block* d, const int32_t* inds, const float* scores, const float* sg,
-                   float* mag, int nthreads) {
+/* Forward error bound of every block output element: how far an fp32
+ * evaluation of the block from the exact inputs (bf16 x and weights, the
+ * oracle's routing) may land from the exact value, to first order, with
+ * every sum accumulated in any order (gamma_n bounds, u = 2^-24):
+ *   out[t,n] = sum_s w_s y_s[n] + sg y_shared[n]
+ *   bound    = sum_s (|w_s| eb_s[n] + gamma_16 |w_s y_s[n]|)
+ *              + |sg| eb_sh[n] + |d sg| |y_sh[n]| + gamma_9 sum |terms|
+ * with the routing weights' own rounding (softmax, renormalisation) taken
+ * as gamma_16 |w_s| and the shared gate's d sg = sg (1 - sg) gamma_H
+ * sum_k |x_k w_sg,k| + 2u sg.  Without scores (scores == NULL) the bound is
+ * that of each slot's unweighted SwitchGLU output: bound [T,k,H].  The
+ * parity tests use it as the floor of their per-element tolerance. */
+int rnbo_block_bound(const rnbo_block* d, const int32_t* inds, const float* scores, const float* sg,
+                     float* bound, int nthreads) {
   if (!block_valid(d)) return RNBO_EINVAL;
   const int T = d->T, H = d->H, I = d->I, K = d->k, bits = d->bits, G = d->group;
   for (int i = 0; i < T * K; ++i)
@@ -371,40 +407,57 @@ int rnbo_block_mag(const rnbo_block* d, const int32_t* inds, const float* scores
   const size_t gu_we = (size_t)2 * I * H * bits / 32, gu_se = (size_t)2 * I * H / G;
   const size_t dn_we = (size_t)H * I * bits / 32, dn_se = (size_t)H * I / G;
   const int per_slot = scores == NULL;
-  int rc = RNBO_OK;
+  const double g16 = gamma_n(16.0), g9 = gamma_n(9.0), gH = gamma_n(H), u = 0x1p-24;
 #pragma omp parallel num_threads(nthreads > 0 ? nthreads : 1)
   {
-    float* xf = (float*)malloc(sizeof(float) * H);
-    float* hb = (float*)malloc(sizeof(float) * I);
+    double* xd = (double*)malloc(sizeof(double) * H);
+    double* h = (double*)malloc(sizeof(double) * I);
+    double* dh = (double*)malloc(sizeof(double) * I);
+    double* y = (double*)malloc(sizeof(double) * H);
+    double* eb = (double*)malloc(sizeof(double) * H);
     double* acc = (double*)malloc(sizeof(double) * H);
+    double* tabs = (double*)malloc(sizeof(double) * H);
 #pragma omp for schedule(dynamic, 1)
     for (int t = 0; t < T; ++t) {
-      x_row_f32(d, t, xf);
-      for (int n = 0; n < H; ++n) acc[n] = 0.0;
+      for (int k = 0; k < H; ++k) xd[k] = (double)rnbo_bf16_to_f32(d->x[(size_t)t * H + k]);
+      for (int n = 0; n < H; ++n) acc[n] = tabs[n] = 0.0;
       for (int s = 0; s < K; ++s) {
         const size_t e = (size_t)inds[(size_t)t * K + s];
-        const double wgt = per_slot ? 1.0 : fabs((double)scores[(size_t)t * K + s]);
-        expert_mag(H, I, bits, G, d->gu_w + e * gu_we, d->gu_s + e * gu_se, d->gu_b + e * gu_se,
-                   d->dn_w + e * dn_we, d->dn_s + e * dn_se, d->dn_b + e * dn_se, xf, hb, wgt, acc);
+        expert_bound(H, I, bits, G, d->gu_w + e * gu_we, d->gu_s + e * gu_se, d->gu_b + e * gu_se,
+                     d->dn_w + e * dn_we, d->dn_s + e * dn_se, d->dn_b + e * dn_se, xd, h, dh, y, eb);
         if (per_slot) {
-          for (int n = 0; n < H; ++n) {
-            mag[((size_t)t * K + s) * H + n] = (float)acc[n];
-            acc[n] = 0.0;
-          }
+          for (int n = 0; n < H; ++n) bound[((size_t)t * K + s) * H + n] = (float)eb[n];
+          continue;
+        }
+        const double wgt = fabs((double)scores[(size_t)t * K + s]);
+        for (int n = 0; n < H; ++n) {
+          acc[n] += wgt * eb[n] + g16 * wgt * fabs(y[n]);
+          tabs[n] += wgt * fabs(y[n]);
         }
       }
-      if (!per_slot) {
-        if (sg && d->sgu_w)
-          expert_mag(H, I, bits, G, d->sgu_w, d->sgu_s, d->sgu_b, d->sdn_w, d->sdn_s, d->sdn_b, xf, hb,
-                     fabs((double)sg[t]), acc);
-        for (int n = 0; n < H; ++n) mag[(size_t)t * H + n] = (float)acc[n];
+      if (per_slot) continue;
+      if (sg && d->sgu_w) {
+        expert_bound(H, I, bits, G, d->sgu_w, d->sgu_s, d->sgu_b, d->sdn_w, d->sdn_s, d->sdn_b, xd, h, dh, y, eb);
+        double a = 0.0;
+        for (int k = 0; k < H; ++k) a += fabs(xd[k] * (double)rnbo_bf16_to_f32(d->shared_gate_w[k]));
+        const double g = fabs((double)sg[t]);
+        const double dsg = g * (1.0 - g) * gH * a + 2.0 * u * g;
+        for (int n = 0; n < H; ++n) {
+          acc[n] += g * eb[n] + dsg * fabs(y[n]);
+          tabs[n] += g * fabs(y[n]);
+        }
       }
+      for (int n = 0; n < H; ++n) bound[(size_t)t * H + n] = (float)(acc[n] + g9 * tabs[n]);
     }
-    free(xf);
-    free(hb);
+    free(xd);
+    free(h);
+    free(dh);
+    free(y);
+    free(eb);
     free(acc);
+    free(tabs);
   }
-  return rc;
+  return RNBO_OK;
 }
 
 /* Whole block: out[t] = sum_s score[t,s] * y[t,s] + sigmoid(x.w_sg) * shared(x). */

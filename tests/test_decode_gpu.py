@@ -61,10 +61,10 @@ def test_block_matches_oracle(bits, T):
     blk, bt, w = _setup(bits)
     x = _x(blk, T)
     out, inds, scores = ops.moe_block(bt, x, return_routing=True)
-    ref, oinds, oscores, mag = oracle_block(w, blk.x[:T])
+    ref, oinds, oscores, bound = oracle_block(w, blk.x[:T])
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
     np.testing.assert_allclose(scores.cpu().numpy(), oscores, rtol=2e-5, atol=1e-7)
-    s = assert_close(_f32(out), ref, f"block q{bits} T={T}", mag=mag)
+    s = assert_close(_f32(out), ref, f"block q{bits} T={T}", bound=bound)
     print(f"q{bits} T={T}: {json.dumps(s)}")
 
 
@@ -79,11 +79,11 @@ def test_switchglu_matches_oracle_with_repeated_experts(bits):
     x = _x(blk, T)
     y = ops.switchglu(bt, x, torch.from_numpy(inds).cuda(), out_dtype=torch.float32)
     ref = oracle.switchglu(w, blk.x[:T], inds)
-    mag = oracle.block_mag(w, blk.x[:T], inds)
-    assert_close(y.cpu().numpy(), ref, "switchglu fp32", mag=mag)
+    bound = oracle.block_bound(w, blk.x[:T], inds)
+    assert_close(y.cpu().numpy(), ref, "switchglu fp32", bound=bound)
     yb = ops.switchglu(bt, x, torch.from_numpy(inds).cuda())
     assert yb.dtype == torch.bfloat16 and yb.shape == (T, k, 2048)
-    assert_close(_f32(yb), ref, "switchglu bf16", mag=mag)
+    assert_close(_f32(yb), ref, "switchglu bf16", bound=bound)
 
 
 @pytest.mark.parametrize("bits,expected", [(8, 6.836), (4, 170.073)])
@@ -105,9 +105,9 @@ def test_reference_two_stage_kat_on_gpu(bits, expected):
     out = (data["route_w"].astype(np.float64)[:, None] * y).sum(0)
     kw = oracle.BlockWeights(bits=bits, group=64, router_w=np.zeros((64, 2048), np.uint16),
                              **{n: data[n] for n in ("gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b")})
-    mag = oracle.block_mag(kw, data["x"].reshape(1, -1), data["selected"].astype(np.int32).reshape(1, 8),
+    bound = oracle.block_bound(kw, data["x"].reshape(1, -1), data["selected"].astype(np.int32).reshape(1, 8),
                            data["route_w"].reshape(1, 8))[0]
-    assert_close(out, ref_out, f"two-stage KAT q{bits}", mag=mag, rel_l2=1e-3)
+    assert_close(out, ref_out, f"two-stage KAT q{bits}", bound=bound, rel_l2=1e-3)
     assert abs(out.sum() - ref_cs) < 5e-3, (out.sum(), ref_cs)
 
 
@@ -123,9 +123,9 @@ def test_block_beyond_one_launch_chain(T):
     bt = ops.BlockTensors.from_numpy(blk, "cuda")
     w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
     out, inds, _ = ops.moe_block(bt, _x(blk, T), return_routing=True)
-    ref, oinds, _, mag = oracle_block(w, blk.x)
+    ref, oinds, _, bound = oracle_block(w, blk.x)
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
-    assert_close(_f32(out), ref, f"block T={T}", mag=mag)
+    assert_close(_f32(out), ref, f"block T={T}", bound=bound)
 
 
 def test_expert_shard_switchglu():
@@ -222,21 +222,21 @@ def test_persistent_kernel_matches_chain_and_oracle(bits, T):
     out, inds, scores = ops.moe_block(bt, x, return_routing=True)
     chain = ops.BlockTensors(**{**bt.__dict__, "flags": bt.flags | _lib.FLAG_CHAIN})
     out_c, inds_c, _ = ops.moe_block(chain, x, return_routing=True)
-    ref, oinds, oscores, mag = oracle_block(w, blk.x[:T])
+    ref, oinds, oscores, bound = oracle_block(w, blk.x[:T])
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
     np.testing.assert_array_equal(inds_c.cpu().numpy(), oinds)
     np.testing.assert_allclose(scores.cpu().numpy(), oscores, rtol=2e-5, atol=1e-7)
-    assert_close(_f32(out), ref, f"persistent q{bits} T={T}", mag=mag)
-    assert_close(_f32(out_c), ref, f"chain q{bits} T={T}", mag=mag)
+    assert_close(_f32(out), ref, f"persistent q{bits} T={T}", bound=bound)
+    assert_close(_f32(out_c), ref, f"chain q{bits} T={T}", bound=bound)
     ws = ops.Workspace("cuda")
     for i in range(3):  # back-to-back calls reuse the counters
         xn = inputs.make_tokens(9 + i, T)
         xi = torch.from_numpy(xn).view(torch.int16).view(torch.bfloat16).cuda()
         a = ops.moe_block(bt, xi, ws=ws)
         b = ops.moe_block(chain, xi, ws=ws)
-        ref_i, _, _, mag_i = oracle_block(w, xn)
-        assert_close(_f32(a), ref_i, f"persistent call {i}", mag=mag_i)
-        assert_close(_f32(b), ref_i, f"chain call {i}", mag=mag_i)
+        ref_i, _, _, bound_i = oracle_block(w, xn)
+        assert_close(_f32(a), ref_i, f"persistent call {i}", bound=bound_i)
+        assert_close(_f32(b), ref_i, f"chain call {i}", bound=bound_i)
     assert ws.status() == 0
 
 
@@ -270,10 +270,10 @@ def test_small_bank_many_tokens_fresh_workspace(T):
     bt = ops.BlockTensors.from_numpy(blk, "cuda")
     x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
     w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
-    ref, oinds, _, mag = oracle_block(w, blk.x)
+    ref, oinds, _, bound = oracle_block(w, blk.x)
     out, inds, _ = ops.moe_block(bt, x, ws=ops.Workspace("cuda"), return_routing=True)
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
-    assert_close(out.float().cpu().numpy(), ref, f"E=16 T={T} fresh workspace", mag=mag)
+    assert_close(out.float().cpu().numpy(), ref, f"E=16 T={T} fresh workspace", bound=bound)
     shard = ops.BlockTensors.from_numpy(blk, "cuda", E_range=(4, 12))
     part = ops.moe_block(ops.BlockTensors(**{**shard.__dict__, "flags": _lib.FLAG_Y_F32 | _lib.FLAG_NO_SHARED}),
                          x, ws=ops.Workspace("cuda"))
@@ -282,4 +282,4 @@ def test_small_bank_many_tokens_fresh_workspace(T):
     y = oracle.switchglu(w, blk.x, oinds)
     wk = np.where(keep, osc, 0.0).astype(np.float32)
     assert_close(part.cpu().numpy(), np.einsum("tk,tkh->th", wk, y), f"E=16 shard T={T} fresh workspace",
-                 mag=oracle.block_mag(w, blk.x, oinds, wk))
+                 bound=oracle.block_bound(w, blk.x, oinds, wk))

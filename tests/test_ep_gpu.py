@@ -21,7 +21,7 @@ BITS, SEED = 4, 1
 
 
 def _ref(blk, T):
-    """(ref, inds, scores, mag) of the oracle on the first T tokens."""
+    """(ref, inds, scores, bound) of the oracle on the first T tokens."""
     w = oracle.BlockWeights(bits=BITS, group=64, **blk.weight_fields())
     return oracle_block(w, blk.x[:T])
 
@@ -35,14 +35,14 @@ def test_single_rank_context_matches_block():
     try:
         for T in (1, 8, 5):
             out, inds, _ = ctx.moe_block(bt, x[:T], return_routing=True)
-            ref, oinds, _, mag = _ref(blk, T)
+            ref, oinds, _, bound = _ref(blk, T)
             np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
-            assert_close(out.float().cpu().numpy(), ref, f"ep world 1 T={T}", mag=mag)
+            assert_close(out.float().cpu().numpy(), ref, f"ep world 1 T={T}", bound=bound)
         f32 = ops.BlockTensors(**{**bt.__dict__, "flags": _lib.FLAG_Y_F32})
         out = ctx.moe_block(f32, x[:2])
         assert out.dtype == torch.float32
         r2 = _ref(blk, 2)
-        assert_close(out.cpu().numpy(), r2[0], "ep world 1 fp32", mag=r2[3])
+        assert_close(out.cpu().numpy(), r2[0], "ep world 1 fp32", bound=r2[3])
     finally:
         ctx.close()
 
@@ -73,9 +73,9 @@ def _rank_main(rank, world, port):
         for T in (1, 8, 3, 1, 8, 2):  # repeated calls alternate the exchange parity
             dist.barrier(group=gloo)  # ranks enter each exchange together
             out, inds, _ = ctx.moe_block(shard, x[:T], ws=ws, return_routing=True)
-            ref, oinds, _, mag = _ref(blk, T)
+            ref, oinds, _, bound = _ref(blk, T)
             np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
-            assert_close(out.float().cpu().numpy(), ref, f"ep p2p rank {rank} T={T}", mag=mag)
+            assert_close(out.float().cpu().numpy(), ref, f"ep p2p rank {rank} T={T}", bound=bound)
             # every rank holds the same bits (the sum runs in rank order everywhere)
             allv = [torch.empty_like(out) for _ in range(world)]
             dist.all_gather(allv, out)
@@ -84,7 +84,7 @@ def _rank_main(rank, world, port):
         assert ws.status() == 0
         out_n = ep.moe_block_nccl(shard, x[:8], rank, ws=ws)
         r8 = _ref(blk, 8)
-        assert_close(out_n.float().cpu().numpy(), r8[0], f"ep nccl rank {rank}", mag=r8[3])
+        assert_close(out_n.float().cpu().numpy(), r8[0], f"ep nccl rank {rank}", bound=r8[3])
         # a two-layer stack, expert parallel, against the same stack on one GPU
         from runnel_b200 import stack
         lo, hi, _ = ep.plan(rank, world)

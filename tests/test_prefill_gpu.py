@@ -23,10 +23,10 @@ def _run(bits, seed, T, skew=None, sample=None):
     out, inds, scores = ops.moe_block(bt, x, return_routing=True)
     w = oracle.BlockWeights(bits=bits, group=64, **blk.weight_fields())
     rows = np.arange(T) if sample is None else np.sort(np.random.default_rng(seed).choice(T, sample, replace=False))
-    ref, oinds, oscores, mag = oracle_block(w, np.ascontiguousarray(blk.x[rows]))
+    ref, oinds, oscores, bound = oracle_block(w, np.ascontiguousarray(blk.x[rows]))
     np.testing.assert_array_equal(inds.cpu().numpy()[rows], oinds)
     np.testing.assert_allclose(scores.cpu().numpy()[rows], oscores, rtol=2e-5, atol=1e-7)
-    s = assert_close(out.float().cpu().numpy()[rows], ref, f"prefill q{bits} T={T} skew={skew}", mag=mag)
+    s = assert_close(out.float().cpu().numpy()[rows], ref, f"prefill q{bits} T={T} skew={skew}", bound=bound)
     return blk, bt, x, out, s
 
 
@@ -116,7 +116,7 @@ def test_experts_fwd_given_routing_matches_oracle():
     w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
     _, inds, scores, _ = oracle.router(w, blk.x, k=8)
     y = oracle.switchglu(w, blk.x, inds)
-    ymag = oracle.block_mag(w, blk.x, inds)
+    ybound = oracle.block_bound(w, blk.x, inds)
     x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
     ti = torch.from_numpy(inds.astype(np.int32)).cuda()
     ts = torch.from_numpy(scores).cuda()
@@ -125,14 +125,14 @@ def test_experts_fwd_given_routing_matches_oracle():
         local = (inds >= lo) & (inds < hi)
         wk = np.where(local, scores, 0.0).astype(np.float32)
         ref = np.einsum("tk,tkh->th", wk, y)
-        mag = np.einsum("tk,tkh->th", wk, ymag)
+        bound = np.einsum("tk,tkh->th", wk, ybound)
         for T in (70, 3):
             out = ops.experts_fwd(bt, x[:T], ti[:T], ts[:T])
             assert out.dtype == torch.float32
-            assert_close(out.cpu().numpy(), ref[:T], f"experts_fwd [{lo},{hi}) T={T}", mag=mag[:T])
+            assert_close(out.cpu().numpy(), ref[:T], f"experts_fwd [{lo},{hi}) T={T}", bound=bound[:T])
     out16 = ops.experts_fwd(bt, x, ti, ts, out_f32=False)
     assert out16.dtype == torch.bfloat16
-    assert_close(out16.float().cpu().numpy(), ref, "experts_fwd bf16", mag=mag)
+    assert_close(out16.float().cpu().numpy(), ref, "experts_fwd bf16", bound=bound)
     # an id outside [0, E_total) is skipped and flagged
     bad = ti.clone()
     bad[0, 0] = 999
@@ -147,4 +147,4 @@ def test_experts_fwd_given_routing_matches_oracle():
     keep = np.where(local[:2], scores[:2], 0.0)
     keep[0, 0] = 0.0
     assert_close(out.cpu().numpy(), np.einsum("tk,tkh->th", keep.astype(np.float32), y[:2]), "experts_fwd bad id",
-                 mag=np.einsum("tk,tkh->th", keep.astype(np.float32), ymag[:2]))
+                 bound=np.einsum("tk,tkh->th", keep.astype(np.float32), ybound[:2]))

@@ -107,9 +107,9 @@ def test_two_stage_dataset_probe_reference_kat(bits, expected, tmp_path):
     from tests._parity import assert_close
     kw = oracle.BlockWeights(bits=bits, group=64, router_w=np.zeros((64, 2048), np.uint16),
                              **{n: data[n] for n in ("gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b")})
-    mag = oracle.block_mag(kw, data["x"].reshape(1, -1), data["selected"].astype(np.int32).reshape(1, 8),
+    bound = oracle.block_bound(kw, data["x"].reshape(1, -1), data["selected"].astype(np.int32).reshape(1, 8),
                            data["route_w"].reshape(1, 8))[0]
-    assert_close(y, ref_out, f"two-stage dataset q{bits}", mag=mag)
+    assert_close(y, ref_out, f"two-stage dataset q{bits}", bound=bound)
     # The grouped GEMM feeds the SwiGLU rows to the down projection as fp16
     # (11-bit significand); every output shares those rows, so their rounding
     # reaches the checksum coherently: within 1e-3 of it, not the 5e-3
@@ -142,9 +142,9 @@ def test_checkpoint_block_and_layer_sweep(tmp_path):
     fields = {k: a[k] for k in ("router_w", "shared_gate_w", "gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b",
                                 "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b")}
     from tests._parity import assert_close, oracle_block
-    ref, oinds, _, mag = oracle_block(oracle.BlockWeights(bits=4, group=64, **fields), x_bits)
+    ref, oinds, _, bound = oracle_block(oracle.BlockWeights(bits=4, group=64, **fields), x_bits)
     np.testing.assert_array_equal(np.sort(inds.cpu().numpy(), 1), np.sort(oinds, 1))
-    assert_close(out.float().cpu().numpy(), ref, "checkpoint block", mag=mag)
+    assert_close(out.float().cpu().numpy(), ref, "checkpoint block", bound=bound)
     doc = layers.sweep(root, "q4", [0], experts="3,1,7,0,5,2,6,4", warmups=1, trials=2)
     rec = doc["records"][0]
     assert rec["layer"] == 0 and rec["manifest"]["total_experts"] == 8

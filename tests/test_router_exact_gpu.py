@@ -79,10 +79,10 @@ def test_block_midpoints(T):
     bt = ops.BlockTensors.from_numpy(blk, "cuda")
     x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).cuda()
     out, inds, scores = ops.moe_block(bt, x, return_routing=True)
-    ref, oinds, oscores, mag = oracle_block(_oracle(blk, bits), blk.x)
+    ref, oinds, oscores, bound = oracle_block(_oracle(blk, bits), blk.x)
     np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
     np.testing.assert_allclose(scores.cpu().numpy(), oscores, rtol=2e-5, atol=1e-7)
-    assert_close(out.float().cpu().numpy(), ref, f"midpoint block T={T}", mag=mag)
+    assert_close(out.float().cpu().numpy(), ref, f"midpoint block T={T}", bound=bound)
 
 
 @pytest.mark.gpu

@@ -70,8 +70,8 @@ def test_stack_layer_by_layer_matches_oracle():
             np.testing.assert_array_equal(_bits(xa), rxa)
             assert _ulp_steps(_bits(xn), rxn).max() <= 1
             # block l on the GPU's own input
-            ref, oinds, _, mag = oracle_block(ws[l], _bits(xn))
-            assert_close(y.float().cpu().numpy(), ref, f"token {tok} layer {l}", mag=mag)
+            ref, oinds, _, bound = oracle_block(ws[l], _bits(xn))
+            assert_close(y.float().cpu().numpy(), ref, f"token {tok} layer {l}", bound=bound)
         last = stack.reference_add_rmsnorm(_bits(rec[-1][0]), _bits(rec[-1][2]), norms_bits[-1])[0]
         np.testing.assert_array_equal(_bits(out), last)
         x = out

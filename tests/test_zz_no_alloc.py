@@ -59,9 +59,9 @@ def test_noalloc_matches_workspace_entry_point_twice():
         assert torch.equal(out, ref), "the no-alloc call differs from the workspace call"
         # and on its own against the CPU oracle
         w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
-        oref, oinds, _, mag = oracle_block(w, x_np)
+        oref, oinds, _, bound = oracle_block(w, x_np)
         np.testing.assert_array_equal(inds.cpu().numpy(), oinds)
-        assert_close(out.float().cpu().numpy(), oref, "noalloc vs oracle", mag=mag)
+        assert_close(out.float().cpu().numpy(), oref, "noalloc vs oracle", bound=bound)
     # the two calls set no status bit (no timeout, no bad index), and reading
     # the status clears it
     status = ctypes.c_uint32(0xFFFFFFFF)
