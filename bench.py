@@ -133,6 +133,40 @@ class ClockSampler:
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
 
 
+def timed_trials(run_k, stream, dist, dev, min_s):
+    """Times run_k() -- exactly K steps queued on `stream` -- in repeated
+    trials, each bracketed by a barrier (under torchrun) and a device
+    synchronize and timed with CUDA events on `stream`, until at least min_s
+    seconds of trials have run; every rank runs the same number of trials.
+    Returns the per-trial milliseconds, each the maximum over ranks."""
+    import torch
+
+    def one():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            run_k()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    first = one()
+    n = int(min(10000, max(3, np.ceil(min_s * 1e3 / max(first, 1e-3)))))
+    if dist:
+        t = torch.tensor([n], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        n = int(t.item())
+    return [first] + [one() for _ in range(n - 1)]
+
+
 def cpu_baseline(bits, T, budget_s=10.0, seed=1):
     from oracle import oracle
     from runnel_b200 import inputs
@@ -383,47 +417,21 @@ def run_prefill_bench(args, cfg):
     stream.synchronize()
     assert ws.status() == 0
     K = args.steps
+    moved.update(sent=0, received=0)
     sampler = ClockSampler(local)
     sampler.start()
-    # a calibrated, rank-uniform number of soak rounds (all-to-all steps are collective)
-    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        c0.record(stream)
-        for i in range(4):
-            step(i)
-        c1.record(stream)
-    torch.cuda.synchronize()
-    round_ms = torch.tensor([c0.elapsed_time(c1)], device=dev)
-    if dist:
-        dist.all_reduce(round_ms, op=dist.ReduceOp.MAX)
-    n_soak = int(min(2000, max(1, args.soak * 1e3 / max(float(round_ms.item()), 1e-3))))
-    with torch.cuda.stream(stream):
-        for r in range(n_soak):
-            for i in range(4):
-                step(i)
-            if r % 8 == 7:
-                stream.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    moved.update(sent=0, received=0)
     _lib.stage_timing(True)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
+
+    def run_k():
         for i in range(K):
             step(i)
-        ev1.record(stream)
-    torch.cuda.synchronize()
+
+    trials = timed_trials(run_k, stream, dist, dev, args.min_time)
     _lib.stage_timing(False)
     stages, ncalls = _lib.stage_times()
     clocks = sampler.stop()
-    moved_timed = dict(moved)
-    ms = ev0.elapsed_time(ev1)
-    if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    moved_timed = {k: v / len(trials) for k, v in moved.items()}
+    ms = statistics.median(trials)
     ms_step = ms / K
     tok_s = T * K * world / (ms * 1e-3)
     assert ws.status() == 0
@@ -449,20 +457,13 @@ def run_prefill_bench(args, cfg):
         for i in range(3):
             host_step(i)
     stream.synchronize()
-    Ke = max(4, min(K, 64))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for i in range(Ke):
+
+    def e2e_k():  # K steps through the public API, each from and to pinned host memory
+        for i in range(K):
             host_step(i)
-        e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_tok_s = T * Ke * world / (e2e_ms * 1e-3)
+
+    e2e_ms = statistics.median(timed_trials(e2e_k, stream, dist, dev, args.min_time / 2))
+    e2e_tok_s = T * K * world / (e2e_ms * 1e-3)
 
     gemm_flops, all_flops = prefill_flops(T)
     _, bf16_burst, src = peaks()
@@ -471,12 +472,17 @@ def run_prefill_bench(args, cfg):
     if os.path.exists(pth):
         sustained = json.load(open(pth)).get("bf16_tflops_sustained")
     peak = sustained or bf16_burst
-    gemm_ms = (stages.get("gateup", 0.0) + stages.get("down", 0.0)) / K
+    # stage times are summed over every timed call (all trials); per step:
+    calls_per_step = max(ncalls, 1) / (K * len(trials))
+    gemm_ms = (stages.get("gateup", 0.0) + stages.get("down", 0.0)) / max(ncalls, 1) * calls_per_step
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
     line = {
         "metric": "moe_block_prefill_tokens_per_s", "value": tok_s, "unit": "tokens/s",
         "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "trials": len(trials), "trial_ms": {"median": ms, "min": min(trials), "max": max(trials)},
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "mma_operands": "fp16 (tcgen05 kind::f16: weights dequantised to fp16, tokens scaled by exact powers "
+                        "of two), fp32 accumulation in TMEM",
         "data": "synthetic (seeded MLX-affine block, N(0,1) bf16 tokens)",
         "config": {"workload": f"config{args.config} q{bits} prefill T={T}", "bits": bits,
                    "tokens_per_step": T, "routing": routing, "H": 2048, "I": 512, "E": 256, "top_k": 8,
@@ -499,7 +505,7 @@ def run_prefill_bench(args, cfg):
                      "algorithmic_flops_per_step": gemm_flops,
                      "kernel": "k_pre_gemm (gate/up + down launches)", "gemm_ms_per_step": gemm_ms,
                      "block_tflops": all_flops / (ms_step * 1e-3) / 1e12},
-        "stages_ms_per_step": {k: v / K for k, v in stages.items()},
+        "stages_ms_per_step": {k: v / max(ncalls, 1) * calls_per_step for k, v in stages.items()},
         # route, sort, scatter, gather, gate/up, row scale, down, final (twice per step with all-to-all)
         "gpu_launches": 8 * K * (2 if a2a else 1),
         "clocks": clocks,
@@ -543,7 +549,8 @@ def run_stack_bench(args, cfg):
 
     bits, L = args.bits, args.layers or cfg["layers"]
     E_range = epm.plan(rank, world)[:2] if world > 1 else None
-    layers, norms = stack.synthetic_layers(L, bits, args.seed, dev, E_range=E_range)
+    # layer l = inputs.make_block(bits, seed=1000 * seed + l): the canonical generator
+    layers, norms = stack.canonical_layers(L, bits, args.seed, dev, E_range=E_range)
     ctx = epm.ExpertParallel(rank, world) if world > 1 else None
     ws = ops.Workspace(dev)
     st = stack.LayerStack(layers, norms, ep=ctx, ws=ws)
@@ -576,68 +583,42 @@ def run_stack_bench(args, cfg):
         for _ in range(W):
             g.replay()
     stream.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
-    # sustained replays so the clock sampler sees the GPU under this load (the
-    # count is the same on every rank: expert-parallel layers pair up)
-    t0 = time.time()
-    with torch.cuda.stream(stream):
-        g.replay()
-    stream.synchronize()
-    n_soak = max(1, int(args.soak / max(time.time() - t0, 1e-4)))
-    if dist:
-        t = torch.tensor([n_soak], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MIN)
-        n_soak = int(t.item())
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        for _ in range(n_soak):
-            g.replay()
-        ev0.record(stream)
+
+    def run_k():  # K sequential tokens: each replay is one token through every layer
         for _ in range(K):
             g.replay()
-        ev1.record(stream)
-    torch.cuda.synchronize()
+
+    trials = timed_trials(run_k, stream, dist, dev, args.min_time)
     clocks = sampler.stop()
-    ms = ev0.elapsed_time(ev1)
-    if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = statistics.median(trials)
     us_tok = ms * 1e3 / K
     # end to end: each token's input copied in from pinned host memory and its
     # output read back, every step
     xh = x0.cpu().pin_memory()
     oh = torch.empty_like(xh).pin_memory()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
+    hb = [xh, oh]
+
+    def e2e_k():
         for _ in range(K):
-            xin.copy_(xh, non_blocking=True)
+            xin.copy_(hb[0], non_blocking=True)
             g.replay()
-            oh.copy_(xout, non_blocking=True)
-            xh, oh = oh, xh
-        e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+            hb[1].copy_(xout, non_blocking=True)
+            hb.reverse()
+
+    e2e_ms = statistics.median(timed_trials(e2e_k, stream, dist, dev, args.min_time / 2))
     assert ws.status() == 0, "device status reported a timeout or a bad index"
     hbm, _, src = peaks()
     achieved = per_tok / (us_tok * 1e-6) / 1e9
     line = {
         "metric": "moe_stack_decode_us_per_token", "value": us_tok, "unit": "us/token",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": us_tok * 1e-3,
+        "trials": len(trials), "trial_ms": {"median": ms, "min": min(trials), "max": max(trials)},
         "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-        "dtype": "f16", "data": "synthetic (seeded torch generator on the device, inputs.py distributions)",
+        "dtype": "bf16",
+        "mma_operands": "fp16 (codes exact, activations scaled by exact powers of two), fp32 accumulation",
+        "data": "synthetic (runnel_b200.inputs: layer l = make_block(4, seed=1000*seed + l), numpy PCG64)",
         "config": {"workload": f"config4 {L} q{bits} layers, batch-1 sequential decode", "bits": bits,
                    "layers": L, "tokens_per_step": 1, "H": 2048, "I": 512, "E": 256, "top_k": 8,
                    "l2": f"inputs larger than L2: {L} layers of weights per step",
@@ -774,51 +755,27 @@ def run_ours(args):
     distinct = float(np.mean([len(np.unique(ii.cpu().numpy())) for ii in inds_all]))
     per_step = step_bytes(bits, distinct, T)  # whole block, all ranks
 
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        for i in range(R):
-            one(i)
-    reps = max(1, (args.steps + R - 1) // R)
-    K = reps * R
-    wreps = max(1, (args.warmup + R - 1) // R)
+    # The K timed steps and the W warm-up steps are each one CUDA graph; step
+    # i uses weight copy i % R and token block i % R.
+    K, W = args.steps, args.warmup
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                one(i % R)
+        return g
+
+    g_warm, g_time = capture(W), capture(K)
     with torch.cuda.stream(stream):
-        for _ in range(wreps):
-            g.replay()
+        g_warm.replay()
     stream.synchronize()
 
     sampler = ClockSampler(local)
     sampler.start()
-    # sustained replays so the clock sampler sees the GPU under this load; the
-    # count is the same on every rank (expert-parallel steps pair up across ranks)
-    t0 = time.time()
-    with torch.cuda.stream(stream):
-        g.replay()
-    stream.synchronize()
-    n_soak = max(1, int(args.soak / max(time.time() - t0, 1e-4)))
-    if dist:
-        t = torch.tensor([n_soak], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MIN)
-        n_soak = int(t.item())
-    with torch.cuda.stream(stream):
-        for _ in range(n_soak):
-            g.replay()
-    stream.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        for _ in range(reps):
-            g.replay()
-        ev1.record(stream)
-    torch.cuda.synchronize()
+    trials = timed_trials(g_time.replay, stream, dist, dev, args.min_time)
     clocks = sampler.stop()
-    ms = ev0.elapsed_time(ev1)
-    if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = statistics.median(trials)
     ms_step = ms / K
     us_tok = ms_step * 1e3 / T
 
@@ -840,35 +797,28 @@ def run_ours(args):
             block_call(copies[i], xd, od)
             oh[i].copy_(od, non_blocking=True)
     with torch.cuda.stream(stream):
-        for i in range(min(R, args.warmup + 1)):
-            host_step(i)
+        for i in range(W):
+            host_step(i % R)
     stream.synchronize()
-    if dist:
-        dist.barrier()
-        torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for s in range(K):
-            host_step(s % R)
-        e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_us = e2e_ms * 1e3 / (K * T)
+
+    def e2e_k():  # K steps through the public API, each from and to pinned host memory
+        for s_ in range(K):
+            host_step(s_ % R)
+
+    e2e_trials = timed_trials(e2e_k, stream, dist, dev, args.min_time / 2)
+    e2e_us = statistics.median(e2e_trials) * 1e3 / (K * T)
     assert ws.status() == 0, "device status reported a timeout or a bad index"
 
     hbm, _, src = peaks()
     achieved = per_step / (ms_step * 1e-3) / 1e9  # all ranks together
-    persistent = T <= (2 if bits == 4 else 1)
+    persistent = T == 1 or (T == 2 and bits == 4)
     line = {
         "metric": "moe_block_decode_us_per_token", "value": us_tok, "unit": "us/token",
-        "n_gpus": world, "steps": K, "warmup": wreps * R, "ms_per_step": ms_step,
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step,
+        "trials": len(trials), "trial_ms": {"median": ms, "min": min(trials), "max": max(trials)},
         "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-        "dtype": "f16",
+        "dtype": "bf16",
+        "mma_operands": "fp16 (codes exact, activations scaled by exact powers of two), fp32 accumulation",
         "data": "synthetic (seeded MLX-affine block, N(0,1) bf16 tokens)",
         "config": {"workload": f"config{args.config} q{bits} decode T={T}", "bits": bits,
                    "tokens_per_step": T, "H": 2048, "I": 512, "E": 256, "top_k": 8,
@@ -896,7 +846,7 @@ def run_ours(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:
-        del g
+        del g_time, g_warm
         dist.barrier()
         if ctx is not None:
             ctx.close()
@@ -994,12 +944,14 @@ def main():
     ap.add_argument("--steps", type=int, default=480)
     ap.add_argument("--warmup", type=int, default=48)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--bits", type=int, default=None)
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--layers", type=int, default=None, help="configuration 4: number of layers (default 40)")
     ap.add_argument("--seed", type=int, default=None)
-    ap.add_argument("--soak", type=float, default=1.5)
+    ap.add_argument("--soak", type=float, default=1.5, help="probe mode: seconds of load before timing")
+    ap.add_argument("--min-time", type=float, default=1.0,
+                    help="seconds of timed trials (each trial is exactly --steps steps; the median is reported)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--prefill-par", default="gather", choices=["gather", "a2a", "replica"],

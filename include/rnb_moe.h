@@ -250,6 +250,11 @@ typedef struct rnb_ep rnb_ep;
 RNB_API int rnb_ep_create(int rank, int world, int H, rnb_ep** ep, void* handle_out);
 RNB_API int rnb_ep_connect(rnb_ep* ep, const void* handles);
 RNB_API int rnb_ep_destroy(rnb_ep* ep);
+/* How long a call of this context waits for the other ranks' partial words
+ * before it gives up, sets RNB_STATUS_TIMEOUT and returns (its results are
+ * then void); default 2000 ms (ranks launch independently).  ms in
+ * [1, 600000]. */
+RNB_API int rnb_ep_set_wait_limit_ms(rnb_ep* ep, int ms);
 RNB_API int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* x, void* out,
                                  uint32_t* inds_out, float* scores_out, void* ws, size_t ws_bytes,
                                  void* stream);

@@ -76,6 +76,7 @@ SIGNATURES = {
     "rnb_ep_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp), _vp]),
     "rnb_ep_connect": (ctypes.c_int, [_vp, _vp]),
     "rnb_ep_destroy": (ctypes.c_int, [_vp]),
+    "rnb_ep_set_wait_limit_ms": (ctypes.c_int, [_vp, ctypes.c_int]),
     "rnb_moe_block_ep_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "rnb_moe_block_norm_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _sz,
                                               _vp]),

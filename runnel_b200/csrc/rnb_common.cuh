@@ -34,10 +34,12 @@ constexpr int kGroup = 64;
 
 // ------------------------------------------------------------------ PTX
 
+// (not volatile: a pure function of its operands, so the compiler may
+// interleave independent MMAs)
 __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t a0, const uint32_t a1,
                                         const uint32_t a2, const uint32_t a3, const uint32_t b0,
                                         const uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

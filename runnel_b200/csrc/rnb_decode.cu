@@ -29,6 +29,7 @@
 
 #include "rnb_common.cuh"
 #include "rnb_route.cuh"
+#include "rnb_umma.cuh"
 #include "rnb_internal.h"
 #include "rnb_moe.h"
 
@@ -63,6 +64,9 @@ struct Ws {
   float* yws;         // [T][k+1][H]
   uint32_t* ctr;      // [1 + H/16]
   uint32_t* status;   // [1]
+  uint32_t* seq;      // [0] call sequence word, [1] exit counter (persistent kernel)
+  uint2* lw;          // [2][E_total + 1] logit exchange words (persistent kernel)
+  uint2* hw;          // [2][k + 1][I] SwiGLU exchange words (persistent kernel)
 };
 
 struct Params {
@@ -89,6 +93,7 @@ struct Params {
   // sequence word + 1 (device memory, so graph replays advance it; the
   // kernel's last CTA increments it).
   int ep_world, ep_rank;
+  uint64_t ep_limit_ns;  // bounded wait for the peers' words
   uint2* ep_recv[kMaxEpRanks];
   uint32_t* ep_seq;  // [0] sequence word, [1] exit counter of k_ep_reduce
   // Fused layer glue (persistent kernel, norm_w non-null): the block input
@@ -111,11 +116,12 @@ __device__ __forceinline__ void trace_mark(const Params& p, int i) {
   if (threadIdx.x == 0) {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 32 + i] = t;
+    reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 64 + i] = t;
+    reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 64 + 32 + i] = clock64();
   }
 }
 __device__ __forceinline__ void trace_value(const Params& p, int i, int v) {
-  reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 32 + i] = static_cast<uint64_t>(v);
+  reinterpret_cast<uint64_t*>(p.ws.yws)[blockIdx.x * 64 + i] = static_cast<uint64_t>(v);
 }
 #define RNB_TRACE_MARK(p, i) trace_mark(p, i)
 #else
@@ -872,172 +878,50 @@ __global__ void __launch_bounds__(32 * kDownMaxWarps) k_down(Params p) {
 
 // ------------------------------------------------- k_decode (persistent)
 //
-// One cooperative launch, one CTA of 16 warps per SM, for small token
-// counts.  CTAs coordinate through three counters in the workspace, each
-// wait bounded in time:
-//   phase A  (no routing needed) router tiles in registers; shared-expert
-//            gate/up and shared-expert down tiles staged with cp.async;
-//            every CTA preps the activations itself in shared memory.
-//            Router CTAs publish logits and arrive on BAR1.
-//   routing  after BAR1 every CTA reads the logits and computes top-k, the
-//            weights and the per-expert token lists redundantly.
-//   phase B  routed gate/up tasks (expert x 8 channels, hidden dim split over
-//            the 16 warps) spread round-robin over CTAs and streamed through
-//            a shared-memory ring; the CTA's routed down tiles are requested
-//            first.  Each CTA arrives once on BAR2 with its task count.
-//   phase C  after BAR2 each CTA owning a 16-row output tile runs the down
-//            projection of every source (routed experts + shared expert) in
-//            K quarters, then the ordered weighted combine.
-//   exit     the last CTA to leave resets the counters.
+// One launch for one or two tokens, one CTA of 16 warps per SM, launched
+// with programmatic stream serialisation so that its prologue (weights
+// only) overlaps the previous kernel's tail.  CTAs hand data to each other
+// through 8-byte {value, epoch} words in the workspace header's exchange
+// region: the epoch is the workspace's call sequence word + 1, so a word
+// carrying it was written by this call.  A reader polls the words it needs
+// (bounded in time); there are no arrival counters, fences or grid
+// barriers on the data path.
+//   prologue  this CTA's router rows into registers; its shared-expert
+//             gate/up slice (ring slot 0) and shared-expert down tiles into
+//             shared memory.
+//   router    two router rows (of E_total + 1; the last is the shared gate)
+//             against the tokens -> logit words (bf16 candidate intervals,
+//             rnb_route.cuh); activation prep; the shared-expert gate/up task
+//             -> h words.
+//   routing   every CTA polls the logit words, selects the top k exactly and
+//             derives the same task lists.
+//   gate/up   routed tasks (expert x 8 channels, hidden dimension split over
+//             the 16 warps) round-robin over CTAs.  Each warp streams its
+//             slices of the CTA's tasks, then its down slices, through its
+//             own ring of shared-memory slots (cp.async groups; no CTA
+//             barrier in the stream).  Epilogue: SwiGLU -> h words.
+//   down      CTAs owning 16 output rows: per source (routed experts, shared
+//             expert) and 128-channel quarter, a warp polls that quarter's
+//             h words, converts them to fp16 with one power-of-two scale per
+//             64-group and runs the MMAs; then the ordered weighted combine
+//             (or, expert parallel, the cross-rank exchange).
+//   exit      the last CTA out advances the sequence word.
 
 constexpr int kPWarps = 16;
-// Phase C feeds the SwiGLU activations to the down projection as one fp16
-// per value (11-bit significand, per-column power-of-two scale) -- the
-// precision of the prefill GEMMs.  With true it adds the fp16 remainder
-// (about 22 bits) at twice the MMAs and conversions.
-constexpr bool kPhaseCSplit = false;
-constexpr int kPMaxT = 8;
+constexpr int kPMaxT = 2;
+constexpr int kPMaxK = 8;
+constexpr int kPMaxAct = kPMaxT * kPMaxK;  // distinct local experts of one call
+constexpr int kPMaxMine = 8;               // routed gate/up tasks of one CTA
+constexpr int kDownBatch = 3;              // down units a warp handles per round trip for their h words
 constexpr uint64_t kSpinLimitNs = 200ull * 1000 * 1000;  // a wait gives up after 200 ms
-// Waits on other GPUs: ranks launch independently, so allow host-side skew.
+// Waits on other GPUs: ranks launch independently, so allow host-side skew
+// (the default of an EP context; rnb_ep_set_wait_limit_ms changes it).
 constexpr uint64_t kEpSpinLimitNs = 2000ull * 1000 * 1000;
-
-// Two-group weight tile of one warp (16 rows x 128 inputs): codes with a
-// 16-byte-chunk XOR swizzle instead of padding, then bf16 scales and biases.
-// 8-bit rows are 128 B: chunk ^= (row & 1) << 2, so the 8 lanes of a 16-byte
-// read phase (rows g, g+1) hit disjoint banks; 4-bit rows are 64 B: chunk ^=
-// ((row >> 1) & 1) << 1, so the 16 lanes of an 8-byte phase (rows g..g+3) do.
-template <int BITS>
-struct Tile2 {
-  static constexpr int kRowBytes = 2 * 8 * BITS;
-  static constexpr int kCodeBytes = 16 * kRowBytes;
-  static constexpr int kParBytes = 16 * 2 * 2;
-  static constexpr int kBytes = kCodeBytes + 2 * kParBytes;
-  static constexpr int kChunks = kRowBytes / 16;
-  __device__ static __forceinline__ int swz(int row) {
-    return BITS == 8 ? ((row & 1) << 2) : (((row >> 1) & 1) << 1);
-  }
-};
-
-template <int BITS, typename RowOf>
-__device__ __forceinline__ void tile2_issue(char* sm, const uint32_t* wbase, const uint16_t* sbase,
-                                            const uint16_t* bbase, size_t wrow, size_t srow, int g0,
-                                            RowOf row, int lane) {
-  using TL = Tile2<BITS>;
-  const size_t kw0 = static_cast<size_t>(g0) * kGroup * BITS / 32;
-#pragma unroll
-  for (int q = lane; q < 16 * TL::kChunks; q += 32) {
-    const int i = q / TL::kChunks, j = q % TL::kChunks;
-    cp_async16(sm + i * TL::kRowBytes + ((j ^ TL::swz(i)) * 16), wbase + row(i) * wrow + kw0 + j * 4);
-  }
-  if (lane < 16) {
-    const size_t r = row(lane);
-    cp_async4(sm + TL::kCodeBytes + lane * 4, sbase + r * srow + g0);
-    cp_async4(sm + TL::kCodeBytes + TL::kParBytes + lane * 4, bbase + r * srow + g0);
-  }
-}
-
-template <int BITS, bool SPLIT, typename BFrag, typename GSum>
-__device__ __forceinline__ void tile2_mma(const char* sm, int g, int c, BFrag bfrag, GSum gsum,
-                                          float (&acc)[4]) {
-  using TL = Tile2<BITS>;
-  const uint16_t* S = reinterpret_cast<const uint16_t*>(sm + TL::kCodeBytes);
-  const uint16_t* B = reinterpret_cast<const uint16_t*>(sm + TL::kCodeBytes + TL::kParBytes);
-  const int q = (c == 1) ? 2 : (c == 2) ? 1 : c;
-#pragma unroll
-  for (int gi = 0; gi < 2; ++gi) {
-    RowPairs pa, pb;
-    if (BITS == 8) {
-      const int ch = gi * 4 + c;
-      pa = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16));
-      pb = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16));
-    } else {
-      const int ch = gi * 2 + (q >> 1), off = 8 * (q & 1);
-      pa = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16 + off));
-      pb = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16 + off));
-    }
-    uint32_t xh[8], xl[8];
-    bfrag(gi, xh, xl);
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xh[2 * m], xh[2 * m + 1]);
-      if (SPLIT)
-        mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xl[2 * m], xl[2 * m + 1]);
-    }
-    // the codes entered the MMAs as fp16 subnormals q * 2^-24 (rnb_common.cuh):
-    // the scales carry the 2^24 back (exact)
-    const float sa = bf16_bits_to_f32(S[g * 2 + gi]) * 0x1p24f, ba = bf16_bits_to_f32(B[g * 2 + gi]);
-    const float sb = bf16_bits_to_f32(S[(g + 8) * 2 + gi]) * 0x1p24f, bb = bf16_bits_to_f32(B[(g + 8) * 2 + gi]);
-    const float xs0 = gsum(gi, 0), xs1 = gsum(gi, 1);
-    acc[0] = fmaf(sa, d[0], fmaf(ba, xs0, acc[0]));
-    acc[1] = fmaf(sa, d[1], fmaf(ba, xs1, acc[1]));
-    acc[2] = fmaf(sb, d[2], fmaf(bb, xs0, acc[2]));
-    acc[3] = fmaf(sb, d[3], fmaf(bb, xs1, acc[3]));
-  }
-}
-
-struct PPlan {
-  int db;        // phase-B ring depth (tasks in flight per CTA)
-  int cb;        // phase-C tasks staged together per warp
-  int n_rtiles;  // router tiles of 16 rows (E_total + 1 rows)
-  uint32_t off_x, off_xs, off_br, off_cr, off_h, off_red, off_redc, off_misc;
-  uint32_t off_xn;  // fused glue: the normalised tokens [T][H] bf16
-};
-
-struct PTask {
-  const uint32_t* ent;  // entry ids t*(K+1)+slot of the columns
-  int ncols;
-  int ch0;
-};
-
-struct PMisc {
-  uint32_t inds[kPMaxT][8];
-  float scores[kPMaxT][8];
-  float sg[kPMaxT];
-  float xinv[kPMaxT];
-  float red[kPWarps];
-  uint32_t n_act;
-  uint32_t act_e[kPMaxT * 8];
-  uint32_t act_cnt[kPMaxT * 8];
-  uint32_t act_ent[kPMaxT * 8][kPMaxT];  // entry ids t*(k+1)+slot
-  uint8_t first[kPMaxT * 8];
-  uint32_t shared_ent[8];
-  PTask tasks[4];
-  float rnorm[kPWarps][48];  // router tile partials: per token sum x^2, max|x|; per row sum w^2, sum |w|
-};
-
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void arrive_release(uint32_t* p, uint32_t n = 1) {
-  __threadfence();
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(n) : "memory");
-}
-
-// Thread 0 polls (bounded in time); the CTA continues together.  On timeout
-// the status word gets RNB_STATUS_TIMEOUT and the results of the call are void.
-__device__ void cta_wait_count(const uint32_t* ctr, uint32_t target, uint32_t* status) {
-  if (threadIdx.x == 0) {
-    uint64_t t0, now;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    while (ld_acquire_gpu(ctr) < target) {
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-      if (now - t0 > kSpinLimitNs) {
-        atomicOr(status, RNB_STATUS_TIMEOUT);
-        break;
-      }
-      __nanosleep(32);
-    }
-  }
-  __syncthreads();
-}
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 
-// wait until at most n of this thread's committed groups are pending (n <= 7)
+// Wait until at most n of this thread's committed groups are pending; an n
+// above 7 waits for all but the newest 7 (more than asked: still correct).
 __device__ __forceinline__ void cp_async_wait_pending(int n) {
   switch (n) {
     case 0: asm volatile("cp.async.wait_group 0;\n" ::: "memory"); break;
@@ -1051,9 +935,148 @@ __device__ __forceinline__ void cp_async_wait_pending(int n) {
   }
 }
 
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// One 8-byte {value, epoch} exchange word, written and read as a single
+// 64-bit access (single-copy atomic): a reader that sees the epoch sees the
+// value stored with it.  .gpu scope within one device; .sys across devices.
+__device__ __forceinline__ void xw_store(uint2* p, uint32_t v, uint32_t epoch) {
+  const uint64_t w = (static_cast<uint64_t>(epoch) << 32) | v;
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;\n" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t xw_load(const uint2* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];\n" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ void xw_store_sys(uint2* p, uint32_t v, uint32_t epoch) {
+  const uint64_t w = (static_cast<uint64_t>(epoch) << 32) | v;
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;\n" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t xw_load_sys(const uint2* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];\n" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+// The value of word p once it carries `epoch`.  Polls until then or until
+// `deadline` (globaltimer ns); on timeout sets RNB_STATUS_TIMEOUT in *status
+// and returns 0 (the call's results are void).  Each lane polls its own word.
+__device__ __forceinline__ uint32_t xw_wait(const uint2* p, uint32_t epoch, uint64_t deadline, uint32_t* status) {
+  uint64_t w = xw_load(p);
+  while (static_cast<uint32_t>(w >> 32) != epoch) {
+    if (gtimer() > deadline) {
+      atomicOr(status, RNB_STATUS_TIMEOUT);
+      return 0u;
+    }
+    __nanosleep(40);
+    w = xw_load(p);
+  }
+  return static_cast<uint32_t>(w);
+}
+
+// Expert-parallel all-reduce of one 16-column output tile for T tokens.
+// Every rank's fp32 partial part(t, r) (t < T, r < 16) goes to each rank as
+// one 8-byte {value, epoch} word (a single 64-bit store, single-copy atomic),
+// so a word that carries this call's epoch carries this call's value: the
+// receiver polls the words themselves, with no separate flag and no fence,
+// and sums the ranks' values in rank order (the same order on every rank)
+// before handing them to emit(t, r, sum).  Polls are bounded; on timeout the
+// status word gets RNB_STATUS_TIMEOUT and that value is not emitted.  Buffers
+// alternate by epoch parity: a rank cannot start epoch e+2 before every rank
+// has sent epoch e+1, which each rank does only after reading epoch e.
+template <typename Part, typename Emit>
+__device__ void ep_exchange_tile(const Params& p, int n0, int T, Part part, Emit emit) {
+  const int tid = threadIdx.x, W = p.ep_world;
+  __shared__ uint32_t s_epoch;
+  if (tid == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(p.ep_seq) + 1u;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const size_t par = static_cast<size_t>(epoch & 1u) * W * kEpMaxT * p.H;
+  for (int i = tid; i < T * 16; i += blockDim.x) {
+    const int t = i >> 4, r = i & 15;
+    const uint32_t v = __float_as_uint(part(t, r));
+    const size_t o = par + (static_cast<size_t>(p.ep_rank) * kEpMaxT + t) * p.H + n0 + r;
+    for (int q = 0; q < W; ++q) xw_store_sys(p.ep_recv[q] + o, v, epoch);
+  }
+  const uint64_t deadline = gtimer() + p.ep_limit_ns;
+  for (int i = tid; i < T * 16; i += blockDim.x) {
+    const int t = i >> 4, r = i & 15;
+    const uint2* own = p.ep_recv[p.ep_rank] + par + static_cast<size_t>(t) * p.H + n0 + r;
+    float sum = 0.f;
+    bool ok = true;
+    for (int q = 0; q < W && ok; ++q) {
+      const uint2* src = own + static_cast<size_t>(q) * kEpMaxT * p.H;
+      uint64_t w = xw_load_sys(src);
+      while (static_cast<uint32_t>(w >> 32) != epoch) {
+        if (gtimer() > deadline) {
+          atomicOr(p.ws.status, RNB_STATUS_TIMEOUT);
+          ok = false;
+          break;
+        }
+        w = xw_load_sys(src);
+      }
+      sum += __uint_as_float(static_cast<uint32_t>(w));
+    }
+    if (ok) emit(t, r, sum);
+  }
+}
+
+// Expert-parallel reduction after the decode chain: CTA b owns output
+// columns [16b, 16b+16) of the fp32 partial (p.ws.yws reused as [T][H]).
+// Cooperative launch, so every CTA is resident while it waits for peers.
+__global__ void __launch_bounds__(256) k_ep_reduce(Params p, const float* partial) {
+  const int n0 = blockIdx.x * 16;
+  ep_exchange_tile(
+      p, n0, p.T, [&](int t, int r) { return __ldcg(partial + static_cast<size_t>(t) * p.H + n0 + r); },
+      [&](int t, int r, float v) {
+        const size_t o = static_cast<size_t>(t) * p.H + n0 + r;
+        if (p.y_f32)
+          static_cast<float*>(p.out)[o] = v;
+        else
+          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
+      });
+  // the last CTA out advances the sequence word for the next exchange
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.ep_seq + 1, 1u) == gridDim.x - 1) {
+      p.ep_seq[1] = 0;
+      p.ep_seq[0] += 1;
+      __threadfence();
+    }
+  }
+}
+
+// Shared-memory plan of k_decode (host-computed).
+struct PPlan {
+  int S;  // ring slots per warp
+  uint32_t off_ring, off_sdn, off_x, off_xs, off_xn, off_ivl, off_red, off_hf, off_redc, off_misc;
+};
+
+struct PMisc {
+  uint32_t inds[kPMaxT][kPMaxK];
+  float scores[kPMaxT][kPMaxK];
+  float sg[kPMaxT];
+  float xinv[kPMaxT];
+  float red[kPWarps];
+  uint32_t epoch;
+  uint32_t n_act;
+  uint32_t act_e[kPMaxAct];        // local expert of active expert a
+  uint32_t act_cnt[kPMaxAct];      // its columns (tokens that selected it)
+  uint32_t act_ent[kPMaxAct][kPMaxT];  // entry id t*(K+1)+slot of each column
+  double rdot[kPWarps][4];   // router partials: dot (row i, token t) at 2i+t, fp64
+  float rnorm[kPWarps][8];   // [0,2) sum w^2; [2,4) sum |w|; [4,6) sum x^2; [6,8) max |x|
+};
+
 // Activation prep of T tokens (H = 2048) by the whole CTA (512 threads, 4
 // consecutive values each): power-of-two scale into fp16 range, per-group
-// sums, then the MMA pair order of Ws.xperm.  xh: 2048-half scratch.
+// sums, then the MMA pair order [T][G][4][8] of the gate/up B operand.
+// xh: 2048-half scratch.
 template <int BITS>
 __device__ void xprep_cta(const uint16_t* x, int T, uint32_t* sX, float* sXs, float* xinv, __half* xh,
                           float* red) {
@@ -1103,220 +1126,225 @@ __device__ void xprep_cta(const uint16_t* x, int T, uint32_t* sX, float* sXs, fl
   }
 }
 
-// Gate/up tasks: 16 rows = 8 up + 8 gate channels starting at ch0, tile in
-// `slot` (16 per-warp two-group tiles).  p_gateup_mma leaves this warp's
-// K-slice partial sums in red[warp]; after a CTA barrier p_gateup_epilogue
-// finishes up to 4 tasks at once (SwiGLU, activations, per-tile maxima).
-
+// Where position r (0..63) of a 64-group sits in the MMA pair order of the
+// activation operand: quad (lane c) and u32 pair index i, half h.
 template <int BITS>
-__device__ __forceinline__ void p_gateup_mma(const Params& p, const char* slot, const uint32_t* sX,
-                                             const float* sXs, float* red, const PTask& tk) {
-  using TL = Tile2<BITS>;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  const int K = p.k, G = p.H / kGroup, g0 = warp * 2, ncols = tk.ncols;
-  const int colB = g < ncols ? g : 0;
-  const int tB = static_cast<int>(tk.ent[colB] / (K + 1));
-  const int t0 = static_cast<int>(tk.ent[2 * c < ncols ? 2 * c : 0] / (K + 1));
-  const int t1 = static_cast<int>(tk.ent[2 * c + 1 < ncols ? 2 * c + 1 : 0] / (K + 1));
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  tile2_mma<BITS, false>(
-      slot + warp * TL::kBytes, g, c,
-      [&](int gi, uint32_t(&xb)[8], uint32_t(&)[8]) {
-        const uint32_t* src = sX + (static_cast<size_t>(tB) * G + g0 + gi) * 32 + c * 8;
-        const uint4 u0 = reinterpret_cast<const uint4*>(src)[0];
-        const uint4 u1 = reinterpret_cast<const uint4*>(src)[1];
-        xb[0] = u0.x; xb[1] = u0.y; xb[2] = u0.z; xb[3] = u0.w;
-        xb[4] = u1.x; xb[5] = u1.y; xb[6] = u1.z; xb[7] = u1.w;
-      },
-      [&](int gi, int col) { return sXs[(col ? t1 : t0) * G + g0 + gi]; }, acc);
-  float* rw = red + warp * 128;
-  rw[g * 8 + 2 * c] = acc[0];
-  rw[g * 8 + 2 * c + 1] = acc[1];
-  rw[(g + 8) * 8 + 2 * c] = acc[2];
-  rw[(g + 8) * 8 + 2 * c + 1] = acc[3];
+__device__ __forceinline__ void pair_slot(int r, int& cq, int& i, int& h) {
+  if (BITS == 8) {
+    cq = r >> 4;
+    const int rr = r & 15;
+    i = 2 * (rr >> 2) + ((rr & 3) >> 1);
+    h = rr & 1;
+  } else {
+    const int qq = r >> 4;  // 16q + 8(i>>2) + (i&3) + 4h with q = {0,2,1,3}[c]
+    cq = (qq == 1) ? 2 : (qq == 2) ? 1 : qq;
+    const int rr = r & 15;
+    i = 4 * (rr >> 3) + (rr & 3);
+    h = (rr >> 2) & 1;
+  }
 }
 
-// Threads [0, 64*nt) after a barrier: thread q -> task q/64, row q%8, column (q/8)%8.
-__device__ __forceinline__ void p_gateup_epilogue(const Params& p, const float* red, const PTask* tks,
-                                                  int nt, const float* xinv) {
+// Gate/up epilogue of up to nt tasks (threads q < nt*16: task q/16, channel
+// (q/2)%8, column q%2): sum the 16 warps' partials, SwiGLU, publish the h word
+// of the column's (token, slot) entry.  red: [task][warp][16 rows][2 columns].
+__device__ __forceinline__ void p_gateup_epilogue(const Params& p, const float* red, int nt, const uint32_t* ent_of,
+                                                  const int* ncols_of, const int* ch0_of, const float* xinv,
+                                                  uint2* hw, uint32_t epoch) {
   const int q = threadIdx.x;
-  if (q >= nt * 64) return;  // whole warps: 64*nt is a multiple of 32
-  const int K = p.k;
-  const PTask& tk = tks[q >> 6];
-  const float* rt = red + (q >> 6) * kPWarps * 128;
-  const int r = q & 7, n = (q >> 3) & 7;
-  const bool ok = n < tk.ncols;
-  float hv = 0.f;
-  uint32_t id = 0;
-  if (ok) {
-    float up = 0.f, gate = 0.f;
+  if (q >= nt * 16) return;
+  const int m = q >> 4, r = (q >> 1) & 7, n = q & 1;
+  if (n >= ncols_of[m]) return;
+  const float* rt = red + m * kPWarps * 32;
+  float up = 0.f, gate = 0.f;
 #pragma unroll
-    for (int w = 0; w < kPWarps; ++w) {
-      up += rt[w * 128 + r * 8 + n];
-      gate += rt[w * 128 + (8 + r) * 8 + n];
-    }
-    id = tk.ent[n];
-    const float inv = xinv[id / (K + 1)];
-    up *= inv;
-    gate *= inv;
-    hv = (gate / (1.0f + expf(-gate))) * up;
-    p.ws.h[static_cast<size_t>(id) * p.I + tk.ch0 + r] = hv;
+  for (int w = 0; w < kPWarps; ++w) {
+    up += rt[w * 32 + r * 2 + n];
+    gate += rt[w * 32 + (8 + r) * 2 + n];
   }
-  float m = fabsf(hv);
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-  if (ok && r == 0) p.ws.hmaxp[static_cast<size_t>(id) * (p.I / 8) + tk.ch0 / 8] = m;
+  const uint32_t id = ent_of[m * kPMaxT + n];
+  const float inv = xinv[id / (p.k + 1)];
+  up *= inv;
+  gate *= inv;
+  const float hv = (gate / (1.0f + expf(-gate))) * up;
+  xw_store(hw + static_cast<size_t>(id) * p.I + ch0_of[m] + r, __float_as_uint(hv), epoch);
 }
 
-// Expert-parallel all-reduce of one 16-column output tile for T tokens.
-// Every rank's fp32 partial part(t, r) (t < T, r < 16) goes to each rank as
-// one 8-byte store {value, epoch} (single-copy atomic), so a word that
-// carries this call's epoch carries this call's value: the receiver polls
-// the words themselves, with no separate flag and no fence, and sums the
-// ranks' values in rank order (the same order on every rank) before
-// handing them to emit(t, r, sum).  Polls are bounded; on timeout the status
-// word gets RNB_STATUS_TIMEOUT and that value is not emitted.  Buffers
-// alternate by epoch parity: a rank cannot start epoch e+2 before every rank
-// has sent epoch e+1, which each rank does only after reading epoch e.
-template <typename Part, typename Emit>
-__device__ void ep_exchange_tile(const Params& p, int n0, int T, Part part, Emit emit) {
-  const int tid = threadIdx.x, W = p.ep_world;
-  __shared__ uint32_t s_epoch;
-  if (tid == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(p.ep_seq) + 1u;
-  __syncthreads();
-  const uint32_t epoch = s_epoch;
-  const size_t par = static_cast<size_t>(epoch & 1u) * W * kEpMaxT * p.H;
-  for (int i = tid; i < T * 16; i += blockDim.x) {
-    const int t = i >> 4, r = i & 15;
-    const uint32_t v = __float_as_uint(part(t, r));
-    const size_t o = par + (static_cast<size_t>(p.ep_rank) * kEpMaxT + t) * p.H + n0 + r;
-    for (int q = 0; q < W; ++q)
-      asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};\n" ::"l"(p.ep_recv[q] + o), "r"(v), "r"(epoch)
-                   : "memory");
+// Two-group weight tile of one warp (16 rows x 128 inputs): codes with a
+// 16-byte-chunk XOR swizzle instead of padding, then bf16 scales and biases.
+// 8-bit rows are 128 B: chunk ^= (row & 1) << 2, so the 8 lanes of a 16-byte
+// read phase (rows g, g+1) hit disjoint banks; 4-bit rows are 64 B: chunk ^=
+// ((row >> 1) & 1) << 1, so the 16 lanes of an 8-byte phase (rows g..g+3) do.
+template <int BITS>
+struct Tile2 {
+  static constexpr int kRowBytes = 2 * 8 * BITS;
+  static constexpr int kCodeBytes = 16 * kRowBytes;
+  static constexpr int kParBytes = 16 * 2 * 2;
+  static constexpr int kBytes = kCodeBytes + 2 * kParBytes;
+  static constexpr int kChunks = kRowBytes / 16;
+  __device__ static __forceinline__ int swz(int row) {
+    return BITS == 8 ? ((row & 1) << 2) : (((row >> 1) & 1) << 1);
   }
-  for (int i = tid; i < T * 16; i += blockDim.x) {
-    const int t = i >> 4, r = i & 15;
-    const uint2* own = p.ep_recv[p.ep_rank] + par + static_cast<size_t>(t) * p.H + n0 + r;
-    float sum = 0.f;
-    bool ok = true;
-    for (int q = 0; q < W && ok; ++q) {
-      const uint2* src = own + static_cast<size_t>(q) * kEpMaxT * p.H;
-      uint32_t val, ep;
-      uint64_t t0 = 0, now;
-      for (int spin = 0;; ++spin) {
-        asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];\n" : "=r"(val), "=r"(ep) : "l"(src) : "memory");
-        if (ep == epoch) break;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-        if (spin == 0) t0 = now;
-        if (now - t0 > kEpSpinLimitNs) {
-          atomicOr(p.ws.status, RNB_STATUS_TIMEOUT);
-          ok = false;
-          break;
-        }
-      }
-      sum += __uint_as_float(val);
-    }
-    if (ok) emit(t, r, sum);
+};
+
+template <int BITS, typename RowOf>
+__device__ __forceinline__ void tile2_issue(char* sm, const uint32_t* wbase, const uint16_t* sbase,
+                                            const uint16_t* bbase, size_t wrow, size_t srow, int g0,
+                                            RowOf row, int lane) {
+  using TL = Tile2<BITS>;
+  const size_t kw0 = static_cast<size_t>(g0) * kGroup * BITS / 32;
+#pragma unroll
+  for (int q = lane; q < 16 * TL::kChunks; q += 32) {
+    const int i = q / TL::kChunks, j = q % TL::kChunks;
+    cp_async16(sm + i * TL::kRowBytes + ((j ^ TL::swz(i)) * 16), wbase + row(i) * wrow + kw0 + j * 4);
+  }
+  if (lane < 16) {
+    const size_t r = row(lane);
+    cp_async4(sm + TL::kCodeBytes + lane * 4, sbase + r * srow + g0);
+    cp_async4(sm + TL::kCodeBytes + TL::kParBytes + lane * 4, bbase + r * srow + g0);
   }
 }
 
-// Expert-parallel reduction after the decode chain: CTA b owns output
-// columns [16b, 16b+16) of the fp32 partial (p.ws.yws reused as [T][H]).
-// Cooperative launch, so every CTA is resident while it waits for peers.
-__global__ void __launch_bounds__(256) k_ep_reduce(Params p, const float* partial) {
-  const int n0 = blockIdx.x * 16;
-  ep_exchange_tile(
-      p, n0, p.T, [&](int t, int r) { return __ldcg(partial + static_cast<size_t>(t) * p.H + n0 + r); },
-      [&](int t, int r, float v) {
-        const size_t o = static_cast<size_t>(t) * p.H + n0 + r;
-        if (p.y_f32)
-          static_cast<float*>(p.out)[o] = v;
-        else
-          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
-      });
-  // the last CTA out advances the sequence word for the next exchange
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(p.ep_seq + 1, 1u) == gridDim.x - 1) {
-      p.ep_seq[1] = 0;
-      p.ep_seq[0] += 1;
-      __threadfence();
+// acc[0..3] (rows g, g+8 x columns 2c, 2c+1) += affine(tile . B) over the
+// tile's two groups.  bfrag(gi, xb) fills the 8 activation pairs of group gi
+// for this lane's column g; gsum(gi, col) is the group sum of column col
+// (0 -> 2c, 1 -> 2c+1) of the values the MMAs see; ginv(gi, col) multiplies
+// the group's contribution (an activation scale undone per group).
+template <int BITS, typename BFrag, typename GSum, typename GInv>
+__device__ __forceinline__ void tile2_mma(const char* sm, int g, int c, BFrag bfrag, GSum gsum, GInv ginv,
+                                          float (&acc)[4]) {
+  using TL = Tile2<BITS>;
+  const uint16_t* S = reinterpret_cast<const uint16_t*>(sm + TL::kCodeBytes);
+  const uint16_t* B = reinterpret_cast<const uint16_t*>(sm + TL::kCodeBytes + TL::kParBytes);
+  const int q = (c == 1) ? 2 : (c == 2) ? 1 : c;
+#pragma unroll
+  for (int gi = 0; gi < 2; ++gi) {
+    RowPairs pa, pb;
+    if (BITS == 8) {
+      const int ch = gi * 4 + c;
+      pa = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16));
+      pb = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16));
+    } else {
+      const int ch = gi * 2 + (q >> 1), off = 8 * (q & 1);
+      pa = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(sm + g * TL::kRowBytes + (ch ^ TL::swz(g)) * 16 + off));
+      pb = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(sm + (g + 8) * TL::kRowBytes + (ch ^ TL::swz(g + 8)) * 16 + off));
     }
+    uint32_t xb[8];
+    bfrag(gi, xb);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+      mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xb[2 * m], xb[2 * m + 1]);
+    // the codes entered the MMAs as fp16 subnormals q * 2^-24 (rnb_common.cuh):
+    // the scales carry the 2^24 back (exact)
+    const float sa = bf16_bits_to_f32(S[g * 2 + gi]) * 0x1p24f, ba = bf16_bits_to_f32(B[g * 2 + gi]);
+    const float sb = bf16_bits_to_f32(S[(g + 8) * 2 + gi]) * 0x1p24f, bb = bf16_bits_to_f32(B[(g + 8) * 2 + gi]);
+    const float xs0 = gsum(gi, 0), xs1 = gsum(gi, 1);
+    const float i0 = ginv(gi, 0), i1 = ginv(gi, 1);
+    acc[0] = fmaf(i0, fmaf(sa, d[0], ba * xs0), acc[0]);
+    acc[1] = fmaf(i1, fmaf(sa, d[1], ba * xs1), acc[1]);
+    acc[2] = fmaf(i0, fmaf(sb, d[2], bb * xs0), acc[2]);
+    acc[3] = fmaf(i1, fmaf(sb, d[3], bb * xs1), acc[3]);
   }
 }
 
 // EP: compiled with the expert-parallel exchange (ep_world > 1); the
 // single-GPU instance carries no exchange code.
 template <int BITS, bool EP>
-__global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) {
+__global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan pl) {
   extern __shared__ __align__(16) char sm[];
+  // The parameters are read from a shared-memory copy: a kernel parameter
+  // is an operand in the constant bank, and on this single-pass kernel each
+  // of its scattered reads would otherwise risk a constant-cache miss (an L2
+  // round trip) on the critical path.
+  __shared__ __align__(16) Params s_params;
+  for (int i = threadIdx.x; i < static_cast<int>(sizeof(Params) / 4); i += blockDim.x)
+    reinterpret_cast<uint32_t*>(&s_params)[i] = reinterpret_cast<const uint32_t*>(&p_arg)[i];
   using TL = Tile2<BITS>;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int cta = blockIdx.x, NC = gridDim.x;
-  const int T = p.T, K = p.k, Et = p.E_total;
+  const int S = pl.S;  // ring slots per warp
+  char* ring = sm + pl.off_ring + static_cast<size_t>(warp) * S * TL::kBytes;  // this warp's slots
+  char* sSdn = sm + pl.off_sdn;
   uint32_t* sX = reinterpret_cast<uint32_t*>(sm + pl.off_x);
   float* sXs = reinterpret_cast<float*>(sm + pl.off_xs);
-  char* sBR = sm + pl.off_br;
-  char* sCR = sm + pl.off_cr;
-  float* sH = reinterpret_cast<float*>(sm + pl.off_h);
+  uint32_t* sIvl = reinterpret_cast<uint32_t*>(sm + pl.off_ivl);
   float* sRed = reinterpret_cast<float*>(sm + pl.off_red);
+  // this warp's B fragments of the down MMAs: [kDownBatch units][T columns][64]
+  uint32_t* sHf = reinterpret_cast<uint32_t*>(sm + pl.off_hf) + warp * (kDownBatch * 64 * p_arg.T);
   float* sRedC = reinterpret_cast<float*>(sm + pl.off_redc);
   PMisc* ms = reinterpret_cast<PMisc*>(sm + pl.off_misc);
-  const size_t task_bytes = static_cast<size_t>(kPWarps) * TL::kBytes;
-  const size_t gwrow = static_cast<size_t>(p.H) * BITS / 32, gsrow = p.H / kGroup;
-  const size_t dwrow = static_cast<size_t>(p.I) * BITS / 32, dsrow = p.I / kGroup;
-  const int n_ch = p.I / 8;
-  const int nq = p.I / 128;  // K quarters of the down projection
-  uint32_t* bar1 = p.ws.ctr + 1 + p.H / 16;
-  uint32_t* bar2 = bar1 + 1;
-  uint32_t* exitc = bar1 + 2;
-  const bool owns_sgu = p.has_shared && cta >= pl.n_rtiles && cta < pl.n_rtiles + n_ch &&
-                        ((p.shared_qmask >> (((cta - pl.n_rtiles) * 8) / 128)) & 1u);
-  const int n_sch = p.has_shared ? __popc(p.shared_qmask & ((1u << nq) - 1u)) * 16 : 0;  // shared gate/up tasks
-  auto is_local = [&](uint32_t e) { return e - static_cast<uint32_t>(p.off) < static_cast<uint32_t>(p.E); };
-  const int n0 = cta * 16;
-  const bool owns_rows = n0 < p.H;
-  auto gu_row = [&](int ch0) { return [=](int i) -> size_t { return i < 8 ? ch0 + i : p.I + ch0 + i - 8; }; };
+  const uint32_t off_xn = pl.off_xn, off_hf = pl.off_hf;
+  __syncthreads();
+  const Params& p = s_params;
+  const int T = p.T, K = p.k, Et = p.E_total, I = p.I, H = p.H;
+  const int G = H / kGroup;
+  const size_t gwrow = static_cast<size_t>(H) * BITS / 32, gsrow = H / kGroup;
+  const size_t dwrow = static_cast<size_t>(I) * BITS / 32, dsrow = I / kGroup;
+  const int n_ch = I / 8;  // gate/up tasks per expert
+  const int nq = I / 128;  // down K quarters
+  uint2* lw = p.ws.lw;     // [T][Et + 1] logit words
+  uint2* hw = p.ws.hw;     // [T][K + 1][I] h words
+  const uint32_t e_off = static_cast<uint32_t>(p.off), e_cnt = static_cast<uint32_t>(p.E);
+  auto is_local = [&](uint32_t e) { return e - e_off < e_cnt; };
+  // roles
+  const int row_cta0 = NC - H / 16;  // CTAs [row_cta0, NC) own 16 output rows each
+  const bool owns_rows = cta >= row_cta0;
+  const int n0 = (cta - row_cta0) * 16;
+  const uint32_t qmask = p.shared_qmask & ((1u << nq) - 1u);
+  const bool has_shared = p.has_shared != 0;
+  // the shared-expert gate/up tasks go to the last I/8 CTAs: routed tasks are
+  // dealt round-robin from CTA 0, so the last CTAs have one fewer
+  const int sg_task = cta - (NC - n_ch);
+  const bool owns_sgu = has_shared && sg_task >= 0 && ((qmask >> ((sg_task * 8) / 128)) & 1u);
+  const bool sh_down = owns_rows && has_shared && qmask != 0u;
+  const int j0 = owns_sgu ? 1 : 0;  // ring unit 0: this warp's slice of the shared-expert gate/up task
+  auto gu_row = [&](int ch0) { return [=](int i) -> size_t { return i < 8 ? ch0 + i : I + ch0 + i - 8; }; };
   auto dn_row = [=](int i) -> size_t { return static_cast<size_t>(n0 + i); };
 
+  // ---- prologue: weights only (before the programmatic-launch wait)
   RNB_TRACE_MARK(p, 0);
-  // ---- phase A: requests that need no routing
-  // Router rows of this CTA: cta and cta + NC of the E_total + 1 rows (the
-  // last is the shared-expert gate); warp w covers hidden [128 w, 128 w + 128),
-  // 4 values per lane.  The rows are read before the programmatic-launch wait.
+  // Router rows of this CTA: cta and cta + NC of the Et + 1 rows (the last is
+  // the shared gate); warp w covers hidden [128 w, 128 w + 128), 4 values per lane.
   const int k0r = warp * 128 + lane * 4;
   uint2 wr[2];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const uint16_t* pr = router_row(p, cta + i * NC);
+    const int row = cta + i * NC;
+    const uint16_t* pr = row < Et ? p.router_w + static_cast<size_t>(row) * H
+                                  : (row == Et && has_shared ? p.sgate_w : nullptr);
     wr[i] = pr ? __ldg(reinterpret_cast<const uint2*>(pr + k0r)) : make_uint2(0, 0);
   }
-  if (owns_sgu) {
-    const int ch0 = (cta - pl.n_rtiles) * 8;
-    tile2_issue<BITS>(sBR + warp * TL::kBytes, p.sgu_w, p.sgu_s, p.sgu_b, gwrow, gsrow, warp * 2, gu_row(ch0), lane);
-  }
-  cp_async_commit();  // group: shared gate/up
-  if (owns_rows && p.has_shared && warp < nq && ((p.shared_qmask >> warp) & 1u)) {
-    // phase-C slots 0..nq-1: shared expert down, K quarter = warp
-    tile2_issue<BITS>(sCR + warp * TL::kBytes, p.sdn_w, p.sdn_s, p.sdn_b, dwrow, dsrow, warp * 2, dn_row, lane);
-  }
-  cp_async_commit();  // group: shared down
+  if (owns_sgu)
+    tile2_issue<BITS>(ring, p.sgu_w, p.sgu_s, p.sgu_b, gwrow, gsrow, warp * 2, gu_row(sg_task * 8), lane);
+  cp_async_commit();  // group: shared gate/up slice (ring unit 0; may be empty)
+  if (sh_down && warp < nq && ((qmask >> warp) & 1u))
+    tile2_issue<BITS>(sSdn + warp * TL::kBytes, p.sdn_w, p.sdn_s, p.sdn_b, dwrow, dsrow, warp * 2, dn_row, lane);
+  cp_async_commit();  // group: this warp's shared-down quarter
   RNB_TRACE_MARK(p, 1);
-  griddep_wait();  // x may come from the previous kernel on the stream
+  griddep_launch_dependents();
+  griddep_wait();  // x (and the workspace) may come from the previous kernel on the stream
+  RNB_TRACE_MARK(p, 2);
+  if (tid == 0) ms->epoch = *reinterpret_cast<volatile uint32_t*>(p.ws.seq) + 1u;
+  // this lane's router activations (tokens 0, 1), loaded together with the
+  // sequence word: one round trip (the fused layer glue reads them below)
+  uint2 xr[2] = {make_uint2(0, 0), make_uint2(0, 0)};
+  if (!p.norm_w) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+      if (t < T) xr[t] = *reinterpret_cast<const uint2*>(p.x + static_cast<size_t>(t) * H + k0r);
+  }
   // Fused layer glue: this CTA's own copy of the normalised tokens.  The sum
   // of squares runs exactly as in rnb_add_rmsnorm (threads 0..255 striding by
   // 256, a shuffle tree, the 8 warp sums in order), so both paths give the
   // same bits.  CTA 0 also writes the residual sum and the normalised tokens.
   const uint16_t* xin = p.x;
   if (p.norm_w) {
-    uint16_t* sXn = reinterpret_cast<uint16_t*>(sm + pl.off_xn);
+    uint16_t* sXn = reinterpret_cast<uint16_t*>(sm + off_xn);
     for (int t = 0; t < T; ++t) {
-      const size_t b = static_cast<size_t>(t) * p.H;
+      const size_t b = static_cast<size_t>(t) * H;
       if (tid < 256) {
         float ss = 0.f;
-        for (int i = tid; i < p.H; i += 256) {
+        for (int i = tid; i < H; i += 256) {
           float v = bf16_bits_to_f32(p.resid[b + i]);
           if (p.y_prev) v = bf16_round(v + bf16_bits_to_f32(p.y_prev[b + i]));
           sXn[b + i] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
@@ -1330,8 +1358,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
       float tot = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) tot += ms->red[i];
-      const float r = rsqrtf(tot / static_cast<float>(p.H) + p.norm_eps);
-      for (int i = tid; i < p.H; i += blockDim.x) {
+      const float r = rsqrtf(tot / static_cast<float>(H) + p.norm_eps);
+      for (int i = tid; i < H; i += blockDim.x) {
         const uint16_t rv = sXn[b + i];
         const uint16_t xn = __bfloat16_as_ushort(__float2bfloat16_rn(bf16_bits_to_f32(rv) * r * bf16_bits_to_f32(p.norm_w[i])));
         if (cta == 0) {
@@ -1344,462 +1372,506 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p, PPlan pl) 
     }
     xin = sXn;
   }
+  __syncthreads();
+  const uint32_t epoch = ms->epoch;
+
+  // ---- router: rows cta, cta + NC against tokens 0, 1
   {
-    // Per lane 4 products per (row, token), summed with FMAs, then a 5-level
-    // shuffle tree and a 4-level tree over the warps: at most 12 roundings of
-    // partial sums bounded by sum |x_i w_i|, well inside the 2^-18 allowance
-    // of the rounding certificate (rnb_route.cuh).
-    float* q = ms->rnorm[warp];  // [0,4): dots (row i, token t) at 2i+t; [4,6) sum w^2; [6,8) sum |w|; [8,10) sum x^2; [10,12) max |x|
+    // Dots in fp64: bf16 products are exact and the fp64 partial sums err by
+    // at most ~2^-49 of sum |x_i w_i|, so the bf16 rounding of each logit is
+    // certified (route_interval_f64) without an fp64 recompute in routing.
+    // Norms (for the certificate's bound) in fp32.
     float xf[2][4];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      const uint2 xv = t < T ? *reinterpret_cast<const uint2*>(xin + static_cast<size_t>(t) * p.H + k0r)
-                             : make_uint2(0, 0);
+      const uint2 xv = p.norm_w && t < T ? *reinterpret_cast<const uint2*>(xin + static_cast<size_t>(t) * H + k0r) : xr[t];
       xf[t][0] = __uint_as_float(xv.x << 16);
       xf[t][1] = __uint_as_float(xv.x & 0xFFFF0000u);
       xf[t][2] = __uint_as_float(xv.y << 16);
       xf[t][3] = __uint_as_float(xv.y & 0xFFFF0000u);
     }
-    float v[12];
+    double dv[4];
+    float v[8];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const float wf[4] = {__uint_as_float(wr[i].x << 16), __uint_as_float(wr[i].x & 0xFFFF0000u),
                            __uint_as_float(wr[i].y << 16), __uint_as_float(wr[i].y & 0xFFFF0000u)};
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
-        float d = wf[0] * xf[t][0];
-        d = fmaf(wf[1], xf[t][1], d);
-        d = fmaf(wf[2], xf[t][2], d);
-        d = fmaf(wf[3], xf[t][3], d);
-        v[2 * i + t] = d;
+        double d = static_cast<double>(wf[0]) * static_cast<double>(xf[t][0]);
+        d = fma(static_cast<double>(wf[1]), static_cast<double>(xf[t][1]), d);
+        d = fma(static_cast<double>(wf[2]), static_cast<double>(xf[t][2]), d);
+        d = fma(static_cast<double>(wf[3]), static_cast<double>(xf[t][3]), d);
+        dv[2 * i + t] = d;
       }
-      v[4 + i] = fmaf(wf[0], wf[0], fmaf(wf[1], wf[1], fmaf(wf[2], wf[2], wf[3] * wf[3])));
-      v[6 + i] = (fabsf(wf[0]) + fabsf(wf[1])) + (fabsf(wf[2]) + fabsf(wf[3]));
+      v[i] = fmaf(wf[0], wf[0], fmaf(wf[1], wf[1], fmaf(wf[2], wf[2], wf[3] * wf[3])));
+      v[2 + i] = (fabsf(wf[0]) + fabsf(wf[1])) + (fabsf(wf[2]) + fabsf(wf[3]));
     }
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      v[8 + t] = fmaf(xf[t][0], xf[t][0], fmaf(xf[t][1], xf[t][1], fmaf(xf[t][2], xf[t][2], xf[t][3] * xf[t][3])));
-      v[10 + t] = fmaxf(fmaxf(fabsf(xf[t][0]), fabsf(xf[t][1])), fmaxf(fabsf(xf[t][2]), fabsf(xf[t][3])));
+      v[4 + t] = fmaf(xf[t][0], xf[t][0], fmaf(xf[t][1], xf[t][1], fmaf(xf[t][2], xf[t][2], xf[t][3] * xf[t][3])));
+      v[6 + t] = fmaxf(fmaxf(fabsf(xf[t][0]), fabsf(xf[t][1])), fmaxf(fabsf(xf[t][2]), fabsf(xf[t][3])));
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
+    for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-      for (int j = 0; j < 12; ++j) {
+      for (int j = 0; j < 4; ++j) dv[j] += __shfl_xor_sync(0xffffffffu, dv[j], o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
         const float u = __shfl_xor_sync(0xffffffffu, v[j], o);
-        v[j] = j >= 10 ? fmaxf(v[j], u) : v[j] + u;
+        v[j] = j >= 6 ? fmaxf(v[j], u) : v[j] + u;
       }
-    if (lane < 12) {
+    }
+    if (lane < 4) {
+      double mine = dv[0];
+#pragma unroll
+      for (int j = 1; j < 4; ++j) mine = lane == j ? dv[j] : mine;
+      ms->rdot[warp][lane] = mine;
+    } else if (lane < 12) {
       float mine = v[0];
 #pragma unroll
-      for (int j = 1; j < 12; ++j) mine = lane == j ? v[j] : mine;
-      q[lane] = mine;
+      for (int j = 1; j < 8; ++j) mine = lane - 4 == j ? v[j] : mine;
+      ms->rnorm[warp][lane - 4] = mine;
     }
     __syncthreads();
-    if (tid < 4) {
-      const int i = tid >> 1, t = tid & 1, row = cta + i * NC;
+    // warp w < 4 finishes (row cta + (w >> 1) * NC, token w & 1): lanes 0..15
+    // hold the 16 warps' partials, added by a fixed shuffle tree
+    if (warp < 4) {
+      const int i = warp >> 1, t = warp & 1, row = cta + i * NC;
       if (row <= Et && t < T) {
-        float a[5][16];
+        const int w = lane & 15;
+        double a0 = ms->rdot[w][2 * i + t];
+        float a1 = ms->rnorm[w][i], a2 = ms->rnorm[w][2 + i], a3 = ms->rnorm[w][4 + t], a4 = ms->rnorm[w][6 + t];
 #pragma unroll
-        for (int w = 0; w < kPWarps; ++w) {
-          const float* qw = ms->rnorm[w];
-          a[0][w] = qw[2 * i + t];
-          a[1][w] = qw[4 + i];
-          a[2][w] = qw[6 + i];
-          a[3][w] = qw[8 + t];
-          a[4][w] = qw[10 + t];
+        for (int o = 8; o > 0; o >>= 1) {
+          a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+          a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+          a2 += __shfl_xor_sync(0xffffffffu, a2, o);
+          a3 += __shfl_xor_sync(0xffffffffu, a3, o);
+          a4 = fmaxf(a4, __shfl_xor_sync(0xffffffffu, a4, o));
         }
-#pragma unroll
-        for (int st = 8; st > 0; st >>= 1)
-#pragma unroll
-          for (int w = 0; w < st; ++w) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) a[j][w] += a[j][w + st];
-            a[4][w] = fmaxf(a[4][w], a[4][w + st]);
-          }
         // expert rows: candidate interval of the bf16 logit; last row: fp32 shared-gate logit
-        reinterpret_cast<uint32_t*>(p.ws.logit)[static_cast<size_t>(t) * (Et + 1) + row] =
-            row < Et ? route_interval(a[0][0], a[3][0], a[4][0], a[1][0], a[2][0], kRouteRelDecode)
-                     : __float_as_uint(a[0][0]);
+        if (lane == 0) {
+          const uint32_t val = row < Et ? route_interval_f64(a0, a3, a4, a1, a2) : __float_as_uint(static_cast<float>(a0));
+          xw_store(lw + static_cast<size_t>(t) * (Et + 1) + row, val, epoch);
+        }
       }
     }
-    __syncthreads();
-    if (tid == 0) arrive_release(bar1);
-    RNB_TRACE_MARK(p, 2);
-  }
-  xprep_cta<BITS>(xin, T, sX, sXs, ms->xinv, reinterpret_cast<__half*>(sH), ms->red);
-
-  if (owns_sgu) {
-    cp_async_wait_pending(1);  // the shared-down group may still be in flight
-    __syncwarp();
-    if (tid < 8) ms->shared_ent[tid] = static_cast<uint32_t>((tid < T ? tid : 0) * (K + 1) + K);
-    __syncthreads();
-    const PTask tk{ms->shared_ent, T, (cta - pl.n_rtiles) * 8};
-    p_gateup_mma<BITS>(p, sBR, sX, sXs, sRed, tk);
-    __syncthreads();
-    p_gateup_epilogue(p, sRed, &tk, 1, ms->xinv);
-    __syncthreads();
-    RNB_TRACE_MARK(p, 4);
   }
   RNB_TRACE_MARK(p, 3);
+  // (the B-fragment area is free until the down phase: 4 KB of it are xprep's scratch)
+  xprep_cta<BITS>(xin, T, sX, sXs, ms->xinv, reinterpret_cast<__half*>(sm + off_hf), ms->red);
+  RNB_TRACE_MARK(p, 4);
 
-  // ---- routing (every CTA, redundantly)
-  cta_wait_count(bar1, static_cast<uint32_t>(NC), p.ws.status);
-  RNB_TRACE_MARK(p, 5);
-  for (int q = tid; q < T * (Et + 1); q += blockDim.x)
-    reinterpret_cast<uint32_t*>(sH)[q] = __ldcg(reinterpret_cast<const uint32_t*>(p.ws.logit) + q);
+  // B operand of the gate/up MMAs: this lane's column g is entry ent[g].
+  auto gateup_mma = [&](const char* slot, const uint32_t* ent, int ncols, float (&acc)[4]) {
+    const int colB = g < ncols ? g : 0;
+    const int tB = static_cast<int>(ent[colB] / (K + 1));
+    const int t0 = static_cast<int>(ent[2 * c < ncols ? 2 * c : 0] / (K + 1));
+    const int t1 = static_cast<int>(ent[2 * c + 1 < ncols ? 2 * c + 1 : 0] / (K + 1));
+    const int g0 = warp * 2;
+    tile2_mma<BITS>(
+        slot, g, c,
+        [&](int gi, uint32_t(&xb)[8]) {
+          const uint32_t* src = sX + (static_cast<size_t>(tB) * G + g0 + gi) * 32 + c * 8;
+          const uint4 u0 = reinterpret_cast<const uint4*>(src)[0];
+          const uint4 u1 = reinterpret_cast<const uint4*>(src)[1];
+          xb[0] = u0.x; xb[1] = u0.y; xb[2] = u0.z; xb[3] = u0.w;
+          xb[4] = u1.x; xb[5] = u1.y; xb[6] = u1.z; xb[7] = u1.w;
+        },
+        [&](int gi, int col) { return sXs[(col ? t1 : t0) * G + g0 + gi]; }, [](int, int) { return 1.0f; }, acc);
+  };
+  // partials of this warp for task m: lanes c == 0 hold columns 0, 1
+  auto store_partials = [&](int m, const float (&acc)[4]) {
+    if (c == 0) {
+      float* rw = sRed + (m * kPWarps + warp) * 32;
+      rw[g * 2] = acc[0];
+      rw[g * 2 + 1] = acc[1];
+      rw[(g + 8) * 2] = acc[2];
+      rw[(g + 8) * 2 + 1] = acc[3];
+    }
+  };
+
+  __shared__ uint32_t s_ent[kPMaxMine + 1][kPMaxT];
+  __shared__ int s_ncols[kPMaxMine + 1], s_ch0[kPMaxMine + 1];
+
+  // ---- routing (every CTA, redundantly): poll the logit words
+  {
+    const uint64_t deadline = gtimer() + kSpinLimitNs;
+    for (int i = tid; i < T * (Et + 1); i += blockDim.x) sIvl[i] = xw_wait(lw + i, epoch, deadline, p.ws.status);
+  }
   __syncthreads();
+  RNB_TRACE_MARK(p, 6);
   if (warp < T) {
     const int t = warp;
-    const uint32_t* ivl = reinterpret_cast<const uint32_t*>(sH + t * (Et + 1));
     int e;
     float sc;
-    RNB_TRACE_MARK(p, 12);
-    const int nre = warp_route_token_body(ivl, Et, K, xin + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane,
-                                          false, nullptr, &e, &sc);
-    RNB_TRACE_MARK(p, 13);
+    const int nre = warp_route_token_body(sIvl + t * (Et + 1), Et, K, xin + static_cast<size_t>(t) * H, p.router_w, H,
+                                          lane, false, nullptr, &e, &sc);
 #ifdef RNB_TRACE
-    if (t == 0 && lane == 0) trace_value(p, 11, nre);
+    if (t == 0 && lane == 0) trace_value(p, 31, nre);
 #else
     (void)nre;
 #endif
+    RNB_TRACE_MARK(p, 18);
     if (lane < K) {
       ms->inds[t][lane] = static_cast<uint32_t>(e);
       ms->scores[t][lane] = sc;
     }
-    if (lane == 0) ms->sg[t] = p.has_shared ? 1.0f / (1.0f + expf(-sH[t * (Et + 1) + Et])) : 0.f;
+    if (lane == 0) ms->sg[t] = p.has_shared ? 1.0f / (1.0f + expf(-__uint_as_float(sIvl[t * (Et + 1) + Et]))) : 0.f;
   }
   __syncthreads();
-  RNB_TRACE_MARK(p, 15);
-  // per-expert token lists: entry i = t*K + slot, ordered by (expert, i);
-  // one token: its K distinct experts in slot order
-  // (act_e holds local expert indices; experts of other ranks are left out)
-  if (T == 1) {
-    if (tid == 0) {
-      uint32_t n = 0;
-      for (int s2 = 0; s2 < K; ++s2) {
-        const uint32_t e = ms->inds[0][s2];
-        if (!is_local(e)) continue;
-        ms->act_e[n] = e - static_cast<uint32_t>(p.off);
-        ms->act_cnt[n] = 1;
-        ms->act_ent[n][0] = static_cast<uint32_t>(s2);
-        ++n;
-      }
-      ms->n_act = n;
-    }
-  } else if (tid < T * K) {
-    const uint32_t e = ms->inds[tid / K][tid % K];
-    bool first = is_local(e);
-    for (int q = 0; q < tid; ++q)
-      if (ms->inds[q / K][q % K] == e) first = false;
-    ms->first[tid] = first;
-  }
-  __syncthreads();
-  if (T > 1 && tid < T * K && is_local(ms->inds[tid / K][tid % K])) {
-    const int i = tid;
-    const uint32_t e = ms->inds[i / K][i % K];
-    uint32_t a = 0, cnt = 0, pos = 0;
-    for (int j = 0; j < T * K; ++j) {
-      const uint32_t ej = ms->inds[j / K][j % K];
-      if (ms->first[j] && ej < e) ++a;
-      if (ej == e) {
-        ++cnt;
-        if (j < i) ++pos;
+  RNB_TRACE_MARK(p, 7);
+  // active local experts in (token, slot) order of first use, with their
+  // columns: lane i < T*K holds entry i; lanes holding the same expert find
+  // each other with one match, the expert's index is the number of first
+  // occurrences before its first lane
+  if (warp == 0) {
+    const bool act = lane < T * K;
+    const uint32_t e = act ? ms->inds[lane / K][lane % K] : 0xFFFFFFFFu;
+    const bool loc = act && is_local(e);
+    const uint32_t same = __match_any_sync(0xffffffffu, e);
+    const uint32_t below = (1u << lane) - 1u;
+    const bool first = loc && (same & below) == 0u;
+    const uint32_t firsts = __ballot_sync(0xffffffffu, first);
+    const int lead = __ffs(same) - 1;
+    const int a = __popc(firsts & ((1u << lead) - 1u));
+    if (loc) {
+      ms->act_ent[a][__popc(same & below)] = static_cast<uint32_t>((lane / K) * (K + 1) + lane % K);
+      if (first) {
+        ms->act_e[a] = e - static_cast<uint32_t>(p.off);
+        ms->act_cnt[a] = static_cast<uint32_t>(__popc(same));
       }
     }
-    ms->act_ent[a][pos] = static_cast<uint32_t>((i / K) * (K + 1) + (i % K));
-    if (ms->first[i]) {
-      ms->act_e[a] = e - static_cast<uint32_t>(p.off);
-      ms->act_cnt[a] = cnt;
-    }
-  }
-  if (T > 1 && tid == 0) {
-    uint32_t n = 0;
-    for (int j = 0; j < T * K; ++j) n += ms->first[j];
-    ms->n_act = n;
+    if (lane == 0) ms->n_act = static_cast<uint32_t>(__popc(firsts));
   }
   __syncthreads();
+  RNB_TRACE_MARK(p, 20);
   const int n_act = static_cast<int>(ms->n_act);
-  RNB_TRACE_MARK(p, 6);
   if (cta == 0 && tid < T * K) {
     const int t = tid / K, s = tid % K;
     if (p.inds_out) p.inds_out[tid] = ms->inds[t][s];
     if (p.scores_out) p.scores_out[tid] = ms->scores[t][s];
   }
 
-  // ---- phase B: routed gate/up tasks i = cta, cta + NC, ...
-  // Tasks i = rc, rc + NC, ... with the CTA order rotated so that the CTAs
-  // which computed a shared gate/up task in phase A (they leave the routing
-  // barrier last) come last and get the smaller task counts.
+  // ---- this CTA's work.  Every warp streams, in this order, its units
+  // through its own ring of S shared-memory slots (unit j in slot j % S,
+  // issued once unit j - S has been consumed; one cp.async group each):
+  //   [its slice of the shared-expert gate/up task (CTAs < I/8)], its slices
+  //   of the routed gate/up tasks m < mine (task i = cta + m NC: expert
+  //   i / (I/8), channels 8 (i % (I/8))), then its down pairs (routed source,
+  //   quarter) k = warp, warp + 16, ... of this CTA's rows.  The gate/up
+  //   slices go out first (the down weights are needed only after every
+  //   CTA's gate/up is done); the shared expert's down quarters were loaded
+  //   in the prologue.
   const int n_btask = n_act * n_ch;
-  const int rc = (cta + NC - (pl.n_rtiles + n_ch) % NC) % NC;
-  const int mine = n_btask > rc ? (n_btask - rc + NC - 1) / NC : 0;
-  auto issue_b = [&](int m) {
-    const int i = rc + m * NC;
-    const int a = i / n_ch, ch0 = (i % n_ch) * 8;
-    const uint32_t le = ms->act_e[a];
-    const size_t ew = static_cast<size_t>(2) * p.I * gwrow, es = static_cast<size_t>(2) * p.I * gsrow;
-    tile2_issue<BITS>(sBR + (m % pl.db) * task_bytes + warp * TL::kBytes, p.gu_w + le * ew, p.gu_s + le * es,
-                      p.gu_b + le * es, gwrow, gsrow, warp * 2, gu_row(ch0), lane);
-  };
-  // rounds of up to db tasks: all of a round's tiles resident, one barrier
-  // and one epilogue per round; the next round's copies start right after
-  for (int m = 0; m < pl.db && m < mine; ++m) issue_b(m);
-  cp_async_commit();  // group: first gate/up round
-  // phase C requests for routed experts (slots c_base.. ; shared took 0..nq-1),
-  // after the first gate/up round so that round's tiles arrive first
-  const int c_base = p.has_shared ? nq : 0;
-  const int n_ctask = c_base + nq * n_act;
-  if (owns_rows) {
-    for (int q = c_base + warp; q < n_ctask; q += kPWarps) {
-      const int a = (q - c_base) / nq, qq = (q - c_base) % nq;
-      const uint32_t le = ms->act_e[a];
-      const size_t ew = static_cast<size_t>(p.H) * dwrow, es = static_cast<size_t>(p.H) * dsrow;
-      tile2_issue<BITS>(sCR + q * TL::kBytes, p.dn_w + le * ew, p.dn_s + le * es, p.dn_b + le * es, dwrow, dsrow,
-                        qq * 2, dn_row, lane);
-    }
+  const int mine = n_btask > cta ? (n_btask - cta + NC - 1) / NC : 0;  // <= kPMaxMine (host-checked)
+  if (tid < mine) {
+    const int i = cta + tid * NC, a = i / n_ch;
+    s_ncols[tid] = static_cast<int>(ms->act_cnt[a]);
+    s_ch0[tid] = (i % n_ch) * 8;
+    for (int n = 0; n < kPMaxT; ++n) s_ent[tid][n] = ms->act_ent[a][n < static_cast<int>(ms->act_cnt[a]) ? n : 0];
   }
-  cp_async_commit();  // group: routed down
-
-#pragma unroll 1
-  for (int r0 = 0; r0 < mine; r0 += pl.db) {
-    const int nr = mine - r0 < pl.db ? mine - r0 : pl.db;
-    cp_async_wait_pending(r0 == 0 ? 1 : 0);  // the routed-down group may stay in flight
-    __syncwarp();
-    if (r0 == 0) RNB_TRACE_MARK(p, 16);
-    // A warp needs only its own tiles (its cp.async groups, waited above):
-    // it starts its MMAs without waiting for the other warps' copies; the
-    // task records for the epilogue are read after the next barrier.
-    if (tid < nr) {
-      const int i = rc + (r0 + tid) * NC, a = i / n_ch;
-      ms->tasks[tid] = PTask{ms->act_ent[a], static_cast<int>(ms->act_cnt[a]), (i % n_ch) * 8};
+  if (tid < kPMaxT) s_ent[kPMaxMine][tid] = static_cast<uint32_t>((tid < T ? tid : 0) * (K + 1) + K);
+  const int n_rpair = owns_rows ? n_act * nq : 0;  // routed down pairs of the CTA
+  const int my_down = n_rpair > warp ? (n_rpair - warp + kPWarps - 1) / kPWarps : 0;
+  const int n_units = j0 + mine + my_down;
+  auto issue = [&](int j) {  // unit j of this warp (j >= j0)
+    char* slot = ring + (j % S) * TL::kBytes;
+    const int u = j - j0;
+    if (u < mine) {
+      const int i = cta + u * NC, a = i / n_ch;
+      const uint32_t le = ms->act_e[a];
+      const size_t ew = static_cast<size_t>(2) * I * gwrow, es = static_cast<size_t>(2) * I * gsrow;
+      tile2_issue<BITS>(slot, p.gu_w + le * ew, p.gu_s + le * es, p.gu_b + le * es, gwrow, gsrow, warp * 2,
+                        gu_row((i % n_ch) * 8), lane);
+    } else {
+      const int q = warp + (u - mine) * kPWarps, a = q / nq, qq = q % nq;
+      const uint32_t le = ms->act_e[a];
+      const size_t ew = static_cast<size_t>(H) * dwrow, es = static_cast<size_t>(H) * dsrow;
+      tile2_issue<BITS>(slot, p.dn_w + le * ew, p.dn_s + le * es, p.dn_b + le * es, dwrow, dsrow, qq * 2, dn_row,
+                        lane);
     }
-#pragma unroll 1
-    for (int k2 = 0; k2 < nr; ++k2) {
-      const int i = rc + (r0 + k2) * NC, a = i / n_ch;
-      const PTask tk{ms->act_ent[a], static_cast<int>(ms->act_cnt[a]), (i % n_ch) * 8};
-      p_gateup_mma<BITS>(p, sBR + ((r0 + k2) % pl.db) * task_bytes, sX, sXs, sRed + k2 * kPWarps * 128, tk);
-    }
-    if (r0 == 0) RNB_TRACE_MARK(p, 17);
-    __syncthreads();
-    p_gateup_epilogue(p, sRed, ms->tasks, nr, ms->xinv);
-    __syncthreads();
-    if (r0 < 4) RNB_TRACE_MARK(p, 10 + r0 / pl.db);
-    for (int m = r0 + pl.db; m < r0 + 2 * pl.db && m < mine; ++m) issue_b(m);
+  };
+  RNB_TRACE_MARK(p, 21);
+  int issued = j0;  // next unit to issue (unit 0, the shared slice, went out in the prologue)
+  for (; issued < j0 + mine && issued < S; ++issued) {
+    issue(issued);
     cp_async_commit();
   }
-  // one release per CTA for all of its gate/up tasks (shared one included)
-  const uint32_t done_tasks = static_cast<uint32_t>(mine) + (owns_sgu ? 1u : 0u);
-  if (tid == 0 && done_tasks) arrive_release(bar2, done_tasks);
-  RNB_TRACE_MARK(p, 7);
-
-  // ---- phase C: down projection + combine for rows [n0, n0 + 16)
-  if (owns_rows) {
-    cp_async_wait_pending(0);
+  RNB_TRACE_MARK(p, 22);
+  // unit j: at most (issued - 1 - j) younger groups may stay pending
+  auto wait_unit = [&](int j) {
+    cp_async_wait_pending(issued - 1 - j);
     __syncwarp();
-    cta_wait_count(bar2, static_cast<uint32_t>(n_btask + n_sch), p.ws.status);
-    RNB_TRACE_MARK(p, 8);
-    // this warp's tasks q = warp, warp + 16, ... in batches of pl.cb: stage
-    // each task's activations (128 per column) and column maxima (I/8 per
-    // column) with one round trip
-    const int nt_i = p.I / 8;
-    const int per_col = 128 + nt_i;
-    float* hw = sH + static_cast<size_t>(warp) * pl.cb * T * per_col;
-    for (int q0 = warp; q0 < n_ctask; q0 += kPWarps * pl.cb) {
-      uint32_t ent_b[4];
-      int nb = 0;
-#pragma unroll 1
-      for (int bq = 0; bq < pl.cb; ++bq) {
-        const int q = q0 + bq * kPWarps;
-        if (q >= n_ctask) break;
-        const bool shared = q < c_base;
-        ++nb;
-        ent_b[bq] = 0;
-        if (shared && !((p.shared_qmask >> q) & 1u)) continue;  // another rank's quarter
-        const int a = shared ? 0 : (q - c_base) / nq, qq = shared ? q : (q - c_base) % nq;
-        const int ncols = shared ? T : static_cast<int>(ms->act_cnt[a]);
-        uint32_t ent_l = 0;
-        if (lane < 8) {
-          const int col = lane < ncols ? lane : 0;
-          ent_l = shared ? static_cast<uint32_t>(col * (K + 1) + K) : ms->act_ent[a][col];
-        }
-        float* hq = hw + bq * T * per_col;
-        float* mq = hq + T * 128;
-        // warp-uniform trip counts: every lane reaches the shuffles
-        for (int q3 = 0; q3 < ncols * 32; q3 += 32) {  // 32 16-byte pieces per column
-          const int col = q3 >> 5, piece = lane;
-          const uint32_t id = __shfl_sync(0xffffffffu, ent_l, col);
-          cp_async16(hq + col * 128 + piece * 4, p.ws.h + static_cast<size_t>(id) * p.I + qq * 128 + piece * 4);
-        }
-        for (int q3 = 0; q3 < ncols * (nt_i / 4); q3 += 32) {
-          const int q2 = q3 + lane;
-          const int col = q2 / (nt_i / 4), piece = q2 % (nt_i / 4);
-          const uint32_t id = __shfl_sync(0xffffffffu, ent_l, col < 8 ? col : 0);
-          if (q2 < ncols * (nt_i / 4))
-            cp_async16(mq + col * nt_i + piece * 4, p.ws.hmaxp + static_cast<size_t>(id) * nt_i + piece * 4);
-        }
-        ent_b[bq] = ent_l;
-      }
-      cp_async_commit();
-      cp_async_wait_pending(0);
-      __syncwarp();
-      if (q0 == warp) RNB_TRACE_MARK(p, 19);
-#pragma unroll 1
-      for (int bq = 0; bq < nb; ++bq) {
-        const int q = q0 + bq * kPWarps;
-        const bool shared = q < c_base;
-        if (shared && !((p.shared_qmask >> q) & 1u)) continue;
-        const int a = shared ? 0 : (q - c_base) / nq, qq = shared ? q : (q - c_base) % nq;
-        const int ncols = shared ? T : static_cast<int>(ms->act_cnt[a]);
-        const uint32_t ent_l = ent_b[bq];
-        const float* hq = hw + bq * T * per_col;
-        const float* mq = hq + T * 128;
-        float cmax = 0.f;  // lane col: max |h| of column col
-#pragma unroll 1
-        for (int col = 0; col < ncols; ++col) {
-          float m = 0.f;
-          for (int j = lane; j < nt_i; j += 32) m = fmaxf(m, mq[col * nt_i + j]);
-          m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
-          if (lane == col) cmax = m;
-        }
-        float hs_l = 1.f, hi_l = 1.f;
-        fp16_range_scale(cmax, hs_l, hi_l);
-        // Convert this task's activations once, in place: per column, 128
-        // fp32 values become fp16 fragments in MMA pair order (2 groups x 4
-        // lane quads x 8 pairs each; with kPhaseCSplit also the fp16
-        // remainders, 64 words further) and two group sums of what the MMAs
-        // see.  Lane l converts pairs 2(l&3), 2(l&3)+1 of quad (l>>2)&3,
-        // group l>>4.
-        {
-          const int cg = lane >> 4, cq = (lane >> 2) & 3, i0 = (lane & 3) * 2;
-          const int pb = BITS == 8 ? 16 * cq : 16 * ((cq == 1) ? 2 : (cq == 2) ? 1 : cq);
-          uint32_t* frag = reinterpret_cast<uint32_t*>(const_cast<float*>(hq));
-          float* gsb = const_cast<float*>(mq);
-#pragma unroll 1
-          for (int col = 0; col < ncols; ++col) {
-            const float sc = __shfl_sync(0xffffffffu, hs_l, col);
-            const float* src = hq + col * 128 + cg * kGroup + pb;
-            float v[4];
+  };
+  auto refill = [&]() {  // the slot of the unit just consumed is free again
+    __syncwarp();
+    if (issued < n_units) issue(issued);
+    cp_async_commit();  // (an empty group keeps the pending count exact)
+    ++issued;
+  };
+  __syncthreads();  // s_ent / s_ncols / s_ch0 visible
+
+  // ---- the shared-expert gate/up task (unit 0), loaded since the prologue
+  if (owns_sgu) {
+    cp_async_wait_pending(issued - j0 + 1);  // its group is older than the shared-down group and the ring's
+    __syncwarp();
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    gateup_mma(ring, s_ent[kPMaxMine], T, acc);
+    store_partials(0, acc);  // red slot 0; the routed tasks use 1 .. mine
+  }
+  RNB_TRACE_MARK(p, 5);
+
+  // ---- routed gate/up: each slice as it arrives; its slot takes the
+  // warp's next unit at once
+  RNB_TRACE_MARK(p, 8);
+  for (int m = 0; m < mine; ++m) {
+    const int j = j0 + m;
+    wait_unit(j);
+    if (m == 0) RNB_TRACE_MARK(p, 9);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    gateup_mma(ring + (j % S) * TL::kBytes, s_ent[m], s_ncols[m], acc);
+    store_partials(m + 1, acc);
+    refill();
+    if (m == 0) RNB_TRACE_MARK(p, 10);
+  }
+  // the remaining down units, into the slots still free (unit j takes slot
+  // j % S once unit j - S has been consumed: every unit below j0 + mine has
+  // been; the plan gives S >= 1 + the warp's down units, so all fit)
+  for (; issued < n_units && issued < j0 + mine + S; ++issued) {
+    issue(issued);
+    cp_async_commit();
+  }
+  RNB_TRACE_MARK(p, 11);
+  __syncthreads();
+  p_gateup_epilogue(p, sRed + kPWarps * 32, mine, &s_ent[0][0], s_ncols, s_ch0, ms->xinv, hw, epoch);
+  if (owns_sgu && tid >= 256 && tid < 256 + 16 * T) {
+    // threads of the upper half publish the shared task (red slot 0)
+    const int q = tid - 256;
+    const float* rt = sRed;
+    const int r = (q >> 1) & 7, n = q & 1;
+    float up = 0.f, gate = 0.f;
 #pragma unroll
-            for (int k2 = 0; k2 < 2; ++k2) {
-              v[2 * k2] = src[pair_rel<BITS>(i0 + k2, 0)] * sc;
-              v[2 * k2 + 1] = src[pair_rel<BITS>(i0 + k2, 1)] * sc;
-            }
-            __syncwarp();  // every lane has read the column before it is overwritten
-            float part = 0.f;
+    for (int w = 0; w < kPWarps; ++w) {
+      up += rt[w * 32 + r * 2 + n];
+      gate += rt[w * 32 + (8 + r) * 2 + n];
+    }
+    const uint32_t id = static_cast<uint32_t>(n * (K + 1) + K);
+    up *= ms->xinv[n];
+    gate *= ms->xinv[n];
+    xw_store(hw + static_cast<size_t>(id) * I + sg_task * 8 + r, __float_as_uint((gate / (1.0f + expf(-gate))) * up),
+             epoch);
+  }
+  RNB_TRACE_MARK(p, 12);
+
+  bool timed_out = false;
+  if (!owns_rows) {
+    cp_async_wait_pending(0);
+  } else {
+    // ---- down projection of rows [n0, n0 + 16): this warp's pairs (source,
+    // quarter): the shared expert's quarter `warp` (warp < nq, in this rank's
+    // share; tile in sSdn) and the routed pairs of its ring units, up to
+    // kDownBatch at a time.  For each batch the warp reads the pairs' h words (one round
+    // trip), converts them to fp16 with one power-of-two scale per 64-group
+    // (fp16_range_scale) into its fragment area, and runs the MMAs.
+    const uint64_t deadline = gtimer() + kSpinLimitNs;
+    const bool sh_unit = sh_down && warp < nq && ((qmask >> warp) & 1u);
+    const int n_du = (sh_unit ? 1 : 0) + my_down;
+    cp_async_wait_pending(0);  // every tile of this warp (the shared-down group and the ring units)
+    __syncwarp();
+    RNB_TRACE_MARK(p, 13);
+    // unit b of this warp: tile, quarter, columns
+    auto unit_of = [&](int b, const char*& tile, int& qq, uint32_t (&ent)[kPMaxT], int& ncols) {
+      if (sh_unit && b == 0) {
+        tile = sSdn + warp * TL::kBytes;
+        qq = warp;
+        ncols = T;
 #pragma unroll
-            for (int k2 = 0; k2 < 2; ++k2) {
-              const __half2 hi = __floats2half2_rn(v[2 * k2], v[2 * k2 + 1]);
-              const float2 hf = __half22float2(hi);
-              // 4-bit pairs 1 and 3 of a word meet codes times 16 (subnormal form)
-              const bool x16 = BITS == 4 && ((i0 + k2) & 1);
-              const __half2 q = __float2half2_rn(x16 ? 0.0625f : 1.0f);
-              const __half2 his = __hmul2(hi, q);
-              frag[col * 128 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&his);
-              if (kPhaseCSplit) {
-                const __half2 lo = __floats2half2_rn(v[2 * k2] - hf.x, v[2 * k2 + 1] - hf.y);
-                const float2 lf = __half22float2(lo);
-                const __half2 los = __hmul2(lo, q);
-                frag[col * 128 + 64 + cg * 32 + cq * 8 + i0 + k2] = *reinterpret_cast<const uint32_t*>(&los);
-                part += lf.x + lf.y;
-              }
-              part += hf.x + hf.y;
-            }
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
-            part += __shfl_xor_sync(0xffffffffu, part, 2);
-            part += __shfl_xor_sync(0xffffffffu, part, 4);
-            part += __shfl_xor_sync(0xffffffffu, part, 8);
-            __syncwarp();  // column maxima were read above; group sums reuse that space
-            if ((lane & 15) == 0) gsb[col * nt_i + cg] = part;
-          }
-          __syncwarp();
-        }
-        if (q0 == warp && bq == 0) RNB_TRACE_MARK(p, 20);
-        const int colB = g < ncols ? g : 0;
-        const int cl0 = 2 * c < ncols ? 2 * c : 0, cl1 = 2 * c + 1 < ncols ? 2 * c + 1 : 0;
-        const uint32_t* fr = reinterpret_cast<const uint32_t*>(hq) + colB * 128;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        auto bfrag = [&](int gi, uint32_t(&xh)[8], uint32_t(&xl)[8]) {
-          const uint4 h0 = *reinterpret_cast<const uint4*>(fr + gi * 32 + c * 8);
-          const uint4 h1 = *reinterpret_cast<const uint4*>(fr + gi * 32 + c * 8 + 4);
-          const uint4 l0 = *reinterpret_cast<const uint4*>(fr + 64 + gi * 32 + c * 8);
-          const uint4 l1 = *reinterpret_cast<const uint4*>(fr + 64 + gi * 32 + c * 8 + 4);
-          xh[0] = h0.x; xh[1] = h0.y; xh[2] = h0.z; xh[3] = h0.w;
-          xh[4] = h1.x; xh[5] = h1.y; xh[6] = h1.z; xh[7] = h1.w;
-          xl[0] = l0.x; xl[1] = l0.y; xl[2] = l0.z; xl[3] = l0.w;
-          xl[4] = l1.x; xl[5] = l1.y; xl[6] = l1.z; xl[7] = l1.w;
-        };
-        auto gsum = [&](int gi, int col) { return mq[(col ? cl1 : cl0) * nt_i + gi]; };
-        tile2_mma<BITS, kPhaseCSplit>(sCR + q * TL::kBytes, g, c, bfrag, gsum, acc);
-        if (q0 == warp && bq == 0) RNB_TRACE_MARK(p, 21);
-        const float inv0 = __shfl_sync(0xffffffffu, hi_l, 2 * c);
-        const float inv1 = __shfl_sync(0xffffffffu, hi_l, 2 * c + 1);
-        const uint32_t id0 = __shfl_sync(0xffffffffu, ent_l, 2 * c);
-        const uint32_t id1 = __shfl_sync(0xffffffffu, ent_l, 2 * c + 1);
-        if (2 * c < ncols) {
-          float* dst = sRedC + (static_cast<size_t>(id0) * nq + qq) * 16;
-          dst[g] = acc[0] * inv0;
-          dst[g + 8] = acc[2] * inv0;
-        }
-        if (2 * c + 1 < ncols) {
-          float* dst = sRedC + (static_cast<size_t>(id1) * nq + qq) * 16;
-          dst[g] = acc[1] * inv1;
-          dst[g + 8] = acc[3] * inv1;
-        }
+        for (int n = 0; n < kPMaxT; ++n) ent[n] = static_cast<uint32_t>((n < T ? n : 0) * (K + 1) + K);
+      } else {
+        const int u = b - (sh_unit ? 1 : 0);
+        const int jj = j0 + mine + u, q = warp + u * kPWarps, a = q / nq;
+        tile = ring + (jj % S) * TL::kBytes;
+        qq = q % nq;
+        ncols = static_cast<int>(ms->act_cnt[a]);
+#pragma unroll
+        for (int n = 0; n < kPMaxT; ++n) ent[n] = ms->act_ent[a][n < ncols ? n : 0];
       }
-    }
-    RNB_TRACE_MARK(p, 22);
-    __syncthreads();
-    RNB_TRACE_MARK(p, 23);
-    // each source's quarters summed in place (quarter 0 slot), then the
-    // ordered weighted sum per (token, row)
-    const int nsrc = K + (p.has_shared ? 1 : 0);
-    for (int q = tid; q < T * nsrc * 16; q += blockDim.x) {
-      const int t = q / (nsrc * 16), s = (q / 16) % nsrc, r = q % 16;
-      if (s < K && !is_local(ms->inds[t][s])) continue;
-      float* y = sRedC + static_cast<size_t>(t * (K + 1) + (s < K ? s : K)) * nq * 16;
-      float ys = 0.f;
-      for (int qq = 0; qq < nq; ++qq)
-        if (s < K || ((p.shared_qmask >> qq) & 1u)) ys += y[qq * 16 + r];
-      y[r] = ys;
-    }
-    __syncthreads();
-    float acc = 0.f;
-    if (tid < T * 16) {
-      const int t = tid >> 4, r = tid & 15;
-      for (int s = 0; s < K; ++s)
-        if (is_local(ms->inds[t][s])) acc += ms->scores[t][s] * sRedC[static_cast<size_t>(t * (K + 1) + s) * nq * 16 + r];
-      if (p.has_shared && (p.shared_qmask & ((1u << nq) - 1u)))
-        acc += ms->sg[t] * sRedC[static_cast<size_t>(t * (K + 1) + K) * nq * 16 + r];
-    }
-    auto emit = [&](int t, int r, float v) {
-      const size_t o = static_cast<size_t>(t) * p.H + n0 + r;
-      if (p.y_f32)
-        static_cast<float*>(p.out)[o] = v;
-      else
-        static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
     };
-    RNB_TRACE_MARK(p, 14);
+    for (int b0 = 0; b0 < n_du; b0 += kDownBatch) {
+      const int nb = n_du - b0 < kDownBatch ? n_du - b0 : kDownBatch;
+      const char* tile[kDownBatch];
+      int qq[kDownBatch], ncols[kDownBatch];
+      uint32_t ent[kDownBatch][kPMaxT];
+      uint64_t wv[kDownBatch][kPMaxT][4];
+#pragma unroll
+      for (int b = 0; b < kDownBatch; ++b) {
+        ncols[b] = 0;
+        if (b < nb) {
+          unit_of(b0 + b, tile[b], qq[b], ent[b], ncols[b]);
+#pragma unroll
+          for (int n = 0; n < kPMaxT; ++n)
+            if (n < ncols[b]) {
+              const uint2* src = hw + static_cast<size_t>(ent[b][n]) * I + qq[b] * 128 + lane * 4;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) wv[b][n][j] = xw_load(src + j);
+            }
+        }
+      }
+      // words that did not yet carry this call's epoch are polled again, all
+      // of them per round trip, until they do (bounded)
+      for (;;) {
+        bool all = true;
+#pragma unroll
+        for (int b = 0; b < kDownBatch; ++b)
+#pragma unroll
+          for (int n = 0; n < kPMaxT; ++n)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (n < ncols[b] && static_cast<uint32_t>(wv[b][n][j] >> 32) != epoch) {
+                all = false;
+                wv[b][n][j] = xw_load(hw + static_cast<size_t>(ent[b][n]) * I + qq[b] * 128 + lane * 4 + j);
+              }
+        if (__all_sync(0xffffffffu, all)) break;
+        if (gtimer() > deadline) {
+          timed_out = true;
+          break;  // results void; stale words are used as they are
+        }
+        __nanosleep(32);
+      }
+      float inv_l[kDownBatch][kPMaxT][2], gs_l[kDownBatch][kPMaxT][2];
+#pragma unroll
+      for (int b = 0; b < kDownBatch; ++b) {
+        uint32_t* frag = sHf + b * (T * 64);
+#pragma unroll
+        for (int n = 0; n < kPMaxT; ++n) {
+          inv_l[b][n][0] = inv_l[b][n][1] = gs_l[b][n][0] = gs_l[b][n][1] = 0.f;
+          if (n >= ncols[b]) continue;
+          // lane l: channels 128 qq + 4 l .. +3 of column n
+          float hv[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) hv[j] = __uint_as_float(static_cast<uint32_t>(wv[b][n][j]));
+          float m = fmaxf(fmaxf(fabsf(hv[0]), fabsf(hv[1])), fmaxf(fabsf(hv[2]), fabsf(hv[3])));
+#pragma unroll
+          for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          float sc, inv;
+          fp16_range_scale(m, sc, inv);
+          float part = 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __half hh = __float2half_rn(hv[j] * sc);
+            part += __half2float(hh);
+            const int r = ((lane & 15) << 2) + j;  // position within the 64-group
+            int cq, ii, hf;
+            pair_slot<BITS>(r, cq, ii, hf);
+            // 4-bit pairs 1 and 3 of a word meet codes times 16 (subnormal form)
+            const __half hs = (BITS == 4 && (ii & 1)) ? __hmul(hh, __float2half_rn(0.0625f)) : hh;
+            reinterpret_cast<__half*>(frag + n * 64 + (lane >> 4) * 32 + cq * 8 + ii)[hf] = hs;
+          }
+#pragma unroll
+          for (int o = 1; o < 16; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+          // lane 0 holds group 0's sum and scale, lane 16 group 1's
+          inv_l[b][n][0] = __shfl_sync(0xffffffffu, inv, 0);
+          inv_l[b][n][1] = __shfl_sync(0xffffffffu, inv, 16);
+          gs_l[b][n][0] = __shfl_sync(0xffffffffu, part, 0);
+          gs_l[b][n][1] = __shfl_sync(0xffffffffu, part, 16);
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int b = 0; b < kDownBatch; ++b) {
+        if (ncols[b] == 0) continue;
+        const uint32_t* frag = sHf + b * (T * 64);
+        const int nc = ncols[b];
+        const int colB = g < nc ? g : 0;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        tile2_mma<BITS>(
+            tile[b], g, c,
+            [&](int gi, uint32_t(&xb)[8]) {
+              const uint32_t* fr = frag + colB * 64 + gi * 32 + c * 8;
+              const uint4 u0 = reinterpret_cast<const uint4*>(fr)[0];
+              const uint4 u1 = reinterpret_cast<const uint4*>(fr)[1];
+              xb[0] = u0.x; xb[1] = u0.y; xb[2] = u0.z; xb[3] = u0.w;
+              xb[4] = u1.x; xb[5] = u1.y; xb[6] = u1.z; xb[7] = u1.w;
+            },
+            [&](int gi, int col) { return c == 0 ? gs_l[b][col][gi] : 0.f; },
+            [&](int gi, int col) { return c == 0 ? inv_l[b][col][gi] : 0.f; }, acc);
+        if (c == 0) {
+#pragma unroll
+          for (int n = 0; n < kPMaxT; ++n) {
+            if (n < nc) {
+              float* dst = sRedC + (static_cast<size_t>(ent[b][n]) * nq + qq[b]) * 16;
+              dst[g] = n == 0 ? acc[0] : acc[1];
+              dst[g + 8] = n == 0 ? acc[2] : acc[3];
+            }
+          }
+        }
+      }
+      __syncwarp();  // the fragments are read before the next batch overwrites them
+      if (b0 == 0) RNB_TRACE_MARK(p, 14);
+    }
+    RNB_TRACE_MARK(p, 15);
+    __syncthreads();
+    RNB_TRACE_MARK(p, 16);
+    // Ordered weighted sum per (token, row), four lanes per output: lane j
+    // of the four takes sources s = j, j + 4, ... (slot order; source K is the
+    // shared expert), each the sum of its quarters in order; then the four
+    // partial sums are added in a fixed tree.
+    float acc = 0.f;
+    if (tid < 64 * T) {
+      const int o = tid >> 2, jl = tid & 3, t = o >> 4, r = o & 15;
+      for (int s3 = jl; s3 <= K; s3 += 4) {
+        float wgt;
+        uint32_t qm;
+        if (s3 < K) {
+          if (!is_local(ms->inds[t][s3])) continue;
+          wgt = ms->scores[t][s3];
+          qm = (1u << nq) - 1u;
+        } else {
+          if (!sh_down) continue;
+          wgt = ms->sg[t];
+          qm = qmask;
+        }
+        const float* y = sRedC + static_cast<size_t>(t * (K + 1) + s3) * nq * 16 + r;
+        float ys = 0.f;
+        for (int q2 = 0; q2 < nq; ++q2)
+          if ((qm >> q2) & 1u) ys += y[q2 * 16];
+        acc = fmaf(wgt, ys, acc);
+      }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    RNB_TRACE_MARK(p, 19);
+    void* const out = p.out;
+    const bool y_f32 = p.y_f32 != 0;
+    auto emit = [&](int t, int r, float v) {
+      const size_t o = static_cast<size_t>(t) * H + n0 + r;
+      if (y_f32)
+        static_cast<float*>(out)[o] = v;
+      else
+        static_cast<__nv_bfloat16*>(out)[o] = __float2bfloat16_rn(v);
+    };
     if (EP) {
       float* stage = sRed;  // this tile's partials, [t][r]
-      if (tid < T * 16) stage[tid] = acc;
+      __syncthreads();
+      if (tid < 64 * T && (tid & 3) == 0) stage[tid >> 2] = acc;
       __syncthreads();
       ep_exchange_tile(p, n0, T, [&](int t, int r) { return stage[t * 16 + r]; }, emit);
-    } else if (tid < T * 16) {
-      emit(tid >> 4, tid & 15, acc);
+    } else if (tid < 64 * T && (tid & 3) == 0) {
+      emit(tid >> 6, (tid >> 2) & 15, acc);
     }
   }
+  RNB_TRACE_MARK(p, 17);
+  if (timed_out) atomicOr(p.ws.status, RNB_STATUS_TIMEOUT);
 
-  RNB_TRACE_MARK(p, 9);
-  // ---- exit: the last CTA out resets the counters
+  // ---- exit: the last CTA out advances the sequence word
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
-    const uint32_t prev = atomicAdd(exitc, 1u);
-    if (prev == static_cast<uint32_t>(NC - 1)) {
-      __threadfence();
-      atomicExch(bar1, 0u);
-      atomicExch(bar2, 0u);
-      atomicExch(exitc, 0u);
+    uint32_t* seq = p.ws.seq;
+    if (atomicAdd(seq + 1, 1u) == static_cast<uint32_t>(NC - 1)) {
+      seq[1] = 0u;
+      seq[0] = epoch;
       if (EP) p.ep_seq[0] += 1;  // every CTA's exchange is done
       __threadfence();
     }
@@ -1819,7 +1891,7 @@ size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 struct Layout {
   size_t xperm, xsum, xinv, logit, inds, scores, sgate, nact, rec, entries, h,
-      hmax, yws, ctr, status, total;
+      hmax, yws, ctr, status, xchg, total;
 };
 
 Layout make_layout(const rnb_moe_desc& d) {
@@ -1833,6 +1905,7 @@ Layout make_layout(const rnb_moe_desc& d) {
   };
   L.status = take(4);                // offset 0: rnb_moe_status reads it without a descriptor
   L.ctr = take(ws_counter_bytes(d));  // arrival counters, back to zero after every call
+  L.xchg = take(kXchgBytes);          // persistent kernel's exchange words (same offset in every layout)
   L.xperm = take(T * H * 2);
   L.xsum = take(T * G * 4);
   L.xinv = take(T * 4);
@@ -1869,6 +1942,9 @@ Ws bind(const Layout& L, void* ws) {
   w.yws = reinterpret_cast<float*>(b + L.yws);
   w.ctr = reinterpret_cast<uint32_t*>(b + L.ctr);
   w.status = reinterpret_cast<uint32_t*>(b + L.status);
+  w.seq = reinterpret_cast<uint32_t*>(b + L.status + kWsSeqOffset);
+  w.lw = reinterpret_cast<uint2*>(b + L.xchg);
+  w.hw = w.lw + kXchgLogitWords;
   return w;
 }
 
@@ -1957,7 +2033,7 @@ size_t persistent_static_smem() {
     cudaFuncAttributes fb;
     const bool ok = cudaFuncGetAttributes(&fa, k_decode<BITS, false>) == cudaSuccess &&
                     cudaFuncGetAttributes(&fb, k_decode<BITS, true>) == cudaSuccess;
-    return ok ? (fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes) : size_t(1024);
+    return ok ? (fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes) : size_t(2048);
   }();
   return bytes;
 }
@@ -1965,50 +2041,51 @@ size_t persistent_static_smem() {
 // Shared-memory plan of k_decode; false when the call does not fit it.
 template <int BITS>
 bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem) {
-  // Phase A computes the router dots of two tokens at once (tokens 0 and 1):
-  // more tokens take the decode chain, whatever the shared-memory plan allows.
-  if (p.mode != kModeBlock || p.T < 1 || p.T > 2 || p.H != 2048 || p.I != 512 || p.E_total > 256 ||
-      p.k > 8 || p.off < 0 || p.off + p.E > p.E_total)
+  if (p.mode != kModeBlock || p.T < 1 || p.T > kPMaxT || p.H != 2048 || p.I != 512 || p.E_total > 256 ||
+      p.k > kPMaxK || p.off < 0 || p.off + p.E > p.E_total)
     return false;
-  pl.n_rtiles = (p.E_total + 1 + 15) / 16;
-  if (di.sms < p.H / 16 || di.sms < pl.n_rtiles + p.I / 8) return false;
-  if (2 * di.sms < p.E_total + 1) return false;  // each CTA computes at most two router rows
+  const int NC = di.sms;
+  // roles: H/16 CTAs own 16 output rows, the first I/8 CTAs a shared-expert
+  // gate/up task, every CTA at most two router rows, and no CTA more than
+  // kPMaxMine routed gate/up tasks
+  if (NC < p.H / 16 || NC < p.I / 8 || 2 * NC < p.E_total + 1) return false;
+  const int n_act_max = p.T * p.k < p.E ? p.T * p.k : p.E;
+  const int mine_max = (n_act_max * (p.I / 8) + NC - 1) / NC;
+  if (mine_max > kPMaxMine) return false;
   using TL = Tile2<BITS>;
   const int T = p.T, G = p.H / kGroup, nq = p.I / 128;
-  const int n_ctask = nq * (1 + (p.T * p.k < p.E ? p.T * p.k : p.E));
   size_t o = 0;
   auto take = [&](size_t bytes) {
     const size_t at = o;
     o = (o + bytes + 127) & ~static_cast<size_t>(127);
     return static_cast<uint32_t>(at);
   };
-  pl.off_xn = p.norm_w ? take(static_cast<size_t>(T) * p.H * 2) : 0u;
+  pl.off_sdn = take(static_cast<size_t>(nq) * TL::kBytes);
   pl.off_x = take(static_cast<size_t>(T) * G * 32 * 4);
   pl.off_xs = take(static_cast<size_t>(T) * G * 4);
-  pl.off_misc = take(sizeof(PMisc));
+  pl.off_xn = p.norm_w ? take(static_cast<size_t>(T) * p.H * 2) : 0u;
+  pl.off_ivl = take(static_cast<size_t>(T) * (p.E_total + 1) * 4);
+  pl.off_red = take(static_cast<size_t>(1 + mine_max) * kPWarps * 32 * 4);
+  pl.off_hf = take(std::max<size_t>(static_cast<size_t>(kPWarps) * kDownBatch * T * 64 * 4, 4096));  // also xprep's scratch
   pl.off_redc = take(static_cast<size_t>(T) * (p.k + 1) * nq * 16 * 4);
-  pl.cb = (n_ctask + kPWarps - 1) / kPWarps;  // phase-C tasks per warp, staged at once
-  if (pl.cb > 4) pl.cb = 4;
-  const size_t hbytes = static_cast<size_t>(kPWarps) * pl.cb * T * (128 + p.I / 8) * 4;
-  const size_t lbytes = static_cast<size_t>(T) * (p.E_total + 1) * 4;
-  const size_t xbytes = 2048 * 2;
-  size_t hb = hbytes > lbytes ? hbytes : lbytes;
-  hb = hb > xbytes ? hb : xbytes;
-  pl.off_h = take(hb);
-  pl.off_cr = take(static_cast<size_t>(n_ctask) * TL::kBytes);
-  const size_t task = static_cast<size_t>(kPWarps) * TL::kBytes;
-  const size_t red1 = static_cast<size_t>(kPWarps) * 128 * 4;  // partial sums of one task
+  pl.off_misc = take(sizeof(PMisc));
   const size_t limit = static_cast<size_t>(di.smem_optin) - persistent_static_smem<BITS>();
-  for (pl.db = 4; pl.db >= 1; --pl.db) {
-    if (o + pl.db * (task + red1) + 256 <= limit) break;
-  }
-  if (pl.db < 1) return false;
-  pl.off_red = take(pl.db * red1);
-  pl.off_br = take(pl.db * task);
+  if (o + 256 > limit) return false;
+  const size_t per_slot = static_cast<size_t>(kPWarps) * TL::kBytes;
+  pl.S = static_cast<int>((limit - o - 256) / per_slot);
+  if (pl.S > 8) pl.S = 8;
+  // every warp's down units must all be in flight once its gate/up units are
+  // consumed: a slot each, plus the shared gate/up slice's
+  const int max_down = (nq * n_act_max + kPWarps - 1) / kPWarps;
+  if (pl.S < 2 || pl.S < 1 + max_down) return false;
+  pl.off_ring = take(pl.S * per_slot);
   smem = o;
   return smem <= limit;
 }
 
+// One launch with programmatic stream serialisation: the kernel's prologue
+// (weights only) may start while the previous kernel on the stream drains;
+// its griddepcontrol.wait holds everything else back.
 template <int BITS>
 int run_persistent(Params& p, const PPlan& pl, size_t smem, int nc, cudaStream_t st) {
   auto kern = p.ep_world > 1 ? k_decode<BITS, true> : k_decode<BITS, false>;
@@ -2020,8 +2097,8 @@ int run_persistent(Params& p, const PPlan& pl, size_t smem, int nc, cudaStream_t
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   stage_begin(st);
@@ -2104,6 +2181,7 @@ Params base_params(const rnb_moe_desc* d, const void* x, void* ws, int mode) {
   p.ws = bind(make_layout(*d), ws);
   p.shared_qmask = (1u << (d->I / 128)) - 1u;
   p.ep_world = 1;
+  p.ep_limit_ns = kEpSpinLimitNs;
   p.y_f32 = (mode == kModeBlock && (d->flags & RNB_FLAG_Y_F32)) ? 1 : 0;
   return p;
 }
@@ -2497,6 +2575,7 @@ int rnb_moe_noalloc_status(uint32_t* status, void* stream) {
 
 struct rnb_ep {
   int rank = 0, world = 1, H = 0, dev = 0;
+  uint64_t wait_ns = rnb::kEpSpinLimitNs;
   size_t recv_bytes = 0, bytes = 0;
   void* local = nullptr;
   uint2* recv[rnb::kMaxEpRanks] = {};
@@ -2577,6 +2656,14 @@ int rnb_ep_connect(rnb_ep* ep, const void* handles) {
   return RNB_OK;
 }
 
+int rnb_ep_set_wait_limit_ms(rnb_ep* ep, int ms) {
+  using namespace rnb;
+  if (!ep) return fail(RNB_ERR_INVALID, "rnb_ep_set_wait_limit_ms: ep is NULL");
+  if (ms < 1 || ms > 600000) return fail(RNB_ERR_INVALID, "rnb_ep_set_wait_limit_ms: ms must be in [1, 600000]");
+  ep->wait_ns = static_cast<uint64_t>(ms) * 1000000ull;
+  return RNB_OK;
+}
+
 int rnb_ep_destroy(rnb_ep* ep) {
   if (!ep) return RNB_OK;
   for (int q = 0; q < ep->world; ++q)
@@ -2606,6 +2693,7 @@ int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* x, void*
   auto set_ep = [&](Params& p) {
     p.ep_world = ep->world;
     p.ep_rank = ep->rank;
+    p.ep_limit_ns = ep->wait_ns;
     for (int q = 0; q < ep->world; ++q) {
       p.ep_recv[q] = ep->recv[q];
     }
@@ -2700,6 +2788,7 @@ int rnb_moe_block_norm_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* resid,
       for (int q = ep->rank; q < nq; q += ep->world) p.shared_qmask |= 1u << q;
       p.ep_world = ep->world;
       p.ep_rank = ep->rank;
+      p.ep_limit_ns = ep->wait_ns;
       for (int q = 0; q < ep->world; ++q) p.ep_recv[q] = ep->recv[q];
       p.ep_seq = ep->seq;
     }

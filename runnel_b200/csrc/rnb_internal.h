@@ -29,6 +29,19 @@ DevInfo dev_info();
 constexpr size_t kWsCountersOffset = 256;
 inline size_t ws_counter_bytes(const rnb_moe_desc& d) { return 4u * (4u + static_cast<size_t>(d.H) / 16u); }
 
+// The first 256-byte slot holds, besides the status word (offset 0), the
+// persistent decode kernel's call sequence word (offset 64) and exit counter
+// (offset 68); neither is ever cleared by a call or by rnb_moe_status.
+constexpr size_t kWsSeqOffset = 64;
+
+// After the counters, both layouts reserve the persistent decode kernel's
+// exchange words: 8-byte {value, epoch} words that only that kernel writes
+// (an epoch is a sequence number, so no other path may leave data there):
+// router logits [2 tokens][257 rows] and SwiGLU rows [2 tokens][9 slots][512].
+constexpr size_t kXchgLogitWords = 2 * 257;
+constexpr size_t kXchgHWords = 2 * 9 * 512;
+constexpr size_t kXchgBytes = 8 * (kXchgLogitWords + kXchgHWords);
+
 // Stage timing (rnb_timing.cu): no-ops unless rnb_stage_timing(1) was called.
 void stage_begin(cudaStream_t st);
 void stage_end(cudaStream_t st, int stage);

@@ -1024,6 +1024,7 @@ Layout make_layout(const rnb_moe_desc& d) {
   };
   L.status = take(4);
   take(ws_counter_bytes(d));  // the decode kernels' arrival counters: never touched here
+  take(kXchgBytes);           // the persistent decode kernel's exchange words: never touched here
   L.counts = take(E1 * 4);
   L.fill = take(E1 * 4);
   L.base = take(E1 * 4);

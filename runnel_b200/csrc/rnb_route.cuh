@@ -79,6 +79,22 @@ __device__ __forceinline__ uint32_t route_interval(float L, float xn2, float xin
   return lo | (hi << 16);
 }
 
+// Packed candidate interval of a logit accumulated in fp64 from bf16 inputs:
+// every product is exact and each of the at most ~12 roundings of a partial
+// sum (per-lane chain, shuffle tree, cross-warp tree) errs by at most 2^-53 of
+// sum |x_i w_i|, so B = 2^-40 * (norm bound) covers the error with a wide
+// margin and the interval is nearly always a single bf16 value (no fp64
+// recompute needed).  Norms as for route_interval.
+__device__ __forceinline__ uint32_t route_interval_f64(double L, float xn2, float xinf, float wn2, float wn1) {
+  float nb = xinf * wn1;
+  if (xn2 >= 0x1p-100f && wn2 >= 0x1p-100f) nb = fminf(nb, sqrtf(xn2) * sqrtf(wn2));
+  const double B = 0x1p-40 * 1.001 * static_cast<double>(nb);
+  if (!(B <= 3.0e38) || L != L) return 0xFF80u | (0x7F80u << 16);  // (-inf, +inf): recompute
+  const uint32_t lo = f64_to_bf16_bits(L - B);
+  const uint32_t hi = f64_to_bf16_bits(L + B);
+  return lo | (hi << 16);
+}
+
 // Per-lane partial norms of a router tile in the mma.sync m16n8k16 layout:
 // lane 4g+c sees, per 32-wide chunk, 8 activations of token g and 8 weights
 // of each of the tile rows g and g+8.

@@ -84,6 +84,13 @@ class ExpertParallel:
             self._ep = None
             raise
 
+    def set_wait_limit_ms(self, ms: int) -> None:
+        """How long a call waits for the other ranks before it gives up and
+        sets RNB_STATUS_TIMEOUT (default 2000 ms)."""
+        if not self._ep:
+            raise RuntimeError("ExpertParallel context is closed")
+        _lib.call("rnb_ep_set_wait_limit_ms", self._ep, int(ms))
+
     def close(self) -> None:
         """Release the buffers (after a host barrier on every rank)."""
         if self._ep:

@@ -135,6 +135,32 @@ def make_block(bits: int, seed: int, T: int = 1, H: int = 2048, I: int = 512, E:
         sdn_s=sdn[1], sdn_b=sdn[2], norm_w=norm_w, meta=meta)
 
 
+def _make_block_args(args):
+    bits, seed, kw = args
+    return make_block(bits, seed=seed, **kw)
+
+
+def make_blocks(bits: int, seeds, workers: int | None = None, **kw) -> list[SyntheticBlock]:
+    """:func:`make_block` for several seeds, in spawned worker processes (so
+    it may run after CUDA is initialised); identical to calling it in turn."""
+    import concurrent.futures
+    import multiprocessing
+    import os
+
+    seeds = list(seeds)
+    if len(seeds) <= 1:
+        return [make_block(bits, seed=s, **kw) for s in seeds]
+    n = workers or min(len(seeds), max(1, (os.cpu_count() or 1) // 2), 16)
+    ctx = multiprocessing.get_context("spawn")
+    with concurrent.futures.ProcessPoolExecutor(max_workers=n, mp_context=ctx) as pool:
+        return list(pool.map(_make_block_args, [(bits, s, kw) for s in seeds]))
+
+
+def stack_layer_seed(seed: int, layer: int) -> int:
+    """Seed of layer ``layer`` of configuration 4's stack (``seed`` = 3)."""
+    return seed * 1000 + layer
+
+
 def make_tokens(seed: int, T: int, H: int = 2048) -> np.ndarray:
     """Extra bf16 activations ``[T,H]`` from an independent stream."""
     rng = np.random.default_rng([seed, 2])

@@ -93,6 +93,29 @@ def reference_add_rmsnorm(x_bits: np.ndarray, y_bits: np.ndarray | None, w_bits:
     return xo, xn
 
 
+def canonical_layers(L: int, bits: int, seed: int, device, E_range: tuple[int, int] | None = None,
+                     on_block=None) -> tuple[list[BlockTensors], list[torch.Tensor]]:
+    """The stack of benchmark configuration 4 from the canonical generator:
+    layer l is ``inputs.make_block(bits, seed=inputs.stack_layer_seed(seed, l))``
+    (numpy PCG64, the distributions of runnel_b200.inputs) with its RMSNorm
+    weight ``norm_w`` rounded to bf16.  Layers are generated eight at a time
+    in worker processes and uploaded; ``on_block(l, block)`` sees each host
+    block before it is dropped.  With E_range only that expert shard of each
+    layer is uploaded."""
+    from . import inputs
+    from .quant import f32_to_bf16_bits
+
+    layers, norms = [], []
+    for l0 in range(0, L, 8):
+        seeds = [inputs.stack_layer_seed(seed, l) for l in range(l0, min(L, l0 + 8))]
+        for i, b in enumerate(inputs.make_blocks(bits, seeds, T=1)):
+            layers.append(BlockTensors.from_numpy(b, device, E_range=E_range))
+            norms.append(torch.from_numpy(f32_to_bf16_bits(b.norm_w).view(np.int16)).view(torch.bfloat16).to(device))
+            if on_block is not None:
+                on_block(l0 + i, b)
+    return layers, norms
+
+
 def synthetic_layers(L: int, bits: int, seed: int, device, E_range: tuple[int, int] | None = None,
                      H: int = 2048, I: int = 512, E: int = 256) -> tuple[list[BlockTensors], list[torch.Tensor]]:
     """L distinct blocks generated on the device from a seeded torch generator

@@ -135,3 +135,66 @@ def test_two_rank_expert_parallel_decode():
     import torch.multiprocessing as mp
 
     mp.spawn(_rank_main, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _idle_rank(conn):
+    """Rank 1 of a two-rank context that never makes a block call: it makes
+    its receive buffer, hands over its handle and waits to be told to exit
+    (no kernel of its own ever runs)."""
+    import ctypes
+
+    import torch
+
+    from runnel_b200 import _lib
+
+    torch.cuda.set_device(0)
+    ep = ctypes.c_void_p()
+    buf = (ctypes.c_char * _lib.EP_HANDLE_BYTES)()
+    _lib.call("rnb_ep_create", 1, 2, 2048, ctypes.byref(ep), buf)
+    conn.send(bytes(buf))
+    conn.recv()
+    _lib.load().rnb_ep_destroy(ep)
+
+
+def test_peer_that_never_calls_times_out_then_a_fresh_context_is_correct():
+    """A two-rank expert-parallel call whose second rank never calls: the
+    bounded wait for its words (lowered to 50 ms) runs out, the call returns
+    with RNB_STATUS_TIMEOUT, and a fresh context computes correctly again.
+    The missing rank is a host process that never launches (no GPU fault)."""
+    import multiprocessing
+
+    ctx = multiprocessing.get_context("spawn")
+    parent, child = ctx.Pipe()
+    proc = ctx.Process(target=_idle_rank, args=(child,))
+    proc.start()
+    dev = torch.device("cuda", 0)
+    blk = inputs.make_block(BITS, seed=SEED, T=2)
+    x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).to(dev)
+    try:
+        assert parent.poll(180), "the idle rank did not start"
+        h1 = parent.recv()
+        ctx2 = ep.ExpertParallel(0, 2, handles_fn=lambda h: [h, h1])
+        try:
+            ctx2.set_wait_limit_ms(50)
+            shard = ep.shard_tensors(blk, 0, 2, dev)
+            ws = ops.Workspace(dev)
+            for T in (1, 2):  # the persistent kernel (T <= 2) and again on the same context
+                ctx2.moe_block(shard, x[:T], ws=ws)
+                torch.cuda.synchronize()
+                assert ws.status() & _lib.STATUS_TIMEOUT
+        finally:
+            ctx2.close()
+    finally:
+        parent.send(1)
+        proc.join(60)
+    one = ep.ExpertParallel(0, 1, handles_fn=lambda h: [h])
+    try:
+        bt = ep.shard_tensors(blk, 0, 1, dev)
+        ws = ops.Workspace(dev)
+        out = one.moe_block(bt, x, ws=ws)
+        torch.cuda.synchronize()
+        assert ws.status() == 0
+        ref, _, _, bound = _ref(blk, 2)
+        assert_close(out.float().cpu().numpy(), ref, "fresh context after a timeout", bound=bound)
+    finally:
+        one.close()

@@ -74,6 +74,14 @@ def test_host_entry_point_chunked_copies(T):
     assert bc.ws.status() == 0
 
 
+@pytest.mark.parametrize("skew", [None, "adversarial"])
+def test_config5_T16384_sampled(skew):
+    """Benchmark configuration 5 at its size: q8, 16384 tokens, seed 4, the
+    uniform and the adversarial step (a quarter of the tokens forced onto one
+    expert); 64 tokens sampled for the oracle."""
+    _run(8, seed=4, T=16384, skew=skew, sample=64)
+
+
 def test_prefill_adversarial_routing_sampled():
     """A quarter of the tokens all route to one expert (many 128-row tiles of one expert)."""
     blk, bt, x, out, _ = _run(8, seed=4, T=1024, skew="adversarial", sample=32)

@@ -125,3 +125,46 @@ def test_fused_layer_glue_is_bit_identical(T):
         ops.moe_block(layers[l], xn, ws=ws, out=y)
         stack.add_rmsnorm(xa, y, norms[l + 1] if l + 1 < L else norms[l], xa, xn)
     assert torch.equal(_dev(_bits(fused)), _dev(_bits(xa)))
+
+
+def test_config4_forty_layers_eight_tokens_against_oracle():
+    """Benchmark configuration 4 as benchmarked: the 40 canonical q4 layers
+    (inputs.make_block(4, seed=3000 + l)) and 8 sequential batch-1 tokens,
+    each token's input the previous token's output.  Every layer's block is
+    checked against the oracle on the GPU's own input, and every glue step
+    against numpy, so error growth over the 40 residual layers is covered."""
+    L, bits, seed, ntok = 40, 4, 3, 8
+    layers, norms = stack.canonical_layers(L, bits, seed, DEV)
+    st = stack.LayerStack(layers, norms, ws=ops.Workspace(DEV))
+    norms_bits = [_bits(n) for n in norms]
+    x = _dev(inputs.make_tokens(seed, 1))
+    xn_in = np.zeros((L, ntok, 2048), np.uint16)
+    y_out = np.zeros((L, ntok, 2048), np.float32)
+    for tok in range(ntok):
+        rec = []
+        out = st.forward(x, record=rec)
+        prev = _bits(x)
+        for l, (xa, xn, y) in enumerate(rec):
+            if l == 0:
+                rxa, rxn = stack.reference_add_rmsnorm(prev, None, norms_bits[0])
+            else:
+                rxa, rxn = stack.reference_add_rmsnorm(_bits(rec[l - 1][0]), _bits(rec[l - 1][2]), norms_bits[l])
+            np.testing.assert_array_equal(_bits(xa), rxa)
+            assert _ulp_steps(_bits(xn), rxn).max() <= 1
+            xn_in[l, tok] = _bits(xn)[0]
+            y_out[l, tok] = y.float().cpu().numpy()[0]
+        last = stack.reference_add_rmsnorm(_bits(rec[-1][0]), _bits(rec[-1][2]), norms_bits[-1])[0]
+        np.testing.assert_array_equal(_bits(out), last)
+        x = out
+    del layers, st
+    torch.cuda.empty_cache()
+    worst = 0.0
+    for l0 in range(0, L, 8):
+        seeds = [inputs.stack_layer_seed(seed, l) for l in range(l0, min(L, l0 + 8))]
+        for i, b in enumerate(inputs.make_blocks(bits, seeds, T=1)):
+            l = l0 + i
+            w = oracle.BlockWeights(bits=bits, group=64, **b.weight_fields())
+            ref, _, _, bound = oracle_block(w, xn_in[l])
+            s = assert_close(y_out[l], ref, f"config 4 layer {l}, {ntok} tokens", bound=bound)
+            worst = max(worst, s["max_tol_ratio"])
+    print(f"config 4: worst max_tol_ratio over 40 layers x {ntok} tokens = {worst:.3f}")
