@@ -183,7 +183,7 @@ def cpu_baseline(bits, T, budget_s=10.0, seed=1):
             break
     cores = os.cpu_count() or 1
     return {"value": el / (n * T) * 1e6, "unit": "us/token", "cores": cores, "kind": "port",
-            "sample": f"{n} block calls of T={T} tokens, q{bits} (CPU oracle, C + OpenMP, fp32)"}
+            "sample": f"{n} block calls of T={T} tokens, q{bits} (the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP, fp32 -- a checker, not an optimised CPU implementation)"}
 
 
 def run_reference(args, cfg=None):
@@ -192,12 +192,11 @@ def run_reference(args, cfg=None):
         return
     if cfg is not None:
         return run_reference_prefill(args, cfg)
-    bits, T = 4, args.tokens
-    times = []
+    bits, T = args.bits, args.tokens
     from oracle import oracle
     from runnel_b200 import inputs
 
-    blk = inputs.make_block(bits, seed=1, T=T)
+    blk = inputs.make_block(bits, seed=args.seed, T=T)
     w = oracle.BlockWeights(bits=bits, group=64, **blk.weight_fields())
     for _ in range(args.warmup):
         oracle.moe_block(w, blk.x, k=8)
@@ -212,9 +211,9 @@ def run_reference(args, cfg=None):
         "unit": "us/token", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"config2 q4 decode T={T}", "bits": bits, "tokens_per_step": T},
+        "config": {"workload": f"config{args.config} q{bits} decode T={T}", "bits": bits, "tokens_per_step": T},
         "cpu_baseline": {"value": us_tok, "unit": "us/token", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} block calls of T={T} (CPU oracle, C + OpenMP)"},
+                         "sample": f"{args.steps} block calls of T={T} (the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP -- a checker, not an optimised CPU implementation)"},
         "e2e": {"value": us_tok, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -254,7 +253,9 @@ def run_reference_stack(args, cfg, n_layers=4):
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"config4 {L} q{bits} layers, batch-1 sequential decode", "bits": bits, "layers": L},
         "cpu_baseline": {"value": us_tok, "unit": "us/token", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} tokens through {n_layers} layers, scaled by {L}/{n_layers}"},
+                         "sample": f"{args.steps} tokens through {n_layers} layers, scaled by {L}/{n_layers} "
+                                   "(the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP -- a checker, "
+                                   "not an optimised CPU implementation)"},
         "e2e": {"value": us_tok, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -286,7 +287,9 @@ def run_reference_prefill(args, cfg, sample_T=16):
         "config": {"workload": f"config{args.config} q{bits} prefill T={cfg['T']}", "bits": bits,
                    "tokens_per_step": sample_T, "routing": routing},
         "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} oracle calls of the first {sample_T} tokens of each batch"},
+                         "sample": f"{args.steps} oracle calls of the first {sample_T} tokens of each batch "
+                                   "(the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP -- a checker, "
+                                   "not an optimised CPU implementation)"},
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -345,7 +348,7 @@ def cpu_baseline_prefill(blocks, bits, sample_T=32, budget_s=10.0):
             break
     return {"value": n * sample_T / el, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
             "sample": f"{n} oracle block calls of {sample_T} tokens (first tokens of the workload's batches), "
-                      f"q{bits}, C + OpenMP fp32"}
+                      f"q{bits}; the exact-order CPU oracle (C, -O2 -ffp-contract=off, OpenMP, fp32), not an optimised CPU implementation"}
 
 
 def prefill_blocks(cfg, bits, seed):
@@ -682,8 +685,8 @@ def cpu_baseline_stack(layers, norms, bits, x0, n_layers=4, budget_s=10.0):
             break
     L = len(layers)
     return {"value": el / n * 1e6 * L / n_layers, "unit": "us/token", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": f"{n} tokens through the first {n_layers} of {L} layers (CPU oracle, C + OpenMP fp32), "
-                      f"scaled by {L}/{n_layers}"}
+            "sample": f"{n} tokens through the first {n_layers} of {L} layers (the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP, fp32; "
+                      f"not an optimised CPU implementation), scaled by {L}/{n_layers}"}
 
 
 def run_ours(args):

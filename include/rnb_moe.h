@@ -85,6 +85,20 @@ typedef struct rnb_moe_desc {
   const uint32_t* sdn_w; /* [H, I*bits/32] */
   const uint16_t* sdn_s; /* [H, I/64] */
   const uint16_t* sdn_b;
+  /* 8-bit router (real Ornith checkpoints keep mlp.gate and
+   * mlp.shared_expert_gate as 8-bit MLX affine, group 64).  router_bits 0 or
+   * 16: router_w [E_total, H] and shared_gate_w [H] are bf16.  router_bits 8:
+   * router_w points at uint32 codes [E_total, H/4] and shared_gate_w at codes
+   * [H/4], with bf16 scales and biases per 64 inputs in router_s / router_b
+   * [E_total, H/64] and sgate_s / sgate_b [H/64]; a logit is then the
+   * correctly rounded bf16 of the exact dot product with the dequantised row
+   * s * code + b. */
+  int32_t router_bits;
+  int32_t reserved0;
+  const uint16_t* router_s;
+  const uint16_t* router_b;
+  const uint16_t* sgate_s;
+  const uint16_t* sgate_b;
 } rnb_moe_desc;
 
 /* rnb_moe_desc.flags */

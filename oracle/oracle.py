@@ -38,6 +38,9 @@ class _Block(ctypes.Structure):
         ("dn_w", _u32p), ("dn_s", _u16p), ("dn_b", _u16p),
         ("sgu_w", _u32p), ("sgu_s", _u16p), ("sgu_b", _u16p),
         ("sdn_w", _u32p), ("sdn_s", _u16p), ("sdn_b", _u16p),
+        ("router_bits", ctypes.c_int),
+        ("router_q", _u32p), ("router_s", _u16p), ("router_b", _u16p),
+        ("sgate_q", _u32p), ("sgate_s", _u16p), ("sgate_b", _u16p),
     ]
 
 
@@ -114,6 +117,16 @@ class BlockWeights:
     sdn_w: np.ndarray | None = None  # [H,I*bits/32]
     sdn_s: np.ndarray | None = None
     sdn_b: np.ndarray | None = None
+    # 8-bit affine router and shared gate (router_bits=8): codes [E,H/4] /
+    # [H/4], bf16 scales and biases [E,H/64] / [H/64]; router_w and
+    # shared_gate_w are then unused
+    router_bits: int = 16
+    router_q: np.ndarray | None = None
+    router_s: np.ndarray | None = None
+    router_b: np.ndarray | None = None
+    sgate_q: np.ndarray | None = None
+    sgate_s: np.ndarray | None = None
+    sgate_b: np.ndarray | None = None
 
     @property
     def E(self) -> int:
@@ -134,15 +147,17 @@ def _block_struct(w: BlockWeights, x: np.ndarray, k: int, keep: list) -> _Block:
     T = x.shape[0]
     arrays = {}
     for name in ("router_w", "gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b", "shared_gate_w",
-                 "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b"):
+                 "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b",
+                 "router_q", "router_s", "router_b", "sgate_q", "sgate_s", "sgate_b"):
         a = getattr(w, name)
         if a is not None:
             a = np.ascontiguousarray(a)
             keep.append(a)
         arrays[name] = a
-    u32 = {"gu_w", "dn_w", "sgu_w", "sdn_w"}
+    u32 = {"gu_w", "dn_w", "sgu_w", "sdn_w", "router_q", "sgate_q"}
     kw = {n: _p(a, _u32p if n in u32 else _u16p) for n, a in arrays.items()}
-    return _Block(T=T, H=w.H, I=w.I, E=w.E, k=k, bits=w.bits, group=w.group, x=_p(x, _u16p), **kw)
+    return _Block(T=T, H=w.H, I=w.I, E=w.E, k=k, bits=w.bits, group=w.group, x=_p(x, _u16p),
+                  router_bits=w.router_bits, **kw)
 
 
 def router(w: BlockWeights, x: np.ndarray, k: int = 8, nthreads: int | None = None):

@@ -182,10 +182,38 @@ typedef struct rnbo_block {
   const uint32_t* sdn_w; /* [H,I*bits/32] */
   const uint16_t* sdn_s;
   const uint16_t* sdn_b;
+  /* 8-bit affine router and shared gate (router_bits == 8; real Ornith
+   * checkpoints store mlp.gate and mlp.shared_expert_gate so): codes
+   * [E,H/4] / [H/4] in router_q / sgate_q, bf16 scales and biases per 64
+   * inputs.  router_bits 0 or 16: the bf16 router_w / shared_gate_w above. */
+  int router_bits;
+  const uint32_t* router_q;
+  const uint16_t* router_s; /* [E,H/64] */
+  const uint16_t* router_b;
+  const uint32_t* sgate_q; /* [H/4] */
+  const uint16_t* sgate_s; /* [H/64] */
+  const uint16_t* sgate_b;
 } rnbo_block;
+
+/* Router weight (row e; e == E is the shared gate) at input h, exact in
+ * double: bf16, or the 8-bit affine scale * code + bias (a bf16 times an
+ * 8-bit integer plus a bf16 is exact in double). */
+static double router_weight(const rnbo_block* d, int e, int h) {
+  const int H = d->H, shared = e == d->E;
+  if (d->router_bits == 8) {
+    const uint32_t* q = shared ? d->sgate_q : d->router_q + (size_t)e * (H / 4);
+    const uint16_t* sc = shared ? d->sgate_s : d->router_s + (size_t)e * (H / 64);
+    const uint16_t* bi = shared ? d->sgate_b : d->router_b + (size_t)e * (H / 64);
+    const double code = (double)((q[h / 4] >> (8 * (h % 4))) & 0xFFu);
+    return (double)rnbo_bf16_to_f32(sc[h / 64]) * code + (double)rnbo_bf16_to_f32(bi[h / 64]);
+  }
+  const uint16_t* w = shared ? d->shared_gate_w : d->router_w + (size_t)e * H;
+  return (double)rnbo_bf16_to_f32(w[h]);
+}
 
 static int block_valid(const rnbo_block* d) {
   if (!d || d->T < 0 || d->H <= 0 || d->I <= 0 || d->E <= 0 || d->k <= 0 || d->k > d->E) return 0;
+  if (d->router_bits == 8 && (!d->router_q || !d->router_s || !d->router_b || d->H % 64)) return 0;
   if ((d->bits != 4 && d->bits != 8) || d->group <= 0) return 0;
   if (d->H % d->group || d->I % d->group) return 0;
   return 1;
@@ -215,8 +243,7 @@ int rnbo_router(const rnbo_block* d, float* logits, int32_t* inds, float* scores
          * 2048 of them is far below bf16 resolution: the logit is the
          * correctly rounded bf16 of the exact dot product */
         double acc = 0.0;
-        const uint16_t* wr = d->router_w + (size_t)e * H;
-        for (int h = 0; h < H; ++h) acc += (double)xf[h] * (double)rnbo_bf16_to_f32(wr[h]);
+        for (int h = 0; h < H; ++h) acc += (double)xf[h] * router_weight(d, e, h);
         lg[e] = rnbo_f64_to_bf16_f32(acc);
         if (logits) logits[(size_t)t * E + e] = lg[e];
       }
@@ -241,9 +268,10 @@ int rnbo_router(const rnbo_block* d, float* logits, int32_t* inds, float* scores
       }
       for (int s = 0; s < K; ++s) scores[(size_t)t * K + s] = sel_p[s] / sel_sum;
       if (shared_gate) {
-        if (d->shared_gate_w) {
+        if (d->router_bits == 8 ? d->sgate_q != NULL : d->shared_gate_w != NULL) {
+          /* fp32, the dequantised weight rounded to fp32 (exact for bf16) */
           float acc = 0.0f;
-          for (int h = 0; h < H; ++h) acc += xf[h] * rnbo_bf16_to_f32(d->shared_gate_w[h]);
+          for (int h = 0; h < H; ++h) acc += xf[h] * (float)router_weight(d, E, h);
           shared_gate[t] = 1.0f / (1.0f + expf(-acc));
         } else {
           shared_gate[t] = 0.0f;
@@ -439,7 +467,7 @@ int rnbo_block_bound(const rnbo_block* d, const int32_t* inds, const float* scor
       if (sg && d->sgu_w) {
         expert_bound(H, I, bits, G, d->sgu_w, d->sgu_s, d->sgu_b, d->sdn_w, d->sdn_s, d->sdn_b, xd, h, dh, y, eb);
         double a = 0.0;
-        for (int k = 0; k < H; ++k) a += fabs(xd[k] * (double)rnbo_bf16_to_f32(d->shared_gate_w[k]));
+        for (int k = 0; k < H; ++k) a += fabs(xd[k] * router_weight(d, d->E, k));
         const double g = fabs((double)sg[t]);
         const double dsg = g * (1.0 - g) * gH * a + 2.0 * u * g;
         for (int n = 0; n < H; ++n) {

@@ -48,6 +48,8 @@ class RnbMoeDesc(ctypes.Structure):
         ("router_w", _vp), ("shared_gate_w", _vp),
         ("sgu_w", _vp), ("sgu_s", _vp), ("sgu_b", _vp),
         ("sdn_w", _vp), ("sdn_s", _vp), ("sdn_b", _vp),
+        ("router_bits", ctypes.c_int32), ("reserved0", ctypes.c_int32),
+        ("router_s", _vp), ("router_b", _vp), ("sgate_s", _vp), ("sgate_b", _vp),
     ]
 
 

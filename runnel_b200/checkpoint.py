@@ -16,8 +16,9 @@ Three pieces, following the reference's tooling:
   (router, routed experts, shared expert and its gate) from a checkpoint
   layer, by the mlx-lm Qwen3.5 MoE names.  Real checkpoints quantize the
   router and the shared-expert gate to 8 bits (80 per-tensor overrides,
-  reference tests/test_checkpoint.py:149-152); the B200 block takes them as
-  bf16, so they are dequantised (s*q + b in fp32, rounded to bf16) at load.
+  reference tests/test_checkpoint.py:149-152); the block takes them as they
+  are stored (router_bits 8: codes, scales and biases), and the arrays also
+  carry a bf16 dequantisation (s*q + b in fp32, rounded) for plain-torch use.
 """
 from __future__ import annotations
 
@@ -272,14 +273,31 @@ def _dense_bf16(store: TensorStore, base: str, K: int) -> np.ndarray:
     return _dequant_bf16(w, s, b, bits)
 
 
+def _affine8(store: TensorStore, base: str, K: int):
+    """(codes, scales, biases) of an 8-bit affine Linear, else None."""
+    w, _ = store.read(f"{base}.weight")
+    if w.dtype != np.uint32 or _bits_of(w.shape[-1], K) != 8:
+        return None
+    return w, store.read(f"{base}.scales")[0], store.read(f"{base}.biases")[0]
+
+
 def load_block_arrays(store: TensorStore, layer: int) -> dict:
-    """numpy arrays of a layer's whole MoE block (fields of SyntheticBlock)."""
+    """numpy arrays of a layer's whole MoE block (fields of SyntheticBlock).
+
+    An 8-bit router and shared gate come as stored (router_bits 8, router_q /
+    router_s / router_b, sgate_q / sgate_s / sgate_b) and, in router_w /
+    shared_gate_w, as their bf16 dequantisation."""
     routed, _ = read_routed(store, layer)
     bits = routed["bits"]
     H = routed["dn_w"].shape[1]
     p = layer_prefix(layer)
     out = dict(routed)
     out["router_w"] = _dense_bf16(store, f"{p}.gate", H)
+    out["router_bits"] = 16
+    q8 = _affine8(store, f"{p}.gate", H)
+    if q8 is not None:
+        out["router_bits"] = 8
+        out["router_q"], out["router_s"], out["router_b"] = q8
     sh = f"{p}.shared_expert"
     if f"{sh}.up_proj.weight" in store:
         parts = {}
@@ -294,6 +312,11 @@ def load_block_arrays(store: TensorStore, layer: int) -> dict:
         out["sgu_b"] = np.concatenate((parts[("up", "biases")], parts[("gate", "biases")]), axis=0)
         out["sdn_w"], out["sdn_s"], out["sdn_b"] = (parts[("down", p2)] for p2 in ("weight", "scales", "biases"))
         out["shared_gate_w"] = _dense_bf16(store, f"{p}.shared_expert_gate", H).reshape(-1)
+        g8 = _affine8(store, f"{p}.shared_expert_gate", H)
+        if (g8 is not None) != (q8 is not None):
+            raise ValueError("the router and the shared-expert gate must both be 8-bit, or both not")
+        if g8 is not None:
+            out["sgate_q"], out["sgate_s"], out["sgate_b"] = (v.reshape(-1) for v in g8)
     norm = f"language_model.model.layers.{layer}.post_attention_layernorm.weight"
     if norm in store:
         out["norm_w"] = store.read(norm)[0]
@@ -314,12 +337,21 @@ def load_block(store: TensorStore, layer: int, device="cuda", E_range: tuple[int
         t = t.view(torch.uint32) if arr.dtype == np.uint32 else (t.view(torch.bfloat16) if bf16 else t)
         return t.to(device)
 
+    q8 = a["router_bits"] == 8
     bt = BlockTensors(bits=a["bits"], gu_w=up(a["gu_w"][lo:hi]), gu_s=up(a["gu_s"][lo:hi], True),
                       gu_b=up(a["gu_b"][lo:hi], True), dn_w=up(a["dn_w"][lo:hi]), dn_s=up(a["dn_s"][lo:hi], True),
-                      dn_b=up(a["dn_b"][lo:hi], True), router_w=up(a["router_w"], True),
+                      dn_b=up(a["dn_b"][lo:hi], True),
+                      router_w=up(a["router_q"]) if q8 else up(a["router_w"], True),
                       E_total=a["gu_w"].shape[0], expert_offset=lo)
+    if q8:
+        bt.router_bits = 8
+        bt.router_s, bt.router_b = up(a["router_s"], True), up(a["router_b"], True)
     if "sgu_w" in a:
-        bt.shared_gate_w = up(a["shared_gate_w"], True)
+        if q8:
+            bt.shared_gate_w = up(a["sgate_q"])
+            bt.sgate_s, bt.sgate_b = up(a["sgate_s"], True), up(a["sgate_b"], True)
+        else:
+            bt.shared_gate_w = up(a["shared_gate_w"], True)
         bt.sgu_w, bt.sdn_w = up(a["sgu_w"]), up(a["sdn_w"])
         bt.sgu_s, bt.sgu_b = up(a["sgu_s"], True), up(a["sgu_b"], True)
         bt.sdn_s, bt.sdn_b = up(a["sdn_s"], True), up(a["sdn_b"], True)

@@ -75,8 +75,10 @@ struct Params {
   int router_ctas;
   const uint16_t* x;
   const uint32_t* inds_in;
-  const uint16_t* router_w;
-  const uint16_t* sgate_w;
+  const uint16_t* router_w;  // bf16 [E_total][H], or (router_q8) uint32 codes [E_total][H/4]
+  const uint16_t* sgate_w;   // bf16 [H], or (router_q8) uint32 codes [H/4]
+  int router_q8;             // 8-bit affine router and shared gate
+  const uint16_t *router_s, *router_b, *sgate_s, *sgate_b;  // [E_total][H/64], [H/64] bf16
   const uint32_t *gu_w, *dn_w, *sgu_w, *sdn_w;
   const uint16_t *gu_s, *gu_b, *dn_s, *dn_b, *sgu_s, *sgu_b, *sdn_s, *sdn_b;
   void* out;  // bf16 [T][H] (block) or [T][k][H] (switchglu)
@@ -108,6 +110,23 @@ struct Params {
   uint16_t* xn_out;
 };
 
+// The router rows for the exact fp64 recompute of uncertain logits.
+__device__ __forceinline__ RouterSrc router_src(const Params& p) {
+  RouterSrc r;
+  r.w = p.router_q8 ? nullptr : p.router_w;
+  r.q = p.router_q8 ? reinterpret_cast<const uint32_t*>(p.router_w) : nullptr;
+  r.s = p.router_s;
+  r.b = p.router_b;
+  return r;
+}
+
+// Dequantised 8-bit router weights, exactly: w = s * code + b for the four
+// codes of `word` (inputs 4j .. 4j+3 of a 64-group with scale s, bias b).
+__device__ __forceinline__ void q8_router_quad(uint32_t word, double s, double b, double (&w)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) w[j] = fma(s, static_cast<double>((word >> (8 * j)) & 0xFFu), b);
+}
+
 // Optional phase timeline (compile with -DRNB_TRACE): thread 0 of each CTA
 // records %globaltimer at phase boundaries into the per-slot output area of
 // the workspace, which the persistent kernel does not otherwise use.
@@ -134,7 +153,8 @@ __device__ __forceinline__ void trace_value(const Params& p, int i, int v) {
 // (E_total+1)-row matrix whose last row is the shared-expert gate.  Warp w
 // owns hidden range [w*H/16, (w+1)*H/16) in 32-wide chunks.
 struct RouterRegs {
-  uint4 a[4][2];  // up to 4 chunks (H <= 2048) x rows g, g+8
+  uint4 a[4][2];  // up to 4 chunks (H <= 2048) x rows g, g+8: bf16 rows, or (8-bit
+                  // router) .x,.y the 8 codes and .z the packed bf16 scale | bias << 16
 };
 
 __device__ __forceinline__ const uint16_t* router_row(const Params& p, int r) {
@@ -146,15 +166,62 @@ __device__ __forceinline__ const uint16_t* router_row(const Params& p, int r) {
 __device__ __forceinline__ void router_load(const Params& p, int tile, int warp, int lane, RouterRegs& rr) {
   const int g = lane >> 2, c = lane & 3;
   const int nch = p.H / (kRouterWarps * 32);
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  if (p.router_q8) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = tile * 16 + g + 8 * h;
+      const bool sh = r == p.E_total && p.has_shared;
+      const bool ok = r < p.E_total || sh;
+      const uint32_t* q = sh ? reinterpret_cast<const uint32_t*>(p.sgate_w)
+                             : reinterpret_cast<const uint32_t*>(p.router_w) + static_cast<size_t>(r) * (p.H / 4);
+      const uint16_t* sc = sh ? p.sgate_s : p.router_s + static_cast<size_t>(r) * (p.H / 64);
+      const uint16_t* bi = sh ? p.sgate_b : p.router_b + static_cast<size_t>(r) * (p.H / 64);
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        const int k0 = (warp * nch + ch) * 32 + 8 * c;
+        if (ch < nch && ok) {
+          const uint2 w = __ldg(reinterpret_cast<const uint2*>(q + k0 / 4));
+          rr.a[ch][h] = make_uint4(w.x, w.y, static_cast<uint32_t>(__ldg(sc + k0 / 64)) |
+                                                 (static_cast<uint32_t>(__ldg(bi + k0 / 64)) << 16), 0u);
+        } else {
+          rr.a[ch][h] = z;
+        }
+      }
+    }
+    return;
+  }
   const uint16_t* pa = router_row(p, tile * 16 + g);
   const uint16_t* pb = router_row(p, tile * 16 + g + 8);
-  const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
   for (int ch = 0; ch < 4; ++ch) {
     const int k0 = (warp * nch + ch) * 32 + 8 * c;
     rr.a[ch][0] = (ch < nch && pa) ? ld_stream_v4(pa + k0) : z;
     rr.a[ch][1] = (ch < nch && pb) ? ld_stream_v4(pb + k0) : z;
   }
+}
+
+// The 8 dequantised weights of an 8-bit router chunk (RouterRegs form) as
+// two bf16 parts, w = hi + lo + r with |r| <= 2^-16.9 |w|: s * code is exact
+// in fp32 (a bf16 times an 8-bit integer), adding b rounds once (2^-24), and
+// hi = bf16(w32), lo = bf16(w32 - hi) (the difference is exact).
+__device__ __forceinline__ void q8_router_split(const uint4 v, uint4& hi, uint4& lo) {
+  const float s = __uint_as_float(v.z << 16), b = __uint_as_float(v.z & 0xFFFF0000u);
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t word = j < 2 ? v.x : v.y;
+    const int sh = 16 * (j & 1);
+    const float w0 = fmaf(s, static_cast<float>((word >> sh) & 0xFFu), b);
+    const float w1 = fmaf(s, static_cast<float>((word >> (sh + 8)) & 0xFFu), b);
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(w0, w1);
+    const float2 hf = __bfloat1622float2(hh);
+    const __nv_bfloat162 ll = __floats2bfloat162_rn(w0 - hf.x, w1 - hf.y);
+    h[j] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[j] = *reinterpret_cast<const uint32_t*>(&ll);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 __device__ void router_cta(const Params& p, int tile, const RouterRegs& rr) {
@@ -174,9 +241,17 @@ __device__ void router_cta(const Params& p, int tile, const RouterRegs& rr) {
       if (ch < nch) {
         const int k0 = (warp * nch + ch) * 32 + 8 * c;
         const uint4 bx = tb < p.T ? __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(tb) * p.H + k0)) : z;
-        mma_bf16(d, rr.a[ch][0].x, rr.a[ch][1].x, rr.a[ch][0].y, rr.a[ch][1].y, bx.x, bx.y);
-        mma_bf16(d, rr.a[ch][0].z, rr.a[ch][1].z, rr.a[ch][0].w, rr.a[ch][1].w, bx.z, bx.w);
-        rn.add(bx, rr.a[ch][0], rr.a[ch][1]);
+        uint4 a0 = rr.a[ch][0], a1 = rr.a[ch][1];
+        if (p.router_q8) {
+          uint4 l0, l1;
+          q8_router_split(rr.a[ch][0], a0, l0);
+          q8_router_split(rr.a[ch][1], a1, l1);
+          mma_bf16(d, l0.x, l1.x, l0.y, l1.y, bx.x, bx.y);
+          mma_bf16(d, l0.z, l1.z, l0.w, l1.w, bx.z, bx.w);
+        }
+        mma_bf16(d, a0.x, a1.x, a0.y, a1.y, bx.x, bx.y);
+        mma_bf16(d, a0.z, a1.z, a0.w, a1.w, bx.z, bx.w);
+        rn.add(bx, a0, a1);
       }
     }
     rn.reduce_quad();
@@ -194,8 +269,12 @@ __device__ void router_cta(const Params& p, int tile, const RouterRegs& rr) {
 #pragma unroll
         for (int w = 0; w < kRouterWarps; ++w) acc += red[w][r][n];
         // expert rows: candidate interval of the bf16 logit; last row: fp32 shared-gate logit
+        // (8-bit router: twice the MMA steps, the hi + lo split's residual
+        // and norms taken from hi -- a wider allowance)
         reinterpret_cast<uint32_t*>(p.ws.logit)[static_cast<size_t>(t) * rows + row] =
-            row < p.E_total ? router_interval_from(&s_norm[0][0], kRouterWarps, r, n, acc) : __float_as_uint(acc);
+            row < p.E_total ? router_interval_from(&s_norm[0][0], kRouterWarps, r, n, acc,
+                                                   p.router_q8 ? kRouteRelQ8 : kRouteRelDecode)
+                            : __float_as_uint(acc);
       }
     }
     __syncthreads();
@@ -280,7 +359,7 @@ __device__ void route_finalize(const Params& p) {
         float sc;
         // a caller asking for the logits gets every one resolved exactly
         warp_route_token(reinterpret_cast<const uint32_t*>(s_lg[warp]), p.E_total, K,
-                         p.x + static_cast<size_t>(t) * p.H, p.router_w, p.H, lane, p.logits_out != nullptr,
+                         p.x + static_cast<size_t>(t) * p.H, router_src(p), p.H, lane, p.logits_out != nullptr,
                          p.logits_out ? p.logits_out + static_cast<size_t>(t) * p.E_total : nullptr, &e, &sc);
         if (lane < K) {
           p.ws.inds[t * K + lane] = static_cast<uint32_t>(e);
@@ -1304,15 +1383,27 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   // ---- prologue: weights only (before the programmatic-launch wait)
   RNB_TRACE_MARK(p, 0);
   // Router rows of this CTA: cta and cta + NC of the Et + 1 rows (the last is
-  // the shared gate); warp w covers hidden [128 w, 128 w + 128), 4 values per lane.
+  // the shared gate); warp w covers hidden [128 w, 128 w + 128), 4 values per
+  // lane: 4 bf16, or (8-bit router) the word of 4 codes in .x and the group's
+  // bf16 scale | bias << 16 in .y.
   const int k0r = warp * 128 + lane * 4;
   uint2 wr[2];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int row = cta + i * NC;
-    const uint16_t* pr = row < Et ? p.router_w + static_cast<size_t>(row) * H
-                                  : (row == Et && has_shared ? p.sgate_w : nullptr);
-    wr[i] = pr ? __ldg(reinterpret_cast<const uint2*>(pr + k0r)) : make_uint2(0, 0);
+    const bool sh = row == Et && has_shared;
+    if (p.router_q8) {
+      const uint32_t* q = sh ? reinterpret_cast<const uint32_t*>(p.sgate_w)
+                             : reinterpret_cast<const uint32_t*>(p.router_w) + static_cast<size_t>(row) * (H / 4);
+      const uint16_t* sc = sh ? p.sgate_s : p.router_s + static_cast<size_t>(row) * (H / 64);
+      const uint16_t* bi = sh ? p.sgate_b : p.router_b + static_cast<size_t>(row) * (H / 64);
+      wr[i] = row < Et || sh ? make_uint2(__ldg(q + k0r / 4), static_cast<uint32_t>(__ldg(sc + k0r / 64)) |
+                                                                 (static_cast<uint32_t>(__ldg(bi + k0r / 64)) << 16))
+                             : make_uint2(0, 0);
+    } else {
+      const uint16_t* pr = row < Et ? p.router_w + static_cast<size_t>(row) * H : (sh ? p.sgate_w : nullptr);
+      wr[i] = pr ? __ldg(reinterpret_cast<const uint2*>(pr + k0r)) : make_uint2(0, 0);
+    }
   }
   if (owns_sgu)
     tile2_issue<BITS>(ring, p.sgu_w, p.sgu_s, p.sgu_b, gwrow, gsrow, warp * 2, gu_row(sg_task * 8), lane);
@@ -1377,10 +1468,11 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
 
   // ---- router: rows cta, cta + NC against tokens 0, 1
   {
-    // Dots in fp64: bf16 products are exact and the fp64 partial sums err by
-    // at most ~2^-49 of sum |x_i w_i|, so the bf16 rounding of each logit is
-    // certified (route_interval_f64) without an fp64 recompute in routing.
-    // Norms (for the certificate's bound) in fp32.
+    // Dots in fp64: bf16 products (and 8-bit dequantised weights s * code + b
+    // and their products) are exact or within 2^-53, and the fp64 partial sums
+    // err by at most ~2^-49 of sum |x_i w_i|, so the bf16 rounding of each
+    // logit is certified (route_interval_f64) without an fp64 recompute in
+    // routing.  Norms (for the certificate's bound) in fp32.
     float xf[2][4];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
@@ -1394,14 +1486,24 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     float v[8];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const float wf[4] = {__uint_as_float(wr[i].x << 16), __uint_as_float(wr[i].x & 0xFFFF0000u),
-                           __uint_as_float(wr[i].y << 16), __uint_as_float(wr[i].y & 0xFFFF0000u)};
+      double wd[4];
+      if (p.router_q8) {
+        q8_router_quad(wr[i].x, static_cast<double>(__uint_as_float(wr[i].y << 16)),
+                       static_cast<double>(__uint_as_float(wr[i].y & 0xFFFF0000u)), wd);
+      } else {
+        wd[0] = __uint_as_float(wr[i].x << 16);
+        wd[1] = __uint_as_float(wr[i].x & 0xFFFF0000u);
+        wd[2] = __uint_as_float(wr[i].y << 16);
+        wd[3] = __uint_as_float(wr[i].y & 0xFFFF0000u);
+      }
+      const float wf[4] = {static_cast<float>(wd[0]), static_cast<float>(wd[1]), static_cast<float>(wd[2]),
+                           static_cast<float>(wd[3])};
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
-        double d = static_cast<double>(wf[0]) * static_cast<double>(xf[t][0]);
-        d = fma(static_cast<double>(wf[1]), static_cast<double>(xf[t][1]), d);
-        d = fma(static_cast<double>(wf[2]), static_cast<double>(xf[t][2]), d);
-        d = fma(static_cast<double>(wf[3]), static_cast<double>(xf[t][3]), d);
+        double d = wd[0] * static_cast<double>(xf[t][0]);
+        d = fma(wd[1], static_cast<double>(xf[t][1]), d);
+        d = fma(wd[2], static_cast<double>(xf[t][2]), d);
+        d = fma(wd[3], static_cast<double>(xf[t][3]), d);
         dv[2 * i + t] = d;
       }
       v[i] = fmaf(wf[0], wf[0], fmaf(wf[1], wf[1], fmaf(wf[2], wf[2], wf[3] * wf[3])));
@@ -1506,7 +1608,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     const int t = warp;
     int e;
     float sc;
-    const int nre = warp_route_token_body(sIvl + t * (Et + 1), Et, K, xin + static_cast<size_t>(t) * H, p.router_w, H,
+    const int nre = warp_route_token_body(sIvl + t * (Et + 1), Et, K, xin + static_cast<size_t>(t) * H, router_src(p), H,
                                           lane, false, nullptr, &e, &sc);
 #ifdef RNB_TRACE
     if (t == 0 && lane == 0) trace_value(p, 31, nre);
@@ -1721,7 +1823,13 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       }
       // words that did not yet carry this call's epoch are polled again, all
       // of them per round trip, until they do (bounded)
+#ifdef RNB_TRACE
+      int polls = 0;
+#endif
       for (;;) {
+#ifdef RNB_TRACE
+        ++polls;
+#endif
         bool all = true;
 #pragma unroll
         for (int b = 0; b < kDownBatch; ++b)
@@ -1740,6 +1848,12 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
         }
         __nanosleep(32);
       }
+#ifdef RNB_TRACE
+      if (b0 == 0) {
+        RNB_TRACE_MARK(p, 23);
+        if (tid == 0) trace_value(p, 30, polls);
+      }
+#endif
       float inv_l[kDownBatch][kPMaxT][2], gs_l[kDownBatch][kPMaxT][2];
 #pragma unroll
       for (int b = 0; b < kDownBatch; ++b) {
@@ -1971,9 +2085,19 @@ int validate(const rnb_moe_desc* d, bool need_router, bool need_bank) {
       if (!aligned16(q)) return fail(RNB_ERR_ALIGN, "routed expert tensors must be 16-byte aligned");
     }
   }
+  if (d->router_bits != 0 && d->router_bits != 16 && d->router_bits != 8)
+    return fail(RNB_ERR_INVALID, "router_bits must be 0, 16 or 8");
   if (need_router) {
     if (!d->router_w) return fail(RNB_ERR_INVALID, "router_w must be non-NULL");
     if (!aligned16(d->router_w)) return fail(RNB_ERR_ALIGN, "router_w must be 16-byte aligned");
+    if (d->router_bits == 8) {
+      if (!d->router_s || !d->router_b)
+        return fail(RNB_ERR_INVALID, "an 8-bit router needs router_s and router_b");
+      if (d->shared_gate_w && !(d->flags & RNB_FLAG_NO_SHARED) && (!d->sgate_s || !d->sgate_b))
+        return fail(RNB_ERR_INVALID, "an 8-bit shared gate needs sgate_s and sgate_b");
+      if (d->shared_gate_w && !aligned16(d->shared_gate_w))
+        return fail(RNB_ERR_ALIGN, "shared_gate_w must be 16-byte aligned");
+    }
   }
   return RNB_OK;
 }
@@ -2166,6 +2290,11 @@ Params base_params(const rnb_moe_desc* d, const void* x, void* ws, int mode) {
   p.x = static_cast<const uint16_t*>(x);
   p.router_w = d->router_w;
   p.sgate_w = d->shared_gate_w;
+  p.router_q8 = d->router_bits == 8 ? 1 : 0;
+  p.router_s = d->router_s;
+  p.router_b = d->router_b;
+  p.sgate_s = d->sgate_s;
+  p.sgate_b = d->sgate_b;
   p.gu_w = d->gu_w;
   p.gu_s = d->gu_s;
   p.gu_b = d->gu_b;

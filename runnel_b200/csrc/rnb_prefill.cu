@@ -75,14 +75,19 @@ struct Ws {
   __half* y16;       // [rows_cap][H] down outputs times their weight, fp16, one scale per (row, n-tile)
   float* yinv;       // [rows_cap][H/128] inverse of that scale
   uint32_t* rowpos;  // [T][K+1] sorted row of entry t*(K+1)+slot, 0xFFFFFFFF if none
+  uint16_t* rhi;     // 8-bit router: [E_total+1][H] bf16 high parts of the dequantised rows
+  uint16_t* rlo;     //   (the last row the shared gate) and [E_total+1][H] low parts
 };
 
 struct Params {
   int T, H, I, E, E_total, off, k, has_shared, y_f32;
   int rows_cap, max_mt;
   const uint16_t* x;
-  const uint16_t* router_w;
-  const uint16_t* sgate_w;
+  const uint16_t* router_w;  // bf16 router rows (8-bit router: ws.rhi)
+  const uint16_t* sgate_w;   // bf16 shared-gate row (8-bit router: row E_total of ws.rhi)
+  int router_q8;             // 8-bit affine router: codes, scales and biases below
+  const uint32_t *router_q, *sgate_q;
+  const uint16_t *router_s, *router_b, *sgate_s, *sgate_b;
   const uint32_t *gu_w, *dn_w, *sgu_w, *sdn_w;
   const uint16_t *gu_s, *gu_b, *dn_s, *dn_b, *sgu_s, *sgu_b, *sdn_s, *sdn_b;
   void* out;  // bf16 [T][H], or fp32 with y_f32
@@ -254,6 +259,40 @@ __global__ void __launch_bounds__(512) k_qmm_prep(Params p) {
 //             absolute values; rows spread over the token tiles);
 //   warps 4-7 one token per thread (one TMEM lane each): the 128 fp32 logits.
 // k_pre_select turns the logits into candidate intervals and routes.
+// 8-bit router: a warp per row of the router (and the shared gate) writes the
+// dequantised weights w = fp32(s * code + b) as two bf16 parts, hi = bf16(w)
+// and lo = bf16(w - hi), so the router GEMM runs on bf16 tensor cores over
+// hi and then lo (|w - hi - lo| <= 2^-17.9 |w|; kRouteRelQ8 covers it).
+__global__ void __launch_bounds__(512) k_router_split(Params p) {
+  const int lane = threadIdx.x & 31, row = blockIdx.x * 16 + (threadIdx.x >> 5);
+  const int H = p.H, Et = p.E_total;
+  if (row > Et || (row == Et && !p.has_shared)) return;
+  const uint32_t* q = row < Et ? p.router_q + static_cast<size_t>(row) * (H / 4) : p.sgate_q;
+  const uint16_t* sc = row < Et ? p.router_s + static_cast<size_t>(row) * (H / 64) : p.sgate_s;
+  const uint16_t* bi = row < Et ? p.router_b + static_cast<size_t>(row) * (H / 64) : p.sgate_b;
+  uint4* hi = reinterpret_cast<uint4*>(p.ws.rhi + static_cast<size_t>(row) * H);
+  uint4* lo = reinterpret_cast<uint4*>(p.ws.rlo + static_cast<size_t>(row) * H);
+  for (int c = lane; c < H / 8; c += 32) {
+    const uint2 w = __ldg(reinterpret_cast<const uint2*>(q) + c);
+    const float s = bf16_bits_to_f32(__ldg(sc + c / 8)), b = bf16_bits_to_f32(__ldg(bi + c / 8));
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t word = j < 2 ? w.x : w.y;
+      const int sh = 16 * (j & 1);
+      const float w0 = fmaf(s, static_cast<float>((word >> sh) & 0xFFu), b);
+      const float w1 = fmaf(s, static_cast<float>((word >> (sh + 8)) & 0xFFu), b);
+      const __nv_bfloat162 hh = __floats2bfloat162_rn(w0, w1);
+      const float2 hf = __bfloat1622float2(hh);
+      const __nv_bfloat162 ll = __floats2bfloat162_rn(w0 - hf.x, w1 - hf.y);
+      h[j] = *reinterpret_cast<const uint32_t*>(&hh);
+      l[j] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+    hi[c] = make_uint4(h[0], h[1], h[2], h[3]);
+    lo[c] = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
 constexpr int kRgStages = 6;
 constexpr int kRgTile = 128 * 128;                    // 128 rows x 64 bf16
 constexpr int kRgStage = 2 * kRgTile;                 // x tile + router tile
@@ -261,7 +300,7 @@ constexpr size_t kRgSmem = static_cast<size_t>(kRgStages) * kRgStage + 1024;
 static_assert(kRgStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 
 struct RouteMaps {
-  CUtensorMap x, w;
+  CUtensorMap x, w, wl;  // wl: the low parts of an 8-bit router (unused otherwise)
 };
 
 __global__ void __launch_bounds__(256, 1) k_route_gemm(Params p, const __grid_constant__ RouteMaps tm) {
@@ -272,6 +311,8 @@ __global__ void __launch_bounds__(256, 1) k_route_gemm(Params p, const __grid_co
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * 128, e0 = blockIdx.y * 128;
   const int H = p.H, Et = p.E_total, nks = H / 64, qk = nks / 4;
+  // an 8-bit router runs the K range twice: high parts, then low parts
+  const int nsteps = p.router_q8 ? 2 * nks : nks;
   if (tid == 0) {
     for (int s = 0; s < kRgStages; ++s) {
       mbar_init(&full[s], 1);
@@ -288,34 +329,34 @@ __global__ void __launch_bounds__(256, 1) k_route_gemm(Params p, const __grid_co
   bool timed_out = false;
   if (warp == 0) {
     if (lane == 0) {
-      for (int ks = 0; ks < nks; ++ks) {
-        const int s = ks % kRgStages, n = ks / kRgStages;
+      for (int ks = 0; ks < nsteps; ++ks) {
+        const int s = ks % kRgStages, n = ks / kRgStages, kk = ks % nks;
         if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, kWaitNs)) {
           timed_out = true;
           break;
         }
         const uint32_t bar = smem_u32(&full[s]);
         mbar_arrive_expect_tx(&full[s], kRgStage);
-        tma_load_2d(smem_u32(sm + s * kRgStage), &tm.x, ks * 64, t0, bar);
-        tma_load_2d(smem_u32(sm + s * kRgStage + kRgTile), &tm.w, ks * 64, e0, bar);
+        tma_load_2d(smem_u32(sm + s * kRgStage), &tm.x, kk * 64, t0, bar);
+        tma_load_2d(smem_u32(sm + s * kRgStage + kRgTile), ks < nks ? &tm.w : &tm.wl, kk * 64, e0, bar);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(128, 128, true);
-      for (int ks = 0; ks < nks; ++ks) {
-        const int s = ks % kRgStages, n = ks / kRgStages;
+      for (int ks = 0; ks < nsteps; ++ks) {
+        const int s = ks % kRgStages, n = ks / kRgStages, kk = ks % nks;
         if (!mbar_wait(&full[s], n & 1, kWaitNs)) {
           timed_out = true;
           break;
         }
         tc_fence_after();
         const uint32_t a0 = smem_u32(sm + s * kRgStage), b0 = a0 + kRgTile;
-        const uint32_t d = taddr + static_cast<uint32_t>(ks / qk) * 128u;
+        const uint32_t d = taddr + static_cast<uint32_t>(kk / qk) * 128u;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_f16(d, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(b0 + k * 32), idesc,
-                   (ks % qk == 0 && k == 0) ? 0u : 1u);
+                   (ks < nks && kk % qk == 0 && k == 0) ? 0u : 1u);
         umma_commit(smem_u32(&empty[s]));
       }
       umma_commit(smem_u32(&mdone));  // also when the loop ended early: every issued MMA done
@@ -403,21 +444,27 @@ __global__ void __launch_bounds__(512, 2) k_pre_select(Params p) {
     const size_t tg = static_cast<size_t>(t);
     const uint4* xr = reinterpret_cast<const uint4*>(p.x + tg * H);
     const uint4* gr = reinterpret_cast<const uint4*>(p.sgate_w);
+    // 8-bit shared gate: the high parts above, the low parts here
+    const uint4* grl = p.router_q8 ? reinterpret_cast<const uint4*>(p.ws.rlo + static_cast<size_t>(Et) * H) : nullptr;
     uint4 xv[kSelMaxH / 256];
     float xn2 = 0.f, xinf = 0.f, sgl = 0.f;
 #pragma unroll
     for (int q = 0; q < kSelMaxH / 256; ++q) {
       if (q < nq) {
         xv[q] = __ldg(xr + q * 32 + lane);
-        uint4 gw = make_uint4(0u, 0u, 0u, 0u);
-        if (p.has_shared) gw = __ldg(gr + q * 32 + lane);
-        const uint32_t w[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w}, g[4] = {gw.x, gw.y, gw.z, gw.w};
+        uint4 gw = make_uint4(0u, 0u, 0u, 0u), gl = gw;
+        if (p.has_shared) gw = __ldcg(gr + q * 32 + lane);
+        if (p.has_shared && grl) gl = __ldcg(grl + q * 32 + lane);
+        const uint32_t w[4] = {xv[q].x, xv[q].y, xv[q].z, xv[q].w}, g[4] = {gw.x, gw.y, gw.z, gw.w},
+                       gq[4] = {gl.x, gl.y, gl.z, gl.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xFFFF0000u);
           xn2 = fmaf(lo, lo, fmaf(hi, hi, xn2));
           xinf = fmaxf(xinf, fmaxf(fabsf(lo), fabsf(hi)));
-          sgl = fmaf(lo, __uint_as_float(g[j] << 16), fmaf(hi, __uint_as_float(g[j] & 0xFFFF0000u), sgl));
+          const float g0 = __uint_as_float(g[j] << 16) + __uint_as_float(gq[j] << 16);
+          const float g1 = __uint_as_float(g[j] & 0xFFFF0000u) + __uint_as_float(gq[j] & 0xFFFF0000u);
+          sgl = fmaf(lo, g0, fmaf(hi, g1, sgl));
         }
       }
     }
@@ -457,12 +504,18 @@ __global__ void __launch_bounds__(512, 2) k_pre_select(Params p) {
 #pragma unroll
     for (int i = 0; i < kMaxE / 32; ++i) {
       const int e = lane + 32 * i;
-      if (e < Et) s_ivl[warp][e] = route_interval(lv[i], xn2, xinf, w2[i], w1[i], kRouteRelTc);
+      if (e < Et)
+        s_ivl[warp][e] = route_interval(lv[i], xn2, xinf, w2[i], w1[i], p.router_q8 ? kRouteRelQ8 : kRouteRelTc);
     }
     __syncwarp();
     int e;
     float sc;
-    warp_route_token(s_ivl[warp], Et, K, p.x + tg * H, p.router_w, H, lane, false, nullptr, &e, &sc);
+    RouterSrc rs;
+    rs.w = p.router_q8 ? nullptr : p.router_w;
+    rs.q = p.router_q8 ? p.router_q : nullptr;
+    rs.s = p.router_s;
+    rs.b = p.router_b;
+    warp_route_token(s_ivl[warp], Et, K, p.x + tg * H, rs, H, lane, false, nullptr, &e, &sc);
     if (lane < K) {
       p.ws.inds[tg * K + lane] = static_cast<uint32_t>(e);
       p.ws.scores[tg * K + lane] = sc;
@@ -1004,7 +1057,7 @@ size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 struct Layout {
   size_t status, counts, fill, base, n_mt, tiles, perm, inds, scores, sg, xscale, x16, xs16, h16, hinv, hrow, lg, wn, y16, yinv,
-      rowpos, total;
+      rowpos, rhi, rlo, total;
   int rows_cap, max_mt;
 };
 
@@ -1045,6 +1098,9 @@ Layout make_layout(const rnb_moe_desc& d) {
   L.y16 = take(static_cast<size_t>(L.rows_cap) * d.H * 2);
   L.yinv = take(static_cast<size_t>(L.rows_cap) * (d.H / 128) * 4);
   L.rowpos = take(T * (K + 1) * 4);
+  const size_t rsplit = d.router_bits == 8 ? static_cast<size_t>(d.E_total + 1) * d.H * 2 : 0;
+  L.rhi = take(rsplit);
+  L.rlo = take(rsplit);
   L.total = o;
   return L;
 }
@@ -1159,8 +1215,12 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
     if (!encode_2d(&rm.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.x, p.H, static_cast<uint64_t>(p.T),
                    static_cast<uint64_t>(p.H) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&rm.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.router_w, p.H, static_cast<uint64_t>(p.E_total),
-                   static_cast<uint64_t>(p.H) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+                   static_cast<uint64_t>(p.H) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&rm.wl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.router_q8 ? p.ws.rlo : p.router_w, p.H,
+                   static_cast<uint64_t>(p.E_total), static_cast<uint64_t>(p.H) * 2, 64, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
       return fail(RNB_ERR_CUDA, "prefill: router tensor map encoding failed");
+    if (p.router_q8) k_router_split<<<(p.E_total + 1 + 15) / 16, 512, 0, st>>>(p);
     const dim3 rg((p.T + 127) / 128, (p.E_total + 127) / 128);
     k_route_gemm<<<rg, 256, kRgSmem, st>>>(p, rm);
     k_pre_select<<<(p.T + 15) / 16, 512, 0, st>>>(p);
@@ -1208,6 +1268,20 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
   p.x = static_cast<const uint16_t*>(x);
   p.router_w = d->router_w;
   p.sgate_w = d->shared_gate_w;
+  if (d->router_bits == 8) {
+    // the router GEMM, the norms and the shared gate read the split rows
+    // (the workspace's rhi / rlo); the exact recompute reads the codes
+    char* wsb = static_cast<char*>(ws);
+    p.router_q8 = 1;
+    p.router_q = reinterpret_cast<const uint32_t*>(d->router_w);
+    p.sgate_q = reinterpret_cast<const uint32_t*>(d->shared_gate_w);
+    p.router_s = d->router_s;
+    p.router_b = d->router_b;
+    p.sgate_s = d->sgate_s;
+    p.sgate_b = d->sgate_b;
+    p.router_w = reinterpret_cast<const uint16_t*>(wsb + L.rhi);
+    p.sgate_w = p.router_w + static_cast<size_t>(d->E_total) * d->H;
+  }
   p.gu_w = d->gu_w;
   p.gu_s = d->gu_s;
   p.gu_b = d->gu_b;
@@ -1246,6 +1320,8 @@ int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_
   p.ws.y16 = reinterpret_cast<__half*>(b + L.y16);
   p.ws.yinv = reinterpret_cast<float*>(b + L.yinv);
   p.ws.rowpos = reinterpret_cast<uint32_t*>(b + L.rowpos);
+  p.ws.rhi = reinterpret_cast<uint16_t*>(b + L.rhi);
+  p.ws.rlo = reinterpret_cast<uint16_t*>(b + L.rlo);
   return d->bits == 8 ? launch_prefill<8>(p, L, st) : launch_prefill<4>(p, L, st);
 }
 

@@ -62,6 +62,11 @@ __device__ __forceinline__ uint16_t f64_to_bf16_bits(double v) {
 // sum's rounding to fp32 is the 2^-21 |L| term of the bound).
 constexpr float kRouteRelDecode = 0x1p-18f;
 constexpr float kRouteRelTc = 0x1p-18f;
+// 8-bit affine routers on the tensor cores: each dequantised weight w
+// (fp32 s*code + b, one rounding) runs as two bf16 parts hi + lo, which leave
+// a residual of at most 2^-17.9 |w|; the MMA steps double (hi and lo), and
+// the norms come from hi (|w| <= (1 + 2^-8) |hi|).  2^-16 covers the sum.
+constexpr float kRouteRelQ8 = 0x1p-16f;
 
 // Packed candidate interval (lo | hi << 16) of an fp32 logit L with error
 // allowance rel * sum |x_i w_i|.  Norms of the token (xn2 = sum x^2, xinf =
@@ -142,7 +147,8 @@ struct RouterNorms {
 };
 
 // Interval of tile row r (0..15), token n (0..7) from nw warps' partials.
-__device__ __forceinline__ uint32_t router_interval_from(const float* part, int nw, int r, int n, float L) {
+__device__ __forceinline__ uint32_t router_interval_from(const float* part, int nw, int r, int n, float L,
+                                                         float rel = kRouteRelDecode) {
   float xn2 = 0.f, xinf = 0.f, wn2 = 0.f, wn1 = 0.f;
   for (int w = 0; w < nw; ++w) {
     const float* q = part + w * 48;
@@ -151,7 +157,7 @@ __device__ __forceinline__ uint32_t router_interval_from(const float* part, int 
     wn2 += q[16 + r];  // rows 8..15 continue into [24, 32)
     wn1 += q[32 + r];
   }
-  return route_interval(L, xn2, xinf, wn2, wn1, kRouteRelDecode);
+  return route_interval(L, xn2, xinf, wn2, wn1, rel);
 }
 
 // fp64 dot product of two bf16 rows of length H (H % 8 == 0, 16-byte
@@ -184,6 +190,65 @@ static __device__ __noinline__ double warp_dot_f64(const uint16_t* x, const uint
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   return s;
+}
+
+// Router rows for the fp64 recompute: bf16 rows w [rows][H] (q == nullptr),
+// or 8-bit affine rows: codes q [rows][H/4], bf16 scales s and biases b
+// [rows][H/64]; row E_total is the shared gate (sq / ss / sb, or sw).
+struct RouterSrc {
+  const uint16_t* w;
+  const uint32_t* q;
+  const uint16_t* s;
+  const uint16_t* b;
+};
+
+// fp64 dot product of a bf16 token row with router row e of an 8-bit affine
+// router (H % 2048 == 0 or smaller H a multiple of 256), warp-cooperative;
+// every lane returns the sum.  The dequantised weight s * code + b (a bf16
+// times an 8-bit integer plus a bf16) is exact in fp64, and so is each
+// product with a bf16 activation.
+static __device__ __noinline__ double warp_dot_q8_f64(const uint16_t* x, const uint32_t* q, const uint16_t* s,
+                                                       const uint16_t* b, int H, int lane) {
+  double a0 = 0.0, a1 = 0.0;
+  for (int k0 = 0; k0 < H; k0 += 2048) {
+    uint4 xv[8];
+    uint2 qv[8];
+    uint32_t sb[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = k0 + j * 256 + lane * 8;
+      const bool in = k < H;
+      xv[j] = in ? *reinterpret_cast<const uint4*>(x + k) : make_uint4(0, 0, 0, 0);  // x: global or shared
+      qv[j] = in ? __ldg(reinterpret_cast<const uint2*>(q + k / 4)) : make_uint2(0, 0);
+      sb[j] = in ? (static_cast<uint32_t>(__ldg(s + k / 64)) | (static_cast<uint32_t>(__ldg(b + k / 64)) << 16)) : 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const double sc = static_cast<double>(__uint_as_float(sb[j] << 16));
+      const double bi = static_cast<double>(__uint_as_float(sb[j] & 0xFFFF0000u));
+      const uint32_t xs[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t word = i < 2 ? qv[j].x : qv[j].y;
+        const int sh = 16 * (i & 1);
+        const double w0 = fma(sc, static_cast<double>((word >> sh) & 0xFFu), bi);
+        const double w1 = fma(sc, static_cast<double>((word >> (sh + 8)) & 0xFFu), bi);
+        a0 = fma(static_cast<double>(__uint_as_float(xs[i] << 16)), w0, a0);
+        a1 = fma(static_cast<double>(__uint_as_float(xs[i] & 0xFFFF0000u)), w1, a1);
+      }
+    }
+  }
+  double r = a0 + a1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+  return r;
+}
+
+__device__ __forceinline__ double warp_dot_router_f64(const uint16_t* x, const RouterSrc& rs, int e, int H, int lane) {
+  if (rs.q)
+    return warp_dot_q8_f64(x, rs.q + static_cast<size_t>(e) * (H / 4), rs.s + static_cast<size_t>(e) * (H / 64),
+                           rs.b + static_cast<size_t>(e) * (H / 64), H, lane);
+  return warp_dot_f64(x, rs.w + static_cast<size_t>(e) * H, H, lane);
 }
 
 // The K largest of the warp's keys (8 per lane, unique, 0 = empty): lane
@@ -228,7 +293,7 @@ __device__ __forceinline__ uint32_t warp_select_k(const uint32_t (&keys)[8], int
 // unrolled: it runs for a minority of tokens, and the common path stays
 // small (its instructions are fetched once per token by the decode kernel).
 static __device__ __noinline__ int route_resolve(uint32_t (&klo)[8], uint32_t need, int K, const uint16_t* xrow,
-                                                 const uint16_t* router_w, int H, int lane, uint32_t& mine) {
+                                                 const RouterSrc rs, int H, int lane, uint32_t& mine) {
   int n = 0;
 #pragma unroll 1
   for (int i = 0; i < 8; ++i) {
@@ -238,7 +303,7 @@ static __device__ __noinline__ int route_resolve(uint32_t (&klo)[8], uint32_t ne
       const int src = __ffs(m) - 1;
       m &= m - 1;
       const int e = src + 32 * i;
-      const double d = warp_dot_f64(xrow, router_w + static_cast<size_t>(e) * H, H, lane);
+      const double d = warp_dot_router_f64(xrow, rs, e, H, lane);
       if (lane == src) klo[i] = route_key(f64_to_bf16_bits(d), e);
     }
   }
@@ -247,7 +312,7 @@ static __device__ __noinline__ int route_resolve(uint32_t (&klo)[8], uint32_t ne
 }
 
 __device__ __forceinline__ int warp_route_token_body(const uint32_t* ivl, int Et, int K, const uint16_t* xrow,
-                                                     const uint16_t* router_w, int H, int lane, bool exact_all,
+                                                     const RouterSrc rs, int H, int lane, bool exact_all,
                                                      float* logits_row, int* e_out, float* score_out) {
   uint32_t klo[8], vhi = 0;  // vhi bit i: lo != hi for expert lane + 32 i
   uint16_t hib[8];
@@ -271,7 +336,7 @@ __device__ __forceinline__ int warp_route_token_body(const uint32_t* ivl, int Et
   for (int i = 0; i < 8; ++i)
     if (((vhi >> i) & 1u) && (exact_all || route_key(hib[i], lane + 32 * i) >= theta)) need |= 1u << i;
   int n_exact = 0;
-  if (__any_sync(0xffffffffu, need != 0)) n_exact = route_resolve(klo, need, K, xrow, router_w, H, lane, mine);
+  if (__any_sync(0xffffffffu, need != 0)) n_exact = route_resolve(klo, need, K, xrow, rs, H, lane, mine);
   if (logits_row) {
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -287,9 +352,9 @@ __device__ __forceinline__ int warp_route_token_body(const uint32_t* ivl, int Et
 
 // Out-of-line form for kernels where code size matters less than one copy.
 static __device__ __noinline__ int warp_route_token(const uint32_t* ivl, int Et, int K, const uint16_t* xrow,
-                                                     const uint16_t* router_w, int H, int lane, bool exact_all,
+                                                     const RouterSrc rs, int H, int lane, bool exact_all,
                                                      float* logits_row, int* e_out, float* score_out) {
-  return warp_route_token_body(ivl, Et, K, xrow, router_w, H, lane, exact_all, logits_row, e_out, score_out);
+  return warp_route_token_body(ivl, Et, K, xrow, rs, H, lane, exact_all, logits_row, e_out, score_out);
 }
 
 }  // namespace rnb

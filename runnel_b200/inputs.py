@@ -57,6 +57,17 @@ class SyntheticBlock:
     sdn_b: np.ndarray
     norm_w: np.ndarray  # [H] fp32 RMSNorm weight
     meta: dict = field(default_factory=dict)
+    # 8-bit affine router and shared gate (router_bits=8, as real Ornith
+    # checkpoints store mlp.gate / mlp.shared_expert_gate): the same fp32
+    # draws quantized per 64 inputs (quant.quantize); router_w and
+    # shared_gate_w then hold their plain bf16 roundings, unused by the block
+    router_bits: int = 16
+    router_q: np.ndarray | None = None  # [E,H/4] u32
+    router_s: np.ndarray | None = None  # [E,H/64] u16
+    router_b: np.ndarray | None = None
+    sgate_q: np.ndarray | None = None  # [H/4] u32
+    sgate_s: np.ndarray | None = None  # [H/64] u16
+    sgate_b: np.ndarray | None = None
 
     @property
     def E(self) -> int:
@@ -73,7 +84,12 @@ class SyntheticBlock:
     def weight_fields(self) -> dict:
         names = ("router_w", "shared_gate_w", "gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b",
                  "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b")
-        return {n: getattr(self, n) for n in names}
+        out = {n: getattr(self, n) for n in names}
+        if self.router_bits == 8:
+            out["router_bits"] = 8
+            for n in ("router_q", "router_s", "router_b", "sgate_q", "sgate_s", "sgate_b"):
+                out[n] = getattr(self, n)
+        return out
 
 
 def _words(rng, shape) -> np.ndarray:
@@ -97,7 +113,7 @@ def _bank(rng, lead, rows, K, bits, group):
 
 def make_block(bits: int, seed: int, T: int = 1, H: int = 2048, I: int = 512, E: int = 256,
                group: int = 64, skew: str | None = None, zipf_s: float = 1.1,
-               adversarial_frac: float = 0.25) -> SyntheticBlock:
+               adversarial_frac: float = 0.25, router_bits: int = 16) -> SyntheticBlock:
     if bits not in (4, 8):
         raise ValueError("bits must be 4 or 8")
     rng = np.random.default_rng(seed)
@@ -128,11 +144,20 @@ def make_block(bits: int, seed: int, T: int = 1, H: int = 2048, I: int = 512, E:
             meta["hot_tokens"] = int(chosen.sum())
         else:
             raise ValueError(f"unknown skew {skew!r}")
-    return SyntheticBlock(
+    blk = SyntheticBlock(
         bits=bits, group=group, x=f32_to_bf16_bits(x), router_w=f32_to_bf16_bits(router),
         shared_gate_w=f32_to_bf16_bits(sgate), gu_w=gu[0], gu_s=gu[1], gu_b=gu[2], dn_w=dn[0],
         dn_s=dn[1], dn_b=dn[2], sgu_w=sgu[0], sgu_s=sgu[1], sgu_b=sgu[2], sdn_w=sdn[0],
         sdn_s=sdn[1], sdn_b=sdn[2], norm_w=norm_w, meta=meta)
+    if router_bits == 8:
+        from .quant import quantize
+        blk.router_bits = 8
+        blk.router_q, blk.router_s, blk.router_b = quantize(router, 8, group)
+        blk.sgate_q, blk.sgate_s, blk.sgate_b = quantize(sgate, 8, group)
+        meta["router_bits"] = 8
+    elif router_bits != 16:
+        raise ValueError("router_bits must be 16 or 8")
+    return blk
 
 
 def _make_block_args(args):

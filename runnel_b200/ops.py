@@ -10,6 +10,7 @@ from __future__ import annotations
 import ctypes
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -29,7 +30,8 @@ def _ptr(t: torch.Tensor | None) -> int | None:
 
 # the descriptor's tensor fields, in rnb_moe_desc order
 _BANK_FIELDS = ("gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b", "router_w", "shared_gate_w",
-                "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b")
+                "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b",
+                "router_s", "router_b", "sgate_s", "sgate_b")
 
 
 @dataclass
@@ -43,8 +45,8 @@ class BlockTensors:
     dn_w: torch.Tensor  # [E, H, I*bits/32]
     dn_s: torch.Tensor
     dn_b: torch.Tensor
-    router_w: torch.Tensor | None = None  # [E_total, H] bf16
-    shared_gate_w: torch.Tensor | None = None  # [H] or [1, H] bf16
+    router_w: torch.Tensor | None = None  # [E_total, H] bf16 (router_bits 8: [E_total, H/4] uint32)
+    shared_gate_w: torch.Tensor | None = None  # [H] or [1, H] bf16 (router_bits 8: [H/4] uint32)
     sgu_w: torch.Tensor | None = None  # [2I, H*bits/32]
     sgu_s: torch.Tensor | None = None
     sgu_b: torch.Tensor | None = None
@@ -55,6 +57,13 @@ class BlockTensors:
     E_total: int | None = None
     expert_offset: int = 0
     flags: int = 0
+    # 8-bit affine router and shared gate (mlp.gate / mlp.shared_expert_gate
+    # stored 8-bit): bf16 scales and biases per 64 inputs
+    router_bits: int = 16
+    router_s: torch.Tensor | None = None  # [E_total, H/64] bf16
+    router_b: torch.Tensor | None = None
+    sgate_s: torch.Tensor | None = None  # [H/64] bf16
+    sgate_b: torch.Tensor | None = None
 
     @property
     def E(self) -> int:
@@ -79,14 +88,25 @@ class BlockTensors:
             return t.to(device)
 
         lo, hi = E_range if E_range else (0, blk.E)
+        q8 = getattr(blk, "router_bits", 16) == 8
         bt = cls(
             bits=blk.bits, group=blk.group,
             gu_w=up(blk.gu_w[lo:hi], torch.uint32), gu_s=up(blk.gu_s[lo:hi], torch.bfloat16),
             gu_b=up(blk.gu_b[lo:hi], torch.bfloat16), dn_w=up(blk.dn_w[lo:hi], torch.uint32),
             dn_s=up(blk.dn_s[lo:hi], torch.bfloat16), dn_b=up(blk.dn_b[lo:hi], torch.bfloat16),
-            router_w=up(blk.router_w, torch.bfloat16), E_total=blk.E, expert_offset=lo)
+            router_w=up(blk.router_q, torch.uint32) if q8 else up(blk.router_w, torch.bfloat16),
+            E_total=blk.E, expert_offset=lo)
+        if q8:
+            bt.router_bits = 8
+            bt.router_s = up(blk.router_s, torch.bfloat16)
+            bt.router_b = up(blk.router_b, torch.bfloat16)
         if with_shared:
-            bt.shared_gate_w = up(blk.shared_gate_w, torch.bfloat16)
+            if q8:
+                bt.shared_gate_w = up(np.ascontiguousarray(blk.sgate_q.reshape(-1)), torch.uint32)
+                bt.sgate_s = up(np.ascontiguousarray(blk.sgate_s.reshape(-1)), torch.bfloat16)
+                bt.sgate_b = up(np.ascontiguousarray(blk.sgate_b.reshape(-1)), torch.bfloat16)
+            else:
+                bt.shared_gate_w = up(blk.shared_gate_w, torch.bfloat16)
             bt.sgu_w = up(blk.sgu_w, torch.uint32)
             bt.sgu_s = up(blk.sgu_s, torch.bfloat16)
             bt.sgu_b = up(blk.sgu_b, torch.bfloat16)
@@ -101,6 +121,7 @@ class BlockTensors:
         d.E_total = self.E_total if self.E_total is not None else self.E
         d.expert_offset = self.expert_offset
         d.k, d.bits, d.group, d.flags = k, self.bits, self.group, self.flags
+        d.router_bits = self.router_bits
         for name in _BANK_FIELDS:
             setattr(d, name, _ptr(getattr(self, name)))
         return d

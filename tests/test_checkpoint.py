@@ -95,6 +95,12 @@ def test_whole_block_arrays_dequantise_router(model):
     got = bf16_bits_to_f32(a["router_w"])
     assert np.abs(got - ref).max() <= np.abs(ref).max() * 2.0 ** -8  # one bf16 rounding
     assert a["shared_gate_w"].shape == (2048,)
+    # the 8-bit router and shared gate also come as stored, for the block
+    assert a["router_bits"] == 8
+    np.testing.assert_array_equal(a["router_q"], w)
+    np.testing.assert_array_equal(a["router_s"], s)
+    np.testing.assert_array_equal(a["router_b"], b)
+    assert a["sgate_q"].shape == (512,) and a["sgate_s"].shape == (32,) and a["sgate_b"].shape == (32,)
     assert a["sgu_w"].shape == (1024, 256)
     np.testing.assert_array_equal(a["sgu_w"][512:], st.read(f"{P}.shared_expert.gate_proj.weight")[0])
     assert a["norm_w"].shape == (2048,)

@@ -143,6 +143,34 @@ def test_oracle_block_routing_semantics():
     np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-4)
 
 
+def test_oracle_eight_bit_router_is_the_exact_dot_with_dequantised_rows():
+    # an 8-bit router's logit is the bf16 rounding of the exact dot product
+    # of the token with the dequantised row s * code + b (every term exact in
+    # fp64 here); the shared gate is fp32 with the same weights
+    blk = inputs.make_block(4, seed=7, T=5, H=512, I=256, E=16, router_bits=8)
+    assert blk.router_q.shape == (16, 128) and blk.sgate_q.reshape(-1).shape == (128,)
+    w = oracle.BlockWeights(bits=4, group=64, **_routed(blk))
+    logits, inds, scores, sg = oracle.router(w, blk.x, k=4)
+    def exact_rows(q, s_, b_):
+        codes = quant.unpack_codes(q, 8).astype(np.float64)
+        sc = np.repeat(quant.bf16_bits_to_f32(s_).astype(np.float64), 64, axis=-1)
+        bi = np.repeat(quant.bf16_bits_to_f32(b_).astype(np.float64), 64, axis=-1)
+        return codes * sc + bi
+    wq = exact_rows(blk.router_q, blk.router_s, blk.router_b)
+    x = quant.bf16_bits_to_f32(blk.x).astype(np.float64)
+    exact = x @ wq.T
+    # one rounding, fp64 -> bf16 (8 significant bits, nearest, ties to even)
+    m, e = np.frexp(exact)
+    np.testing.assert_array_equal(logits, np.ldexp(np.round(m * 256.0), e - 8).astype(np.float32))
+    gq = exact_rows(blk.sgate_q.reshape(1, -1), blk.sgate_s.reshape(1, -1), blk.sgate_b.reshape(1, -1))
+    np.testing.assert_allclose(sg, 1.0 / (1.0 + np.exp(-(x @ gq.T)[:, 0])), rtol=1e-5)
+    # the quantized rows differ from the bf16 ones: the two routers are not the same
+    l16, _, _, _ = oracle.router(oracle.BlockWeights(bits=4, group=64, **{
+        k: v for k, v in _routed(blk).items() if k not in ("router_bits", "router_q", "router_s", "router_b",
+                                                          "sgate_q", "sgate_s", "sgate_b")}), blk.x, k=4)
+    assert not np.array_equal(l16, logits)
+
+
 def test_prepared_block_call_refuses_host_tensors():
     # the prepared call builds the same descriptor as every other entry point:
     # a bank held in host memory fails loudly instead of running anywhere else

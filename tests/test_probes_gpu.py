@@ -120,9 +120,9 @@ def test_two_stage_dataset_probe_reference_kat(bits, expected, tmp_path):
 
 
 def test_checkpoint_block_and_layer_sweep(tmp_path):
-    """A synthetic MLX checkpoint: the whole block loaded by name runs and
-    matches the oracle on the same (dequantised-router) arrays; the layer sweep
-    writes one record per layer."""
+    """A synthetic MLX checkpoint: the whole block loaded by name (its 8-bit
+    router and shared gate as stored) runs and matches the oracle on the same
+    arrays; the layer sweep writes one record per layer."""
     import importlib.util
     from runnel_b200 import checkpoint, layers, ops
     spec = importlib.util.spec_from_file_location(
@@ -140,7 +140,9 @@ def test_checkpoint_block_and_layer_sweep(tmp_path):
     x = torch.from_numpy(x_bits.view(np.int16)).view(torch.bfloat16).cuda()
     out, inds, _ = ops.moe_block(bt, x, return_routing=True)
     fields = {k: a[k] for k in ("router_w", "shared_gate_w", "gu_w", "gu_s", "gu_b", "dn_w", "dn_s", "dn_b",
-                                "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b")}
+                                "sgu_w", "sgu_s", "sgu_b", "sdn_w", "sdn_s", "sdn_b", "router_bits",
+                                "router_q", "router_s", "router_b", "sgate_q", "sgate_s", "sgate_b")}
+    assert bt.router_bits == 8 and fields["router_bits"] == 8  # the checkpoint's router is 8-bit
     from tests._parity import assert_close, oracle_block
     ref, oinds, _, bound = oracle_block(oracle.BlockWeights(bits=4, group=64, **fields), x_bits)
     np.testing.assert_array_equal(np.sort(inds.cpu().numpy(), 1), np.sort(oinds, 1))
