@@ -159,7 +159,7 @@ RNB_API int rnb_moe_block_fwd(const rnb_moe_desc* d, const void* x, void* out, u
 /* rnb_moe_block_fwd for callers that cannot allocate device memory -- for
  * example a host that may not call cudaMalloc while it captures a CUDA graph,
  * or an engine plugin that owns no allocator.  It takes no workspace: scratch
- * is a static 8 MiB device array inside this library, present on every GPU
+ * is a static 12 MiB device array inside this library, present on every GPU
  * that loads it (enough for the Ornith shapes; larger shapes are rejected
  * with RNB_ERR_WORKSPACE).  The first call on a device looks up that array's
  * address, so make it before any stream capture.  All calls share the one

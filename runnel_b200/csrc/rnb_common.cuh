@@ -216,20 +216,19 @@ __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
 
-// Power-of-two scale that maps max|v| into [2^14, 2^15) (fp16 headroom)
-// and its inverse; both exact.
+// Power-of-two scale 2^e that maps max|v| into [2^14, 2^15) (fp16
+// headroom), e clamped to [-100, 100], and its inverse; both exact.  With
+// maxabs = m 2^p, m in [0.5, 1), e = 15 - p; for a normal maxabs with biased
+// exponent field E, p = E - 126, so e = 141 - E (a subnormal maxabs, E = 0,
+// clamps to 100 as its true p would).  Built from exponent bits: no branches
+// beyond the zero / non-finite case.
 __device__ __forceinline__ void fp16_range_scale(float maxabs, float& scale, float& inv) {
-  if (!(maxabs > 0.0f) || !isfinite(maxabs)) {
-    scale = 1.0f;
-    inv = 1.0f;
-    return;
-  }
-  int p;
-  frexpf(maxabs, &p);  // maxabs = m * 2^p, m in [0.5, 1)
-  int e = 15 - p;
+  const int E = static_cast<int>((__float_as_uint(maxabs) >> 23) & 0xFFu);
+  int e = 141 - E;
   e = e > 100 ? 100 : (e < -100 ? -100 : e);
-  scale = ldexpf(1.0f, e);
-  inv = ldexpf(1.0f, -e);
+  const bool ok = maxabs > 0.0f && E != 255;
+  scale = ok ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23) : 1.0f;
+  inv = ok ? __uint_as_float(static_cast<uint32_t>(127 - e) << 23) : 1.0f;
 }
 
 __device__ __forceinline__ float warp_max(float v) {

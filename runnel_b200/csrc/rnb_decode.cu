@@ -26,6 +26,7 @@
 #include <algorithm>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "rnb_common.cuh"
 #include "rnb_route.cuh"
@@ -67,6 +68,7 @@ struct Ws {
   uint32_t* seq;      // [0] call sequence word, [1] exit counter (persistent kernel)
   uint2* lw;          // [2][E_total + 1] logit exchange words (persistent kernel)
   uint2* hw;          // [2][k + 1][I] SwiGLU exchange words (persistent kernel)
+  uint2* yw;          // [16 (k + 1)][H] split-K partial words (persistent kernel, one token)
 };
 
 struct Params {
@@ -125,6 +127,42 @@ __device__ __forceinline__ RouterSrc router_src(const Params& p) {
 __device__ __forceinline__ void q8_router_quad(uint32_t word, double s, double b, double (&w)[4]) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) w[j] = fma(s, static_cast<double>((word >> (8 * j)) & 0xFFu), b);
+}
+
+// The four router weights (as doubles, exact) held by a lane of the
+// persistent decode kernel: 4 bf16 in w, or (8-bit router) the word of 4
+// codes in w.x and the group's bf16 scale | bias << 16 in w.y.
+__device__ __forceinline__ void router_quad(const uint2 w, bool q8, double (&wd)[4]) {
+  if (q8) {
+    q8_router_quad(w.x, static_cast<double>(__uint_as_float(w.y << 16)),
+                   static_cast<double>(__uint_as_float(w.y & 0xFFFF0000u)), wd);
+  } else {
+    wd[0] = __uint_as_float(w.x << 16);
+    wd[1] = __uint_as_float(w.x & 0xFFFF0000u);
+    wd[2] = __uint_as_float(w.y << 16);
+    wd[3] = __uint_as_float(w.y & 0xFFFF0000u);
+  }
+}
+
+// Reduce-scatter of four per-lane values over the warp: afterwards lane l
+// holds the warp total of value 2 * bit4(l) + bit3(l).  Three shuffles fewer
+// per value than four full butterflies; values 2 and 3 are reduced with max
+// when max23 is set, every other value with +.
+template <typename V>
+__device__ __forceinline__ V warp_reduce_scatter4(const V (&v)[4], int lane, bool max23) {
+  const bool b4 = (lane & 16) != 0, b3 = (lane & 8) != 0;
+  const bool mx = max23 && b4;  // the values this lane ends up with are 2, 3
+  auto op = [&](V a, V b) { return mx ? static_cast<V>(fmax(a, b)) : a + b; };
+  V k0 = b4 ? v[2] : v[0], k1 = b4 ? v[3] : v[1];
+  const V s0 = b4 ? v[0] : v[2], s1 = b4 ? v[1] : v[3];
+  k0 = op(k0, __shfl_xor_sync(0xffffffffu, s0, 16));
+  k1 = op(k1, __shfl_xor_sync(0xffffffffu, s1, 16));
+  V k = b3 ? k1 : k0;
+  k = op(k, __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8));
+  k = op(k, __shfl_xor_sync(0xffffffffu, k, 4));
+  k = op(k, __shfl_xor_sync(0xffffffffu, k, 2));
+  k = op(k, __shfl_xor_sync(0xffffffffu, k, 1));
+  return k;
 }
 
 // Optional phase timeline (compile with -DRNB_TRACE): thread 0 of each CTA
@@ -991,7 +1029,6 @@ constexpr int kPMaxT = 2;
 constexpr int kPMaxK = 8;
 constexpr int kPMaxAct = kPMaxT * kPMaxK;  // distinct local experts of one call
 constexpr int kPMaxMine = 8;               // routed gate/up tasks of one CTA
-constexpr int kDownBatch = 3;              // down units a warp handles per round trip for their h words
 constexpr uint64_t kSpinLimitNs = 200ull * 1000 * 1000;  // a wait gives up after 200 ms
 // Waits on other GPUs: ranks launch independently, so allow host-side skew
 // (the default of an EP context; rnb_ep_set_wait_limit_ms changes it).
@@ -1030,6 +1067,16 @@ __device__ __forceinline__ void xw_store(uint2* p, uint32_t v, uint32_t epoch) {
 __device__ __forceinline__ uint64_t xw_load(const uint2* p) {
   uint64_t w;
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];\n" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// Two neighbouring exchange words (16-byte aligned) in one access; each word
+// is read single-copy atomically on its own.
+__device__ __forceinline__ void xw_load2(const uint2* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];\n" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint64_t xw_load_acquire(const uint2* p) {
+  uint64_t w;
+  asm volatile("ld.acquire.gpu.global.b64 %0, [%1];\n" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
 __device__ __forceinline__ void xw_store_sys(uint2* p, uint32_t v, uint32_t epoch) {
@@ -1133,9 +1180,110 @@ __global__ void __launch_bounds__(256) k_ep_reduce(Params p, const float* partia
 
 // Shared-memory plan of k_decode (host-computed).
 struct PPlan {
-  int S;  // ring slots per warp
+  int S;   // ring slots per warp
+  int sk;  // the split-K form (one token, one GPU)
+  uint32_t off_tma;  // (split-K) the TMA destinations start at the next 1024-byte boundary from here
   uint32_t off_ring, off_sdn, off_x, off_xs, off_xn, off_ivl, off_red, off_hf, off_redc, off_misc;
 };
+
+// ---- split-K form of k_decode (one token, one GPU)
+//
+// Task i < 16 (k + 1) of CTA i: source s = i / 16 (routed slot s < k, the
+// shared expert at s = k) and channel slice j = i % 16, channels
+// [32 j, 32 j + 32).  The CTA computes the slice's gate/up (64 weight rows,
+// its 16 warps splitting the hidden dimension), SwiGLU, and the slice's
+// share of the down projection, y_i = W_down[:, slice] h[slice] over all H
+// rows, weighted by the slot's routing weight (or the shared gate).  So h
+// never leaves the CTA.  The weighted partials go out as {value, epoch}
+// words; CTA r < H / 16 polls and sums the 16 (k + 1) partials of rows
+// [16 r, 16 r + 16) in task order.
+// The shared expert's CTAs know their weights at launch and load them in the
+// prologue.
+constexpr int kSkC = 32;                 // channels per task
+constexpr int kSkUnits = kSkC / 8;       // gate/up tiles (8 up + 8 gate rows) per task
+constexpr int kSkTasksPerSource = 512 / kSkC;
+
+// TMA descriptors of the split-K loads (host-encoded, cached per tensor).
+// Gate/up codes: 4-D {a warp's K slice (Tile2 row bytes, as u32), 2I rows,
+// 16 slices, experts}, box {slice, 32 rows, 16 slices, 1}: one request puts
+// a task's 32 up (or gate) rows in shared memory as [slice][32 rows][slice
+// bytes], swizzled (64 B or 128 B) so that the MMA reads are conflict-free.
+// Gate/up scales and biases: 3-D {H/64 groups, 2I rows, experts}, box
+// {H/64, 32, 1}.  Down codes: 4-D {row words, 256 rows, H/256 blocks,
+// experts}, box {the slice's words, 256, H/256, 1}: the slice's codes of all
+// H rows, [H][slice bytes].
+struct SkMaps {
+  CUtensorMap gu_w, gu_s, gu_b, dn_w;      // the routed bank
+  CUtensorMap sgu_w, sgu_s, sgu_b, sdn_w;  // the shared expert
+};
+
+// The down slice's codes, [H rows][slice bytes] in shared memory (warp w
+// takes rows [128 w, 128 w + 128)); each warp's rows' group scales and
+// biases go to registers (lane l: rows l, l + 32, l + 64, l + 96; each a
+// 4-byte word with the neighbouring group's value), as coalesced loads.
+template <int BITS>
+struct SkDown {
+  static constexpr int kRow = kSkC * BITS / 8;  // code bytes per row (16 or 32)
+  static constexpr int kCodeBytes = 128 * kRow;
+  static constexpr int kBytes = kCodeBytes;
+};
+
+__device__ __forceinline__ void sk_down_sb(const uint16_t* sc, const uint16_t* bi, int I, int row0, int j, int lane,
+                                           uint32_t (&sw)[4], uint32_t (&bw)[4]) {
+  const size_t srow = I / kGroup;
+  const int grp2 = (j * kSkC / kGroup) & ~1;  // the word of groups (grp2, grp2 + 1)
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const size_t o = static_cast<size_t>(row0 + lane + 32 * k) * srow + grp2;
+    sw[k] = __ldg(reinterpret_cast<const uint32_t*>(sc + o));
+    bw[k] = __ldg(reinterpret_cast<const uint32_t*>(bi + o));
+  }
+}
+
+// The slice's down MMAs for one warp: 8 tiles of 16 rows x 32 channels.
+// bt: the B pairs [lane c][pair 4] of the fp16 h slice; hs: its sum; hinv:
+// its inverse scale; emit(row, value) for the rows this lane finishes
+// (c == 0: rows g and g + 8 of each tile).
+template <int BITS, typename Emit>
+__device__ __forceinline__ void sk_down_mma(const char* sm, const uint32_t (&sw)[4], const uint32_t (&bw)[4],
+                                            const uint32_t* bt, float hs, float hinv, int j, int g, int c,
+                                            Emit emit) {
+  using SD = SkDown<BITS>;
+  const uint32_t b0 = bt[c * 4 + 0], b1 = bt[c * 4 + 1], b2 = bt[c * 4 + 2], b3 = bt[c * 4 + 3];
+  const int half = (j * kSkC / kGroup) & 1;
+#pragma unroll
+  for (int v = 0; v < 8; ++v) {
+    const int ra = 16 * v + g, rb = ra + 8;
+    uint32_t pa[4], pb[4];
+    if (BITS == 8) {
+      const uint2 wa = *reinterpret_cast<const uint2*>(sm + ra * SD::kRow + 8 * c);
+      const uint2 wb = *reinterpret_cast<const uint2*>(sm + rb * SD::kRow + 8 * c);
+      q8_word_to_pairs_sub(wa.x, pa[0], pa[1]);
+      q8_word_to_pairs_sub(wa.y, pa[2], pa[3]);
+      q8_word_to_pairs_sub(wb.x, pb[0], pb[1]);
+      q8_word_to_pairs_sub(wb.y, pb[2], pb[3]);
+    } else {
+      const uint32_t wa = *reinterpret_cast<const uint32_t*>(sm + ra * SD::kRow + 4 * c);
+      const uint32_t wb = *reinterpret_cast<const uint32_t*>(sm + rb * SD::kRow + 4 * c);
+      q4_word_to_pairs_sub(wa, pa[0], pa[1], pa[2], pa[3]);
+      q4_word_to_pairs_sub(wb, pb[0], pb[1], pb[2], pb[3]);
+    }
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_f16(d, pa[0], pb[0], pa[1], pb[1], b0, b1);
+    mma_f16(d, pa[2], pb[2], pa[3], pb[3], b2, b3);
+    // rows ra and rb are held by lanes ra % 32 and rb % 32 in register v / 2
+    const uint32_t sa2 = __shfl_sync(0xffffffffu, sw[v >> 1], ra & 31);
+    const uint32_t ba2 = __shfl_sync(0xffffffffu, bw[v >> 1], ra & 31);
+    const uint32_t sb2 = __shfl_sync(0xffffffffu, sw[v >> 1], rb & 31);
+    const uint32_t bb2 = __shfl_sync(0xffffffffu, bw[v >> 1], rb & 31);
+    if (c == 0) {
+      auto pick = [&](uint32_t w2) { return __uint_as_float(half ? (w2 & 0xFFFF0000u) : (w2 << 16)); };
+      // the codes entered the MMAs as fp16 subnormals q * 2^-24: the scale carries 2^24 back
+      emit(ra, hinv * fmaf(pick(sa2) * 0x1p24f, d[0], pick(ba2) * hs));
+      emit(rb, hinv * fmaf(pick(sb2) * 0x1p24f, d[2], pick(bb2) * hs));
+    }
+  }
+}
 
 struct PMisc {
   uint32_t inds[kPMaxT][kPMaxK];
@@ -1150,6 +1298,8 @@ struct PMisc {
   uint32_t act_ent[kPMaxAct][kPMaxT];  // entry id t*(K+1)+slot of each column
   double rdot[kPWarps][4];   // router partials: dot (row i, token t) at 2i+t, fp64
   float rnorm[kPWarps][8];   // [0,2) sum w^2; [2,4) sum |w|; [4,6) sum x^2; [6,8) max |x|
+  uint32_t skbt[16];         // split-K: B pairs [lane c][pair] of the fp16 h slice
+  float skhs, skhinv;        // split-K: sum of the fp16 h slice, its inverse scale
 };
 
 // Activation prep of T tokens (H = 2048) by the whole CTA (512 threads, 4
@@ -1326,11 +1476,68 @@ __device__ __forceinline__ void tile2_mma(const char* sm, int g, int c, BFrag bf
   }
 }
 
+// Physical byte offset of 16-byte chunk ch of row r in a TMA-swizzled block
+// whose rows are kRowBytes long (64: 64-byte swizzle, 128: 128-byte).
+template <int BITS>
+__device__ __forceinline__ int sk_swz_chunk(int r, int ch) {
+  return BITS == 8 ? ((ch ^ (r & 7)) << 4) : ((ch ^ ((r >> 1) & 3)) << 4);
+}
+
+// acc (rows g: up channel 8u + g, g + 8: gate channel 8u + g; columns 2c,
+// 2c + 1) += affine(tile . B) over this warp's two groups, from the
+// TMA-loaded blocks: up / gate codes [16 slices][32 rows][Tile2 row bytes],
+// sb = [up scales | gate scales | up biases | gate biases], each [32 rows][H/64].
+template <int BITS, typename BFrag, typename GSum, typename GInv>
+__device__ __forceinline__ void sk_gu_mma(const char* up, const char* gate, const uint16_t* sb, int G, int u, int w,
+                                          int g, int c, BFrag bfrag, GSum gsum, GInv ginv, float (&acc)[4]) {
+  using TL = Tile2<BITS>;
+  const int r = 8 * u + g;
+  const char* ua = up + (w * 32 + r) * TL::kRowBytes;
+  const char* ga = gate + (w * 32 + r) * TL::kRowBytes;
+  const int q = (c == 1) ? 2 : (c == 2) ? 1 : c;
+#pragma unroll
+  for (int gi = 0; gi < 2; ++gi) {
+    RowPairs pa, pb;
+    if (BITS == 8) {
+      const int ch = gi * 4 + c;
+      pa = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(ua + sk_swz_chunk<BITS>(r, ch)));
+      pb = q8_group_pairs_sub(*reinterpret_cast<const uint4*>(ga + sk_swz_chunk<BITS>(r, ch)));
+    } else {
+      const int ch = gi * 2 + (q >> 1), off = 8 * (q & 1);
+      pa = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(ua + sk_swz_chunk<BITS>(r, ch) + off));
+      pb = q4_group_pairs_sub(*reinterpret_cast<const uint2*>(ga + sk_swz_chunk<BITS>(r, ch) + off));
+    }
+    uint32_t xb[8];
+    bfrag(gi, xb);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+      mma_f16(d, pa.p[2 * m], pb.p[2 * m], pa.p[2 * m + 1], pb.p[2 * m + 1], xb[2 * m], xb[2 * m + 1]);
+    const int gcol = 2 * w + gi, n = 32 * G;
+    const float sa = bf16_bits_to_f32(sb[r * G + gcol]) * 0x1p24f, ba = bf16_bits_to_f32(sb[2 * n + r * G + gcol]);
+    const float sg = bf16_bits_to_f32(sb[n + r * G + gcol]) * 0x1p24f, bg = bf16_bits_to_f32(sb[3 * n + r * G + gcol]);
+    const float xs0 = gsum(gi, 0), xs1 = gsum(gi, 1);
+    const float i0 = ginv(gi, 0), i1 = ginv(gi, 1);
+    acc[0] = fmaf(i0, fmaf(sa, d[0], ba * xs0), acc[0]);
+    acc[1] = fmaf(i1, fmaf(sa, d[1], ba * xs1), acc[1]);
+    acc[2] = fmaf(i0, fmaf(sg, d[2], bg * xs0), acc[2]);
+    acc[3] = fmaf(i1, fmaf(sg, d[3], bg * xs1), acc[3]);
+  }
+}
+
 // EP: compiled with the expert-parallel exchange (ep_world > 1); the
 // single-GPU instance carries no exchange code.
-template <int BITS, bool EP>
-__global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan pl) {
+// SK: the split-K form for one token on one GPU (see kSkC); otherwise the
+// h-exchange form (one or two tokens, expert parallel included).
+template <int BITS, bool EP, bool SK>
+__global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan pl, const __grid_constant__ SkMaps skm) {
   extern __shared__ __align__(16) char sm[];
+  __shared__ __align__(8) uint64_t sk_bar[2];  // (split-K) gate/up and down TMA phases
+  if (SK && threadIdx.x == 0) {
+    mbar_init(&sk_bar[0], 1);
+    mbar_init(&sk_bar[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
   // The parameters are read from a shared-memory copy: a kernel parameter
   // is an operand in the constant bank, and on this single-pass kernel each
   // of its scattered reads would otherwise risk a constant-cache miss (an L2
@@ -1348,8 +1555,6 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   float* sXs = reinterpret_cast<float*>(sm + pl.off_xs);
   uint32_t* sIvl = reinterpret_cast<uint32_t*>(sm + pl.off_ivl);
   float* sRed = reinterpret_cast<float*>(sm + pl.off_red);
-  // this warp's B fragments of the down MMAs: [kDownBatch units][T columns][64]
-  uint32_t* sHf = reinterpret_cast<uint32_t*>(sm + pl.off_hf) + warp * (kDownBatch * 64 * p_arg.T);
   float* sRedC = reinterpret_cast<float*>(sm + pl.off_redc);
   PMisc* ms = reinterpret_cast<PMisc*>(sm + pl.off_misc);
   const uint32_t off_xn = pl.off_xn, off_hf = pl.off_hf;
@@ -1374,8 +1579,48 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   // the shared-expert gate/up tasks go to the last I/8 CTAs: routed tasks are
   // dealt round-robin from CTA 0, so the last CTAs have one fewer
   const int sg_task = cta - (NC - n_ch);
-  const bool owns_sgu = has_shared && sg_task >= 0 && ((qmask >> ((sg_task * 8) / 128)) & 1u);
-  const bool sh_down = owns_rows && has_shared && qmask != 0u;
+  const bool owns_sgu = !SK && has_shared && sg_task >= 0 && ((qmask >> ((sg_task * 8) / 128)) & 1u);
+  const bool sh_down = !SK && owns_rows && has_shared && qmask != 0u;
+  // split-K task of this CTA: source (routed slot, or the shared expert at
+  // slot k) and 32-channel slice; CTAs past the last task only route
+  const int sk_src = cta / kSkTasksPerSource, sk_j = cta % kSkTasksPerSource;
+  const bool sk_shared = SK && has_shared && sk_src == K;
+  const bool sk_task = SK && (sk_src < K || sk_shared);
+  using SD = SkDown<BITS>;
+  // (split-K) TMA destinations, from the first 1024-byte boundary at or after
+  // off_tma: up and gate codes [16 slices][32 rows][Tile2 row bytes] each,
+  // their scales and biases, the down codes [H][slice bytes]
+  constexpr uint32_t kSkGuBox = 16u * 32u * TL::kRowBytes;
+  constexpr uint32_t kSkSbBox = 32u * 32u * 2u;  // 32 rows x H/64 groups (H = 2048)
+  char* skb = sm + pl.off_tma + (1024u - (smem_u32(sm) + pl.off_tma) % 1024u) % 1024u;
+  char* sGu = skb;
+  const uint16_t* sGsb = reinterpret_cast<const uint16_t*>(skb + 2 * kSkGuBox);
+  char* sDnA = skb + 2 * kSkGuBox + 4 * kSkSbBox;
+  char* sDn = sDnA + static_cast<size_t>(warp) * SD::kBytes;  // (split-K) this warp's down rows
+  uint32_t sk_sw[4], sk_bw[4];  // (split-K) this lane's down rows' scale and bias words
+  // (split-K) the task's loads: thread 0 issues the TMA requests (gate/up
+  // codes, scales and biases on barrier 0; the down codes on barrier 1),
+  // every lane loads its down rows' scale and bias words
+  auto sk_issue_all = [&](bool shared, int e, const uint16_t* ds, const uint16_t* db) {
+    if (tid == 0) {
+      const CUtensorMap* mw = shared ? &skm.sgu_w : &skm.gu_w;
+      const CUtensorMap* msc = shared ? &skm.sgu_s : &skm.gu_s;
+      const CUtensorMap* mbi = shared ? &skm.sgu_b : &skm.gu_b;
+      const CUtensorMap* md = shared ? &skm.sdn_w : &skm.dn_w;
+      const uint32_t b0 = smem_u32(&sk_bar[0]), b1 = smem_u32(&sk_bar[1]);
+      const int r0 = sk_j * kSkC;
+      mbar_arrive_expect_tx(&sk_bar[0], 2 * kSkGuBox + 4 * kSkSbBox);
+      tma_load_4d(smem_u32(sGu), mw, 0, r0, 0, e, b0);
+      tma_load_4d(smem_u32(sGu + kSkGuBox), mw, 0, I + r0, 0, e, b0);
+      tma_load_3d(smem_u32(sGsb), msc, 0, r0, e, b0);
+      tma_load_3d(smem_u32(sGsb + 1 * kSkSbBox / 2), msc, 0, I + r0, e, b0);
+      tma_load_3d(smem_u32(sGsb + 2 * kSkSbBox / 2), mbi, 0, r0, e, b0);
+      tma_load_3d(smem_u32(sGsb + 3 * kSkSbBox / 2), mbi, 0, I + r0, e, b0);
+      mbar_arrive_expect_tx(&sk_bar[1], static_cast<uint32_t>(H) * SD::kRow);
+      tma_load_4d(smem_u32(sDnA), md, sk_j * BITS, 0, 0, e, b1);
+    }
+    sk_down_sb(ds, db, I, warp * 128, sk_j, lane, sk_sw, sk_bw);
+  };
   const int j0 = owns_sgu ? 1 : 0;  // ring unit 0: this warp's slice of the shared-expert gate/up task
   auto gu_row = [&](int ch0) { return [=](int i) -> size_t { return i < 8 ? ch0 + i : I + ch0 + i - 8; }; };
   auto dn_row = [=](int i) -> size_t { return static_cast<size_t>(n0 + i); };
@@ -1408,6 +1653,22 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   if (owns_sgu)
     tile2_issue<BITS>(ring, p.sgu_w, p.sgu_s, p.sgu_b, gwrow, gsrow, warp * 2, gu_row(sg_task * 8), lane);
   cp_async_commit();  // group: shared gate/up slice (ring unit 0; may be empty)
+  {
+    // the router rows' norms (weights only): sum w^2 and sum |w| of rows
+    // cta, cta + NC, per warp into ms->rnorm[warp][0..3]
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      double wd[4];
+      router_quad(wr[i], p.router_q8 != 0, wd);
+      const float wf[4] = {static_cast<float>(wd[0]), static_cast<float>(wd[1]), static_cast<float>(wd[2]),
+                           static_cast<float>(wd[3])};
+      v[i] = fmaf(wf[0], wf[0], fmaf(wf[1], wf[1], fmaf(wf[2], wf[2], wf[3] * wf[3])));
+      v[2 + i] = (fabsf(wf[0]) + fabsf(wf[1])) + (fabsf(wf[2]) + fabsf(wf[3]));
+    }
+    const float r = warp_reduce_scatter4(v, lane, false);
+    if ((lane & 7) == 0) ms->rnorm[warp][lane >> 3] = r;
+  }
   if (sh_down && warp < nq && ((qmask >> warp) & 1u))
     tile2_issue<BITS>(sSdn + warp * TL::kBytes, p.sdn_w, p.sdn_s, p.sdn_b, dwrow, dsrow, warp * 2, dn_row, lane);
   cp_async_commit();  // group: this warp's shared-down quarter
@@ -1483,21 +1744,11 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       xf[t][3] = __uint_as_float(xv.y & 0xFFFF0000u);
     }
     double dv[4];
-    float v[8];
+    float v[4];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       double wd[4];
-      if (p.router_q8) {
-        q8_router_quad(wr[i].x, static_cast<double>(__uint_as_float(wr[i].y << 16)),
-                       static_cast<double>(__uint_as_float(wr[i].y & 0xFFFF0000u)), wd);
-      } else {
-        wd[0] = __uint_as_float(wr[i].x << 16);
-        wd[1] = __uint_as_float(wr[i].x & 0xFFFF0000u);
-        wd[2] = __uint_as_float(wr[i].y << 16);
-        wd[3] = __uint_as_float(wr[i].y & 0xFFFF0000u);
-      }
-      const float wf[4] = {static_cast<float>(wd[0]), static_cast<float>(wd[1]), static_cast<float>(wd[2]),
-                           static_cast<float>(wd[3])};
+      router_quad(wr[i], p.router_q8 != 0, wd);
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         double d = wd[0] * static_cast<double>(xf[t][0]);
@@ -1506,34 +1757,19 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
         d = fma(wd[3], static_cast<double>(xf[t][3]), d);
         dv[2 * i + t] = d;
       }
-      v[i] = fmaf(wf[0], wf[0], fmaf(wf[1], wf[1], fmaf(wf[2], wf[2], wf[3] * wf[3])));
-      v[2 + i] = (fabsf(wf[0]) + fabsf(wf[1])) + (fabsf(wf[2]) + fabsf(wf[3]));
     }
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      v[4 + t] = fmaf(xf[t][0], xf[t][0], fmaf(xf[t][1], xf[t][1], fmaf(xf[t][2], xf[t][2], xf[t][3] * xf[t][3])));
-      v[6 + t] = fmaxf(fmaxf(fabsf(xf[t][0]), fabsf(xf[t][1])), fmaxf(fabsf(xf[t][2]), fabsf(xf[t][3])));
+      v[t] = fmaf(xf[t][0], xf[t][0], fmaf(xf[t][1], xf[t][1], fmaf(xf[t][2], xf[t][2], xf[t][3] * xf[t][3])));
+      v[2 + t] = fmaxf(fmaxf(fabsf(xf[t][0]), fabsf(xf[t][1])), fmaxf(fabsf(xf[t][2]), fabsf(xf[t][3])));
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) dv[j] += __shfl_xor_sync(0xffffffffu, dv[j], o);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float u = __shfl_xor_sync(0xffffffffu, v[j], o);
-        v[j] = j >= 6 ? fmaxf(v[j], u) : v[j] + u;
-      }
-    }
-    if (lane < 4) {
-      double mine = dv[0];
-#pragma unroll
-      for (int j = 1; j < 4; ++j) mine = lane == j ? dv[j] : mine;
-      ms->rdot[warp][lane] = mine;
-    } else if (lane < 12) {
-      float mine = v[0];
-#pragma unroll
-      for (int j = 1; j < 8; ++j) mine = lane - 4 == j ? v[j] : mine;
-      ms->rnorm[warp][lane - 4] = mine;
+    // lane 8q holds the warp's dot q = 2 * row + token and token statistic
+    // q (sum x^2 of tokens 0, 1, then max |x| of tokens 0, 1)
+    const double dq = warp_reduce_scatter4(dv, lane, false);
+    const float xq = warp_reduce_scatter4(v, lane, true);
+    if ((lane & 7) == 0) {
+      ms->rdot[warp][lane >> 3] = dq;
+      ms->rnorm[warp][4 + (lane >> 3)] = xq;
     }
     __syncthreads();
     // warp w < 4 finishes (row cta + (w >> 1) * NC, token w & 1): lanes 0..15
@@ -1561,6 +1797,9 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     }
   }
   RNB_TRACE_MARK(p, 3);
+  // (split-K) the shared expert's tasks know their weights: load them now,
+  // once this CTA's router rows are out (they are on every CTA's path)
+  if (sk_shared) sk_issue_all(true, 0, p.sdn_s, p.sdn_b);
   // (the B-fragment area is free until the down phase: 4 KB of it are xprep's scratch)
   xprep_cta<BITS>(xin, T, sX, sXs, ms->xinv, reinterpret_cast<__half*>(sm + off_hf), ms->red);
   RNB_TRACE_MARK(p, 4);
@@ -1621,13 +1860,18 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       ms->scores[t][lane] = sc;
     }
     if (lane == 0) ms->sg[t] = p.has_shared ? 1.0f / (1.0f + expf(-__uint_as_float(sIvl[t * (Et + 1) + Et]))) : 0.f;
+    // the routing warps meet (warp 0 reads every token's selection); the
+    // rest of the CTA waits at the one CTA barrier below
+    if (T > 1)
+      asm volatile("bar.sync 1, %0;\n" ::"r"(32 * T) : "memory");
+    else
+      __syncwarp();
   }
-  __syncthreads();
   RNB_TRACE_MARK(p, 7);
-  // active local experts in (token, slot) order of first use, with their
-  // columns: lane i < T*K holds entry i; lanes holding the same expert find
-  // each other with one match, the expert's index is the number of first
-  // occurrences before its first lane
+  // Warp 0: the active local experts in (token, slot) order of first use,
+  // with their columns (lane i < T*K holds entry i; lanes holding the same
+  // expert find each other with one match, the expert's index is the number
+  // of first occurrences before its first lane), then the CTA's task list.
   if (warp == 0) {
     const bool act = lane < T * K;
     const uint32_t e = act ? ms->inds[lane / K][lane % K] : 0xFFFFFFFFu;
@@ -1646,6 +1890,18 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       }
     }
     if (lane == 0) ms->n_act = static_cast<uint32_t>(__popc(firsts));
+    __syncwarp();
+    // this CTA's routed gate/up tasks m < mine: task i = cta + m NC
+    const int nb = __popc(firsts) * n_ch;
+    const int mn = nb > cta ? (nb - cta + NC - 1) / NC : 0;
+    if (lane < mn) {
+      const int i = cta + lane * NC, a2 = i / n_ch;
+      const int cnt = static_cast<int>(ms->act_cnt[a2]);
+      s_ncols[lane] = cnt;
+      s_ch0[lane] = (i % n_ch) * 8;
+      for (int n = 0; n < kPMaxT; ++n) s_ent[lane][n] = ms->act_ent[a2][n < cnt ? n : 0];
+    }
+    if (lane < kPMaxT) s_ent[kPMaxMine][lane] = static_cast<uint32_t>((lane < T ? lane : 0) * (K + 1) + K);
   }
   __syncthreads();
   RNB_TRACE_MARK(p, 20);
@@ -1655,6 +1911,134 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     if (p.inds_out) p.inds_out[tid] = ms->inds[t][s];
     if (p.scores_out) p.scores_out[tid] = ms->scores[t][s];
   }
+
+  bool timed_out = false;
+  if constexpr (SK) {
+    // ---- split-K (one token): this CTA's task, then the combine of its rows
+    const int ntask = kSkTasksPerSource * (K + (has_shared ? 1 : 0));
+    uint2* yw = p.ws.yw;  // [task][H] weighted partial words
+    if (sk_task) {
+      float wgt = ms->sg[0];
+      if (!sk_shared) {
+        const uint32_t le = ms->inds[0][sk_src] - static_cast<uint32_t>(p.off);
+        const size_t dse = static_cast<size_t>(H) * dsrow;
+        wgt = ms->scores[0][sk_src];
+        RNB_TRACE_MARK(p, 21);
+        sk_issue_all(false, static_cast<int>(le), p.dn_s + le * dse, p.dn_b + le * dse);
+        RNB_TRACE_MARK(p, 22);
+      }
+      // gate/up: the four 8-channel tiles, once the task's TMA loads are in
+      RNB_TRACE_MARK(p, 9);
+      if (!mbar_wait(&sk_bar[0], 0, kSpinLimitNs)) timed_out = true;
+      RNB_TRACE_MARK(p, 10);
+      const int g0 = warp * 2;
+#pragma unroll 1
+      for (int u = 0; u < kSkUnits; ++u) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        sk_gu_mma<BITS>(
+            sGu, sGu + kSkGuBox, sGsb, G, u, warp, g, c,
+            [&](int gi, uint32_t(&xb)[8]) {
+              const uint32_t* src = sX + static_cast<size_t>(g0 + gi) * 32 + c * 8;
+              const uint4 u0 = reinterpret_cast<const uint4*>(src)[0];
+              const uint4 u1 = reinterpret_cast<const uint4*>(src)[1];
+              xb[0] = u0.x; xb[1] = u0.y; xb[2] = u0.z; xb[3] = u0.w;
+              xb[4] = u1.x; xb[5] = u1.y; xb[6] = u1.z; xb[7] = u1.w;
+            },
+            [&](int gi, int) { return sXs[g0 + gi]; }, [](int, int) { return 1.0f; }, acc);
+        store_partials(u, acc);
+      }
+      RNB_TRACE_MARK(p, 11);
+      __syncthreads();
+      // SwiGLU of the slice's 32 channels (warp 0, lane = channel), its fp16
+      // form with one power-of-two scale, and the down MMAs' B pairs
+      if (warp == 0) {
+        const int u = lane >> 3, r = lane & 7;
+        float up = 0.f, gate = 0.f;
+#pragma unroll
+        for (int w = 0; w < kPWarps; ++w) {
+          up += sRed[(u * kPWarps + w) * 32 + r * 2];
+          gate += sRed[(u * kPWarps + w) * 32 + (8 + r) * 2];
+        }
+        up *= ms->xinv[0];
+        gate *= ms->xinv[0];
+        const float h = (gate / (1.0f + expf(-gate))) * up;
+        float sc, inv;
+        fp16_range_scale(warp_max(fabsf(h)), sc, inv);
+        const __half hh = __float2half_rn(h * sc);
+        const float hs = warp_sum(__half2float(hh));
+        const uint32_t hb = __half_as_ushort(hh);
+        // lane t < 16: pair (c = t / 4, i = t % 4) of the positions a lane c
+        // of a quad holds (its codes 8c .. 8c + 7): (8c + i, 8c + i + 4) at 4
+        // bits, odd pairs times 1/16 (they meet codes times 16); (8c + 2i,
+        // 8c + 2i + 1) at 8 bits
+        const int cq = (lane >> 2) & 3, ip = lane & 3;
+        const int plo = BITS == 8 ? 8 * cq + 2 * ip : 8 * cq + ip, phi = BITS == 8 ? plo + 1 : plo + 4;
+        __half lo = __ushort_as_half(static_cast<uint16_t>(__shfl_sync(0xffffffffu, hb, plo)));
+        __half hi = __ushort_as_half(static_cast<uint16_t>(__shfl_sync(0xffffffffu, hb, phi)));
+        if (BITS == 4 && (ip & 1)) {
+          lo = __hmul(lo, __float2half_rn(0.0625f));
+          hi = __hmul(hi, __float2half_rn(0.0625f));
+        }
+        if (lane < 16)
+          ms->skbt[lane] = static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+        if (lane == 0) {
+          ms->skhs = hs;
+          ms->skhinv = inv;
+        }
+      }
+      if (!mbar_wait(&sk_bar[1], 0, kSpinLimitNs)) timed_out = true;  // the down codes
+      __syncthreads();
+      RNB_TRACE_MARK(p, 12);
+      uint2* ydst = yw + static_cast<size_t>(cta) * H + warp * 128;
+      sk_down_mma<BITS>(sDn, sk_sw, sk_bw, ms->skbt, ms->skhs, ms->skhinv, sk_j, g, c,
+                        [&](int r, float v) { xw_store(ydst + r, __float_as_uint(v * wgt), epoch); });
+      RNB_TRACE_MARK(p, 14);
+    }
+    if (cta < H / 16) {
+      // rows [16 cta, 16 cta + 16): warp w sums row 16 cta + w over the
+      // tasks, lane l taking tasks l, l + 32, ... (all its words polled
+      // together, bounded) in order, then a fixed butterfly
+      constexpr int kMaxPer = (kSkTasksPerSource * (kPMaxK + 1) + 31) / 32;
+      const uint2* yp = yw + 16 * cta + warp;
+      uint64_t wv[kMaxPer];
+#pragma unroll
+      for (int k2 = 0; k2 < kMaxPer; ++k2) {
+        const int t = lane + 32 * k2;
+        wv[k2] = t < ntask ? xw_load(yp + static_cast<size_t>(t) * H) : (static_cast<uint64_t>(epoch) << 32);
+      }
+      const uint64_t deadline = gtimer() + kSpinLimitNs;
+      for (;;) {
+        bool all = true;
+#pragma unroll
+        for (int k2 = 0; k2 < kMaxPer; ++k2) {
+          const int t = lane + 32 * k2;
+          if (static_cast<uint32_t>(wv[k2] >> 32) != epoch) {
+            all = false;
+            wv[k2] = xw_load(yp + static_cast<size_t>(t) * H);
+          }
+        }
+        const bool late = !all && gtimer() > deadline;
+        if (late) timed_out = true;
+        if (__all_sync(0xffffffffu, all || late)) break;
+        __nanosleep(32);
+      }
+      RNB_TRACE_MARK(p, 23);
+      float acc = 0.f;
+#pragma unroll
+      for (int k2 = 0; k2 < kMaxPer; ++k2)
+        if (lane + 32 * k2 < ntask) acc += __uint_as_float(static_cast<uint32_t>(wv[k2]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) {
+        const size_t o = static_cast<size_t>(16 * cta + warp);
+        if (p.y_f32)
+          static_cast<float*>(p.out)[o] = acc;
+        else
+          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(acc);
+      }
+      RNB_TRACE_MARK(p, 19);
+    }
+  } else {
 
   // ---- this CTA's work.  Every warp streams, in this order, its units
   // through its own ring of S shared-memory slots (unit j in slot j % S,
@@ -1668,13 +2052,6 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   //   in the prologue.
   const int n_btask = n_act * n_ch;
   const int mine = n_btask > cta ? (n_btask - cta + NC - 1) / NC : 0;  // <= kPMaxMine (host-checked)
-  if (tid < mine) {
-    const int i = cta + tid * NC, a = i / n_ch;
-    s_ncols[tid] = static_cast<int>(ms->act_cnt[a]);
-    s_ch0[tid] = (i % n_ch) * 8;
-    for (int n = 0; n < kPMaxT; ++n) s_ent[tid][n] = ms->act_ent[a][n < static_cast<int>(ms->act_cnt[a]) ? n : 0];
-  }
-  if (tid < kPMaxT) s_ent[kPMaxMine][tid] = static_cast<uint32_t>((tid < T ? tid : 0) * (K + 1) + K);
   const int n_rpair = owns_rows ? n_act * nq : 0;  // routed down pairs of the CTA
   const int my_down = n_rpair > warp ? (n_rpair - warp + kPWarps - 1) / kPWarps : 0;
   const int n_units = j0 + mine + my_down;
@@ -1713,7 +2090,6 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     cp_async_commit();  // (an empty group keeps the pending count exact)
     ++issued;
   };
-  __syncthreads();  // s_ent / s_ncols / s_ch0 visible
 
   // ---- the shared-expert gate/up task (unit 0), loaded since the prologue
   if (owns_sgu) {
@@ -1767,22 +2143,139 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   }
   RNB_TRACE_MARK(p, 12);
 
-  bool timed_out = false;
   if (!owns_rows) {
     cp_async_wait_pending(0);
   } else {
-    // ---- down projection of rows [n0, n0 + 16): this warp's pairs (source,
-    // quarter): the shared expert's quarter `warp` (warp < nq, in this rank's
-    // share; tile in sSdn) and the routed pairs of its ring units, up to
-    // kDownBatch at a time.  For each batch the warp reads the pairs' h words (one round
-    // trip), converts them to fp16 with one power-of-two scale per 64-group
-    // (fp16_range_scale) into its fragment area, and runs the MMAs.
+    // ---- down projection of rows [n0, n0 + 16).  First the whole CTA polls
+    // every h word it needs (each warp until its own words are in) and
+    // converts it once: thread c takes 8-channel
+    // chunks c, c + 512, ... of the T (K + 1) entries (an entry's channels
+    // are 64 chunks; a 64-group is 8 chunks on 8 neighbouring lanes), with
+    // one power-of-two fp16 scale per (entry, group) (fp16_range_scale) and
+    // the group's sum, into the B fragments sHE[entry][group][32].  Entries
+    // whose expert is not on this rank, and shared-expert quarters outside
+    // this rank's share, are never produced and are skipped.  Then each warp
+    // runs its pairs (source, quarter): the shared expert's quarter `warp`
+    // (tile in sSdn) and the routed pairs of its ring units.
     const uint64_t deadline = gtimer() + kSpinLimitNs;
     const bool sh_unit = sh_down && warp < nq && ((qmask >> warp) & 1u);
     const int n_du = (sh_unit ? 1 : 0) + my_down;
-    cp_async_wait_pending(0);  // every tile of this warp (the shared-down group and the ring units)
-    __syncwarp();
+    const int n_ent = T * (K + 1), cpe = I / 8;  // entries, chunks per entry
+    uint32_t* sHE = reinterpret_cast<uint32_t*>(sm + off_hf);
+    float* sHs = reinterpret_cast<float*>(sHE + static_cast<size_t>(n_ent) * (I / 64) * 32);
+    float* sHi = sHs + n_ent * (I / 64);
     RNB_TRACE_MARK(p, 13);
+    {
+      constexpr int kMaxRounds = (kPMaxT * (kPMaxK + 1) * 64 + 32 * kPWarps - 1) / (32 * kPWarps);
+      uint64_t wv[kMaxRounds][8];
+      bool need[kMaxRounds];
+#pragma unroll
+      for (int r = 0; r < kMaxRounds; ++r) {
+        const int ch = tid + r * 32 * kPWarps, en = ch / cpe, k8 = ch % cpe;
+        bool nd = ch < n_ent * cpe;
+        if (nd) {
+          const int t = en / (K + 1), sl = en % (K + 1);
+          nd = sl < K ? is_local(ms->inds[t][sl]) : (sh_down && ((qmask >> (k8 / 16)) & 1u));
+        }
+        need[r] = nd;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wv[r][j] = static_cast<uint64_t>(epoch) << 32;  // (never polled)
+        if (nd) {
+          const uint2* src = hw + static_cast<size_t>(en) * I + k8 * 8;
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) xw_load2(src + j, wv[r][j], wv[r][j + 1]);
+        }
+      }
+      // words that did not yet carry this call's epoch are polled again, all
+      // of them per round trip, until they do (bounded)
+#ifdef RNB_TRACE
+      int polls = 0;
+#endif
+      for (;;) {
+#ifdef RNB_TRACE
+        ++polls;
+#endif
+        bool all = true;
+#pragma unroll
+        for (int r = 0; r < kMaxRounds; ++r) {
+          const int ch = tid + r * 32 * kPWarps;
+          const uint2* src = hw + static_cast<size_t>(ch / cpe) * I + (ch % cpe) * 8;
+#pragma unroll
+          for (int j = 0; j < 8; j += 2)
+            if (need[r] && (static_cast<uint32_t>(wv[r][j] >> 32) != epoch ||
+                            static_cast<uint32_t>(wv[r][j + 1] >> 32) != epoch)) {
+              all = false;
+              xw_load2(src + j, wv[r][j], wv[r][j + 1]);
+            }
+        }
+        // the warp leaves together (its lanes share 64-groups): once every
+        // lane has its words or is past the deadline (then the results are
+        // void; stale words are used as they are)
+        const bool late = !all && gtimer() > deadline;
+        if (late) timed_out = true;
+        if (__all_sync(0xffffffffu, all || late)) break;
+        __nanosleep(32);
+      }
+#ifdef RNB_TRACE
+      RNB_TRACE_MARK(p, 23);
+      if (tid == 0) trace_value(p, 30, polls);
+#endif
+      // convert: the 8 lanes of a 64-group share its scale and sum
+#pragma unroll
+      for (int r = 0; r < kMaxRounds; ++r) {
+        const int ch = tid + r * 32 * kPWarps;
+        if (r * 32 * kPWarps >= n_ent * cpe) break;  // CTA-uniform
+        float hv[8];
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          hv[j] = need[r] ? __uint_as_float(static_cast<uint32_t>(wv[r][j])) : 0.f;
+          m = fmaxf(m, fabsf(hv[j]));
+        }
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        float sc, inv;
+        fp16_range_scale(m, sc, inv);
+        const int en = ch / cpe, k8 = ch % cpe, grp = k8 >> 3;
+        float part = 0.f;
+        __half hh[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          hh[j] = __float2half_rn(hv[j] * sc);
+          part += __half2float(hh[j]);
+        }
+        // The chunk's 8 values fill 4 consecutive fragment words (pair_slot
+        // of positions 8 (k8 % 8) + j): word cq 8 + 4 (k8 % 2) + w holds
+        // values (w, w + 4) at 4 bits, (2w, 2w + 1) at 8 bits.  4-bit pairs
+        // 1 and 3 of a word (odd w) meet codes times 16 (subnormal form).
+        const int qk = (k8 & 7) >> 1;
+        const int cq = BITS == 8 ? qk : ((qk == 1) ? 2 : (qk == 2) ? 1 : qk);
+        uint32_t wd[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          __half lo = BITS == 8 ? hh[2 * w] : hh[w], hi = BITS == 8 ? hh[2 * w + 1] : hh[w + 4];
+          if (BITS == 4 && (w & 1)) {
+            lo = __hmul(lo, __float2half_rn(0.0625f));
+            hi = __hmul(hi, __float2half_rn(0.0625f));
+          }
+          wd[w] = static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+        }
+        if (ch < n_ent * cpe)
+          *reinterpret_cast<uint4*>(sHE + (static_cast<size_t>(en) * (I / 64) + grp) * 32 + cq * 8 + 4 * (k8 & 1)) =
+              make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        part += __shfl_xor_sync(0xffffffffu, part, 2);
+        part += __shfl_xor_sync(0xffffffffu, part, 4);
+        if ((k8 & 7) == 0 && ch < n_ent * cpe) {
+          sHs[en * (I / 64) + grp] = part;
+          sHi[en * (I / 64) + grp] = inv;
+        }
+      }
+    }
+    cp_async_wait_pending(0);  // every tile of this warp (the shared-down group and the ring units)
+    __syncthreads();
+    RNB_TRACE_MARK(p, 14);
     // unit b of this warp: tile, quarter, columns
     auto unit_of = [&](int b, const char*& tile, int& qq, uint32_t (&ent)[kPMaxT], int& ncols) {
       if (sh_unit && b == 0) {
@@ -1801,129 +2294,37 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
         for (int n = 0; n < kPMaxT; ++n) ent[n] = ms->act_ent[a][n < ncols ? n : 0];
       }
     };
-    for (int b0 = 0; b0 < n_du; b0 += kDownBatch) {
-      const int nb = n_du - b0 < kDownBatch ? n_du - b0 : kDownBatch;
-      const char* tile[kDownBatch];
-      int qq[kDownBatch], ncols[kDownBatch];
-      uint32_t ent[kDownBatch][kPMaxT];
-      uint64_t wv[kDownBatch][kPMaxT][4];
-#pragma unroll
-      for (int b = 0; b < kDownBatch; ++b) {
-        ncols[b] = 0;
-        if (b < nb) {
-          unit_of(b0 + b, tile[b], qq[b], ent[b], ncols[b]);
-#pragma unroll
-          for (int n = 0; n < kPMaxT; ++n)
-            if (n < ncols[b]) {
-              const uint2* src = hw + static_cast<size_t>(ent[b][n]) * I + qq[b] * 128 + lane * 4;
-#pragma unroll
-              for (int j = 0; j < 4; ++j) wv[b][n][j] = xw_load(src + j);
-            }
-        }
-      }
-      // words that did not yet carry this call's epoch are polled again, all
-      // of them per round trip, until they do (bounded)
-#ifdef RNB_TRACE
-      int polls = 0;
-#endif
-      for (;;) {
-#ifdef RNB_TRACE
-        ++polls;
-#endif
-        bool all = true;
-#pragma unroll
-        for (int b = 0; b < kDownBatch; ++b)
-#pragma unroll
-          for (int n = 0; n < kPMaxT; ++n)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              if (n < ncols[b] && static_cast<uint32_t>(wv[b][n][j] >> 32) != epoch) {
-                all = false;
-                wv[b][n][j] = xw_load(hw + static_cast<size_t>(ent[b][n]) * I + qq[b] * 128 + lane * 4 + j);
-              }
-        if (__all_sync(0xffffffffu, all)) break;
-        if (gtimer() > deadline) {
-          timed_out = true;
-          break;  // results void; stale words are used as they are
-        }
-        __nanosleep(32);
-      }
-#ifdef RNB_TRACE
-      if (b0 == 0) {
-        RNB_TRACE_MARK(p, 23);
-        if (tid == 0) trace_value(p, 30, polls);
-      }
-#endif
-      float inv_l[kDownBatch][kPMaxT][2], gs_l[kDownBatch][kPMaxT][2];
-#pragma unroll
-      for (int b = 0; b < kDownBatch; ++b) {
-        uint32_t* frag = sHf + b * (T * 64);
+#pragma unroll 1
+    for (int b = 0; b < n_du; ++b) {
+      const char* tile;
+      int qq, nc;
+      uint32_t ent[kPMaxT];
+      unit_of(b, tile, qq, ent, nc);
+      const int colB = g < nc ? g : 0;
+      const uint32_t* fB = sHE + (static_cast<size_t>(ent[colB]) * (I / 64) + 2 * qq) * 32 + c * 8;
+      const int h0 = static_cast<int>(ent[0]) * (I / 64) + 2 * qq;
+      const int h1 = static_cast<int>(ent[nc > 1 ? 1 : 0]) * (I / 64) + 2 * qq;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      tile2_mma<BITS>(
+          tile, g, c,
+          [&](int gi, uint32_t(&xb)[8]) {
+            const uint4 u0 = reinterpret_cast<const uint4*>(fB + gi * 32)[0];
+            const uint4 u1 = reinterpret_cast<const uint4*>(fB + gi * 32)[1];
+            xb[0] = u0.x; xb[1] = u0.y; xb[2] = u0.z; xb[3] = u0.w;
+            xb[4] = u1.x; xb[5] = u1.y; xb[6] = u1.z; xb[7] = u1.w;
+          },
+          [&](int gi, int col) { return (c == 0 && col < nc) ? sHs[(col ? h1 : h0) + gi] : 0.f; },
+          [&](int gi, int col) { return (c == 0 && col < nc) ? sHi[(col ? h1 : h0) + gi] : 0.f; }, acc);
+      if (c == 0) {
 #pragma unroll
         for (int n = 0; n < kPMaxT; ++n) {
-          inv_l[b][n][0] = inv_l[b][n][1] = gs_l[b][n][0] = gs_l[b][n][1] = 0.f;
-          if (n >= ncols[b]) continue;
-          // lane l: channels 128 qq + 4 l .. +3 of column n
-          float hv[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) hv[j] = __uint_as_float(static_cast<uint32_t>(wv[b][n][j]));
-          float m = fmaxf(fmaxf(fabsf(hv[0]), fabsf(hv[1])), fmaxf(fabsf(hv[2]), fabsf(hv[3])));
-#pragma unroll
-          for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          float sc, inv;
-          fp16_range_scale(m, sc, inv);
-          float part = 0.f;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const __half hh = __float2half_rn(hv[j] * sc);
-            part += __half2float(hh);
-            const int r = ((lane & 15) << 2) + j;  // position within the 64-group
-            int cq, ii, hf;
-            pair_slot<BITS>(r, cq, ii, hf);
-            // 4-bit pairs 1 and 3 of a word meet codes times 16 (subnormal form)
-            const __half hs = (BITS == 4 && (ii & 1)) ? __hmul(hh, __float2half_rn(0.0625f)) : hh;
-            reinterpret_cast<__half*>(frag + n * 64 + (lane >> 4) * 32 + cq * 8 + ii)[hf] = hs;
-          }
-#pragma unroll
-          for (int o = 1; o < 16; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-          // lane 0 holds group 0's sum and scale, lane 16 group 1's
-          inv_l[b][n][0] = __shfl_sync(0xffffffffu, inv, 0);
-          inv_l[b][n][1] = __shfl_sync(0xffffffffu, inv, 16);
-          gs_l[b][n][0] = __shfl_sync(0xffffffffu, part, 0);
-          gs_l[b][n][1] = __shfl_sync(0xffffffffu, part, 16);
-        }
-      }
-      __syncwarp();
-#pragma unroll
-      for (int b = 0; b < kDownBatch; ++b) {
-        if (ncols[b] == 0) continue;
-        const uint32_t* frag = sHf + b * (T * 64);
-        const int nc = ncols[b];
-        const int colB = g < nc ? g : 0;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        tile2_mma<BITS>(
-            tile[b], g, c,
-            [&](int gi, uint32_t(&xb)[8]) {
-              const uint32_t* fr = frag + colB * 64 + gi * 32 + c * 8;
-              const uint4 u0 = reinterpret_cast<const uint4*>(fr)[0];
-              const uint4 u1 = reinterpret_cast<const uint4*>(fr)[1];
-              xb[0] = u0.x; xb[1] = u0.y; xb[2] = u0.z; xb[3] = u0.w;
-              xb[4] = u1.x; xb[5] = u1.y; xb[6] = u1.z; xb[7] = u1.w;
-            },
-            [&](int gi, int col) { return c == 0 ? gs_l[b][col][gi] : 0.f; },
-            [&](int gi, int col) { return c == 0 ? inv_l[b][col][gi] : 0.f; }, acc);
-        if (c == 0) {
-#pragma unroll
-          for (int n = 0; n < kPMaxT; ++n) {
-            if (n < nc) {
-              float* dst = sRedC + (static_cast<size_t>(ent[b][n]) * nq + qq[b]) * 16;
-              dst[g] = n == 0 ? acc[0] : acc[1];
-              dst[g + 8] = n == 0 ? acc[2] : acc[3];
-            }
+          if (n < nc) {
+            float* dst = sRedC + (static_cast<size_t>(ent[n]) * nq + qq) * 16;
+            dst[g] = n == 0 ? acc[0] : acc[1];
+            dst[g + 8] = n == 0 ? acc[2] : acc[3];
           }
         }
       }
-      __syncwarp();  // the fragments are read before the next batch overwrites them
-      if (b0 == 0) RNB_TRACE_MARK(p, 14);
     }
     RNB_TRACE_MARK(p, 15);
     __syncthreads();
@@ -1976,6 +2377,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       emit(tid >> 6, (tid >> 2) & 15, acc);
     }
   }
+  }  // h-exchange form
   RNB_TRACE_MARK(p, 17);
   if (timed_out) atomicOr(p.ws.status, RNB_STATUS_TIMEOUT);
 
@@ -2059,6 +2461,7 @@ Ws bind(const Layout& L, void* ws) {
   w.seq = reinterpret_cast<uint32_t*>(b + L.status + kWsSeqOffset);
   w.lw = reinterpret_cast<uint2*>(b + L.xchg);
   w.hw = w.lw + kXchgLogitWords;
+  w.yw = w.hw + kXchgHWords;
   return w;
 }
 
@@ -2155,16 +2558,139 @@ size_t persistent_static_smem() {
   static size_t bytes = [] {
     cudaFuncAttributes fa;
     cudaFuncAttributes fb;
-    const bool ok = cudaFuncGetAttributes(&fa, k_decode<BITS, false>) == cudaSuccess &&
-                    cudaFuncGetAttributes(&fb, k_decode<BITS, true>) == cudaSuccess;
-    return ok ? (fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes) : size_t(2048);
+    cudaFuncAttributes fc;
+    const bool ok = cudaFuncGetAttributes(&fa, k_decode<BITS, false, false>) == cudaSuccess &&
+                    cudaFuncGetAttributes(&fb, k_decode<BITS, true, false>) == cudaSuccess &&
+                    cudaFuncGetAttributes(&fc, k_decode<BITS, false, true>) == cudaSuccess;
+    size_t m = fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes;
+    m = m > fc.sharedSizeBytes ? m : fc.sharedSizeBytes;
+    return ok ? m : size_t(2048);
   }();
   return bytes;
+}
+
+// Tensor maps of the split-K loads (SkMaps), encoded once per weight tensor
+// and shape and then served from a process-wide cache (encoding costs a few
+// microseconds of host time; decode calls repeat with the same weights).
+struct SkMapKey {
+  const void* base;
+  int kind, bits, E, H, I;
+  bool operator==(const SkMapKey& o) const {
+    return base == o.base && kind == o.kind && bits == o.bits && E == o.E && H == o.H && I == o.I;
+  }
+};
+struct SkMapKeyHash {
+  size_t operator()(const SkMapKey& k) const {
+    size_t h = reinterpret_cast<size_t>(k.base);
+    for (int v : {k.kind, k.bits, k.E, k.H, k.I}) h = h * 1000003u ^ static_cast<size_t>(v);
+    return h;
+  }
+};
+
+// kind 0: gate/up codes, 1: gate/up scales or biases, 2: down codes.
+bool sk_map(CUtensorMap* m, int kind, const void* base, int bits, int E, int H, int I) {
+  static std::mutex mu;
+  static std::unordered_map<SkMapKey, CUtensorMap, SkMapKeyHash> cache;
+  const SkMapKey key{base, kind, bits, E, H, I};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *m = it->second;
+      return true;
+    }
+  }
+  const uint64_t rowb = static_cast<uint64_t>(H) * bits / 8, I2 = 2ull * I, G = H / kGroup;
+  const uint64_t slice = 16ull * bits;  // a warp's K slice of a gate/up row (Tile2 row bytes)
+  bool ok = false;
+  if (kind == 0) {
+    const uint64_t dims[4] = {slice / 4, I2, static_cast<uint64_t>(H) * bits / 8 / slice, static_cast<uint64_t>(E)};
+    const uint64_t str[3] = {rowb, slice, I2 * rowb};
+    const uint32_t box[4] = {static_cast<uint32_t>(slice / 4), 32, static_cast<uint32_t>(dims[2]), 1};
+    ok = encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, base, dims, str, box,
+                      bits == 8 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  } else if (kind == 1) {
+    const uint64_t dims[3] = {G, I2, static_cast<uint64_t>(E)};
+    const uint64_t str[2] = {G * 2, I2 * G * 2};
+    const uint32_t box[3] = {static_cast<uint32_t>(G), 32, 1};
+    ok = encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else {
+    const uint64_t rw = static_cast<uint64_t>(I) * bits / 32;  // words per down row
+    const uint64_t dims[4] = {rw, 256, static_cast<uint64_t>(H) / 256, static_cast<uint64_t>(E)};
+    const uint64_t str[3] = {rw * 4, 256 * rw * 4, static_cast<uint64_t>(H) * rw * 4};
+    const uint32_t box[4] = {static_cast<uint32_t>(kSkC * bits / 32), 256, static_cast<uint32_t>(H / 256), 1};
+    ok = encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  if (!ok) return false;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, *m);
+  return true;
+}
+
+bool sk_maps(const Params& p, int bits, SkMaps& m) {
+  bool ok = sk_map(&m.gu_w, 0, p.gu_w, bits, p.E, p.H, p.I) && sk_map(&m.gu_s, 1, p.gu_s, bits, p.E, p.H, p.I) &&
+            sk_map(&m.gu_b, 1, p.gu_b, bits, p.E, p.H, p.I) && sk_map(&m.dn_w, 2, p.dn_w, bits, p.E, p.H, p.I);
+  if (ok && p.has_shared) {
+    ok = sk_map(&m.sgu_w, 0, p.sgu_w, bits, 1, p.H, p.I) && sk_map(&m.sgu_s, 1, p.sgu_s, bits, 1, p.H, p.I) &&
+         sk_map(&m.sgu_b, 1, p.sgu_b, bits, 1, p.H, p.I) && sk_map(&m.sdn_w, 2, p.sdn_w, bits, 1, p.H, p.I);
+  } else if (ok) {
+    m.sgu_w = m.gu_w;  // (never read without a shared expert)
+    m.sgu_s = m.gu_s;
+    m.sgu_b = m.gu_b;
+    m.sdn_w = m.dn_w;
+  }
+  return ok;
+}
+
+// Shared-memory plan of the split-K form: one token, the whole expert bank
+// on this GPU (no expert parallelism, the whole shared expert), and a CTA for
+// each of the 16 (k + 1) tasks.
+template <int BITS>
+bool persistent_plan_sk(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem) {
+  const int nq = p.I / 128;
+  if (p.mode != kModeBlock || p.T != 1 || p.ep_world > 1 || p.H != 2048 || p.I != 512 || p.E_total > 256 ||
+      p.k > kPMaxK || p.off != 0 || p.E != p.E_total || p.shared_qmask != (1u << nq) - 1u)
+    return false;
+  const int NC = di.sms;
+  if (NC < p.H / 16 || 2 * NC < p.E_total + 1) return false;
+  if (kSkTasksPerSource * (p.k + (p.has_shared ? 1 : 0)) > NC) return false;
+  using TL = Tile2<BITS>;
+  using SD = SkDown<BITS>;
+  const int G = p.H / kGroup;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = (o + bytes + 127) & ~static_cast<size_t>(127);
+    return static_cast<uint32_t>(at);
+  };
+  pl.sk = 1;
+  pl.S = 1;
+  pl.off_ring = 0;
+  pl.off_sdn = 0;
+  pl.off_x = take(static_cast<size_t>(G) * 32 * 4);
+  pl.off_xs = take(static_cast<size_t>(G) * 4);
+  pl.off_xn = p.norm_w ? take(static_cast<size_t>(p.H) * 2) : 0u;
+  pl.off_ivl = take(static_cast<size_t>(p.E_total + 1) * 4);
+  pl.off_red = take(static_cast<size_t>(kSkUnits) * kPWarps * 32 * 4);
+  pl.off_hf = pl.off_red;  // xprep's scratch (done before the partials are written)
+  pl.off_redc = 0;
+  pl.off_misc = take(sizeof(PMisc));
+  // the TMA destinations: up and gate codes, 4 scale / bias blocks, down codes
+  pl.off_tma = static_cast<uint32_t>(o);
+  o += 1023 + 2 * 16 * 32 * TL::kRowBytes + 4 * 32 * (p.H / kGroup) * 2 + static_cast<size_t>(p.H) * SD::kRow;
+  const size_t limit = static_cast<size_t>(di.smem_optin) - persistent_static_smem<BITS>();
+  smem = o;
+  if (smem > limit) return false;
+  SkMaps probe;  // (cached: the launch reuses them)
+  return sk_maps(p, BITS, probe);
 }
 
 // Shared-memory plan of k_decode; false when the call does not fit it.
 template <int BITS>
 bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem) {
+  if (persistent_plan_sk<BITS>(p, di, pl, smem)) return true;
+  pl.sk = 0;
   if (p.mode != kModeBlock || p.T < 1 || p.T > kPMaxT || p.H != 2048 || p.I != 512 || p.E_total > 256 ||
       p.k > kPMaxK || p.off < 0 || p.off + p.E > p.E_total)
     return false;
@@ -2190,7 +2716,9 @@ bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem
   pl.off_xn = p.norm_w ? take(static_cast<size_t>(T) * p.H * 2) : 0u;
   pl.off_ivl = take(static_cast<size_t>(T) * (p.E_total + 1) * 4);
   pl.off_red = take(static_cast<size_t>(1 + mine_max) * kPWarps * 32 * 4);
-  pl.off_hf = take(std::max<size_t>(static_cast<size_t>(kPWarps) * kDownBatch * T * 64 * 4, 4096));  // also xprep's scratch
+  // the down MMAs' B fragments of every entry (fp16, [T(k+1)][I/64][32] words)
+  // with a sum and an inverse scale per (entry, group); also xprep's scratch
+  pl.off_hf = take(std::max<size_t>(static_cast<size_t>(T) * (p.k + 1) * (p.I / 64) * (32 + 2) * 4, 4096));
   pl.off_redc = take(static_cast<size_t>(T) * (p.k + 1) * nq * 16 * 4);
   pl.off_misc = take(sizeof(PMisc));
   const size_t limit = static_cast<size_t>(di.smem_optin) - persistent_static_smem<BITS>();
@@ -2212,7 +2740,11 @@ bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem
 // its griddepcontrol.wait holds everything else back.
 template <int BITS>
 int run_persistent(Params& p, const PPlan& pl, size_t smem, int nc, cudaStream_t st) {
-  auto kern = p.ep_world > 1 ? k_decode<BITS, true> : k_decode<BITS, false>;
+  auto kern = p.ep_world > 1 ? k_decode<BITS, true, false>
+                             : (pl.sk ? k_decode<BITS, false, true> : k_decode<BITS, false, false>);
+  SkMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (pl.sk && !sk_maps(p, BITS, maps)) return fail(RNB_ERR_CUDA, "k_decode: tensor map encoding failed");
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_decode smem attribute: ") + cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
@@ -2226,7 +2758,7 @@ int run_persistent(Params& p, const PPlan& pl, size_t smem, int nc, cudaStream_t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   stage_begin(st);
-  e = cudaLaunchKernelEx(&cfg, kern, p, pl);
+  e = cudaLaunchKernelEx(&cfg, kern, p, pl, maps);
   if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("k_decode launch: ") + cudaGetErrorString(e));
   stage_end(st, RNB_STAGE_DECODE);
   return RNB_OK;
@@ -2345,7 +2877,7 @@ namespace rnb {
 // Scratch for rnb_moe_block_fwd_noalloc: a file-scope device array, so a
 // caller that cannot allocate device memory still gets the workspace the
 // kernels need.  Every GPU that loads this library holds it until exit.
-constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB; Ornith shapes need 7.2 MB
+constexpr size_t kNoAllocScratchBytes = 12u << 20;  // 12 MiB; Ornith shapes need 9.6 MB
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // Device address of g_noalloc_scratch on the current device.  The host-side
@@ -2842,11 +3374,9 @@ int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* x, void*
     const DevInfo di = dev_info();
     PPlan pl;
     size_t smem = 0;
+    set_ep(p);  // (before the plan: the split-K form is for one GPU only)
     const bool ok = d->bits == 8 ? persistent_plan<8>(p, di, pl, smem) : persistent_plan<4>(p, di, pl, smem);
-    if (ok) {
-      set_ep(p);
-      return d->bits == 8 ? run_persistent<8>(p, pl, smem, di.sms, st) : run_persistent<4>(p, pl, smem, di.sms, st);
-    }
+    if (ok) return d->bits == 8 ? run_persistent<8>(p, pl, smem, di.sms, st) : run_persistent<4>(p, pl, smem, di.sms, st);
   }
   // Otherwise per 64-token chunk: the decode chain writes this rank's fp32
   // partial (shared expert on rank 0), then k_ep_reduce exchanges and sums.

@@ -1,6 +1,7 @@
 // rnb_internal.h -- host-side helpers shared by the decode and prefill units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -15,6 +16,13 @@ namespace rnb {
 int fail(int code, const std::string& msg);
 bool aligned16(const void* p);
 bool has_shared(const rnb_moe_desc* d);
+
+// A tiled TMA tensor map of `rank` dimensions (innermost first): dims in
+// elements, strides in bytes for dimensions 1 .. rank-1, box in elements.
+// Uses the driver's encoder through the runtime (no link against the
+// driver).  False when the encoder is missing or rejects the description.
+bool encode_tiled(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+                  const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle sw);
 
 struct DevInfo {
   int sms = 0;
@@ -37,10 +45,12 @@ constexpr size_t kWsSeqOffset = 64;
 // After the counters, both layouts reserve the persistent decode kernel's
 // exchange words: 8-byte {value, epoch} words that only that kernel writes
 // (an epoch is a sequence number, so no other path may leave data there):
-// router logits [2 tokens][257 rows] and SwiGLU rows [2 tokens][9 slots][512].
+// router logits [2 tokens][257 rows], SwiGLU rows [2 tokens][9 slots][512]
+// and the one-token split-K partials [16 tasks x 9 sources][2048 rows].
 constexpr size_t kXchgLogitWords = 2 * 257;
 constexpr size_t kXchgHWords = 2 * 9 * 512;
-constexpr size_t kXchgBytes = 8 * (kXchgLogitWords + kXchgHWords);
+constexpr size_t kXchgYWords = 16 * 9 * 2048;
+constexpr size_t kXchgBytes = 8 * (kXchgLogitWords + kXchgHWords + kXchgYWords);
 
 // Stage timing (rnb_timing.cu): no-ops unless rnb_stage_timing(1) was called.
 void stage_begin(cudaStream_t st);

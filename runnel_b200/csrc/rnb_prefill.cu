@@ -1133,6 +1133,26 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+}  // namespace pre
+
+bool encode_tiled(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+                  const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle sw) {
+  const pre::EncodeTiledFn enc = pre::encode_fn();
+  if (!enc || rank < 1 || rank > 5) return false;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  return enc(m, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace pre {
+
 // 2-D tensor map over a row-major [rows][inner] array (inner in elements).
 bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
                uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {

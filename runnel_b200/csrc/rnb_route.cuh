@@ -251,27 +251,39 @@ __device__ __forceinline__ double warp_dot_router_f64(const uint16_t* x, const R
   return warp_dot_f64(x, rs.w + static_cast<size_t>(e) * H, H, lane);
 }
 
-// The K largest of the warp's keys (8 per lane, unique, 0 = empty): lane
-// s < K receives the s-th in `mine`; returns the K-th.  One redux per pick.
+// Compare-exchange for a descending order: a keeps the larger key.
+__device__ __forceinline__ void cas_desc(uint32_t& a, uint32_t& b) {
+  const uint32_t hi = max(a, b), lo = min(a, b);
+  a = hi;
+  b = lo;
+}
+
+// The K largest (K <= 16) of the warp's keys (8 per lane, unique, 0 =
+// empty): lane s < K receives the s-th in `mine`; returns the K-th.  Each
+// lane first sorts its 8 keys (Batcher's 19-comparator network, no
+// cross-lane traffic); then every pick is one redux over the lanes' heads,
+// and the lane that owned the winner shifts its list by one (branch-free).
 __device__ __forceinline__ uint32_t warp_select_k(const uint32_t (&keys)[8], int K, int lane, uint32_t& mine) {
-  uint32_t k2[8], best = 0, w = 0;
+  uint32_t a[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    k2[i] = keys[i];
-    best = max(best, k2[i]);
-  }
+  for (int i = 0; i < 8; ++i) a[i] = keys[i];
+  cas_desc(a[0], a[1]); cas_desc(a[2], a[3]); cas_desc(a[4], a[5]); cas_desc(a[6], a[7]);
+  cas_desc(a[0], a[2]); cas_desc(a[1], a[3]); cas_desc(a[4], a[6]); cas_desc(a[5], a[7]);
+  cas_desc(a[1], a[2]); cas_desc(a[5], a[6]);
+  cas_desc(a[0], a[4]); cas_desc(a[1], a[5]); cas_desc(a[2], a[6]); cas_desc(a[3], a[7]);
+  cas_desc(a[2], a[4]); cas_desc(a[3], a[5]);
+  cas_desc(a[1], a[2]); cas_desc(a[3], a[4]); cas_desc(a[5], a[6]);
+  uint32_t w = 0;
   mine = 0;
-#pragma unroll 1
-  for (int slot = 0; slot < K; ++slot) {
-    w = __reduce_max_sync(0xffffffffu, best);
-    if (lane == slot) mine = w;
-    if (best == w) {
-      best = 0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        k2[i] = k2[i] == w ? 0u : k2[i];
-        best = max(best, k2[i]);
-      }
+  for (int slot = 0; slot < 16; ++slot) {
+    if (slot < K) {  // K is warp-uniform
+      w = __reduce_max_sync(0xffffffffu, a[0]);
+      mine = lane == slot ? w : mine;
+      const bool hit = a[0] == w;  // keys are unique: one lane at most
+#pragma unroll
+      for (int i = 0; i < 7; ++i) a[i] = hit ? a[i + 1] : a[i];
+      a[7] = hit ? 0u : a[7];
     }
   }
   return w;
@@ -344,7 +356,15 @@ __device__ __forceinline__ int warp_route_token_body(const uint32_t* ivl, int Et
   }
   const float mx = route_key_value(__shfl_sync(0xffffffffu, mine, 0));
   const float pw = lane < K ? expf(route_key_value(mine) - mx) : 0.f;
-  const float selsum = warp_sum(pw);
+  // the sum of the K terms (lanes < K), by a butterfly over as few lanes as K needs
+  float selsum = pw;
+  selsum += __shfl_xor_sync(0xffffffffu, selsum, 1);
+  selsum += __shfl_xor_sync(0xffffffffu, selsum, 2);
+  selsum += __shfl_xor_sync(0xffffffffu, selsum, 4);
+  if (K > 8) {  // warp-uniform
+    selsum += __shfl_xor_sync(0xffffffffu, selsum, 8);
+    selsum += __shfl_xor_sync(0xffffffffu, selsum, 16);
+  }
   *e_out = route_key_expert(mine);
   *score_out = pw / selsum;
   return n_exact;

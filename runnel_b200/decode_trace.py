@@ -25,10 +25,10 @@ from . import _lib
 TRACE_LIB = os.path.join(os.path.dirname(os.path.abspath(__file__)), "librnb_moe_trace.so")
 
 NAMES = {0: "start", 1: "prologue", 2: "griddep", 3: "router", 4: "xprep", 5: "sh-gateup", 6: "logits",
-         7: "routed", 8: "tasks", 9: "gu-wait0", 10: "gu-mma0", 11: "gu-done", 12: "gu-epi", 13: "sh-down",
-         14: "dn-unit0", 15: "dn-done", 16: "dn-sync", 17: "end", 18: "route-body", 19: "combine",
-         20: "act-list", 21: "pre-issue", 22: "issued", 23: "dn-poll0"}
-VALUES = {30: "h-word polls of the first down batch (thread 0)", 31: "exact router recomputes (CTA 0)"}
+         7: "routed", 8: "tasks", 9: "gu-wait0", 10: "gu-mma0", 11: "gu-done", 12: "gu-epi", 13: "dn-start",
+         14: "h-conv", 15: "dn-done", 16: "dn-sync", 17: "end", 18: "route-body", 19: "combine",
+         20: "task-list", 21: "pre-issue", 22: "issued", 23: "h-polled"}
+VALUES = {30: "h-word poll rounds of the down phase (thread 0)", 31: "exact router recomputes (CTA 0)"}
 
 
 def summarise(tr: np.ndarray) -> list[str]:
