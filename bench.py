@@ -70,7 +70,8 @@ def step_bytes(bits, distinct_experts, T, H=2048, I=512, E=256, shared=True):
 # DRAM bytes (read + write) per step of the dominant kernel, from one ncu
 # capture of the same workload (profiles/ holds the summary and the command).
 MEASURED_TRAFFIC = {
-    "config2 q4 decode T=1": (17_090_560, "profiles/k_decode_q4_T1.md"),
+    "config1 q8 decode T=1": (31_422_720, "profiles/k_decode_q8_T1.md"),
+    "config2 q4 decode T=1": (17_211_648, "profiles/k_decode_q4_T1.md"),
     "config3 q8 prefill T=2048": (577_900_000, "profiles/k_pre_gemm_q8_T2048.md"),
     "config5 q8 prefill T=16384": (2_400_000_000, "profiles/k_pre_gemm_q8_T16384.md"),
 }
