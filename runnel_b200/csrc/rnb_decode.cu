@@ -1931,20 +1931,28 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       RNB_TRACE_MARK(p, 9);
       if (!mbar_wait(&sk_bar[0], 0, kSpinLimitNs)) timed_out = true;
       RNB_TRACE_MARK(p, 10);
+      // the token's B fragments and group sums of this warp's two groups,
+      // the same for every tile
       const int g0 = warp * 2;
-#pragma unroll 1
+      uint32_t xbr[2][8];
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi) {
+        const uint4* src = reinterpret_cast<const uint4*>(sX + static_cast<size_t>(g0 + gi) * 32 + c * 8);
+        const uint4 u0 = src[0], u1 = src[1];
+        xbr[gi][0] = u0.x; xbr[gi][1] = u0.y; xbr[gi][2] = u0.z; xbr[gi][3] = u0.w;
+        xbr[gi][4] = u1.x; xbr[gi][5] = u1.y; xbr[gi][6] = u1.z; xbr[gi][7] = u1.w;
+      }
+      const float xs0 = sXs[g0], xs1 = sXs[g0 + 1];
+#pragma unroll
       for (int u = 0; u < kSkUnits; ++u) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         sk_gu_mma<BITS>(
             sGu, sGu + kSkGuBox, sGsb, G, u, warp, g, c,
             [&](int gi, uint32_t(&xb)[8]) {
-              const uint32_t* src = sX + static_cast<size_t>(g0 + gi) * 32 + c * 8;
-              const uint4 u0 = reinterpret_cast<const uint4*>(src)[0];
-              const uint4 u1 = reinterpret_cast<const uint4*>(src)[1];
-              xb[0] = u0.x; xb[1] = u0.y; xb[2] = u0.z; xb[3] = u0.w;
-              xb[4] = u1.x; xb[5] = u1.y; xb[6] = u1.z; xb[7] = u1.w;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) xb[i] = gi ? xbr[1][i] : xbr[0][i];
             },
-            [&](int gi, int) { return sXs[g0 + gi]; }, [](int, int) { return 1.0f; }, acc);
+            [&](int gi, int) { return gi ? xs1 : xs0; }, [](int, int) { return 1.0f; }, acc);
         store_partials(u, acc);
       }
       RNB_TRACE_MARK(p, 11);
