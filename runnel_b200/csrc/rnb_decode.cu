@@ -1598,11 +1598,10 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   char* sDnA = skb + 2 * kSkGuBox + 4 * kSkSbBox;
   char* sDn = sDnA + static_cast<size_t>(warp) * SD::kBytes;  // (split-K) this warp's down rows
   uint32_t sk_sw[4], sk_bw[4];  // (split-K) this lane's down rows' scale and bias words
-  // (split-K) the task's loads: thread 0 issues the TMA requests (gate/up
-  // codes, scales and biases on barrier 0; the down codes on barrier 1),
-  // every lane loads its down rows' scale and bias words
-  auto sk_issue_all = [&](bool shared, int e, const uint16_t* ds, const uint16_t* db) {
-    if (tid == 0) {
+  // (split-K) the task's TMA requests, by one thread: gate/up codes, scales
+  // and biases on barrier 0; the down codes on barrier 1
+  auto sk_issue_tma = [&](bool shared, int e) {
+    {
       const CUtensorMap* mw = shared ? &skm.sgu_w : &skm.gu_w;
       const CUtensorMap* msc = shared ? &skm.sgu_s : &skm.gu_s;
       const CUtensorMap* mbi = shared ? &skm.sgu_b : &skm.gu_b;
@@ -1619,7 +1618,6 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       mbar_arrive_expect_tx(&sk_bar[1], static_cast<uint32_t>(H) * SD::kRow);
       tma_load_4d(smem_u32(sDnA), md, sk_j * BITS, 0, 0, e, b1);
     }
-    sk_down_sb(ds, db, I, warp * 128, sk_j, lane, sk_sw, sk_bw);
   };
   const int j0 = owns_sgu ? 1 : 0;  // ring unit 0: this warp's slice of the shared-expert gate/up task
   auto gu_row = [&](int ch0) { return [=](int i) -> size_t { return i < 8 ? ch0 + i : I + ch0 + i - 8; }; };
@@ -1799,7 +1797,10 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   RNB_TRACE_MARK(p, 3);
   // (split-K) the shared expert's tasks know their weights: load them now,
   // once this CTA's router rows are out (they are on every CTA's path)
-  if (sk_shared) sk_issue_all(true, 0, p.sdn_s, p.sdn_b);
+  if (sk_shared) {
+    if (tid == 0) sk_issue_tma(true, 0);
+    sk_down_sb(p.sdn_s, p.sdn_b, I, warp * 128, sk_j, lane, sk_sw, sk_bw);
+  }
   // (the B-fragment area is free until the down phase: 4 KB of it are xprep's scratch)
   xprep_cta<BITS>(xin, T, sX, sXs, ms->xinv, reinterpret_cast<__half*>(sm + off_hf), ms->red);
   RNB_TRACE_MARK(p, 4);
@@ -1860,6 +1861,13 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       ms->scores[t][lane] = sc;
     }
     if (lane == 0) ms->sg[t] = p.has_shared ? 1.0f / (1.0f + expf(-__uint_as_float(sIvl[t * (Et + 1) + Et]))) : 0.f;
+    if (SK) {
+      // (split-K, one token) the routing warp issues its task's loads at once
+      const int es = __shfl_sync(0xffffffffu, e, sk_src < K ? sk_src : 0);
+      RNB_TRACE_MARK(p, 21);
+      if (sk_task && !sk_shared && lane == 0) sk_issue_tma(false, es - p.off);
+      RNB_TRACE_MARK(p, 22);
+    }
     // the routing warps meet (warp 0 reads every token's selection); the
     // rest of the CTA waits at the one CTA barrier below
     if (T > 1)
@@ -1871,8 +1879,9 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   // Warp 0: the active local experts in (token, slot) order of first use,
   // with their columns (lane i < T*K holds entry i; lanes holding the same
   // expert find each other with one match, the expert's index is the number
-  // of first occurrences before its first lane), then the CTA's task list.
-  if (warp == 0) {
+  // of first occurrences before its first lane), then the CTA's task list
+  // (the h-exchange form only).
+  if (!SK && warp == 0) {
     const bool act = lane < T * K;
     const uint32_t e = act ? ms->inds[lane / K][lane % K] : 0xFFFFFFFFu;
     const bool loc = act && is_local(e);
@@ -1920,12 +1929,11 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     if (sk_task) {
       float wgt = ms->sg[0];
       if (!sk_shared) {
+        // (the TMA requests went out from the routing warp)
         const uint32_t le = ms->inds[0][sk_src] - static_cast<uint32_t>(p.off);
         const size_t dse = static_cast<size_t>(H) * dsrow;
         wgt = ms->scores[0][sk_src];
-        RNB_TRACE_MARK(p, 21);
-        sk_issue_all(false, static_cast<int>(le), p.dn_s + le * dse, p.dn_b + le * dse);
-        RNB_TRACE_MARK(p, 22);
+        sk_down_sb(p.dn_s + le * dse, p.dn_b + le * dse, I, warp * 128, sk_j, lane, sk_sw, sk_bw);
       }
       // gate/up: the four 8-channel tiles, once the task's TMA loads are in
       RNB_TRACE_MARK(p, 9);
