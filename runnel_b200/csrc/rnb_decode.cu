@@ -1205,8 +1205,8 @@ constexpr int kSkTasksPerSource = 512 / kSkC;
 
 // TMA descriptors of the split-K loads (host-encoded, cached per tensor).
 // Gate/up codes: 4-D {a warp's K slice (Tile2 row bytes, as u32), 2I rows,
-// 16 slices, experts}, box {slice, 32 rows, 16 slices, 1}: one request puts
-// a task's 32 up (or gate) rows in shared memory as [slice][32 rows][slice
+// 16 slices, experts}, box {slice, 8 rows, 16 slices, 1}: one request puts
+// one tile's 8 up (or gate) rows in shared memory as [slice][8 rows][slice
 // bytes], swizzled (64 B or 128 B) so that the MMA reads are conflict-free.
 // Gate/up scales and biases: 3-D {H/64 groups, 2I rows, experts}, box
 // {H/64, 32, 1}.  Down codes: 4-D {row words, 256 rows, H/256 blocks,
@@ -1485,15 +1485,15 @@ __device__ __forceinline__ int sk_swz_chunk(int r, int ch) {
 
 // acc (rows g: up channel 8u + g, g + 8: gate channel 8u + g; columns 2c,
 // 2c + 1) += affine(tile . B) over this warp's two groups, from the
-// TMA-loaded blocks: up / gate codes [16 slices][32 rows][Tile2 row bytes],
+// TMA-loaded blocks: up / gate codes [4 tiles][16 slices][8 rows][Tile2 row bytes],
 // sb = [up scales | gate scales | up biases | gate biases], each [32 rows][H/64].
 template <int BITS, typename BFrag, typename GSum, typename GInv>
 __device__ __forceinline__ void sk_gu_mma(const char* up, const char* gate, const uint16_t* sb, int G, int u, int w,
                                           int g, int c, BFrag bfrag, GSum gsum, GInv ginv, float (&acc)[4]) {
   using TL = Tile2<BITS>;
   const int r = 8 * u + g;
-  const char* ua = up + (w * 32 + r) * TL::kRowBytes;
-  const char* ga = gate + (w * 32 + r) * TL::kRowBytes;
+  const char* ua = up + (u * 128 + w * 8 + g) * TL::kRowBytes;
+  const char* ga = gate + (u * 128 + w * 8 + g) * TL::kRowBytes;
   const int q = (c == 1) ? 2 : (c == 2) ? 1 : c;
 #pragma unroll
   for (int gi = 0; gi < 2; ++gi) {
@@ -1532,10 +1532,11 @@ __device__ __forceinline__ void sk_gu_mma(const char* up, const char* gate, cons
 template <int BITS, bool EP, bool SK>
 __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan pl, const __grid_constant__ SkMaps skm) {
   extern __shared__ __align__(16) char sm[];
-  __shared__ __align__(8) uint64_t sk_bar[2];  // (split-K) gate/up and down TMA phases
+  // (split-K) TMA phases: gate/up tiles 0..3 (tile 0 with the scales and
+  // biases), then the down codes
+  __shared__ __align__(8) uint64_t sk_bar[kSkUnits + 1];
   if (SK && threadIdx.x == 0) {
-    mbar_init(&sk_bar[0], 1);
-    mbar_init(&sk_bar[1], 1);
+    for (int i = 0; i <= kSkUnits; ++i) mbar_init(&sk_bar[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   // The parameters are read from a shared-memory copy: a kernel parameter
@@ -1588,9 +1589,10 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   const bool sk_task = SK && (sk_src < K || sk_shared);
   using SD = SkDown<BITS>;
   // (split-K) TMA destinations, from the first 1024-byte boundary at or after
-  // off_tma: up and gate codes [16 slices][32 rows][Tile2 row bytes] each,
-  // their scales and biases, the down codes [H][slice bytes]
+  // off_tma: up and gate codes, [tile 4][16 slices][8 rows][Tile2 row bytes]
+  // each, their scales and biases, the down codes [H][slice bytes]
   constexpr uint32_t kSkGuBox = 16u * 32u * TL::kRowBytes;
+  constexpr uint32_t kSkGuTile = kSkGuBox / kSkUnits;
   constexpr uint32_t kSkSbBox = 32u * 32u * 2u;  // 32 rows x H/64 groups (H = 2048)
   char* skb = sm + pl.off_tma + (1024u - (smem_u32(sm) + pl.off_tma) % 1024u) % 1024u;
   char* sGu = skb;
@@ -1606,16 +1608,22 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       const CUtensorMap* msc = shared ? &skm.sgu_s : &skm.gu_s;
       const CUtensorMap* mbi = shared ? &skm.sgu_b : &skm.gu_b;
       const CUtensorMap* md = shared ? &skm.sdn_w : &skm.dn_w;
-      const uint32_t b0 = smem_u32(&sk_bar[0]), b1 = smem_u32(&sk_bar[1]);
+      const uint32_t b0 = smem_u32(&sk_bar[0]), b1 = smem_u32(&sk_bar[kSkUnits]);
       const int r0 = sk_j * kSkC;
-      mbar_arrive_expect_tx(&sk_bar[0], 2 * kSkGuBox + 4 * kSkSbBox);
+      mbar_arrive_expect_tx(&sk_bar[0], 2 * kSkGuTile + 4 * kSkSbBox);
       tma_load_4d(smem_u32(sGu), mw, 0, r0, 0, e, b0);
       tma_load_4d(smem_u32(sGu + kSkGuBox), mw, 0, I + r0, 0, e, b0);
       tma_load_3d(smem_u32(sGsb), msc, 0, r0, e, b0);
       tma_load_3d(smem_u32(sGsb + 1 * kSkSbBox / 2), msc, 0, I + r0, e, b0);
       tma_load_3d(smem_u32(sGsb + 2 * kSkSbBox / 2), mbi, 0, r0, e, b0);
       tma_load_3d(smem_u32(sGsb + 3 * kSkSbBox / 2), mbi, 0, I + r0, e, b0);
-      mbar_arrive_expect_tx(&sk_bar[1], static_cast<uint32_t>(H) * SD::kRow);
+      for (int u = 1; u < kSkUnits; ++u) {
+        const uint32_t bu = smem_u32(&sk_bar[u]);
+        mbar_arrive_expect_tx(&sk_bar[u], 2 * kSkGuTile);
+        tma_load_4d(smem_u32(sGu + u * kSkGuTile), mw, 0, r0 + 8 * u, 0, e, bu);
+        tma_load_4d(smem_u32(sGu + kSkGuBox + u * kSkGuTile), mw, 0, I + r0 + 8 * u, 0, e, bu);
+      }
+      mbar_arrive_expect_tx(&sk_bar[kSkUnits], static_cast<uint32_t>(H) * SD::kRow);
       tma_load_4d(smem_u32(sDnA), md, sk_j * BITS, 0, 0, e, b1);
     }
   };
@@ -1935,10 +1943,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
         wgt = ms->scores[0][sk_src];
         sk_down_sb(p.dn_s + le * dse, p.dn_b + le * dse, I, warp * 128, sk_j, lane, sk_sw, sk_bw);
       }
-      // gate/up: the four 8-channel tiles, once the task's TMA loads are in
+      // gate/up: the four 8-channel tiles, each once its TMA loads are in
       RNB_TRACE_MARK(p, 9);
-      if (!mbar_wait(&sk_bar[0], 0, kSpinLimitNs)) timed_out = true;
-      RNB_TRACE_MARK(p, 10);
       // the token's B fragments and group sums of this warp's two groups,
       // the same for every tile
       const int g0 = warp * 2;
@@ -1953,6 +1959,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       const float xs0 = sXs[g0], xs1 = sXs[g0 + 1];
 #pragma unroll
       for (int u = 0; u < kSkUnits; ++u) {
+        if (!mbar_wait(&sk_bar[u], 0, kSpinLimitNs)) timed_out = true;
+        if (u == 0) RNB_TRACE_MARK(p, 10);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         sk_gu_mma<BITS>(
             sGu, sGu + kSkGuBox, sGsb, G, u, warp, g, c,
@@ -2002,7 +2010,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
           ms->skhinv = inv;
         }
       }
-      if (!mbar_wait(&sk_bar[1], 0, kSpinLimitNs)) timed_out = true;  // the down codes
+      if (!mbar_wait(&sk_bar[kSkUnits], 0, kSpinLimitNs)) timed_out = true;  // the down codes
       __syncthreads();
       RNB_TRACE_MARK(p, 12);
       uint2* ydst = yw + static_cast<size_t>(cta) * H + warp * 128;
@@ -2622,7 +2630,7 @@ bool sk_map(CUtensorMap* m, int kind, const void* base, int bits, int E, int H, 
   if (kind == 0) {
     const uint64_t dims[4] = {slice / 4, I2, static_cast<uint64_t>(H) * bits / 8 / slice, static_cast<uint64_t>(E)};
     const uint64_t str[3] = {rowb, slice, I2 * rowb};
-    const uint32_t box[4] = {static_cast<uint32_t>(slice / 4), 32, static_cast<uint32_t>(dims[2]), 1};
+    const uint32_t box[4] = {static_cast<uint32_t>(slice / 4), 8, static_cast<uint32_t>(dims[2]), 1};
     ok = encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, base, dims, str, box,
                       bits == 8 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   } else if (kind == 1) {
