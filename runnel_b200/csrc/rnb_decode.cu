@@ -1567,7 +1567,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   const size_t dwrow = static_cast<size_t>(I) * BITS / 32, dsrow = I / kGroup;
   const int n_ch = I / 8;  // gate/up tasks per expert
   const int nq = I / 128;  // down K quarters
-  uint2* lw = p.ws.lw;     // [T][Et + 1] logit words
+  uint2* lw = p.ws.lw;     // [T][Et + 1] logit words, one per 128-byte line
   uint2* hw = p.ws.hw;     // [T][K + 1][I] h words
   const uint32_t e_off = static_cast<uint32_t>(p.off), e_cnt = static_cast<uint32_t>(p.E);
   auto is_local = [&](uint32_t e) { return e - e_off < e_cnt; };
@@ -1797,7 +1797,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
         // expert rows: candidate interval of the bf16 logit; last row: fp32 shared-gate logit
         if (lane == 0) {
           const uint32_t val = row < Et ? route_interval_f64(a0, a3, a4, a1, a2) : __float_as_uint(static_cast<float>(a0));
-          xw_store(lw + static_cast<size_t>(t) * (Et + 1) + row, val, epoch);
+          xw_store(lw + (static_cast<size_t>(t) * (Et + 1) + row) * kLwStride, val, epoch);
         }
       }
     }
@@ -1848,7 +1848,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   // ---- routing (every CTA, redundantly): poll the logit words
   {
     const uint64_t deadline = gtimer() + kSpinLimitNs;
-    for (int i = tid; i < T * (Et + 1); i += blockDim.x) sIvl[i] = xw_wait(lw + i, epoch, deadline, p.ws.status);
+    for (int i = tid; i < T * (Et + 1); i += blockDim.x)
+      sIvl[i] = xw_wait(lw + static_cast<size_t>(i) * kLwStride, epoch, deadline, p.ws.status);
   }
   __syncthreads();
   RNB_TRACE_MARK(p, 6);

@@ -47,7 +47,10 @@ constexpr size_t kWsSeqOffset = 64;
 // (an epoch is a sequence number, so no other path may leave data there):
 // router logits [2 tokens][257 rows], SwiGLU rows [2 tokens][9 slots][512]
 // and the one-token split-K partials [16 tasks x 9 sources][2048 rows].
-constexpr size_t kXchgLogitWords = 2 * 257;
+// Each logit word has a 128-byte line of its own: every CTA polls all of
+// them, and packed into a few lines the polls would queue at a few L2 slices.
+constexpr size_t kLwStride = 16;
+constexpr size_t kXchgLogitWords = 2 * 257 * kLwStride;
 constexpr size_t kXchgHWords = 2 * 9 * 512;
 constexpr size_t kXchgYWords = 16 * 9 * 2048;
 constexpr size_t kXchgBytes = 8 * (kXchgLogitWords + kXchgHWords + kXchgYWords);
