@@ -1600,31 +1600,30 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   char* sDnA = skb + 2 * kSkGuBox + 4 * kSkSbBox;
   char* sDn = sDnA + static_cast<size_t>(warp) * SD::kBytes;  // (split-K) this warp's down rows
   uint32_t sk_sw[4], sk_bw[4];  // (split-K) this lane's down rows' scale and bias words
-  // (split-K) the task's TMA requests, by one thread: gate/up codes, scales
-  // and biases on barrier 0; the down codes on barrier 1
-  auto sk_issue_tma = [&](bool shared, int e) {
-    {
+  // (split-K) the task's TMA requests, by lanes 0 .. kSkUnits of one warp,
+  // each the sole arrival on its barrier: lane u < kSkUnits the codes of
+  // gate/up tile u (lane 0 also the scales and biases), lane kSkUnits the
+  // down codes
+  auto sk_issue_tma = [&](bool shared, int e, int ln) {
+    const int r0 = sk_j * kSkC;
+    if (ln < kSkUnits) {
       const CUtensorMap* mw = shared ? &skm.sgu_w : &skm.gu_w;
-      const CUtensorMap* msc = shared ? &skm.sgu_s : &skm.gu_s;
-      const CUtensorMap* mbi = shared ? &skm.sgu_b : &skm.gu_b;
-      const CUtensorMap* md = shared ? &skm.sdn_w : &skm.dn_w;
-      const uint32_t b0 = smem_u32(&sk_bar[0]), b1 = smem_u32(&sk_bar[kSkUnits]);
-      const int r0 = sk_j * kSkC;
-      mbar_arrive_expect_tx(&sk_bar[0], 2 * kSkGuTile + 4 * kSkSbBox);
-      tma_load_4d(smem_u32(sGu), mw, 0, r0, 0, e, b0);
-      tma_load_4d(smem_u32(sGu + kSkGuBox), mw, 0, I + r0, 0, e, b0);
-      tma_load_3d(smem_u32(sGsb), msc, 0, r0, e, b0);
-      tma_load_3d(smem_u32(sGsb + 1 * kSkSbBox / 2), msc, 0, I + r0, e, b0);
-      tma_load_3d(smem_u32(sGsb + 2 * kSkSbBox / 2), mbi, 0, r0, e, b0);
-      tma_load_3d(smem_u32(sGsb + 3 * kSkSbBox / 2), mbi, 0, I + r0, e, b0);
-      for (int u = 1; u < kSkUnits; ++u) {
-        const uint32_t bu = smem_u32(&sk_bar[u]);
-        mbar_arrive_expect_tx(&sk_bar[u], 2 * kSkGuTile);
-        tma_load_4d(smem_u32(sGu + u * kSkGuTile), mw, 0, r0 + 8 * u, 0, e, bu);
-        tma_load_4d(smem_u32(sGu + kSkGuBox + u * kSkGuTile), mw, 0, I + r0 + 8 * u, 0, e, bu);
+      const uint32_t bu = smem_u32(&sk_bar[ln]);
+      mbar_arrive_expect_tx(&sk_bar[ln], 2 * kSkGuTile + (ln == 0 ? 4 * kSkSbBox : 0u));
+      tma_load_4d(smem_u32(sGu + ln * kSkGuTile), mw, 0, r0 + 8 * ln, 0, e, bu);
+      tma_load_4d(smem_u32(sGu + kSkGuBox + ln * kSkGuTile), mw, 0, I + r0 + 8 * ln, 0, e, bu);
+      if (ln == 0) {
+        const CUtensorMap* msc = shared ? &skm.sgu_s : &skm.gu_s;
+        const CUtensorMap* mbi = shared ? &skm.sgu_b : &skm.gu_b;
+        tma_load_3d(smem_u32(sGsb), msc, 0, r0, e, bu);
+        tma_load_3d(smem_u32(sGsb + 1 * kSkSbBox / 2), msc, 0, I + r0, e, bu);
+        tma_load_3d(smem_u32(sGsb + 2 * kSkSbBox / 2), mbi, 0, r0, e, bu);
+        tma_load_3d(smem_u32(sGsb + 3 * kSkSbBox / 2), mbi, 0, I + r0, e, bu);
       }
+    } else if (ln == kSkUnits) {
+      const CUtensorMap* md = shared ? &skm.sdn_w : &skm.dn_w;
       mbar_arrive_expect_tx(&sk_bar[kSkUnits], static_cast<uint32_t>(H) * SD::kRow);
-      tma_load_4d(smem_u32(sDnA), md, sk_j * BITS, 0, 0, e, b1);
+      tma_load_4d(smem_u32(sDnA), md, sk_j * BITS, 0, 0, e, smem_u32(&sk_bar[kSkUnits]));
     }
   };
   const int j0 = owns_sgu ? 1 : 0;  // ring unit 0: this warp's slice of the shared-expert gate/up task
@@ -1806,7 +1805,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   // (split-K) the shared expert's tasks know their weights: load them now,
   // once this CTA's router rows are out (they are on every CTA's path)
   if (sk_shared) {
-    if (tid == 0) sk_issue_tma(true, 0);
+    if (warp == 0) sk_issue_tma(true, 0, lane);
     sk_down_sb(p.sdn_s, p.sdn_b, I, warp * 128, sk_j, lane, sk_sw, sk_bw);
   }
   // (the B-fragment area is free until the down phase: 4 KB of it are xprep's scratch)
@@ -1874,7 +1873,7 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       // (split-K, one token) the routing warp issues its task's loads at once
       const int es = __shfl_sync(0xffffffffu, e, sk_src < K ? sk_src : 0);
       RNB_TRACE_MARK(p, 21);
-      if (sk_task && !sk_shared && lane == 0) sk_issue_tma(false, es - p.off);
+      if (sk_task && !sk_shared) sk_issue_tma(false, es - p.off, lane);
       RNB_TRACE_MARK(p, 22);
     }
     // the routing warps meet (warp 0 reads every token's selection); the
@@ -2020,26 +2019,32 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       RNB_TRACE_MARK(p, 14);
     }
     if (cta < H / 16) {
-      // rows [16 cta, 16 cta + 16): warp w sums row 16 cta + w over the
-      // tasks, lane l taking tasks l, l + 32, ... (all its words polled
-      // together, bounded) in order, then a fixed butterfly
+      // rows [16 cta, 16 cta + 16): warp w takes tasks [tpw w, tpw w + tpw),
+      // whose 16-row words are one 128-byte line each: lanes 0-15 read rows
+      // 0-15 of one task, lanes 16-31 of the next (all polled together,
+      // bounded); each warp's row sums (its tasks in order) then add up
+      // over the warps in order
       constexpr int kMaxPer = (kSkTasksPerSource * (kPMaxK + 1) + 31) / 32;
-      const uint2* yp = yw + 16 * cta + warp;
+      const int tpw = (ntask + kPWarps - 1) / kPWarps;
+      const int rr = lane & 15;
       uint64_t wv[kMaxPer];
+      auto word_of = [&](int k2) {
+        const int q = lane + 32 * k2, t = warp * tpw + (q >> 4);
+        return (q >> 4) < tpw && t < ntask ? yw + static_cast<size_t>(t) * H + 16 * cta + rr : nullptr;
+      };
 #pragma unroll
       for (int k2 = 0; k2 < kMaxPer; ++k2) {
-        const int t = lane + 32 * k2;
-        wv[k2] = t < ntask ? xw_load(yp + static_cast<size_t>(t) * H) : (static_cast<uint64_t>(epoch) << 32);
+        const uint2* w = word_of(k2);
+        wv[k2] = w ? xw_load(w) : (static_cast<uint64_t>(epoch) << 32);
       }
       const uint64_t deadline = gtimer() + kSpinLimitNs;
       for (;;) {
         bool all = true;
 #pragma unroll
         for (int k2 = 0; k2 < kMaxPer; ++k2) {
-          const int t = lane + 32 * k2;
           if (static_cast<uint32_t>(wv[k2] >> 32) != epoch) {
             all = false;
-            wv[k2] = xw_load(yp + static_cast<size_t>(t) * H);
+            wv[k2] = xw_load(word_of(k2));
           }
         }
         const bool late = !all && gtimer() > deadline;
@@ -2051,15 +2056,19 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       float acc = 0.f;
 #pragma unroll
       for (int k2 = 0; k2 < kMaxPer; ++k2)
-        if (lane + 32 * k2 < ntask) acc += __uint_as_float(static_cast<uint32_t>(wv[k2]));
+        if (word_of(k2)) acc += __uint_as_float(static_cast<uint32_t>(wv[k2]));
+      acc += __shfl_xor_sync(0xffffffffu, acc, 16);  // lanes r and r + 16 hold the same row
+      if (lane < 16) sRed[warp * 16 + lane] = acc;
+      __syncthreads();
+      if (tid < 16) {
+        float sum = 0.f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) {
-        const size_t o = static_cast<size_t>(16 * cta + warp);
+        for (int w = 0; w < kPWarps; ++w) sum += sRed[w * 16 + tid];
+        const size_t o = static_cast<size_t>(16 * cta + tid);
         if (p.y_f32)
-          static_cast<float*>(p.out)[o] = acc;
+          static_cast<float*>(p.out)[o] = sum;
         else
-          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(acc);
+          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(sum);
       }
       RNB_TRACE_MARK(p, 19);
     }
