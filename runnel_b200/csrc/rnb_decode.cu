@@ -1308,12 +1308,16 @@ struct PMisc {
 // xh: 2048-half scratch.
 template <int BITS>
 __device__ void xprep_cta(const uint16_t* x, int T, uint32_t* sX, float* sXs, float* xinv, __half* xh,
-                          float* red) {
+                          float* red, bool from_regs = false, uint2 xr0 = make_uint2(0, 0),
+                          uint2 xr1 = make_uint2(0, 0)) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int H = 2048, G = H / kGroup;
 #pragma unroll 1
   for (int t = 0; t < T; ++t) {
-    const uint2 u = reinterpret_cast<const uint2*>(x + static_cast<size_t>(t) * H)[tid];  // global or shared
+    // this thread's 4 values of token t: given (the router's registers), or
+    // from global or shared memory
+    const uint2 u = from_regs ? (t == 0 ? xr0 : xr1)
+                              : reinterpret_cast<const uint2*>(x + static_cast<size_t>(t) * H)[tid];
     const float v[4] = {__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
                         __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u)};
     const float m4 = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
@@ -1809,7 +1813,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     sk_down_sb(p.sdn_s, p.sdn_b, I, warp * 128, sk_j, lane, sk_sw, sk_bw);
   }
   // (the B-fragment area is free until the down phase: 4 KB of it are xprep's scratch)
-  xprep_cta<BITS>(xin, T, sX, sXs, ms->xinv, reinterpret_cast<__half*>(sm + off_hf), ms->red);
+  xprep_cta<BITS>(xin, T, sX, sXs, ms->xinv, reinterpret_cast<__half*>(sm + off_hf), ms->red, !p.norm_w, xr[0],
+                  xr[1]);
   RNB_TRACE_MARK(p, 4);
 
   // B operand of the gate/up MMAs: this lane's column g is entry ent[g].
