@@ -273,6 +273,35 @@ RNB_API int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* 
                                  uint32_t* inds_out, float* scores_out, void* ws, size_t ws_bytes,
                                  void* stream);
 
+/* ---- Expert parallelism for many tokens: device-side all-to-all ----
+ * (No reference counterpart.)  Every rank holds its own T tokens (the same T
+ * on every rank) and the expert shard [rank E, rank E + E) of E_total =
+ * world E, with the router and the whole shared expert.  One
+ * rnb_moe_block_a2a_fwd call computes the full block for this rank's tokens:
+ * the home block on the shard (routing, its experts, the shared expert),
+ * then each token's row goes by NVLink stores (CUDA IPC, no multicast) to
+ * every other rank that owns one of its experts, those ranks run their
+ * experts on the rows they received (the grouped GEMM pipeline), the fp32
+ * sums come back the same way, and the partials are added in a fixed order.
+ * There is no host synchronisation inside a call; cross-GPU waits are
+ * bounded and set RNB_STATUS_TIMEOUT in the workspace status word.
+ * rnb_a2a_create allocates this rank's areas for up to max_tokens tokens and
+ * writes its IPC handle (RNB_A2A_HANDLE_BYTES); gather every rank's handle
+ * (rank order) and pass them to rnb_a2a_connect.  Every rank then makes the
+ * same sequence of calls with the same T; the descriptor is this rank's
+ * shard (E_total = world E, expert_offset = rank E).  The workspace size
+ * comes from rnb_moe_block_a2a_workspace_size.  Call rnb_a2a_destroy on every
+ * rank after a host barrier. */
+#define RNB_A2A_HANDLE_BYTES 64
+typedef struct rnb_a2a rnb_a2a;
+RNB_API int rnb_a2a_create(int rank, int world, int H, int k, int max_tokens, rnb_a2a** a, void* handle_out);
+RNB_API int rnb_a2a_connect(rnb_a2a* a, const void* handles);
+RNB_API int rnb_a2a_destroy(rnb_a2a* a);
+RNB_API int rnb_a2a_set_wait_limit_ms(rnb_a2a* a, int ms);
+RNB_API int rnb_moe_block_a2a_workspace_size(const rnb_moe_desc* d, rnb_a2a* a, size_t* bytes);
+RNB_API int rnb_moe_block_a2a_fwd(const rnb_moe_desc* d, rnb_a2a* a, const void* x, void* out, uint32_t* inds_out,
+                                  float* scores_out, void* ws, size_t ws_bytes, void* stream);
+
 /* Layer glue of a decoder stack, around the block (no reference counterpart in
  * runnel itself -- mlx-lm's Qwen3.5 decoder layer does `x + mlp(rms_norm(x))`).  For T tokens of H bf16 values:
  *   x_out = bf16(x + y)   (y may be NULL: x_out = x)

@@ -31,6 +31,7 @@ FLAG_NO_SHARED = 0x2
 FLAG_Y_F32 = 0x4
 FLAG_CHAIN = 0x8
 EP_HANDLE_BYTES = 64
+A2A_HANDLE_BYTES = 64
 
 # Every function include/rnb_moe.h declares, with its ctypes signature.
 _vp = ctypes.c_void_p
@@ -80,6 +81,13 @@ SIGNATURES = {
     "rnb_ep_destroy": (ctypes.c_int, [_vp]),
     "rnb_ep_set_wait_limit_ms": (ctypes.c_int, [_vp, ctypes.c_int]),
     "rnb_moe_block_ep_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "rnb_a2a_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.POINTER(_vp), _vp]),
+    "rnb_a2a_connect": (ctypes.c_int, [_vp, _vp]),
+    "rnb_a2a_destroy": (ctypes.c_int, [_vp]),
+    "rnb_a2a_set_wait_limit_ms": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "rnb_moe_block_a2a_workspace_size": (ctypes.c_int, [_DescP, _vp, ctypes.POINTER(_sz)]),
+    "rnb_moe_block_a2a_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "rnb_moe_block_norm_fwd": (ctypes.c_int, [_DescP, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _sz,
                                               _vp]),
     "rnb_add_rmsnorm": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),

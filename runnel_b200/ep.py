@@ -129,6 +129,85 @@ class ExpertParallel:
         return (out, inds, scores) if return_routing else out
 
 
+class DeviceAllToAll:
+    """This rank's device-side all-to-all context for expert-parallel blocks
+    over many tokens (``rnb_a2a_*``): every rank holds its own ``T`` tokens
+    (the same ``T`` everywhere, at most ``max_tokens``) and its expert shard.
+    A call routes the rank's tokens, sends each row by NVLink stores to the
+    ranks that own one of its experts, runs this shard's experts on the rows
+    it received, returns the fp32 sums the same way and adds them up -- all
+    on the stream, with no host synchronisation."""
+
+    def __init__(self, rank: int, world: int, H: int = 2048, k: int = 8, max_tokens: int = 16384,
+                 handles_fn=gather_handles):
+        self.rank, self.world, self.H, self.k, self.max_tokens = rank, world, H, k, max_tokens
+        self._a = ctypes.c_void_p()
+        buf = (ctypes.c_char * _lib.A2A_HANDLE_BYTES)()
+        _lib.call("rnb_a2a_create", rank, world, H, k, max_tokens, ctypes.byref(self._a), buf)
+        try:
+            handles = handles_fn(bytes(buf))
+            if len(handles) != world or any(len(h) != _lib.A2A_HANDLE_BYTES for h in handles):
+                raise ValueError("handle exchange returned a malformed list")
+            _lib.call("rnb_a2a_connect", self._a, ctypes.c_char_p(b"".join(handles)))
+        except BaseException:
+            _lib.load().rnb_a2a_destroy(self._a)
+            self._a = None
+            raise
+        self._ws: torch.Tensor | None = None
+
+    def set_wait_limit_ms(self, ms: int) -> None:
+        """How long a call waits for the other ranks before it gives up and
+        sets RNB_STATUS_TIMEOUT (default 2000 ms)."""
+        if not self._a:
+            raise RuntimeError("DeviceAllToAll context is closed")
+        _lib.call("rnb_a2a_set_wait_limit_ms", self._a, int(ms))
+
+    def close(self) -> None:
+        """Release the buffers (after a host barrier on every rank)."""
+        if self._a:
+            _lib.load().rnb_a2a_destroy(self._a)
+            self._a = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: the library may be gone
+            pass
+
+    def status(self) -> int:
+        """Reads and clears the status bits of this context's workspace (synchronises)."""
+        if self._ws is None:
+            return 0
+        out = ctypes.c_uint32()
+        _lib.call("rnb_moe_status", self._ws.data_ptr(), self._ws.numel(), ctypes.byref(out), _stream())
+        return out.value
+
+    def moe_block(self, bt: BlockTensors, x: torch.Tensor, out: torch.Tensor | None = None,
+                  return_routing: bool = False):
+        """The block on this rank's tokens ``x`` from its shard ``bt``."""
+        if not self._a:
+            raise RuntimeError("DeviceAllToAll context is closed")
+        xt = _tokens(x, bt.H)
+        T = xt.shape[0]
+        f32 = bool(bt.flags & _lib.FLAG_Y_F32)
+        dt = torch.float32 if f32 else torch.bfloat16
+        if out is None:
+            out = torch.empty(xt.shape, dtype=dt, device=xt.device)
+        inds = scores = None
+        if return_routing:
+            inds = torch.empty((T, self.k), dtype=torch.int32, device=xt.device)
+            scores = torch.empty((T, self.k), dtype=torch.float32, device=xt.device)
+        d = bt.desc(T, self.k)
+        need = ctypes.c_size_t()
+        _lib.call("rnb_moe_block_a2a_workspace_size", ctypes.byref(d), self._a, ctypes.byref(need))
+        if self._ws is None or self._ws.numel() < need.value:
+            self._ws = torch.zeros(need.value, dtype=torch.uint8, device=xt.device)
+        _lib.call("rnb_moe_block_a2a_fwd", ctypes.byref(d), self._a, _ptr(xt), _ptr(out), _ptr(inds),
+                  _ptr(scores), self._ws.data_ptr(), self._ws.numel(), _stream())
+        out = out.reshape(x.shape)
+        return (out, inds, scores) if return_routing else out
+
+
 def shard_tensors(blk, rank: int, world: int, device) -> BlockTensors:
     """Upload rank's expert shard of a synthetic block (router, shared expert replicated)."""
     lo, hi, _ = plan(rank, world, blk.E, blk.I)

@@ -198,3 +198,67 @@ def test_peer_that_never_calls_times_out_then_a_fresh_context_is_correct():
         assert_close(out.float().cpu().numpy(), ref, "fresh context after a timeout", bound=bound)
     finally:
         one.close()
+
+
+def test_single_rank_device_all_to_all_is_the_block():
+    blk = inputs.make_block(BITS, seed=SEED, T=130)
+    dev = torch.device("cuda", 0)
+    bt = ep.shard_tensors(blk, 0, 1, dev)
+    x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).to(dev)
+    a2a = ep.DeviceAllToAll(0, 1, max_tokens=256, handles_fn=lambda h: [h])
+    try:
+        got = a2a.moe_block(bt, x)
+        want = ops.moe_block(ops.BlockTensors.from_numpy(blk, dev), x)
+        assert torch.equal(got, want)
+    finally:
+        a2a.close()
+
+
+def _rank_main_a2a(rank, world, port):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    a2a = None
+    try:
+        blk = inputs.make_block(8, seed=5, T=1)
+        shard = ep.shard_tensors(blk, rank, world, dev)
+        full = ops.BlockTensors.from_numpy(blk, dev)
+        w = oracle.BlockWeights(bits=8, group=64, **blk.weight_fields())
+        a2a = ep.DeviceAllToAll(rank, world, max_tokens=512, handles_fn=lambda h: ep.gather_handles(h))
+        a2a.set_wait_limit_ms(20000)
+        g = torch.Generator(device=dev)
+        # prefill- and decode-size calls; repeated calls alternate the areas' parity
+        for i, T in enumerate((300, 5, 512, 300, 64)):
+            g.manual_seed(1000 * i + rank)
+            xr = torch.randn((T, blk.H), device=dev, generator=g).to(torch.bfloat16)
+            dist.barrier()
+            got, inds, scores = a2a.moe_block(shard, xr, return_routing=True)
+            want, winds, wscores = ops.moe_block(full, xr, return_routing=True)
+            assert torch.equal(inds, winds) and torch.equal(scores, wscores)
+            assert_close_gpu_pair(got.float().cpu().numpy(), want.float().cpu().numpy(),
+                                  f"device all-to-all rank {rank} T={T}")
+            rows = np.linspace(0, T - 1, min(T, 16)).astype(int)
+            xb = xr[rows].view(torch.int16).cpu().numpy().view(np.uint16)
+            ref, oinds, _, bound = oracle_block(w, np.ascontiguousarray(xb))
+            np.testing.assert_array_equal(inds.cpu().numpy()[rows], oinds)
+            assert_close(got.float().cpu().numpy()[rows], ref, f"device all-to-all rank {rank} T={T} (oracle)",
+                         bound=bound)
+        assert a2a.status() == 0
+        torch.cuda.synchronize()
+        dist.barrier()
+    finally:
+        if a2a is not None:
+            a2a.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_device_all_to_all():
+    import torch.multiprocessing as mp
+
+    mp.spawn(_rank_main_a2a, args=(2, _free_port()), nprocs=2, join=True)
