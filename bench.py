@@ -380,11 +380,14 @@ def run_prefill_bench(args, cfg):
 
     bits, T = args.bits, cfg["T"]
     blocks, routing = prefill_blocks(cfg, bits, args.seed)
-    a2a = world > 1 and args.prefill_par in ("a2a", "gather")
+    a2a = world > 1 and args.prefill_par in ("device", "a2a", "gather")
     E_range = None
+    dctx = None
     if a2a:
         from runnel_b200 import ep as epm
         E_range = epm.plan(rank, world)[:2]
+        if args.prefill_par == "device":
+            dctx = epm.DeviceAllToAll(rank, world, max_tokens=T)
     base = ops.BlockTensors.from_numpy(blocks[0], dev, E_range=E_range)
     kinds = [base]
     for b in blocks[1:]:  # same expert weights, the step kind's router
@@ -400,7 +403,9 @@ def run_prefill_bench(args, cfg):
     moved = {"sent": 0, "received": 0}
 
     def block(i, x, o):
-        if a2a and args.prefill_par == "gather":
+        if dctx is not None:
+            dctx.moe_block(kinds[i % nk], x, out=o)
+        elif a2a and args.prefill_par == "gather":
             o.copy_(epm.moe_block_gather(kinds[i % nk], x, rank, world, ws=ws))
             moved["sent"] += x.shape[0] * (world - 1)
             moved["received"] += x.shape[0] * (world - 1)
@@ -420,6 +425,18 @@ def run_prefill_bench(args, cfg):
             step(i)
     stream.synchronize()
     assert ws.status() == 0
+    dev_rows = None
+    if dctx is not None:
+        # rows each step sends: (token, other rank owning one of its experts)
+        assert dctx.status() == 0
+        rows = []
+        for i in range(nk):
+            _, inds, _ = dctx.moe_block(kinds[i], xs[i], out=out, return_routing=True)
+            own = inds.long() // (256 // world)
+            hit = torch.zeros((inds.shape[0], world), dtype=torch.bool, device=dev).scatter_(1, own, True)
+            hit[:, rank] = False
+            rows.append(int(hit.sum()))
+        dev_rows = sum(rows) / len(rows)
     K = args.steps
     moved.update(sent=0, received=0)
     sampler = ClockSampler(local)
@@ -439,6 +456,8 @@ def run_prefill_bench(args, cfg):
     ms_step = ms / K
     tok_s = T * K * world / (ms * 1e-3)
     assert ws.status() == 0
+    if dctx is not None:
+        assert dctx.status() == 0
 
     # end to end through the public API: pinned host tokens in, host output back
     xh = [x.cpu().pin_memory() for x in xs]
@@ -492,7 +511,10 @@ def run_prefill_bench(args, cfg):
                    "tokens_per_step": T, "routing": routing, "H": 2048, "I": 512, "E": 256, "top_k": 8,
                    "l2": "inputs larger than L2: every step reads the whole expert bank (>= 0.8 GB)",
                    "tokens_per_step_per_gpu": T,
-                   "parallelism": ((f"ep{world} ({256 // world} experts/GPU; dispatch NCCL all_gather, combine "
+                   "parallelism": ((f"ep{world} device all-to-all ({256 // world} experts/GPU; rows and fp32 "
+                                    "sums by NVLink stores inside the kernels, no host synchronisation; shared "
+                                    "expert on every rank for its own tokens)" if args.prefill_par == "device" else
+                                    f"ep{world} ({256 // world} experts/GPU; dispatch NCCL all_gather, combine "
                                     "NCCL reduce_scatter of fp32 partials; shared expert on every rank for its "
                                     "own tokens)" if args.prefill_par == "gather" else
                                     f"ep{world} all-to-all ({256 // world} experts/GPU, NCCL all_to_all_single "
@@ -511,10 +533,13 @@ def run_prefill_bench(args, cfg):
                      "block_tflops": all_flops / (ms_step * 1e-3) / 1e12},
         "stages_ms_per_step": {k: v / max(ncalls, 1) * calls_per_step for k, v in stages.items()},
         # route, sort, scatter, gather, gate/up, row scale, down, final (twice per step with all-to-all)
-        "gpu_launches": 8 * K * (2 if a2a else 1),
+        "gpu_launches": K * (21 if dctx is not None else 8 * (2 if a2a else 1)),
         "clocks": clocks,
     }
-    if a2a:
+    if dctx is not None:
+        line["ep_rows_per_step"] = {"sent": dev_rows, "bytes_out": dev_rows * (2048 * 2 + 64),
+                                    "bytes_back": dev_rows * 2048 * 4, "rank": rank, "exchange": "device"}
+    elif a2a:
         mv = moved_timed
         line["ep_rows_per_step"] = {"sent": mv["sent"] / K, "received": mv["received"] / K,
                                     "bytes_out": mv["sent"] / K * (2048 * 2 + 64),
@@ -526,6 +551,10 @@ def run_prefill_bench(args, cfg):
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
+        if dctx is not None:
+            torch.cuda.synchronize()
+            dctx.close()  # every rank past the barrier: no peer reads its areas any more
+            dist.barrier()
         dist.destroy_process_group()
 
 
@@ -958,7 +987,7 @@ def main():
                     help="seconds of timed trials (each trial is exactly --steps steps; the median is reported)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--prefill-par", default="gather", choices=["gather", "a2a", "replica"],
+    ap.add_argument("--prefill-par", default="device", choices=["device", "gather", "a2a", "replica"],
                     help="prefill at N > 1: expert parallel with gather/reduce-scatter or all-to-all exchange, "
                          "or whole-bank replicas")
     ap.add_argument("--profile", action="store_true",
