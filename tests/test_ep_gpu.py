@@ -101,7 +101,7 @@ def _rank_main(rank, world, port):
         g = torch.Generator(device=dev)
         for i, (t0, t1) in enumerate(((300, 77), (5, 64), (0, 130))):
             g.manual_seed(100 * i + rank)
-            xr = torch.randn(((t0, t1)[rank], blk.H), device=dev, generator=g).to(torch.bfloat16)
+            xr = torch.randn(((t0, t1)[rank % 2], blk.H), device=dev, generator=g).to(torch.bfloat16)
             dist.barrier(group=gloo)
             stats = {}
             got = ep.moe_block_a2a(shard, xr, rank, world, ws=ws, stats=stats)
@@ -135,6 +135,15 @@ def test_two_rank_expert_parallel_decode():
     import torch.multiprocessing as mp
 
     mp.spawn(_rank_main, args=(2, _free_port()), nprocs=2, join=True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
+def test_every_gpu_expert_parallel_decode():
+    """The expert-parallel decode paths on every GPU of the box (4 or 8 ranks)."""
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    mp.spawn(_rank_main, args=(world, _free_port()), nprocs=world, join=True)
 
 
 def _idle_rank(conn):
@@ -262,3 +271,13 @@ def test_two_rank_device_all_to_all():
     import torch.multiprocessing as mp
 
     mp.spawn(_rank_main_a2a, args=(2, _free_port()), nprocs=2, join=True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
+def test_every_gpu_device_all_to_all():
+    """The same on every GPU of the box (4 or 8 ranks): the slot mapping and
+    the flag arrays at more than two ranks."""
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    mp.spawn(_rank_main_a2a, args=(world, _free_port()), nprocs=world, join=True)
