@@ -1300,6 +1300,8 @@ struct PMisc {
   float rnorm[kPWarps][8];   // [0,2) sum w^2; [2,4) sum |w|; [4,6) sum x^2; [6,8) max |x|
   uint32_t skbt[16];         // split-K: B pairs [lane c][pair] of the fp16 h slice
   float skhs, skhinv;        // split-K: sum of the fp16 h slice, its inverse scale
+  int sk_slot;               // split-K: this CTA's routed slot (-1: none)
+  uint32_t sk_lmask;         // split-K: the slots whose expert is on this GPU
 };
 
 // Activation prep of T tokens (H = 2048) by the whole CTA (512 threads, 4
@@ -1586,11 +1588,18 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   const int sg_task = cta - (NC - n_ch);
   const bool owns_sgu = !SK && has_shared && sg_task >= 0 && ((qmask >> ((sg_task * 8) / 128)) & 1u);
   const bool sh_down = !SK && owns_rows && has_shared && qmask != 0u;
-  // split-K task of this CTA: source (routed slot, or the shared expert at
-  // slot k) and 32-channel slice; CTAs past the last task only route
-  const int sk_src = cta / kSkTasksPerSource, sk_j = cta % kSkTasksPerSource;
-  const bool sk_shared = SK && has_shared && sk_src == K;
-  const bool sk_task = SK && (sk_src < K || sk_shared);
+  // split-K task of this CTA: a 32-channel slice j of a source.  One GPU:
+  // CTAs [0, 16k) the routed slots' slices, then the shared expert's 16.
+  // Expert parallel: first this rank's shared slices (j = rank, rank +
+  // world, ...), then 16 per local routed slot (the m-th local slot for CTA
+  // sk_rbase + 16 m + j; known after routing).  CTAs past the last task only
+  // route (and combine).
+  const int sk_nsh = (SK && has_shared) ? (EP ? kSkTasksPerSource / p.ep_world : kSkTasksPerSource) : 0;
+  const int sk_rbase = EP ? sk_nsh : 0, sk_sbase = EP ? 0 : kSkTasksPerSource * K;
+  const bool sk_shared = SK && cta >= sk_sbase && cta < sk_sbase + sk_nsh;
+  const int sk_j = sk_shared ? (EP ? p.ep_rank + p.ep_world * (cta - sk_sbase) : cta - sk_sbase)
+                             : (cta - sk_rbase) % kSkTasksPerSource;
+  const int sk_m = (cta - sk_rbase) / kSkTasksPerSource;  // (routed) which local slot
   using SD = SkDown<BITS>;
   // (split-K) TMA destinations, from the first 1024-byte boundary at or after
   // off_tma: up and gate codes, [tile 4][16 slices][8 rows][Tile2 row bytes]
@@ -1875,10 +1884,19 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     }
     if (lane == 0) ms->sg[t] = p.has_shared ? 1.0f / (1.0f + expf(-__uint_as_float(sIvl[t * (Et + 1) + Et]))) : 0.f;
     if (SK) {
-      // (split-K, one token) the routing warp issues its task's loads at once
-      const int es = __shfl_sync(0xffffffffu, e, sk_src < K ? sk_src : 0);
+      // (split-K, one token) the routing warp finds this CTA's routed slot
+      // (the sk_m-th slot whose expert is on this GPU) and issues its loads
+      const uint32_t lmask = __ballot_sync(0xffffffffu, lane < K && is_local(static_cast<uint32_t>(e)));
+      uint32_t mm = lmask;
+      for (int i = 0; i < sk_m; ++i) mm &= mm - 1u;
+      const int slot = (!sk_shared && cta >= sk_rbase && sk_m < kPMaxK && mm) ? __ffs(mm) - 1 : -1;
+      if (lane == 0) {
+        ms->sk_slot = slot;
+        ms->sk_lmask = lmask;
+      }
+      const int es = __shfl_sync(0xffffffffu, e, slot >= 0 ? slot : 0);
       RNB_TRACE_MARK(p, 21);
-      if (sk_task && !sk_shared) sk_issue_tma(false, es - p.off, lane);
+      if (slot >= 0) sk_issue_tma(false, es - p.off, lane);
       RNB_TRACE_MARK(p, 22);
     }
     // the routing warps meet (warp 0 reads every token's selection); the
@@ -1938,14 +1956,23 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   if constexpr (SK) {
     // ---- split-K (one token): this CTA's task, then the combine of its rows
     const int ntask = kSkTasksPerSource * (K + (has_shared ? 1 : 0));
-    uint2* yw = p.ws.yw;  // [task][H] weighted partial words
+    uint2* yw = p.ws.yw;  // [task][H] weighted partial words (task g: slot g / 16, slice g % 16)
+    const int sk_slot = ms->sk_slot;
+    const uint32_t sk_lmask = ms->sk_lmask;
+    const bool sk_task = sk_shared || sk_slot >= 0;
+    // the tasks on this GPU: its routed slots' slices, and its shared slices
+    auto task_here = [&](int t) {
+      if (t < kSkTasksPerSource * K) return ((sk_lmask >> (t / kSkTasksPerSource)) & 1u) != 0u;
+      const int j = t - kSkTasksPerSource * K;
+      return has_shared && j < kSkTasksPerSource && (!EP || j % p.ep_world == p.ep_rank);
+    };
     if (sk_task) {
       float wgt = ms->sg[0];
       if (!sk_shared) {
         // (the TMA requests went out from the routing warp)
-        const uint32_t le = ms->inds[0][sk_src] - static_cast<uint32_t>(p.off);
+        const uint32_t le = ms->inds[0][sk_slot] - static_cast<uint32_t>(p.off);
         const size_t dse = static_cast<size_t>(H) * dsrow;
-        wgt = ms->scores[0][sk_src];
+        wgt = ms->scores[0][sk_slot];
         sk_down_sb(p.dn_s + le * dse, p.dn_b + le * dse, I, warp * 128, sk_j, lane, sk_sw, sk_bw);
       }
       // gate/up: the four 8-channel tiles, each once its TMA loads are in
@@ -2018,7 +2045,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       if (!mbar_wait(&sk_bar[kSkUnits], 0, kSpinLimitNs)) timed_out = true;  // the down codes
       __syncthreads();
       RNB_TRACE_MARK(p, 12);
-      uint2* ydst = yw + static_cast<size_t>(cta) * H + warp * 128;
+      const int gtask = sk_shared ? kSkTasksPerSource * K + sk_j : kSkTasksPerSource * sk_slot + sk_j;
+      uint2* ydst = yw + static_cast<size_t>(gtask) * H + warp * 128;
       sk_down_mma<BITS>(sDn, sk_sw, sk_bw, ms->skbt, ms->skhs, ms->skhinv, sk_j, g, c,
                         [&](int r, float v) { xw_store(ydst + r, __float_as_uint(v * wgt), epoch); });
       RNB_TRACE_MARK(p, 14);
@@ -2035,7 +2063,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       uint64_t wv[kMaxPer];
       auto word_of = [&](int k2) {
         const int q = lane + 32 * k2, t = warp * tpw + (q >> 4);
-        return (q >> 4) < tpw && t < ntask ? yw + static_cast<size_t>(t) * H + 16 * cta + rr : nullptr;
+        return (q >> 4) < tpw && t < ntask && task_here(t) ? yw + static_cast<size_t>(t) * H + 16 * cta + rr
+                                                             : nullptr;
       };
 #pragma unroll
       for (int k2 = 0; k2 < kMaxPer; ++k2) {
@@ -2065,15 +2094,27 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
       acc += __shfl_xor_sync(0xffffffffu, acc, 16);  // lanes r and r + 16 hold the same row
       if (lane < 16) sRed[warp * 16 + lane] = acc;
       __syncthreads();
+      auto emit = [&](int, int r, float v) {
+        const size_t o = static_cast<size_t>(16 * cta + r);
+        if (p.y_f32)
+          static_cast<float*>(p.out)[o] = v;
+        else
+          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
+      };
       if (tid < 16) {
         float sum = 0.f;
 #pragma unroll
         for (int w = 0; w < kPWarps; ++w) sum += sRed[w * 16 + tid];
-        const size_t o = static_cast<size_t>(16 * cta + tid);
-        if (p.y_f32)
-          static_cast<float*>(p.out)[o] = sum;
+        if (EP)
+          sRed[kPWarps * 16 + tid] = sum;  // this rank's part of the rows
         else
-          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(sum);
+          emit(0, tid, sum);
+      }
+      if (EP) {
+        // expert parallel: the ranks' parts of the 16 rows over NVLink,
+        // added in rank order
+        __syncthreads();
+        ep_exchange_tile(p, 16 * cta, 1, [&](int, int r) { return sRed[kPWarps * 16 + r]; }, emit);
       }
       RNB_TRACE_MARK(p, 19);
     }
@@ -2597,12 +2638,14 @@ size_t persistent_static_smem() {
   static size_t bytes = [] {
     cudaFuncAttributes fa;
     cudaFuncAttributes fb;
-    cudaFuncAttributes fc;
+    cudaFuncAttributes fc, fd;
     const bool ok = cudaFuncGetAttributes(&fa, k_decode<BITS, false, false>) == cudaSuccess &&
                     cudaFuncGetAttributes(&fb, k_decode<BITS, true, false>) == cudaSuccess &&
-                    cudaFuncGetAttributes(&fc, k_decode<BITS, false, true>) == cudaSuccess;
+                    cudaFuncGetAttributes(&fc, k_decode<BITS, false, true>) == cudaSuccess &&
+                    cudaFuncGetAttributes(&fd, k_decode<BITS, true, true>) == cudaSuccess;
     size_t m = fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes;
     m = m > fc.sharedSizeBytes ? m : fc.sharedSizeBytes;
+    m = m > fd.sharedSizeBytes ? m : fd.sharedSizeBytes;
     return ok ? m : size_t(2048);
   }();
   return bytes;
@@ -2688,9 +2731,15 @@ bool sk_maps(const Params& p, int bits, SkMaps& m) {
 template <int BITS>
 bool persistent_plan_sk(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem) {
   const int nq = p.I / 128;
-  if (p.mode != kModeBlock || p.T != 1 || p.ep_world > 1 || p.H != 2048 || p.I != 512 || p.E_total > 256 ||
-      p.k > kPMaxK || p.off != 0 || p.E != p.E_total || p.shared_qmask != (1u << nq) - 1u)
+  if (p.mode != kModeBlock || p.T != 1 || p.H != 2048 || p.I != 512 || p.E_total > 256 || p.k > kPMaxK)
     return false;
+  if (p.ep_world > 1) {
+    // expert parallel: even expert shards, the shared expert's 16 slices
+    // split evenly over the ranks
+    if (kSkTasksPerSource % p.ep_world || p.E * p.ep_world != p.E_total || p.off != p.ep_rank * p.E) return false;
+  } else if (p.off != 0 || p.E != p.E_total || p.shared_qmask != (1u << nq) - 1u) {
+    return false;
+  }
   const int NC = di.sms;
   if (NC < p.H / 16 || 2 * NC < p.E_total + 1) return false;
   if (kSkTasksPerSource * (p.k + (p.has_shared ? 1 : 0)) > NC) return false;
@@ -2779,7 +2828,7 @@ bool persistent_plan(const Params& p, const DevInfo& di, PPlan& pl, size_t& smem
 // its griddepcontrol.wait holds everything else back.
 template <int BITS>
 int run_persistent(Params& p, const PPlan& pl, size_t smem, int nc, cudaStream_t st) {
-  auto kern = p.ep_world > 1 ? k_decode<BITS, true, false>
+  auto kern = p.ep_world > 1 ? (pl.sk ? k_decode<BITS, true, true> : k_decode<BITS, true, false>)
                              : (pl.sk ? k_decode<BITS, false, true> : k_decode<BITS, false, false>);
   SkMaps maps;
   memset(&maps, 0, sizeof(maps));
