@@ -1600,6 +1600,8 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
   const int sk_j = sk_shared ? (EP ? p.ep_rank + p.ep_world * (cta - sk_sbase) : cta - sk_sbase)
                              : (cta - sk_rbase) % kSkTasksPerSource;
   const int sk_m = (cta - sk_rbase) / kSkTasksPerSource;  // (routed) which local slot
+  // one GPU: every slot is local, so CTA i < 16k takes slot i / 16 (static)
+  const int sk_slot0 = (SK && !EP && cta < kSkTasksPerSource * K) ? sk_m : -1;
   using SD = SkDown<BITS>;
   // (split-K) TMA destinations, from the first 1024-byte boundary at or after
   // off_tma: up and gate codes, [tile 4][16 slices][8 rows][Tile2 row bytes]
@@ -1884,15 +1886,19 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     }
     if (lane == 0) ms->sg[t] = p.has_shared ? 1.0f / (1.0f + expf(-__uint_as_float(sIvl[t * (Et + 1) + Et]))) : 0.f;
     if (SK) {
-      // (split-K, one token) the routing warp finds this CTA's routed slot
-      // (the sk_m-th slot whose expert is on this GPU) and issues its loads
-      const uint32_t lmask = __ballot_sync(0xffffffffu, lane < K && is_local(static_cast<uint32_t>(e)));
-      uint32_t mm = lmask;
-      for (int i = 0; i < sk_m; ++i) mm &= mm - 1u;
-      const int slot = (!sk_shared && cta >= sk_rbase && sk_m < kPMaxK && mm) ? __ffs(mm) - 1 : -1;
-      if (lane == 0) {
-        ms->sk_slot = slot;
-        ms->sk_lmask = lmask;
+      // (split-K, one token) the routing warp issues this CTA's loads; expert
+      // parallel, it first finds the CTA's routed slot (the sk_m-th slot
+      // whose expert is on this GPU)
+      int slot = sk_slot0;
+      if (EP) {
+        const uint32_t lmask = __ballot_sync(0xffffffffu, lane < K && is_local(static_cast<uint32_t>(e)));
+        uint32_t mm = lmask;
+        for (int i = 0; i < sk_m; ++i) mm &= mm - 1u;
+        slot = (!sk_shared && cta >= sk_rbase && sk_m < kPMaxK && mm) ? __ffs(mm) - 1 : -1;
+        if (lane == 0) {
+          ms->sk_slot = slot;
+          ms->sk_lmask = lmask;
+        }
       }
       const int es = __shfl_sync(0xffffffffu, e, slot >= 0 ? slot : 0);
       RNB_TRACE_MARK(p, 21);
@@ -1957,11 +1963,13 @@ __global__ void __launch_bounds__(32 * kPWarps, 1) k_decode(Params p_arg, PPlan 
     // ---- split-K (one token): this CTA's task, then the combine of its rows
     const int ntask = kSkTasksPerSource * (K + (has_shared ? 1 : 0));
     uint2* yw = p.ws.yw;  // [task][H] weighted partial words (task g: slot g / 16, slice g % 16)
-    const int sk_slot = ms->sk_slot;
-    const uint32_t sk_lmask = ms->sk_lmask;
+    const int sk_slot = EP ? ms->sk_slot : sk_slot0;
+    const uint32_t sk_lmask = EP ? ms->sk_lmask : 0u;
     const bool sk_task = sk_shared || sk_slot >= 0;
     // the tasks on this GPU: its routed slots' slices, and its shared slices
+    // (one GPU: all of them)
     auto task_here = [&](int t) {
+      if (!EP) return true;
       if (t < kSkTasksPerSource * K) return ((sk_lmask >> (t / kSkTasksPerSource)) & 1u) != 0u;
       const int j = t - kSkTasksPerSource * K;
       return has_shared && j < kSkTasksPerSource && (!EP || j % p.ep_world == p.ep_rank);
