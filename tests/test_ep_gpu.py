@@ -209,6 +209,66 @@ def test_peer_that_never_calls_times_out_then_a_fresh_context_is_correct():
         one.close()
 
 
+def _idle_rank_a2a(conn):
+    """Rank 1 of a two-rank device all-to-all that never makes a call: it
+    makes its areas, hands over its handle and waits to be told to exit."""
+    import ctypes
+
+    import torch
+
+    from runnel_b200 import _lib
+
+    torch.cuda.set_device(0)
+    a = ctypes.c_void_p()
+    buf = (ctypes.c_char * _lib.A2A_HANDLE_BYTES)()
+    _lib.call("rnb_a2a_create", 1, 2, 2048, 8, 64, ctypes.byref(a), buf)
+    conn.send(bytes(buf))
+    conn.recv()
+    _lib.load().rnb_a2a_destroy(a)
+
+
+def test_all_to_all_peer_that_never_calls_times_out_then_a_fresh_context_is_correct():
+    """A device all-to-all call whose second rank never calls: both bounded
+    waits (rows in, sums back; lowered to 50 ms) run out, the call returns
+    with RNB_STATUS_TIMEOUT in its workspace, and a fresh context computes
+    correctly.  The missing rank is a host process that never launches."""
+    import multiprocessing
+
+    mpc = multiprocessing.get_context("spawn")
+    parent, child = mpc.Pipe()
+    proc = mpc.Process(target=_idle_rank_a2a, args=(child,))
+    proc.start()
+    dev = torch.device("cuda", 0)
+    blk = inputs.make_block(BITS, seed=SEED, T=40)
+    x = torch.from_numpy(blk.x).view(torch.int16).view(torch.bfloat16).to(dev)
+    try:
+        assert parent.poll(180), "the idle rank did not start"
+        h1 = parent.recv()
+        a2a = ep.DeviceAllToAll(0, 2, max_tokens=64, handles_fn=lambda h: [h, h1])
+        try:
+            a2a.set_wait_limit_ms(50)
+            shard = ep.shard_tensors(blk, 0, 2, dev)
+            for T in (40, 3):
+                a2a.moe_block(shard, x[:T])
+                torch.cuda.synchronize()
+                assert a2a.status() & _lib.STATUS_TIMEOUT
+        finally:
+            a2a.close()
+    finally:
+        parent.send(1)
+        proc.join(60)
+    one = ep.DeviceAllToAll(0, 1, max_tokens=64, handles_fn=lambda h: [h])
+    try:
+        bt = ep.shard_tensors(blk, 0, 1, dev)
+        out = one.moe_block(bt, x)
+        torch.cuda.synchronize()
+        assert one.status() == 0
+        want = ops.moe_block(ops.BlockTensors.from_numpy(blk, dev), x)
+        assert torch.equal(out, want)
+    finally:
+        one.close()
+
+
 def test_single_rank_device_all_to_all_is_the_block():
     blk = inputs.make_block(BITS, seed=SEED, T=130)
     dev = torch.device("cuda", 0)
