@@ -284,7 +284,10 @@ RNB_API int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* 
  * experts on the rows they received (the grouped GEMM pipeline), the fp32
  * sums come back the same way, and the partials are added in a fixed order.
  * There is no host synchronisation inside a call; cross-GPU waits are
- * bounded and set RNB_STATUS_TIMEOUT in the workspace status word.
+ * bounded and set RNB_STATUS_TIMEOUT in the workspace status word.  The
+ * exchange and the remote experts run on a stream of the context's own,
+ * which forks from the caller's stream once the home routing is queued and
+ * joins it before the combine (a captured call is one fork and one join).
  * rnb_a2a_create allocates this rank's areas for up to max_tokens tokens and
  * writes its IPC handle (RNB_A2A_HANDLE_BYTES); gather every rank's handle
  * (rank order) and pass them to rnb_a2a_connect.  Every rank then makes the

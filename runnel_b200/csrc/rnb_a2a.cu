@@ -19,6 +19,12 @@
 //      as in 2; k_a2a_wait again;
 //   6. combine (k_a2a_combine): out[t] = bf16(home[t] + the returned rows of
 //      t in rank order) -- only the rows its routing sent out are read.
+// Steps 2-5 run on the context's own stream, which forks from the caller's
+// as soon as the home block's routing is queued (prefill) or after the home
+// block (decode sizes) and joins it before the combine: the NVLink traffic
+// and the remote experts overlap the home block's gather and GEMMs.  The
+// workspace is two regions, the home block's and the remote experts'; the
+// combine folds the second region's status bits into the first's.
 // Receive and return areas alternate by the call's parity: a rank cannot
 // start call n + 2 before every peer has returned call n + 1's rows, which
 // a peer does only after it has consumed call n.  The epoch is a per-context
@@ -89,6 +95,7 @@ struct A2aParams {
   uint32_t epoch;
   uint64_t wait_ns;
   uint32_t* status;
+  uint32_t* status2;         // the remote experts' status word, folded in by the combine
   char* peer[kA2aMaxRanks];  // each rank's shared region, this call's parity
   A2aArea area;
   const uint16_t* x;       // [T][H] this rank's tokens
@@ -198,6 +205,13 @@ __global__ void __launch_bounds__(256) k_a2a_return(const __grid_constant__ A2aP
 __global__ void __launch_bounds__(256) k_a2a_combine(const __grid_constant__ A2aParams p) {
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int H8 = p.H / 8;
+  if (i == 0 && p.status2) {
+    const uint32_t s2 = *p.status2;
+    if (s2) {
+      atomicOr(p.status, s2);
+      *p.status2 = 0;
+    }
+  }
   if (i >= static_cast<size_t>(p.T) * H8) return;
   const int t = static_cast<int>(i / H8), h0 = static_cast<int>(i % H8) * 8;
   uint32_t mask = 0;
@@ -246,6 +260,9 @@ struct rnb_a2a {
   uint32_t* inds = nullptr; // [Tmax][k]
   float* scores = nullptr;  // [Tmax][k]
   float* y = nullptr;       // [(world - 1) Tmax][H] remote experts' sums
+  cudaStream_t side = nullptr;     // dispatch, remote experts and return
+  cudaEvent_t ev_route = nullptr;  // the home routing is in a->inds / a->scores
+  cudaEvent_t ev_done = nullptr;   // the side stream's work of the call is queued
   bool connected = false;
 };
 
@@ -258,6 +275,9 @@ void a2a_free(rnb_a2a* a) {
   for (void* p : {a->local, static_cast<void*>(a->part), static_cast<void*>(a->inds), static_cast<void*>(a->scores),
                   static_cast<void*>(a->y)})
     if (p) cudaFree(p);
+  if (a->ev_route) cudaEventDestroy(a->ev_route);
+  if (a->ev_done) cudaEventDestroy(a->ev_done);
+  if (a->side) cudaStreamDestroy(a->side);
   delete a;
 }
 
@@ -277,11 +297,36 @@ int a2a_check(const rnb_moe_desc* d, const rnb_a2a* a) {
   return RNB_OK;
 }
 
+// The two workspace regions: the home block's [0, home) and the remote
+// experts' [home, home + experts).  `home` is sized for the context's
+// max_tokens, so the experts' region (its status word first) starts at the
+// same offset in every call whatever its T: the home block's scratch of one
+// call never lands under the experts' status word of another.
+int a2a_ws_split(const rnb_moe_desc* d, const rnb_a2a* a, size_t* home, size_t* experts);
+
 rnb_moe_desc a2a_experts_desc(const rnb_moe_desc* d, const rnb_a2a* a) {
   rnb_moe_desc e = *d;
   e.T = (a->world - 1) * d->T;
   e.flags |= RNB_FLAG_Y_F32;
   return e;
+}
+
+int a2a_ws_split(const rnb_moe_desc* d, const rnb_a2a* a, size_t* home, size_t* experts) {
+  rnb_moe_desc h = *d;
+  h.flags |= RNB_FLAG_Y_F32;
+  h.T = a->Tmax;  // the block's workspace size grows with T
+  size_t b0 = 0, b1 = 0;
+  int rc = rnb_moe_workspace_size(&h, &b0);
+  if (rc) return rc;
+  if (a->world > 1) {
+    const rnb_moe_desc e = a2a_experts_desc(d, a);
+    rc = rnb_moe_experts_workspace_size(&e, &b1);
+    if (rc) return rc;
+    b0 = (b0 + 255) & ~static_cast<size_t>(255);
+  }
+  *home = b0;
+  *experts = b1;
+  return RNB_OK;
 }
 
 }  // namespace
@@ -314,6 +359,13 @@ int rnb_a2a_create(int rank, int world, int H, int k, int max_tokens, rnb_a2a** 
   if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&a->scores), T * k * 4);
   if (e == cudaSuccess && world > 1)
     e = cudaMalloc(reinterpret_cast<void**>(&a->y), static_cast<size_t>(world - 1) * T * H * 4);
+  if (e == cudaSuccess && world > 1) {
+    int least = 0, greatest = 0;
+    e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+    if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&a->side, cudaStreamNonBlocking, greatest);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a->ev_route, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a->ev_done, cudaEventDisableTiming);
+  }
   cudaIpcMemHandle_t h;
   memset(&h, 0, sizeof(h));
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, a->local);
@@ -374,17 +426,10 @@ int rnb_moe_block_a2a_workspace_size(const rnb_moe_desc* d, rnb_a2a* a, size_t* 
   using namespace rnb;
   if (!bytes) return fail(RNB_ERR_INVALID, "rnb_moe_block_a2a_workspace_size: bytes is NULL");
   if (!d || !a) return fail(RNB_ERR_INVALID, "rnb_moe_block_a2a_workspace_size: NULL descriptor or context");
-  rnb_moe_desc h = *d;
-  h.flags |= RNB_FLAG_Y_F32;
   size_t b0 = 0, b1 = 0;
-  int rc = rnb_moe_workspace_size(&h, &b0);
+  const int rc = a2a_ws_split(d, a, &b0, &b1);
   if (rc) return rc;
-  if (a->world > 1) {
-    const rnb_moe_desc e = a2a_experts_desc(d, a);
-    rc = rnb_moe_experts_workspace_size(&e, &b1);
-    if (rc) return rc;
-  }
-  *bytes = b0 > b1 ? b0 : b1;
+  *bytes = b0 + b1;
   return RNB_OK;
 }
 
@@ -403,11 +448,23 @@ int rnb_moe_block_a2a_fwd(const rnb_moe_desc* d, rnb_a2a* a, const void* x, void
   const int T = d->T, H = d->H, k = d->k;
   if (T == 0) return RNB_OK;
   if (a->world == 1) return rnb_moe_block_fwd(d, x, out, inds_out, scores_out, ws, ws_bytes, stream);
-  // 1. home block: the shard's experts and the shared expert, fp32, and the routing
+  size_t b0 = 0, b1 = 0;
+  rc = a2a_ws_split(d, a, &b0, &b1);
+  if (rc) return rc;
+  char* ws0 = static_cast<char*>(ws);
+  char* ws1 = ws0 + b0;
+  // 1. home block: the shard's experts and the shared expert, fp32, and the
+  // routing; ev_route marks the routing (prefill) or the whole block (decode)
   rnb_moe_desc h = *d;
   h.flags |= RNB_FLAG_Y_F32;
-  rc = rnb_moe_block_fwd(&h, x, a->part, a->inds, a->scores, ws, ws_bytes, stream);
+  bool fired = false;
+  set_prefill_route_event(a->ev_route, &fired);
+  rc = rnb_moe_block_fwd(&h, x, a->part, a->inds, a->scores, ws0, b0, stream);
+  set_prefill_route_event(nullptr, nullptr);
   if (rc) return rc;
+  cudaError_t e = fired ? cudaSuccess : cudaEventRecord(a->ev_route, st);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(a->side, a->ev_route, 0);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("rnb_moe_block_a2a_fwd fork: ") + cudaGetErrorString(e));
   const uint32_t epoch = ++a->calls;
   const size_t par = static_cast<size_t>(epoch & 1u) * a->par_bytes;
   A2aParams p;
@@ -420,7 +477,8 @@ int rnb_moe_block_a2a_fwd(const rnb_moe_desc* d, rnb_a2a* a, const void* x, void
   p.per = d->E;
   p.epoch = epoch;
   p.wait_ns = a->wait_ns;
-  p.status = static_cast<uint32_t*>(ws);  // the workspace status word (offset 0)
+  p.status = reinterpret_cast<uint32_t*>(ws0);   // the home region's status word (offset 0)
+  p.status2 = reinterpret_cast<uint32_t*>(ws1);  // the remote experts' (offset 0 of theirs)
   for (int q = 0; q < a->world; ++q) p.peer[q] = a->peer[q] + par;
   p.area = a2a_area(a->world, H, k, a->Tmax);
   p.x = static_cast<const uint16_t*>(x);
@@ -430,20 +488,30 @@ int rnb_moe_block_a2a_fwd(const rnb_moe_desc* d, rnb_a2a* a, const void* x, void
   p.y = a->y;
   p.out = out;
   p.y_f32 = (d->flags & RNB_FLAG_Y_F32) ? 1 : 0;
-  // 2-3. dispatch, then every peer's rows in
-  k_a2a_dispatch<<<kA2aCtas, 256, 0, st>>>(p);
-  k_a2a_wait<<<1, 256, 0, st>>>(p, p.area.rx_flags);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("rnb_moe_block_a2a_fwd dispatch: ") + cudaGetErrorString(e));
-  // 4. this shard's experts on the received rows
-  const char* own = p.peer[a->rank];
-  const rnb_moe_desc ed = a2a_experts_desc(d, a);
-  rc = rnb_moe_experts_fwd(&ed, own + p.area.rx_x, reinterpret_cast<const uint32_t*>(own + p.area.rx_i),
-                           reinterpret_cast<const float*>(own + p.area.rx_s), a->y, ws, ws_bytes, stream);
+  // 2-5 on the side stream, which always joins the caller's stream again
+  // (also on an error) so that a captured call stays one fork and one join
+  const cudaStream_t sd = a->side;
+  k_a2a_dispatch<<<kA2aCtas, 256, 0, sd>>>(p);
+  k_a2a_wait<<<1, 256, 0, sd>>>(p, p.area.rx_flags);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) rc = fail(RNB_ERR_CUDA, std::string("rnb_moe_block_a2a_fwd dispatch: ") + cudaGetErrorString(e));
+  if (!rc) {
+    const char* own = p.peer[a->rank];
+    const rnb_moe_desc ed = a2a_experts_desc(d, a);
+    rc = rnb_moe_experts_fwd(&ed, own + p.area.rx_x, reinterpret_cast<const uint32_t*>(own + p.area.rx_i),
+                             reinterpret_cast<const float*>(own + p.area.rx_s), a->y, ws1, b1, sd);
+  }
+  if (!rc) {
+    k_a2a_return<<<kA2aCtas, 256, 0, sd>>>(p);
+    k_a2a_wait<<<1, 256, 0, sd>>>(p, p.area.back_flags);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) rc = fail(RNB_ERR_CUDA, std::string("rnb_moe_block_a2a_fwd return: ") + cudaGetErrorString(e));
+  }
+  e = cudaEventRecord(a->ev_done, sd);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(st, a->ev_done, 0);
+  if (e != cudaSuccess) return fail(RNB_ERR_CUDA, std::string("rnb_moe_block_a2a_fwd join: ") + cudaGetErrorString(e));
   if (rc) return rc;
-  // 5-6. the sums back, every peer's in, then the combine
-  k_a2a_return<<<kA2aCtas, 256, 0, st>>>(p);
-  k_a2a_wait<<<1, 256, 0, st>>>(p, p.area.back_flags);
+  // 6. the combine on the caller's stream
   const size_t n = static_cast<size_t>(T) * (H / 8);
   k_a2a_combine<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(p);
   e = cudaGetLastError();

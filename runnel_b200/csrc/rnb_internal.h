@@ -63,6 +63,11 @@ void stage_end(cudaStream_t st, int stage);
 // whether it supports the descriptor's shapes.
 size_t prefill_workspace_bytes(const rnb_moe_desc& d);
 bool prefill_supported(const rnb_moe_desc& d);
+// When set (per host thread), the prefill pipeline records this event on its
+// stream as soon as the routing stage is queued, and sets *fired; the
+// device-side all-to-all uses it to start its dispatch before the home
+// experts run.  Null (the default) records nothing.
+void set_prefill_route_event(cudaEvent_t ev, bool* fired);
 // inds_in / scores_in ([T][k]): given routing (no router, no shared expert).
 int run_prefill(const rnb_moe_desc* d, const void* x, void* out, uint32_t* inds_out, float* scores_out,
                 void* ws, size_t ws_bytes, cudaStream_t st, const uint32_t* inds_in = nullptr,

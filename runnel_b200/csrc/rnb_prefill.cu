@@ -1202,6 +1202,16 @@ bool make_maps(const Params& p, int mode, int rows_cap, TmaMaps& tm) {
 
 }  // namespace pre
 
+namespace {
+thread_local cudaEvent_t g_route_event = nullptr;
+thread_local bool* g_route_fired = nullptr;
+}  // namespace
+
+void set_prefill_route_event(cudaEvent_t ev, bool* fired) {
+  g_route_event = ev;
+  g_route_fired = fired;
+}
+
 template <int BITS>
 static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st) {
   using namespace pre;
@@ -1246,6 +1256,7 @@ static int launch_prefill(pre::Params& p, const pre::Layout& L, cudaStream_t st)
     k_pre_select<<<(p.T + 15) / 16, 512, 0, st>>>(p);
   }
   stage_end(st, RNB_STAGE_ROUTE);
+  if (g_route_event && cudaEventRecord(g_route_event, st) == cudaSuccess && g_route_fired) *g_route_fired = true;
   k_pre_sort<<<1, 512, 0, st>>>(p);
   stage_end(st, RNB_STAGE_SORT);
   const size_t n_scatter = static_cast<size_t>(p.T) * (p.k + 1);

@@ -317,7 +317,20 @@ def _rank_main_a2a(rank, world, port):
             np.testing.assert_array_equal(inds.cpu().numpy()[rows], oinds)
             assert_close(got.float().cpu().numpy()[rows], ref, f"device all-to-all rank {rank} T={T} (oracle)",
                          bound=bound)
-        assert a2a.status() == 0
+        # back-to-back calls, no host barrier between them: each call's
+        # exchange stream forks from and joins the caller's stream
+        xs = []
+        for i in range(4):
+            g.manual_seed(7000 + 10 * i + rank)
+            xs.append(torch.randn((384, blk.H), device=dev, generator=g).to(torch.bfloat16))
+        wants = [ops.moe_block(full, xi) for xi in xs]
+        dist.barrier()
+        gots = [a2a.moe_block(shard, xi) for xi in xs]
+        for i, (gt, wt) in enumerate(zip(gots, wants)):
+            assert_close_gpu_pair(gt.float().cpu().numpy(), wt.float().cpu().numpy(),
+                                  f"device all-to-all rank {rank} back-to-back call {i}")
+        st = a2a.status()
+        assert st == 0, f"rank {rank}: status bits {st:#x}"
         torch.cuda.synchronize()
         dist.barrier()
     finally:
