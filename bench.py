@@ -530,7 +530,10 @@ def run_prefill_bench(args, cfg):
                      "traffic_source": MEASURED_TRAFFIC.get(f"config{args.config} q{bits} prefill T={T}", (None, None))[1],
                      "algorithmic_flops_per_step": gemm_flops,
                      "kernel": "k_pre_gemm (gate/up + down launches)", "gemm_ms_per_step": gemm_ms,
-                     "block_tflops": all_flops / (ms_step * 1e-3) / 1e12},
+                     "block_tflops": all_flops / (ms_step * 1e-3) / 1e12,
+                     **({"note": "the home and the remote experts' GEMMs run at the same time on two streams; "
+                                 "their event-timed durations overlap, so achieved is a lower bound"}
+                        if a2a and args.prefill_par == "device" and world > 1 else {})},
         "stages_ms_per_step": {k: v / max(ncalls, 1) * calls_per_step for k, v in stages.items()},
         # route, sort, scatter, gather, gate/up, row scale, down, final (twice per step with all-to-all)
         "gpu_launches": K * (21 if dctx is not None else 8 * (2 if a2a else 1)),
