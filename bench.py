@@ -28,7 +28,10 @@ Also reported:
   roofline      algorithmic HBM bytes per step (distinct experts' weights +
                 shared expert + router + activations) / step time, against
                 MEASURED_PEAKS.json hbm_gbs.
-  cpu_baseline  the CPU oracle (C restatement, OpenMP) on the same workload.
+  cpu_baseline  the vectorised CPU restatement of the block (oracle/rnb_cpu_fast.c:
+                -O3, AVX2/FMA, OpenMP over every host thread, experts grouped;
+                routing identical to the exact-order oracle) on a bounded
+                sample of the same workload.
   --impl reference  times that CPU path alone (the reference's own MLX path
                 cannot run here: no Apple GPU, no MLX).
 """
@@ -168,6 +171,16 @@ def timed_trials(run_k, stream, dist, dev, min_s):
     return [first] + [one() for _ in range(n - 1)]
 
 
+def cpu_port_desc():
+    """How the timed CPU path computes (the vectorised restatement)."""
+    from oracle import oracle
+
+    return ("the vectorised CPU restatement, oracle/rnb_cpu_fast.c: C -O3, "
+            + ("AVX2/FMA" if oracle.fast_simd() else "plain C (no AVX2/FMA on this host)")
+            + " kernels, OpenMP over every host thread, experts grouped so each weight panel is dequantised "
+              "once per call; routing identical to the exact-order oracle, outputs within the parity tolerance")
+
+
 def cpu_baseline(bits, T, budget_s=10.0, seed=1):
     from oracle import oracle
     from runnel_b200 import inputs
@@ -177,14 +190,14 @@ def cpu_baseline(bits, T, budget_s=10.0, seed=1):
     n = 0
     t0 = time.perf_counter()
     while True:
-        oracle.moe_block(w, blk.x, k=8)
+        oracle.moe_block_fast(w, blk.x, k=8)
         n += 1
         el = time.perf_counter() - t0
         if el >= budget_s or n >= 10000:
             break
     cores = os.cpu_count() or 1
     return {"value": el / (n * T) * 1e6, "unit": "us/token", "cores": cores, "kind": "port",
-            "sample": f"{n} block calls of T={T} tokens, q{bits} (the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP, fp32 -- a checker, not an optimised CPU implementation)"}
+            "sample": f"{n} block calls of T={T} tokens, q{bits} ({cpu_port_desc()})"}
 
 
 def run_reference(args, cfg=None):
@@ -200,10 +213,10 @@ def run_reference(args, cfg=None):
     blk = inputs.make_block(bits, seed=args.seed, T=T)
     w = oracle.BlockWeights(bits=bits, group=64, **blk.weight_fields())
     for _ in range(args.warmup):
-        oracle.moe_block(w, blk.x, k=8)
+        oracle.moe_block_fast(w, blk.x, k=8)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.moe_block(w, blk.x, k=8)
+        oracle.moe_block_fast(w, blk.x, k=8)
     el = time.perf_counter() - t0
     us_tok = el / (args.steps * T) * 1e6
     cores = os.cpu_count() or 1
@@ -214,7 +227,7 @@ def run_reference(args, cfg=None):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"config{args.config} q{bits} decode T={T}", "bits": bits, "tokens_per_step": T},
         "cpu_baseline": {"value": us_tok, "unit": "us/token", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} block calls of T={T} (the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP -- a checker, not an optimised CPU implementation)"},
+                         "sample": f"{args.steps} block calls of T={T} ({cpu_port_desc()})"},
         "e2e": {"value": us_tok, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -236,7 +249,7 @@ def run_reference_stack(args, cfg, n_layers=4):
     def token(x):
         xa, xn = stack.reference_add_rmsnorm(x, None, nw[0])
         for l in range(n_layers):
-            y, _, _ = oracle.moe_block(ws[l], xn, k=8)
+            y, _, _ = oracle.moe_block_fast(ws[l], xn, k=8)
             xa, xn = stack.reference_add_rmsnorm(xa, f32_to_bf16_bits(y), nw[l + 1])
         return xa
 
@@ -255,14 +268,13 @@ def run_reference_stack(args, cfg, n_layers=4):
         "config": {"workload": f"config4 {L} q{bits} layers, batch-1 sequential decode", "bits": bits, "layers": L},
         "cpu_baseline": {"value": us_tok, "unit": "us/token", "cores": cores, "kind": "port",
                          "sample": f"{args.steps} tokens through {n_layers} layers, scaled by {L}/{n_layers} "
-                                   "(the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP -- a checker, "
-                                   "not an optimised CPU implementation)"},
+                                   f"({cpu_port_desc()})"},
         "e2e": {"value": us_tok, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_reference_prefill(args, cfg, sample_T=16):
+def run_reference_prefill(args, cfg, sample_T=2048):
     """The CPU path (oracle) on the prefill workload: each step is the first
     sample_T tokens of that step's batch, alternating over the step kinds."""
     from oracle import oracle
@@ -273,11 +285,11 @@ def run_reference_prefill(args, cfg, sample_T=16):
           for b in blocks]
     for i in range(args.warmup):
         w, x = ws[i % len(ws)]
-        oracle.moe_block(w, x, k=8)
+        oracle.moe_block_fast(w, x, k=8)
     t0 = time.perf_counter()
     for i in range(args.steps):
         w, x = ws[i % len(ws)]
-        oracle.moe_block(w, x, k=8)
+        oracle.moe_block_fast(w, x, k=8)
     el = time.perf_counter() - t0
     tok_s = args.steps * sample_T / el
     cores = os.cpu_count() or 1
@@ -288,9 +300,7 @@ def run_reference_prefill(args, cfg, sample_T=16):
         "config": {"workload": f"config{args.config} q{bits} prefill T={cfg['T']}", "bits": bits,
                    "tokens_per_step": sample_T, "routing": routing},
         "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} oracle calls of the first {sample_T} tokens of each batch "
-                                   "(the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP -- a checker, "
-                                   "not an optimised CPU implementation)"},
+                         "sample": f"{args.steps} calls of the first {sample_T} tokens of each batch ({cpu_port_desc()})"},
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -331,9 +341,9 @@ def run_profile(args, cfg=None):
                       "calls": args.warmup + args.steps}))
 
 
-def cpu_baseline_prefill(blocks, bits, sample_T=32, budget_s=10.0):
-    """CPU oracle tokens/s on a bounded sample: the first sample_T tokens of
-    each step's batch, alternating over the step kinds of the workload."""
+def cpu_baseline_prefill(blocks, bits, sample_T=2048, budget_s=10.0):
+    """CPU tokens/s on a bounded sample: the first sample_T tokens of each
+    step's batch, alternating over the step kinds of the workload."""
     from oracle import oracle
 
     ws = [(oracle.BlockWeights(bits=bits, group=64, **b.weight_fields()), np.ascontiguousarray(b.x[:sample_T]))
@@ -342,14 +352,14 @@ def cpu_baseline_prefill(blocks, bits, sample_T=32, budget_s=10.0):
     t0 = time.perf_counter()
     while True:
         w, x = ws[n % len(ws)]
-        oracle.moe_block(w, x, k=8)
+        oracle.moe_block_fast(w, x, k=8)
         n += 1
         el = time.perf_counter() - t0
         if el >= budget_s:
             break
     return {"value": n * sample_T / el, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": f"{n} oracle block calls of {sample_T} tokens (first tokens of the workload's batches), "
-                      f"q{bits}; the exact-order CPU oracle (C, -O2 -ffp-contract=off, OpenMP, fp32), not an optimised CPU implementation"}
+            "sample": f"{n} block calls of {sample_T} tokens (first tokens of the workload's batches), "
+                      f"q{bits} ({cpu_port_desc()})"}
 
 
 def prefill_blocks(cfg, bits, seed):
@@ -710,7 +720,7 @@ def cpu_baseline_stack(layers, norms, bits, x0, n_layers=4, budget_s=10.0):
     while True:
         xa, xn = stack.reference_add_rmsnorm(x, None, nw[0])
         for l in range(n_layers):
-            y, _, _ = oracle.moe_block(ws[l], xn, k=8)
+            y, _, _ = oracle.moe_block_fast(ws[l], xn, k=8)
             xa, xn = stack.reference_add_rmsnorm(xa, f32_to_bf16_bits(y), nw[l + 1])
         n += 1
         el = time.perf_counter() - t0
@@ -718,8 +728,8 @@ def cpu_baseline_stack(layers, norms, bits, x0, n_layers=4, budget_s=10.0):
             break
     L = len(layers)
     return {"value": el / n * 1e6 * L / n_layers, "unit": "us/token", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": f"{n} tokens through the first {n_layers} of {L} layers (the exact-order CPU oracle: C, -O2 -ffp-contract=off, OpenMP, fp32; "
-                      f"not an optimised CPU implementation), scaled by {L}/{n_layers}"}
+            "sample": f"{n} tokens through the first {n_layers} of {L} layers ({cpu_port_desc()}), "
+                      f"scaled by {L}/{n_layers}"}
 
 
 def run_ours(args):

@@ -40,8 +40,7 @@
 #include <omp.h>
 #endif
 
-#define RNBO_OK 0
-#define RNBO_EINVAL -1
+#include "rnb_oracle.h"
 
 /* ---------------------------------------------------------------- bf16 */
 
@@ -164,36 +163,6 @@ int rnbo_affine_matvec(const uint32_t* w, const uint16_t* s, const uint16_t* b, 
 }
 
 /* ------------------------------------------------------- MoE block */
-
-typedef struct rnbo_block {
-  int T, H, I, E, k, bits, group;
-  const uint16_t* x;             /* [T,H] bf16 */
-  const uint16_t* router_w;      /* [E,H] bf16 */
-  const uint16_t* shared_gate_w; /* [H] bf16, NULL = no shared expert */
-  const uint32_t* gu_w;          /* [E,2I,H*bits/32] packed up||gate */
-  const uint16_t* gu_s;          /* [E,2I,H/group] */
-  const uint16_t* gu_b;
-  const uint32_t* dn_w; /* [E,H,I*bits/32] */
-  const uint16_t* dn_s; /* [E,H,I/group] */
-  const uint16_t* dn_b;
-  const uint32_t* sgu_w; /* [2I,H*bits/32] shared up||gate */
-  const uint16_t* sgu_s;
-  const uint16_t* sgu_b;
-  const uint32_t* sdn_w; /* [H,I*bits/32] */
-  const uint16_t* sdn_s;
-  const uint16_t* sdn_b;
-  /* 8-bit affine router and shared gate (router_bits == 8; real Ornith
-   * checkpoints store mlp.gate and mlp.shared_expert_gate so): codes
-   * [E,H/4] / [H/4] in router_q / sgate_q, bf16 scales and biases per 64
-   * inputs.  router_bits 0 or 16: the bf16 router_w / shared_gate_w above. */
-  int router_bits;
-  const uint32_t* router_q;
-  const uint16_t* router_s; /* [E,H/64] */
-  const uint16_t* router_b;
-  const uint32_t* sgate_q; /* [H/4] */
-  const uint16_t* sgate_s; /* [H/64] */
-  const uint16_t* sgate_b;
-} rnbo_block;
 
 /* Router weight (row e; e == E is the shared gate) at input h, exact in
  * double: bf16, or the 8-bit affine scale * code + bias (a bf16 times an
