@@ -287,7 +287,9 @@ RNB_API int rnb_moe_block_ep_fwd(const rnb_moe_desc* d, rnb_ep* ep, const void* 
  * bounded and set RNB_STATUS_TIMEOUT in the workspace status word.  The
  * exchange and the remote experts run on a stream of the context's own,
  * which forks from the caller's stream once the home routing is queued and
- * joins it before the combine (a captured call is one fork and one join).
+ * joins it before the combine.  Not for CUDA graph capture: the exchange
+ * epoch is the context's host-side call count, which a replay would not
+ * advance.
  * rnb_a2a_create allocates this rank's areas for up to max_tokens tokens and
  * writes its IPC handle (RNB_A2A_HANDLE_BYTES); gather every rank's handle
  * (rank order) and pass them to rnb_a2a_connect.  Every rank then makes the

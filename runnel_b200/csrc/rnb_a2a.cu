@@ -489,7 +489,8 @@ int rnb_moe_block_a2a_fwd(const rnb_moe_desc* d, rnb_a2a* a, const void* x, void
   p.out = out;
   p.y_f32 = (d->flags & RNB_FLAG_Y_F32) ? 1 : 0;
   // 2-5 on the side stream, which always joins the caller's stream again
-  // (also on an error) so that a captured call stays one fork and one join
+  // (also on an error), so later work on the caller's stream never runs
+  // beside a half-finished exchange
   const cudaStream_t sd = a->side;
   k_a2a_dispatch<<<kA2aCtas, 256, 0, sd>>>(p);
   k_a2a_wait<<<1, 256, 0, sd>>>(p, p.area.rx_flags);
