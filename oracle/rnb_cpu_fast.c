@@ -348,7 +348,7 @@ static void route(const rnbo_block* d, const float* xf, float* lg, int32_t* inds
     lg[te] = rnbo_f64_to_bf16_f32(router_dot(d, xf + (size_t)t * H, e));
   }
   const int has_sg = d->router_bits == 8 ? d->sgate_q != NULL : d->shared_gate_w != NULL;
-  float* wsg = (float*)malloc(sizeof(float) * H);
+  float wsg[8192]; /* the shared gate's weights, fp32 (H <= 8192, checked by the caller) */
   for (int h = 0; h < H; ++h) {
     if (!has_sg) {
       wsg[h] = 0.0f;
@@ -382,7 +382,6 @@ static void route(const rnbo_block* d, const float* xf, float* lg, int32_t* inds
     for (int s = 0; s < K; ++s) scores[(size_t)t * K + s] = p[s] / psum;
     sg[t] = has_sg ? 1.0f / (1.0f + expf(-dot_f32(xf + (size_t)t * H, wsg, H))) : 0.0f;
   }
-  free(wsg);
 }
 
 /* -------------------------------------------------------------- block */
@@ -414,7 +413,7 @@ int rnbc_moe_block(const rnbo_block* d, float* out, int32_t* inds, float* scores
   if (!d || d->T < 0 || d->H <= 0 || d->I <= 0 || d->E <= 0 || d->k <= 0 || d->k > d->E || d->k > 64)
     return RNBO_EINVAL;
   if ((d->bits != 4 && d->bits != 8) || d->group <= 0 || d->H % d->group || d->I % d->group) return RNBO_EINVAL;
-  if (d->I % 8 || d->H % RNBC_PANEL) return RNBO_EINVAL;
+  if (d->I % 8 || d->H % RNBC_PANEL || d->H > 8192) return RNBO_EINVAL;
   if (d->router_bits == 8 && (!d->router_q || !d->router_s || !d->router_b || d->H % 64)) return RNBO_EINVAL;
   if (nthreads < 1) nthreads = 1;
   rnbc_simd();
@@ -443,6 +442,10 @@ int rnbc_moe_block(const rnbo_block* d, float* out, int32_t* inds, float* scores
   for (int e = 0; e < NE; ++e) cnt[e + 1] += cnt[e];
   {
     int* fill = (int*)malloc(sizeof(int) * NE);
+    if (!fill) {
+      free(xf), free(lg), free(sg), free(cnt), free(ent), free(hid), free(y);
+      return RNBO_EINVAL;
+    }
     memcpy(fill, cnt, sizeof(int) * NE);
     for (int t = 0; t < T; ++t) {
       for (int s = 0; s < K; ++s) ent[fill[inds[(size_t)t * K + s]]++] = t * S + s;
@@ -455,17 +458,27 @@ int rnbc_moe_block(const rnbo_block* d, float* out, int32_t* inds, float* scores
   const int gu_per = I / 8, dn_per = H / RNBC_PANEL;
   int n_act = 0;
   int* act = (int*)malloc(sizeof(int) * NE);
+  if (!act) {
+    free(xf), free(lg), free(sg), free(cnt), free(ent), free(hid), free(y);
+    return RNBO_EINVAL;
+  }
   for (int e = 0; e < NE; ++e)
     if (cnt[e + 1] > cnt[e]) act[n_act++] = e;
 
+  int oom = 0;
 #pragma omp parallel num_threads(nthreads)
   {
     const int kmax = H > I ? H : I;
     float* panel = (float*)malloc(sizeof(float) * (size_t)RNBC_PANEL * kmax);
+    if (!panel) {
+#pragma omp atomic write
+      oom = 1;
+    }
     float res[RNBC_TR][RNBC_TT];
     const float* xr[RNBC_TT];
 #pragma omp for schedule(dynamic, 4)
     for (long it = 0; it < (long)n_act * gu_per; ++it) {
+      if (!panel) continue;
       const int e = act[it / gu_per], c0 = (int)(it % gu_per) * 8;
       const expert_w w = expert_at(d, e);
 #ifdef RNBC_X86
@@ -502,6 +515,7 @@ int rnbc_moe_block(const rnbo_block* d, float* out, int32_t* inds, float* scores
     }
 #pragma omp for schedule(dynamic, 4)
     for (long it = 0; it < (long)n_act * dn_per; ++it) {
+      if (!panel) continue;
       const int e = act[it / dn_per], n0 = (int)(it % dn_per) * RNBC_PANEL;
       const expert_w w = expert_at(d, e);
 #ifdef RNBC_X86
@@ -526,6 +540,11 @@ int rnbc_moe_block(const rnbo_block* d, float* out, int32_t* inds, float* scores
       }
     }
     free(panel);
+  }
+  if (oom) {
+    free(act);
+    free(xf), free(lg), free(sg), free(cnt), free(ent), free(hid), free(y);
+    return RNBO_EINVAL;
   }
   /* combine: the slots in order, then the gated shared expert */
 #pragma omp parallel for num_threads(nthreads) schedule(static)
