@@ -43,6 +43,18 @@ def test_fast_block_adversarial_routing():
     assert_close(out, ref, "CPU baseline adversarial", bound=bound)
 
 
+def test_fast_block_small_bank():
+    """A 16-expert bank of other sizes (H 512, I 256): most experts hold many
+    tokens, so the panel tiles carry the block."""
+    blk = inputs.make_block(4, seed=8, T=37, H=512, I=256, E=16)
+    w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
+    ref, oinds, oscores, bound = oracle_block(w, blk.x)
+    out, inds, scores = oracle.moe_block_fast(w, blk.x)
+    np.testing.assert_array_equal(inds, oinds)
+    np.testing.assert_array_equal(scores, oscores)
+    assert_close(out, ref, "CPU baseline, 16-expert bank", bound=bound)
+
+
 def test_fast_block_empty_and_threads():
     blk = inputs.make_block(4, seed=2, T=3)
     w = oracle.BlockWeights(bits=4, group=64, **blk.weight_fields())
